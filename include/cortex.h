@@ -1,0 +1,211 @@
+/*
+ * cortex.h - C ABI of libcortex.so, the B200 (sm_100a) decode engine.
+ *
+ * Part 1 is the reference's boundary: the thirteen symbols core/cortex.nim
+ * exports with {.exportc, dynlib, cdecl.} (core/cortex.nim:16) and that the
+ * PHP host binds with FFI::cdef (src/tensor_ffi_adapter.php:46-61,
+ * src/snai_inference.php:84-91).  Names, argument types, argument meaning,
+ * ownership and error behaviour are the reference's; each declaration names
+ * the line it replaces.  PHP resolves every declared symbol when it parses
+ * the cdef block, so all of them exist, including the training ones.
+ *
+ * Part 2 is an additive batched API (the PHP host does not need it): many
+ * independent sequences ("slots") per state, token ids sampled on the GPU
+ * with the reference's two samplers, and a stateless sampler over device
+ * logits.  All functions of part 2 return 0 on success and a negative code on
+ * failure; cortex_last_error() then describes the failure.
+ *
+ * Threading: a state is used by one host thread at a time (the reference is
+ * single-threaded too, core/cortex.nim:61).  Different states may live on
+ * different GPUs and be driven from different threads.
+ */
+#ifndef SNAI_CORTEX_H
+#define SNAI_CORTEX_H
+
+#include <stdbool.h>
+
+#if defined(__GNUC__)
+#define CORTEX_API __attribute__((visibility("default")))
+#else
+#define CORTEX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ======================================================================== */
+/* Part 1 - reference boundary                                              */
+/* ======================================================================== */
+
+/* core/cortex.nim:261 cortex_init.  Allocates a state of the given shape with
+ * zero weights and unit RMSNorm weights (core/cortex.nim:433-438).  ffn is
+ * 4*dim; head size is dim/heads forced even and >= 2 (:267-271).  NULL on
+ * failure (no GPU, out of memory, unsupported shape). */
+CORTEX_API void *cortex_init(int vocab_size, int hidden_dim, int ctx_size, int num_layers, int num_heads);
+
+/* core/cortex.nim:978 cortex_load_stream.  Reads a SNAI_V4 file (28-byte
+ * header: magic[8], vocab, hidden, ffn, ctx, layers as u32 LE, then fp32 LE
+ * tensors in the order of core/cortex.nim:1002-1041).  NULL when the file
+ * cannot be opened, the magic is not "SNAI_V4" or a read comes up short. */
+CORTEX_API void *cortex_load_stream(const char *filepath, int num_heads);
+
+/* core/cortex.nim:487 cortex_forward.  Feeds num_tokens ids (out-of-range ids
+ * read as 0, :493) at the next cache positions; stops silently at ctx
+ * (:495).  Writes vocab fp32 logits of the last token into the caller's
+ * buffer, before returning, only if that token was processed.  If the GPU
+ * fails, the logits are set to NaN (which the PHP host's NaN check at
+ * src/snai_inference.php:146 turns into a stop) and cortex_last_error() says
+ * why. */
+CORTEX_API void cortex_forward(void *state, int *raw_tokens, int num_tokens, float *raw_logits);
+
+/* core/cortex.nim:484 cortex_reset_cache: the next token goes to position 0. */
+CORTEX_API void cortex_reset_cache(void *state);
+
+/* core/cortex.nim:824 cortex_free.  NULL-safe. */
+CORTEX_API void cortex_free(void *state);
+
+/* core/cortex.nim:1046 cortex_init_gpu.  Selects and initialises the CUDA
+ * device (SNAI_DEVICE, default 0).  Unlike the reference it does not claim
+ * success on failure: the failure is kept in cortex_last_error(). */
+CORTEX_API void cortex_init_gpu(void);
+
+/* core/cortex.nim:1050 / :1054.  0 for a NULL state. */
+CORTEX_API int get_vocab_size(void *state);
+CORTEX_API int get_ctx_size(void *state);
+
+/* core/cortex.nim:464 / :469.  Copies one tensor in or out by (layer, type):
+ * layer -1: 0 embeddings [V,d], 1 w_out [V,d], 2 rms_final [d];
+ * layer l : 10 rms_att, 11 rms_ffn [d], 12 Wq, 13 Wk, 14 Wv, 15 Wo [d,d],
+ *           16 W_up [4d,d], 17 W_down [d,4d]  (fp32, row-major).
+ * A size mismatch or unknown (layer, type) is a silent no-op (:465). */
+CORTEX_API void cortex_load_layer(void *state, int layer_idx, int tensor_type, float *raw_weights, int num_weights);
+CORTEX_API void cortex_extract_layer(void *state, int layer_idx, int tensor_type, float *raw_weights, int num_weights);
+
+/* core/cortex.nim:474 / :479.  Adam moment storage per tensor (m when
+ * is_variance is false, v otherwise); zero until loaded.  Kept in host
+ * memory: this library runs no optimizer. */
+CORTEX_API void cortex_load_adam_layer(void *state, int layer_idx, int tensor_type, bool is_variance, float *raw, int size);
+CORTEX_API void cortex_extract_adam_layer(void *state, int layer_idx, int tensor_type, bool is_variance, float *raw, int size);
+
+/* core/cortex.nim:565 cortex_train_step.  Training is not part of this
+ * library: returns NaN (the PHP worker aborts on a NaN loss,
+ * src/train_worker.php:152-155) and sets cortex_last_error(). */
+CORTEX_API float cortex_train_step(void *state, int *raw_inputs, int *raw_targets, int num_tokens, float lr);
+
+/* ======================================================================== */
+/* Part 2 - batched extension                                               */
+/* ======================================================================== */
+
+/* GEMM operand precision.  FP32 runs every projection as fp32 FFMA GEMV
+ * (closest to the reference).  TF32 / BF16 run projections with at least 64
+ * rows on tcgen05 tensor cores (fp32 accumulate); fewer rows use fp32 GEMV. */
+#define SNAI_PREC_FP32 0
+#define SNAI_PREC_TF32 1
+#define SNAI_PREC_BF16 2
+
+/* Pointer-location flag for the batched calls. */
+#define SNAI_HOST_PTRS 0   /* tokens, uniforms, ids, logits are host memory; the call returns when done */
+#define SNAI_DEVICE_PTRS 1 /* device memory; work is queued on the state's stream, no host wait */
+
+/* The two samplers of the reference.
+ * variant 0 = src/snai_inference.php:151-195: logits /= temperature (stored as
+ *   fp32), repetition penalty over the unique history (L>0: /= rep, else *= rep,
+ *   stored as fp32), greedy iff temperature <= 0.01, else softmax (double) and
+ *   the first id whose running sum reaches u*sum.
+ * variant 1 = src/tensor_ffi_adapter.php:168-204: subtract rep from the logits
+ *   of ids in the history, stable descending order, keep top_k, greedy iff
+ *   temperature < 0.01, else exp(v/T) (no max shift), keep the prefix whose
+ *   running sum reaches top_p, then the first id with u*cum <= running sum.
+ * u comes from the caller (one fp32 uniform per row) in place of
+ * mt_rand()/mt_getrandmax().  nan_guard (variant 0 only): a row whose logit 0
+ * is NaN yields id -1, as the host loop's NaN check stops there
+ * (src/snai_inference.php:146). */
+typedef struct snai_sample_params {
+  int variant;
+  double temperature;
+  double rep_penalty;
+  int top_k;    /* variant 1; 1 <= top_k <= 1024 */
+  double top_p; /* variant 1 */
+  int nan_guard;
+} snai_sample_params;
+
+/* Last error of the calling thread ("" if none). */
+CORTEX_API const char *cortex_last_error(void);
+
+/* cortex_load_stream with max_seqs independent sequence slots on CUDA device
+ * `device`, using the given GEMM precision. */
+CORTEX_API void *cortex_load_stream_ex(const char *filepath, int num_heads, int max_seqs, int device, int precision);
+
+/* cortex_init with slots, device and precision. */
+CORTEX_API void *cortex_init_ex(int vocab_size, int hidden_dim, int ctx_size, int num_layers, int num_heads, int max_seqs,
+                     int device, int precision);
+
+CORTEX_API int cortex_num_slots(void *state);
+CORTEX_API int cortex_head_size(void *state);
+CORTEX_API int cortex_num_heads(void *state);
+
+/* Resets the given slots (all slots when slots is NULL) to position 0. */
+CORTEX_API int cortex_seq_reset(void *state, const int *slots, int n);
+
+/* Current cache position of a slot (-1 on error). */
+CORTEX_API int cortex_seq_pos(void *state, int slot);
+
+/* Feeds n_tok tokens to each of `batch` slots (tokens row-major [batch][n_tok];
+ * slots[b], or b when slots is NULL).  Each slot behaves as cortex_forward on
+ * its own cache (ctx cut-off per slot).  The logits of each slot's last token
+ * stay on the device for cortex_decode_batch; if `logits` is not NULL they are
+ * also copied to logits[b][vocab] for the slots whose last token was
+ * processed.  flags: SNAI_HOST_PTRS or SNAI_DEVICE_PTRS. */
+CORTEX_API int cortex_forward_batch(void *state, const int *tokens, int batch, int n_tok, const int *slots, float *logits,
+                         int flags);
+
+/* One step of the host loop of src/snai_inference.php:139-215 for `batch`
+ * slots at once: sample an id per slot from its current logits (history =
+ * every token fed to the slot so far), then feed that id.  uniforms[b] is the
+ * draw of row b; out_ids[b] receives the sampled id. */
+CORTEX_API int cortex_decode_batch(void *state, const int *slots, int batch, const float *uniforms,
+                        const snai_sample_params *params, int *out_ids, int flags);
+
+/* Copies the current device logits of the given slots to host memory
+ * out[n][vocab]. */
+CORTEX_API int cortex_get_logits(void *state, const int *slots, int n, float *out);
+
+/* Stateless sampler over device memory: logits[rows][ld] (row stride ld >=
+ * vocab), history ids hist[rows][hist_cols] of which hist_len[r] (all
+ * hist_cols when hist_len is NULL) are used, uniforms[rows], out_ids[rows].
+ * Queued on `stream` (a cudaStream_t; NULL = legacy default stream). */
+CORTEX_API int cortex_sample(const float *logits, int rows, int vocab, long long ld, const int *hist, int hist_cols,
+                  const int *hist_len, const float *uniforms, const snai_sample_params *params, int *out_ids,
+                  void *stream);
+
+/* Makes the state queue its work on `stream` (a cudaStream_t of the state's
+ * device; NULL restores the state's own stream). */
+CORTEX_API int cortex_set_stream(void *state, void *stream);
+
+/* Waits for the state's queued work; reports a device-side error if any. */
+CORTEX_API int cortex_synchronize(void *state);
+
+/* Moves the given slots (all when slots is NULL) back to cache position
+ * `pos` (<= their current position): later tokens are forgotten and will be
+ * overwritten.  The slots' current logits are kept. */
+CORTEX_API int cortex_seq_rewind(void *state, const int *slots, int n, int pos);
+
+/* Kernel-class profiler.  When on, every launch is bracketed by CUDA events
+ * on the state's stream and its algorithmic bytes and FLOPs are counted.
+ * kind: 0 embedding+norm, 1 rmsnorm, 2 QKV projection, 3 attention,
+ * 4 Wo projection, 5 W_up, 6 W_down, 7 logits projection, 8 sampler.
+ * Enabling (or disabling) clears the counters; reading waits for the
+ * stream. */
+CORTEX_API int cortex_profile_enable(void *state, int on);
+CORTEX_API int cortex_profile_read(void *state, int kind, long long *launches, double *ms, double *bytes,
+                                   double *flops);
+
+/* Number of kernels the state has launched since it was created. */
+CORTEX_API long long cortex_kernel_launches(void *state);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SNAI_CORTEX_H */

@@ -1,0 +1,906 @@
+// cortex_api.cu - the C ABI of libcortex.so (include/cortex.h).
+//
+// Host side of the engine: model loading (SNAI_V4), device memory layout,
+// the reference's thirteen entry points and the batched extension.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <limits>
+#include <string>
+#include <vector>
+
+#include "../../include/cortex.h"
+#include "engine.h"
+
+namespace snai {
+
+static thread_local std::string g_err;
+
+void set_error(const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+}
+
+void clear_error() { g_err.clear(); }
+
+namespace {
+
+int env_int(const char *name, int def) {
+  const char *v = getenv(name);
+  if (!v || !*v) return def;
+  return atoi(v);
+}
+
+struct DeviceGuard {
+  int prev = -1, want;
+  explicit DeviceGuard(int d) : want(d) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != d) cudaSetDevice(d);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0 && prev != want) cudaSetDevice(prev);
+  }
+};
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Carves aligned sub-buffers out of one allocation.
+struct Carver {
+  size_t off = 0;
+  std::vector<std::pair<void **, size_t>> items;
+  void add(void **p, size_t bytes) {
+    items.push_back({p, off});
+    off = align_up(off + std::max<size_t>(bytes, 1), 256);
+  }
+  template <typename T>
+  void add(T **p, size_t n) {
+    add(reinterpret_cast<void **>(p), n * sizeof(T));
+  }
+  void place(void *base) {
+    for (auto &it : items) *it.first = static_cast<char *>(base) + it.second;
+  }
+};
+
+// Shape rules of core/cortex.nim:261-271 plus this engine's limits.
+bool make_dims(int vocab, int dim, int ctx, int layers, int heads, Dims *d) {
+  if (vocab < 1 || dim < 4 || ctx < 1 || layers < 1) {
+    set_error("unsupported shape: vocab=%d dim=%d ctx=%d layers=%d (need vocab>=1, dim>=4, ctx>=1, layers>=1)", vocab,
+              dim, ctx, layers);
+    return false;
+  }
+  if (dim % 4 != 0) {
+    set_error("hidden_dim %d is not a multiple of 4 (this engine reads activations in 16-byte units)", dim);
+    return false;
+  }
+  d->V = vocab;
+  d->D = dim;
+  d->F = dim * 4;
+  d->ctx = ctx;
+  d->L = layers;
+  d->heads = std::max(1, heads);
+  int hs = dim / d->heads;
+  if (hs % 2 != 0) hs -= 1;
+  if (hs < 2) hs = 2;
+  d->hs = hs;
+  d->att_ch = d->heads * hs;
+  if (d->att_ch > dim) {
+    // core/cortex.nim:515-538 would read past the end of each cache row
+    set_error("num_heads %d gives head size %d: %d heads x %d > hidden_dim %d", heads, hs, d->heads, hs, dim);
+    return false;
+  }
+  if ((size_t)ctx * sizeof(float) + 2048 > 200 * 1024) {
+    set_error("ctx_size %d exceeds this engine's attention limit (%d)", ctx, (200 * 1024 - 2048) / 4);
+    return false;
+  }
+  return true;
+}
+
+void free_engine(Engine *e) {
+  if (!e) return;
+  DeviceGuard g(e->device);
+  if (e->own_stream) cudaStreamSynchronize(e->own_stream);
+  cudaFree(e->wblock);
+  cudaFree(e->hblock);
+  cudaFree(e->kv);
+  cudaFree(e->ablock);
+  if (e->own_stream) cudaStreamDestroy(e->own_stream);
+  delete e;
+}
+
+Engine *create_engine(const Dims &d, int max_seqs, int device, int precision) {
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    set_error("no CUDA device available (libcortex runs on the GPU only)");
+    return nullptr;
+  }
+  if (device < 0 || device >= ndev) {
+    set_error("device %d out of range (%d devices)", device, ndev);
+    return nullptr;
+  }
+  if (max_seqs < 1) {
+    set_error("max_seqs must be >= 1");
+    return nullptr;
+  }
+  if (precision < kFP32 || precision > kBF16) {
+    set_error("unknown precision %d", precision);
+    return nullptr;
+  }
+  DeviceGuard g(device);
+  Engine *e = new Engine();
+  e->d = d;
+  e->device = device;
+  e->precision = precision;
+  e->max_seqs = max_seqs;
+  int chunk = env_int("SNAI_CHUNK_ROWS", 0);
+  if (chunk <= 0) chunk = std::max(max_seqs, std::min(8192, std::max(d.ctx, 256)));
+  e->m_max = (int)align_up((size_t)std::max(chunk, max_seqs), 128);
+
+  const size_t D = d.D, F = d.F, V = d.V;
+  // ---- weights ----
+  Carver w;
+  w.add(&e->emb, V * D);
+  w.add(&e->w_out, V * D);
+  w.add(&e->rms_final, D);
+  e->layers.resize(d.L);
+  for (auto &l : e->layers) {
+    w.add(&l.rms_att, D);
+    w.add(&l.rms_ffn, D);
+    w.add(&l.wqkv, 3 * D * D);
+    w.add(&l.wo, D * D);
+    w.add(&l.wup, F * D);
+    w.add(&l.wdown, D * F);
+  }
+  Carver hw;
+  if (precision == kBF16) {
+    hw.add(&e->w_out_h, V * D);
+    for (auto &l : e->layers) {
+      hw.add(&l.wqkv_h, 3 * D * D);
+      hw.add(&l.wo_h, D * D);
+      hw.add(&l.wup_h, F * D);
+      hw.add(&l.wdown_h, D * F);
+    }
+  }
+  // ---- activations and per-slot state ----
+  const size_t M = e->m_max;
+  Carver a;
+  a.add(&e->rows_d, M);
+  a.add(&e->outrows_d, M);
+  a.add(&e->h, M * D);
+  a.add(&e->x, M * D * sizeof(float));
+  a.add(&e->q, M * (size_t)d.att_ch);
+  a.add(&e->att, M * D * sizeof(float));
+  a.add(&e->u, M * F * sizeof(float));
+  a.add(&e->xo, M * D * sizeof(float));
+  a.add(&e->logits, (size_t)max_seqs * V);
+  a.add(&e->hist, (size_t)max_seqs * d.ctx);
+  a.add(&e->seq_len_d, (size_t)max_seqs);
+  a.add(&e->ids_d, (size_t)max_seqs);
+  a.add(&e->unif_d, (size_t)max_seqs);
+  a.add(&e->slots_d, (size_t)max_seqs);
+  a.add(&e->rope, (size_t)d.ctx * (d.hs / 2));
+  a.add(&e->err_d, 4);
+
+  e->kv_head_stride = (size_t)d.ctx * d.hs;
+  e->kv_part_stride = e->kv_head_stride * d.heads;
+  e->kv_layer_stride = 2 * e->kv_part_stride;
+  e->kv_slot_stride = e->kv_layer_stride * d.L;
+  const size_t kv_bytes = e->kv_slot_stride * max_seqs * sizeof(float);
+
+  cudaError_t err = cudaMalloc(&e->wblock, w.off);
+  if (err == cudaSuccess && hw.off) err = cudaMalloc(&e->hblock, hw.off);
+  if (err == cudaSuccess) err = cudaMalloc(&e->ablock, a.off);
+  if (err == cudaSuccess) err = cudaMalloc(reinterpret_cast<void **>(&e->kv), kv_bytes);
+  if (err != cudaSuccess) {
+    set_error("device allocation failed (weights %zu B, activations %zu B, kv cache %zu B): %s", w.off, a.off,
+              kv_bytes, cudaGetErrorString(err));
+    cudaGetLastError();
+    free_engine(e);
+    return nullptr;
+  }
+  w.place(e->wblock);
+  if (hw.off) hw.place(e->hblock);
+  a.place(e->ablock);
+  if (cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    set_error("cudaStreamCreate failed");
+    free_engine(e);
+    return nullptr;
+  }
+  e->stream = e->own_stream;
+  cudaMemsetAsync(e->wblock, 0, w.off, e->stream);
+  if (hw.off) cudaMemsetAsync(e->hblock, 0, hw.off, e->stream);
+  cudaMemsetAsync(e->ablock, 0, a.off, e->stream);
+  cudaMemsetAsync(e->kv, 0, kv_bytes, e->stream);
+  // RMSNorm weights start at 1 (core/cortex.nim:433-438)
+  fill_f32(*e, e->rms_final, D, 1.0f);
+  for (auto &l : e->layers) {
+    fill_f32(*e, l.rms_att, D, 1.0f);
+    fill_f32(*e, l.rms_ffn, D, 1.0f);
+  }
+  // RoPE table, with the reference's float expressions (core/cortex.nim:79-82)
+  std::vector<float2> rope((size_t)d.ctx * (d.hs / 2));
+  for (int p = 0; p < d.ctx; ++p)
+    for (int i = 0; i + 1 < d.hs; i += 2) {
+      const float freq = 1.0f / ::powf(10000.0f, (float)i / (float)d.hs);
+      const float theta = (float)p * freq;
+      rope[(size_t)p * (d.hs / 2) + i / 2] = make_float2(::cosf(theta), 1.0f * ::sinf(theta));
+    }
+  cudaMemcpyAsync(e->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice, e->stream);
+  e->sqrt_hs = ::sqrtf((float)d.hs);
+  e->pos.assign(max_seqs, 0);
+  e->logits_valid.assign(max_seqs, 0);
+  if (cudaStreamSynchronize(e->stream) != cudaSuccess) {
+    set_error("engine initialisation failed: %s", cudaGetErrorString(cudaGetLastError()));
+    free_engine(e);
+    return nullptr;
+  }
+  return e;
+}
+
+// fp32 -> bf16 copies of every projection weight (BF16 mode).
+int refresh_bf16(Engine &e) {
+  if (e.precision != kBF16) return 0;
+  const size_t D = e.d.D, F = e.d.F, V = e.d.V;
+  int rc = convert_bf16(e, e.w_out, e.w_out_h, V * D);
+  for (auto &l : e.layers) {
+    rc |= convert_bf16(e, l.wqkv, l.wqkv_h, 3 * D * D);
+    rc |= convert_bf16(e, l.wo, l.wo_h, D * D);
+    rc |= convert_bf16(e, l.wup, l.wup_h, F * D);
+    rc |= convert_bf16(e, l.wdown, l.wdown_h, D * F);
+  }
+  return rc;
+}
+
+// Device pointer and element count of a tensor (core/cortex.nim:439-462).
+float *tensor_ptr(Engine &e, int layer, int type, size_t *n) {
+  const size_t D = e.d.D, F = e.d.F, V = e.d.V;
+  if (layer >= e.d.L || layer < -1) return nullptr;
+  if (layer == -1) {
+    if (type == 0) { *n = V * D; return e.emb; }
+    if (type == 1) { *n = V * D; return e.w_out; }
+    if (type == 2) { *n = D; return e.rms_final; }
+    return nullptr;
+  }
+  LayerWeights &l = e.layers[layer];
+  switch (type) {
+    case 10: *n = D; return l.rms_att;
+    case 11: *n = D; return l.rms_ffn;
+    case 12: *n = D * D; return l.wqkv;
+    case 13: *n = D * D; return l.wqkv + D * D;
+    case 14: *n = D * D; return l.wqkv + 2 * D * D;
+    case 15: *n = D * D; return l.wo;
+    case 16: *n = F * D; return l.wup;
+    case 17: *n = D * F; return l.wdown;
+  }
+  return nullptr;
+}
+
+// bf16 copy of a tensor, if it has one.
+__nv_bfloat16 *tensor_ptr_h(Engine &e, int layer, int type) {
+  if (e.precision != kBF16) return nullptr;
+  const size_t D = e.d.D;
+  if (layer == -1) return type == 1 ? e.w_out_h : nullptr;
+  if (layer < 0 || layer >= e.d.L) return nullptr;
+  LayerWeights &l = e.layers[layer];
+  switch (type) {
+    case 12: return l.wqkv_h;
+    case 13: return l.wqkv_h + D * D;
+    case 14: return l.wqkv_h + 2 * D * D;
+    case 15: return l.wo_h;
+    case 16: return l.wup_h;
+    case 17: return l.wdown_h;
+  }
+  return nullptr;
+}
+
+int check_device_error(Engine &e) {
+  int code = 0;
+  if (cudaMemcpy(&code, e.err_d, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+    set_error("CUDA error: %s", cudaGetErrorString(cudaGetLastError()));
+    return -4;
+  }
+  if (code) {
+    cudaMemset(e.err_d, 0, sizeof(int));
+    set_error("device-side error %d (a bounded wait expired or the sampler overflowed)", code);
+    return -6;
+  }
+  return 0;
+}
+
+int finish(Engine &e, bool wait) {
+  if (!wait) {
+    const cudaError_t le = cudaGetLastError();
+    if (le != cudaSuccess) {
+      set_error("CUDA error: %s", cudaGetErrorString(le));
+      return -4;
+    }
+    return 0;
+  }
+  if (cudaStreamSynchronize(e.stream) != cudaSuccess) {
+    set_error("CUDA error: %s", cudaGetErrorString(cudaGetLastError()));
+    return -4;
+  }
+  return check_device_error(e);
+}
+
+bool slots_ok(Engine &e, const int *slots, int batch) {
+  std::vector<char> seen(e.max_seqs, 0);
+  for (int b = 0; b < batch; ++b) {
+    const int s = slots ? slots[b] : b;
+    if (s < 0 || s >= e.max_seqs) {
+      set_error("slot %d out of range [0, %d)", s, e.max_seqs);
+      return false;
+    }
+    if (seen[s]) {
+      set_error("slot %d appears twice in one batch", s);
+      return false;
+    }
+    seen[s] = 1;
+  }
+  return true;
+}
+
+int upload_seq_len(Engine &e) {
+  return cudaMemcpyAsync(e.seq_len_d, e.pos.data(), sizeof(int) * e.max_seqs, cudaMemcpyHostToDevice, e.stream) ==
+                 cudaSuccess
+             ? 0
+             : -4;
+}
+
+int forward_batch(Engine &e, const int *tokens, int batch, int n_tok, const int *slots, float *logits, int flags) {
+  clear_error();
+  if (batch < 0 || n_tok < 0) {
+    set_error("negative batch or token count");
+    return -2;
+  }
+  if (batch == 0 || n_tok == 0) return 0;
+  if (!tokens) {
+    set_error("tokens is NULL");
+    return -2;
+  }
+  if (!slots_ok(e, slots, batch)) return -2;
+  const bool dev = flags & SNAI_DEVICE_PTRS;
+  DeviceGuard g(e.device);
+  std::vector<RowDesc> rows;
+  rows.reserve((size_t)batch * n_tok);
+  std::vector<int> done(batch, 0);
+  for (int b = 0; b < batch; ++b) {
+    const int s = slots ? slots[b] : b;
+    const int p0 = e.pos[s];
+    for (int i = 0; i < n_tok; ++i) {
+      if (p0 + i >= e.d.ctx) break;  // core/cortex.nim:495
+      const int idx = b * n_tok + i;
+      rows.push_back(RowDesc{s, p0 + i, dev ? idx : tokens[idx], i == n_tok - 1 ? s : -1});
+      done[b]++;
+    }
+  }
+  int rc = run_rows(e, rows.data(), (int)rows.size(), dev ? tokens : nullptr);
+  if (rc) return rc;
+  for (int b = 0; b < batch; ++b) {
+    const int s = slots ? slots[b] : b;
+    e.pos[s] += done[b];
+    if (done[b] == n_tok) e.logits_valid[s] = 1;
+  }
+  if (logits) {
+    for (int b = 0; b < batch; ++b) {
+      const int s = slots ? slots[b] : b;
+      if (done[b] != n_tok) continue;  // reference leaves the buffer untouched
+      if (cudaMemcpyAsync(logits + (size_t)b * e.d.V, e.logits + (size_t)s * e.d.V, sizeof(float) * e.d.V,
+                          dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, e.stream) != cudaSuccess) {
+        set_error("logits copy failed");
+        return -4;
+      }
+    }
+  }
+  return finish(e, !dev);
+}
+
+Engine *load_stream(const char *path, int num_heads, int max_seqs, int device, int precision) {
+  clear_error();
+  if (!path) {
+    set_error("filepath is NULL");
+    return nullptr;
+  }
+  FILE *f = fopen(path, "rb");
+  if (!f) {
+    set_error("cannot open %s", path);
+    return nullptr;
+  }
+  unsigned char hdr[28];
+  if (fread(hdr, 1, 28, f) != 28) {
+    fclose(f);
+    set_error("%s: short header", path);
+    return nullptr;
+  }
+  // magic: the non-NUL characters of the first 8 bytes (core/cortex.nim:986-990)
+  std::string magic;
+  for (int i = 0; i < 8; ++i)
+    if (hdr[i]) magic.push_back((char)hdr[i]);
+  if (magic != "SNAI_V4") {
+    fclose(f);
+    set_error("%s: magic is not SNAI_V4", path);
+    return nullptr;
+  }
+  uint32_t p[5];
+  for (int i = 0; i < 5; ++i)
+    p[i] = (uint32_t)hdr[8 + 4 * i] | ((uint32_t)hdr[9 + 4 * i] << 8) | ((uint32_t)hdr[10 + 4 * i] << 16) |
+           ((uint32_t)hdr[11 + 4 * i] << 24);
+  const uint32_t vocab = p[0], dim = p[1], ffn = p[2], ctx = p[3], layers = p[4];
+  if (vocab > (uint32_t)std::numeric_limits<int>::max() || dim > 65536 || ctx > (1u << 24) || layers > 4096) {
+    fclose(f);
+    set_error("%s: header values out of range", path);
+    return nullptr;
+  }
+  if ((uint64_t)ffn > 4ull * dim) {
+    // the reference would read ffn*dim floats into a 4*dim*dim buffer
+    fclose(f);
+    set_error("%s: ffn_dim %u > 4 * hidden_dim %u", path, ffn, dim);
+    return nullptr;
+  }
+  Dims d;
+  if (!make_dims((int)vocab, (int)dim, (int)ctx, (int)layers, num_heads, &d)) {
+    fclose(f);
+    return nullptr;
+  }
+  Engine *e = create_engine(d, max_seqs, device, precision);
+  if (!e) {
+    fclose(f);
+    return nullptr;
+  }
+  DeviceGuard g(e->device);
+  const size_t kChunk = 16u << 20;  // floats per staging round
+  std::vector<float> stage;
+  stage.resize(std::min<size_t>(kChunk, (size_t)vocab * dim + 16));
+  bool ok = true;
+  auto blast = [&](float *dst, size_t n) {
+    // core/cortex.nim:998-1000: read n floats or fail
+    for (size_t done = 0; ok && done < n;) {
+      const size_t c = std::min(stage.size(), n - done);
+      if (fread(stage.data(), sizeof(float), c, f) != c) {
+        ok = false;
+        break;
+      }
+      if (cudaMemcpy(dst + done, stage.data(), c * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+        ok = false;
+        break;
+      }
+      done += c;
+    }
+  };
+  const size_t D = dim, FF = (size_t)ffn * dim;
+  blast(e->emb, (size_t)vocab * D);
+  blast(e->w_out, (size_t)vocab * D);
+  blast(e->rms_final, D);
+  for (uint32_t l = 0; ok && l < layers; ++l) {
+    LayerWeights &w = e->layers[l];
+    blast(w.rms_att, D);
+    blast(w.rms_ffn, D);
+    blast(w.wqkv, D * D);
+    blast(w.wqkv + D * D, D * D);
+    blast(w.wqkv + 2 * D * D, D * D);
+    blast(w.wo, D * D);
+    blast(w.wup, FF);
+    blast(w.wdown, FF);
+  }
+  fclose(f);
+  if (!ok) {
+    set_error("%s: file ends before all tensors were read", path);
+    free_engine(e);
+    return nullptr;
+  }
+  if (refresh_bf16(*e) || cudaStreamSynchronize(e->stream) != cudaSuccess) {
+    set_error("weight conversion failed: %s", cudaGetErrorString(cudaGetLastError()));
+    free_engine(e);
+    return nullptr;
+  }
+  return e;
+}
+
+int legacy_device() {
+  int d = env_int("SNAI_DEVICE", -1);
+  if (d >= 0) return d;
+  if (cudaGetDevice(&d) != cudaSuccess) d = 0;
+  return d;
+}
+
+int legacy_precision() { return env_int("SNAI_PRECISION", kFP32); }
+
+}  // namespace
+}  // namespace snai
+
+using namespace snai;
+
+// ============================================================================
+// Part 1 - reference boundary
+// ============================================================================
+
+extern "C" void *cortex_init(int vocab_size, int hidden_dim, int ctx_size, int num_layers, int num_heads) {
+  return cortex_init_ex(vocab_size, hidden_dim, ctx_size, num_layers, num_heads, 1, legacy_device(),
+                        legacy_precision());
+}
+
+extern "C" void *cortex_load_stream(const char *filepath, int num_heads) {
+  return load_stream(filepath, num_heads, 1, legacy_device(), legacy_precision());
+}
+
+extern "C" void cortex_forward(void *state, int *raw_tokens, int num_tokens, float *raw_logits) {
+  if (!state) return;
+  Engine &e = *static_cast<Engine *>(state);
+  const int zero = 0;
+  // logits are copied only if the call's last token was processed (:555)
+  const int rc = forward_batch(e, raw_tokens, 1, num_tokens, &zero, raw_logits, SNAI_HOST_PTRS);
+  if (rc != 0) {
+    fprintf(stderr, "libcortex: cortex_forward failed: %s\n", g_err.c_str());
+    if (raw_logits)
+      for (int v = 0; v < e.d.V; ++v) raw_logits[v] = std::numeric_limits<float>::quiet_NaN();
+  }
+}
+
+extern "C" void cortex_reset_cache(void *state) {
+  if (!state) return;
+  const int zero = 0;
+  cortex_seq_reset(state, &zero, 1);
+}
+
+extern "C" void cortex_free(void *state) { free_engine(static_cast<Engine *>(state)); }
+
+extern "C" void cortex_init_gpu(void) {
+  clear_error();
+  int ndev = 0;
+  cudaError_t err = cudaGetDeviceCount(&ndev);
+  if (err != cudaSuccess || ndev == 0) {
+    set_error("cortex_init_gpu: no CUDA device (%s)", cudaGetErrorString(err));
+    fprintf(stderr, "libcortex: %s\n", g_err.c_str());
+    return;
+  }
+  const int d = env_int("SNAI_DEVICE", 0);
+  err = cudaSetDevice(d);
+  if (err == cudaSuccess) err = cudaFree(nullptr);
+  if (err != cudaSuccess) {
+    set_error("cortex_init_gpu: device %d: %s", d, cudaGetErrorString(err));
+    fprintf(stderr, "libcortex: %s\n", g_err.c_str());
+  }
+}
+
+extern "C" int get_vocab_size(void *state) { return state ? static_cast<Engine *>(state)->d.V : 0; }
+extern "C" int get_ctx_size(void *state) { return state ? static_cast<Engine *>(state)->d.ctx : 0; }
+
+extern "C" void cortex_load_layer(void *state, int layer_idx, int tensor_type, float *raw_weights, int num_weights) {
+  if (!state || !raw_weights) return;
+  Engine &e = *static_cast<Engine *>(state);
+  size_t n = 0;
+  float *p = tensor_ptr(e, layer_idx, tensor_type, &n);
+  if (!p || (size_t)num_weights != n) return;  // core/cortex.nim:465: silent on mismatch
+  DeviceGuard g(e.device);
+  cudaStreamSynchronize(e.stream);
+  cudaMemcpy(p, raw_weights, n * sizeof(float), cudaMemcpyHostToDevice);
+  if (__nv_bfloat16 *h = tensor_ptr_h(e, layer_idx, tensor_type)) {
+    convert_bf16(e, p, h, n);
+    cudaStreamSynchronize(e.stream);
+  }
+}
+
+extern "C" void cortex_extract_layer(void *state, int layer_idx, int tensor_type, float *raw_weights,
+                                     int num_weights) {
+  if (!state || !raw_weights) return;
+  Engine &e = *static_cast<Engine *>(state);
+  size_t n = 0;
+  float *p = tensor_ptr(e, layer_idx, tensor_type, &n);
+  if (!p || (size_t)num_weights != n) return;
+  DeviceGuard g(e.device);
+  cudaStreamSynchronize(e.stream);
+  cudaMemcpy(raw_weights, p, n * sizeof(float), cudaMemcpyDeviceToHost);
+}
+
+extern "C" void cortex_load_adam_layer(void *state, int layer_idx, int tensor_type, bool is_variance, float *raw,
+                                       int size) {
+  if (!state || !raw) return;
+  Engine &e = *static_cast<Engine *>(state);
+  size_t n = 0;
+  if (!tensor_ptr(e, layer_idx, tensor_type, &n) || (size_t)size != n) return;
+  auto &buf = e.adam[std::make_tuple(layer_idx, tensor_type, is_variance ? 1 : 0)];
+  buf.assign(raw, raw + n);
+}
+
+extern "C" void cortex_extract_adam_layer(void *state, int layer_idx, int tensor_type, bool is_variance, float *raw,
+                                          int size) {
+  if (!state || !raw) return;
+  Engine &e = *static_cast<Engine *>(state);
+  size_t n = 0;
+  if (!tensor_ptr(e, layer_idx, tensor_type, &n) || (size_t)size != n) return;
+  auto it = e.adam.find(std::make_tuple(layer_idx, tensor_type, is_variance ? 1 : 0));
+  if (it == e.adam.end())
+    std::fill(raw, raw + n, 0.0f);  // fresh moments are zero (allocShared0)
+  else
+    std::copy(it->second.begin(), it->second.end(), raw);
+}
+
+extern "C" float cortex_train_step(void *, int *, int *, int, float) {
+  set_error("cortex_train_step: training is not part of this library (decode engine only)");
+  return std::numeric_limits<float>::quiet_NaN();
+}
+
+// ============================================================================
+// Part 2 - batched extension
+// ============================================================================
+
+extern "C" const char *cortex_last_error(void) { return g_err.c_str(); }
+
+extern "C" void *cortex_load_stream_ex(const char *filepath, int num_heads, int max_seqs, int device, int precision) {
+  return load_stream(filepath, num_heads, max_seqs, device, precision);
+}
+
+extern "C" void *cortex_init_ex(int vocab_size, int hidden_dim, int ctx_size, int num_layers, int num_heads,
+                                int max_seqs, int device, int precision) {
+  clear_error();
+  Dims d;
+  if (!make_dims(vocab_size, hidden_dim, ctx_size, num_layers, num_heads, &d)) return nullptr;
+  Engine *e = create_engine(d, max_seqs, device, precision);
+  if (e && refresh_bf16(*e)) {
+    free_engine(e);
+    return nullptr;
+  }
+  return e;
+}
+
+extern "C" int cortex_num_slots(void *state) { return state ? static_cast<Engine *>(state)->max_seqs : 0; }
+extern "C" int cortex_head_size(void *state) { return state ? static_cast<Engine *>(state)->d.hs : 0; }
+extern "C" int cortex_num_heads(void *state) { return state ? static_cast<Engine *>(state)->d.heads : 0; }
+
+extern "C" int cortex_seq_reset(void *state, const int *slots, int n) {
+  clear_error();
+  if (!state) {
+    set_error("state is NULL");
+    return -1;
+  }
+  Engine &e = *static_cast<Engine *>(state);
+  if (!slots) {
+    std::fill(e.pos.begin(), e.pos.end(), 0);
+    std::fill(e.logits_valid.begin(), e.logits_valid.end(), 0);
+  } else {
+    for (int i = 0; i < n; ++i) {
+      if (slots[i] < 0 || slots[i] >= e.max_seqs) {
+        set_error("slot %d out of range", slots[i]);
+        return -2;
+      }
+      e.pos[slots[i]] = 0;
+      e.logits_valid[slots[i]] = 0;
+    }
+  }
+  DeviceGuard g(e.device);
+  if (upload_seq_len(e)) {
+    set_error("cudaMemcpy failed");
+    return -4;
+  }
+  return finish(e, true);
+}
+
+extern "C" int cortex_seq_pos(void *state, int slot) {
+  if (!state) return -1;
+  Engine &e = *static_cast<Engine *>(state);
+  if (slot < 0 || slot >= e.max_seqs) return -1;
+  return e.pos[slot];
+}
+
+extern "C" int cortex_forward_batch(void *state, const int *tokens, int batch, int n_tok, const int *slots,
+                                    float *logits, int flags) {
+  if (!state) {
+    set_error("state is NULL");
+    return -1;
+  }
+  return forward_batch(*static_cast<Engine *>(state), tokens, batch, n_tok, slots, logits, flags);
+}
+
+extern "C" int cortex_decode_batch(void *state, const int *slots, int batch, const float *uniforms,
+                                   const snai_sample_params *params, int *out_ids, int flags) {
+  clear_error();
+  if (!state || !params || !out_ids) {
+    set_error("state, params and out_ids must not be NULL");
+    return -1;
+  }
+  Engine &e = *static_cast<Engine *>(state);
+  if (batch < 0 || batch > e.max_seqs) {
+    set_error("batch %d outside [0, %d]", batch, e.max_seqs);
+    return -2;
+  }
+  if (batch == 0) return 0;
+  if (!slots_ok(e, slots, batch)) return -2;
+  for (int b = 0; b < batch; ++b) {
+    const int s = slots ? slots[b] : b;
+    if (!e.logits_valid[s]) {
+      set_error("slot %d has no logits yet (feed its prompt first)", s);
+      return -2;
+    }
+  }
+  const bool dev = flags & SNAI_DEVICE_PTRS;
+  DeviceGuard g(e.device);
+  std::vector<int> sl(batch);
+  for (int b = 0; b < batch; ++b) sl[b] = slots ? slots[b] : b;
+  if (cudaMemcpyAsync(e.slots_d, sl.data(), sizeof(int) * batch, cudaMemcpyHostToDevice, e.stream) != cudaSuccess) {
+    set_error("slot upload failed");
+    return -4;
+  }
+  const float *u = uniforms;
+  if (uniforms && !dev) {
+    if (cudaMemcpyAsync(e.unif_d, uniforms, sizeof(float) * batch, cudaMemcpyHostToDevice, e.stream) !=
+        cudaSuccess) {
+      set_error("uniform upload failed");
+      return -4;
+    }
+    u = e.unif_d;
+  }
+  SampleLaunch s;
+  s.logits = e.logits;
+  s.ld = e.d.V;
+  s.row_map = e.slots_d;
+  s.rows = batch;
+  s.V = e.d.V;
+  s.hist = e.hist;
+  s.hist_ld = e.d.ctx;
+  s.hist_cols = e.d.ctx;
+  s.hist_len = e.seq_len_d;
+  s.uniforms = u;
+  s.variant = params->variant;
+  s.temperature = params->temperature;
+  s.rep = params->rep_penalty;
+  s.top_k = params->top_k;
+  s.top_p = params->top_p;
+  s.nan_guard = params->nan_guard;
+  s.out_ids = e.ids_d;
+  s.err = e.err_d;
+  double hist_total = 0;
+  for (int b = 0; b < batch; ++b) hist_total += e.pos[sl[b]];
+  const int ptok = prof_begin(e);
+  int rc = launch_sampler(s, e.stream);
+  if (rc) return rc;
+  e.launches++;
+  prof_end(e, ptok, kProfSampler, 4.0 * batch * e.d.V + 4.0 * hist_total + 12.0 * batch, 0.0);
+  std::vector<RowDesc> rows;
+  rows.reserve(batch);
+  for (int b = 0; b < batch; ++b) {
+    const int sl_b = sl[b];
+    if (e.pos[sl_b] >= e.d.ctx) continue;
+    rows.push_back(RowDesc{sl_b, e.pos[sl_b], b, sl_b});
+  }
+  rc = run_rows(e, rows.data(), (int)rows.size(), e.ids_d);
+  if (rc) return rc;
+  for (const RowDesc &r : rows) e.pos[r.slot] += 1;
+  if (cudaMemcpyAsync(out_ids, e.ids_d, sizeof(int) * batch, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                      e.stream) != cudaSuccess) {
+    set_error("id copy failed");
+    return -4;
+  }
+  return finish(e, !dev);
+}
+
+extern "C" int cortex_get_logits(void *state, const int *slots, int n, float *out) {
+  clear_error();
+  if (!state || !out) {
+    set_error("state and out must not be NULL");
+    return -1;
+  }
+  Engine &e = *static_cast<Engine *>(state);
+  DeviceGuard g(e.device);
+  for (int i = 0; i < n; ++i) {
+    const int s = slots ? slots[i] : i;
+    if (s < 0 || s >= e.max_seqs) {
+      set_error("slot %d out of range", s);
+      return -2;
+    }
+    cudaMemcpyAsync(out + (size_t)i * e.d.V, e.logits + (size_t)s * e.d.V, sizeof(float) * e.d.V,
+                    cudaMemcpyDeviceToHost, e.stream);
+  }
+  return finish(e, true);
+}
+
+extern "C" int cortex_sample(const float *logits, int rows, int vocab, long long ld, const int *hist, int hist_cols,
+                             const int *hist_len, const float *uniforms, const snai_sample_params *params,
+                             int *out_ids, void *stream) {
+  clear_error();
+  if (!params) {
+    set_error("params is NULL");
+    return -1;
+  }
+  SampleLaunch s;
+  s.logits = logits;
+  s.ld = ld;
+  s.rows = rows;
+  s.V = vocab;
+  s.hist = hist;
+  s.hist_ld = hist_cols;
+  s.hist_cols = hist_cols;
+  s.hist_len = hist_len;
+  s.uniforms = uniforms;
+  s.variant = params->variant;
+  s.temperature = params->temperature;
+  s.rep = params->rep_penalty;
+  s.top_k = params->top_k;
+  s.top_p = params->top_p;
+  s.nan_guard = params->nan_guard;
+  s.out_ids = out_ids;
+  return launch_sampler(s, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cortex_set_stream(void *state, void *stream) {
+  if (!state) return -1;
+  Engine &e = *static_cast<Engine *>(state);
+  e.stream = stream ? static_cast<cudaStream_t>(stream) : e.own_stream;
+  return 0;
+}
+
+extern "C" int cortex_synchronize(void *state) {
+  clear_error();
+  if (!state) {
+    set_error("state is NULL");
+    return -1;
+  }
+  Engine &e = *static_cast<Engine *>(state);
+  DeviceGuard g(e.device);
+  return finish(e, true);
+}
+
+extern "C" int cortex_seq_rewind(void *state, const int *slots, int n, int pos) {
+  clear_error();
+  if (!state) {
+    set_error("state is NULL");
+    return -1;
+  }
+  Engine &e = *static_cast<Engine *>(state);
+  for (int i = 0; i < n; ++i) {
+    const int s = slots ? slots[i] : i;
+    if (s < 0 || s >= e.max_seqs) {
+      set_error("slot %d out of range", s);
+      return -2;
+    }
+    if (pos < 0 || pos > e.pos[s]) {
+      set_error("slot %d: cannot rewind from %d to %d", s, e.pos[s], pos);
+      return -2;
+    }
+  }
+  for (int i = 0; i < n; ++i) e.pos[slots ? slots[i] : i] = pos;
+  DeviceGuard g(e.device);
+  if (upload_seq_len(e)) {
+    set_error("cudaMemcpy failed");
+    return -4;
+  }
+  return finish(e, false);
+}
+
+extern "C" int cortex_profile_enable(void *state, int on) {
+  if (!state) return -1;
+  Engine &e = *static_cast<Engine *>(state);
+  DeviceGuard g(e.device);
+  prof_collect(e);
+  for (int k = 0; k < 16; ++k) {
+    e.prof_count[k] = 0;
+    e.prof_ms[k] = e.prof_bytes[k] = e.prof_flops[k] = 0.0;
+  }
+  e.prof = on != 0;
+  return 0;
+}
+
+extern "C" int cortex_profile_read(void *state, int kind, long long *launches, double *ms, double *bytes,
+                                   double *flops) {
+  if (!state || kind < 0 || kind >= kProfKinds) return -1;
+  Engine &e = *static_cast<Engine *>(state);
+  DeviceGuard g(e.device);
+  prof_collect(e);
+  if (launches) *launches = e.prof_count[kind];
+  if (ms) *ms = e.prof_ms[kind];
+  if (bytes) *bytes = e.prof_bytes[kind];
+  if (flops) *flops = e.prof_flops[kind];
+  return 0;
+}
+
+extern "C" long long cortex_kernel_launches(void *state) {
+  return state ? static_cast<Engine *>(state)->launches : 0;
+}

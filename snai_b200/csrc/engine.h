@@ -1,0 +1,157 @@
+// engine.h - internal state of a libcortex decode engine (host side).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+
+namespace snai {
+
+enum Precision { kFP32 = 0, kTF32 = 1, kBF16 = 2 };
+
+// Shape of a model.  Rules of core/cortex.nim:261-271: ffn = 4*dim whatever
+// the file header says; head size hs = dim/heads forced even and >= 2; RoPE
+// rotates dim/hs heads (core/cortex.nim:75); attention uses `heads` heads, so
+// only the first heads*hs channels of q, k, v are ever read.
+struct Dims {
+  int V = 0, D = 0, F = 0, ctx = 0, L = 0;
+  int heads = 0, hs = 0;
+  int att_ch = 0;  // heads * hs
+};
+
+// One row of a forward pass: a token at a cache position of a slot.
+// `out` >= 0 asks for the logits of this row in logits slot `out`.
+// When the pass takes tokens from a device array, `token` is the index into it.
+struct RowDesc {
+  int slot, pos, token, out;
+};
+
+struct LayerWeights {
+  float *rms_att = nullptr, *rms_ffn = nullptr;
+  float *wqkv = nullptr;  // [3D, D]: Wq, Wk, Wv stacked (their file order)
+  float *wo = nullptr;    // [D, D]
+  float *wup = nullptr;   // [F, D]
+  float *wdown = nullptr; // [D, F]
+  __nv_bfloat16 *wqkv_h = nullptr, *wo_h = nullptr, *wup_h = nullptr, *wdown_h = nullptr;
+};
+
+struct Engine {
+  Dims d;
+  int device = 0;
+  int precision = kFP32;
+  int max_seqs = 1;
+  int m_max = 0;  // rows per forward chunk
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+
+  // weights (fp32 masters; bf16 copies in BF16 mode)
+  void *wblock = nullptr;
+  void *hblock = nullptr;
+  float *emb = nullptr, *w_out = nullptr, *rms_final = nullptr;
+  __nv_bfloat16 *w_out_h = nullptr;
+  std::vector<LayerWeights> layers;
+
+  // KV cache: kv[slot][layer][k|v][head][ctx][hs] fp32
+  float *kv = nullptr;
+  size_t kv_slot_stride = 0, kv_layer_stride = 0, kv_part_stride = 0, kv_head_stride = 0;
+
+  // RoPE table [ctx][hs/2] of (cos, sin), computed on the host with the
+  // reference's float expressions (core/cortex.nim:79-82).
+  float2 *rope = nullptr;
+  float sqrt_hs = 1.f;  // sqrtf(hs), the attention score divisor (:521)
+
+  // activations for m_max rows
+  void *ablock = nullptr;
+  RowDesc *rows_d = nullptr;
+  int2 *outrows_d = nullptr;  // (chunk row, logits slot)
+  float *h = nullptr;         // [m_max, D] residual stream
+  void *x = nullptr;          // [m_max, D] normed input of a projection (fp32 or bf16)
+  float *q = nullptr;         // [m_max, att_ch]
+  void *att = nullptr;        // [m_max, D]
+  void *u = nullptr;          // [m_max, F]
+  void *xo = nullptr;         // [m_max, D] normed rows that need logits
+  float *logits = nullptr;    // [max_seqs, V], per slot
+  int *hist = nullptr;        // [max_seqs, ctx] every token fed to the slot
+  int *seq_len_d = nullptr;   // [max_seqs] tokens fed (device copy of pos)
+  int *ids_d = nullptr;       // [max_seqs]
+  float *unif_d = nullptr;    // [max_seqs]
+  int *slots_d = nullptr;     // [max_seqs]
+  int *err_d = nullptr;       // device error word
+
+  // host staging of a chunk's rows.  Pageable on purpose: cudaMemcpyAsync
+  // from pageable memory returns once the source has been consumed, so the
+  // buffers can be refilled by the next call without waiting for the GPU.
+  std::vector<RowDesc> rows_stage;
+  std::vector<int2> out_stage;
+
+  // host mirrors
+  std::vector<int> pos;            // per slot
+  std::vector<char> logits_valid;  // per slot
+  std::map<std::tuple<int, int, int>, std::vector<float>> adam;  // (layer, type, is_v)
+  long long launches = 0;
+
+  // optional per-kernel-class timing (CUDA events on the engine stream)
+  bool prof = false;
+  struct ProfPending {
+    int kind;
+    cudaEvent_t a, b;
+    double bytes, flops;
+  };
+  std::vector<ProfPending> prof_pending;
+  std::vector<cudaEvent_t> prof_free;
+  long long prof_count[16] = {};
+  double prof_ms[16] = {}, prof_bytes[16] = {}, prof_flops[16] = {};
+};
+
+// Kernel classes of the profiler (cortex_profile_read `kind`).
+enum ProfKind : int {
+  kProfEmbed = 0, kProfNorm = 1, kProfQKV = 2, kProfAttention = 3, kProfWo = 4, kProfUp = 5, kProfDown = 6,
+  kProfLogits = 7, kProfSampler = 8, kProfKinds = 9
+};
+// Brackets one launch: returns a token for prof_end (or -1 when off).
+int prof_begin(Engine &e);
+void prof_end(Engine &e, int token, int kind, double bytes, double flops);
+// Folds finished events into the totals (synchronizes the stream).
+void prof_collect(Engine &e);
+
+// ---- error reporting (cortex_api.cu) ----
+void set_error(const char *fmt, ...);
+void clear_error();
+
+// ---- forward pass (forward.cu) ----
+// Runs rows[0..n) (each slot's positions ascending) through the model in
+// chunks of at most e.m_max rows.  If tokens_d is not null, row tokens are
+// tokens_d[row.token].  Returns 0 or a negative error.
+int run_rows(Engine &e, const RowDesc *rows, int n, const int *tokens_d);
+// fp32 -> bf16 copy of a weight tensor on e.stream.
+int convert_bf16(Engine &e, const float *src, __nv_bfloat16 *dst, size_t n);
+// Fills n floats with a value on e.stream.
+int fill_f32(Engine &e, float *dst, size_t n, float v);
+
+// ---- sampler (sampler.cu) ----
+struct SampleLaunch {
+  const float *logits = nullptr;
+  long long ld = 0;
+  const int *row_map = nullptr;  // row b reads logits/hist/hist_len row row_map[b]
+  int rows = 0, V = 0;
+  const int *hist = nullptr;
+  long long hist_ld = 0;
+  int hist_cols = 0;
+  const int *hist_len = nullptr;
+  const float *uniforms = nullptr;
+  int variant = 0;
+  double temperature = 1.0, rep = 1.0, top_p = 1.0;
+  int top_k = 1;
+  int nan_guard = 0;
+  int *out_ids = nullptr;
+  int *err = nullptr;
+};
+// Checks the arguments; returns 0 or a negative error (with set_error).
+int check_sample_args(const SampleLaunch &a);
+int launch_sampler(const SampleLaunch &a, cudaStream_t stream);
+
+}  // namespace snai

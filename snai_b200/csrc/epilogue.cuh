@@ -1,0 +1,114 @@
+// epilogue.cuh - what a projection does with its fp32 results.
+//
+// store(m, n, v, cnt) receives v[0..cnt) = C[m][n .. n+cnt) for an even n.
+// The element-wise arithmetic mirrors core/cortex.nim operation for
+// operation (explicit _rn intrinsics: no contraction into FMA), so the only
+// differences from the reference are the dot products' summation order.
+#pragma once
+
+#include "common.cuh"
+#include "engine.h"
+
+namespace snai {
+
+// Q|K|V = x * [Wq;Wk;Wv]^T.  RoPE on q and k (core/cortex.nim:74-87, applied
+// at :504 and :509), q to a row buffer, k and v appended to the cache at the
+// row's position (:506-510).  Channels >= heads*hs are never read by
+// attention and are dropped.
+struct EpiQKV {
+  const RowDesc *rows;
+  float *q;
+  float *kv;
+  const float2 *rope;
+  int D, att_ch, hs;
+  size_t slot_stride, layer_off, part_stride, head_stride;
+
+  __device__ __forceinline__ void pair(const RowDesc &rd, int m, int n, float a, float b) const {
+    const int part = n / D;
+    const int ch = n - part * D;
+    if (ch >= att_ch) return;
+    const int head = ch / hs;
+    const int j = ch - head * hs;
+    if (part < 2) {
+      const float2 cs = rope[(size_t)rd.pos * (hs >> 1) + (j >> 1)];
+      const float a2 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+      const float b2 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+      a = a2;
+      b = b2;
+    }
+    if (part == 0) {
+      *reinterpret_cast<float2 *>(q + (size_t)m * att_ch + ch) = make_float2(a, b);
+    } else {
+      float *dst = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)(part - 1) * part_stride +
+                   (size_t)head * head_stride + (size_t)rd.pos * hs + j;
+      *reinterpret_cast<float2 *>(dst) = make_float2(a, b);
+    }
+  }
+
+  __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
+    const RowDesc rd = rows[m];
+#pragma unroll
+    for (int i = 0; i + 1 < 16; i += 2)
+      if (i + 1 < cnt) pair(rd, m, n + i, v[i], v[i + 1]);
+  }
+};
+
+// h += C  (residual adds after Wo and W_down, core/cortex.nim:541-542, 550-551)
+struct EpiResidual {
+  float *h;
+  int ld;
+  __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
+    float *p = h + (size_t)m * ld + n;
+    if (cnt == 16 && (ld & 3) == 0) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        float4 o = *reinterpret_cast<float4 *>(p + i);
+        o.x = __fadd_rn(o.x, v[i]);
+        o.y = __fadd_rn(o.y, v[i + 1]);
+        o.z = __fadd_rn(o.z, v[i + 2]);
+        o.w = __fadd_rn(o.w, v[i + 3]);
+        *reinterpret_cast<float4 *>(p + i) = o;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < cnt) p[i] = __fadd_rn(p[i], v[i]);
+    }
+  }
+};
+
+// u = SiLU(C) = C * (1 / (1 + exp(-C)))  (core/cortex.nim:545-548)
+template <typename TA>
+struct EpiSilu {
+  TA *u;
+  int ld;
+  __device__ static __forceinline__ float silu(float x) {
+    return __fmul_rn(x, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))));
+  }
+  __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
+    TA *p = u + (size_t)m * ld + n;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (i < cnt) ActIO<TA>::store(p + i, silu(v[i]));
+  }
+};
+
+// logits[out slot][n] = C  (core/cortex.nim:555-561)
+struct EpiLogits {
+  float *logits;
+  const int2 *outrows;  // chunk-local logits row -> (chunk row, slot)
+  long long ld;
+  __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
+    float *p = logits + (size_t)outrows[m].y * ld + n;
+    if (cnt == 16 && (ld & 3) == 0) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4 *>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < cnt) p[i] = v[i];
+    }
+  }
+};
+
+}  // namespace snai

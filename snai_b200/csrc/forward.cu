@@ -1,0 +1,587 @@
+// forward.cu - the .snai forward step on sm_100a (core/cortex.nim:487-563).
+//
+// A pass runs a list of rows (slot, position, token) through the model in
+// chunks.  Per chunk:
+//   embed_norm     h = E[token] (ids outside [0,V) read row 0, :493);
+//                  x = RMSNorm(h, rms_att[0]); hist[slot][pos] = token
+//   per layer l:   QKV projection -> RoPE, q rows, k/v appended to the cache
+//                  attention      -> att (per row and head, positions 0..pos)
+//                  Wo projection  -> h += .
+//                  rmsnorm        -> x = RMSNorm(h, rms_ffn[l])
+//                  W_up projection-> u = SiLU(.)
+//                  W_down proj.   -> h += .
+//                  rmsnorm        -> x = RMSNorm(h, rms_att[l+1])
+//   rows that need logits: x = RMSNorm(h, rms_final) -> W_out projection.
+// Projections with fewer than 64 rows (or in FP32 mode) run as fp32 GEMV;
+// larger ones as tcgen05 GEMMs (gemm_tc.cuh) in TF32 or BF16.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "engine.h"
+#include "epilogue.cuh"
+#include "gemm_tc.cuh"
+
+namespace snai {
+
+// ============================================================================
+// element-wise / row kernels
+// ============================================================================
+
+__global__ void fill_f32_kernel(float *dst, size_t n, float v) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) dst[i] = v;
+}
+
+__global__ void to_bf16_kernel(const float *__restrict__ src, __nv_bfloat16 *__restrict__ dst, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+constexpr int kNormThreads = 256;
+
+// Block sum of squares of a D-vector (parallel tree; the reference sums
+// sequentially, core/cortex.nim:119).
+__device__ __forceinline__ float block_sumsq(const float *x, int D, float *red) {
+  float s = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) s = __fmaf_rn(x[i], x[i], s);
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+  __syncthreads();
+  return t;
+}
+
+// 1 / sqrt(ss/D + 1e-5), in the reference's float operations (:121).
+__device__ __forceinline__ float rms_inv(float ss, int D) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
+}
+
+template <typename TA>
+__global__ void __launch_bounds__(kNormThreads) embed_norm_kernel(const RowDesc *__restrict__ rows,
+                                                                  const int *__restrict__ tokens_d,
+                                                                  const float *__restrict__ emb,
+                                                                  const float *__restrict__ w, float *__restrict__ h,
+                                                                  TA *__restrict__ x, int *__restrict__ hist,
+                                                                  int *__restrict__ seq_len, int V, int D, int ctx) {
+  __shared__ float red[kNormThreads / 32];
+  const int m = blockIdx.x;
+  const RowDesc rd = rows[m];
+  const int raw = tokens_d ? tokens_d[rd.token] : rd.token;
+  const int tid = (raw < 0 || raw >= V) ? 0 : raw;
+  const float *e = emb + (size_t)tid * D;
+  float *hr = h + (size_t)m * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) hr[i] = e[i];
+  if (threadIdx.x == 0) {
+    hist[(size_t)rd.slot * ctx + rd.pos] = raw;
+    atomicMax(&seq_len[rd.slot], rd.pos + 1);
+  }
+  __syncthreads();
+  const float inv = rms_inv(block_sumsq(hr, D, red), D);
+  TA *xr = x + (size_t)m * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) ActIO<TA>::store(xr + i, __fmul_rn(__fmul_rn(hr[i], inv), w[i]));
+}
+
+// x[i] = RMSNorm(h[src(i)], w); src(i) = i, or outrows[i].x when gathering.
+template <typename TA>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *__restrict__ h, const int2 *__restrict__ gather,
+                                                               const float *__restrict__ w, TA *__restrict__ x, int D) {
+  __shared__ float red[kNormThreads / 32];
+  const int m = blockIdx.x;
+  const int src = gather ? gather[m].x : m;
+  const float *hr = h + (size_t)src * D;
+  const float inv = rms_inv(block_sumsq(hr, D, red), D);
+  TA *xr = x + (size_t)m * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) ActIO<TA>::store(xr + i, __fmul_rn(__fmul_rn(hr[i], inv), w[i]));
+}
+
+// ============================================================================
+// attention over the KV cache (core/cortex.nim:512-538)
+// ============================================================================
+//
+// One CTA per (row, head).  Scores s_t = (q . k_t) / sqrtf(hs) for t <= pos go
+// to shared memory; max starts at -9999 as in the reference (:517); then
+// e_t = exp(s_t - max), the sum, w_t = e_t / sum, and att = sum_t w_t v_t.
+// Channels >= heads*hs of att are zero (:512-513).
+//
+// Fast path HS = 64: a warp reads two positions per load instruction (16
+// lanes x 16 bytes per 256-byte key row), so every load is a contiguous
+// 512-byte span of the head-major cache.
+
+constexpr int kAttThreads = 128;
+
+template <typename TA>
+__device__ __forceinline__ void att_zero_tail(TA *out_row, int att_ch, int D) {
+  for (int c = att_ch + threadIdx.x; c < D; c += blockDim.x) ActIO<TA>::store(out_row + c, 0.f);
+}
+
+// softmax over s[0..n) in place: s_t <- exp(s_t - max)/sum.  Returns nothing;
+// uses red[32] scratch.
+__device__ __forceinline__ void att_softmax(float *s, int n, float *red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  float mx = -9999.0f;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) mx = fmaxf(mx, s[t]);
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < nw; ++w) mx = fmaxf(mx, red[w]);
+  __syncthreads();
+  float sum = 0.f;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const float e = expf(__fsub_rn(s[t], mx));
+    s[t] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) red[warp] = sum;
+  __syncthreads();
+  sum = 0.f;
+  for (int w = 0; w < nw; ++w) sum += red[w];
+  for (int t = threadIdx.x; t < n; t += blockDim.x) s[t] = __fdiv_rn(s[t], sum);
+  __syncthreads();
+}
+
+template <typename TA>
+__global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
+    const RowDesc *__restrict__ rows, const float *__restrict__ q, const float *__restrict__ kv, TA *__restrict__ out,
+    int D, int att_ch, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride, float sqrt_hs) {
+  constexpr int HS = 64;
+  extern __shared__ float smem_att[];
+  float *red = smem_att;        // [32]
+  float *acc = smem_att + 32;   // [4 warps][64]
+  float *s = smem_att + 32 + 4 * HS;
+  const int m = blockIdx.y, head = blockIdx.x;
+  const RowDesc rd = rows[m];
+  const int n = rd.pos + 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int half = lane >> 4, part = lane & 15;
+
+  const float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
+  const float *vbase = kbase + part_stride;
+  const float4 qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + part * 4);
+
+  // ---- scores: warp w takes position pairs w, w+4, ...; 8 pairs per sweep ----
+  constexpr int U = 8;
+  for (int p0 = warp * U; 2 * p0 < n; p0 += 4 * U) {
+    float4 kr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = 2 * (p0 + u) + half;
+      kr[u] = t < n ? __ldcs(reinterpret_cast<const float4 *>(kbase + (size_t)t * HS + part * 4))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float d = qv.x * kr[u].x + qv.y * kr[u].y + qv.z * kr[u].z + qv.w * kr[u].w;
+      d += __shfl_xor_sync(0xffffffffu, d, 8);
+      d += __shfl_xor_sync(0xffffffffu, d, 4);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      const int t = 2 * (p0 + u) + half;
+      if (part == 0 && t < n) s[t] = __fdiv_rn(d, sqrt_hs);
+    }
+  }
+  __syncthreads();
+  att_softmax(s, n, red);
+
+  // ---- weighted sum of values ----
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int p0 = warp * U; 2 * p0 < n; p0 += 4 * U) {
+    float4 vr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = 2 * (p0 + u) + half;
+      vr[u] = t < n ? __ldcs(reinterpret_cast<const float4 *>(vbase + (size_t)t * HS + part * 4))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = 2 * (p0 + u) + half;
+      const float wt = t < n ? s[t] : 0.f;
+      a.x = __fadd_rn(a.x, __fmul_rn(vr[u].x, wt));
+      a.y = __fadd_rn(a.y, __fmul_rn(vr[u].y, wt));
+      a.z = __fadd_rn(a.z, __fmul_rn(vr[u].z, wt));
+      a.w = __fadd_rn(a.w, __fmul_rn(vr[u].w, wt));
+    }
+  }
+  a.x += __shfl_xor_sync(0xffffffffu, a.x, 16);
+  a.y += __shfl_xor_sync(0xffffffffu, a.y, 16);
+  a.z += __shfl_xor_sync(0xffffffffu, a.z, 16);
+  a.w += __shfl_xor_sync(0xffffffffu, a.w, 16);
+  if (half == 0) *reinterpret_cast<float4 *>(acc + warp * HS + part * 4) = a;
+  __syncthreads();
+  TA *orow = out + (size_t)m * D;
+  if (threadIdx.x < HS) {
+    const float r = acc[threadIdx.x] + acc[HS + threadIdx.x] + acc[2 * HS + threadIdx.x] + acc[3 * HS + threadIdx.x];
+    ActIO<TA>::store(orow + head * HS + threadIdx.x, r);
+  }
+  if (head == gridDim.x - 1) att_zero_tail(orow, att_ch, D);
+}
+
+// Any even head size: threads take positions for the scores and channels for
+// the weighted sum.
+template <typename TA>
+__global__ void __launch_bounds__(kAttThreads) attention_generic_kernel(
+    const RowDesc *__restrict__ rows, const float *__restrict__ q, const float *__restrict__ kv, TA *__restrict__ out,
+    int D, int att_ch, int hs, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride,
+    float sqrt_hs) {
+  extern __shared__ float smem_att[];
+  float *red = smem_att;
+  float *s = smem_att + 32;
+  const int m = blockIdx.y, head = blockIdx.x;
+  const RowDesc rd = rows[m];
+  const int n = rd.pos + 1;
+  const float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
+  const float *vbase = kbase + part_stride;
+  const float *qr = q + (size_t)m * att_ch + (size_t)head * hs;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const float *kr = kbase + (size_t)t * hs;
+    float d = 0.f;
+    for (int j = 0; j < hs; ++j) d = __fadd_rn(d, __fmul_rn(qr[j], kr[j]));
+    s[t] = __fdiv_rn(d, sqrt_hs);
+  }
+  __syncthreads();
+  att_softmax(s, n, red);
+  TA *orow = out + (size_t)m * D;
+  for (int j = threadIdx.x; j < hs; j += blockDim.x) {
+    float a = 0.f;
+    for (int t = 0; t < n; ++t) a = __fadd_rn(a, __fmul_rn(vbase[(size_t)t * hs + j], s[t]));
+    ActIO<TA>::store(orow + (size_t)head * hs + j, a);
+  }
+  if (head == gridDim.x - 1) att_zero_tail(orow, att_ch, D);
+}
+
+// ============================================================================
+// fp32 GEMV for small row counts: C[M,N] = X[M,K] * W[N,K]^T
+// ============================================================================
+//
+// Each warp owns two adjacent weight rows (a RoPE pair), streams them once
+// with 16-byte loads (lane k-slices of 4), and multiplies them with up to MB
+// activation rows per sweep; activation rows are re-read through L1/L2.
+
+constexpr int kGemvWarps = 8;
+
+template <int MB, class Epi>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_f32_kernel(const float *__restrict__ W, int N, int K,
+                                                                   const float *__restrict__ X, int M, Epi epi) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = (blockIdx.x * kGemvWarps + warp) * 2;
+  if (n0 >= N) return;
+  const bool two = n0 + 1 < N;
+  const float *w0 = W + (size_t)n0 * K;
+  const float *w1 = two ? w0 + K : w0;
+  for (int m0 = 0; m0 < M; m0 += MB) {
+    float a0[MB], a1[MB];
+#pragma unroll
+    for (int j = 0; j < MB; ++j) a0[j] = a1[j] = 0.f;
+#pragma unroll 2
+    for (int k = lane * 4; k < K; k += 128) {
+      const float4 wa = __ldcs(reinterpret_cast<const float4 *>(w0 + k));
+      const float4 wb = __ldcs(reinterpret_cast<const float4 *>(w1 + k));
+#pragma unroll
+      for (int j = 0; j < MB; ++j) {
+        if (m0 + j < M) {
+          const float4 xv = __ldg(reinterpret_cast<const float4 *>(X + (size_t)(m0 + j) * K + k));
+          a0[j] = fmaf(wa.x, xv.x, fmaf(wa.y, xv.y, fmaf(wa.z, xv.z, fmaf(wa.w, xv.w, a0[j]))));
+          a1[j] = fmaf(wb.x, xv.x, fmaf(wb.y, xv.y, fmaf(wb.z, xv.z, fmaf(wb.w, xv.w, a1[j]))));
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < MB; ++j) {
+      a0[j] = warp_sum(a0[j]);
+      a1[j] = warp_sum(a1[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < MB; ++j) {
+      if (lane == j && m0 + j < M) {
+        float v[16] = {a0[j], a1[j]};
+        epi.store(m0 + j, n0, v, two ? 2 : 1);
+      }
+    }
+  }
+}
+
+// ============================================================================
+// host side
+// ============================================================================
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D K-major operand [rows][K] with 128-byte-wide, box_rows-high boxes.
+static bool make_tmap(CUtensorMap *map, const void *base, bool bf16, int K, int rows, int box_rows) {
+  auto enc = get_encode_fn();
+  if (!enc) return false;
+  const size_t es = bf16 ? 2 : 4;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * es};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                   const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static bool tc_path(const Engine &e, int M) {
+  return e.precision != kFP32 && M >= 64 && e.d.D % 16 == 0 && e.d.D >= 64;
+}
+
+constexpr int kTcBN = 128;
+constexpr int kTcStages = 3;
+
+template <typename TIn, class Epi>
+static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
+  using Sm = TcSmem<kTcBN, kTcStages>;
+  auto kern = gemm_tc_kernel<TIn, kTcBN, kTcStages, 2, Epi>;
+  static unsigned long long attr_set = 0;  // per instantiation, one bit per device
+  if (!(attr_set & (1ull << e.device))) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Sm::kBytes) != cudaSuccess) {
+      set_error("cudaFuncSetAttribute failed for the tensor-core GEMM");
+      return -5;
+    }
+    attr_set |= 1ull << e.device;
+  }
+  CUtensorMap ta, tb;
+  const bool bf = sizeof(TIn) == 2;
+  if (!make_tmap(&ta, A, bf, K, M, kTcBM) || !make_tmap(&tb, W, bf, K, N, kTcBN)) {
+    set_error("cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", M, N, K);
+    return -5;
+  }
+  dim3 grid((M + kTcBM - 1) / kTcBM, (N + kTcBN - 1) / kTcBN);
+  kern<<<grid, 128, Sm::kBytes, e.stream>>>(ta, tb, M, N, K, epi, e.err_d);
+  e.launches++;
+  return 0;
+}
+
+template <class Epi>
+static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const float *W, const Epi &epi) {
+  const int warps = (N + 1) / 2;
+  dim3 grid((warps + kGemvWarps - 1) / kGemvWarps);
+  if (M <= 1)
+    gemv_f32_kernel<1, Epi><<<grid, kGemvWarps * 32, 0, e.stream>>>(W, N, K, X, M, epi);
+  else if (M <= 2)
+    gemv_f32_kernel<2, Epi><<<grid, kGemvWarps * 32, 0, e.stream>>>(W, N, K, X, M, epi);
+  else if (M <= 4)
+    gemv_f32_kernel<4, Epi><<<grid, kGemvWarps * 32, 0, e.stream>>>(W, N, K, X, M, epi);
+  else
+    gemv_f32_kernel<8, Epi><<<grid, kGemvWarps * 32, 0, e.stream>>>(W, N, K, X, M, epi);
+  e.launches++;
+}
+
+// C[M,N] = A[M,K] * W[N,K]^T with the epilogue `epi`.  `a_bytes` / `out_bytes`:
+// bytes per element of A and algorithmic output bytes (for the profiler).
+template <class Epi>
+static int project(Engine &e, int kind, int M, int N, int K, const void *A, const float *W32,
+                   const __nv_bfloat16 *W16, const Epi &epi, double out_bytes) {
+  if (M <= 0) return 0;
+  const bool tc = tc_path(e, M);
+  const bool bf = tc && e.precision == kBF16;
+  const double w_bytes = (double)N * K * (bf ? 2 : 4), a_bytes = (double)M * K * (bf ? 2 : 4);
+  const int tok = prof_begin(e);
+  int rc = 0;
+  if (tc) {
+    rc = bf ? launch_tc<__nv_bfloat16>(e, M, N, K, A, W16, epi) : launch_tc<float>(e, M, N, K, A, W32, epi);
+  } else {
+    launch_gemv(e, M, N, K, static_cast<const float *>(A), W32, epi);
+  }
+  prof_end(e, tok, kind, w_bytes + a_bytes + out_bytes, 2.0 * M * N * K);
+  return rc;
+}
+
+template <typename TA>
+static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_positions) {
+  const Dims &d = e.d;
+  const int tok = prof_begin(e);
+  const size_t layer_off = (size_t)layer * e.kv_layer_stride;
+  dim3 grid(d.heads, M);
+  const int max_n = d.ctx;
+  static unsigned long long attr_set = 0;  // one bit per device
+  if (!(attr_set & (1ull << e.device))) {
+    cudaFuncSetAttribute(attention_hs64_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(attention_generic_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr_set |= 1ull << e.device;
+  }
+  if (d.hs == 64) {
+    const size_t sm = (32 + 4 * 64 + (size_t)max_n) * sizeof(float);
+    attention_hs64_kernel<TA><<<grid, kAttThreads, sm, e.stream>>>(e.rows_d, e.q, e.kv, out, d.D, d.att_ch,
+                                                                    e.kv_slot_stride, layer_off, e.kv_part_stride,
+                                                                    e.kv_head_stride, e.sqrt_hs);
+  } else {
+    const size_t sm = (32 + (size_t)max_n) * sizeof(float);
+    attention_generic_kernel<TA><<<grid, kAttThreads, sm, e.stream>>>(e.rows_d, e.q, e.kv, out, d.D, d.att_ch, d.hs,
+                                                                       e.kv_slot_stride, layer_off, e.kv_part_stride,
+                                                                       e.kv_head_stride, e.sqrt_hs);
+  }
+  e.launches++;
+  // K and V of positions 0..pos per row, q in, att out
+  prof_end(e, tok, kProfAttention, kv_positions * 2.0 * d.att_ch * 4 + (double)M * d.att_ch * 4 + (double)M * d.D * sizeof(TA),
+           kv_positions * 4.0 * d.att_ch);
+}
+
+template <typename TA>
+static void launch_norm(Engine &e, int M, const int2 *gather, const float *w, TA *x) {
+  const int tok = prof_begin(e);
+  rmsnorm_kernel<TA><<<M, kNormThreads, 0, e.stream>>>(e.h, gather, w, x, e.d.D);
+  e.launches++;
+  prof_end(e, tok, kProfNorm, (double)M * e.d.D * (4 + sizeof(TA)), 0.0);
+}
+
+template <typename TA>
+static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, bool out_tc, double kv_positions) {
+  const Dims &d = e.d;
+  const double ea = sizeof(TA);
+  TA *x = static_cast<TA *>(e.x);
+  TA *att = static_cast<TA *>(e.att);
+  TA *u = static_cast<TA *>(e.u);
+  int tok = prof_begin(e);
+  embed_norm_kernel<TA><<<M, kNormThreads, 0, e.stream>>>(e.rows_d, tokens_d, e.emb, e.layers[0].rms_att, e.h, x,
+                                                          e.hist, e.seq_len_d, d.V, d.D, d.ctx);
+  e.launches++;
+  prof_end(e, tok, kProfEmbed, (double)M * d.D * (8 + ea), 0.0);
+  for (int l = 0; l < d.L; ++l) {
+    const LayerWeights &w = e.layers[l];
+    EpiQKV eq{e.rows_d, e.q, e.kv, e.rope, d.D, d.att_ch, d.hs, e.kv_slot_stride, (size_t)l * e.kv_layer_stride,
+              e.kv_part_stride, e.kv_head_stride};
+    int rc = project(e, kProfQKV, M, 3 * d.D, d.D, x, w.wqkv, w.wqkv_h, eq, 3.0 * M * d.att_ch * 4);
+    if (rc) return rc;
+    launch_attention<TA>(e, M, l, att, kv_positions);
+    rc = project(e, kProfWo, M, d.D, d.D, att, w.wo, w.wo_h, EpiResidual{e.h, d.D}, 8.0 * M * d.D);
+    if (rc) return rc;
+    launch_norm<TA>(e, M, nullptr, w.rms_ffn, x);
+    rc = project(e, kProfUp, M, d.F, d.D, x, w.wup, w.wup_h, EpiSilu<TA>{u, d.F}, ea * M * d.F);
+    if (rc) return rc;
+    rc = project(e, kProfDown, M, d.D, d.F, u, w.wdown, w.wdown_h, EpiResidual{e.h, d.D}, 8.0 * M * d.D);
+    if (rc) return rc;
+    if (l + 1 < d.L) launch_norm<TA>(e, M, nullptr, e.layers[l + 1].rms_att, x);
+  }
+  if (n_out > 0) {
+    EpiLogits el{e.logits, e.outrows_d, (long long)d.V};
+    const double ob = 4.0 * n_out * d.V;
+    if (out_tc && e.precision == kBF16) {
+      __nv_bfloat16 *xo = static_cast<__nv_bfloat16 *>(e.xo);
+      launch_norm<__nv_bfloat16>(e, n_out, e.outrows_d, e.rms_final, xo);
+      return project(e, kProfLogits, n_out, d.V, d.D, xo, e.w_out, e.w_out_h, el, ob);
+    }
+    float *xo = static_cast<float *>(e.xo);
+    launch_norm<float>(e, n_out, e.outrows_d, e.rms_final, xo);
+    return project(e, kProfLogits, n_out, d.V, d.D, xo, e.w_out, e.w_out_h, el, ob);
+  }
+  return 0;
+}
+
+int run_rows(Engine &e, const RowDesc *rows, int n, const int *tokens_d) {
+  for (int c0 = 0; c0 < n; c0 += e.m_max) {
+    const int M = std::min(e.m_max, n - c0);
+    // rows of this chunk and the ones that need logits
+    e.rows_stage.assign(rows + c0, rows + c0 + M);
+    e.out_stage.clear();
+    double kv_positions = 0;
+    for (int i = 0; i < M; ++i) {
+      kv_positions += e.rows_stage[i].pos + 1;
+      if (e.rows_stage[i].out >= 0) e.out_stage.push_back(make_int2(i, e.rows_stage[i].out));
+    }
+    const int n_out = (int)e.out_stage.size();
+    if (cudaMemcpyAsync(e.rows_d, e.rows_stage.data(), sizeof(RowDesc) * M, cudaMemcpyHostToDevice, e.stream) !=
+            cudaSuccess ||
+        (n_out && cudaMemcpyAsync(e.outrows_d, e.out_stage.data(), sizeof(int2) * n_out, cudaMemcpyHostToDevice,
+                                  e.stream) != cudaSuccess)) {
+      set_error("row upload failed: %s", cudaGetErrorString(cudaGetLastError()));
+      return -4;
+    }
+    const bool tc = tc_path(e, M);
+    const bool out_tc = tc_path(e, n_out);
+    const int rc = (tc && e.precision == kBF16)
+                       ? run_chunk_typed<__nv_bfloat16>(e, M, tokens_d, n_out, out_tc, kv_positions)
+                       : run_chunk_typed<float>(e, M, tokens_d, n_out, out_tc, kv_positions);
+    if (rc) return rc;
+    const cudaError_t le = cudaGetLastError();
+    if (le != cudaSuccess) {
+      set_error("kernel launch failed: %s", cudaGetErrorString(le));
+      return -4;
+    }
+  }
+  return 0;
+}
+
+// ---- profiler ----
+static cudaEvent_t prof_event(Engine &e) {
+  if (!e.prof_free.empty()) {
+    cudaEvent_t ev = e.prof_free.back();
+    e.prof_free.pop_back();
+    return ev;
+  }
+  cudaEvent_t ev = nullptr;
+  cudaEventCreate(&ev);
+  return ev;
+}
+
+int prof_begin(Engine &e) {
+  if (!e.prof) return -1;
+  cudaEvent_t a = prof_event(e);
+  cudaEventRecord(a, e.stream);
+  e.prof_pending.push_back(Engine::ProfPending{-1, a, nullptr, 0.0, 0.0});
+  return (int)e.prof_pending.size() - 1;
+}
+
+void prof_end(Engine &e, int token, int kind, double bytes, double flops) {
+  if (token < 0 || token >= (int)e.prof_pending.size()) return;
+  cudaEvent_t b = prof_event(e);
+  cudaEventRecord(b, e.stream);
+  Engine::ProfPending &p = e.prof_pending[token];
+  p.kind = kind;
+  p.b = b;
+  p.bytes = bytes;
+  p.flops = flops;
+}
+
+void prof_collect(Engine &e) {
+  if (e.prof_pending.empty()) return;
+  cudaStreamSynchronize(e.stream);
+  for (auto &p : e.prof_pending) {
+    if (p.b && p.kind >= 0 && p.kind < kProfKinds) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, p.a, p.b) == cudaSuccess) {
+        e.prof_ms[p.kind] += ms;
+        e.prof_count[p.kind] += 1;
+        e.prof_bytes[p.kind] += p.bytes;
+        e.prof_flops[p.kind] += p.flops;
+      }
+      e.prof_free.push_back(p.b);
+    }
+    e.prof_free.push_back(p.a);
+  }
+  e.prof_pending.clear();
+}
+
+int convert_bf16(Engine &e, const float *src, __nv_bfloat16 *dst, size_t n) {
+  to_bf16_kernel<<<1184, 256, 0, e.stream>>>(src, dst, n);
+  e.launches++;
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+int fill_f32(Engine &e, float *dst, size_t n, float v) {
+  fill_f32_kernel<<<592, 256, 0, e.stream>>>(dst, n, v);
+  e.launches++;
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+}  // namespace snai

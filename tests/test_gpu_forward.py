@@ -1,0 +1,246 @@
+"""GPU forward pass through the C ABI vs the oracle (teacher-forced logits,
+fp32-relative tolerance per GEMM precision) and the fused decode step's ids
+vs the oracle sampler applied to the GPU's own logits (bit-exact)."""
+import ctypes
+import math
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+from snai_b200 import (PREC_BF16, PREC_FP32, PREC_TF32, Cortex, SnaiCortexBridge, VARIANT_A,  # noqa: E402
+                       VARIANT_B, load, run_inference, sample_params)
+from conftest import make_model, rel_err  # noqa: E402
+
+# logits tolerance: max |gpu - oracle| / max |oracle|
+TOL = {PREC_FP32: 2e-5, PREC_TF32: 4e-3, PREC_BF16: 3e-2}
+
+
+def oracle_logits_seq(path, heads, tokens_steps):
+    """Feeds each list in tokens_steps in turn; returns the logits after each."""
+    o = O.Oracle(path, num_heads=heads)
+    out = [o.forward(t).copy() for t in tokens_steps]
+    o.close()
+    return out
+
+
+def test_legacy_api_prompt_and_steps(small_model, built):
+    lib = load()
+    s = lib.cortex_load_stream(small_model.encode(), 2)
+    assert s, lib.cortex_last_error()
+    V = lib.get_vocab_size(s)
+    assert V == 1000 and lib.get_ctx_size(s) == 96
+    rng = np.random.default_rng(0)
+    steps = [list(rng.integers(0, V, 40))] + [[int(x)] for x in rng.integers(-5, V + 5, 12)]
+    ref = oracle_logits_seq(small_model, 2, steps)
+    buf = np.zeros(V, dtype=np.float32)
+    for i, t in enumerate(steps):
+        a = np.ascontiguousarray(t, dtype=np.int32)
+        lib.cortex_forward(s, a.ctypes.data_as(ctypes.c_void_p), len(a), buf.ctypes.data_as(ctypes.c_void_p))
+        assert rel_err(buf, ref[i]) < TOL[PREC_FP32], i
+    lib.cortex_free(s)
+
+
+def test_ctx_cutoff_reset_and_clamp(model_dir, built):
+    p = make_model(model_dir, "ctx16.snai", 300, 64, 16, 1, seed=3, std=0.1)
+    e = Cortex(p, num_heads=1)
+    assert e.head_size == 64
+    o = O.Oracle(p, num_heads=1)
+    toks = np.arange(10, 24, dtype=np.int32)
+    a = e.forward([toks])
+    b = o.forward(toks)
+    assert rel_err(a[0], b) < TOL[PREC_FP32]
+    # positions 14, 15 then ctx: the last token is dropped -> no logits written
+    lib = load()
+    sentinel = np.full(300, 5.0, dtype=np.float32)
+    t2 = np.asarray([1, 2, 3], dtype=np.int32)
+    lib.cortex_forward(e.h, t2.ctypes.data_as(ctypes.c_void_p), 3, sentinel.ctypes.data_as(ctypes.c_void_p))
+    assert e.pos(0) == 16 and np.all(sentinel == 5.0)
+    e.reset([0])
+    assert e.pos(0) == 0
+    o.reset()
+    bad = np.asarray([-4, 299, 300, 12345], dtype=np.int32)  # out-of-range ids read row 0
+    assert rel_err(e.forward([bad])[0], o.forward(bad)) < TOL[PREC_FP32]
+    e.close()
+
+
+def test_load_extract_adam_train(small_model, built):
+    lib = load()
+    s = lib.cortex_load_stream(small_model.encode(), 2)
+    D, V = 128, 1000
+    w = np.zeros(D * D, dtype=np.float32)
+    lib.cortex_extract_layer(s, 1, 13, w.ctypes.data_as(ctypes.c_void_p), D * D)
+    from snai_b200 import modelgen
+    _, t = modelgen.read_model(small_model)
+    assert np.array_equal(w.reshape(D, D), t["1.w_k"])
+    neww = (np.arange(D * D, dtype=np.float32) * 1e-4).astype(np.float32)
+    lib.cortex_load_layer(s, 1, 13, neww.ctypes.data_as(ctypes.c_void_p), D * D)
+    lib.cortex_extract_layer(s, 1, 13, w.ctypes.data_as(ctypes.c_void_p), D * D)
+    assert np.array_equal(w, neww)
+    junk = np.ones(7, dtype=np.float32)
+    lib.cortex_load_layer(s, 1, 13, junk.ctypes.data_as(ctypes.c_void_p), 7)  # size mismatch: no-op
+    lib.cortex_extract_layer(s, 1, 13, w.ctypes.data_as(ctypes.c_void_p), D * D)
+    assert np.array_equal(w, neww)
+    m = np.zeros(V * D, dtype=np.float32)
+    lib.cortex_extract_adam_layer(s, -1, 0, False, m.ctypes.data_as(ctypes.c_void_p), V * D)
+    assert not m.any()
+    m[:] = 0.5
+    lib.cortex_load_adam_layer(s, -1, 0, True, m.ctypes.data_as(ctypes.c_void_p), V * D)
+    m2 = np.zeros_like(m)
+    lib.cortex_extract_adam_layer(s, -1, 0, True, m2.ctypes.data_as(ctypes.c_void_p), V * D)
+    assert np.array_equal(m, m2)
+    assert math.isnan(lib.cortex_train_step(s, None, None, 0, 0.01))
+    lib.cortex_free(s)
+    # cortex_init: zero weights, unit RMSNorm weights -> zero logits
+    z = lib.cortex_init(50, 32, 8, 1, 1)
+    assert z
+    buf = np.full(50, 3.0, dtype=np.float32)
+    a = np.asarray([3], dtype=np.int32)
+    lib.cortex_forward(z, a.ctypes.data_as(ctypes.c_void_p), 1, buf.ctypes.data_as(ctypes.c_void_p))
+    assert not buf.any()
+    r = np.zeros(32, dtype=np.float32)
+    lib.cortex_extract_layer(z, 0, 10, r.ctypes.data_as(ctypes.c_void_p), 32)
+    assert np.all(r == 1.0)
+    lib.cortex_free(z)
+
+
+def test_bad_files(tmp_path, small_model, built):
+    lib = load()
+    data = open(small_model, "rb").read()
+    (tmp_path / "short.snai").write_bytes(data[:-8])
+    (tmp_path / "magic.snai").write_bytes(b"SNAI_V5\x00" + data[8:])
+    assert not lib.cortex_load_stream(str(tmp_path / "short.snai").encode(), 2)
+    assert not lib.cortex_load_stream(str(tmp_path / "magic.snai").encode(), 2)
+    assert not lib.cortex_load_stream(b"/nonexistent/x.snai", 2)
+
+
+@pytest.mark.parametrize("prec", [PREC_FP32, PREC_TF32, PREC_BF16])
+def test_batched_teacher_forced(prec, small_model, built):
+    """B slots with a shared prompt length, then teacher-forced decode steps;
+    B=70 puts >= 64 rows through the tensor-core path in TF32/BF16 mode."""
+    B, plen, steps = 70, 20, 4
+    rng = np.random.default_rng(prec)
+    prompts = rng.integers(0, 1000, (B, plen)).astype(np.int32)
+    forced = rng.integers(0, 1000, (B, steps)).astype(np.int32)
+    e = Cortex(small_model, num_heads=2, max_seqs=B, precision=prec)
+    got = [e.forward(prompts)]
+    for s in range(steps):
+        got.append(e.forward(forced[:, s:s + 1]))
+    o = O.Oracle(small_model, num_heads=2)
+    _, ref, _ = o.generate(prompts, steps, np.zeros((B, steps), np.float32), VARIANT_A, 0.8, 1.15,
+                           forced=forced, want_logits=True)
+    for s in range(steps + 1):
+        err = max(rel_err(got[s][b], ref[b, s]) for b in range(B))
+        assert err < TOL[prec], (s, err)
+    e.close()
+
+
+@pytest.mark.parametrize("prec", [PREC_FP32, PREC_BF16])
+def test_single_sequence_long_prompt(prec, small_model, built):
+    """A 90-token prompt of one sequence: 90 rows in one pass (tensor cores in
+    BF16 mode) with causal attention inside the pass."""
+    rng = np.random.default_rng(4)
+    toks = rng.integers(0, 1000, 90).astype(np.int32)
+    e = Cortex(small_model, num_heads=2, precision=prec)
+    a = e.forward([toks])[0]
+    b = O.Oracle(small_model, num_heads=2).forward(toks)
+    assert rel_err(a, b) < TOL[prec]
+    e.close()
+
+
+@pytest.mark.parametrize("variant", [VARIANT_A, VARIANT_B])
+@pytest.mark.parametrize("prec", [PREC_FP32, PREC_BF16])
+def test_decode_batch_ids_exact(variant, prec, small_model, built):
+    """cortex_decode_batch: each sampled id equals the oracle sampler applied to
+    the GPU's logits with the slot's history (every token fed so far)."""
+    B, plen, steps = 66, 12, 5
+    rng = np.random.default_rng(10 + variant)
+    prompts = rng.integers(0, 1000, (B, plen)).astype(np.int32)
+    e = Cortex(small_model, num_heads=2, max_seqs=B, precision=prec)
+    e.forward(prompts, want_logits=False)
+    hist = [list(p) for p in prompts]
+    if variant == VARIANT_A:
+        prm, args = sample_params(VARIANT_A, 0.8, 1.15), dict(T=0.8, rep=1.15)
+    else:
+        prm, args = sample_params(VARIANT_B, 0.7, 1.1, 40, 0.9), dict(T=0.7, rep=1.1)
+    for s in range(steps):
+        lg = e.logits(np.arange(B))
+        U = rng.random(B).astype(np.float32)
+        ids = e.decode(U, prm)
+        for b in range(B):
+            if variant == VARIANT_A:
+                want = O.sample_a(lg[b], hist[b], args["T"], args["rep"], U[b])
+            else:
+                want = O.sample_b(lg[b], hist[b], args["T"], 40, 0.9, args["rep"], U[b])
+            assert ids[b] == want, (s, b)
+            hist[b].append(int(ids[b]))
+    e.close()
+
+
+def test_decode_matches_oracle_trajectory(small_model, built):
+    """Full generation (FP32): ids of GPU and oracle agree step by step while
+    their logits agree to fp32 tolerance (a flip needs a near-tie)."""
+    B, plen, steps = 8, 16, 24
+    rng = np.random.default_rng(21)
+    prompts = rng.integers(0, 1000, (B, plen)).astype(np.int32)
+    U = rng.random((B, steps)).astype(np.float32)
+    e = Cortex(small_model, num_heads=2, max_seqs=B)
+    e.forward(prompts, want_logits=False)
+    prm = sample_params(VARIANT_A, 0.25, 1.15)
+    got = np.stack([e.decode(U[:, s], prm) for s in range(steps)], axis=1)
+    ids, _, _ = O.Oracle(small_model, num_heads=2).generate(prompts, steps, U, VARIANT_A, 0.25, 1.15)
+    agree = (got == ids).mean()
+    assert agree > 0.95, agree
+    e.close()
+
+
+def test_run_inference_and_bridge(small_model, built):
+    rng = np.random.default_rng(2)
+    prompt = list(rng.integers(3, 1000, 20))
+    U = rng.random(64).astype(np.float32)
+    out, why = run_inference(small_model, prompt, U, max_new_tokens=30, stop_tokens=())
+    assert why == "max" and len(out) == 30
+    br = SnaiCortexBridge(small_model, num_heads=1)
+    window = list(rng.integers(0, 1000, 30))
+    tok = br.generate_next_token(window, 0.7, 40, 0.9, 1.15, u=0.37)
+    o = O.Oracle(small_model, num_heads=1)
+    lg = o.forward(window)
+    # same id as the oracle sampler on the GPU logits, and (tolerance permitting) on the oracle's
+    assert tok == O.sample_b(br.cached_c_logits, window, 0.7, 40, 0.9, 1.15, 0.37)
+    assert rel_err(br.cached_c_logits, lg) < TOL[PREC_FP32]
+    st = br.extract_state()
+    assert len(st["tensors"]["layers"]) == 2
+    br.close()
+
+
+def test_device_pointer_path(small_model, built):
+    """SNAI_DEVICE_PTRS: tokens, uniforms and ids in device memory, work on a
+    torch stream; same ids as the host-pointer path."""
+    B = 16
+    rng = np.random.default_rng(8)
+    prompts = rng.integers(0, 1000, (B, 10)).astype(np.int32)
+    U = rng.random(B).astype(np.float32)
+    prm = sample_params(VARIANT_B, 0.7, 1.1, 40, 0.9)
+    e1 = Cortex(small_model, num_heads=2, max_seqs=B)
+    e1.forward(prompts, want_logits=False)
+    ids_host = e1.decode(U, prm)
+    e2 = Cortex(small_model, num_heads=2, max_seqs=B)
+    st = torch.cuda.Stream()
+    e2.set_stream(st.cuda_stream)
+    with torch.cuda.stream(st):
+        tok = torch.from_numpy(prompts.ravel()).cuda()
+        e2.forward_dev(tok, B, 10)
+        ut = torch.from_numpy(U).cuda()
+        ids = torch.zeros(B, dtype=torch.int32, device="cuda")
+        e2.decode_dev(ut, prm, ids)
+    st.synchronize()
+    assert np.array_equal(ids.cpu().numpy(), ids_host)
+    e1.close()
+    e2.close()

@@ -1,0 +1,141 @@
+"""GPU sampler (cortex_sample through the C ABI) vs the oracle: sampled ids
+must be bit-identical for the same logits and uniforms."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+from snai_b200 import VARIANT_A, VARIANT_B, sample_device, sample_params  # noqa: E402
+from test_oracle import load_kats, random_rows  # noqa: E402
+
+
+def gpu_sample(L, hist, U, params, hist_len=None, ld=None):
+    dev = torch.device("cuda")
+    L = np.ascontiguousarray(L, dtype=np.float32)
+    R, V = L.shape
+    if ld is not None and ld > V:
+        big = np.zeros((R, ld), dtype=np.float32)
+        big[:, :V] = L
+        lt = torch.from_numpy(big).to(dev)[:, :V]
+    else:
+        lt = torch.from_numpy(L).to(dev)
+    H = np.ascontiguousarray(hist, dtype=np.int32).reshape(R, -1)
+    ht = torch.from_numpy(H).to(dev) if H.shape[1] > 0 else None
+    hl = None if hist_len is None else torch.from_numpy(np.ascontiguousarray(hist_len, dtype=np.int32)).to(dev)
+    ut = torch.from_numpy(np.ascontiguousarray(U, dtype=np.float32)).to(dev)
+    out = torch.full((R,), -7, dtype=torch.int32, device=dev)
+    sample_device(lt, ut, params, ht, hl, out)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def oracle_ids(L, hist, U, variant, T, rep, k=40, p=0.9, exp_mode=1, hist_len=None):
+    ids = []
+    for r in range(L.shape[0]):
+        h = hist[r] if hist_len is None else hist[r][:hist_len[r]]
+        if variant == VARIANT_A:
+            ids.append(O.sample_a(L[r], h, T, rep, U[r], exp_mode))
+        else:
+            ids.append(O.sample_b(L[r], h, T, k, p, rep, U[r], exp_mode))
+    return np.asarray(ids, dtype=np.int32)
+
+
+@pytest.mark.parametrize("case", load_kats(), ids=lambda c: c["name"])
+def test_gpu_sampler_kats(case, built):
+    L = np.asarray([case["logits"]], dtype=np.float32)
+    hist = np.asarray([case["hist"]], dtype=np.int32).reshape(1, -1)
+    if case["variant"] == 0:
+        prm = sample_params(VARIANT_A, case["T"], case["rep"], nan_guard=0)
+    else:
+        prm = sample_params(VARIANT_B, case["T"], case["rep"], case["top_k"], case["top_p"])
+    got = gpu_sample(L, hist, [case["u"]], prm)
+    assert got[0] == case["expect"], case["why"]
+
+
+def synth(rng, R, V, H=256, spikes=True):
+    L = rng.normal(0, 4, (R, V)).astype(np.float32)
+    if spikes:
+        L[rng.random((R, V)) < 0.01] += 12.0
+    hist = rng.integers(0, V, (R, H)).astype(np.int32)
+    U = rng.random(R).astype(np.float32)
+    return L, hist, U
+
+
+@pytest.mark.parametrize("V", [1000, 1001, 16384, 32000])
+@pytest.mark.parametrize("T", [0.01, 0.25, 0.7, 2.0])
+def test_variant_a_matches_oracle(V, T, built):
+    rng = np.random.default_rng(V + int(T * 100))
+    L, hist, U = synth(rng, 48, V)
+    prm = sample_params(VARIANT_A, T, 1.15, nan_guard=0)
+    got = gpu_sample(L, hist, U, prm)
+    assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_A, T, 1.15, exp_mode=1))
+    # libm exp (what PHP calls) gives the same ids on these rows
+    assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_A, T, 1.15, exp_mode=0))
+
+
+@pytest.mark.parametrize("V", [1000, 1001, 16384, 32000])
+@pytest.mark.parametrize("cfg", [(0.0, 40, 0.9), (0.7, 40, 0.9), (0.7, 50, 0.95), (1.0, 1, 0.9), (0.9, 1024, 1.0)])
+def test_variant_b_matches_oracle(V, cfg, built):
+    T, k, p = cfg
+    rng = np.random.default_rng(V + k)
+    L, hist, U = synth(rng, 48, V)
+    prm = sample_params(VARIANT_B, T, 1.1, k, p)
+    got = gpu_sample(L, hist, U, prm)
+    assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_B, T, 1.1, k, p, exp_mode=1))
+    assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_B, T, 1.1, k, p, exp_mode=0))
+
+
+def test_large_vocab_both_variants(built):
+    rng = np.random.default_rng(5)
+    L, hist, U = synth(rng, 16, 131072)
+    for prm, args in [(sample_params(VARIANT_A, 0.7, 1.15, nan_guard=0), (VARIANT_A, 0.7, 1.15)),
+                      (sample_params(VARIANT_A, 0.01, 1.15, nan_guard=0), (VARIANT_A, 0.01, 1.15)),
+                      (sample_params(VARIANT_B, 0.7, 1.1, 50, 0.95), (VARIANT_B, 0.7, 1.1, 50, 0.95))]:
+        got = gpu_sample(L, hist, U, prm)
+        assert np.array_equal(got, oracle_ids(L, hist, U, *args))
+
+
+def test_ties_and_edge_uniforms(built):
+    """Whole rows of equal logits (variant B's tie path), quantised logits,
+    u = 0 and u = 1, history shorter per row, a padded row stride."""
+    rng = np.random.default_rng(9)
+    R, V = 24, 16384
+    L = np.round(rng.normal(0, 1, (R, V)) * 2).astype(np.float32) / 2
+    L[0:4] = 0.25  # all equal
+    L[4:6] = -3.0
+    U = rng.random(R).astype(np.float32)
+    U[0::3] = 0.0
+    U[1::3] = 1.0
+    hist = rng.integers(0, V, (R, 300)).astype(np.int32)
+    hist_len = rng.integers(0, 301, R).astype(np.int32)
+    for prm, args in [(sample_params(VARIANT_A, 0.9, 1.3, nan_guard=0), (VARIANT_A, 0.9, 1.3)),
+                      (sample_params(VARIANT_A, 0.005, 1.3, nan_guard=0), (VARIANT_A, 0.005, 1.3)),
+                      (sample_params(VARIANT_B, 0.7, 0.5, 40, 0.9), (VARIANT_B, 0.7, 0.5, 40, 0.9)),
+                      (sample_params(VARIANT_B, 0.0, 0.5, 40, 0.9), (VARIANT_B, 0.0, 0.5, 40, 0.9)),
+                      (sample_params(VARIANT_B, 1.0, 0.0, 1024, 1.0), (VARIANT_B, 1.0, 0.0, 1024, 1.0))]:
+        got = gpu_sample(L, hist, U, prm, hist_len=hist_len, ld=V + 36)
+        assert np.array_equal(got, oracle_ids(L, hist, U, *args, hist_len=hist_len))
+
+
+def test_nan_guard_and_argument_errors(built):
+    from snai_b200 import CortexError
+    rng = np.random.default_rng(1)
+    L, hist, U = synth(rng, 4, 2048)
+    L[1, 0] = np.nan
+    got = gpu_sample(L, hist, U, sample_params(VARIANT_A, 0.8, 1.15, nan_guard=1))
+    assert got[1] == -1 and got[0] >= 0 and got[2] >= 0
+    with pytest.raises(CortexError):
+        gpu_sample(L, hist, U, sample_params(VARIANT_A, 0.0, 1.15))  # PHP: division by zero
+    with pytest.raises(CortexError):
+        gpu_sample(L, hist, U, sample_params(VARIANT_B, 0.7, 1.1, 0, 0.9))
+    with pytest.raises(CortexError):
+        gpu_sample(L, hist, U, sample_params(VARIANT_B, 0.7, 1.1, 5000, 0.9))
