@@ -330,6 +330,68 @@ def our_arm(args, rank, world, local_rank):
     eng.close()
 
 
+def sampler_bench(args):
+    """Isolated sampler workload: fp32 logits [8192, V], V in {16384, 32000,
+    131072}, N(0, 4) with 1% of entries raised by 12, a 256-id history per
+    row, one uniform per row; greedy, variant A (T 0.7, rep 1.15) and variant
+    B (T 0.7, top-k 50, top-p 0.95, rep 1.15).  Algorithmic bytes per row:
+    4V (logits) + 4*256 (history) + 4 (uniform) + 4 (id).  Each line also
+    checks 64 rows against the oracle (bit-exact ids)."""
+    import torch
+
+    import oracle as O
+    from snai_b200 import VARIANT_A, VARIANT_B, sample_device, sample_params
+    peak, peak_kind = load_peaks()
+    rows, H = 8192, 256
+    dev = torch.device("cuda")
+    modes = [("greedy", sample_params(VARIANT_A, 0.01, 1.15, nan_guard=0), (VARIANT_A, 0.01, 1.15, 40, 0.9)),
+             ("A_T0.7", sample_params(VARIANT_A, 0.7, 1.15, nan_guard=0), (VARIANT_A, 0.7, 1.15, 40, 0.9)),
+             ("B_T0.7_k50_p0.95", sample_params(VARIANT_B, 0.7, 1.15, 50, 0.95), (VARIANT_B, 0.7, 1.15, 50, 0.95))]
+    for V in (16384, 32000, 131072):
+        g = torch.Generator(device=dev).manual_seed(V)
+        L = torch.randn(rows, V, device=dev, generator=g) * 2.0
+        L += (torch.rand(rows, V, device=dev, generator=g) < 0.01).float() * 12.0
+        hist = torch.randint(0, V, (rows, H), device=dev, generator=g, dtype=torch.int32)
+        U = torch.rand(rows, device=dev, generator=g)
+        out = torch.zeros(rows, dtype=torch.int32, device=dev)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        for name, prm, oargs in modes:
+            for _ in range(args.warmup):
+                sample_device(L, U, prm, hist, None, out)
+            ts = []
+            for _ in range(args.steps):
+                flush.zero_()  # 256 MB > L2 between timed launches
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                sample_device(L, U, prm, hist, None, out)
+                e1.record()
+                e1.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            ms = float(np.median(ts))
+            nbytes = rows * (4 * V + 4 * H + 8)
+            gbs = nbytes / (ms / 1e3) / 1e9
+            n_chk = 64
+            Lh = L[:n_chk].cpu().numpy()
+            Hh = hist[:n_chk].cpu().numpy()
+            Uh = U[:n_chk].cpu().numpy()
+            want, _ = O.sample_rows(Lh, Hh, Uh, *oargs, exp_mode=1)
+            exact = bool(np.array_equal(out[:n_chk].cpu().numpy(), want))
+            # CPU baseline: the oracle port on all host threads over 256 rows
+            n_cpu = 256
+            _, rate = O.sample_rows(L[:n_cpu].cpu().numpy(), hist[:n_cpu].cpu().numpy(), U[:n_cpu].cpu().numpy(),
+                                    *oargs, exp_mode=0, nthreads=os.cpu_count() or 1)
+            line = {"metric": "sampling GB/s", "value": gbs, "unit": "GB/s", "mode": name, "vocab": V,
+                    "rows": rows, "ms": ms, "rows_per_s": rows / (ms / 1e3),
+                    "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                                 "frac": gbs / peak, "peak_source": f"{peak_kind} hbm_gbs"},
+                    "bit_exact_vs_oracle_64_rows": exact,
+                    "cpu_baseline": {"value": rate, "unit": "rows/s", "cores": os.cpu_count(), "kind": "port",
+                                     "sample": f"{n_cpu} rows"}}
+            print(json.dumps(line), flush=True)
+        del L, hist, U, out, flush
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -337,6 +399,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sampler", action="store_true", help="run the isolated sampling micro-benchmark")
     ap.add_argument("--seqs", type=int, default=TOTAL_SEQS,
                     help="total sequences (default 4096; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -349,6 +412,10 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return
+    if args.sampler:
+        if rank == 0:
+            sampler_bench(args)
         return
     if world > 1:
         import datetime

@@ -47,6 +47,36 @@ struct EpiQKV {
 
   __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
     const RowDesc rd = rows[m];
+    if (cnt == 16 && (hs & 15) == 0 && (D & 15) == 0) {
+      // 16 channels of one head of one part (n is a multiple of 16)
+      const int part = n / D;
+      const int ch = n - part * D;
+      if (ch >= att_ch) return;
+      const int head = ch / hs;
+      const int j = ch - head * hs;
+      float o[16];
+      if (part < 2) {
+        const float4 *cs = reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (hs >> 1) + (j >> 1));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 c = cs[i];  // (cos, sin) of two consecutive pairs
+          const float a0 = v[4 * i], b0 = v[4 * i + 1], a1 = v[4 * i + 2], b1 = v[4 * i + 3];
+          o[4 * i] = __fsub_rn(__fmul_rn(a0, c.x), __fmul_rn(b0, c.y));
+          o[4 * i + 1] = __fadd_rn(__fmul_rn(a0, c.y), __fmul_rn(b0, c.x));
+          o[4 * i + 2] = __fsub_rn(__fmul_rn(a1, c.z), __fmul_rn(b1, c.w));
+          o[4 * i + 3] = __fadd_rn(__fmul_rn(a1, c.w), __fmul_rn(b1, c.z));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = v[i];
+      }
+      float *dst = part == 0 ? q + (size_t)m * att_ch + ch
+                             : kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)(part - 1) * part_stride +
+                                   (size_t)head * head_stride + (size_t)rd.pos * hs + j;
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4 *>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+      return;
+    }
 #pragma unroll
     for (int i = 0; i + 1 < 16; i += 2)
       if (i + 1 < cnt) pair(rd, m, n + i, v[i], v[i + 1]);
@@ -87,6 +117,23 @@ struct EpiSilu {
   }
   __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
     TA *p = u + (size_t)m * ld + n;
+    if (cnt == 16 && (ld & 15) == 0) {
+      if constexpr (sizeof(TA) == 2) {
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(silu(v[2 * i]), silu(v[2 * i + 1]));
+          w[i] = *reinterpret_cast<const uint32_t *>(&h2);
+        }
+        reinterpret_cast<uint4 *>(p)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        reinterpret_cast<uint4 *>(p)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+          *reinterpret_cast<float4 *>(p + i) = make_float4(silu(v[i]), silu(v[i + 1]), silu(v[i + 2]), silu(v[i + 3]));
+      }
+      return;
+    }
 #pragma unroll
     for (int i = 0; i < 16; ++i)
       if (i < cnt) ActIO<TA>::store(p + i, silu(v[i]));

@@ -1,30 +1,39 @@
 // sampler.cu - the reference's two logits -> token samplers on sm_100a.
 //
-// One CTA of 512 threads per row.  Both kernels reproduce the PHP code's
-// double-precision arithmetic *bit for bit* for given logits and uniform u:
+// One CTA of 512 threads per row; a row of up to 32768 logits is held in
+// registers (thread t owns the 16-byte chunks t, t+512, ...), larger rows are
+// re-read from L2 on every pass.  Both kernels reproduce the PHP code's
+// double-precision decisions bit for bit for given logits and uniform u.
 //
 // Variant A (src/snai_inference.php:151-195).
-//   t_v = fp32(L_v / T); penalised ids (the unique history, held as a bitmap
-//   in shared memory): t = fp32(t / rep) if t > 0 else fp32(t * rep).
-//   Greedy (T <= 0.01): first index of the maximum.  Otherwise
-//   p_v = exp(t_v - max) in double (snai_exp.h), S = sequential sum of p_v
-//   in vocab order, r = u*S, id = first v whose running sum >= r.
-//   The sequential sum is replaced by a parallel one whose distance from the
-//   sequential one is bounded (below); when r is far enough from the running
-//   sums around the chosen id, the choice provably equals the sequential
-//   one.  Otherwise (probability ~ V^2 2^-52) warp 0 redoes the row
-//   sequentially.  Either way the id is the sequential algorithm's id.
+//   t_v = fp32(L_v / T); penalised ids (the unique history, a bitmap in shared
+//   memory): t = fp32(t / rep) if t > 0 else fp32(t * rep).  Greedy
+//   (T <= 0.01): first index of the maximum.  Otherwise p_v = exp(t_v - max)
+//   in double (snai_exp.h), S = sequential sum in vocab order, r = u*S, and
+//   the id is the first v whose running sum reaches r.
+//   The kernel replaces the sequential running sums by parallel ones with a
+//   proven error bound and accepts the id only when r is farther from the
+//   running sums around it than the bound ("certified"):
+//     tier 1: p_v from fp32 expf (error bound per element: expf is within
+//             2 ulp, the argument's rounding to float adds |x| 2^-24);
+//     tier 2: p_v from the contract exponential itself (no exp error);
+//     tier 3: warp 0 runs the sequential loop.
+//   Each tier is exact whenever it answers, so the id is always the
+//   sequential algorithm's id.
 //
 // Variant B (src/tensor_ffi_adapter.php:168-204).
-//   val_v = L_v - rep for ids in the input set, else L_v (double).  Stable
-//   descending sort + top_k = the k smallest (-val, v).  The kernel
-//   radix-selects a threshold on 32-bit keys of fp32 lower bounds of val,
-//   gathers every element whose fp32 upper bound reaches the threshold (a
-//   superset of the top k), sorts that set exactly by (val desc, v asc) and
-//   runs the PHP softmax / top-p / draw sequentially over the k survivors.
+//   val_v = L_v - rep for ids in the input set, else L_v (double).  The
+//   stable descending sort + top_k keeps the k smallest (-val, v).  Fast
+//   path: a histogram of fp32 lower bounds of val over distance bins below
+//   the row maximum finds a threshold bin holding the k-th largest; every
+//   element whose fp32 upper bound reaches that bin is gathered (a superset
+//   of the top k), sorted exactly by (val desc, v asc), and the PHP softmax
+//   / top-p / draw runs sequentially over the k survivors.  Rows the fast
+//   path cannot settle (non-finite maxima, huge exact ties) go through a
+//   general radix select.
 #include <cfloat>
-#include <cmath>
 #include <climits>
+#include <cmath>
 #include <cstdio>
 
 #include "common.cuh"
@@ -36,9 +45,11 @@ namespace snai {
 constexpr int kSampThreads = 512;
 constexpr int kSampWarps = kSampThreads / 32;
 constexpr int kMaxTopK = 1024;
-constexpr int kCandCap = 4096;  // exact-sort capacity of variant B
+constexpr int kCandCap = 4096;   // exact-sort capacity (general path)
+constexpr int kFastCand = 2048;  // candidates the fast path accepts
 constexpr int kMaxVocab = 1 << 19;
 constexpr int kMaxSeg = kMaxVocab / 2048;
+constexpr int kSegGroup = 32;    // segments reduced per shared-memory round
 
 struct SampArgs {
   const float *logits;
@@ -103,6 +114,12 @@ __device__ __forceinline__ float tempered(const SampArgs &a, const uint32_t *bit
   return t;
 }
 
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
 // Exclusive block scan of doubles in thread order; `tot` = block total.
 // Summation order is fixed (warp Kogge-Stone, then warp totals in order).
 __device__ double block_excl_scan(double v, double *wsum, double &tot) {
@@ -128,25 +145,241 @@ __device__ double block_excl_scan(double v, double *wsum, double &tot) {
   return __dadd_rn(base, ex);
 }
 
+// A row of logits: 16-byte chunk i of thread t covers entries
+// 4*(t + 512*i) .. +3.  NV4 > 0: the row (V <= 2048*NV4) sits in registers;
+// NV4 == 0: every access reads global memory (L2 after the first pass).
+template <int NV4>
+struct Row {
+  const float *L;
+  int V;
+  bool vec;
+  float4 r[NV4 > 0 ? NV4 : 1];
+
+  __device__ __forceinline__ int layers() const { return NV4 > 0 ? NV4 : (V + 2047) / 2048; }
+  __device__ __forceinline__ float4 fetch(int i) const {
+    const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+    if (vec && v0 + 3 < V) return __ldg(reinterpret_cast<const float4 *>(L + v0));
+    float4 f;
+    f.x = v0 < V ? L[v0] : 0.f;
+    f.y = v0 + 1 < V ? L[v0 + 1] : 0.f;
+    f.z = v0 + 2 < V ? L[v0 + 2] : 0.f;
+    f.w = v0 + 3 < V ? L[v0 + 3] : 0.f;
+    return f;
+  }
+  __device__ __forceinline__ void load() {
+    if constexpr (NV4 > 0) {
+#pragma unroll
+      for (int i = 0; i < NV4; ++i) r[i] = fetch(i);
+    }
+  }
+  // Chunk layer i; with registers the choice is a chain of predicated moves,
+  // so a run-time i never sends the array to local memory.
+  __device__ __forceinline__ float4 get(int i) const {
+    if constexpr (NV4 > 0) {
+      float4 o = r[0];
+#pragma unroll
+      for (int q = 1; q < NV4; ++q)
+        if (q == i) o = r[q];
+      return o;
+    } else {
+      return fetch(i);
+    }
+  }
+};
+
+__device__ __forceinline__ float f4_at(const float4 &f, int j) { return j == 0 ? f.x : j == 1 ? f.y : j == 2 ? f.z : f.w; }
+__device__ __forceinline__ void f4_set(float4 &f, int j, float v) {
+  if (j == 0) f.x = v;
+  else if (j == 1) f.y = v;
+  else if (j == 2) f.z = v;
+  else f.w = v;
+}
+
 // ---------------------------------------------------------------------------
 // Variant A
 // ---------------------------------------------------------------------------
 
 struct SmemA {
-  double seg[kMaxSeg];      // per-segment sums (segment = 2048 entries)
+  double wp[kSegGroup][kSampWarps];  // per-warp partial sums of p
+  double we[kSegGroup][kSampWarps];  // per-warp partial sums of the error bound
+  double seg[kMaxSeg];
+  double segerr[kMaxSeg];
   double wsum[kSampWarps];
   float bmax[kSampWarps];
   int bidx[kSampWarps];
-  double S, r;
+  double S, r, seg_base, err_base, err_tot;
   int seg_star;
-  double seg_base;
   int cand;
-  double cand_hi, cand_lo;  // running sums at cand and cand-1
+  double cand_hi, cand_lo, ecand_hi, ecand_lo;
   int certified;
 };
 
-// p_v for an index (t_v known) in the contract's arithmetic.
-__device__ __forceinline__ double prob_a(float t, double maxv) { return snai_exp(__dsub_rn((double)t, maxv)); }
+// p_v and its error bound.  EXACT: the contract exponential, error 0.  Else
+// fp32 expf (CUDA: at most 2 ulp) of the argument rounded to float (relative
+// error |x| 2^-24 after exp), bounded as p~ (3e-7 + 7e-8 |x|); below -87 the
+// float result underflows and the bound is e^-87.
+template <bool EXACT>
+__device__ __forceinline__ double prob(float t, double maxv, double &err) {
+  const double xd = __dsub_rn((double)t, maxv);
+  if constexpr (EXACT) {
+    err = 0.0;
+    return snai_exp(xd);
+  } else {
+    if (!(xd >= -87.0)) {
+      err = 1.7e-38;
+      return 0.0;
+    }
+    const float xf = __double2float_rn(xd);
+    const float pf = expf(xf);
+    err = (double)pf * (3e-7 + 7e-8 * (double)fabsf(xf));
+    return (double)pf;
+  }
+}
+
+// tier 1 / tier 2 of variant A: returns the id, or -1 if not certified.
+// `tv(i)` gives this thread's chunk i of tempered values.
+template <bool EXACT, class TV>
+__device__ int certified_draw(SmemA &sm, int V, int nl, double maxv, double u, const TV &tv) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // ---- segment sums (segment i = chunk layer i = 2048 consecutive ids) ----
+  for (int g0 = 0; g0 < nl; g0 += kSegGroup) {
+    const int g1 = min(nl, g0 + kSegGroup);
+    for (int i = g0; i < g1; ++i) {
+      const float4 t = tv(i);
+      const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+      double c = 0.0, ce = 0.0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (v0 + j < V) {
+          double e;
+          c = __dadd_rn(c, prob<EXACT>(f4_at(t, j), maxv, e));
+          ce += e;
+        }
+      c = warp_sum_d(c);
+      ce = warp_sum_d(ce);
+      if (lane == 0) {
+        sm.wp[i - g0][warp] = c;
+        sm.we[i - g0][warp] = ce;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < g1 - g0) {
+      double s = 0.0, e = 0.0;
+      for (int w = 0; w < kSampWarps; ++w) {
+        s = __dadd_rn(s, sm.wp[threadIdx.x][w]);
+        e += sm.we[threadIdx.x][w];
+      }
+      sm.seg[g0 + threadIdx.x] = s;
+      sm.segerr[g0 + threadIdx.x] = e;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    double S = 0.0, Et = 0.0;
+    for (int s = 0; s < nl; ++s) {
+      S = __dadd_rn(S, sm.seg[s]);
+      Et += sm.segerr[s];
+    }
+    const double r = __dmul_rn(u, S);
+    int ss = -1;
+    double base = 0.0, run = 0.0, eb = 0.0;
+    for (int s = 0; s < nl; ++s) {
+      const double nxt = __dadd_rn(run, sm.seg[s]);
+      if (nxt >= r) {
+        ss = s;
+        base = run;
+        break;
+      }
+      run = nxt;
+      eb += sm.segerr[s];
+    }
+    sm.S = S;
+    sm.r = r;
+    sm.err_tot = Et;
+    sm.err_base = eb;
+    sm.seg_star = ss;
+    sm.seg_base = base;
+    sm.cand = INT_MAX;
+    sm.certified = 0;
+  }
+  __syncthreads();
+  const double S = sm.S, r = sm.r;
+  const int ss = sm.seg_star;
+  if (!(isfinite(S) && isfinite(r) && ss >= 0 && u >= 0.0 && u <= 1.0)) return -1;
+
+  // ---- running sums inside the crossing segment ----
+  const int v0 = (threadIdx.x + kSampThreads * ss) * 4;
+  const float4 t = tv(ss);
+  double p[4] = {0.0, 0.0, 0.0, 0.0}, pe[4] = {0.0, 0.0, 0.0, 0.0};
+  double c = 0.0, ce = 0.0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (v0 + j < V) {
+      p[j] = prob<EXACT>(f4_at(t, j), maxv, pe[j]);
+      c = __dadd_rn(c, p[j]);
+      ce += pe[j];
+    }
+  double tot, etot;
+  const double ex = block_excl_scan(c, sm.wsum, tot);
+  const double eex = block_excl_scan(ce, sm.wsum, etot);
+  double prev = __dadd_rn(sm.seg_base, ex);
+  int mine = -1;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (mine < 0 && v0 + j < V) {
+      const double cur = __dadd_rn(prev, p[j]);
+      if (cur >= r) mine = j;
+      prev = cur;
+    }
+  }
+  if (mine >= 0) atomicMin(&sm.cand, v0 + mine);
+  __syncthreads();
+  const int cand = sm.cand;
+  if (cand >= v0 && cand < v0 + 4 && v0 < V) {
+    double pre = __dadd_rn(sm.seg_base, ex);
+    double ep = sm.err_base + eex;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < cand - v0) {
+        pre = __dadd_rn(pre, p[j]);
+        ep += pe[j];
+      }
+    double phi = pre, ehi = ep;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j == cand - v0) {
+        phi = __dadd_rn(pre, p[j]);
+        ehi = ep + pe[j];
+      }
+    sm.cand_lo = pre;
+    sm.cand_hi = phi;
+    sm.ecand_lo = ep;
+    sm.ecand_hi = ehi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 0;
+    if (cand != INT_MAX) {
+      // A summation tree of depth h over non-negative terms is within
+      // h 2^-53 (1+o(1)) of the exact sum.  The sequential running sum at v has
+      // depth v; ours at most nl + 50 (4 per chunk, 5 + 16 per reduction or
+      // scan, nl segments).  The rounding bounds below use 2^-52 (twice the
+      // first-order constant); the exp-error sums get a (1 + 1e-6) margin for
+      // their own rounding.
+      const double slack = (double)(nl + 64);
+      const double Er = u * (sm.err_tot * (1.0 + 1e-6) + ((double)V + slack) * 0x1p-52 * S) + 0x1p-52 * r;
+      const double hi = sm.cand_hi, lo = sm.cand_lo;
+      const double Ehi = sm.ecand_hi * (1.0 + 1e-6) + ((double)cand + slack) * 0x1p-52 * hi;
+      const double Elo = sm.ecand_lo * (1.0 + 1e-6) + ((double)cand + slack) * 0x1p-52 * lo;
+      const bool up = hi - Ehi >= r + Er;
+      const bool dn = cand == 0 || lo + Elo < r - Er;
+      ok = up && dn;
+    }
+    sm.certified = ok;
+  }
+  __syncthreads();
+  return sm.certified ? cand : -1;
+}
 
 // The sequential algorithm of src/snai_inference.php:178-194, by warp 0.
 __device__ int sequential_a(const SampArgs &a, const uint32_t *bits, const float *L, double maxv, double u) {
@@ -154,7 +387,8 @@ __device__ int sequential_a(const SampArgs &a, const uint32_t *bits, const float
   double sum = 0.0;
   for (int b = 0; b < a.V; b += 32) {
     const int v = b + lane;
-    const double p = v < a.V ? prob_a(tempered(a, bits, L[v], v), maxv) : 0.0;
+    double e;
+    const double p = v < a.V ? prob<true>(tempered(a, bits, L[v], v), maxv, e) : 0.0;
     const int cnt = min(32, a.V - b);
     for (int j = 0; j < cnt; ++j) sum = __dadd_rn(sum, __shfl_sync(0xffffffffu, p, j));
   }
@@ -162,7 +396,8 @@ __device__ int sequential_a(const SampArgs &a, const uint32_t *bits, const float
   double cum = 0.0;
   for (int b = 0; b < a.V; b += 32) {
     const int v = b + lane;
-    const double p = v < a.V ? prob_a(tempered(a, bits, L[v], v), maxv) : 0.0;
+    double e;
+    const double p = v < a.V ? prob<true>(tempered(a, bits, L[v], v), maxv, e) : 0.0;
     const int cnt = min(32, a.V - b);
     for (int j = 0; j < cnt; ++j) {
       cum = __dadd_rn(cum, __shfl_sync(0xffffffffu, p, j));
@@ -172,6 +407,7 @@ __device__ int sequential_a(const SampArgs &a, const uint32_t *bits, const float
   return 0;  // `$best_token = 0` when nothing qualifies (NaN sums)
 }
 
+template <int NV4>
 __global__ void __launch_bounds__(kSampThreads) sample_a_kernel(SampArgs a) {
   extern __shared__ __align__(16) uint8_t smem_dyn[];
   SmemA &sm = *reinterpret_cast<SmemA *>(smem_dyn);
@@ -189,40 +425,73 @@ __global__ void __launch_bounds__(kSampThreads) sample_a_kernel(SampArgs a) {
       return;
     }
   }
+  Row<NV4> row;
+  row.L = L;
+  row.V = V;
+  row.vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
+  row.load();
   build_bitmap(a, mrow, bits);
+  const int nl = row.layers();
 
-  // ---- pass 1: tempered values, maximum and the first index attaining it ----
+  // ---- pass 1: tempered values (kept in registers), maximum, first argmax ----
+  auto temper = [&](int i) {
+    float4 x = row.fetch(i);
+    const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) f4_set(x, j, v0 + j < V ? tempered(a, bits, f4_at(x, j), v0 + j) : -INFINITY);
+    return x;
+  };
+  if constexpr (NV4 > 0) {
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) {
+      const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        f4_set(row.r[i], j, v0 + j < V ? tempered(a, bits, f4_at(row.r[i], j), v0 + j) : -INFINITY);
+    }
+  }
+  auto tv = [&](int i) {
+    if constexpr (NV4 > 0)
+      return row.get(i);
+    else
+      return temper(i);
+  };
   float best = -INFINITY;
   int bi = INT_MAX;
-  const bool vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
-  for (int v0 = threadIdx.x * 4; v0 < V; v0 += kSampThreads * 4) {
-    float x[4];
-    if (vec && v0 + 3 < V) {
-      const float4 q = __ldg(reinterpret_cast<const float4 *>(L + v0));
-      x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
-    } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) x[j] = v0 + j < V ? L[v0 + j] : NAN;
-    }
+  for (int i = 0; i < nl; ++i) {
+    const float4 t = tv(i);
+    const int v0 = (threadIdx.x + kSampThreads * i) * 4;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      if (v0 + j >= V) break;
-      const float t = tempered(a, bits, x[j], v0 + j);
-      if (t > best) { best = t; bi = v0 + j; }  // indices ascend per thread: ties keep the first
+      const float tj = f4_at(t, j);
+      if (tj > best) {  // ids ascend along a thread's chunks: ties keep the first
+        best = tj;
+        bi = v0 + j;
+      }
     }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ob = __shfl_xor_sync(0xffffffffu, best, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
   }
-  if (lane == 0) { sm.bmax[warp] = best; sm.bidx[warp] = bi; }
+  if (lane == 0) {
+    sm.bmax[warp] = best;
+    sm.bidx[warp] = bi;
+  }
   __syncthreads();
   best = sm.bmax[0];
   bi = sm.bidx[0];
   for (int w = 1; w < kSampWarps; ++w)
-    if (sm.bmax[w] > best || (sm.bmax[w] == best && sm.bidx[w] < bi)) { best = sm.bmax[w]; bi = sm.bidx[w]; }
+    if (sm.bmax[w] > best || (sm.bmax[w] == best && sm.bidx[w] < bi)) {
+      best = sm.bmax[w];
+      bi = sm.bidx[w];
+    }
   // PHP: max starts at -INF and only a strictly larger value moves it.
   const bool any = best > -INFINITY;
   const double maxv = any ? (double)best : -INFINITY;
@@ -231,111 +500,13 @@ __global__ void __launch_bounds__(kSampThreads) sample_a_kernel(SampArgs a) {
     return;
   }
   const double u = (double)a.uniforms[b];
-
-  // ---- pass 2: segment sums of p_v (segment = 2048 consecutive ids) ----
-  const int nseg = (V + 2047) / 2048;
-  for (int s = 0; s < nseg; ++s) {
-    const int v0 = s * 2048 + threadIdx.x * 4;
-    double c = 0.0;
-    if (v0 < V) {
-      float x[4];
-      if (vec && v0 + 3 < V) {
-        const float4 q = __ldg(reinterpret_cast<const float4 *>(L + v0));
-        x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) x[j] = v0 + j < V ? L[v0 + j] : 0.f;
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (v0 + j < V) c = __dadd_rn(c, prob_a(tempered(a, bits, x[j], v0 + j), maxv));
-    }
-    double tot;
-    block_excl_scan(c, sm.wsum, tot);
-    if (threadIdx.x == 0) sm.seg[s] = tot;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double S = 0.0;
-    for (int s = 0; s < nseg; ++s) S = __dadd_rn(S, sm.seg[s]);
-    const double r = __dmul_rn(u, S);
-    int ss = -1;
-    double base = 0.0, run = 0.0;
-    for (int s = 0; s < nseg; ++s) {
-      const double nxt = __dadd_rn(run, sm.seg[s]);
-      if (nxt >= r) { ss = s; base = run; break; }
-      run = nxt;
-    }
-    sm.S = S;
-    sm.r = r;
-    sm.seg_star = ss;
-    sm.seg_base = base;
-    sm.cand = INT_MAX;
-    sm.certified = 0;
-  }
-  __syncthreads();
-  const double S = sm.S, r = sm.r;
-  const int ss = sm.seg_star;
-  bool fallback = !(isfinite(S) && isfinite(r) && ss >= 0 && u >= 0.0 && u <= 1.0);
-
-  if (!fallback) {
-    // ---- pass 3: scan inside the crossing segment ----
-    const int v0 = ss * 2048 + threadIdx.x * 4;
-    double p[4] = {0.0, 0.0, 0.0, 0.0};
-    double c = 0.0;
-    if (v0 < V) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (v0 + j < V) {
-          p[j] = prob_a(tempered(a, bits, L[v0 + j], v0 + j), maxv);
-          c = __dadd_rn(c, p[j]);
-        }
-    }
-    double tot;
-    const double ex = block_excl_scan(c, sm.wsum, tot);
-    double prev = __dadd_rn(sm.seg_base, ex);
-    for (int j = 0; j < 4; ++j) {
-      if (v0 + j >= V) break;
-      const double cur = __dadd_rn(prev, p[j]);
-      if (cur >= r) {
-        atomicMin(&sm.cand, v0 + j);
-        break;
-      }
-      prev = cur;
-    }
-    __syncthreads();
-    const int cand = sm.cand;
-    if (cand >= v0 && cand < v0 + 4 && v0 < V) {
-      // running sums P'(cand-1), P'(cand) as this thread formed them
-      double pre = __dadd_rn(sm.seg_base, ex);
-      for (int j = 0; j < cand - v0; ++j) pre = __dadd_rn(pre, p[j]);
-      sm.cand_lo = pre;
-      sm.cand_hi = __dadd_rn(pre, p[cand - v0]);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int ok = 0;
-      if (cand != INT_MAX) {
-        // Any summation tree of depth h over non-negative terms is within
-        // h 2^-53 (1+o(1)) of the exact sum.  The sequential running sum at v
-        // has depth v; ours has depth <= nseg + 56 (4 per chunk, 5 per warp
-        // scan, 16 warps, nseg segments, twice).  Bounds below use 2^-52,
-        // twice the first-order constant.
-        const double slack = (double)(nseg + 64);
-        const double Er = ((double)V + slack) * 0x1p-52 * r;
-        const double hi = sm.cand_hi, lo = sm.cand_lo;
-        const bool up = hi - ((double)cand + slack) * 0x1p-52 * hi >= r + Er;
-        const bool dn = cand == 0 || lo + ((double)cand + slack) * 0x1p-52 * lo < r - Er;
-        ok = up && dn;
-      }
-      sm.certified = ok;
-    }
-    __syncthreads();
-    if (sm.certified) {
-      if (threadIdx.x == 0) a.out[b] = cand;
+  if (any) {
+    int id = certified_draw<false>(sm, V, nl, maxv, u, tv);
+    if (id < 0) id = certified_draw<true>(sm, V, nl, maxv, u, tv);
+    if (id >= 0) {
+      if (threadIdx.x == 0) a.out[b] = id;
       return;
     }
-    fallback = true;
   }
   if (warp == 0) {
     const int id = sequential_a(a, bits, L, maxv, u);
@@ -362,8 +533,11 @@ struct SmemB {
   double val[kMaxTopK];
   double p[kMaxTopK];
   double cum[kMaxTopK];
-  int nf;
   int overflow;
+  float fmax[kSampWarps];
+  float fsum[kSampWarps], fsq[kSampWarps];
+  int fcnt[kSampWarps];
+  float R;
 };
 
 // Monotone 32-bit key of a float (NaN lowest; -0 and +0 equal, as PHP
@@ -386,10 +560,11 @@ __device__ __forceinline__ double key_to_double(unsigned long long k) {
   return __longlong_as_double((long long)u);
 }
 
-// val_v and the fp32 keys bracketing it.
+// val_v and the fp32 values bracketing it (lo <= val <= hi; equal unless the
+// entry is penalised).
 struct ValB {
   double val;
-  unsigned int klo, khi;
+  float lo, hi;
   bool pen;
 };
 __device__ __forceinline__ ValB val_b(const SampArgs &a, const uint32_t *bits, float x, int v) {
@@ -397,11 +572,11 @@ __device__ __forceinline__ ValB val_b(const SampArgs &a, const uint32_t *bits, f
   r.pen = in_set(bits, v);
   if (!r.pen) {
     r.val = (double)x;
-    r.klo = r.khi = okey32(x);
+    r.lo = r.hi = x;
   } else {
     r.val = __dsub_rn((double)x, a.rep);
-    r.klo = okey32(__double2float_rd(r.val));
-    r.khi = okey32(__double2float_ru(r.val));
+    r.lo = __double2float_rd(r.val);
+    r.hi = __double2float_ru(r.val);
   }
   return r;
 }
@@ -423,25 +598,189 @@ __device__ __forceinline__ void push_cand(SmemB &sm, double val, int v) {
   }
 }
 
+// Warp-cooperative append (every lane calls it; `want` selects).
+__device__ __forceinline__ void push_cand_warp(SmemB &sm, bool want, double val, int v, int cap) {
+  const unsigned int m = __ballot_sync(0xffffffffu, want);
+  if (!m) return;
+  const int lane = threadIdx.x & 31;
+  int base = 0;
+  if (lane == 0) base = atomicAdd(&sm.ncand, __popc(m));
+  base = __shfl_sync(0xffffffffu, base, 0);
+  if (want) {
+    const int slot = base + __popc(m & ((1u << lane) - 1u));
+    if (slot < cap) {
+      sm.ckey[slot] = okey64(val);
+      sm.cidx[slot] = v;
+    }
+  }
+}
+
 // candidate i precedes candidate j in PHP's arsort order
 __device__ __forceinline__ bool precedes(unsigned long long ki, int vi, unsigned long long kj, int vj) {
   return ki > kj || (ki == kj && vi < vj);
 }
 
-__global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
-  extern __shared__ __align__(16) uint8_t smem_dyn[];
-  SmemB &sm = *reinterpret_cast<SmemB *>(smem_dyn);
-  uint32_t *bits = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemB));
-  const int b = blockIdx.x;
-  const int mrow = a.row_map ? a.row_map[b] : b;
-  const float *L = a.logits + (size_t)mrow * a.ld;
+// Sorts the nc gathered candidates and keeps the first k in sm.order / sm.val.
+__device__ void rank_candidates(SmemB &sm, int nc, int k) {
+  for (int i = threadIdx.x; i < nc; i += kSampThreads) {
+    const unsigned long long ki = sm.ckey[i];
+    const int vi = sm.cidx[i];
+    int rank = 0;
+    for (int j = 0; j < nc; ++j) rank += precedes(sm.ckey[j], sm.cidx[j], ki, vi) ? 1 : 0;
+    if (rank < k) {
+      sm.order[rank] = vi;
+      sm.val[rank] = key_to_double(ki);
+    }
+  }
+  __syncthreads();
+}
+
+// Fast selection (see the file comment).  Returns false when the row needs
+// the general path.  All threads return the same value.
+template <int NV4>
+__device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row<NV4> &row, SmemB &sm, int k) {
+  const int V = a.V, nl = row.layers();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // pass 1: maximum of the lower bounds, and their spread
+  float mx = -INFINITY, s1 = 0.f, s2 = 0.f;
+  int cnt = 0;
+#pragma unroll
+  for (int i = 0; i < nl; ++i) {
+    const float4 x = row.get(i);
+    const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (v0 + j < V) {
+        const ValB e = val_b(a, bits, f4_at(x, j), v0 + j);
+        if (isfinite(e.lo)) {
+          mx = fmaxf(mx, e.lo);
+          s1 += e.lo;
+          s2 = fmaf(e.lo, e.lo, s2);
+          ++cnt;
+        } else if (e.lo > 0.f) {
+          cnt = -(1 << 24);  // +inf: leave the row to the general path
+        }
+      }
+    }
+  }
+  mx = warp_max(mx);
+  s1 = warp_sum(s1);
+  s2 = warp_sum(s2);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  if (lane == 0) {
+    sm.fmax[warp] = mx;
+    sm.fsum[warp] = s1;
+    sm.fsq[warp] = s2;
+    sm.fcnt[warp] = cnt;
+  }
+  __syncthreads();
+  mx = -INFINITY;
+  s1 = s2 = 0.f;
+  cnt = 0;
+  for (int w = 0; w < kSampWarps; ++w) {
+    mx = fmaxf(mx, sm.fmax[w]);
+    s1 += sm.fsum[w];
+    s2 += sm.fsq[w];
+    cnt += sm.fcnt[w];
+  }
+  __syncthreads();
+  if (!isfinite(mx) || cnt < k) return false;
+  const float mean = s1 / cnt;
+  const float sd = sqrtf(fmaxf(s2 / cnt - mean * mean, 0.f));
+  float R = 2.5f * sd;
+  if (!(R > 0.f) || !isfinite(R)) return false;  // all equal: ties, general path
+
+  // pass 2: histogram of the distance below the maximum, 255 bins over [0, R)
+  int bstar = 255;
+  for (int attempt = 0; attempt < 3 && bstar >= 255; ++attempt, R *= 8.f) {
+    const float inv_w = 255.f / R;
+    for (int i = threadIdx.x; i < 256; i += kSampThreads) sm.hist[i] = 0u;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < nl; ++i) {
+      const float4 x = row.get(i);
+      const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (v0 + j < V) {
+          const float d = mx - val_b(a, bits, f4_at(x, j), v0 + j).lo;
+          if (d >= 0.f && d < R) atomicAdd(&sm.hist[min((int)(d * inv_w), 254)], 1u);
+        }
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // inclusive prefix over bins 0..255, 8 per lane
+      unsigned int c[8], run = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        run += sm.hist[lane * 8 + q];
+        c[q] = run;
+      }
+      unsigned int incl = run;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      const unsigned int before = incl - run;
+      int bs = 255;
+#pragma unroll
+      for (int q = 7; q >= 0; --q)
+        if (before + c[q] >= (unsigned)k) bs = lane * 8 + q;
+      // smallest bin reaching k
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) bs = min(bs, __shfl_xor_sync(0xffffffffu, bs, o));
+      if (lane == 0) {
+        sm.bstar = bs;
+        sm.R = R;
+      }
+    }
+    __syncthreads();
+    bstar = sm.bstar;
+    __syncthreads();
+  }
+  if (bstar >= 255) return false;
+  R = sm.R;
+  const float inv_w = 255.f / R;
+
+  // pass 3: gather every entry whose upper bound falls in a bin <= bstar
+  if (threadIdx.x == 0) sm.ncand = 0;
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < nl; ++i) {
+    const float4 x = row.get(i);
+    const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      bool want = false;
+      double val = 0.0;
+      if (v0 + j < V) {
+        const ValB e = val_b(a, bits, f4_at(x, j), v0 + j);
+        const float d = mx - e.hi;
+        want = d < R && min((int)(d * inv_w), 254) <= bstar;
+        val = e.val;
+      }
+      push_cand_warp(sm, want, val, v0 + j, kFastCand);
+    }
+  }
+  __syncthreads();
+  const int nc = sm.ncand;
+  __syncthreads();
+  if (nc > kFastCand || nc < k) return false;
+  rank_candidates(sm, nc, k);
+  return true;
+}
+
+// General selection: radix select on the 32-bit keys of the lower bounds
+// (12 + 12 + 8 bits), superset gather by the upper bounds, exact sort.
+// Handles ties of any size: when more than 1024 entries share the exact
+// threshold value, only the first `need` of them in vocab order are kept
+// (the later ones tie in value and lose on index).
+__device__ bool general_select_b(const SampArgs &a, const uint32_t *bits, const float *L, SmemB &sm, int k) {
   const int V = a.V;
-  const int k = min(a.top_k, V);
-  build_bitmap(a, mrow, bits);
-
   const int iters = (V + kSampThreads - 1) / kSampThreads;  // warp-uniform trip count
-
-  // ---- radix select on klo: 12 + 12 + 8 bits, most significant first ----
   if (threadIdx.x == 0) {
     sm.prefix = 0u;
     sm.pmask = 0u;
@@ -463,9 +802,9 @@ __global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
       bool act = false;
       unsigned int bin = 0;
       if (v < V) {
-        const ValB x = val_b(a, bits, L[v], v);
-        act = (x.klo & pmask) == prefix;
-        bin = (x.klo >> sh) & bmask;
+        const unsigned int klo = okey32(val_b(a, bits, L[v], v).lo);
+        act = (klo & pmask) == prefix;
+        bin = (klo >> sh) & bmask;
       }
       hist_add(sm.hist, bin, act);
     }
@@ -478,7 +817,6 @@ __global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
       const int lo = threadIdx.x * per;
       unsigned int mine = 0;
       for (int i = 0; i < per; ++i) mine += sm.hist[lo + i];
-      // inclusive suffix sum over lanes (lane l: bins >= lo)
       unsigned int suf = mine;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -492,7 +830,10 @@ __global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
         int bs = lo;
         for (int i = per - 1; i >= 0; --i) {
           const unsigned int c = sm.hist[lo + i];
-          if (acc + c >= (unsigned)need) { bs = lo + i; break; }
+          if (acc + c >= (unsigned)need) {
+            bs = lo + i;
+            break;
+          }
           acc += c;
         }
         sm.bstar = bs;
@@ -508,20 +849,17 @@ __global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
     __syncthreads();  // everyone has read bcount before the next pass clears hist
     if (bcount <= 1024u) break;
   }
-  const unsigned int tau = sm.prefix;  // klo threshold (low unresolved bits 0)
+  const unsigned int tau = sm.prefix;  // lower-bound key threshold (low unresolved bits 0)
   const bool tie_path = exact && sm.bcount > 1024u;
   __syncthreads();
 
-  // ---- gather the superset {khi >= tau} ----
-  // On the tie path the many non-penalised entries equal to tau are taken
-  // only as the first `need` of them in vocab order (the later ones cannot
-  // reach the top k: they tie in value and lose on index).
+  // gather the superset {key(hi) >= tau}
   for (int it = 0; it < iters; ++it) {
     const int v = it * kSampThreads + threadIdx.x;
     if (v < V) {
       const ValB x = val_b(a, bits, L[v], v);
-      if (x.khi >= tau) {
-        if (!(tie_path && !x.pen && x.klo == tau)) push_cand(sm, x.val, v);
+      if (okey32(x.hi) >= tau) {
+        if (!(tie_path && !x.pen && okey32(x.lo) == tau)) push_cand(sm, x.val, v);
       }
     }
   }
@@ -534,7 +872,7 @@ __global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
       double val = 0.0;
       if (v < V) {
         const ValB x = val_b(a, bits, L[v], v);
-        f = !x.pen && x.klo == tau;
+        f = !x.pen && okey32(x.lo) == tau;
         val = x.val;
       }
       // rank of this flag among the block's flags in index order
@@ -557,27 +895,37 @@ __global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
     }
   }
   __syncthreads();
-  if (sm.overflow) {
-    if (threadIdx.x == 0) {
-      a.out[b] = -2;
-      record_error(a.err, kErrSamplerArgs);
-    }
-    return;
-  }
-  const int nc = sm.ncand;
+  if (sm.overflow) return false;
+  rank_candidates(sm, sm.ncand, k);
+  return true;
+}
 
-  // ---- exact order of the candidates: rank by counting ----
-  for (int i = threadIdx.x; i < nc; i += kSampThreads) {
-    const unsigned long long ki = sm.ckey[i];
-    const int vi = sm.cidx[i];
-    int rank = 0;
-    for (int j = 0; j < nc; ++j) rank += precedes(sm.ckey[j], sm.cidx[j], ki, vi) ? 1 : 0;
-    if (rank < k) {
-      sm.order[rank] = vi;
-      sm.val[rank] = key_to_double(ki);
+template <int NV4>
+__global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  SmemB &sm = *reinterpret_cast<SmemB *>(smem_dyn);
+  uint32_t *bits = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemB));
+  const int b = blockIdx.x;
+  const int mrow = a.row_map ? a.row_map[b] : b;
+  const float *L = a.logits + (size_t)mrow * a.ld;
+  const int V = a.V;
+  const int k = min(a.top_k, V);
+  Row<NV4> row;
+  row.L = L;
+  row.V = V;
+  row.vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
+  row.load();
+  build_bitmap(a, mrow, bits);
+
+  if (!fast_select_b<NV4>(a, bits, row, sm, k)) {
+    if (!general_select_b(a, bits, L, sm, k)) {
+      if (threadIdx.x == 0) {
+        a.out[b] = -2;
+        record_error(a.err, kErrSamplerArgs);
+      }
+      return;
     }
   }
-  __syncthreads();
 
   // ---- src/tensor_ffi_adapter.php:180-204 over the k survivors ----
   if (a.T < 0.01) {
@@ -586,14 +934,14 @@ __global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
   }
   for (int i = threadIdx.x; i < k; i += kSampThreads) sm.p[i] = snai_exp(__ddiv_rn(sm.val[i], a.T));
   __syncthreads();
-  __shared__ double sum_sh;
   if (threadIdx.x == 0) {
     double s = 0.0;
     for (int i = 0; i < k; ++i) s = __dadd_rn(s, sm.p[i]);
-    sum_sh = s;
+    sm.cum[0] = s;  // the sum, handed to all threads
   }
   __syncthreads();
-  const double sum = sum_sh;
+  const double sum = sm.cum[0];
+  __syncthreads();
   for (int i = threadIdx.x; i < k; i += kSampThreads) sm.p[i] = __ddiv_rn(sm.p[i], sum);
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -608,7 +956,10 @@ __global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
     const double r = __dmul_rn((double)a.uniforms[b], cum);
     int id = sm.order[0];
     for (int i = 0; i < nf; ++i)
-      if (r <= sm.cum[i]) { id = sm.order[i]; break; }
+      if (r <= sm.cum[i]) {
+        id = sm.order[i];
+        break;
+      }
     a.out[b] = id;
   }
 }
@@ -618,9 +969,18 @@ __global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
 // ---------------------------------------------------------------------------
 
 int check_sample_args(const SampleLaunch &s) {
-  if (s.rows < 0) { set_error("sampler: rows < 0"); return -2; }
-  if (s.V < 1 || s.V > kMaxVocab) { set_error("sampler: vocab %d outside [1, %d]", s.V, kMaxVocab); return -2; }
-  if (s.ld < s.V) { set_error("sampler: row stride %lld < vocab %d", s.ld, s.V); return -2; }
+  if (s.rows < 0) {
+    set_error("sampler: rows < 0");
+    return -2;
+  }
+  if (s.V < 1 || s.V > kMaxVocab) {
+    set_error("sampler: vocab %d outside [1, %d]", s.V, kMaxVocab);
+    return -2;
+  }
+  if (s.ld < s.V) {
+    set_error("sampler: row stride %lld < vocab %d", s.ld, s.V);
+    return -2;
+  }
   if (!s.logits || !s.out_ids || (s.rows > 0 && !s.uniforms && s.temperature > 0.01)) {
     set_error("sampler: null logits / uniforms / output");
     return -2;
@@ -636,12 +996,39 @@ int check_sample_args(const SampleLaunch &s) {
       return -2;
     }
   } else if (s.variant == 1) {
-    if (s.top_k < 1 || s.top_k > kMaxTopK) { set_error("sampler variant 1: top_k %d outside [1, %d]", s.top_k, kMaxTopK); return -2; }
+    if (s.top_k < 1 || s.top_k > kMaxTopK) {
+      set_error("sampler variant 1: top_k %d outside [1, %d]", s.top_k, kMaxTopK);
+      return -2;
+    }
   } else {
     set_error("sampler: unknown variant %d", s.variant);
     return -2;
   }
   return 0;
+}
+
+template <int NV4>
+static void launch_a(const SampArgs &a, int rows, size_t sm, cudaStream_t st) {
+  static unsigned long long done = 0;  // attribute set, one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(done & (1ull << dev))) {
+    cudaFuncSetAttribute(sample_a_kernel<NV4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    done |= 1ull << dev;
+  }
+  sample_a_kernel<NV4><<<rows, kSampThreads, sm, st>>>(a);
+}
+
+template <int NV4>
+static void launch_b(const SampArgs &a, int rows, size_t sm, cudaStream_t st) {
+  static unsigned long long done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(done & (1ull << dev))) {
+    cudaFuncSetAttribute(sample_b_kernel<NV4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    done |= 1ull << dev;
+  }
+  sample_b_kernel<NV4><<<rows, kSampThreads, sm, st>>>(a);
 }
 
 int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
@@ -667,24 +1054,25 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   a.out = s.out_ids;
   a.err = s.err;
   const size_t bitmap = (size_t)((s.V + 31) / 32) * 4;
-  int dev = 0;
-  cudaGetDevice(&dev);
+  const int layers = (s.V + 2047) / 2048;
   if (s.variant == 0) {
     const size_t sm = sizeof(SmemA) + bitmap;
-    static unsigned long long set_mask = 0;
-    if (!(set_mask & (1ull << dev))) {
-      cudaFuncSetAttribute(sample_a_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      set_mask |= 1ull << dev;
-    }
-    sample_a_kernel<<<s.rows, kSampThreads, sm, stream>>>(a);
+    if (layers <= 4)
+      launch_a<4>(a, s.rows, sm, stream);
+    else if (layers <= 8)
+      launch_a<8>(a, s.rows, sm, stream);
+    else
+      launch_a<0>(a, s.rows, sm, stream);
   } else {
     const size_t sm = sizeof(SmemB) + bitmap;
-    static unsigned long long set_mask = 0;
-    if (!(set_mask & (1ull << dev))) {
-      cudaFuncSetAttribute(sample_b_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      set_mask |= 1ull << dev;
-    }
-    sample_b_kernel<<<s.rows, kSampThreads, sm, stream>>>(a);
+    if (layers <= 4)
+      launch_b<4>(a, s.rows, sm, stream);
+    else if (layers <= 8)
+      launch_b<8>(a, s.rows, sm, stream);
+    else if (layers <= 16)
+      launch_b<16>(a, s.rows, sm, stream);
+    else
+      launch_b<0>(a, s.rows, sm, stream);
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
