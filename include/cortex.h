@@ -201,6 +201,22 @@ CORTEX_API int cortex_profile_enable(void *state, int on);
 CORTEX_API int cortex_profile_read(void *state, int kind, long long *launches, double *ms, double *bytes,
                                    double *flops);
 
+/* cortex_forward_batch for callers that must not allocate GPU memory during
+ * the call (their device memory belongs to another allocator or a fixed
+ * pool, or an allocation would stall a latency-critical path).  No
+ * counterpart in the reference.  Same arguments, results and per-slot
+ * effects as cortex_forward_batch; the pass's activation scratch lives in
+ * one 8 MiB array in the library's device image instead of the state's
+ * buffers, and the call makes no cudaMalloc/cudaFree or other allocating
+ * GPU call.  Rows are processed in chunks that fit the array; a model whose
+ * single row needs more than 8 MiB of scratch is rejected with an error.
+ * The first call on a device looks the array's address up (make that first
+ * call before any stream capture).  All calls on a device share the array:
+ * calls that overlap on the GPU (two streams, two threads) race.  Nothing in
+ * the array has to start at zero: every byte a call reads it wrote first. */
+CORTEX_API int cortex_forward_batch_noalloc(void *state, const int *tokens, int batch, int n_tok, const int *slots,
+                                            float *logits, int flags);
+
 /* Number of kernels the state has launched since it was created. */
 CORTEX_API long long cortex_kernel_launches(void *state);
 

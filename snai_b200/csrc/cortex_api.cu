@@ -904,3 +904,110 @@ extern "C" int cortex_profile_read(void *state, int kind, long long *launches, d
 extern "C" long long cortex_kernel_launches(void *state) {
   return state ? static_cast<Engine *>(state)->launches : 0;
 }
+
+// ============================================================================
+// Forward pass without allocation
+// ============================================================================
+//
+// Some callers must not allocate GPU memory while they run: hosts whose
+// device memory is owned by another allocator (a framework's caching
+// allocator, a fixed pool handed out at start-up) or code paths where a
+// cudaMalloc would stall or fail.  cortex_forward_batch_noalloc runs the same
+// forward pass as cortex_forward_batch, but keeps the pass's activation
+// scratch (row lists, hidden states, normed inputs, q, attention output, MLP
+// intermediate) in the file-scope device array below instead of buffers the
+// state owns.  The array is kNoAllocScratchBytes on every GPU that loads this
+// library and stays resident until the process exits.
+namespace snai {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+void *g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  The host-side
+// name is only a stand-in for the symbol, so the address is looked up once
+// per device (with that device current) and cached.
+int noalloc_scratch(int dev, void **out) {
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("device %d outside the no-alloc table", dev);
+    return -2;
+  }
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess || !p) {
+      set_error("cudaGetSymbolAddress(no-alloc scratch) failed on device %d: %s", dev, cudaGetErrorString(err));
+      return -4;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+// Lays the per-row activation buffers of `rows` rows out in `base`; returns
+// the bytes used (the same buffers create_engine carves for m_max rows).
+size_t carve_rows(Engine &e, int rows, void *base) {
+  const size_t M = rows, D = e.d.D, F = e.d.F;
+  Carver a;
+  a.add(&e.rows_d, M);
+  a.add(&e.outrows_d, M);
+  a.add(&e.h, M * D);
+  a.add(&e.x, M * D * sizeof(float));
+  a.add(&e.q, M * (size_t)e.d.att_ch);
+  a.add(&e.att, M * D * sizeof(float));
+  a.add(&e.u, M * F * sizeof(float));
+  a.add(&e.xo, M * D * sizeof(float));
+  if (base) a.place(base);
+  return a.off;
+}
+
+}  // namespace
+}  // namespace snai
+
+extern "C" int cortex_forward_batch_noalloc(void *state, const int *tokens, int batch, int n_tok, const int *slots,
+                                            float *logits, int flags) {
+  clear_error();
+  if (!state) {
+    set_error("state is NULL");
+    return -1;
+  }
+  Engine &e = *static_cast<Engine *>(state);
+  DeviceGuard g(e.device);
+  void *scratch = nullptr;
+  int rc = noalloc_scratch(e.device, &scratch);
+  if (rc) return rc;
+  // rows per chunk that fit the scratch (chunks of any count keep batches unlimited)
+  Engine probe = {};
+  probe.d = e.d;
+  const size_t one = carve_rows(probe, 1, nullptr);
+  int rows = (int)std::min<size_t>((size_t)e.m_max, kNoAllocScratchBytes / std::max<size_t>(one, 1));
+  while (rows > 0 && carve_rows(probe, rows, nullptr) > kNoAllocScratchBytes) --rows;
+  if (rows < 1) {
+    set_error("no-alloc forward: one row of this model needs %zu bytes of scratch, more than the %zu-byte array",
+              one, kNoAllocScratchBytes);
+    return -2;
+  }
+  // Point the pass at the static scratch, run it, restore the state's own buffers.
+  RowDesc *rows_d = e.rows_d;
+  int2 *outrows_d = e.outrows_d;
+  float *h = e.h, *q = e.q;
+  void *x = e.x, *att = e.att, *u = e.u, *xo = e.xo;
+  const int m_max = e.m_max;
+  carve_rows(e, rows, scratch);
+  e.m_max = rows;
+  rc = forward_batch(e, tokens, batch, n_tok, slots, logits, flags);
+  e.rows_d = rows_d;
+  e.outrows_d = outrows_d;
+  e.h = h;
+  e.q = q;
+  e.x = x;
+  e.att = att;
+  e.u = u;
+  e.xo = xo;
+  e.m_max = m_max;
+  return rc;
+}
