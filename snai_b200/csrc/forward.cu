@@ -345,13 +345,23 @@ static bool tc_path(const Engine &e, int M) {
   return e.precision != kFP32 && M >= 64 && e.d.D % 16 == 0 && e.d.D >= 64;
 }
 
-constexpr int kTcBN = 128;
-constexpr int kTcStages = 3;
+static int sm_count(int dev) {
+  static int cached[64] = {};
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
 
-template <typename TIn, class Epi>
-static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
-  using Sm = TcSmem<kTcBN, kTcStages>;
-  auto kern = gemm_tc_kernel<TIn, kTcBN, kTcStages, 2, Epi>;
+// Persistent tcgen05 GEMM (gemm_tcp_kernel): 128 x BN tiles, one CTA per SM.
+template <typename TIn, int BN, class Epi>
+static int launch_tcp(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
+  constexpr int STAGES = BN == 256 ? 4 : 6;
+  using Sm = TcpSmem<BN, STAGES>;
+  auto kern = gemm_tcp_kernel<TIn, BN, STAGES, Epi>;
   static unsigned long long attr_set = 0;  // per instantiation, one bit per device
   if (!(attr_set & (1ull << e.device))) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Sm::kBytes) != cudaSuccess) {
@@ -362,14 +372,21 @@ static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *
   }
   CUtensorMap ta, tb;
   const bool bf = sizeof(TIn) == 2;
-  if (!make_tmap(&ta, A, bf, K, M, kTcBM) || !make_tmap(&tb, W, bf, K, N, kTcBN)) {
+  if (!make_tmap(&ta, A, bf, K, M, kTcBM) || !make_tmap(&tb, W, bf, K, N, BN)) {
     set_error("cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", M, N, K);
     return -5;
   }
-  dim3 grid((M + kTcBM - 1) / kTcBM, (N + kTcBN - 1) / kTcBN);
-  kern<<<grid, 128, Sm::kBytes, e.stream>>>(ta, tb, M, N, K, epi, e.err_d);
+  const int tiles = ((M + kTcBM - 1) / kTcBM) * ((N + BN - 1) / BN);
+  const int grid = std::min(tiles, sm_count(e.device));
+  kern<<<grid, 320, Sm::kBytes, e.stream>>>(ta, tb, M, N, K, epi, e.err_d);
   e.launches++;
   return 0;
+}
+
+template <typename TIn, class Epi>
+static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
+  if (N >= 2048) return launch_tcp<TIn, 256>(e, M, N, K, A, W, epi);
+  return launch_tcp<TIn, 128>(e, M, N, K, A, W, epi);
 }
 
 template <class Epi>

@@ -1,16 +1,10 @@
 // gemm_tc.cuh - C[M,N] = A[M,K] * W[N,K]^T on sm_100a tensor cores.
 //
 // A (activations) and W (weights, row = output feature, the reference's
-// row-major Matrix layout core/cortex.nim:24-27) are both K-major.  One CTA
-// computes one 128 x BN tile:
-//   warp 0 / lane 0 : TMA producer, STAGES-deep shared-memory ring of
-//                     128-byte-wide K slices (SWIZZLE_128B), one mbarrier pair
-//                     per stage;
-//   warp 1          : allocates BN TMEM columns; lane 0 issues
-//                     tcgen05.mma (M=128, N=BN, fp32 accumulate in TMEM) and
-//                     releases each stage with tcgen05.commit;
-//   all 4 warps     : epilogue, each warp reading its 32 TMEM lanes (= 32 rows)
-//                     with tcgen05.ld and handing 16-column runs to `Epi`.
+// row-major Matrix layout core/cortex.nim:24-27) are both K-major and staged
+// by TMA as 128-byte-wide K slices with the 128-byte swizzle; tcgen05.mma
+// (M = 128, N = BN, fp32 accumulate in TMEM) consumes them and the epilogue
+// reads TMEM back with tcgen05.ld.
 // TIn = __nv_bfloat16 -> kind::f16 (bf16 x bf16), TIn = float -> kind::tf32.
 // Rows >= M and columns >= N are zero-filled by TMA and never stored; K tails
 // are zero-filled and contribute nothing.  Every wait is bounded (common.cuh).
@@ -34,15 +28,6 @@ template <> struct TcKind<float> {
 };
 
 constexpr int kTcBM = 128;
-
-template <int BN, int STAGES>
-struct TcSmem {
-  static constexpr int kABytes = kTcBM * 128;
-  static constexpr int kBBytes = BN * 128;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = STAGES * kStageBytes;
-  static constexpr int kBytes = kBarOffset + 256 + 1024;  // barriers + alignment slack
-};
 
 // Shared-memory matrix descriptor of a K-major tile stored as rows of 128
 // bytes with the 128-byte swizzle (8-row atoms 1024 bytes apart).
@@ -86,25 +71,58 @@ __device__ __forceinline__ void tc_mma<float>(uint32_t tmem_d, uint64_t adesc, u
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
-template <typename TIn, int BN, int STAGES, int MIN_BLOCKS, class Epi>
-__global__ void __launch_bounds__(128, MIN_BLOCKS)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                   int K, Epi epi, int *err) {
-  using Sm = TcSmem<BN, STAGES>;
+}  // namespace snai
+
+namespace snai {
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int BN, int STAGES>
+struct TcpSmem {
+  static constexpr int kABytes = kTcBM * 128;
+  static constexpr int kBBytes = BN * 128;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kBytes = kBarOffset + 256 + 1024;
+};
+
+// Persistent, warp-specialised C = A * W^T.  One CTA per SM walks the tiles
+// t = blockIdx.x, + gridDim.x, ... (M-fastest, so CTAs running together share
+// weight tiles in L2).  Roles:
+//   warp 0 lane 0   TMA producer over a STAGES-deep ring (all tiles, one
+//                   running k-block counter);
+//   warp 1          allocates 2*BN TMEM columns (two accumulators); lane 0
+//                   issues the tcgen05.mma of tile i into accumulator i % 2;
+//   warps 2..9      epilogue: two warps per 32-lane TMEM quarter, each taking
+//                   half of the tile's columns; wait for accumulator i % 2,
+//                   tcgen05.ld, hand 16-column runs to Epi, release the
+//                   accumulator; this overlaps the MMAs of tile i + 1.
+// All waits are bounded (common.cuh); a failed wait records an error and the
+// CTA winds down.
+template <typename TIn, int BN, int STAGES, class Epi>
+__global__ void __launch_bounds__(320, 1)
+    gemm_tcp_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                    int K, Epi epi, int *err) {
+  using Sm = TcpSmem<BN, STAGES>;
   constexpr int BK = TcKind<TIn>::kBK;
   constexpr int KSTEPS = BK / TcKind<TIn>::kUK;
   constexpr uint32_t IDESC = tc_idesc<TIn, BN>();
+  constexpr uint32_t TCOLS = 2 * BN;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + Sm::kBarOffset);
   uint64_t *empty = full + STAGES;
-  uint64_t *accb = empty + STAGES;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(accb + 1);
+  uint64_t *tfull = empty + STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(tempty + 2);
   int *cta_fail = reinterpret_cast<int *>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kTcBM, n0 = blockIdx.y * BN;
+  const int num_m = (M + kTcBM - 1) / kTcBM;
+  const int num_tiles = num_m * ((N + BN - 1) / BN);
   const int num_kb = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -112,7 +130,10 @@ __global__ void __launch_bounds__(128, MIN_BLOCKS)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accb, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);
+    }
     *cta_fail = 0;
     fence_barrier_init();
   }
@@ -121,7 +142,7 @@ __global__ void __launch_bounds__(128, MIN_BLOCKS)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, BN);
+    tmem_alloc(tmem_holder, TCOLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -129,72 +150,93 @@ __global__ void __launch_bounds__(128, MIN_BLOCKS)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 0 && lane == 0) {
-    // ---- TMA producer ----
-    int issued = 0;
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-      if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, kErrWaitEmpty)) {
-        atomicExch(cta_fail, 1);
-        break;
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int m0 = (tile % num_m) * kTcBM, n0 = (tile / num_m) * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, kErrWaitEmpty) || *(volatile int *)cta_fail) {
+            atomicExch(cta_fail, 1);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], Sm::kStageBytes);
+          uint8_t *st = smem + s * Sm::kStageBytes;
+          tma_load_2d(st, &tmA, &full[s], kb * BK, m0);
+          tma_load_2d(st + Sm::kABytes, &tmB, &full[s], kb * BK, n0);
+        }
       }
-      if (*(volatile int *)cta_fail) break;
-      mbar_arrive_expect_tx(&full[s], Sm::kStageBytes);
-      uint8_t *st = smem + s * Sm::kStageBytes;
-      tma_load_2d(st, &tmA, &full[s], kb * BK, m0);
-      tma_load_2d(st + Sm::kABytes, &tmB, &full[s], kb * BK, n0);
-      ++issued;
+      // do not leave while a copy into this CTA's shared memory is in flight
+      for (int j = it - 1; j >= 0 && j >= it - STAGES; --j)
+        if (!mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, err, kErrWaitDrain)) break;
     }
-    // Do not leave while a copy into this CTA's shared memory is in flight.
-    for (int kb = issued - 1; kb >= 0 && kb >= issued - STAGES; --kb) {
-      const int s = kb % STAGES;
-      if (!mbar_wait_bounded(&full[s], (uint32_t)(kb / STAGES) & 1u, err, kErrWaitDrain)) break;
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int it = 0, tc = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++tc) {
+        const int acc = tc & 1;
+        if (!mbar_wait_bounded(&tempty[acc], ((uint32_t)(tc >> 1) & 1u) ^ 1u, err, kErrWaitEmpty)) {
+          atomicExch(cta_fail, 1);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait_bounded(&full[s], ph, err, kErrWaitFull) || *(volatile int *)cta_fail) {
+            atomicExch(cta_fail, 1);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + s * Sm::kStageBytes);
+          const uint64_t adesc = sw128_desc(a0), bdesc = sw128_desc(a0 + Sm::kABytes);
+#pragma unroll
+          for (int k = 0; k < KSTEPS; ++k)
+            tc_mma<TIn>(d, adesc + 2u * k, bdesc + 2u * k, IDESC, (kb | k) != 0 ? 1u : 0u);
+          tc_commit(&empty[s]);
+        }
+        tc_commit(&tfull[acc]);
+      }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer ----
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-      if (!mbar_wait_bounded(&full[s], ph, err, kErrWaitFull)) {
+  } else {
+    // epilogue warps 2..9: TMEM lane quarter = warp % 4, column half by warp
+    const int q = warp & 3;
+    const int c_lo = ((warp - 2) >> 2) * (BN / 2);
+    int tc = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tc) {
+      const int acc = tc & 1;
+      if (!mbar_wait_bounded(&tfull[acc], (uint32_t)(tc >> 1) & 1u, err, kErrWaitAccum) ||
+          *(volatile int *)cta_fail) {
         atomicExch(cta_fail, 1);
         break;
       }
       tc_fence_after();
-      const uint32_t a0 = smem_u32(smem + s * Sm::kStageBytes);
-      const uint32_t b0 = a0 + Sm::kABytes;
-      const uint64_t adesc = sw128_desc(a0), bdesc = sw128_desc(b0);
-#pragma unroll
-      for (int k = 0; k < KSTEPS; ++k) {
-        // +32 bytes per K step inside the swizzle atom (start address is in 16-byte units)
-        tc_mma<TIn>(tmem, adesc + 2u * k, bdesc + 2u * k, IDESC, (kb | k) != 0 ? 1u : 0u);
+      const int m0 = (tile % num_m) * kTcBM, n0 = (tile / num_m) * BN;
+      const int row = m0 + q * 32 + lane;
+      const uint32_t tbase = tmem + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c = c_lo; c < c_lo + BN / 2; c += 16) {
+        if (n0 + c >= N) break;  // warp-uniform
+        float v[16];
+        tmem_ld16(tbase + (uint32_t)c, v);
+        if (row < M) epi.store(row, n0 + c, v, min(16, N - (n0 + c)));
       }
-      tc_commit(&empty[s]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
     }
-    tc_commit(accb);
   }
   __syncwarp();
-
-  // ---- epilogue: TMEM -> registers -> Epi ----
-  const bool acc_ok = mbar_wait_bounded(accb, 0, err, kErrWaitAccum);
-  tc_fence_after();
-  if (acc_ok && !*(volatile int *)cta_fail) {
-    const int row = m0 + warp * 32 + lane;
-    const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16);
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      if (n0 + c >= N) break;  // warp-uniform
-      float v[16];
-      tmem_ld16(tbase + (uint32_t)c, v);
-      if (row < M) {
-        const int cnt = min(16, N - (n0 + c));
-        epi.store(row, n0 + c, v, cnt);
-      }
-    }
-  }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, BN);
+  if (warp == 1) tmem_dealloc(tmem, TCOLS);
 }
 
 }  // namespace snai

@@ -1,9 +1,14 @@
 // sampler.cu - the reference's two logits -> token samplers on sm_100a.
 //
-// One CTA of 512 threads per row; a row of up to 32768 logits is held in
-// registers (thread t owns the 16-byte chunks t, t+512, ...), larger rows are
-// re-read from L2 on every pass.  Both kernels reproduce the PHP code's
-// double-precision decisions bit for bit for given logits and uniform u.
+// Persistent CTAs of 512 threads, each taking rows b, b+grid, ...; while a row
+// is processed the next one is prefetched into L2 (cp.async.bulk.prefetch).
+// A row of up to 32768 logits is held in registers (thread t owns the 16-byte
+// chunks t, t+512, ...); larger rows are re-read from L2 on every pass.
+// Both kernels reproduce the PHP code's double-precision decisions bit for
+// bit for given logits and uniform u.  Bulk passes work on the raw fp32
+// logits with a few instructions per entry; exact double arithmetic is spent
+// only on penalised entries (the history, usually a few hundred) and on the
+// handful of entries near a decision.
 //
 // Variant A (src/snai_inference.php:151-195).
 //   t_v = fp32(L_v / T); penalised ids (the unique history, a bitmap in shared
@@ -11,11 +16,13 @@
 //   (T <= 0.01): first index of the maximum.  Otherwise p_v = exp(t_v - max)
 //   in double (snai_exp.h), S = sequential sum in vocab order, r = u*S, and
 //   the id is the first v whose running sum reaches r.
-//   The kernel replaces the sequential running sums by parallel ones with a
-//   proven error bound and accepts the id only when r is farther from the
-//   running sums around it than the bound ("certified"):
-//     tier 1: p_v from fp32 expf (error bound per element: expf is within
-//             2 ulp, the argument's rounding to float adds |x| 2^-24);
+//   For T > 0, t is monotone in L, so the maximum over unpenalised entries is
+//   fp32(max L / T) and only entries within a few ulps of max L can attain it.
+//   The sequential running sums are replaced by parallel ones with a proven
+//   error bound, and an id is accepted only when r is farther from the running
+//   sums around it than the bound ("certified"):
+//     tier 1: p_v = 2^(L_v*(log2e/T) - max*log2e) from ex2.approx, one
+//             relative bound for the whole row;
 //     tier 2: p_v from the contract exponential itself (no exp error);
 //     tier 3: warp 0 runs the sequential loop.
 //   Each tier is exact whenever it answers, so the id is always the
@@ -25,15 +32,16 @@
 //   val_v = L_v - rep for ids in the input set, else L_v (double).  The
 //   stable descending sort + top_k keeps the k smallest (-val, v).  Fast
 //   path: a histogram of fp32 lower bounds of val over distance bins below
-//   the row maximum finds a threshold bin holding the k-th largest; every
-//   element whose fp32 upper bound reaches that bin is gathered (a superset
-//   of the top k), sorted exactly by (val desc, v asc), and the PHP softmax
-//   / top-p / draw runs sequentially over the k survivors.  Rows the fast
-//   path cannot settle (non-finite maxima, huge exact ties) go through a
-//   general radix select.
+//   the row maximum finds the bin of the k-th largest; every entry whose next
+//   float above its lower bound reaches that bin is gathered (a superset of
+//   the top k), sorted exactly by (val desc, v asc), and the PHP softmax /
+//   top-p / draw runs sequentially over the k survivors.  Rows the fast path
+//   cannot settle (non-finite values, huge exact ties) take a general radix
+//   select.
 #include <cfloat>
 #include <climits>
 #include <cmath>
+#include <algorithm>
 #include <cstdio>
 
 #include "common.cuh"
@@ -45,16 +53,16 @@ namespace snai {
 constexpr int kSampThreads = 512;
 constexpr int kSampWarps = kSampThreads / 32;
 constexpr int kMaxTopK = 1024;
-constexpr int kCandCap = 4096;   // exact-sort capacity (general path)
+constexpr int kCandCap = 4096;   // exact-sort capacity
 constexpr int kFastCand = 2048;  // candidates the fast path accepts
 constexpr int kMaxVocab = 1 << 19;
 constexpr int kMaxSeg = kMaxVocab / 2048;
-constexpr int kSegGroup = 32;    // segments reduced per shared-memory round
 
 struct SampArgs {
   const float *logits;
   long long ld;
   const int *row_map;
+  int rows;
   int V;
   const int *hist;
   long long hist_ld;
@@ -72,23 +80,52 @@ struct SampArgs {
 // shared helpers
 // ---------------------------------------------------------------------------
 
+constexpr int kPenCap = 2048;  // unique history ids listed per row
+
 // Marks the row's history ids (each once, ids outside [0,V) ignored) in a
-// shared bitmap of V bits.  Ends with a barrier.
-__device__ void build_bitmap(const SampArgs &a, int mrow, uint32_t *bits) {
+// shared bitmap of V bits and lists each distinct id once in plist (the
+// thread whose atomicOr set the bit lists it).  *npen receives the count
+// (possibly above kPenCap: then the list is incomplete).  Starts and ends with
+// a barrier.
+__device__ void build_bitmap(const SampArgs &a, int mrow, uint32_t *bits, int *plist, int *npen) {
   const int words = (a.V + 31) >> 5;
+  __syncthreads();
   for (int i = threadIdx.x; i < words; i += blockDim.x) bits[i] = 0u;
+  if (threadIdx.x == 0) *npen = 0;
   __syncthreads();
   int n = a.hist_len ? a.hist_len[mrow] : a.hist_cols;
   n = min(max(n, 0), a.hist_cols);
   const int *hr = a.hist + (size_t)mrow * a.hist_ld;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int t = hr[i];
-    if (t >= 0 && t < a.V) atomicOr(&bits[t >> 5], 1u << (t & 31));
+  const int lane = threadIdx.x & 31;
+  for (int i0 = 0; i0 < n; i0 += blockDim.x) {
+    const int i = i0 + threadIdx.x;
+    const int t = i < n ? hr[i] : -1;
+    bool first = false;
+    if (t >= 0 && t < a.V) {
+      const uint32_t bit = 1u << (t & 31);
+      first = !(atomicOr(&bits[t >> 5], bit) & bit);
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, first);
+    int base = 0;
+    if (lane == 0 && m) base = atomicAdd(npen, __popc(m));
+    base = __shfl_sync(0xffffffffu, base, 0) + __popc(m & ((1u << lane) - 1u));
+    if (first && base < kPenCap) plist[base] = t;
   }
   __syncthreads();
 }
 
 __device__ __forceinline__ bool in_set(const uint32_t *bits, int v) { return (bits[v >> 5] >> (v & 31)) & 1u; }
+
+// Prefetches a row into L2 (16-byte aligned rows whose size is a multiple of 16).
+__device__ __forceinline__ void prefetch_row_l2(const float *p, int V) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15) || (V & 3)) return;
+  const unsigned bytes = (unsigned)V * 4u;
+  for (unsigned off = 0; off < bytes; off += 65536u) {
+    const unsigned n = min(65536u, bytes - off);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<const char *>(p) + off), "r"(n)
+                 : "memory");
+  }
+}
 
 // fp32(x / T) for the double T, exactly as fp32(double(x) / T):
 // q = x * (1/T) is within 2 ulp of x/T; rounding q to fp32 gives the same
@@ -104,14 +141,16 @@ __device__ __forceinline__ float div_to_f32(float x, double T, double Tinv) {
   return safe ? __double2float_rn(q) : __double2float_rn(__ddiv_rn((double)x, T));
 }
 
+// The penalty of src/snai_inference.php:160-164 applied to a stored value.
+__device__ __forceinline__ float penalise_a(float t, double rep) {
+  const double d = (double)t;
+  return d > 0.0 ? __double2float_rn(__ddiv_rn(d, rep)) : __double2float_rn(__dmul_rn(d, rep));
+}
+
 // Variant A's stored value for vocab entry v (src/snai_inference.php:153, 160-164).
 __device__ __forceinline__ float tempered(const SampArgs &a, const uint32_t *bits, float x, int v) {
-  float t = div_to_f32(x, a.T, a.Tinv);
-  if (in_set(bits, v)) {
-    const double d = (double)t;
-    t = d > 0.0 ? __double2float_rn(__ddiv_rn(d, a.rep)) : __double2float_rn(__dmul_rn(d, a.rep));
-  }
-  return t;
+  const float t = div_to_f32(x, a.T, a.Tinv);
+  return in_set(bits, v) ? penalise_a(t, a.rep) : t;
 }
 
 __device__ __forceinline__ double warp_sum_d(double v) {
@@ -145,15 +184,39 @@ __device__ double block_excl_scan(double v, double *wsum, double &tot) {
   return __dadd_rn(base, ex);
 }
 
-// A row of logits: 16-byte chunk i of thread t covers entries
-// 4*(t + 512*i) .. +3.  NV4 > 0: the row (V <= 2048*NV4) sits in registers;
-// NV4 == 0: every access reads global memory (L2 after the first pass).
+__device__ __forceinline__ float f4_at(const float4 &f, int j) { return j == 0 ? f.x : j == 1 ? f.y : j == 2 ? f.z : f.w; }
+__device__ __forceinline__ void f4_set(float4 &f, int j, float v) {
+  if (j == 0) f.x = v;
+  else if (j == 1) f.y = v;
+  else if (j == 2) f.z = v;
+  else f.w = v;
+}
+
+// The next float above f (for finite f; +-0 -> the smallest subnormal).
+__device__ __forceinline__ float next_up(float f) {
+  if (f == 0.f) return 1.401298464e-45f;
+  const unsigned u = __float_as_uint(f);
+  return __uint_as_float(f > 0.f ? u + 1u : u - 1u);
+}
+
+__device__ __forceinline__ float ex2_approx(float a) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+
+// A row of logits, 16-byte chunk i of thread t = entries 4*(t + 512*i) .. +3.
+// Entries of the history set are replaced by their exact penalised value
+// (variant-specific `pen_value`) and flagged in `pen`.  NV4 > 0: the row
+// (V <= 2048*NV4) sits in registers; NV4 == 0: every access re-reads global
+// memory and recomputes the penalised values.
 template <int NV4>
 struct Row {
   const float *L;
   int V;
   bool vec;
   float4 r[NV4 > 0 ? NV4 : 1];
+  unsigned long long pen = 0ull;
 
   __device__ __forceinline__ int layers() const { return NV4 > 0 ? NV4 : (V + 2047) / 2048; }
   __device__ __forceinline__ float4 fetch(int i) const {
@@ -166,123 +229,106 @@ struct Row {
     f.w = v0 + 3 < V ? L[v0 + 3] : 0.f;
     return f;
   }
-  __device__ __forceinline__ void load() {
+  // Loads (registers) and replaces flagged entries by their penalised value:
+  // from the side table penv (indexed by vocab id) when it is given, else
+  // computed here by pf.
+  template <class PenFn>
+  __device__ __forceinline__ void load(const uint32_t *bits, const PenFn &pf, const float *penv) {
     if constexpr (NV4 > 0) {
 #pragma unroll
       for (int i = 0; i < NV4; ++i) r[i] = fetch(i);
+#pragma unroll
+      for (int i = 0; i < NV4; ++i) {
+        const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+        if (v0 < V) {
+          const uint32_t w = (bits[v0 >> 5] >> (v0 & 31)) & 0xFu;
+          pen |= (unsigned long long)w << (4 * i);
+          if (w) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if ((w >> j) & 1u) f4_set(r[i], j, penv ? penv[v0 + j] : pf(f4_at(r[i], j)));
+          }
+        }
+      }
     }
   }
-  // Chunk layer i; with registers the choice is a chain of predicated moves,
-  // so a run-time i never sends the array to local memory.
-  __device__ __forceinline__ float4 get(int i) const {
+  // Values and penalty flags of chunk layer i (a run-time i selects among
+  // registers with predicated moves, never through local memory).
+  template <class PenFn>
+  __device__ __forceinline__ float4 get(int i, const uint32_t *bits, const PenFn &pf, uint32_t &pbits) const {
     if constexpr (NV4 > 0) {
       float4 o = r[0];
 #pragma unroll
       for (int q = 1; q < NV4; ++q)
         if (q == i) o = r[q];
+      pbits = (uint32_t)(pen >> (4 * i)) & 0xFu;
       return o;
     } else {
-      return fetch(i);
+      float4 o = fetch(i);
+      const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+      pbits = v0 < V ? (bits[v0 >> 5] >> (v0 & 31)) & 0xFu : 0u;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if ((pbits >> j) & 1u) f4_set(o, j, pf(f4_at(o, j)));
+      return o;
     }
   }
 };
-
-__device__ __forceinline__ float f4_at(const float4 &f, int j) { return j == 0 ? f.x : j == 1 ? f.y : j == 2 ? f.z : f.w; }
-__device__ __forceinline__ void f4_set(float4 &f, int j, float v) {
-  if (j == 0) f.x = v;
-  else if (j == 1) f.y = v;
-  else if (j == 2) f.z = v;
-  else f.w = v;
-}
 
 // ---------------------------------------------------------------------------
 // Variant A
 // ---------------------------------------------------------------------------
 
 struct SmemA {
-  double wp[kSegGroup][kSampWarps];  // per-warp partial sums of p
-  double we[kSegGroup][kSampWarps];  // per-warp partial sums of the error bound
   double seg[kMaxSeg];
-  double segerr[kMaxSeg];
+  double wp[32][kSampWarps];  // per-warp partial sums of 32 segments
   double wsum[kSampWarps];
-  float bmax[kSampWarps];
-  int bidx[kSampWarps];
-  double S, r, seg_base, err_base, err_tot;
+  float wf[3][kSampWarps];
+  int wi[kSampWarps];
+  double S, r, seg_base;
   int seg_star;
   int cand;
-  double cand_hi, cand_lo, ecand_hi, ecand_lo;
+  double cand_hi, cand_lo;
   int certified;
+  float M;
+  int flag;
+  int npen;
+  int plist[kPenCap];
 };
 
-// p_v and its error bound.  EXACT: the contract exponential, error 0.  Else
-// fp32 expf (CUDA: at most 2 ulp) of the argument rounded to float (relative
-// error |x| 2^-24 after exp), bounded as p~ (3e-7 + 7e-8 |x|); below -87 the
-// float result underflows and the bound is e^-87.
-template <bool EXACT>
-__device__ __forceinline__ double prob(float t, double maxv, double &err) {
-  const double xd = __dsub_rn((double)t, maxv);
-  if constexpr (EXACT) {
-    err = 0.0;
-    return snai_exp(xd);
-  } else {
-    if (!(xd >= -87.0)) {
-      err = 1.7e-38;
-      return 0.0;
-    }
-    const float xf = __double2float_rn(xd);
-    const float pf = expf(xf);
-    err = (double)pf * (3e-7 + 7e-8 * (double)fabsf(xf));
-    return (double)pf;
-  }
-}
-
-// tier 1 / tier 2 of variant A: returns the id, or -1 if not certified.
-// `tv(i)` gives this thread's chunk i of tempered values.
-template <bool EXACT, class TV>
-__device__ int certified_draw(SmemA &sm, int V, int nl, double maxv, double u, const TV &tv) {
+// Tier 1 / tier 2 of variant A: returns the id, or -1 if not certified.
+// P(i, j) gives p of entry j of this thread's chunk layer i (as a double);
+// `eps` bounds |p~ - p| / p for every entry (0 for the contract exp) and
+// `eabs` the absolute error of an entry whose p~ underflowed.
+template <class PF>
+__device__ int certified_draw(SmemA &sm, int V, int nl, double u, double eps, double eabs, const PF &P) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // ---- segment sums (segment i = chunk layer i = 2048 consecutive ids) ----
-  for (int g0 = 0; g0 < nl; g0 += kSegGroup) {
-    const int g1 = min(nl, g0 + kSegGroup);
+  for (int g0 = 0; g0 < nl; g0 += 32) {
+    const int g1 = min(nl, g0 + 32);
     for (int i = g0; i < g1; ++i) {
-      const float4 t = tv(i);
       const int v0 = (threadIdx.x + kSampThreads * i) * 4;
-      double c = 0.0, ce = 0.0;
+      double c = 0.0;
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        if (v0 + j < V) {
-          double e;
-          c = __dadd_rn(c, prob<EXACT>(f4_at(t, j), maxv, e));
-          ce += e;
-        }
+        if (v0 + j < V) c = __dadd_rn(c, P(i, j));
       c = warp_sum_d(c);
-      ce = warp_sum_d(ce);
-      if (lane == 0) {
-        sm.wp[i - g0][warp] = c;
-        sm.we[i - g0][warp] = ce;
-      }
+      if (lane == 0) sm.wp[i - g0][warp] = c;
     }
     __syncthreads();
     if (threadIdx.x < g1 - g0) {
-      double s = 0.0, e = 0.0;
-      for (int w = 0; w < kSampWarps; ++w) {
-        s = __dadd_rn(s, sm.wp[threadIdx.x][w]);
-        e += sm.we[threadIdx.x][w];
-      }
+      double s = 0.0;
+      for (int w = 0; w < kSampWarps; ++w) s = __dadd_rn(s, sm.wp[threadIdx.x][w]);
       sm.seg[g0 + threadIdx.x] = s;
-      sm.segerr[g0 + threadIdx.x] = e;
     }
     __syncthreads();
   }
   if (threadIdx.x == 0) {
-    double S = 0.0, Et = 0.0;
-    for (int s = 0; s < nl; ++s) {
-      S = __dadd_rn(S, sm.seg[s]);
-      Et += sm.segerr[s];
-    }
+    double S = 0.0;
+    for (int s = 0; s < nl; ++s) S = __dadd_rn(S, sm.seg[s]);
     const double r = __dmul_rn(u, S);
     int ss = -1;
-    double base = 0.0, run = 0.0, eb = 0.0;
+    double base = 0.0, run = 0.0;
     for (int s = 0; s < nl; ++s) {
       const double nxt = __dadd_rn(run, sm.seg[s]);
       if (nxt >= r) {
@@ -291,12 +337,9 @@ __device__ int certified_draw(SmemA &sm, int V, int nl, double maxv, double u, c
         break;
       }
       run = nxt;
-      eb += sm.segerr[s];
     }
     sm.S = S;
     sm.r = r;
-    sm.err_tot = Et;
-    sm.err_base = eb;
     sm.seg_star = ss;
     sm.seg_base = base;
     sm.cand = INT_MAX;
@@ -309,19 +352,16 @@ __device__ int certified_draw(SmemA &sm, int V, int nl, double maxv, double u, c
 
   // ---- running sums inside the crossing segment ----
   const int v0 = (threadIdx.x + kSampThreads * ss) * 4;
-  const float4 t = tv(ss);
-  double p[4] = {0.0, 0.0, 0.0, 0.0}, pe[4] = {0.0, 0.0, 0.0, 0.0};
-  double c = 0.0, ce = 0.0;
+  double p[4] = {0.0, 0.0, 0.0, 0.0};
+  double c = 0.0;
 #pragma unroll
   for (int j = 0; j < 4; ++j)
     if (v0 + j < V) {
-      p[j] = prob<EXACT>(f4_at(t, j), maxv, pe[j]);
+      p[j] = P(ss, j);
       c = __dadd_rn(c, p[j]);
-      ce += pe[j];
     }
-  double tot, etot;
+  double tot;
   const double ex = block_excl_scan(c, sm.wsum, tot);
-  const double eex = block_excl_scan(ce, sm.wsum, etot);
   double prev = __dadd_rn(sm.seg_base, ex);
   int mine = -1;
 #pragma unroll
@@ -336,25 +376,14 @@ __device__ int certified_draw(SmemA &sm, int V, int nl, double maxv, double u, c
   __syncthreads();
   const int cand = sm.cand;
   if (cand >= v0 && cand < v0 + 4 && v0 < V) {
-    double pre = __dadd_rn(sm.seg_base, ex);
-    double ep = sm.err_base + eex;
+    double pre = __dadd_rn(sm.seg_base, ex), hi = pre;
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (j < cand - v0) {
-        pre = __dadd_rn(pre, p[j]);
-        ep += pe[j];
-      }
-    double phi = pre, ehi = ep;
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (j == cand - v0) {
-        phi = __dadd_rn(pre, p[j]);
-        ehi = ep + pe[j];
-      }
+    for (int j = 0; j < 4; ++j) {
+      if (j < cand - v0) pre = __dadd_rn(pre, p[j]);
+      if (j == cand - v0) hi = __dadd_rn(pre, p[j]);
+    }
     sm.cand_lo = pre;
-    sm.cand_hi = phi;
-    sm.ecand_lo = ep;
-    sm.ecand_hi = ehi;
+    sm.cand_hi = hi;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -363,14 +392,16 @@ __device__ int certified_draw(SmemA &sm, int V, int nl, double maxv, double u, c
       // A summation tree of depth h over non-negative terms is within
       // h 2^-53 (1+o(1)) of the exact sum.  The sequential running sum at v has
       // depth v; ours at most nl + 50 (4 per chunk, 5 + 16 per reduction or
-      // scan, nl segments).  The rounding bounds below use 2^-52 (twice the
-      // first-order constant); the exp-error sums get a (1 + 1e-6) margin for
-      // their own rounding.
+      // scan, nl segments).  Rounding bounds below use 2^-52 (twice the
+      // first-order constant).  The p~ of tier 1 are within eps*p of the
+      // contract values (eabs for an entry that underflowed), so their running
+      // sums are within eps*P(1+2eps) + (v+1)*eabs of the contract's.
       const double slack = (double)(nl + 64);
-      const double Er = u * (sm.err_tot * (1.0 + 1e-6) + ((double)V + slack) * 0x1p-52 * S) + 0x1p-52 * r;
+      const double er = eps * (1.0 + 2.0 * eps) + 1e-12 * (eps > 0.0);
+      const double Er = u * (er * S + (double)V * eabs + ((double)V + slack) * 0x1p-52 * S) + 0x1p-52 * r;
       const double hi = sm.cand_hi, lo = sm.cand_lo;
-      const double Ehi = sm.ecand_hi * (1.0 + 1e-6) + ((double)cand + slack) * 0x1p-52 * hi;
-      const double Elo = sm.ecand_lo * (1.0 + 1e-6) + ((double)cand + slack) * 0x1p-52 * lo;
+      const double Ehi = er * hi + ((double)cand + 1.0) * eabs + ((double)cand + slack) * 0x1p-52 * hi;
+      const double Elo = er * lo + (double)cand * eabs + ((double)cand + slack) * 0x1p-52 * lo;
       const bool up = hi - Ehi >= r + Er;
       const bool dn = cand == 0 || lo + Elo < r - Er;
       ok = up && dn;
@@ -382,13 +413,12 @@ __device__ int certified_draw(SmemA &sm, int V, int nl, double maxv, double u, c
 }
 
 // The sequential algorithm of src/snai_inference.php:178-194, by warp 0.
-__device__ int sequential_a(const SampArgs &a, const uint32_t *bits, const float *L, double maxv, double u) {
+__device__ __noinline__ int sequential_a(const SampArgs &a, const uint32_t *bits, const float *L, double maxv, double u) {
   const int lane = threadIdx.x & 31;
   double sum = 0.0;
   for (int b = 0; b < a.V; b += 32) {
     const int v = b + lane;
-    double e;
-    const double p = v < a.V ? prob<true>(tempered(a, bits, L[v], v), maxv, e) : 0.0;
+    const double p = v < a.V ? snai_exp(__dsub_rn((double)tempered(a, bits, L[v], v), maxv)) : 0.0;
     const int cnt = min(32, a.V - b);
     for (int j = 0; j < cnt; ++j) sum = __dadd_rn(sum, __shfl_sync(0xffffffffu, p, j));
   }
@@ -396,8 +426,7 @@ __device__ int sequential_a(const SampArgs &a, const uint32_t *bits, const float
   double cum = 0.0;
   for (int b = 0; b < a.V; b += 32) {
     const int v = b + lane;
-    double e;
-    const double p = v < a.V ? prob<true>(tempered(a, bits, L[v], v), maxv, e) : 0.0;
+    const double p = v < a.V ? snai_exp(__dsub_rn((double)tempered(a, bits, L[v], v), maxv)) : 0.0;
     const int cnt = min(32, a.V - b);
     for (int j = 0; j < cnt; ++j) {
       cum = __dadd_rn(cum, __shfl_sync(0xffffffffu, p, j));
@@ -407,68 +436,17 @@ __device__ int sequential_a(const SampArgs &a, const uint32_t *bits, const float
   return 0;  // `$best_token = 0` when nothing qualifies (NaN sums)
 }
 
-template <int NV4>
-__global__ void __launch_bounds__(kSampThreads) sample_a_kernel(SampArgs a) {
-  extern __shared__ __align__(16) uint8_t smem_dyn[];
-  SmemA &sm = *reinterpret_cast<SmemA *>(smem_dyn);
-  uint32_t *bits = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemA));
-  const int b = blockIdx.x;
-  const int mrow = a.row_map ? a.row_map[b] : b;
-  const float *L = a.logits + (size_t)mrow * a.ld;
+// Exact maximum and first argmax of the stored values, computed entry by
+// entry (any T); the rare-case path.
+__device__ __noinline__ void exact_max_a(const SampArgs &a, const uint32_t *bits, const float *L, SmemA &sm, float &best, int &bi) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int V = a.V;
-
-  if (a.nan_guard) {
-    const float l0 = L[0];
-    if (l0 != l0) {
-      if (threadIdx.x == 0) a.out[b] = -1;
-      return;
-    }
-  }
-  Row<NV4> row;
-  row.L = L;
-  row.V = V;
-  row.vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
-  row.load();
-  build_bitmap(a, mrow, bits);
-  const int nl = row.layers();
-
-  // ---- pass 1: tempered values (kept in registers), maximum, first argmax ----
-  auto temper = [&](int i) {
-    float4 x = row.fetch(i);
-    const int v0 = (threadIdx.x + kSampThreads * i) * 4;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) f4_set(x, j, v0 + j < V ? tempered(a, bits, f4_at(x, j), v0 + j) : -INFINITY);
-    return x;
-  };
-  if constexpr (NV4 > 0) {
-#pragma unroll
-    for (int i = 0; i < NV4; ++i) {
-      const int v0 = (threadIdx.x + kSampThreads * i) * 4;
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        f4_set(row.r[i], j, v0 + j < V ? tempered(a, bits, f4_at(row.r[i], j), v0 + j) : -INFINITY);
-    }
-  }
-  auto tv = [&](int i) {
-    if constexpr (NV4 > 0)
-      return row.get(i);
-    else
-      return temper(i);
-  };
-  float best = -INFINITY;
-  int bi = INT_MAX;
-#pragma unroll
-  for (int i = 0; i < nl; ++i) {
-    const float4 t = tv(i);
-    const int v0 = (threadIdx.x + kSampThreads * i) * 4;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float tj = f4_at(t, j);
-      if (tj > best) {  // ids ascend along a thread's chunks: ties keep the first
-        best = tj;
-        bi = v0 + j;
-      }
+  best = -INFINITY;
+  bi = INT_MAX;
+  for (int v = threadIdx.x; v < a.V; v += kSampThreads) {
+    const float t = tempered(a, bits, L[v], v);
+    if (t > best) {  // ids ascend per thread: ties keep the first
+      best = t;
+      bi = v;
     }
   }
 #pragma unroll
@@ -480,37 +458,203 @@ __global__ void __launch_bounds__(kSampThreads) sample_a_kernel(SampArgs a) {
       bi = oi;
     }
   }
+  __syncthreads();
   if (lane == 0) {
-    sm.bmax[warp] = best;
-    sm.bidx[warp] = bi;
+    sm.wf[0][warp] = best;
+    sm.wi[warp] = bi;
   }
   __syncthreads();
-  best = sm.bmax[0];
-  bi = sm.bidx[0];
+  best = sm.wf[0][0];
+  bi = sm.wi[0];
   for (int w = 1; w < kSampWarps; ++w)
-    if (sm.bmax[w] > best || (sm.bmax[w] == best && sm.bidx[w] < bi)) {
-      best = sm.bmax[w];
-      bi = sm.bidx[w];
+    if (sm.wf[0][w] > best || (sm.wf[0][w] == best && sm.wi[w] < bi)) {
+      best = sm.wf[0][w];
+      bi = sm.wi[w];
     }
-  // PHP: max starts at -INF and only a strictly larger value moves it.
-  const bool any = best > -INFINITY;
-  const double maxv = any ? (double)best : -INFINITY;
-  if (a.T <= 0.01) {
-    if (threadIdx.x == 0) a.out[b] = any ? bi : 0;
-    return;
-  }
-  const double u = (double)a.uniforms[b];
-  if (any) {
-    int id = certified_draw<false>(sm, V, nl, maxv, u, tv);
-    if (id < 0) id = certified_draw<true>(sm, V, nl, maxv, u, tv);
-    if (id >= 0) {
-      if (threadIdx.x == 0) a.out[b] = id;
-      return;
+  __syncthreads();
+}
+
+template <int NV4>
+__global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sample_a_kernel(SampArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  SmemA &sm = *reinterpret_cast<SmemA *>(smem_dyn);
+  uint32_t *bits = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemA));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int V = a.V;
+  // side table of exact penalised values, indexed by vocab id (register rows only)
+  float *penv = reinterpret_cast<float *>(smem_dyn + sizeof(SmemA) + (((size_t)(V + 31) / 32 * 4 + 15) & ~(size_t)15));
+  const bool vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
+  const double rep = a.rep;
+  auto pen_fn = [&](float x) { return penalise_a(div_to_f32(x, a.T, a.Tinv), rep); };
+
+  for (int b = blockIdx.x; b < a.rows; b += gridDim.x) {
+    const int mrow = a.row_map ? a.row_map[b] : b;
+    const float *L = a.logits + (size_t)mrow * a.ld;
+    if (threadIdx.x == 0 && b + (int)gridDim.x < a.rows) {
+      const int nrow = a.row_map ? a.row_map[b + gridDim.x] : b + gridDim.x;
+      prefetch_row_l2(a.logits + (size_t)nrow * a.ld, V);
     }
-  }
-  if (warp == 0) {
-    const int id = sequential_a(a, bits, L, maxv, u);
-    if (lane == 0) a.out[b] = id;
+    if (a.nan_guard) {
+      const float l0 = L[0];
+      if (l0 != l0) {  // src/snai_inference.php:146
+        if (threadIdx.x == 0) a.out[b] = -1;
+        continue;
+      }
+    }
+    build_bitmap(a, mrow, bits, sm.plist, &sm.npen);
+    const int np = sm.npen;
+    const bool listed = NV4 > 0 && np <= kPenCap;
+    if (listed) {
+      for (int i = threadIdx.x; i < np; i += kSampThreads) {
+        const int h = sm.plist[i];
+        penv[h] = pen_fn(L[h]);
+      }
+      __syncthreads();
+    }
+    Row<NV4> row;
+    row.L = L;
+    row.V = V;
+    row.vec = vec;
+    row.load(bits, pen_fn, listed ? penv : nullptr);
+    const int nl = row.layers();
+
+    // ---- maximum: raw logits of unpenalised entries (t is monotone in L for
+    // T > 0), exact values of penalised ones ----
+    float xmax = -INFINITY, xabs = 0.f, pmax = -INFINITY, pabs = 0.f;
+    int pidx = INT_MAX;
+#pragma unroll
+    for (int i = 0; i < nl; ++i) {
+      uint32_t pb;
+      const float4 x = row.get(i, bits, pen_fn, pb);
+      const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (v0 + j < V) {
+          const float f = f4_at(x, j);
+          if ((pb >> j) & 1u) {
+            if (f > pmax) {
+              pmax = f;
+              pidx = v0 + j;
+            }
+            pabs = fmaxf(pabs, fabsf(f));
+          } else {
+            xmax = fmaxf(xmax, f);
+            xabs = fmaxf(xabs, fabsf(f));
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
+      xabs = fmaxf(xabs, __shfl_xor_sync(0xffffffffu, xabs, o));
+      pabs = fmaxf(pabs, __shfl_xor_sync(0xffffffffu, pabs, o));
+      const float ob = __shfl_xor_sync(0xffffffffu, pmax, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, pidx, o);
+      if (ob > pmax || (ob == pmax && oi < pidx)) {
+        pmax = ob;
+        pidx = oi;
+      }
+    }
+    if (lane == 0) {
+      sm.wf[0][warp] = xmax;
+      sm.wf[1][warp] = fmaxf(xabs, pabs);
+      sm.wf[2][warp] = pmax;
+      sm.wi[warp] = pidx;
+    }
+    __syncthreads();
+    xmax = sm.wf[0][0];
+    float tabs_in = sm.wf[1][0];
+    pmax = sm.wf[2][0];
+    pidx = sm.wi[0];
+    for (int w = 1; w < kSampWarps; ++w) {
+      xmax = fmaxf(xmax, sm.wf[0][w]);
+      tabs_in = fmaxf(tabs_in, sm.wf[1][w]);
+      if (sm.wf[2][w] > pmax || (sm.wf[2][w] == pmax && sm.wi[w] < pidx)) {
+        pmax = sm.wf[2][w];
+        pidx = sm.wi[w];
+      }
+    }
+    __syncthreads();
+    const float tmax = (xmax > -INFINITY) ? div_to_f32(xmax, a.T, a.Tinv) : -INFINITY;
+    const float M = fmaxf(tmax, pmax);
+    const bool simple = a.T > 0.0 && isfinite(M) && isfinite(xmax) && isfinite(tabs_in);
+
+    float best;
+    int bi;
+    if (simple) {
+      // first index attaining M: entries with fp32(x/T) == M have
+      // x >= (M - |M| 2^-23) T; check those exactly
+      const double lowt = (double)M - fabs((double)M) * 0x1p-22 - 1e-44;
+      const float xthr = __double2float_rd(lowt * a.T);
+      if (threadIdx.x == 0) sm.cand = (pmax == M) ? pidx : INT_MAX;
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < nl; ++i) {
+        uint32_t pb;
+        const float4 x = row.get(i, bits, pen_fn, pb);
+        const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float f = f4_at(x, j);
+          if (v0 + j < V && !((pb >> j) & 1u) && f >= xthr && div_to_f32(f, a.T, a.Tinv) == M)
+            atomicMin(&sm.cand, v0 + j);
+        }
+      }
+      __syncthreads();
+      best = M;
+      bi = sm.cand;
+      __syncthreads();
+    } else {
+      exact_max_a(a, bits, L, sm, best, bi);
+    }
+    // PHP: max starts at -INF and only a strictly larger value moves it.
+    const bool any = best > -INFINITY;
+    const double maxv = any ? (double)best : -INFINITY;
+    if (a.T <= 0.01) {
+      if (threadIdx.x == 0) a.out[b] = any ? bi : 0;
+      continue;
+    }
+    const double u = (double)a.uniforms[b];
+    int id = -1;
+    if (any && simple) {
+      // tier 1: p~ = 2^(x c - M log2e), c = fp32(log2e / T); penalised entries
+      // use their exact value t: 2^(t log2e - M log2e).
+      const float c = (float)(1.4426950408889634 * a.Tinv);
+      const float l2e = 1.44269504f;
+      const float m2 = M * l2e;
+      // |t| <= tabs for every entry (|x/T| rounded up a little)
+      const double tabs = (double)tabs_in * fmax(1.0, fabs(a.Tinv)) * (1.0 + 0x1p-20);
+      const double eps = (tabs + fabs((double)M) + 1.0) * 0x1p-21 + 0x1p-19;
+      auto P1 = [&](int i, int j) {
+        uint32_t pb;
+        const float4 x = row.get(i, bits, pen_fn, pb);
+        const float f = f4_at(x, j);
+        const float arg = ((pb >> j) & 1u) ? fmaf(f, l2e, -m2) : fmaf(f, c, -m2);
+        return (double)ex2_approx(arg);
+      };
+      id = certified_draw(sm, V, nl, u, eps, 0x1p-125, P1);
+    }
+    if (id < 0 && any) {
+      // tier 2: the contract exponential of the exact stored values
+      auto P2 = [&](int i, int j) {
+        uint32_t pb;
+        const float4 x = row.get(i, bits, pen_fn, pb);
+        const float f = f4_at(x, j);
+        const float t = ((pb >> j) & 1u) ? f : div_to_f32(f, a.T, a.Tinv);
+        return snai_exp(__dsub_rn((double)t, maxv));
+      };
+      id = certified_draw(sm, V, nl, u, 0.0, 0.0, P2);
+    }
+    if (id < 0) {
+      // tier 3
+      if (warp == 0) {
+        const int s = sequential_a(a, bits, L, maxv, u);
+        if (lane == 0) a.out[b] = s;
+      }
+    } else if (threadIdx.x == 0) {
+      a.out[b] = id;
+    }
   }
 }
 
@@ -518,11 +662,16 @@ __global__ void __launch_bounds__(kSampThreads) sample_a_kernel(SampArgs a) {
 // Variant B
 // ---------------------------------------------------------------------------
 
+// The histogram and candidate arrays live in the dynamic region after the
+// bitmap, where the penalised-value side table lived before the row was
+// loaded into registers.
+constexpr size_t kBUnionBytes = (size_t)kCandCap * 8 + (size_t)kCandCap * 4 + 4096 * 4;
+
 struct SmemB {
-  unsigned int hist[4096];
+  unsigned int *hist;        // [4096]
+  unsigned long long *ckey;  // [kCandCap] exact order key of a candidate
+  int *cidx;                 // [kCandCap]
   unsigned int wtot[kSampWarps];
-  unsigned long long ckey[kCandCap];  // exact order key of a candidate
-  int cidx[kCandCap];
   int ncand;
   unsigned int prefix, pmask;
   int need;
@@ -534,10 +683,10 @@ struct SmemB {
   double p[kMaxTopK];
   double cum[kMaxTopK];
   int overflow;
-  float fmax[kSampWarps];
-  float fsum[kSampWarps], fsq[kSampWarps];
-  int fcnt[kSampWarps];
+  float fw[3][kSampWarps];
   float R;
+  int npen;
+  int plist[kPenCap];
 };
 
 // Monotone 32-bit key of a float (NaN lowest; -0 and +0 equal, as PHP
@@ -598,23 +747,6 @@ __device__ __forceinline__ void push_cand(SmemB &sm, double val, int v) {
   }
 }
 
-// Warp-cooperative append (every lane calls it; `want` selects).
-__device__ __forceinline__ void push_cand_warp(SmemB &sm, bool want, double val, int v, int cap) {
-  const unsigned int m = __ballot_sync(0xffffffffu, want);
-  if (!m) return;
-  const int lane = threadIdx.x & 31;
-  int base = 0;
-  if (lane == 0) base = atomicAdd(&sm.ncand, __popc(m));
-  base = __shfl_sync(0xffffffffu, base, 0);
-  if (want) {
-    const int slot = base + __popc(m & ((1u << lane) - 1u));
-    if (slot < cap) {
-      sm.ckey[slot] = okey64(val);
-      sm.cidx[slot] = v;
-    }
-  }
-}
-
 // candidate i precedes candidate j in PHP's arsort order
 __device__ __forceinline__ bool precedes(unsigned long long ki, int vi, unsigned long long kj, int vj) {
   return ki > kj || (ki == kj && vi < vj);
@@ -635,59 +767,52 @@ __device__ void rank_candidates(SmemB &sm, int nc, int k) {
   __syncthreads();
 }
 
-// Fast selection (see the file comment).  Returns false when the row needs
-// the general path.  All threads return the same value.
-template <int NV4>
-__device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row<NV4> &row, SmemB &sm, int k) {
+// Fast selection (see the file comment).  The row holds lower bounds (the
+// raw logit, or fp32-round-down(L - rep) for penalised entries).  Returns
+// false (the same on every thread) when the row needs the general path.
+template <int NV4, class PenFn>
+__device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row<NV4> &row, const PenFn &pf,
+                              SmemB &sm, int k) {
   const int V = a.V, nl = row.layers();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // pass 1: maximum of the lower bounds, and their spread
+  // pass 1: maximum and spread of the lower bounds
   float mx = -INFINITY, s1 = 0.f, s2 = 0.f;
-  int cnt = 0;
 #pragma unroll
   for (int i = 0; i < nl; ++i) {
-    const float4 x = row.get(i);
+    uint32_t pb;
+    const float4 x = row.get(i, bits, pf, pb);
     const int v0 = (threadIdx.x + kSampThreads * i) * 4;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       if (v0 + j < V) {
-        const ValB e = val_b(a, bits, f4_at(x, j), v0 + j);
-        if (isfinite(e.lo)) {
-          mx = fmaxf(mx, e.lo);
-          s1 += e.lo;
-          s2 = fmaf(e.lo, e.lo, s2);
-          ++cnt;
-        } else if (e.lo > 0.f) {
-          cnt = -(1 << 24);  // +inf: leave the row to the general path
-        }
+        const float f = f4_at(x, j);
+        mx = fmaxf(mx, f);
+        s1 += f;
+        s2 = fmaf(f, f, s2);
       }
     }
   }
   mx = warp_max(mx);
   s1 = warp_sum(s1);
   s2 = warp_sum(s2);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
   if (lane == 0) {
-    sm.fmax[warp] = mx;
-    sm.fsum[warp] = s1;
-    sm.fsq[warp] = s2;
-    sm.fcnt[warp] = cnt;
+    sm.fw[0][warp] = mx;
+    sm.fw[1][warp] = s1;
+    sm.fw[2][warp] = s2;
   }
   __syncthreads();
   mx = -INFINITY;
   s1 = s2 = 0.f;
-  cnt = 0;
   for (int w = 0; w < kSampWarps; ++w) {
-    mx = fmaxf(mx, sm.fmax[w]);
-    s1 += sm.fsum[w];
-    s2 += sm.fsq[w];
-    cnt += sm.fcnt[w];
+    mx = fmaxf(mx, sm.fw[0][w]);
+    s1 += sm.fw[1][w];
+    s2 += sm.fw[2][w];
   }
   __syncthreads();
-  if (!isfinite(mx) || cnt < k) return false;
-  const float mean = s1 / cnt;
-  const float sd = sqrtf(fmaxf(s2 / cnt - mean * mean, 0.f));
+  // any infinite or NaN entry makes s1 or s2 non-finite: general path
+  if (!isfinite(mx) || !isfinite(s1) || !isfinite(s2) || V < k) return false;
+  const float mean = s1 / V;
+  const float sd = sqrtf(fmaxf(s2 / V - mean * mean, 0.f));
   float R = 2.5f * sd;
   if (!(R > 0.f) || !isfinite(R)) return false;  // all equal: ties, general path
 
@@ -699,14 +824,13 @@ __device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < nl; ++i) {
-      const float4 x = row.get(i);
+      uint32_t pb;
+      const float4 x = row.get(i, bits, pf, pb);
       const int v0 = (threadIdx.x + kSampThreads * i) * 4;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if (v0 + j < V) {
-          const float d = mx - val_b(a, bits, f4_at(x, j), v0 + j).lo;
-          if (d >= 0.f && d < R) atomicAdd(&sm.hist[min((int)(d * inv_w), 254)], 1u);
-        }
+        const float d = mx - f4_at(x, j);
+        if (v0 + j < V && d < R) atomicAdd(&sm.hist[min((int)(d * inv_w), 254)], 1u);
       }
     }
     __syncthreads();
@@ -745,24 +869,52 @@ __device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row
   R = sm.R;
   const float inv_w = 255.f / R;
 
-  // pass 3: gather every entry whose upper bound falls in a bin <= bstar
+  // pass 3: gather every entry whose next float above its lower bound falls
+  // in a bin <= bstar (a penalised entry's value lies below that float)
   if (threadIdx.x == 0) sm.ncand = 0;
   __syncthreads();
+  int mine = 0;
 #pragma unroll
   for (int i = 0; i < nl; ++i) {
-    const float4 x = row.get(i);
+    uint32_t pb;
+    const float4 x = row.get(i, bits, pf, pb);
     const int v0 = (threadIdx.x + kSampThreads * i) * 4;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      bool want = false;
-      double val = 0.0;
-      if (v0 + j < V) {
-        const ValB e = val_b(a, bits, f4_at(x, j), v0 + j);
-        const float d = mx - e.hi;
-        want = d < R && min((int)(d * inv_w), 254) <= bstar;
-        val = e.val;
+      const float d = mx - next_up(f4_at(x, j));
+      if (v0 + j < V && d < R && (int)(d * inv_w) <= bstar) ++mine;
+    }
+  }
+  // warp-aggregated slots
+  int incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  int base = 0;
+  if (lane == 31 && incl) base = atomicAdd(&sm.ncand, incl);
+  base = __shfl_sync(0xffffffffu, base, 31) + incl - mine;
+  if (mine) {
+#pragma unroll
+    for (int i = 0; i < nl; ++i) {
+      uint32_t pb;
+      const float4 x = row.get(i, bits, pf, pb);
+      const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float f = f4_at(x, j);
+        const float d = mx - next_up(f);
+        if (v0 + j < V && d < R && (int)(d * inv_w) <= bstar) {
+          if (base < kFastCand) {
+            // exact value: the logit, or logit - rep for a penalised entry
+            const double val = ((pb >> j) & 1u) ? __dsub_rn((double)row.L[v0 + j], a.rep) : (double)f;
+            sm.ckey[base] = okey64(val);
+            sm.cidx[base] = v0 + j;
+          }
+          ++base;
+        }
       }
-      push_cand_warp(sm, want, val, v0 + j, kFastCand);
     }
   }
   __syncthreads();
@@ -772,13 +924,12 @@ __device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row
   rank_candidates(sm, nc, k);
   return true;
 }
-
 // General selection: radix select on the 32-bit keys of the lower bounds
 // (12 + 12 + 8 bits), superset gather by the upper bounds, exact sort.
 // Handles ties of any size: when more than 1024 entries share the exact
 // threshold value, only the first `need` of them in vocab order are kept
 // (the later ones tie in value and lose on index).
-__device__ bool general_select_b(const SampArgs &a, const uint32_t *bits, const float *L, SmemB &sm, int k) {
+__device__ __noinline__ bool general_select_b(const SampArgs &a, const uint32_t *bits, const float *L, SmemB &sm, int k) {
   const int V = a.V;
   const int iters = (V + kSampThreads - 1) / kSampThreads;  // warp-uniform trip count
   if (threadIdx.x == 0) {
@@ -901,66 +1052,94 @@ __device__ bool general_select_b(const SampArgs &a, const uint32_t *bits, const 
 }
 
 template <int NV4>
-__global__ void __launch_bounds__(kSampThreads) sample_b_kernel(SampArgs a) {
+__global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sample_b_kernel(SampArgs a) {
   extern __shared__ __align__(16) uint8_t smem_dyn[];
   SmemB &sm = *reinterpret_cast<SmemB *>(smem_dyn);
   uint32_t *bits = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemB));
-  const int b = blockIdx.x;
-  const int mrow = a.row_map ? a.row_map[b] : b;
-  const float *L = a.logits + (size_t)mrow * a.ld;
   const int V = a.V;
   const int k = min(a.top_k, V);
-  Row<NV4> row;
-  row.L = L;
-  row.V = V;
-  row.vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
-  row.load();
-  build_bitmap(a, mrow, bits);
-
-  if (!fast_select_b<NV4>(a, bits, row, sm, k)) {
-    if (!general_select_b(a, bits, L, sm, k)) {
-      if (threadIdx.x == 0) {
-        a.out[b] = -2;
-        record_error(a.err, kErrSamplerArgs);
-      }
-      return;
-    }
-  }
-
-  // ---- src/tensor_ffi_adapter.php:180-204 over the k survivors ----
-  if (a.T < 0.01) {
-    if (threadIdx.x == 0) a.out[b] = sm.order[0];
-    return;
-  }
-  for (int i = threadIdx.x; i < k; i += kSampThreads) sm.p[i] = snai_exp(__ddiv_rn(sm.val[i], a.T));
-  __syncthreads();
+  // dynamic union region: the penalised-value side table while the row is
+  // loaded, then the candidate keys / indices and the histogram
+  uint8_t *uni = smem_dyn + sizeof(SmemB) + (((size_t)(V + 31) / 32 * 4 + 15) & ~(size_t)15);
+  float *penv = reinterpret_cast<float *>(uni);
   if (threadIdx.x == 0) {
-    double s = 0.0;
-    for (int i = 0; i < k; ++i) s = __dadd_rn(s, sm.p[i]);
-    sm.cum[0] = s;  // the sum, handed to all threads
+    sm.ckey = reinterpret_cast<unsigned long long *>(uni);
+    sm.cidx = reinterpret_cast<int *>(uni + (size_t)kCandCap * 8);
+    sm.hist = reinterpret_cast<unsigned int *>(uni + (size_t)kCandCap * 12);
   }
-  __syncthreads();
-  const double sum = sm.cum[0];
-  __syncthreads();
-  for (int i = threadIdx.x; i < k; i += kSampThreads) sm.p[i] = __ddiv_rn(sm.p[i], sum);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double cum = 0.0;
-    int nf = 0;
-    for (int i = 0; i < k; ++i) {
-      cum = __dadd_rn(cum, sm.p[i]);
-      sm.cum[i] = cum;  // $cum_check after i+1 terms is this same sum
-      nf = i + 1;
-      if (cum >= a.top_p) break;
+  const bool vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
+  const double rep = a.rep;
+  auto pen_fn = [&](float x) { return __double2float_rd(__dsub_rn((double)x, rep)); };
+
+  for (int b = blockIdx.x; b < a.rows; b += gridDim.x) {
+    const int mrow = a.row_map ? a.row_map[b] : b;
+    const float *L = a.logits + (size_t)mrow * a.ld;
+    if (threadIdx.x == 0 && b + (int)gridDim.x < a.rows) {
+      const int nrow = a.row_map ? a.row_map[b + gridDim.x] : b + gridDim.x;
+      prefetch_row_l2(a.logits + (size_t)nrow * a.ld, V);
     }
-    const double r = __dmul_rn((double)a.uniforms[b], cum);
-    int id = sm.order[0];
-    for (int i = 0; i < nf; ++i)
-      if (r <= sm.cum[i]) {
-        id = sm.order[i];
-        break;
+    build_bitmap(a, mrow, bits, sm.plist, &sm.npen);
+    const int np = sm.npen;
+    const bool listed = NV4 > 0 && np <= kPenCap;
+    if (listed) {
+      for (int i = threadIdx.x; i < np; i += kSampThreads) {
+        const int h = sm.plist[i];
+        penv[h] = pen_fn(L[h]);
       }
-    a.out[b] = id;
+      __syncthreads();
+    }
+    Row<NV4> row;
+    row.L = L;
+    row.V = V;
+    row.vec = vec;
+    row.load(bits, pen_fn, listed ? penv : nullptr);
+    __syncthreads();  // the side table's space is reused below
+
+    if (!fast_select_b<NV4>(a, bits, row, pen_fn, sm, k)) {
+      if (!general_select_b(a, bits, L, sm, k)) {
+        if (threadIdx.x == 0) {
+          a.out[b] = -2;
+          record_error(a.err, kErrSamplerArgs);
+        }
+        continue;
+      }
+    }
+
+    // ---- src/tensor_ffi_adapter.php:180-204 over the k survivors ----
+    if (a.T < 0.01) {
+      if (threadIdx.x == 0) a.out[b] = sm.order[0];
+      continue;
+    }
+    for (int i = threadIdx.x; i < k; i += kSampThreads) sm.p[i] = snai_exp(__ddiv_rn(sm.val[i], a.T));
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double s = 0.0;
+      for (int i = 0; i < k; ++i) s = __dadd_rn(s, sm.p[i]);
+      sm.cum[0] = s;  // the sum, handed to all threads
+    }
+    __syncthreads();
+    const double sum = sm.cum[0];
+    __syncthreads();
+    for (int i = threadIdx.x; i < k; i += kSampThreads) sm.p[i] = __ddiv_rn(sm.p[i], sum);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double cum = 0.0;
+      int nf = 0;
+      for (int i = 0; i < k; ++i) {
+        cum = __dadd_rn(cum, sm.p[i]);
+        sm.cum[i] = cum;  // $cum_check after i+1 terms is this same sum
+        nf = i + 1;
+        if (cum >= a.top_p) break;
+      }
+      const double r = __dmul_rn((double)a.uniforms[b], cum);
+      int id = sm.order[0];
+      for (int i = 0; i < nf; ++i)
+        if (r <= sm.cum[i]) {
+          id = sm.order[i];
+          break;
+        }
+      a.out[b] = id;
+    }
   }
 }
 
@@ -1007,28 +1186,43 @@ int check_sample_args(const SampleLaunch &s) {
   return 0;
 }
 
-template <int NV4>
-static void launch_a(const SampArgs &a, int rows, size_t sm, cudaStream_t st) {
-  static unsigned long long done = 0;  // attribute set, one bit per device
+static int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+template <class K>
+static void launch_persistent(K kern, const SampArgs &a, size_t sm, int per_sm, cudaStream_t st,
+                              unsigned long long &done) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(done & (1ull << dev))) {
-    cudaFuncSetAttribute(sample_a_kernel<NV4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     done |= 1ull << dev;
   }
-  sample_a_kernel<NV4><<<rows, kSampThreads, sm, st>>>(a);
+  const int grid = std::min(a.rows, sm_count() * per_sm);
+  kern<<<grid, kSampThreads, sm, st>>>(a);
 }
 
 template <int NV4>
-static void launch_b(const SampArgs &a, int rows, size_t sm, cudaStream_t st) {
+static void launch_a(const SampArgs &a, size_t sm, cudaStream_t st) {
+  static unsigned long long done = 0;  // attributes set, one bit per device
+  launch_persistent(sample_a_kernel<NV4>, a, sm, NV4 > 0 && NV4 <= 8 ? 2 : 1, st, done);
+}
+
+template <int NV4>
+static void launch_b(const SampArgs &a, size_t sm, cudaStream_t st) {
   static unsigned long long done = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(done & (1ull << dev))) {
-    cudaFuncSetAttribute(sample_b_kernel<NV4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    done |= 1ull << dev;
-  }
-  sample_b_kernel<NV4><<<rows, kSampThreads, sm, st>>>(a);
+  launch_persistent(sample_b_kernel<NV4>, a, sm, NV4 > 0 && NV4 <= 8 ? 2 : 1, st, done);
 }
 
 int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
@@ -1039,6 +1233,7 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   a.logits = s.logits;
   a.ld = s.ld;
   a.row_map = s.row_map;
+  a.rows = s.rows;
   a.V = s.V;
   a.hist = s.hist;
   a.hist_ld = s.hist_ld;
@@ -1053,26 +1248,29 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   a.nan_guard = s.nan_guard;
   a.out = s.out_ids;
   a.err = s.err;
-  const size_t bitmap = (size_t)((s.V + 31) / 32) * 4;
+  const size_t bitmap = ((size_t)((s.V + 31) / 32) * 4 + 15) & ~(size_t)15;
   const int layers = (s.V + 2047) / 2048;
+  const size_t side = layers <= 16 ? (size_t)s.V * 4 : 0;  // register rows keep a side table
   if (s.variant == 0) {
-    const size_t sm = sizeof(SmemA) + bitmap;
+    const size_t sm = sizeof(SmemA) + bitmap + side;
     if (layers <= 4)
-      launch_a<4>(a, s.rows, sm, stream);
+      launch_a<4>(a, sm, stream);
     else if (layers <= 8)
-      launch_a<8>(a, s.rows, sm, stream);
-    else
-      launch_a<0>(a, s.rows, sm, stream);
-  } else {
-    const size_t sm = sizeof(SmemB) + bitmap;
-    if (layers <= 4)
-      launch_b<4>(a, s.rows, sm, stream);
-    else if (layers <= 8)
-      launch_b<8>(a, s.rows, sm, stream);
+      launch_a<8>(a, sm, stream);
     else if (layers <= 16)
-      launch_b<16>(a, s.rows, sm, stream);
+      launch_a<16>(a, sm, stream);
     else
-      launch_b<0>(a, s.rows, sm, stream);
+      launch_a<0>(a, sm, stream);
+  } else {
+    const size_t sm = sizeof(SmemB) + bitmap + std::max(side, kBUnionBytes);
+    if (layers <= 4)
+      launch_b<4>(a, sm, stream);
+    else if (layers <= 8)
+      launch_b<8>(a, sm, stream);
+    else if (layers <= 16)
+      launch_b<16>(a, sm, stream);
+    else
+      launch_b<0>(a, sm, stream);
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
