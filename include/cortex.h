@@ -125,7 +125,7 @@ typedef struct snai_sample_params {
   int variant;
   double temperature;
   double rep_penalty;
-  int top_k;    /* variant 1; 1 <= top_k <= 1024 */
+  int top_k;    /* variant 1; 1 <= top_k <= 512 */
   double top_p; /* variant 1 */
   int nan_guard;
 } snai_sample_params;

@@ -52,9 +52,9 @@ namespace snai {
 
 constexpr int kSampThreads = 512;
 constexpr int kSampWarps = kSampThreads / 32;
-constexpr int kMaxTopK = 1024;
-constexpr int kCandCap = 4096;   // exact-sort capacity
-constexpr int kFastCand = 2048;  // candidates the fast path accepts
+constexpr int kMaxTopK = 512;
+constexpr int kCandCap = 2048;   // exact-sort capacity
+constexpr int kFastCand = kCandCap;  // candidates the fast path accepts
 constexpr int kMaxVocab = 1 << 19;
 constexpr int kMaxSeg = kMaxVocab / 2048;
 
@@ -80,7 +80,7 @@ struct SampArgs {
 // shared helpers
 // ---------------------------------------------------------------------------
 
-constexpr int kPenCap = 2048;  // unique history ids listed per row
+constexpr int kPenCap = 1024;  // unique history ids listed per row
 
 // Marks the row's history ids (each once, ids outside [0,V) ignored) in a
 // shared bitmap of V bits and lists each distinct id once in plist (the
@@ -113,6 +113,73 @@ __device__ void build_bitmap(const SampArgs &a, int mrow, uint32_t *bits, int *p
   }
   __syncthreads();
 }
+
+// build_bitmap for ids already in registers: id (tid + 512 r) of the row is
+// h[r] (-1 for none).
+template <int HR>
+__device__ __forceinline__ void build_bitmap_regs(int V, const int (&h)[HR], uint32_t *bits, int *plist, int *npen) {
+  const int words = (V + 31) >> 5;
+  __syncthreads();
+  for (int i = threadIdx.x; i < words; i += blockDim.x) bits[i] = 0u;
+  if (threadIdx.x == 0) *npen = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int r = 0; r < HR; ++r) {
+    const int t = h[r];
+    bool first = false;
+    if (t >= 0 && t < V) {
+      const uint32_t bit = 1u << (t & 31);
+      first = !(atomicOr(&bits[t >> 5], bit) & bit);
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, first);
+    int base = 0;
+    if (lane == 0 && m) base = atomicAdd(npen, __popc(m));
+    base = __shfl_sync(0xffffffffu, base, 0) + __popc(m & ((1u << lane) - 1u));
+    if (first && base < kPenCap) plist[base] = t;
+  }
+  __syncthreads();
+}
+
+constexpr int kHistRegs = 2;  // history ids held per thread (rows of up to 1024 ids)
+
+// Loads the history ids of a row into registers (for build_bitmap_regs).
+__device__ __forceinline__ void load_hist_regs(const SampArgs &a, int mrow, int (&h)[kHistRegs]) {
+  int n = a.hist_len ? a.hist_len[mrow] : a.hist_cols;
+  n = min(max(n, 0), a.hist_cols);
+  const int *hr = a.hist + (size_t)mrow * a.hist_ld;
+#pragma unroll
+  for (int r = 0; r < kHistRegs; ++r) {
+    const int i = threadIdx.x + 512 * r;
+    h[r] = i < n ? __ldg(hr + i) : -1;
+  }
+}
+
+// Rows of logits staged one ahead into shared memory by TMA bulk copies.
+struct RowFeeder {
+  float *stage;
+  uint64_t *bar;
+  int uses = 0;
+  // thread 0: copy row `mrow` into the stage (completion on `bar`)
+  __device__ __forceinline__ void issue(const SampArgs &a, int mrow) const {
+    const char *src = reinterpret_cast<const char *>(a.logits + (size_t)mrow * a.ld);
+    const unsigned bytes = (unsigned)a.V * 4u;
+    mbar_arrive_expect_tx(bar, bytes);
+    for (unsigned off = 0; off < bytes; off += 32768u) {
+      const unsigned n = min(32768u, bytes - off);
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              smem_u32(reinterpret_cast<char *>(stage) + off)),
+          "l"(src + off), "r"(n), "r"(smem_u32(bar))
+          : "memory");
+    }
+  }
+  __device__ __forceinline__ bool wait(int *err) {
+    const bool ok = mbar_wait_bounded(bar, (uint32_t)(uses & 1), err, kErrWaitFull);
+    ++uses;
+    return ok;
+  }
+};
 
 __device__ __forceinline__ bool in_set(const uint32_t *bits, int v) { return (bits[v >> 5] >> (v & 31)) & 1u; }
 
@@ -213,6 +280,7 @@ __device__ __forceinline__ float ex2_approx(float a) {
 template <int NV4>
 struct Row {
   const float *L;
+  const float *S = nullptr;  // the row staged in shared memory (penalised entries already replaced)
   int V;
   bool vec;
   float4 r[NV4 > 0 ? NV4 : 1];
@@ -221,6 +289,7 @@ struct Row {
   __device__ __forceinline__ int layers() const { return NV4 > 0 ? NV4 : (V + 2047) / 2048; }
   __device__ __forceinline__ float4 fetch(int i) const {
     const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+    if (S) return v0 < V ? *reinterpret_cast<const float4 *>(S + v0) : make_float4(0.f, 0.f, 0.f, 0.f);
     if (vec && v0 + 3 < V) return __ldg(reinterpret_cast<const float4 *>(L + v0));
     float4 f;
     f.x = v0 < V ? L[v0] : 0.f;
@@ -229,11 +298,10 @@ struct Row {
     f.w = v0 + 3 < V ? L[v0 + 3] : 0.f;
     return f;
   }
-  // Loads (registers) and replaces flagged entries by their penalised value:
-  // from the side table penv (indexed by vocab id) when it is given, else
-  // computed here by pf.
+  // Loads (registers) and flags penalised entries; their values come
+  // substituted from the staged row, or are computed here by pf.
   template <class PenFn>
-  __device__ __forceinline__ void load(const uint32_t *bits, const PenFn &pf, const float *penv) {
+  __device__ __forceinline__ void load(const uint32_t *bits, const PenFn &pf) {
     if constexpr (NV4 > 0) {
 #pragma unroll
       for (int i = 0; i < NV4; ++i) r[i] = fetch(i);
@@ -246,7 +314,7 @@ struct Row {
           if (w) {
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-              if ((w >> j) & 1u) f4_set(r[i], j, penv ? penv[v0 + j] : pf(f4_at(r[i], j)));
+              if (((w >> j) & 1u) && !S) f4_set(r[i], j, pf(f4_at(r[i], j)));
           }
         }
       }
@@ -275,6 +343,79 @@ struct Row {
   }
 };
 
+// Calls f(i) for every chunk layer i: a fully unrolled loop with a literal
+// trip count when the row is in registers (so every row.get(i) names a
+// fixed register), a plain loop when it streams from memory.
+template <int NV4, class F>
+__device__ __forceinline__ void for_layers(int nl, const F &f) {
+  if constexpr (NV4 > 0) {
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) f(i);
+  } else {
+    for (int i = 0; i < nl; ++i) f(i);
+  }
+}
+
+__device__ __forceinline__ int row_of(const SampArgs &a, int b) { return a.row_map ? a.row_map[b] : b; }
+
+// Start of the staging buffer: after the core struct and the bitmap, rounded
+// up to 128 bytes (bulk copies and 16-byte shared loads need 16-byte
+// alignment; the host adds kStageAlign bytes of slack).
+constexpr size_t kStageAlign = 128;
+__device__ __forceinline__ float *stage_ptr(uint8_t *smem, size_t core_bytes, int V) {
+  const uintptr_t p = reinterpret_cast<uintptr_t>(smem) + core_bytes + (size_t)((V + 31) / 32) * 4;
+  return reinterpret_cast<float *>((p + kStageAlign - 1) & ~(uintptr_t)(kStageAlign - 1));
+}
+
+// Brings row b into `row`: history bitmap and distinct-id list, the staged
+// logits with penalised entries replaced in place (pf), registers loaded;
+// then starts staging row b + gridDim.x and loading its history ids.
+// Returns the raw logit 0 of row b.
+template <int NV4, class PenFn>
+__device__ __forceinline__ float row_prologue(const SampArgs &a, int b, Row<NV4> &row, uint32_t *bits, int *plist, int *npen,
+                              RowFeeder &feed, bool staged, int (&hreg)[kHistRegs], bool hist_in_regs,
+                              const PenFn &pf) {
+  const int mrow = row_of(a, b);
+  const float *L = a.logits + (size_t)mrow * a.ld;
+  if (hist_in_regs)
+    build_bitmap_regs(a.V, hreg, bits, plist, npen);
+  else
+    build_bitmap(a, mrow, bits, plist, npen);
+  const int np = *npen;
+  row.L = L;
+  row.V = a.V;
+  row.vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
+  float l0;
+  if (staged) {
+    feed.wait(a.err);
+    float *st = feed.stage;
+    l0 = st[0];
+    __syncthreads();  // l0 read before the penalty rewrites entry 0
+    if (np <= kPenCap) {
+      for (int i = threadIdx.x; i < np; i += kSampThreads) {
+        const int h = plist[i];
+        st[h] = pf(st[h]);
+      }
+    } else {
+      for (int v = threadIdx.x; v < a.V; v += kSampThreads)
+        if (in_set(bits, v)) st[v] = pf(st[v]);
+    }
+    __syncthreads();
+    row.S = st;
+  } else {
+    l0 = L[0];
+  }
+  row.load(bits, pf);
+  __syncthreads();  // the stage has been consumed
+  const int nb = b + (int)gridDim.x;
+  if (nb < a.rows) {
+    const int nrow = row_of(a, nb);
+    if (staged && threadIdx.x == 0) feed.issue(a, nrow);
+    if (hist_in_regs) load_hist_regs(a, nrow, hreg);
+  }
+  return l0;
+}
+
 // ---------------------------------------------------------------------------
 // Variant A
 // ---------------------------------------------------------------------------
@@ -293,6 +434,7 @@ struct SmemA {
   float M;
   int flag;
   int npen;
+  uint64_t bar;  // staging barrier
   int plist[kPenCap];
 };
 
@@ -300,20 +442,28 @@ struct SmemA {
 // P(i, j) gives p of entry j of this thread's chunk layer i (as a double);
 // `eps` bounds |p~ - p| / p for every entry (0 for the contract exp) and
 // `eabs` the absolute error of an entry whose p~ underflowed.
-template <class PF>
-__device__ int certified_draw(SmemA &sm, int V, int nl, double u, double eps, double eabs, const PF &P) {
+template <int NV4, class PF>
+__device__ __forceinline__ int certified_draw(SmemA &sm, int V, int nl, double u, double eps, double eabs, const PF &P) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // ---- segment sums (segment i = chunk layer i = 2048 consecutive ids) ----
   for (int g0 = 0; g0 < nl; g0 += 32) {
     const int g1 = min(nl, g0 + 32);
-    for (int i = g0; i < g1; ++i) {
+    auto seg = [&](int i) {
       const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+      const bool full = kSampThreads * 4 * (i + 1) <= V;
       double c = 0.0;
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (v0 + j < V) c = __dadd_rn(c, P(i, j));
+      for (int j = 0; j < 4; ++j) {
+        const double pj = (full || v0 + j < V) ? P(i, j) : 0.0;
+        c = __dadd_rn(c, pj);
+      }
       c = warp_sum_d(c);
       if (lane == 0) sm.wp[i - g0][warp] = c;
+    };
+    if constexpr (NV4 > 0) {
+      for_layers<NV4>(nl, seg);  // one group: NV4 <= 32
+    } else {
+      for (int i = g0; i < g1; ++i) seg(i);
     }
     __syncthreads();
     if (threadIdx.x < g1 - g0) {
@@ -438,7 +588,8 @@ __device__ __noinline__ int sequential_a(const SampArgs &a, const uint32_t *bits
 
 // Exact maximum and first argmax of the stored values, computed entry by
 // entry (any T); the rare-case path.
-__device__ __noinline__ void exact_max_a(const SampArgs &a, const uint32_t *bits, const float *L, SmemA &sm, float &best, int &bi) {
+__device__ __noinline__ void exact_max_a(const SampArgs &a, const uint32_t *bits, const float *L, float *wf, int *wi,
+                                         float &best, int &bi) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   best = -INFINITY;
   bi = INT_MAX;
@@ -460,90 +611,83 @@ __device__ __noinline__ void exact_max_a(const SampArgs &a, const uint32_t *bits
   }
   __syncthreads();
   if (lane == 0) {
-    sm.wf[0][warp] = best;
-    sm.wi[warp] = bi;
+    wf[warp] = best;
+    wi[warp] = bi;
   }
   __syncthreads();
-  best = sm.wf[0][0];
-  bi = sm.wi[0];
+  best = wf[0];
+  bi = wi[0];
   for (int w = 1; w < kSampWarps; ++w)
-    if (sm.wf[0][w] > best || (sm.wf[0][w] == best && sm.wi[w] < bi)) {
-      best = sm.wf[0][w];
-      bi = sm.wi[w];
+    if (wf[w] > best || (wf[w] == best && wi[w] < bi)) {
+      best = wf[w];
+      bi = wi[w];
     }
   __syncthreads();
 }
 
 template <int NV4>
-__global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sample_a_kernel(SampArgs a) {
+__global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sample_a_kernel(const __grid_constant__ SampArgs a) {
   extern __shared__ __align__(16) uint8_t smem_dyn[];
   SmemA &sm = *reinterpret_cast<SmemA *>(smem_dyn);
   uint32_t *bits = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemA));
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int V = a.V;
-  // side table of exact penalised values, indexed by vocab id (register rows only)
-  float *penv = reinterpret_cast<float *>(smem_dyn + sizeof(SmemA) + (((size_t)(V + 31) / 32 * 4 + 15) & ~(size_t)15));
-  const bool vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
   const double rep = a.rep;
   auto pen_fn = [&](float x) { return penalise_a(div_to_f32(x, a.T, a.Tinv), rep); };
+  RowFeeder feed;
+  feed.stage = stage_ptr(smem_dyn, sizeof(SmemA), V);
+  feed.bar = &sm.bar;
+  const bool staged = NV4 > 0 && (V & 3) == 0 && ((a.ld & 3) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(feed.stage) & 15) == 0);
+  const bool hist_in_regs = a.hist_cols <= 512 * kHistRegs;
+  int hreg[kHistRegs];
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if ((int)blockIdx.x < a.rows) {
+    const int r0 = row_of(a, blockIdx.x);
+    if (staged && threadIdx.x == 0) feed.issue(a, r0);
+    if (hist_in_regs) load_hist_regs(a, r0, hreg);
+  }
 
   for (int b = blockIdx.x; b < a.rows; b += gridDim.x) {
-    const int mrow = a.row_map ? a.row_map[b] : b;
-    const float *L = a.logits + (size_t)mrow * a.ld;
-    if (threadIdx.x == 0 && b + (int)gridDim.x < a.rows) {
-      const int nrow = a.row_map ? a.row_map[b + gridDim.x] : b + gridDim.x;
-      prefetch_row_l2(a.logits + (size_t)nrow * a.ld, V);
-    }
-    if (a.nan_guard) {
-      const float l0 = L[0];
-      if (l0 != l0) {  // src/snai_inference.php:146
-        if (threadIdx.x == 0) a.out[b] = -1;
-        continue;
-      }
-    }
-    build_bitmap(a, mrow, bits, sm.plist, &sm.npen);
-    const int np = sm.npen;
-    const bool listed = NV4 > 0 && np <= kPenCap;
-    if (listed) {
-      for (int i = threadIdx.x; i < np; i += kSampThreads) {
-        const int h = sm.plist[i];
-        penv[h] = pen_fn(L[h]);
-      }
-      __syncthreads();
-    }
+    const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
     Row<NV4> row;
-    row.L = L;
-    row.V = V;
-    row.vec = vec;
-    row.load(bits, pen_fn, listed ? penv : nullptr);
+    const float l0 = row_prologue(a, b, row, bits, sm.plist, &sm.npen, feed, staged, hreg, hist_in_regs, pen_fn);
+    if (a.nan_guard && l0 != l0) {  // src/snai_inference.php:146
+      if (threadIdx.x == 0) a.out[b] = -1;
+      continue;
+    }
     const int nl = row.layers();
 
     // ---- maximum: raw logits of unpenalised entries (t is monotone in L for
     // T > 0), exact values of penalised ones ----
     float xmax = -INFINITY, xabs = 0.f, pmax = -INFINITY, pabs = 0.f;
     int pidx = INT_MAX;
-#pragma unroll
-    for (int i = 0; i < nl; ++i) {
+    for_layers<NV4>(nl, [&](int i) {
       uint32_t pb;
       const float4 x = row.get(i, bits, pen_fn, pb);
       const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+      // a whole layer is valid but the last (uniform test, no per-entry branch)
+      const bool full = kSampThreads * 4 * (i + 1) <= V;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if (v0 + j < V) {
-          const float f = f4_at(x, j);
-          if ((pb >> j) & 1u) {
-            if (f > pmax) {
-              pmax = f;
-              pidx = v0 + j;
-            }
-            pabs = fmaxf(pabs, fabsf(f));
-          } else {
-            xmax = fmaxf(xmax, f);
-            xabs = fmaxf(xabs, fabsf(f));
-          }
-        }
+        const float f = f4_at(x, j);
+        const bool ok = full || v0 + j < V;
+        const bool pn = (pb >> j) & 1u;
+        const float xf = (ok && !pn) ? f : -INFINITY;
+        const float pf = (ok && pn) ? f : -INFINITY;
+        xmax = fmaxf(xmax, xf);
+        xabs = fmaxf(xabs, (ok && !pn) ? fabsf(f) : 0.f);
+        pabs = fmaxf(pabs, (ok && pn) ? fabsf(f) : 0.f);
+        const bool up = pf > pmax;  // ids ascend along a thread's chunks: ties keep the first
+        pmax = up ? pf : pmax;
+        pidx = up ? v0 + j : pidx;
       }
-    }
+    });
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
@@ -589,24 +733,47 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
       const float xthr = __double2float_rd(lowt * a.T);
       if (threadIdx.x == 0) sm.cand = (pmax == M) ? pidx : INT_MAX;
       __syncthreads();
+      if constexpr (NV4 > 0) {
+        // flag the entries that can reach M, then check only those
+        unsigned long long cm = 0ull;
+        for_layers<NV4>(nl, [&](int i) {
+          uint32_t pb;
+          const float4 x = row.get(i, bits, pen_fn, pb);
+          const int v0 = (threadIdx.x + kSampThreads * i) * 4;
 #pragma unroll
-      for (int i = 0; i < nl; ++i) {
-        uint32_t pb;
-        const float4 x = row.get(i, bits, pen_fn, pb);
-        const int v0 = (threadIdx.x + kSampThreads * i) * 4;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float f = f4_at(x, j);
-          if (v0 + j < V && !((pb >> j) & 1u) && f >= xthr && div_to_f32(f, a.T, a.Tinv) == M)
-            atomicMin(&sm.cand, v0 + j);
+          for (int j = 0; j < 4; ++j) {
+            const bool c = v0 + j < V && !((pb >> j) & 1u) && f4_at(x, j) >= xthr;
+            cm |= (unsigned long long)c << (4 * i + j);
+          }
+        });
+        while (cm) {
+          const int bit = __ffsll((long long)cm) - 1;
+          cm &= cm - 1ull;
+          const int i = bit >> 2, j = bit & 3;
+          uint32_t pb;
+          const float f = f4_at(row.get(i, bits, pen_fn, pb), j);
+          if (div_to_f32(f, a.T, a.Tinv) == M) atomicMin(&sm.cand, (threadIdx.x + kSampThreads * i) * 4 + j);
         }
+      } else {
+        for_layers<NV4>(nl, [&](int i) {
+          uint32_t pb;
+          const float4 x = row.get(i, bits, pen_fn, pb);
+          const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float f = f4_at(x, j);
+            if (v0 + j < V && !((pb >> j) & 1u) && f >= xthr) {
+              if (div_to_f32(f, a.T, a.Tinv) == M) atomicMin(&sm.cand, v0 + j);
+            }
+          }
+        });
       }
       __syncthreads();
       best = M;
       bi = sm.cand;
       __syncthreads();
     } else {
-      exact_max_a(a, bits, L, sm, best, bi);
+      exact_max_a(a, bits, L, sm.wf[0], sm.wi, best, bi);
     }
     // PHP: max starts at -INF and only a strictly larger value moves it.
     const bool any = best > -INFINITY;
@@ -629,11 +796,10 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
       auto P1 = [&](int i, int j) {
         uint32_t pb;
         const float4 x = row.get(i, bits, pen_fn, pb);
-        const float f = f4_at(x, j);
-        const float arg = ((pb >> j) & 1u) ? fmaf(f, l2e, -m2) : fmaf(f, c, -m2);
-        return (double)ex2_approx(arg);
+        const float mult = ((pb >> j) & 1u) ? l2e : c;
+        return (double)ex2_approx(fmaf(f4_at(x, j), mult, -m2));
       };
-      id = certified_draw(sm, V, nl, u, eps, 0x1p-125, P1);
+      id = certified_draw<NV4>(sm, V, nl, u, eps, 0x1p-125, P1);
     }
     if (id < 0 && any) {
       // tier 2: the contract exponential of the exact stored values
@@ -644,7 +810,7 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
         const float t = ((pb >> j) & 1u) ? f : div_to_f32(f, a.T, a.Tinv);
         return snai_exp(__dsub_rn((double)t, maxv));
       };
-      id = certified_draw(sm, V, nl, u, 0.0, 0.0, P2);
+      id = certified_draw<NV4>(sm, V, nl, u, 0.0, 0.0, P2);
     }
     if (id < 0) {
       // tier 3
@@ -662,15 +828,7 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
 // Variant B
 // ---------------------------------------------------------------------------
 
-// The histogram and candidate arrays live in the dynamic region after the
-// bitmap, where the penalised-value side table lived before the row was
-// loaded into registers.
-constexpr size_t kBUnionBytes = (size_t)kCandCap * 8 + (size_t)kCandCap * 4 + 4096 * 4;
-
 struct SmemB {
-  unsigned int *hist;        // [4096]
-  unsigned long long *ckey;  // [kCandCap] exact order key of a candidate
-  int *cidx;                 // [kCandCap]
   unsigned int wtot[kSampWarps];
   int ncand;
   unsigned int prefix, pmask;
@@ -678,14 +836,16 @@ struct SmemB {
   int bstar;
   unsigned int bcount;
   int ties_left;
-  int order[kMaxTopK];
-  double val[kMaxTopK];
-  double p[kMaxTopK];
-  double cum[kMaxTopK];
   int overflow;
   float fw[3][kSampWarps];
   float R;
   int npen;
+  uint64_t bar;  // staging barrier
+  unsigned int hist[256];
+  unsigned long long ckey[kCandCap];  // exact order key of a candidate; p[] and cum[] after ranking
+  int cidx[kCandCap];
+  int order[kMaxTopK];
+  double val[kMaxTopK];
   int plist[kPenCap];
 };
 
@@ -771,14 +931,13 @@ __device__ void rank_candidates(SmemB &sm, int nc, int k) {
 // raw logit, or fp32-round-down(L - rep) for penalised entries).  Returns
 // false (the same on every thread) when the row needs the general path.
 template <int NV4, class PenFn>
-__device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row<NV4> &row, const PenFn &pf,
+__device__ __forceinline__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row<NV4> &row, const PenFn &pf,
                               SmemB &sm, int k) {
   const int V = a.V, nl = row.layers();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // pass 1: maximum and spread of the lower bounds
   float mx = -INFINITY, s1 = 0.f, s2 = 0.f;
-#pragma unroll
-  for (int i = 0; i < nl; ++i) {
+  for_layers<NV4>(nl, [&](int i) {
     uint32_t pb;
     const float4 x = row.get(i, bits, pf, pb);
     const int v0 = (threadIdx.x + kSampThreads * i) * 4;
@@ -791,7 +950,7 @@ __device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row
         s2 = fmaf(f, f, s2);
       }
     }
-  }
+  });
   mx = warp_max(mx);
   s1 = warp_sum(s1);
   s2 = warp_sum(s2);
@@ -822,8 +981,7 @@ __device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row
     const float inv_w = 255.f / R;
     for (int i = threadIdx.x; i < 256; i += kSampThreads) sm.hist[i] = 0u;
     __syncthreads();
-#pragma unroll
-    for (int i = 0; i < nl; ++i) {
+    for_layers<NV4>(nl, [&](int i) {
       uint32_t pb;
       const float4 x = row.get(i, bits, pf, pb);
       const int v0 = (threadIdx.x + kSampThreads * i) * 4;
@@ -832,7 +990,7 @@ __device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row
         const float d = mx - f4_at(x, j);
         if (v0 + j < V && d < R) atomicAdd(&sm.hist[min((int)(d * inv_w), 254)], 1u);
       }
-    }
+    });
     __syncthreads();
     if (warp == 0) {
       // inclusive prefix over bins 0..255, 8 per lane
@@ -874,8 +1032,7 @@ __device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row
   if (threadIdx.x == 0) sm.ncand = 0;
   __syncthreads();
   int mine = 0;
-#pragma unroll
-  for (int i = 0; i < nl; ++i) {
+  for_layers<NV4>(nl, [&](int i) {
     uint32_t pb;
     const float4 x = row.get(i, bits, pf, pb);
     const int v0 = (threadIdx.x + kSampThreads * i) * 4;
@@ -884,7 +1041,7 @@ __device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row
       const float d = mx - next_up(f4_at(x, j));
       if (v0 + j < V && d < R && (int)(d * inv_w) <= bstar) ++mine;
     }
-  }
+  });
   // warp-aggregated slots
   int incl = mine;
 #pragma unroll
@@ -896,8 +1053,7 @@ __device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row
   if (lane == 31 && incl) base = atomicAdd(&sm.ncand, incl);
   base = __shfl_sync(0xffffffffu, base, 31) + incl - mine;
   if (mine) {
-#pragma unroll
-    for (int i = 0; i < nl; ++i) {
+    for_layers<NV4>(nl, [&](int i) {
       uint32_t pb;
       const float4 x = row.get(i, bits, pf, pb);
       const int v0 = (threadIdx.x + kSampThreads * i) * 4;
@@ -915,7 +1071,7 @@ __device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row
           ++base;
         }
       }
-    }
+    });
   }
   __syncthreads();
   const int nc = sm.ncand;
@@ -925,7 +1081,7 @@ __device__ bool fast_select_b(const SampArgs &a, const uint32_t *bits, const Row
   return true;
 }
 // General selection: radix select on the 32-bit keys of the lower bounds
-// (12 + 12 + 8 bits), superset gather by the upper bounds, exact sort.
+// (four 8-bit digits), superset gather by the upper bounds, exact sort.
 // Handles ties of any size: when more than 1024 entries share the exact
 // threshold value, only the first `need` of them in vocab order are kept
 // (the later ones tie in value and lose on index).
@@ -939,13 +1095,11 @@ __device__ __noinline__ bool general_select_b(const SampArgs &a, const uint32_t 
     sm.ncand = 0;
     sm.overflow = 0;
   }
-  const int shifts[3] = {20, 8, 0};
-  const int widths[3] = {12, 12, 8};
   bool exact = false;
-  for (int pass = 0; pass < 3; ++pass) {
-    const int sh = shifts[pass], wd = widths[pass];
+  for (int pass = 0; pass < 4; ++pass) {
+    const int sh = 24 - 8 * pass, wd = 8;
     const unsigned int bmask = (1u << wd) - 1u;
-    for (int i = threadIdx.x; i < 4096; i += kSampThreads) sm.hist[i] = 0u;
+    for (int i = threadIdx.x; i < 256; i += kSampThreads) sm.hist[i] = 0u;
     __syncthreads();
     const unsigned int prefix = sm.prefix, pmask = sm.pmask;
     for (int it = 0; it < iters; ++it) {
@@ -995,7 +1149,7 @@ __device__ __noinline__ bool general_select_b(const SampArgs &a, const uint32_t 
       }
     }
     __syncthreads();
-    exact = (pass == 2);
+    exact = (pass == 3);
     const unsigned int bcount = sm.bcount;
     __syncthreads();  // everyone has read bcount before the next pass clears hist
     if (bcount <= 1024u) break;
@@ -1052,48 +1206,37 @@ __device__ __noinline__ bool general_select_b(const SampArgs &a, const uint32_t 
 }
 
 template <int NV4>
-__global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sample_b_kernel(SampArgs a) {
+__global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sample_b_kernel(const __grid_constant__ SampArgs a) {
   extern __shared__ __align__(16) uint8_t smem_dyn[];
   SmemB &sm = *reinterpret_cast<SmemB *>(smem_dyn);
   uint32_t *bits = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemB));
   const int V = a.V;
   const int k = min(a.top_k, V);
-  // dynamic union region: the penalised-value side table while the row is
-  // loaded, then the candidate keys / indices and the histogram
-  uint8_t *uni = smem_dyn + sizeof(SmemB) + (((size_t)(V + 31) / 32 * 4 + 15) & ~(size_t)15);
-  float *penv = reinterpret_cast<float *>(uni);
-  if (threadIdx.x == 0) {
-    sm.ckey = reinterpret_cast<unsigned long long *>(uni);
-    sm.cidx = reinterpret_cast<int *>(uni + (size_t)kCandCap * 8);
-    sm.hist = reinterpret_cast<unsigned int *>(uni + (size_t)kCandCap * 12);
-  }
-  const bool vec = ((a.ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
   const double rep = a.rep;
   auto pen_fn = [&](float x) { return __double2float_rd(__dsub_rn((double)x, rep)); };
+  RowFeeder feed;
+  feed.stage = stage_ptr(smem_dyn, sizeof(SmemB), V);
+  feed.bar = &sm.bar;
+  const bool staged = NV4 > 0 && (V & 3) == 0 && ((a.ld & 3) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(feed.stage) & 15) == 0);
+  const bool hist_in_regs = a.hist_cols <= 512 * kHistRegs;
+  int hreg[kHistRegs];
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if ((int)blockIdx.x < a.rows) {
+    const int r0 = row_of(a, blockIdx.x);
+    if (staged && threadIdx.x == 0) feed.issue(a, r0);
+    if (hist_in_regs) load_hist_regs(a, r0, hreg);
+  }
 
   for (int b = blockIdx.x; b < a.rows; b += gridDim.x) {
-    const int mrow = a.row_map ? a.row_map[b] : b;
-    const float *L = a.logits + (size_t)mrow * a.ld;
-    if (threadIdx.x == 0 && b + (int)gridDim.x < a.rows) {
-      const int nrow = a.row_map ? a.row_map[b + gridDim.x] : b + gridDim.x;
-      prefetch_row_l2(a.logits + (size_t)nrow * a.ld, V);
-    }
-    build_bitmap(a, mrow, bits, sm.plist, &sm.npen);
-    const int np = sm.npen;
-    const bool listed = NV4 > 0 && np <= kPenCap;
-    if (listed) {
-      for (int i = threadIdx.x; i < np; i += kSampThreads) {
-        const int h = sm.plist[i];
-        penv[h] = pen_fn(L[h]);
-      }
-      __syncthreads();
-    }
+    const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
     Row<NV4> row;
-    row.L = L;
-    row.V = V;
-    row.vec = vec;
-    row.load(bits, pen_fn, listed ? penv : nullptr);
-    __syncthreads();  // the side table's space is reused below
+    row_prologue(a, b, row, bits, sm.plist, &sm.npen, feed, staged, hreg, hist_in_regs, pen_fn);
 
     if (!fast_select_b<NV4>(a, bits, row, pen_fn, sm, k)) {
       if (!general_select_b(a, bits, L, sm, k)) {
@@ -1110,36 +1253,693 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
       if (threadIdx.x == 0) a.out[b] = sm.order[0];
       continue;
     }
-    for (int i = threadIdx.x; i < k; i += kSampThreads) sm.p[i] = snai_exp(__ddiv_rn(sm.val[i], a.T));
+    // the candidate keys are dead after ranking: p and the running sums reuse them
+    double *P = reinterpret_cast<double *>(sm.ckey);
+    double *C = P + kMaxTopK;
+    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = snai_exp(__ddiv_rn(sm.val[i], a.T));
     __syncthreads();
     if (threadIdx.x == 0) {
       double s = 0.0;
-      for (int i = 0; i < k; ++i) s = __dadd_rn(s, sm.p[i]);
-      sm.cum[0] = s;  // the sum, handed to all threads
+      for (int i = 0; i < k; ++i) s = __dadd_rn(s, P[i]);
+      C[0] = s;  // the sum, handed to all threads
     }
     __syncthreads();
-    const double sum = sm.cum[0];
+    const double sum = C[0];
     __syncthreads();
-    for (int i = threadIdx.x; i < k; i += kSampThreads) sm.p[i] = __ddiv_rn(sm.p[i], sum);
+    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = __ddiv_rn(P[i], sum);
     __syncthreads();
     if (threadIdx.x == 0) {
       double cum = 0.0;
       int nf = 0;
       for (int i = 0; i < k; ++i) {
-        cum = __dadd_rn(cum, sm.p[i]);
-        sm.cum[i] = cum;  // $cum_check after i+1 terms is this same sum
+        cum = __dadd_rn(cum, P[i]);
+        C[i] = cum;  // $cum_check after i+1 terms is this same sum
         nf = i + 1;
         if (cum >= a.top_p) break;
       }
       const double r = __dmul_rn((double)a.uniforms[b], cum);
       int id = sm.order[0];
       for (int i = 0; i < nf; ++i)
-        if (r <= sm.cum[i]) {
+        if (r <= C[i]) {
           id = sm.order[i];
           break;
         }
       a.out[b] = id;
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Register-row kernels: rows of at most 2048 * kRegLayers logits with a
+// 16-byte aligned start and a length that is a multiple of 4, and at most
+// kPenCap history ids.  Each row is staged into shared memory by bulk copies
+// one row ahead; the penalised entries are settled there by the threads that
+// listed them, and the row is then held in registers.  Bulk passes read the
+// registers with one to five instructions per entry and no per-entry
+// branches: penalised entries are replaced by a marker (variant A: NaN, with
+// the exact stored value in a side table; variant B: the fp32 lower bound of
+// the penalised value), so only the few entries near a decision take exact
+// double arithmetic.
+// ---------------------------------------------------------------------------
+
+constexpr int kRegLayers = 16;             // chunk layers held in registers at most
+constexpr int kSegLen = kSampThreads * 4;  // ids per chunk layer
+
+__device__ __forceinline__ float4 lds4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ float fmax4(const float4 &x) { return fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)); }
+
+template <int N>
+__device__ __forceinline__ float4 pick_layer(const float4 (&r)[N], int i) {
+  float4 o = r[0];
+#pragma unroll
+  for (int q = 1; q < N; ++q)
+    if (q == i) o = r[q];
+  return o;
+}
+
+template <int N> struct Log2 { static constexpr int v = 1 + Log2<N / 2>::v; };
+template <> struct Log2<1> { static constexpr int v = 0; };
+
+// Per-layer warp totals of N per-lane values by a reduce-scatter butterfly
+// (the file is compiled without contraction, so every + is one rounding):
+// returns the total of layer (lane >> (5 - log2 N)) (every lane of the
+// group holds it).  Each total is a tree of depth 5.
+template <int N, class T>
+__device__ __forceinline__ T warp_reduce_layers(T (&v)[N]) {
+  static_assert(N >= 1 && N <= 32 && (N & (N - 1)) == 0, "power of two");
+#pragma unroll
+  for (int step = 0; step < Log2<N>::v; ++step) {
+    const int o = 16 >> step;
+    const int n = N >> step;
+    const bool up = (threadIdx.x & o) != 0;
+#pragma unroll
+    for (int k = 0; k < n / 2; ++k) {
+      const T send = up ? v[k] : v[k + n / 2];
+      const T keep = up ? v[k + n / 2] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  T s = v[0];
+#pragma unroll
+  for (int o = 16 >> Log2<N>::v; o > 0; o >>= 1) s = s + __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Stages row b's history bitmap and id list, waits for the staged logits,
+// lets `settle(slot, id, raw)` rewrite every penalised entry in the stage
+// (it returns the value to leave there), and returns the raw logit 0.
+// Returns false (on every thread) if the staged copy never arrived.
+template <class Settle>
+__device__ __forceinline__ bool reg_prologue(const SampArgs &a, int (&hreg)[kHistRegs], uint32_t *bits, int *plist,
+                                             int *npen, float *l0raw, RowFeeder &feed, float &l0,
+                                             const Settle &settle) {
+  build_bitmap_regs(a.V, hreg, bits, plist, npen);
+  const int np = *npen;
+  float *st = feed.stage;
+  const bool ok = feed.wait(a.err);
+  for (int s = threadIdx.x; s < np; s += kSampThreads) {
+    const int h = plist[s];
+    const float raw = st[h];
+    if (h == 0) *l0raw = raw;
+    st[h] = settle(s, h, raw);
+  }
+  if (!__syncthreads_and(ok)) return false;
+  l0 = (bits[0] & 1u) ? *l0raw : st[0];
+  return true;
+}
+
+// Loads the staged row into registers (chunks past the vocab get `fill`),
+// waits until every thread has, and starts staging row b + gridDim.x.
+template <int NV4>
+__device__ __forceinline__ void reg_load(const SampArgs &a, int b, float4 (&r)[NV4], float fill, RowFeeder &feed,
+                                         int (&hreg)[kHistRegs]) {
+#pragma unroll
+  for (int i = 0; i < NV4; ++i) {
+    const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+    r[i] = v0 < a.V ? lds4(feed.stage + v0) : make_float4(fill, fill, fill, fill);
+  }
+  __syncthreads();  // the stage has been consumed
+  const int nb = b + (int)gridDim.x;
+  if (nb < a.rows) {
+    const int nrow = row_of(a, nb);
+    if (threadIdx.x == 0) feed.issue(a, nrow);
+    load_hist_regs(a, nrow, hreg);
+  }
+}
+
+struct SmemRA {
+  double wp[kRegLayers][kSampWarps];  // per-warp totals of each chunk layer
+  double segp[kRegLayers];            // penalised entries' share of each layer
+  double wsum[kSampWarps];
+  double segpen[kSegLen];             // p of the penalised entries of the crossing layer
+  float redf[4][kSampWarps];
+  int redi[2][kSampWarps];
+  double S, r, base;
+  int ss, cand, id, real_nan, nan_total;
+  float l0raw;
+  int npen;
+  uint64_t bar;
+  int plist[kPenCap];
+  float pval[kPenCap];  // exact stored value of plist[s]
+};
+
+// Certified draw (tiers 1 and 2 of variant A) over a row read through
+// acc(i) (chunk layer i of this thread: raw logits, NaN for penalised
+// entries and past the vocab).  pe(x) gives p of an unpenalised stored raw value x (0 for the NaN marker;
+// float in tier 1, whose chunk sums and per-warp layer sums are then taken in
+// fp32, double in tier 2); pp(s) gives p of penalised entry plist[s].  Returns the id, -1 if
+// not certified, -2 if the row holds a real NaN (tier 1 only checks).
+template <int NV4, class ACC, class PE, class PP>
+__device__ __forceinline__ int draw_reg(SmemRA &sm, const ACC &acc, int V, int np, int expect_nan, double u,
+                                        double eps, double eabs, bool count_nan, const PE &pe, const PP &pp) {
+  using PT = decltype(pe(0.f));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int SH = 5 - Log2<NV4>::v;
+  PT part[NV4];
+  int nanc = 0;
+#pragma unroll
+  for (int i = 0; i < NV4; ++i) {
+    const float4 x = acc(i);
+    const PT p0 = pe(x.x), p1 = pe(x.y), p2 = pe(x.z), p3 = pe(x.w);
+    if (count_nan) nanc += (x.x != x.x) + (x.y != x.y) + (x.z != x.z) + (x.w != x.w);
+    part[i] = (p0 + p1) + (p2 + p3);
+  }
+  const PT lt = warp_reduce_layers<NV4>(part);
+  if ((lane & ((1 << SH) - 1)) == 0) sm.wp[lane >> SH][warp] = (double)lt;
+  double pq[kPenCap / kSampThreads];
+#pragma unroll
+  for (int q = 0; q < kPenCap / kSampThreads; ++q) {
+    const int s = threadIdx.x + q * kSampThreads;
+    pq[q] = 0.0;
+    if (s < np) {
+      pq[q] = pp(s);
+      atomicAdd(&sm.segp[sm.plist[s] / kSegLen], pq[q]);
+    }
+  }
+  if (count_nan) {
+    nanc = warp_sum_i(nanc);
+    if (lane == 0) sm.redi[0][warp] = nanc;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    double seg = 0.0;
+    if (lane < NV4) {
+      for (int w = 0; w < kSampWarps; ++w) seg = __dadd_rn(seg, sm.wp[lane][w]);
+      seg = __dadd_rn(seg, sm.segp[lane]);
+      sm.segp[lane] = 0.0;  // ready for the next draw
+    }
+    double incl = seg;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl = __dadd_rn(incl, n);
+    }
+    double excl = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (lane == 0) excl = 0.0;
+    const double S = __shfl_sync(0xffffffffu, incl, 31);
+    const double rr = __dmul_rn(u, S);
+    const unsigned hit = __ballot_sync(0xffffffffu, lane < NV4 && incl >= rr);
+    const int ss = hit ? __ffs(hit) - 1 : 0;
+    const double base = __shfl_sync(0xffffffffu, excl, ss);
+    int nt = 0;
+    if (count_nan) nt = warp_sum_i(lane < kSampWarps ? sm.redi[0][lane] : 0);
+    if (lane == 0) {
+      int code = ss;
+      if (count_nan && (nt != expect_nan || sm.real_nan)) code = -2;
+      else if (!(isfinite(S) && isfinite(rr) && hit && u >= 0.0 && u <= 1.0)) code = -1;
+      sm.S = S;
+      sm.r = rr;
+      sm.base = base;
+      sm.ss = code;
+      sm.cand = INT_MAX;
+    }
+  }
+  __syncthreads();
+  const int ss = sm.ss;
+  if (ss < 0) return ss;
+#pragma unroll
+  for (int q = 0; q < kPenCap / kSampThreads; ++q) {
+    const int s = threadIdx.x + q * kSampThreads;
+    if (s < np) {
+      const int h = sm.plist[s];
+      if (h / kSegLen == ss) sm.segpen[h % kSegLen] = pq[q];
+    }
+  }
+  __syncthreads();
+  // ---- running sums inside the crossing layer ----
+  const double S = sm.S, rr = sm.r;
+  const int v0 = (threadIdx.x + kSampThreads * ss) * 4;
+  const float4 x = acc(ss);
+  double p[4];
+  double c = 0.0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float f = f4_at(x, j);
+    p[j] = v0 + j >= V ? 0.0 : (f == f ? (double)pe(f) : sm.segpen[(v0 + j) % kSegLen]);
+    c = __dadd_rn(c, p[j]);
+  }
+  double tot;
+  const double ex = block_excl_scan(c, sm.wsum, tot);
+  double prev = __dadd_rn(sm.base, ex);
+  int mine = -1;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const double cur = __dadd_rn(prev, p[j]);
+    if (mine < 0 && v0 + j < V && cur >= rr) mine = j;
+    prev = cur;
+  }
+  if (mine >= 0) atomicMin(&sm.cand, v0 + mine);
+  __syncthreads();
+  const int cand = sm.cand;
+  if (cand == INT_MAX) {
+    if (threadIdx.x == 0) sm.id = -1;
+  } else if (cand >= v0 && cand < v0 + 4) {
+    double lo = __dadd_rn(sm.base, ex), hi = lo;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j == cand - v0) hi = __dadd_rn(lo, p[j]);
+      if (j < cand - v0) lo = __dadd_rn(lo, p[j]);
+    }
+    // Error model: every p~ is within eps*p (+ eabs if it underflowed) of
+    // the contract value; every computed sum is a tree over non-negative
+    // terms of depth at most nl + np + 64 (chunk, butterfly, warp, layer,
+    // penalised atomics, scan) against the sequential sum's depth of at most
+    // V; 2^-52 per level is twice the first-order rounding constant.
+    const double slack = (double)(NV4 + np + 64);
+    const double er = eps * (1.0 + 2.0 * eps) + 1e-12 * (eps > 0.0);
+    const double Er = u * (er * S + (double)V * eabs + ((double)V + slack) * 0x1p-52 * S) + 0x1p-52 * rr;
+    const double Ehi = er * hi + ((double)cand + 1.0) * eabs + ((double)cand + slack) * 0x1p-52 * hi;
+    const double Elo = er * lo + (double)cand * eabs + ((double)cand + slack) * 0x1p-52 * lo;
+    const bool up = hi - Ehi >= rr + Er;
+    const bool dn = cand == 0 || lo + Elo < rr - Er;
+    sm.id = (up && dn) ? cand : -1;
+  }
+  __syncthreads();
+  return sm.id;
+}
+
+// Tier 2 of the register-row kernel: the contract exponential of the exact
+// stored values, reading the raw row from global memory (a rare path, kept
+// out of line so it does not weigh on the register row's allocation).
+template <int NV4>
+__device__ __noinline__ int tier2_a(const SampArgs &a, const uint32_t *bits, const float *L, SmemRA &sm, int np, double u,
+                                    double maxv) {
+  const int V = a.V;
+  const float kNaN = __int_as_float(0x7fffffff);
+  auto acc = [&](int i) {
+    const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+    float4 x = make_float4(kNaN, kNaN, kNaN, kNaN);
+    if (v0 < V) {
+      x = __ldg(reinterpret_cast<const float4 *>(L + v0));
+      const uint32_t w = (bits[v0 >> 5] >> (v0 & 31)) & 0xFu;
+      if (w & 1u) x.x = kNaN;
+      if (w & 2u) x.y = kNaN;
+      if (w & 4u) x.z = kNaN;
+      if (w & 8u) x.w = kNaN;
+    }
+    return x;
+  };
+  return draw_reg<NV4>(
+      sm, acc, V, np, 0, u, 0.0, 0.0, false,
+      [&](float x) { return x == x ? snai_exp(__dsub_rn((double)div_to_f32(x, a.T, a.Tinv), maxv)) : 0.0; },
+      [&](int s) { return snai_exp(__dsub_rn((double)sm.pval[s], maxv)); });
+}
+
+template <int NV4>
+__global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_a_reg(const __grid_constant__ SampArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  SmemRA &sm = *reinterpret_cast<SmemRA *>(smem_dyn);
+  uint32_t *bits = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemRA));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int V = a.V;
+  const float kNaN = __int_as_float(0x7fffffff);
+  RowFeeder feed;
+  feed.stage = stage_ptr(smem_dyn, sizeof(SmemRA), V);
+  feed.bar = &sm.bar;
+  int hreg[kHistRegs];
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if ((int)blockIdx.x < a.rows) {
+    const int r0 = row_of(a, blockIdx.x);
+    if (threadIdx.x == 0) feed.issue(a, r0);
+    load_hist_regs(a, r0, hreg);
+  }
+  const int npad = kSegLen * NV4 - V;  // NaN-filled entries past the vocab
+
+  // Every shared field a row reads was written after the leading barrier of
+  // that row's bitmap build, which also orders it after the previous row.
+  for (int b = blockIdx.x; b < a.rows; b += gridDim.x) {
+    if (threadIdx.x == 0) sm.real_nan = 0;
+    if (threadIdx.x < kRegLayers) sm.segp[threadIdx.x] = 0.0;
+    float l0;
+    const bool ok = reg_prologue(a, hreg, bits, sm.plist, &sm.npen, &sm.l0raw, feed, l0,
+                                 [&](int s, int h, float raw) {
+                                   if (raw != raw) sm.real_nan = 1;
+                                   sm.pval[s] = penalise_a(div_to_f32(raw, a.T, a.Tinv), a.rep);
+                                   return kNaN;
+                                 });
+    if (!ok) break;
+    const int np = sm.npen;
+    float4 r[NV4];
+    reg_load(a, b, r, kNaN, feed, hreg);
+    if (a.nan_guard && l0 != l0) {  // src/snai_inference.php:146
+      if (threadIdx.x == 0) a.out[b] = -1;
+      continue;
+    }
+
+    // ---- maximum: raw logits of unpenalised entries (t is monotone in L for
+    // T > 0; the NaN markers drop out of fmaxf), exact values of penalised ones
+    float xmax = -INFINITY, xabs = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) {
+      xmax = fmaxf(xmax, fmax4(r[i]));
+      xabs = fmaxf(xabs, fmaxf(fmaxf(fabsf(r[i].x), fabsf(r[i].y)), fmaxf(fabsf(r[i].z), fabsf(r[i].w))));
+    }
+    float pmax = -INFINITY;
+    int pidx = INT_MAX;
+    for (int s = threadIdx.x; s < np; s += kSampThreads) {
+      const float t = sm.pval[s];
+      const int h = sm.plist[s];
+      if (t > pmax || (t == pmax && h < pidx)) {
+        pmax = t;
+        pidx = h;
+      }
+      xabs = fmaxf(xabs, fabsf(t));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
+      xabs = fmaxf(xabs, __shfl_xor_sync(0xffffffffu, xabs, o));
+      const float ob = __shfl_xor_sync(0xffffffffu, pmax, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, pidx, o);
+      if (ob > pmax || (ob == pmax && oi < pidx)) {
+        pmax = ob;
+        pidx = oi;
+      }
+    }
+    if (lane == 0) {
+      sm.redf[0][warp] = xmax;
+      sm.redf[1][warp] = xabs;
+      sm.redf[2][warp] = pmax;
+      sm.redi[1][warp] = pidx;
+    }
+    if (threadIdx.x == 0) sm.cand = INT_MAX;
+    __syncthreads();
+    {
+      const int w = lane & (kSampWarps - 1);
+      xmax = sm.redf[0][w];
+      xabs = sm.redf[1][w];
+      pmax = sm.redf[2][w];
+      pidx = sm.redi[1][w];
+#pragma unroll
+      for (int o = kSampWarps / 2; o > 0; o >>= 1) {
+        xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
+        xabs = fmaxf(xabs, __shfl_xor_sync(0xffffffffu, xabs, o));
+        const float ob = __shfl_xor_sync(0xffffffffu, pmax, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, pidx, o);
+        if (ob > pmax || (ob == pmax && oi < pidx)) {
+          pmax = ob;
+          pidx = oi;
+        }
+      }
+    }
+    const float tmax = (xmax > -INFINITY) ? div_to_f32(xmax, a.T, a.Tinv) : -INFINITY;
+    const float M = fmaxf(tmax, pmax);
+    const bool simple = a.T > 0.0 && isfinite(M) && isfinite(xmax) && isfinite(xabs);
+    const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
+    const bool greedy = a.T <= 0.01;
+
+    float best = M;
+    int bi = INT_MAX;
+    if (!simple) {
+      exact_max_a(a, bits, L, sm.redf[3], sm.redi[0], best, bi);
+    } else if (greedy) {
+      // first index attaining M: entries with fp32(x/T) == M have
+      // x >= (M - |M| 2^-23) T; the chunks holding one are checked exactly
+      const double lowt = (double)M - fabs((double)M) * 0x1p-22 - 1e-44;
+      const float xthr = __double2float_rd(lowt * a.T);
+      int mc = INT_MAX;
+#pragma unroll
+      for (int i = 0; i < NV4; ++i) {
+        if (fmax4(r[i]) >= xthr) {
+          const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float f = f4_at(r[i], j);
+            if (f >= xthr && div_to_f32(f, a.T, a.Tinv) == M) mc = min(mc, v0 + j);
+          }
+        }
+      }
+      if (threadIdx.x == 0 && pmax == M) mc = min(mc, pidx);
+      if (mc != INT_MAX) atomicMin(&sm.cand, mc);
+      __syncthreads();
+      bi = sm.cand;
+    }
+    // PHP: max starts at -INF and only a strictly larger value moves it.
+    const bool any = best > -INFINITY;
+    if (greedy) {
+      if (threadIdx.x == 0) a.out[b] = any ? bi : 0;
+      continue;
+    }
+    const double maxv = any ? (double)best : -INFINITY;
+    const double u = (double)a.uniforms[b];
+    int id = -1;
+    if (any && simple) {
+      // tier 1: p~ = 2^(x c - M log2e), c = fp32(log2e / T); penalised entries
+      // use their exact value t: 2^(t log2e - M log2e).  The fp32 sums (4
+      // entries, then a depth-5 warp tree) add at most 7 * 2^-24 (1 + 2^-20)
+      // < 2^-21 to the relative error.
+      const float c = (float)(1.4426950408889634 * a.Tinv);
+      const float l2e = 1.44269504f;
+      const float m2 = M * l2e;
+      // |t| <= tabs for every entry (|x/T| rounded up a little)
+      const double tabs = (double)xabs * fmax(1.0, fabs(a.Tinv)) * (1.0 + 0x1p-20);
+      const double eps = (tabs + fabs((double)M) + 1.0) * 0x1p-21 + 0x1p-19 + 0x1p-21;
+      id = draw_reg<NV4>(
+          sm, [&](int i) { return pick_layer(r, i); }, V, np, np + npad, u, eps, 0x1p-125, true,
+          [&](float x) { return fmaxf(ex2_approx(fmaf(x, c, -m2)), 0.f); },
+          [&](int s) { return (double)fmaxf(ex2_approx(fmaf(sm.pval[s], l2e, -m2)), 0.f); });
+      if (id == -1) id = tier2_a<NV4>(a, bits, L, sm, np, u, maxv);
+    }
+    if (id < 0) {
+      // tier 3
+      if (warp == 0) {
+        const int s = sequential_a(a, bits, L, maxv, u);
+        if (lane == 0) a.out[b] = s;
+      }
+    } else if (threadIdx.x == 0) {
+      a.out[b] = id;
+    }
+  }
+}
+
+// Variant B over the register row: the fast selection of fast_select_b with
+// one fmaxf per entry for the maximum (the spread is estimated from chunk
+// layer 0), a histogram pass, and a gather by a single threshold.
+template <int NV4>
+__global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(const __grid_constant__ SampArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  SmemB &sm = *reinterpret_cast<SmemB *>(smem_dyn);
+  uint32_t *bits = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemB));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int V = a.V;
+  const int k = min(a.top_k, V);
+  const double rep = a.rep;
+  RowFeeder feed;
+  feed.stage = stage_ptr(smem_dyn, sizeof(SmemB), V);
+  feed.bar = &sm.bar;
+  int hreg[kHistRegs];
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if ((int)blockIdx.x < a.rows) {
+    const int r0 = row_of(a, blockIdx.x);
+    if (threadIdx.x == 0) feed.issue(a, r0);
+    load_hist_regs(a, r0, hreg);
+  }
+  float l0unused = 0.f;
+
+  for (int b = blockIdx.x; b < a.rows; b += gridDim.x) {
+    const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
+    float l0;
+    const bool ok = reg_prologue(a, hreg, bits, sm.plist, &sm.npen, &l0unused, feed, l0,
+                                 [&](int, int, float raw) { return __double2float_rd(__dsub_rn((double)raw, rep)); });
+    if (!ok) break;
+    float4 r[NV4];
+    reg_load(a, b, r, -INFINITY, feed, hreg);
+
+    // ---- pass 1: maximum of the lower bounds; spread from chunk layer 0 ----
+    float mx = -INFINITY, s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) mx = fmaxf(mx, fmax4(r[i]));
+    const int n0 = min(V, kSegLen);
+    if (threadIdx.x * 4 < V) {
+      const float4 x = r[0];
+      s1 = (x.x + x.y) + (x.z + x.w);
+      s2 = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, x.w * x.w)));
+    }
+    mx = warp_max(mx);
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if (lane == 0) {
+      sm.fw[0][warp] = mx;
+      sm.fw[1][warp] = s1;
+      sm.fw[2][warp] = s2;
+    }
+    if (threadIdx.x == 0) sm.ncand = 0;
+    __syncthreads();
+    {
+      const int w = lane & (kSampWarps - 1);
+      mx = sm.fw[0][w];
+      s1 = sm.fw[1][w];
+      s2 = sm.fw[2][w];
+#pragma unroll
+      for (int o = kSampWarps / 2; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      }
+    }
+    bool fast = isfinite(mx) && isfinite(s1) && isfinite(s2) && V >= k;
+    float R = 0.f;
+    if (fast) {
+      const float mean = s1 / n0;
+      const float sd = sqrtf(fmaxf(s2 / n0 - mean * mean, 0.f));
+      R = 2.5f * sd;
+      fast = R > 0.f && isfinite(R);
+    }
+    int bstar = 255;
+    // ---- pass 2: histogram of the distance below the maximum, 255 bins over [0, R)
+    for (int attempt = 0; fast && attempt < 3 && bstar >= 255; ++attempt) {
+      const float inv_w = 255.f / R;
+      for (int i = threadIdx.x; i < 256; i += kSampThreads) sm.hist[i] = 0u;
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < NV4; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float d = mx - f4_at(r[i], j);
+          if (d < R) atomicAdd(&sm.hist[min((int)(d * inv_w), 254)], 1u);
+        }
+      }
+      __syncthreads();
+      if (warp == 0) {
+        unsigned int c[8], run = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          run += sm.hist[lane * 8 + q];
+          c[q] = run;
+        }
+        unsigned int incl = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const unsigned int n = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += n;
+        }
+        const unsigned int before = incl - run;
+        int bs = 255;
+#pragma unroll
+        for (int q = 7; q >= 0; --q)
+          if (before + c[q] >= (unsigned)k) bs = lane * 8 + q;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) bs = min(bs, __shfl_xor_sync(0xffffffffu, bs, o));
+        if (lane == 0) sm.bstar = bs;
+      }
+      __syncthreads();
+      bstar = sm.bstar;
+      if (bstar >= 255) R *= 8.f;
+    }
+    fast = fast && bstar < 255;
+    if (fast) {
+      // ---- pass 3: gather.  An entry lands in a bin <= bstar only if its
+      // lower bound exceeds mx - (bstar+1) (R/255) (1 + 2^-21); every entry
+      // whose exact value reaches the least such bound has a lower bound of
+      // at least the float below it, so `g` admits a superset of the top k.
+      const double gd = (double)mx - (double)(bstar + 1) * ((double)R / 255.0) * (1.0 + 0x1p-20);
+      float g = __double2float_rd(gd);
+      g = (g == -INFINITY) ? g : __uint_as_float(g > 0.f ? __float_as_uint(g) - 1u
+                                                          : (g == 0.f ? 0x80000001u : __float_as_uint(g) + 1u));
+#pragma unroll
+      for (int i = 0; i < NV4; ++i) {
+        if (fmax4(r[i]) >= g) {
+          const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float f = f4_at(r[i], j);
+            if (f >= g) {
+              const int v = v0 + j;
+              const double val = in_set(bits, v) ? __dsub_rn((double)L[v], rep) : (double)f;
+              const int slot = atomicAdd(&sm.ncand, 1);
+              if (slot < kFastCand) {
+                sm.ckey[slot] = okey64(val);
+                sm.cidx[slot] = v;
+              }
+            }
+          }
+        }
+      }
+      __syncthreads();
+      const int nc = sm.ncand;
+      fast = nc <= kFastCand && nc >= k;
+      if (fast) rank_candidates(sm, nc, k);
+    }
+    if (!fast) {
+      __syncthreads();
+      if (!general_select_b(a, bits, L, sm, k)) {
+        if (threadIdx.x == 0) {
+          a.out[b] = -2;
+          record_error(a.err, kErrSamplerArgs);
+        }
+        __syncthreads();
+        continue;
+      }
+    }
+
+    // ---- src/tensor_ffi_adapter.php:180-204 over the k survivors ----
+    if (a.T < 0.01) {
+      if (threadIdx.x == 0) a.out[b] = sm.order[0];
+      __syncthreads();
+      continue;
+    }
+    double *P = reinterpret_cast<double *>(sm.ckey);
+    double *C = P + kMaxTopK;
+    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = snai_exp(__ddiv_rn(sm.val[i], a.T));
+    __syncthreads();
+    if (warp == 0) {
+      // sequential sum, then p / sum, cumulative sums and the draw, by lane 0
+      if (lane == 0) {
+        double s = 0.0;
+        for (int i = 0; i < k; ++i) s = __dadd_rn(s, P[i]);
+        double cum = 0.0;
+        int nf = 0;
+        for (int i = 0; i < k; ++i) {
+          cum = __dadd_rn(cum, __ddiv_rn(P[i], s));
+          C[i] = cum;  // $cum_check after i+1 terms is this same sum
+          nf = i + 1;
+          if (cum >= a.top_p) break;
+        }
+        const double rr = __dmul_rn((double)a.uniforms[b], cum);
+        int id = sm.order[0];
+        for (int i = 0; i < nf; ++i)
+          if (rr <= C[i]) {
+            id = sm.order[i];
+            break;
+          }
+        a.out[b] = id;
+      }
+    }
+    __syncthreads();
   }
 }
 
@@ -1216,13 +2016,19 @@ static void launch_persistent(K kern, const SampArgs &a, size_t sm, int per_sm, 
 template <int NV4>
 static void launch_a(const SampArgs &a, size_t sm, cudaStream_t st) {
   static unsigned long long done = 0;  // attributes set, one bit per device
-  launch_persistent(sample_a_kernel<NV4>, a, sm, NV4 > 0 && NV4 <= 8 ? 2 : 1, st, done);
+  if constexpr (NV4 == 0)
+    launch_persistent(sample_a_kernel<0>, a, sm, 1, st, done);
+  else
+    launch_persistent(sample_a_reg<NV4>, a, sm, NV4 <= 8 ? 2 : 1, st, done);
 }
 
 template <int NV4>
 static void launch_b(const SampArgs &a, size_t sm, cudaStream_t st) {
   static unsigned long long done = 0;
-  launch_persistent(sample_b_kernel<NV4>, a, sm, NV4 > 0 && NV4 <= 8 ? 2 : 1, st, done);
+  if constexpr (NV4 == 0)
+    launch_persistent(sample_b_kernel<0>, a, sm, 1, st, done);
+  else
+    launch_persistent(sample_b_reg<NV4>, a, sm, NV4 <= 8 ? 2 : 1, st, done);
 }
 
 int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
@@ -1249,25 +2055,30 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   a.out = s.out_ids;
   a.err = s.err;
   const size_t bitmap = ((size_t)((s.V + 31) / 32) * 4 + 15) & ~(size_t)15;
-  const int layers = (s.V + 2047) / 2048;
-  const size_t side = layers <= 16 ? (size_t)s.V * 4 : 0;  // register rows keep a side table
+  const int layers = (s.V + kSegLen - 1) / kSegLen;
+  // register rows: whole 16-byte chunks from 16-byte aligned row starts, and
+  // a history that fits the per-row id list
+  const bool reg = layers <= kRegLayers && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 && s.hist_cols <= kPenCap;
+  const int nv4 = !reg ? 0 : layers <= 4 ? 4 : layers <= 8 ? 8 : 16;
+  const size_t stage = reg ? (size_t)s.V * 4 + kStageAlign : 0;  // staging buffer + alignment slack
   if (s.variant == 0) {
-    const size_t sm = sizeof(SmemA) + bitmap + side;
-    if (layers <= 4)
+    const size_t sm = (reg ? sizeof(SmemRA) : sizeof(SmemA)) + bitmap + stage;
+    if (nv4 == 4)
       launch_a<4>(a, sm, stream);
-    else if (layers <= 8)
+    else if (nv4 == 8)
       launch_a<8>(a, sm, stream);
-    else if (layers <= 16)
+    else if (nv4 == 16)
       launch_a<16>(a, sm, stream);
     else
       launch_a<0>(a, sm, stream);
   } else {
-    const size_t sm = sizeof(SmemB) + bitmap + std::max(side, kBUnionBytes);
-    if (layers <= 4)
+    const size_t sm = sizeof(SmemB) + bitmap + stage;
+    if (nv4 == 4)
       launch_b<4>(a, sm, stream);
-    else if (layers <= 8)
+    else if (nv4 == 8)
       launch_b<8>(a, sm, stream);
-    else if (layers <= 16)
+    else if (nv4 == 16)
       launch_b<16>(a, sm, stream);
     else
       launch_b<0>(a, sm, stream);

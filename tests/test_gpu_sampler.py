@@ -83,7 +83,7 @@ def test_variant_a_matches_oracle(V, T, built):
 
 
 @pytest.mark.parametrize("V", [1000, 1001, 16384, 32000])
-@pytest.mark.parametrize("cfg", [(0.0, 40, 0.9), (0.7, 40, 0.9), (0.7, 50, 0.95), (1.0, 1, 0.9), (0.9, 1024, 1.0)])
+@pytest.mark.parametrize("cfg", [(0.0, 40, 0.9), (0.7, 40, 0.9), (0.7, 50, 0.95), (1.0, 1, 0.9), (0.9, 512, 1.0)])
 def test_variant_b_matches_oracle(V, cfg, built):
     T, k, p = cfg
     rng = np.random.default_rng(V + k)
@@ -121,7 +121,7 @@ def test_ties_and_edge_uniforms(built):
                       (sample_params(VARIANT_A, 0.005, 1.3, nan_guard=0), (VARIANT_A, 0.005, 1.3)),
                       (sample_params(VARIANT_B, 0.7, 0.5, 40, 0.9), (VARIANT_B, 0.7, 0.5, 40, 0.9)),
                       (sample_params(VARIANT_B, 0.0, 0.5, 40, 0.9), (VARIANT_B, 0.0, 0.5, 40, 0.9)),
-                      (sample_params(VARIANT_B, 1.0, 0.0, 1024, 1.0), (VARIANT_B, 1.0, 0.0, 1024, 1.0))]:
+                      (sample_params(VARIANT_B, 1.0, 0.0, 512, 1.0), (VARIANT_B, 1.0, 0.0, 512, 1.0))]:
         got = gpu_sample(L, hist, U, prm, hist_len=hist_len, ld=V + 36)
         assert np.array_equal(got, oracle_ids(L, hist, U, *args, hist_len=hist_len))
 
@@ -138,4 +138,4 @@ def test_nan_guard_and_argument_errors(built):
     with pytest.raises(CortexError):
         gpu_sample(L, hist, U, sample_params(VARIANT_B, 0.7, 1.1, 0, 0.9))
     with pytest.raises(CortexError):
-        gpu_sample(L, hist, U, sample_params(VARIANT_B, 0.7, 1.1, 5000, 0.9))
+        gpu_sample(L, hist, U, sample_params(VARIANT_B, 0.7, 1.1, 513, 0.9))
