@@ -1292,14 +1292,22 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
 // ---------------------------------------------------------------------------
 // Register-row kernels: rows of at most 2048 * kRegLayers logits with a
 // 16-byte aligned start and a length that is a multiple of 4, and at most
-// kPenCap history ids.  Each row is staged into shared memory by bulk copies
-// one row ahead; the penalised entries are settled there by the threads that
-// listed them, and the row is then held in registers.  Bulk passes read the
-// registers with one to five instructions per entry and no per-entry
-// branches: penalised entries are replaced by a marker (variant A: NaN, with
-// the exact stored value in a side table; variant B: the fp32 lower bound of
-// the penalised value), so only the few entries near a decision take exact
-// double arithmetic.
+// kPenCap history ids.  Row b is staged into shared memory by bulk copies
+// while row b - grid is processed, then moved into registers (thread t owns
+// the 16-byte chunks t, t + 512, ...), which frees the stage for the next
+// row.  Before that, the threads that listed the row's distinct history ids
+// settle those entries in the stage: variant A replaces them by -inf (they
+// then drop out of the maximum and of every exponential sum) and keeps
+// their exact stored values in a side table; variant B replaces them by the
+// fp32 lower bound of L - rep.  Bulk passes thus cost one to three
+// instructions per entry with no per-entry branches, and only the entries
+// near a decision take exact double arithmetic.
+//
+// Row pipeline (it = this CTA's row counter): the history bitmap and id
+// list of row it are built during row it - 1 (three rotating bitmaps, two
+// lists), the per-row counters have two copies, and block maxima are
+// shared-memory atomics on order-preserving keys, so a greedy row needs
+// three block barriers.
 // ---------------------------------------------------------------------------
 
 constexpr int kRegLayers = 16;             // chunk layers held in registers at most
@@ -1307,6 +1315,15 @@ constexpr int kSegLen = kSampThreads * 4;  // ids per chunk layer
 
 __device__ __forceinline__ float4 lds4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 __device__ __forceinline__ float fmax4(const float4 &x) { return fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)); }
+// inverse of okey32 (key 0, NaN's key, maps to -inf)
+__device__ __forceinline__ float key_to_float(unsigned int k) {
+  if (k == 0u) return -INFINITY;
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+// (value, id) key whose maximum is the largest value, then the smallest id
+__device__ __forceinline__ unsigned long long argmax_key(float t, int v) {
+  return ((unsigned long long)okey32(t) << 32) | (unsigned long long)(0xffffffffu - (unsigned int)v);
+}
 
 template <int N>
 __device__ __forceinline__ float4 pick_layer(const float4 (&r)[N], int i) {
@@ -1345,90 +1362,124 @@ __device__ __forceinline__ T warp_reduce_layers(T (&v)[N]) {
   return s;
 }
 
-__device__ __forceinline__ int warp_sum_i(int v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
+// Per-CTA row pipeline state.  [p] = row parity, bitmaps follow the struct.
+struct RowPipe {
+  uint64_t bar;  // staging barrier
+  int npen[2];   // entries in the row's distinct-id list (variant A)
+  unsigned long long pkey[2][kSampWarps];  // per-warp argmax keys of the penalised values
+  unsigned int xkey[2];
+  int cand[2];
+  float l0[2];
+  float s1[2], s2[2];
+};
+
+__device__ __forceinline__ void pipe_reset(RowPipe &p, int par) {
+  p.npen[par] = 0;
+  p.xkey[par] = 0u;
+  p.cand[par] = INT_MAX;
+  p.s1[par] = 0.f;
+  p.s2[par] = 0.f;
 }
 
-// Stages row b's history bitmap and id list, waits for the staged logits,
-// lets `settle(slot, id, raw)` rewrite every penalised entry in the stage
-// (it returns the value to leave there), and returns the raw logit 0.
-// Returns false (on every thread) if the staged copy never arrived.
-template <class Settle>
-__device__ __forceinline__ bool reg_prologue(const SampArgs &a, int (&hreg)[kHistRegs], uint32_t *bits, int *plist,
-                                             int *npen, float *l0raw, RowFeeder &feed, float &l0,
-                                             const Settle &settle) {
-  build_bitmap_regs(a.V, hreg, bits, plist, npen);
-  const int np = *npen;
-  float *st = feed.stage;
-  const bool ok = feed.wait(a.err);
-  for (int s = threadIdx.x; s < np; s += kSampThreads) {
-    const int h = plist[s];
-    const float raw = st[h];
-    if (h == 0) *l0raw = raw;
-    st[h] = settle(s, h, raw);
+// Marks the history ids in h (each thread's share, -1 for none) in a
+// cleared bitmap; with a list, the thread whose atomicOr set a bit also
+// appends the id to plist (warp-aggregated slots, count in *npen).
+__device__ __forceinline__ void mark_ids(int V, const int (&h)[kHistRegs], uint32_t *bits, int *plist, int *npen) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int r = 0; r < kHistRegs; ++r) {
+    const int t = h[r];
+    bool first = false;
+    if (t >= 0 && t < V) {
+      const uint32_t bit = 1u << (t & 31);
+      const uint32_t old = atomicOr(&bits[t >> 5], bit);
+      first = !(old & bit);
+    }
+    if (plist) {
+      const unsigned m = __ballot_sync(0xffffffffu, first);
+      int base = 0;
+      if (lane == 0 && m) base = atomicAdd(npen, __popc(m));
+      base = __shfl_sync(0xffffffffu, base, 0) + __popc(m & ((1u << lane) - 1u));
+      if (first && base < kPenCap) plist[base] = t;
+    }
   }
-  if (!__syncthreads_and(ok)) return false;
-  l0 = (bits[0] & 1u) ? *l0raw : st[0];
-  return true;
 }
 
-// Loads the staged row into registers (chunks past the vocab get `fill`),
-// waits until every thread has, and starts staging row b + gridDim.x.
-template <int NV4>
-__device__ __forceinline__ void reg_load(const SampArgs &a, int b, float4 (&r)[NV4], float fill, RowFeeder &feed,
-                                         int (&hreg)[kHistRegs]) {
-#pragma unroll
-  for (int i = 0; i < NV4; ++i) {
-    const int v0 = (threadIdx.x + kSampThreads * i) * 4;
-    r[i] = v0 < a.V ? lds4(feed.stage + v0) : make_float4(fill, fill, fill, fill);
+// Kernel start: clears the three bitmaps and both counter sets, builds the
+// bitmap of the CTA's first row and starts its staging.
+__device__ __forceinline__ void pipe_start(const SampArgs &a, RowPipe &p, uint32_t *bm, int words, RowFeeder &feed,
+                                           int (&hreg)[kHistRegs], int *plist0) {
+  if (threadIdx.x == 0) {
+    mbar_init(&p.bar, 1);
+    fence_barrier_init();
+    pipe_reset(p, 0);
+    pipe_reset(p, 1);
   }
-  __syncthreads();  // the stage has been consumed
+  for (int i = threadIdx.x; i < 3 * words; i += kSampThreads) bm[i] = 0u;
+  __syncthreads();
+  const int b0 = blockIdx.x;
+  if (b0 < a.rows) {
+    const int r0 = row_of(a, b0);
+    if (threadIdx.x == 0) feed.issue(a, r0);
+    load_hist_regs(a, r0, hreg);
+    mark_ids(a.V, hreg, bm, plist0, &p.npen[0]);
+    const int b1 = b0 + (int)gridDim.x;
+    if (b1 < a.rows) load_hist_regs(a, row_of(a, b1), hreg);
+  }
+  __syncthreads();
+}
+
+// After the first barrier of row `it` (every thread has moved row b into
+// registers and finished row it - 1): start staging row b + grid, clear the
+// bitmap of row it + 2, mark (and list) row it + 1's history (its bitmap and
+// list count were reset at the start of row it: pipe_reset) and load row
+// it + 2's.
+__device__ __forceinline__ void pipe_advance(const SampArgs &a, RowPipe &p, uint32_t *bm, int words, int it, int b,
+                                             RowFeeder &feed, int (&hreg)[kHistRegs], int *plist_next) {
   const int nb = b + (int)gridDim.x;
+  if (nb < a.rows && threadIdx.x == 0) {
+    // the stage was written through the generic proxy (settled entries)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    feed.issue(a, row_of(a, nb));
+  }
+  uint32_t *clr = bm + ((it + 2) % 3) * words;
+  for (int i = threadIdx.x; i < words; i += kSampThreads) clr[i] = 0u;
   if (nb < a.rows) {
-    const int nrow = row_of(a, nb);
-    if (threadIdx.x == 0) feed.issue(a, nrow);
-    load_hist_regs(a, nrow, hreg);
+    mark_ids(a.V, hreg, bm + ((it + 1) % 3) * words, plist_next, &p.npen[(it + 1) & 1]);
+    const int nnb = nb + (int)gridDim.x;
+    if (nnb < a.rows) load_hist_regs(a, row_of(a, nnb), hreg);
   }
 }
 
 struct SmemRA {
+  RowPipe pipe;
   double wp[kRegLayers][kSampWarps];  // per-warp totals of each chunk layer
   double segp[kRegLayers];            // penalised entries' share of each layer
   double wsum[kSampWarps];
   double segpen[kSegLen];             // p of the penalised entries of the crossing layer
-  float redf[4][kSampWarps];
-  int redi[2][kSampWarps];
   double S, r, base;
-  int ss, cand, id, real_nan, nan_total;
-  float l0raw;
-  int npen;
-  uint64_t bar;
-  int plist[kPenCap];
-  float pval[kPenCap];  // exact stored value of plist[s]
+  int ss, dcand;
+  int plist[2][kPenCap];
+  float pval[2][kPenCap];  // exact stored value of plist[.][s]
 };
 
 // Certified draw (tiers 1 and 2 of variant A) over a row read through
-// acc(i) (chunk layer i of this thread: raw logits, NaN for penalised
-// entries and past the vocab).  pe(x) gives p of an unpenalised stored raw value x (0 for the NaN marker;
-// float in tier 1, whose chunk sums and per-warp layer sums are then taken in
-// fp32, double in tier 2); pp(s) gives p of penalised entry plist[s].  Returns the id, -1 if
-// not certified, -2 if the row holds a real NaN (tier 1 only checks).
+// acc(i) (chunk layer i of this thread: raw logits, -inf for penalised
+// entries and past the vocab).  pe(x) gives p of an unpenalised raw value x
+// (0 for -inf; float in tier 1, whose chunk sums and per-warp layer sums are
+// then taken in fp32, double in tier 2); pp(s) gives p of penalised entry
+// plist[s].  Returns the id, or -1 if not certified.
 template <int NV4, class ACC, class PE, class PP>
-__device__ __forceinline__ int draw_reg(SmemRA &sm, const ACC &acc, int V, int np, int expect_nan, double u,
-                                        double eps, double eabs, bool count_nan, const PE &pe, const PP &pp) {
+__device__ __forceinline__ int draw_reg(SmemRA &sm, const uint32_t *bits, const int *plist, const ACC &acc, int V,
+                                        int np, double u, double eps, double eabs, const PE &pe, const PP &pp) {
   using PT = decltype(pe(0.f));
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   constexpr int SH = 5 - Log2<NV4>::v;
   PT part[NV4];
-  int nanc = 0;
 #pragma unroll
   for (int i = 0; i < NV4; ++i) {
     const float4 x = acc(i);
-    const PT p0 = pe(x.x), p1 = pe(x.y), p2 = pe(x.z), p3 = pe(x.w);
-    if (count_nan) nanc += (x.x != x.x) + (x.y != x.y) + (x.z != x.z) + (x.w != x.w);
-    part[i] = (p0 + p1) + (p2 + p3);
+    part[i] = (pe(x.x) + pe(x.y)) + (pe(x.z) + pe(x.w));
   }
   const PT lt = warp_reduce_layers<NV4>(part);
   if ((lane & ((1 << SH) - 1)) == 0) sm.wp[lane >> SH][warp] = (double)lt;
@@ -1439,12 +1490,8 @@ __device__ __forceinline__ int draw_reg(SmemRA &sm, const ACC &acc, int V, int n
     pq[q] = 0.0;
     if (s < np) {
       pq[q] = pp(s);
-      atomicAdd(&sm.segp[sm.plist[s] / kSegLen], pq[q]);
+      atomicAdd(&sm.segp[plist[s] / kSegLen], pq[q]);
     }
-  }
-  if (count_nan) {
-    nanc = warp_sum_i(nanc);
-    if (lane == 0) sm.redi[0][warp] = nanc;
   }
   __syncthreads();
   if (warp == 0) {
@@ -1467,27 +1514,22 @@ __device__ __forceinline__ int draw_reg(SmemRA &sm, const ACC &acc, int V, int n
     const unsigned hit = __ballot_sync(0xffffffffu, lane < NV4 && incl >= rr);
     const int ss = hit ? __ffs(hit) - 1 : 0;
     const double base = __shfl_sync(0xffffffffu, excl, ss);
-    int nt = 0;
-    if (count_nan) nt = warp_sum_i(lane < kSampWarps ? sm.redi[0][lane] : 0);
     if (lane == 0) {
-      int code = ss;
-      if (count_nan && (nt != expect_nan || sm.real_nan)) code = -2;
-      else if (!(isfinite(S) && isfinite(rr) && hit && u >= 0.0 && u <= 1.0)) code = -1;
       sm.S = S;
       sm.r = rr;
       sm.base = base;
-      sm.ss = code;
-      sm.cand = INT_MAX;
+      sm.ss = (isfinite(S) && isfinite(rr) && hit && u >= 0.0 && u <= 1.0) ? ss : -1;
+      sm.dcand = INT_MAX;
     }
   }
   __syncthreads();
   const int ss = sm.ss;
-  if (ss < 0) return ss;
+  if (ss < 0) return -1;
 #pragma unroll
   for (int q = 0; q < kPenCap / kSampThreads; ++q) {
     const int s = threadIdx.x + q * kSampThreads;
     if (s < np) {
-      const int h = sm.plist[s];
+      const int h = plist[s];
       if (h / kSegLen == ss) sm.segpen[h % kSegLen] = pq[q];
     }
   }
@@ -1496,41 +1538,58 @@ __device__ __forceinline__ int draw_reg(SmemRA &sm, const ACC &acc, int V, int n
   const double S = sm.S, rr = sm.r;
   const int v0 = (threadIdx.x + kSampThreads * ss) * 4;
   const float4 x = acc(ss);
+  const uint32_t pw = v0 < V ? (bits[v0 >> 5] >> (v0 & 31)) & 0xFu : 0u;
   double p[4];
   double c = 0.0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const float f = f4_at(x, j);
-    p[j] = v0 + j >= V ? 0.0 : (f == f ? (double)pe(f) : sm.segpen[(v0 + j) % kSegLen]);
+    p[j] = v0 + j >= V ? 0.0 : ((pw >> j) & 1u) ? sm.segpen[(v0 + j) % kSegLen] : (double)pe(f);
     c = __dadd_rn(c, p[j]);
   }
-  double tot;
-  const double ex = block_excl_scan(c, sm.wsum, tot);
+  // exclusive block scan of c in thread order: warp Kogge-Stone, then the
+  // warp totals scanned by every warp with shuffles
+  double incl = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl = __dadd_rn(incl, n);
+  }
+  if (lane == 31) sm.wsum[warp] = incl;
+  __syncthreads();
+  double wt = lane < kSampWarps ? sm.wsum[lane] : 0.0;
+#pragma unroll
+  for (int o = 1; o < kSampWarps; o <<= 1) {
+    const double n = __shfl_up_sync(0xffffffffu, wt, o);
+    if (lane >= o) wt = __dadd_rn(wt, n);
+  }
+  double wbase = __shfl_sync(0xffffffffu, wt, (warp + 31) & 31);
+  if (warp == 0) wbase = 0.0;
+  double ex = __shfl_up_sync(0xffffffffu, incl, 1);
+  if (lane == 0) ex = 0.0;
+  ex = __dadd_rn(wbase, ex);
   double prev = __dadd_rn(sm.base, ex);
   int mine = -1;
+  double lo = prev, hi = prev;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const double cur = __dadd_rn(prev, p[j]);
-    if (mine < 0 && v0 + j < V && cur >= rr) mine = j;
+    if (mine < 0 && v0 + j < V && cur >= rr) {
+      mine = j;
+      lo = prev;
+      hi = cur;
+    }
     prev = cur;
   }
-  if (mine >= 0) atomicMin(&sm.cand, v0 + mine);
-  __syncthreads();
-  const int cand = sm.cand;
-  if (cand == INT_MAX) {
-    if (threadIdx.x == 0) sm.id = -1;
-  } else if (cand >= v0 && cand < v0 + 4) {
-    double lo = __dadd_rn(sm.base, ex), hi = lo;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (j == cand - v0) hi = __dadd_rn(lo, p[j]);
-      if (j < cand - v0) lo = __dadd_rn(lo, p[j]);
-    }
+  if (mine >= 0) {
+    // A crossing thread certifies its own candidate; the smallest candidate
+    // (the first crossing) wins, with its verdict in the low bit.
     // Error model: every p~ is within eps*p (+ eabs if it underflowed) of
     // the contract value; every computed sum is a tree over non-negative
     // terms of depth at most nl + np + 64 (chunk, butterfly, warp, layer,
     // penalised atomics, scan) against the sequential sum's depth of at most
     // V; 2^-52 per level is twice the first-order rounding constant.
+    const int cand = v0 + mine;
     const double slack = (double)(NV4 + np + 64);
     const double er = eps * (1.0 + 2.0 * eps) + 1e-12 * (eps > 0.0);
     const double Er = u * (er * S + (double)V * eabs + ((double)V + slack) * 0x1p-52 * S) + 0x1p-52 * rr;
@@ -1538,176 +1597,164 @@ __device__ __forceinline__ int draw_reg(SmemRA &sm, const ACC &acc, int V, int n
     const double Elo = er * lo + (double)cand * eabs + ((double)cand + slack) * 0x1p-52 * lo;
     const bool up = hi - Ehi >= rr + Er;
     const bool dn = cand == 0 || lo + Elo < rr - Er;
-    sm.id = (up && dn) ? cand : -1;
+    atomicMin(&sm.dcand, 2 * cand + ((up && dn) ? 0 : 1));
   }
   __syncthreads();
-  return sm.id;
+  const int key = sm.dcand;
+  return (key != INT_MAX && !(key & 1)) ? key >> 1 : -1;
 }
 
 // Tier 2 of the register-row kernel: the contract exponential of the exact
 // stored values, reading the raw row from global memory (a rare path, kept
 // out of line so it does not weigh on the register row's allocation).
 template <int NV4>
-__device__ __noinline__ int tier2_a(const SampArgs &a, const uint32_t *bits, const float *L, SmemRA &sm, int np, double u,
-                                    double maxv) {
+__device__ __noinline__ int tier2_a(const SampArgs &a, const uint32_t *bits, const float *L, SmemRA &sm,
+                                    const int *plist, const float *pval, int np, double u, double maxv) {
   const int V = a.V;
-  const float kNaN = __int_as_float(0x7fffffff);
   auto acc = [&](int i) {
     const int v0 = (threadIdx.x + kSampThreads * i) * 4;
-    float4 x = make_float4(kNaN, kNaN, kNaN, kNaN);
+    float4 x = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
     if (v0 < V) {
       x = __ldg(reinterpret_cast<const float4 *>(L + v0));
       const uint32_t w = (bits[v0 >> 5] >> (v0 & 31)) & 0xFu;
-      if (w & 1u) x.x = kNaN;
-      if (w & 2u) x.y = kNaN;
-      if (w & 4u) x.z = kNaN;
-      if (w & 8u) x.w = kNaN;
+      if (w & 1u) x.x = -INFINITY;
+      if (w & 2u) x.y = -INFINITY;
+      if (w & 4u) x.z = -INFINITY;
+      if (w & 8u) x.w = -INFINITY;
     }
     return x;
   };
   return draw_reg<NV4>(
-      sm, acc, V, np, 0, u, 0.0, 0.0, false,
-      [&](float x) { return x == x ? snai_exp(__dsub_rn((double)div_to_f32(x, a.T, a.Tinv), maxv)) : 0.0; },
-      [&](int s) { return snai_exp(__dsub_rn((double)sm.pval[s], maxv)); });
+      sm, bits, plist, acc, V, np, u, 0.0, 0.0,
+      [&](float x) { return snai_exp(__dsub_rn((double)div_to_f32(x, a.T, a.Tinv), maxv)); },
+      [&](int s) { return snai_exp(__dsub_rn((double)pval[s], maxv)); });
 }
 
 template <int NV4>
 __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_a_reg(const __grid_constant__ SampArgs a) {
   extern __shared__ __align__(16) uint8_t smem_dyn[];
   SmemRA &sm = *reinterpret_cast<SmemRA *>(smem_dyn);
-  uint32_t *bits = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemRA));
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  RowPipe &pp = sm.pipe;
   const int V = a.V;
-  const float kNaN = __int_as_float(0x7fffffff);
+  const int words = (V + 31) >> 5;
+  uint32_t *bm = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemRA));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool greedy = a.T <= 0.01;
   RowFeeder feed;
-  feed.stage = stage_ptr(smem_dyn, sizeof(SmemRA), V);
-  feed.bar = &sm.bar;
+  feed.stage = stage_ptr(smem_dyn, sizeof(SmemRA) + (size_t)8 * words, V);
+  feed.bar = &pp.bar;
   int hreg[kHistRegs];
-  if (threadIdx.x == 0) {
-    mbar_init(&sm.bar, 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-  if ((int)blockIdx.x < a.rows) {
-    const int r0 = row_of(a, blockIdx.x);
-    if (threadIdx.x == 0) feed.issue(a, r0);
-    load_hist_regs(a, r0, hreg);
-  }
-  const int npad = kSegLen * NV4 - V;  // NaN-filled entries past the vocab
+  if (threadIdx.x < kRegLayers) sm.segp[threadIdx.x] = 0.0;
+  pipe_start(a, pp, bm, words, feed, hreg, sm.plist[0]);
 
-  // Every shared field a row reads was written after the leading barrier of
-  // that row's bitmap build, which also orders it after the previous row.
-  for (int b = blockIdx.x; b < a.rows; b += gridDim.x) {
-    if (threadIdx.x == 0) sm.real_nan = 0;
-    if (threadIdx.x < kRegLayers) sm.segp[threadIdx.x] = 0.0;
-    float l0;
-    const bool ok = reg_prologue(a, hreg, bits, sm.plist, &sm.npen, &sm.l0raw, feed, l0,
-                                 [&](int s, int h, float raw) {
-                                   if (raw != raw) sm.real_nan = 1;
-                                   sm.pval[s] = penalise_a(div_to_f32(raw, a.T, a.Tinv), a.rep);
-                                   return kNaN;
-                                 });
-    if (!ok) break;
-    const int np = sm.npen;
-    float4 r[NV4];
-    reg_load(a, b, r, kNaN, feed, hreg);
-    if (a.nan_guard && l0 != l0) {  // src/snai_inference.php:146
-      if (threadIdx.x == 0) a.out[b] = -1;
-      continue;
-    }
-
-    // ---- maximum: raw logits of unpenalised entries (t is monotone in L for
-    // T > 0; the NaN markers drop out of fmaxf), exact values of penalised ones
-    float xmax = -INFINITY, xabs = 0.f;
+  // Every row ends with a block barrier, so at a row's start the previous
+  // row has finished with everything of the other parity.
+  int it = 0;
+  for (int b = blockIdx.x; b < a.rows; b += gridDim.x, ++it) {
+    const int par = it & 1;
+    const uint32_t *bits = bm + (it % 3) * words;
+    int *plist = sm.plist[par];
+    float *pval = sm.pval[par];
+    if (threadIdx.x == 0) pipe_reset(pp, par ^ 1);
+    const bool ok = feed.wait(a.err);
+    const int np = min(pp.npen[par], kPenCap);
+    // exact stored values of the penalised entries, by the threads that
+    // listed them (-inf left in the stage); their (value, id) argmax per warp
+    unsigned long long pk = 0ull;
+    if (warp * 32 < np) {
 #pragma unroll
-    for (int i = 0; i < NV4; ++i) {
-      xmax = fmaxf(xmax, fmax4(r[i]));
-      xabs = fmaxf(xabs, fmaxf(fmaxf(fabsf(r[i].x), fabsf(r[i].y)), fmaxf(fabsf(r[i].z), fabsf(r[i].w))));
-    }
-    float pmax = -INFINITY;
-    int pidx = INT_MAX;
-    for (int s = threadIdx.x; s < np; s += kSampThreads) {
-      const float t = sm.pval[s];
-      const int h = sm.plist[s];
-      if (t > pmax || (t == pmax && h < pidx)) {
-        pmax = t;
-        pidx = h;
-      }
-      xabs = fmaxf(xabs, fabsf(t));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
-      xabs = fmaxf(xabs, __shfl_xor_sync(0xffffffffu, xabs, o));
-      const float ob = __shfl_xor_sync(0xffffffffu, pmax, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, pidx, o);
-      if (ob > pmax || (ob == pmax && oi < pidx)) {
-        pmax = ob;
-        pidx = oi;
-      }
-    }
-    if (lane == 0) {
-      sm.redf[0][warp] = xmax;
-      sm.redf[1][warp] = xabs;
-      sm.redf[2][warp] = pmax;
-      sm.redi[1][warp] = pidx;
-    }
-    if (threadIdx.x == 0) sm.cand = INT_MAX;
-    __syncthreads();
-    {
-      const int w = lane & (kSampWarps - 1);
-      xmax = sm.redf[0][w];
-      xabs = sm.redf[1][w];
-      pmax = sm.redf[2][w];
-      pidx = sm.redi[1][w];
-#pragma unroll
-      for (int o = kSampWarps / 2; o > 0; o >>= 1) {
-        xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
-        xabs = fmaxf(xabs, __shfl_xor_sync(0xffffffffu, xabs, o));
-        const float ob = __shfl_xor_sync(0xffffffffu, pmax, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, pidx, o);
-        if (ob > pmax || (ob == pmax && oi < pidx)) {
-          pmax = ob;
-          pidx = oi;
+      for (int q = 0; q < kPenCap / kSampThreads; ++q) {
+        const int s = threadIdx.x + q * kSampThreads;
+        if (s < np) {
+          const int h = plist[s];
+          const float raw = feed.stage[h];
+          if (h == 0) pp.l0[par] = raw;
+          const float t = penalise_a(div_to_f32(raw, a.T, a.Tinv), a.rep);
+          pval[s] = t;
+          feed.stage[h] = -INFINITY;
+          const unsigned long long key = argmax_key(t, h);
+          pk = key > pk ? key : pk;
         }
       }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long ok2 = __shfl_xor_sync(0xffffffffu, pk, o);
+        pk = ok2 > pk ? ok2 : pk;
+      }
     }
+    if (lane == 0) pp.pkey[par][warp] = pk;
+    __syncthreads();
+
+    // ---- registers; maximum of the unpenalised raw logits ----
+    float4 r[NV4];
+    float xmax = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) {
+      const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+      r[i] = v0 < V ? lds4(feed.stage + v0) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      xmax = fmaxf(xmax, fmax4(r[i]));
+    }
+    if (threadIdx.x == 0 && !(bits[0] & 1u)) pp.l0[par] = r[0].x;
+    const float my_xmax = xmax;
+    xmax = warp_max(xmax);
+    if (lane == 0) atomicMax(&pp.xkey[par], okey32(xmax));
+    if (!__syncthreads_and(ok)) break;
+    pipe_advance(a, pp, bm, words, it, b, feed, hreg, sm.plist[par ^ 1]);
+
+    if (a.nan_guard && pp.l0[par] != pp.l0[par]) {  // src/snai_inference.php:146
+      if (threadIdx.x == 0) a.out[b] = -1;
+      __syncthreads();
+      continue;
+    }
+    xmax = key_to_float(pp.xkey[par]);
+    pk = pp.pkey[par][lane & (kSampWarps - 1)];
+#pragma unroll
+    for (int o = kSampWarps / 2; o > 0; o >>= 1) {
+      const unsigned long long ok2 = __shfl_xor_sync(0xffffffffu, pk, o);
+      pk = ok2 > pk ? ok2 : pk;
+    }
+    const float pmax = key_to_float((unsigned int)(pk >> 32));
+    const int pidx = pk ? (int)(0xffffffffu - (unsigned int)pk) : INT_MAX;
     const float tmax = (xmax > -INFINITY) ? div_to_f32(xmax, a.T, a.Tinv) : -INFINITY;
     const float M = fmaxf(tmax, pmax);
-    const bool simple = a.T > 0.0 && isfinite(M) && isfinite(xmax) && isfinite(xabs);
+    const bool simple = a.T > 0.0 && isfinite(M) && isfinite(xmax);
     const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
-    const bool greedy = a.T <= 0.01;
 
-    float best = M;
-    int bi = INT_MAX;
-    if (!simple) {
-      exact_max_a(a, bits, L, sm.redf[3], sm.redi[0], best, bi);
-    } else if (greedy) {
+    if (greedy && simple) {
       // first index attaining M: entries with fp32(x/T) == M have
-      // x >= (M - |M| 2^-23) T; the chunks holding one are checked exactly
+      // x >= (M - |M| 2^-23) T; only threads holding one look
       const double lowt = (double)M - fabs((double)M) * 0x1p-22 - 1e-44;
       const float xthr = __double2float_rd(lowt * a.T);
       int mc = INT_MAX;
+      if (my_xmax >= xthr) {
 #pragma unroll
-      for (int i = 0; i < NV4; ++i) {
-        if (fmax4(r[i]) >= xthr) {
-          const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+        for (int i = 0; i < NV4; ++i) {
+          if (fmax4(r[i]) >= xthr) {
+            const int v0 = (threadIdx.x + kSampThreads * i) * 4;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float f = f4_at(r[i], j);
-            if (f >= xthr && div_to_f32(f, a.T, a.Tinv) == M) mc = min(mc, v0 + j);
+            for (int j = 0; j < 4; ++j) {
+              const float f = f4_at(r[i], j);
+              if (f >= xthr && div_to_f32(f, a.T, a.Tinv) == M) mc = min(mc, v0 + j);
+            }
           }
         }
       }
       if (threadIdx.x == 0 && pmax == M) mc = min(mc, pidx);
-      if (mc != INT_MAX) atomicMin(&sm.cand, mc);
+      if (mc != INT_MAX) atomicMin(&pp.cand[par], mc);
       __syncthreads();
-      bi = sm.cand;
+      if (threadIdx.x == 0) a.out[b] = pp.cand[par];
+      continue;
     }
+
+    float best = M;
+    int bi = INT_MAX;
+    if (!simple) exact_max_a(a, bits, L, reinterpret_cast<float *>(sm.wsum), reinterpret_cast<int *>(sm.wsum) + 16,
+                             best, bi);
     // PHP: max starts at -INF and only a strictly larger value moves it.
     const bool any = best > -INFINITY;
     if (greedy) {
       if (threadIdx.x == 0) a.out[b] = any ? bi : 0;
+      __syncthreads();
       continue;
     }
     const double maxv = any ? (double)best : -INFINITY;
@@ -1715,23 +1762,28 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_a_reg(c
     int id = -1;
     if (any && simple) {
       // tier 1: p~ = 2^(x c - M log2e), c = fp32(log2e / T); penalised entries
-      // use their exact value t: 2^(t log2e - M log2e).  The fp32 sums (4
-      // entries, then a depth-5 warp tree) add at most 7 * 2^-24 (1 + 2^-20)
-      // < 2^-21 to the relative error.
+      // use their exact value t: 2^(t log2e - M log2e).  Rounding of c, of
+      // fp32(M log2e) and of the fma moves the exponent by at most
+      // 3 (|t| + |M|) log2e 2^-24, and ex2.approx adds a relative 2^-22.
+      // Entries with t < M - 91 have p < 2^-131 and p~ < 2^-125 (flushed or
+      // tiny): an absolute error of eabs = 2^-125 each.  Every other entry
+      // has |t| <= |M| + 91, whence the relative bound below.  A NaN logit
+      // makes S NaN and the row falls through to tier 3; -inf entries give 0
+      // in both.  The fp32 sums (4 entries, then a depth-5 warp tree) add at
+      // most 7 * 2^-24 (1 + 2^-20) < 2^-21.
       const float c = (float)(1.4426950408889634 * a.Tinv);
       const float l2e = 1.44269504f;
       const float m2 = M * l2e;
-      // |t| <= tabs for every entry (|x/T| rounded up a little)
-      const double tabs = (double)xabs * fmax(1.0, fabs(a.Tinv)) * (1.0 + 0x1p-20);
+      const double tabs = fabs((double)M) + 91.0;
       const double eps = (tabs + fabs((double)M) + 1.0) * 0x1p-21 + 0x1p-19 + 0x1p-21;
       id = draw_reg<NV4>(
-          sm, [&](int i) { return pick_layer(r, i); }, V, np, np + npad, u, eps, 0x1p-125, true,
-          [&](float x) { return fmaxf(ex2_approx(fmaf(x, c, -m2)), 0.f); },
-          [&](int s) { return (double)fmaxf(ex2_approx(fmaf(sm.pval[s], l2e, -m2)), 0.f); });
-      if (id == -1) id = tier2_a<NV4>(a, bits, L, sm, np, u, maxv);
+          sm, bits, plist, [&](int i) { return pick_layer(r, i); }, V, np, u, eps, 0x1p-125,
+          [&](float x) { return ex2_approx(fmaf(x, c, -m2)); },
+          [&](int s) { return (double)ex2_approx(fmaf(pval[s], l2e, -m2)); });
+      if (id < 0) id = tier2_a<NV4>(a, bits, L, sm, plist, pval, np, u, maxv);
     }
     if (id < 0) {
-      // tier 3
+      // tier 3 (also every row with a NaN logit)
       if (warp == 0) {
         const int s = sequential_a(a, bits, L, maxv, u);
         if (lane == 0) a.out[b] = s;
@@ -1739,78 +1791,77 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_a_reg(c
     } else if (threadIdx.x == 0) {
       a.out[b] = id;
     }
+    __syncthreads();
   }
 }
 
-// Variant B over the register row: the fast selection of fast_select_b with
-// one fmaxf per entry for the maximum (the spread is estimated from chunk
-// layer 0), a histogram pass, and a gather by a single threshold.
+// Variant B over the register row: the maximum of the lower bounds (one
+// fmaxf per entry), the spread estimated from chunk layer 0, a histogram of
+// the distance below the maximum, and a gather by one threshold.
 template <int NV4>
 __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(const __grid_constant__ SampArgs a) {
   extern __shared__ __align__(16) uint8_t smem_dyn[];
   SmemB &sm = *reinterpret_cast<SmemB *>(smem_dyn);
-  uint32_t *bits = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemB));
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  RowPipe &pp = *reinterpret_cast<RowPipe *>(smem_dyn + sizeof(SmemB));
   const int V = a.V;
+  const int words = (V + 31) >> 5;
+  uint32_t *bm = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemB) + sizeof(RowPipe));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int k = min(a.top_k, V);
   const double rep = a.rep;
   RowFeeder feed;
-  feed.stage = stage_ptr(smem_dyn, sizeof(SmemB), V);
-  feed.bar = &sm.bar;
+  feed.stage = stage_ptr(smem_dyn, sizeof(SmemB) + sizeof(RowPipe) + (size_t)8 * words, V);
+  feed.bar = &pp.bar;
   int hreg[kHistRegs];
-  if (threadIdx.x == 0) {
-    mbar_init(&sm.bar, 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-  if ((int)blockIdx.x < a.rows) {
-    const int r0 = row_of(a, blockIdx.x);
-    if (threadIdx.x == 0) feed.issue(a, r0);
-    load_hist_regs(a, r0, hreg);
-  }
-  float l0unused = 0.f;
+  pipe_start(a, pp, bm, words, feed, hreg, sm.plist);
 
-  for (int b = blockIdx.x; b < a.rows; b += gridDim.x) {
-    const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
-    float l0;
-    const bool ok = reg_prologue(a, hreg, bits, sm.plist, &sm.npen, &l0unused, feed, l0,
-                                 [&](int, int, float raw) { return __double2float_rd(__dsub_rn((double)raw, rep)); });
-    if (!ok) break;
+  int it = 0;
+  for (int b = blockIdx.x; b < a.rows; b += gridDim.x, ++it) {
+    const int par = it & 1;
+    const uint32_t *bits = bm + (it % 3) * words;
+    if (threadIdx.x == 0) pipe_reset(pp, par ^ 1);
+    const bool ok = feed.wait(a.err);
+    // penalised entries -> fp32 lower bound of L - rep, in the stage
+    const int np = min(pp.npen[par], kPenCap);
+    for (int s = threadIdx.x; s < np; s += kSampThreads) {
+      const int h = sm.plist[s];
+      feed.stage[h] = __double2float_rd(__dsub_rn((double)feed.stage[h], rep));
+    }
+    __syncthreads();
+
+    // ---- registers; maximum; spread of chunk layer 0 ----
     float4 r[NV4];
-    reg_load(a, b, r, -INFINITY, feed, hreg);
-
-    // ---- pass 1: maximum of the lower bounds; spread from chunk layer 0 ----
     float mx = -INFINITY, s1 = 0.f, s2 = 0.f;
 #pragma unroll
-    for (int i = 0; i < NV4; ++i) mx = fmaxf(mx, fmax4(r[i]));
-    const int n0 = min(V, kSegLen);
-    if (threadIdx.x * 4 < V) {
-      const float4 x = r[0];
-      s1 = (x.x + x.y) + (x.z + x.w);
-      s2 = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, x.w * x.w)));
+    for (int i = 0; i < NV4; ++i) {
+      const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+      r[i] = v0 < V ? lds4(feed.stage + v0) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      if (i == 0 && v0 < V) {
+        const float4 x = r[0];
+        s1 = (x.x + x.y) + (x.z + x.w);
+        s2 = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, x.w * x.w)));
+      }
+      mx = fmaxf(mx, fmax4(r[i]));
     }
+    const float my_mx = mx;
     mx = warp_max(mx);
     s1 = warp_sum(s1);
     s2 = warp_sum(s2);
     if (lane == 0) {
-      sm.fw[0][warp] = mx;
-      sm.fw[1][warp] = s1;
-      sm.fw[2][warp] = s2;
+      atomicMax(&pp.xkey[par], okey32(mx));
+      atomicAdd(&pp.s1[par], s1);
+      atomicAdd(&pp.s2[par], s2);
     }
+    for (int i = threadIdx.x; i < 256; i += kSampThreads) sm.hist[i] = 0u;
     if (threadIdx.x == 0) sm.ncand = 0;
-    __syncthreads();
-    {
-      const int w = lane & (kSampWarps - 1);
-      mx = sm.fw[0][w];
-      s1 = sm.fw[1][w];
-      s2 = sm.fw[2][w];
-#pragma unroll
-      for (int o = kSampWarps / 2; o > 0; o >>= 1) {
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-      }
-    }
+    if (!__syncthreads_and(ok)) break;
+    pipe_advance(a, pp, bm, words, it, b, feed, hreg, sm.plist);
+
+    const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
+    mx = key_to_float(pp.xkey[par]);
+    s1 = pp.s1[par];
+    s2 = pp.s2[par];
+    const int n0 = min(V, kSegLen);
     bool fast = isfinite(mx) && isfinite(s1) && isfinite(s2) && V >= k;
     float R = 0.f;
     if (fast) {
@@ -1820,11 +1871,13 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
       fast = R > 0.f && isfinite(R);
     }
     int bstar = 255;
-    // ---- pass 2: histogram of the distance below the maximum, 255 bins over [0, R)
+    // ---- histogram of the distance below the maximum, 255 bins over [0, R)
     for (int attempt = 0; fast && attempt < 3 && bstar >= 255; ++attempt) {
+      if (attempt > 0) {
+        for (int i = threadIdx.x; i < 256; i += kSampThreads) sm.hist[i] = 0u;
+        __syncthreads();
+      }
       const float inv_w = 255.f / R;
-      for (int i = threadIdx.x; i < 256; i += kSampThreads) sm.hist[i] = 0u;
-      __syncthreads();
 #pragma unroll
       for (int i = 0; i < NV4; ++i) {
 #pragma unroll
@@ -1862,28 +1915,31 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
     }
     fast = fast && bstar < 255;
     if (fast) {
-      // ---- pass 3: gather.  An entry lands in a bin <= bstar only if its
-      // lower bound exceeds mx - (bstar+1) (R/255) (1 + 2^-21); every entry
-      // whose exact value reaches the least such bound has a lower bound of
-      // at least the float below it, so `g` admits a superset of the top k.
+      // ---- gather.  An entry lands in a bin <= bstar only if its lower
+      // bound exceeds mx - (bstar+1) (R/255) (1 + 2^-21), so at least k
+      // lower bounds reach g; every entry whose exact value reaches the
+      // least of them has a lower bound (its value rounded down) at least
+      // that large, so `g` admits a superset of the top k.
       const double gd = (double)mx - (double)(bstar + 1) * ((double)R / 255.0) * (1.0 + 0x1p-20);
       float g = __double2float_rd(gd);
       g = (g == -INFINITY) ? g : __uint_as_float(g > 0.f ? __float_as_uint(g) - 1u
                                                           : (g == 0.f ? 0x80000001u : __float_as_uint(g) + 1u));
+      if (my_mx >= g) {
 #pragma unroll
-      for (int i = 0; i < NV4; ++i) {
-        if (fmax4(r[i]) >= g) {
-          const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+        for (int i = 0; i < NV4; ++i) {
+          if (fmax4(r[i]) >= g) {
+            const int v0 = (threadIdx.x + kSampThreads * i) * 4;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float f = f4_at(r[i], j);
-            if (f >= g) {
-              const int v = v0 + j;
-              const double val = in_set(bits, v) ? __dsub_rn((double)L[v], rep) : (double)f;
-              const int slot = atomicAdd(&sm.ncand, 1);
-              if (slot < kFastCand) {
-                sm.ckey[slot] = okey64(val);
-                sm.cidx[slot] = v;
+            for (int j = 0; j < 4; ++j) {
+              const float f = f4_at(r[i], j);
+              if (f >= g) {
+                const int v = v0 + j;
+                const double val = in_set(bits, v) ? __dsub_rn((double)L[v], rep) : (double)f;
+                const int slot = atomicAdd(&sm.ncand, 1);
+                if (slot < kFastCand) {
+                  sm.ckey[slot] = okey64(val);
+                  sm.cidx[slot] = v;
+                }
               }
             }
           }
@@ -1916,28 +1972,32 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
     double *C = P + kMaxTopK;
     for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = snai_exp(__ddiv_rn(sm.val[i], a.T));
     __syncthreads();
-    if (warp == 0) {
-      // sequential sum, then p / sum, cumulative sums and the draw, by lane 0
-      if (lane == 0) {
-        double s = 0.0;
-        for (int i = 0; i < k; ++i) s = __dadd_rn(s, P[i]);
-        double cum = 0.0;
-        int nf = 0;
-        for (int i = 0; i < k; ++i) {
-          cum = __dadd_rn(cum, __ddiv_rn(P[i], s));
-          C[i] = cum;  // $cum_check after i+1 terms is this same sum
-          nf = i + 1;
-          if (cum >= a.top_p) break;
-        }
-        const double rr = __dmul_rn((double)a.uniforms[b], cum);
-        int id = sm.order[0];
-        for (int i = 0; i < nf; ++i)
-          if (rr <= C[i]) {
-            id = sm.order[i];
-            break;
-          }
-        a.out[b] = id;
+    if (threadIdx.x == 0) {
+      double s = 0.0;
+      for (int i = 0; i < k; ++i) s = __dadd_rn(s, P[i]);
+      C[0] = s;
+    }
+    __syncthreads();
+    const double sum = C[0];
+    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = __ddiv_rn(P[i], sum);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double cum = 0.0;
+      int nf = 0;
+      for (int i = 0; i < k; ++i) {
+        cum = __dadd_rn(cum, P[i]);
+        C[i] = cum;  // $cum_check after i+1 terms is this same sum
+        nf = i + 1;
+        if (cum >= a.top_p) break;
       }
+      const double rr = __dmul_rn((double)a.uniforms[b], cum);
+      int id = sm.order[0];
+      for (int i = 0; i < nf; ++i)
+        if (rr <= C[i]) {
+          id = sm.order[i];
+          break;
+        }
+      a.out[b] = id;
     }
     __syncthreads();
   }
@@ -2061,9 +2121,10 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   const bool reg = layers <= kRegLayers && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
                    (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 && s.hist_cols <= kPenCap;
   const int nv4 = !reg ? 0 : layers <= 4 ? 4 : layers <= 8 ? 8 : 16;
-  const size_t stage = reg ? (size_t)s.V * 4 + kStageAlign : 0;  // staging buffer + alignment slack
+  // register rows: three bitmaps, then the staging buffer (+ alignment slack)
+  const size_t rsm = reg ? 3 * (size_t)((s.V + 31) / 32) * 4 + (size_t)s.V * 4 + kStageAlign : 0;
   if (s.variant == 0) {
-    const size_t sm = (reg ? sizeof(SmemRA) : sizeof(SmemA)) + bitmap + stage;
+    const size_t sm = reg ? sizeof(SmemRA) + rsm : sizeof(SmemA) + bitmap;
     if (nv4 == 4)
       launch_a<4>(a, sm, stream);
     else if (nv4 == 8)
@@ -2073,7 +2134,7 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
     else
       launch_a<0>(a, sm, stream);
   } else {
-    const size_t sm = sizeof(SmemB) + bitmap + stage;
+    const size_t sm = reg ? sizeof(SmemB) + sizeof(RowPipe) + rsm : sizeof(SmemB) + bitmap;
     if (nv4 == 4)
       launch_b<4>(a, sm, stream);
     else if (nv4 == 8)
