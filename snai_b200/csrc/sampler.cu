@@ -69,7 +69,7 @@ struct SampArgs {
   int hist_cols;
   const int *hist_len;
   const float *uniforms;
-  double T, Tinv, rep, top_p;
+  double T, Tinv, rep, repinv, top_p;
   int top_k;
   int nan_guard;
   int *out;
@@ -208,16 +208,16 @@ __device__ __forceinline__ float div_to_f32(float x, double T, double Tinv) {
   return safe ? __double2float_rn(q) : __double2float_rn(__ddiv_rn((double)x, T));
 }
 
-// The penalty of src/snai_inference.php:160-164 applied to a stored value.
-__device__ __forceinline__ float penalise_a(float t, double rep) {
-  const double d = (double)t;
-  return d > 0.0 ? __double2float_rn(__ddiv_rn(d, rep)) : __double2float_rn(__dmul_rn(d, rep));
+// The penalty of src/snai_inference.php:160-164 applied to a stored value
+// (the division as in div_to_f32).
+__device__ __forceinline__ float penalise_a(float t, double rep, double repinv) {
+  return t > 0.f ? div_to_f32(t, rep, repinv) : __double2float_rn(__dmul_rn((double)t, rep));
 }
 
 // Variant A's stored value for vocab entry v (src/snai_inference.php:153, 160-164).
 __device__ __forceinline__ float tempered(const SampArgs &a, const uint32_t *bits, float x, int v) {
   const float t = div_to_f32(x, a.T, a.Tinv);
-  return in_set(bits, v) ? penalise_a(t, a.rep) : t;
+  return in_set(bits, v) ? penalise_a(t, a.rep, a.repinv) : t;
 }
 
 __device__ __forceinline__ double warp_sum_d(double v) {
@@ -362,9 +362,12 @@ __device__ __forceinline__ int row_of(const SampArgs &a, int b) { return a.row_m
 // up to 128 bytes (bulk copies and 16-byte shared loads need 16-byte
 // alignment; the host adds kStageAlign bytes of slack).
 constexpr size_t kStageAlign = 128;
+// (pointer arithmetic on the shared array, so the result stays a known
+// shared-memory pointer)
 __device__ __forceinline__ float *stage_ptr(uint8_t *smem, size_t core_bytes, int V) {
-  const uintptr_t p = reinterpret_cast<uintptr_t>(smem) + core_bytes + (size_t)((V + 31) / 32) * 4;
-  return reinterpret_cast<float *>((p + kStageAlign - 1) & ~(uintptr_t)(kStageAlign - 1));
+  const uint32_t off = (uint32_t)(core_bytes + (size_t)((V + 31) / 32) * 4);
+  const uint32_t pad = (0u - (smem_u32(smem) + off)) & (uint32_t)(kStageAlign - 1);
+  return reinterpret_cast<float *>(smem + off + pad);
 }
 
 // Brings row b into `row`: history bitmap and distinct-id list, the staged
@@ -633,7 +636,7 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int V = a.V;
   const double rep = a.rep;
-  auto pen_fn = [&](float x) { return penalise_a(div_to_f32(x, a.T, a.Tinv), rep); };
+  auto pen_fn = [&](float x) { return penalise_a(div_to_f32(x, a.T, a.Tinv), rep, a.repinv); };
   RowFeeder feed;
   feed.stage = stage_ptr(smem_dyn, sizeof(SmemA), V);
   feed.bar = &sm.bar;
@@ -1313,7 +1316,12 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
 constexpr int kRegLayers = 16;             // chunk layers held in registers at most
 constexpr int kSegLen = kSampThreads * 4;  // ids per chunk layer
 
-__device__ __forceinline__ float4 lds4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+// 16-byte shared-memory load by shared-window address
+__device__ __forceinline__ float4 lds4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
 __device__ __forceinline__ float fmax4(const float4 &x) { return fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)); }
 // inverse of okey32 (key 0, NaN's key, maps to -inf)
 __device__ __forceinline__ float key_to_float(unsigned int k) {
@@ -1338,7 +1346,7 @@ template <int N> struct Log2 { static constexpr int v = 1 + Log2<N / 2>::v; };
 template <> struct Log2<1> { static constexpr int v = 0; };
 
 // Per-layer warp totals of N per-lane values by a reduce-scatter butterfly
-// (the file is compiled without contraction, so every + is one rounding):
+// (plain additions, each one rounding):
 // returns the total of layer (lane >> (5 - log2 N)) (every lane of the
 // group holds it).  Each total is a tree of depth 5.
 template <int N, class T>
@@ -1454,7 +1462,6 @@ __device__ __forceinline__ void pipe_advance(const SampArgs &a, RowPipe &p, uint
 struct SmemRA {
   RowPipe pipe;
   double wp[kRegLayers][kSampWarps];  // per-warp totals of each chunk layer
-  double segp[kRegLayers];            // penalised entries' share of each layer
   double wsum[kSampWarps];
   double segpen[kSegLen];             // p of the penalised entries of the crossing layer
   double S, r, base;
@@ -1468,7 +1475,8 @@ struct SmemRA {
 // entries and past the vocab).  pe(x) gives p of an unpenalised raw value x
 // (0 for -inf; float in tier 1, whose chunk sums and per-warp layer sums are
 // then taken in fp32, double in tier 2); pp(s) gives p of penalised entry
-// plist[s].  Returns the id, or -1 if not certified.
+// plist[s] (same type), added to its layer's partial sum by the thread that
+// holds slot s.  Returns the id, or -1 if not certified.
 template <int NV4, class ACC, class PE, class PP>
 __device__ __forceinline__ int draw_reg(SmemRA &sm, const uint32_t *bits, const int *plist, const ACC &acc, int V,
                                         int np, double u, double eps, double eabs, const PE &pe, const PP &pp) {
@@ -1481,26 +1489,25 @@ __device__ __forceinline__ int draw_reg(SmemRA &sm, const uint32_t *bits, const 
     const float4 x = acc(i);
     part[i] = (pe(x.x) + pe(x.y)) + (pe(x.z) + pe(x.w));
   }
-  const PT lt = warp_reduce_layers<NV4>(part);
-  if ((lane & ((1 << SH) - 1)) == 0) sm.wp[lane >> SH][warp] = (double)lt;
-  double pq[kPenCap / kSampThreads];
+  PT pq[kPenCap / kSampThreads];
 #pragma unroll
   for (int q = 0; q < kPenCap / kSampThreads; ++q) {
     const int s = threadIdx.x + q * kSampThreads;
-    pq[q] = 0.0;
+    pq[q] = PT(0);
     if (s < np) {
       pq[q] = pp(s);
-      atomicAdd(&sm.segp[plist[s] / kSegLen], pq[q]);
+      const int sg = plist[s] / kSegLen;
+#pragma unroll
+      for (int i = 0; i < NV4; ++i) part[i] = part[i] + (i == sg ? pq[q] : PT(0));
     }
   }
+  const PT lt = warp_reduce_layers<NV4>(part);
+  if ((lane & ((1 << SH) - 1)) == 0) sm.wp[lane >> SH][warp] = (double)lt;
   __syncthreads();
   if (warp == 0) {
     double seg = 0.0;
-    if (lane < NV4) {
+    if (lane < NV4)
       for (int w = 0; w < kSampWarps; ++w) seg = __dadd_rn(seg, sm.wp[lane][w]);
-      seg = __dadd_rn(seg, sm.segp[lane]);
-      sm.segp[lane] = 0.0;  // ready for the next draw
-    }
     double incl = seg;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -1530,7 +1537,7 @@ __device__ __forceinline__ int draw_reg(SmemRA &sm, const uint32_t *bits, const 
     const int s = threadIdx.x + q * kSampThreads;
     if (s < np) {
       const int h = plist[s];
-      if (h / kSegLen == ss) sm.segpen[h % kSegLen] = pq[q];
+      if (h / kSegLen == ss) sm.segpen[h % kSegLen] = (double)pq[q];
     }
   }
   __syncthreads();
@@ -1586,11 +1593,11 @@ __device__ __forceinline__ int draw_reg(SmemRA &sm, const uint32_t *bits, const 
     // (the first crossing) wins, with its verdict in the low bit.
     // Error model: every p~ is within eps*p (+ eabs if it underflowed) of
     // the contract value; every computed sum is a tree over non-negative
-    // terms of depth at most nl + np + 64 (chunk, butterfly, warp, layer,
-    // penalised atomics, scan) against the sequential sum's depth of at most
+    // terms of depth at most nl + 64 (chunk, penalised, butterfly, warp,
+    // layer, scan) against the sequential sum's depth of at most
     // V; 2^-52 per level is twice the first-order rounding constant.
     const int cand = v0 + mine;
-    const double slack = (double)(NV4 + np + 64);
+    const double slack = (double)(NV4 + 64);
     const double er = eps * (1.0 + 2.0 * eps) + 1e-12 * (eps > 0.0);
     const double Er = u * (er * S + (double)V * eabs + ((double)V + slack) * 0x1p-52 * S) + 0x1p-52 * rr;
     const double Ehi = er * hi + ((double)cand + 1.0) * eabs + ((double)cand + slack) * 0x1p-52 * hi;
@@ -1644,7 +1651,6 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_a_reg(c
   feed.stage = stage_ptr(smem_dyn, sizeof(SmemRA) + (size_t)8 * words, V);
   feed.bar = &pp.bar;
   int hreg[kHistRegs];
-  if (threadIdx.x < kRegLayers) sm.segp[threadIdx.x] = 0.0;
   pipe_start(a, pp, bm, words, feed, hreg, sm.plist[0]);
 
   // Every row ends with a block barrier, so at a row's start the previous
@@ -1669,7 +1675,7 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_a_reg(c
           const int h = plist[s];
           const float raw = feed.stage[h];
           if (h == 0) pp.l0[par] = raw;
-          const float t = penalise_a(div_to_f32(raw, a.T, a.Tinv), a.rep);
+          const float t = penalise_a(div_to_f32(raw, a.T, a.Tinv), a.rep, a.repinv);
           pval[s] = t;
           feed.stage[h] = -INFINITY;
           const unsigned long long key = argmax_key(t, h);
@@ -1688,10 +1694,11 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_a_reg(c
     // ---- registers; maximum of the unpenalised raw logits ----
     float4 r[NV4];
     float xmax = -INFINITY;
+    const uint32_t st_u32 = smem_u32(feed.stage);
 #pragma unroll
     for (int i = 0; i < NV4; ++i) {
       const int v0 = (threadIdx.x + kSampThreads * i) * 4;
-      r[i] = v0 < V ? lds4(feed.stage + v0) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      r[i] = v0 < V ? lds4(st_u32 + 4u * v0) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
       xmax = fmaxf(xmax, fmax4(r[i]));
     }
     if (threadIdx.x == 0 && !(bits[0] & 1u)) pp.l0[par] = r[0].x;
@@ -1769,17 +1776,17 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_a_reg(c
       // tiny): an absolute error of eabs = 2^-125 each.  Every other entry
       // has |t| <= |M| + 91, whence the relative bound below.  A NaN logit
       // makes S NaN and the row falls through to tier 3; -inf entries give 0
-      // in both.  The fp32 sums (4 entries, then a depth-5 warp tree) add at
-      // most 7 * 2^-24 (1 + 2^-20) < 2^-21.
+      // in both.  The fp32 sums (4 entries, up to 2 penalised ones, then a
+      // depth-5 warp tree) add at most 9 * 2^-24 (1 + 2^-20) < 2^-20.
       const float c = (float)(1.4426950408889634 * a.Tinv);
       const float l2e = 1.44269504f;
       const float m2 = M * l2e;
       const double tabs = fabs((double)M) + 91.0;
-      const double eps = (tabs + fabs((double)M) + 1.0) * 0x1p-21 + 0x1p-19 + 0x1p-21;
+      const double eps = (tabs + fabs((double)M) + 1.0) * 0x1p-21 + 0x1p-19 + 0x1p-20;
       id = draw_reg<NV4>(
           sm, bits, plist, [&](int i) { return pick_layer(r, i); }, V, np, u, eps, 0x1p-125,
           [&](float x) { return ex2_approx(fmaf(x, c, -m2)); },
-          [&](int s) { return (double)ex2_approx(fmaf(pval[s], l2e, -m2)); });
+          [&](int s) { return ex2_approx(fmaf(pval[s], l2e, -m2)); });
       if (id < 0) id = tier2_a<NV4>(a, bits, L, sm, plist, pval, np, u, maxv);
     }
     if (id < 0) {
@@ -1832,10 +1839,11 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
     // ---- registers; maximum; spread of chunk layer 0 ----
     float4 r[NV4];
     float mx = -INFINITY, s1 = 0.f, s2 = 0.f;
+    const uint32_t st_u32 = smem_u32(feed.stage);
 #pragma unroll
     for (int i = 0; i < NV4; ++i) {
       const int v0 = (threadIdx.x + kSampThreads * i) * 4;
-      r[i] = v0 < V ? lds4(feed.stage + v0) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      r[i] = v0 < V ? lds4(st_u32 + 4u * v0) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
       if (i == 0 && v0 < V) {
         const float4 x = r[0];
         s1 = (x.x + x.y) + (x.z + x.w);
@@ -2109,6 +2117,7 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   a.T = s.temperature;
   a.Tinv = 1.0 / s.temperature;
   a.rep = s.rep;
+  a.repinv = 1.0 / s.rep;
   a.top_p = s.top_p;
   a.top_k = s.top_k;
   a.nan_guard = s.nan_guard;
