@@ -178,6 +178,7 @@ Engine *create_engine(const Dims &d, int max_seqs, int device, int precision) {
   a.add(&e->h, M * D);
   a.add(&e->x, M * D * sizeof(float));
   a.add(&e->q, M * (size_t)d.att_ch);
+  a.add(&e->kvs, M * 2 * (size_t)d.att_ch);
   a.add(&e->att, M * D * sizeof(float));
   a.add(&e->u, M * F * sizeof(float));
   a.add(&e->xo, M * D * sizeof(float));
@@ -958,6 +959,7 @@ size_t carve_rows(Engine &e, int rows, void *base) {
   a.add(&e.h, M * D);
   a.add(&e.x, M * D * sizeof(float));
   a.add(&e.q, M * (size_t)e.d.att_ch);
+  a.add(&e.kvs, M * 2 * (size_t)e.d.att_ch);
   a.add(&e.att, M * D * sizeof(float));
   a.add(&e.u, M * F * sizeof(float));
   a.add(&e.xo, M * D * sizeof(float));
@@ -994,7 +996,7 @@ extern "C" int cortex_forward_batch_noalloc(void *state, const int *tokens, int 
   // Point the pass at the static scratch, run it, restore the state's own buffers.
   RowDesc *rows_d = e.rows_d;
   int2 *outrows_d = e.outrows_d;
-  float *h = e.h, *q = e.q;
+  float *h = e.h, *q = e.q, *kvs = e.kvs;
   void *x = e.x, *att = e.att, *u = e.u, *xo = e.xo;
   const int m_max = e.m_max;
   carve_rows(e, rows, scratch);
@@ -1004,6 +1006,7 @@ extern "C" int cortex_forward_batch_noalloc(void *state, const int *tokens, int 
   e.outrows_d = outrows_d;
   e.h = h;
   e.q = q;
+  e.kvs = kvs;
   e.x = x;
   e.att = att;
   e.u = u;

@@ -71,6 +71,7 @@ struct Engine {
   float *h = nullptr;         // [m_max, D] residual stream
   void *x = nullptr;          // [m_max, D] normed input of a projection (fp32 or bf16)
   float *q = nullptr;         // [m_max, att_ch]
+  float *kvs = nullptr;       // [m_max, 2, att_ch] K and V of the new position, when appended by attention
   void *att = nullptr;        // [m_max, D]
   void *u = nullptr;          // [m_max, F]
   void *xo = nullptr;         // [m_max, D] normed rows that need logits
@@ -86,6 +87,7 @@ struct Engine {
   // from pageable memory returns once the source has been consumed, so the
   // buffers can be refilled by the next call without waiting for the GPU.
   std::vector<RowDesc> rows_stage;
+  std::vector<char> slot_seen;  // per slot, for the one-row-per-slot test of a chunk
   std::vector<int2> out_stage;
 
   // host mirrors

@@ -22,6 +22,15 @@ struct EpiQKV {
   const float2 *rope;
   int D, att_ch, hs;
   size_t slot_stride, layer_off, part_stride, head_stride;
+  // non-null: K and V go to this row-major [M, 2, att_ch] staging buffer and
+  // the attention kernel appends them to the cache (one row per slot)
+  float *kvs;
+
+  __device__ __forceinline__ float *kv_dst(const RowDesc &rd, int m, int part, int head, int j) const {
+    if (kvs) return kvs + ((size_t)m * 2 + (part - 1)) * att_ch + (size_t)head * hs + j;
+    return kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)(part - 1) * part_stride +
+           (size_t)head * head_stride + (size_t)rd.pos * hs + j;
+  }
 
   __device__ __forceinline__ void pair(const RowDesc &rd, int m, int n, float a, float b) const {
     const int part = n / D;
@@ -39,9 +48,7 @@ struct EpiQKV {
     if (part == 0) {
       *reinterpret_cast<float2 *>(q + (size_t)m * att_ch + ch) = make_float2(a, b);
     } else {
-      float *dst = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)(part - 1) * part_stride +
-                   (size_t)head * head_stride + (size_t)rd.pos * hs + j;
-      *reinterpret_cast<float2 *>(dst) = make_float2(a, b);
+      *reinterpret_cast<float2 *>(kv_dst(rd, m, part, head, j)) = make_float2(a, b);
     }
   }
 
@@ -70,9 +77,7 @@ struct EpiQKV {
 #pragma unroll
         for (int i = 0; i < 16; ++i) o[i] = v[i];
       }
-      float *dst = part == 0 ? q + (size_t)m * att_ch + ch
-                             : kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)(part - 1) * part_stride +
-                                   (size_t)head * head_stride + (size_t)rd.pos * hs + j;
+      float *dst = part == 0 ? q + (size_t)m * att_ch + ch : kv_dst(rd, m, part, head, j);
 #pragma unroll
       for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4 *>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
       return;

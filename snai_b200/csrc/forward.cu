@@ -147,10 +147,14 @@ __device__ __forceinline__ void att_softmax(float *s, int n, float *red) {
   __syncthreads();
 }
 
+// kvs non-null: K and V of position pos come from the row's staging entry
+// ([M, 2, att_ch]) and are appended to the cache here, where the slot's
+// cache pages are being read anyway (one row per slot in the pass).
 template <typename TA>
 __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
-    const RowDesc *__restrict__ rows, const float *__restrict__ q, const float *__restrict__ kv, TA *__restrict__ out,
-    int D, int att_ch, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride, float sqrt_hs) {
+    const RowDesc *__restrict__ rows, const float *__restrict__ q, float *__restrict__ kv, TA *__restrict__ out,
+    int D, int att_ch, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride, float sqrt_hs,
+    const float *__restrict__ kvs) {
   constexpr int HS = 64;
   extern __shared__ float smem_att[];
   float *red = smem_att;        // [32]
@@ -162,9 +166,18 @@ __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int half = lane >> 4, part = lane & 15;
 
-  const float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
-  const float *vbase = kbase + part_stride;
+  float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
+  float *vbase = kbase + part_stride;
   const float4 qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + part * 4);
+  // cache positions below nc; position pos from the staging entry when deferred
+  const int nc = kvs ? n - 1 : n;
+  const float *kst = kvs ? kvs + (size_t)m * 2 * att_ch + head * HS : nullptr;
+  const float *vst = kvs ? kst + att_ch : nullptr;
+  if (kvs && warp == 0) {
+    // append: lanes 0..15 the K row, lanes 16..31 the V row (16 bytes each)
+    const float4 r = *reinterpret_cast<const float4 *>((half ? vst : kst) + part * 4);
+    *reinterpret_cast<float4 *>((half ? vbase : kbase) + (size_t)rd.pos * HS + part * 4) = r;
+  }
 
   // ---- scores: warp w takes position pairs w, w+4, ...; 8 pairs per sweep ----
   constexpr int U = 8;
@@ -173,8 +186,9 @@ __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int t = 2 * (p0 + u) + half;
-      kr[u] = t < n ? __ldcs(reinterpret_cast<const float4 *>(kbase + (size_t)t * HS + part * 4))
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      kr[u] = t < nc   ? __ldcs(reinterpret_cast<const float4 *>(kbase + (size_t)t * HS + part * 4))
+              : t < n ? *reinterpret_cast<const float4 *>(kst + part * 4)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -197,8 +211,9 @@ __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int t = 2 * (p0 + u) + half;
-      vr[u] = t < n ? __ldcs(reinterpret_cast<const float4 *>(vbase + (size_t)t * HS + part * 4))
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      vr[u] = t < nc   ? __ldcs(reinterpret_cast<const float4 *>(vbase + (size_t)t * HS + part * 4))
+              : t < n ? *reinterpret_cast<const float4 *>(vst + part * 4)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -228,20 +243,25 @@ __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
 // the weighted sum.
 template <typename TA>
 __global__ void __launch_bounds__(kAttThreads) attention_generic_kernel(
-    const RowDesc *__restrict__ rows, const float *__restrict__ q, const float *__restrict__ kv, TA *__restrict__ out,
+    const RowDesc *__restrict__ rows, const float *__restrict__ q, float *__restrict__ kv, TA *__restrict__ out,
     int D, int att_ch, int hs, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride,
-    float sqrt_hs) {
+    float sqrt_hs, const float *__restrict__ kvs) {
   extern __shared__ float smem_att[];
   float *red = smem_att;
   float *s = smem_att + 32;
   const int m = blockIdx.y, head = blockIdx.x;
   const RowDesc rd = rows[m];
   const int n = rd.pos + 1;
-  const float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
-  const float *vbase = kbase + part_stride;
+  float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
+  float *vbase = kbase + part_stride;
   const float *qr = q + (size_t)m * att_ch + (size_t)head * hs;
+  const float *kst = kvs ? kvs + (size_t)m * 2 * att_ch + (size_t)head * hs : nullptr;
+  const float *vst = kvs ? kst + att_ch : nullptr;
+  if (kvs)
+    for (int j = threadIdx.x; j < 2 * hs; j += blockDim.x)
+      (j < hs ? kbase : vbase)[(size_t)rd.pos * hs + (j % hs)] = (j < hs ? kst : vst)[j % hs];
   for (int t = threadIdx.x; t < n; t += blockDim.x) {
-    const float *kr = kbase + (size_t)t * hs;
+    const float *kr = (kvs && t == n - 1) ? kst : kbase + (size_t)t * hs;
     float d = 0.f;
     for (int j = 0; j < hs; ++j) d = __fadd_rn(d, __fmul_rn(qr[j], kr[j]));
     s[t] = __fdiv_rn(d, sqrt_hs);
@@ -251,7 +271,8 @@ __global__ void __launch_bounds__(kAttThreads) attention_generic_kernel(
   TA *orow = out + (size_t)m * D;
   for (int j = threadIdx.x; j < hs; j += blockDim.x) {
     float a = 0.f;
-    for (int t = 0; t < n; ++t) a = __fadd_rn(a, __fmul_rn(vbase[(size_t)t * hs + j], s[t]));
+    for (int t = 0; t < n; ++t)
+      a = __fadd_rn(a, __fmul_rn((kvs && t == n - 1) ? vst[j] : vbase[(size_t)t * hs + j], s[t]));
     ActIO<TA>::store(orow + (size_t)head * hs + j, a);
   }
   if (head == gridDim.x - 1) att_zero_tail(orow, att_ch, D);
@@ -425,7 +446,7 @@ static int project(Engine &e, int kind, int M, int N, int K, const void *A, cons
 }
 
 template <typename TA>
-static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_positions) {
+static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_positions, bool defer) {
   const Dims &d = e.d;
   const int tok = prof_begin(e);
   const size_t layer_off = (size_t)layer * e.kv_layer_stride;
@@ -441,12 +462,14 @@ static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_pos
     const size_t sm = (32 + 4 * 64 + (size_t)max_n) * sizeof(float);
     attention_hs64_kernel<TA><<<grid, kAttThreads, sm, e.stream>>>(e.rows_d, e.q, e.kv, out, d.D, d.att_ch,
                                                                     e.kv_slot_stride, layer_off, e.kv_part_stride,
-                                                                    e.kv_head_stride, e.sqrt_hs);
+                                                                    e.kv_head_stride, e.sqrt_hs,
+                                                                    defer ? e.kvs : nullptr);
   } else {
     const size_t sm = (32 + (size_t)max_n) * sizeof(float);
     attention_generic_kernel<TA><<<grid, kAttThreads, sm, e.stream>>>(e.rows_d, e.q, e.kv, out, d.D, d.att_ch, d.hs,
                                                                        e.kv_slot_stride, layer_off, e.kv_part_stride,
-                                                                       e.kv_head_stride, e.sqrt_hs);
+                                                                       e.kv_head_stride, e.sqrt_hs,
+                                                                       defer ? e.kvs : nullptr);
   }
   e.launches++;
   // K and V of positions 0..pos per row, q in, att out
@@ -463,7 +486,8 @@ static void launch_norm(Engine &e, int M, const int2 *gather, const float *w, TA
 }
 
 template <typename TA>
-static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, bool out_tc, double kv_positions) {
+static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, bool out_tc, double kv_positions,
+                           bool defer) {
   const Dims &d = e.d;
   const double ea = sizeof(TA);
   TA *x = static_cast<TA *>(e.x);
@@ -477,10 +501,10 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
   for (int l = 0; l < d.L; ++l) {
     const LayerWeights &w = e.layers[l];
     EpiQKV eq{e.rows_d, e.q, e.kv, e.rope, d.D, d.att_ch, d.hs, e.kv_slot_stride, (size_t)l * e.kv_layer_stride,
-              e.kv_part_stride, e.kv_head_stride};
+              e.kv_part_stride, e.kv_head_stride, defer ? e.kvs : nullptr};
     int rc = project(e, kProfQKV, M, 3 * d.D, d.D, x, w.wqkv, w.wqkv_h, eq, 3.0 * M * d.att_ch * 4);
     if (rc) return rc;
-    launch_attention<TA>(e, M, l, att, kv_positions);
+    launch_attention<TA>(e, M, l, att, kv_positions, defer);
     rc = project(e, kProfWo, M, d.D, d.D, att, w.wo, w.wo_h, EpiResidual{e.h, d.D}, 8.0 * M * d.D);
     if (rc) return rc;
     launch_norm<TA>(e, M, nullptr, w.rms_ffn, x);
@@ -517,6 +541,15 @@ int run_rows(Engine &e, const RowDesc *rows, int n, const int *tokens_d) {
       if (e.rows_stage[i].out >= 0) e.out_stage.push_back(make_int2(i, e.rows_stage[i].out));
     }
     const int n_out = (int)e.out_stage.size();
+    // every slot at most once in the chunk (a decode step): the new K and V
+    // are staged and appended by the attention kernel
+    bool defer = true;
+    e.slot_seen.assign((size_t)e.max_seqs, 0);
+    for (int i = 0; i < M && defer; ++i) {
+      const int s = e.rows_stage[i].slot;
+      defer = !e.slot_seen[s];
+      e.slot_seen[s] = 1;
+    }
     if (cudaMemcpyAsync(e.rows_d, e.rows_stage.data(), sizeof(RowDesc) * M, cudaMemcpyHostToDevice, e.stream) !=
             cudaSuccess ||
         (n_out && cudaMemcpyAsync(e.outrows_d, e.out_stage.data(), sizeof(int2) * n_out, cudaMemcpyHostToDevice,
@@ -527,8 +560,8 @@ int run_rows(Engine &e, const RowDesc *rows, int n, const int *tokens_d) {
     const bool tc = tc_path(e, M);
     const bool out_tc = tc_path(e, n_out);
     const int rc = (tc && e.precision == kBF16)
-                       ? run_chunk_typed<__nv_bfloat16>(e, M, tokens_d, n_out, out_tc, kv_positions)
-                       : run_chunk_typed<float>(e, M, tokens_d, n_out, out_tc, kv_positions);
+                       ? run_chunk_typed<__nv_bfloat16>(e, M, tokens_d, n_out, out_tc, kv_positions, defer)
+                       : run_chunk_typed<float>(e, M, tokens_d, n_out, out_tc, kv_positions, defer);
     if (rc) return rc;
     const cudaError_t le = cudaGetLastError();
     if (le != cudaSuccess) {
