@@ -98,8 +98,10 @@ bool make_dims(int vocab, int dim, int ctx, int layers, int heads, Dims *d) {
     set_error("num_heads %d gives head size %d: %d heads x %d > hidden_dim %d", heads, hs, d->heads, hs, dim);
     return false;
   }
-  if ((size_t)ctx * sizeof(float) + 2048 > 200 * 1024) {
-    set_error("ctx_size %d exceeds this engine's attention limit (%d)", ctx, (200 * 1024 - 2048) / 4);
+  // attention keeps a score per position and two rotated head vectors in shared memory
+  if (((size_t)ctx + 2 * (size_t)hs) * sizeof(float) + 2048 > 200 * 1024) {
+    set_error("ctx_size %d with head size %d exceeds this engine's attention limit (%d positions)", ctx, hs,
+              (200 * 1024 - 2048) / 4 - 2 * hs);
     return false;
   }
   return true;

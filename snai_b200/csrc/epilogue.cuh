@@ -1,6 +1,14 @@
 // epilogue.cuh - what a projection does with its fp32 results.
 //
-// store(m, n, v, cnt) receives v[0..cnt) = C[m][n .. n+cnt) for an even n.
+// store(m, n, v, cnt) receives v[0..cnt) = C[m][n .. n+cnt) for an even n
+// (up to 16 columns of one row); store4(m, n, v, cnt, pre) receives up to 4
+// columns from n, a multiple of 4 (the tensor-core drains hand consecutive
+// lanes consecutive 4-column groups of one row, so these stores coalesce),
+// with pre = load4(m, n, cnt), which the drains issue ahead of time (the
+// residual's old values; nothing for the others), and ri = row(m), loaded
+// once per tile by the lane that owns row m.  prefetch(m, n, cols) warms L2
+// with what a tile's drain will read (called before the accumulator is
+// ready).
 // The element-wise arithmetic mirrors core/cortex.nim operation for
 // operation (explicit _rn intrinsics: no contraction into FMA), so the only
 // differences from the reference are the dot products' summation order.
@@ -23,7 +31,10 @@ struct EpiQKV {
   int D, att_ch, hs;
   size_t slot_stride, layer_off, part_stride, head_stride;
   // non-null: K and V go to this row-major [M, 2, att_ch] staging buffer and
-  // the attention kernel appends them to the cache (one row per slot)
+  // the attention kernel appends them to the cache (one row per slot); it
+  // also applies RoPE to q and k then (one position per block there, where a
+  // decode step's rows, all at one position, would otherwise hammer one
+  // table row from every SM at once)
   float *kvs;
 
   __device__ __forceinline__ float *kv_dst(const RowDesc &rd, int m, int part, int head, int j) const {
@@ -38,7 +49,7 @@ struct EpiQKV {
     if (ch >= att_ch) return;
     const int head = ch / hs;
     const int j = ch - head * hs;
-    if (part < 2) {
+    if (part < 2 && !kvs) {
       const float2 cs = rope[(size_t)rd.pos * (hs >> 1) + (j >> 1)];
       const float a2 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
       const float b2 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
@@ -52,6 +63,36 @@ struct EpiQKV {
     }
   }
 
+  struct Pre {};
+  using Row = RowDesc;
+  __device__ __forceinline__ Row row(int m) const { return rows[m]; }
+  __device__ __forceinline__ void prefetch(int, int, int) const {}
+  __device__ __forceinline__ Pre load4(int, int, int) const { return Pre{}; }
+  __device__ __forceinline__ void store4(int m, int n, float4 v, int cnt, Pre, const RowDesc &rd) const {
+    if (cnt == 4 && (hs & 3) == 0 && (D & 3) == 0) {
+      const int part = (n >= D) + (n >= 2 * D);
+      const int ch = n - part * D;
+      if (ch >= att_ch) return;
+      const int head = (hs & (hs - 1)) == 0 ? ch >> (__ffs(hs) - 1) : ch / hs;
+      const int j = ch - head * hs;
+      float4 o = v;
+      if (part < 2 && !kvs) {
+        const float4 c = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (hs >> 1) + (j >> 1));
+        o.x = __fsub_rn(__fmul_rn(v.x, c.x), __fmul_rn(v.y, c.y));
+        o.y = __fadd_rn(__fmul_rn(v.x, c.y), __fmul_rn(v.y, c.x));
+        o.z = __fsub_rn(__fmul_rn(v.z, c.z), __fmul_rn(v.w, c.w));
+        o.w = __fadd_rn(__fmul_rn(v.z, c.w), __fmul_rn(v.w, c.z));
+      }
+      float *dst = part == 0 ? q + (size_t)m * att_ch + ch : kv_dst(rd, m, part, head, j);
+      *reinterpret_cast<float4 *>(dst) = o;
+      return;
+    }
+    const float a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i + 1 < 4; i += 2)
+      if (i + 1 < cnt) pair(rd, m, n + i, a[i], a[i + 1]);
+  }
+
   __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
     const RowDesc rd = rows[m];
     if (cnt == 16 && (hs & 15) == 0 && (D & 15) == 0) {
@@ -62,7 +103,7 @@ struct EpiQKV {
       const int head = ch / hs;
       const int j = ch - head * hs;
       float o[16];
-      if (part < 2) {
+      if (part < 2 && !kvs) {
         const float4 *cs = reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (hs >> 1) + (j >> 1));
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -92,17 +133,47 @@ struct EpiQKV {
 struct EpiResidual {
   float *h;
   int ld;
+  using Pre = float4;
+  struct Row {};
+  __device__ __forceinline__ Row row(int) const { return Row{}; }
+  __device__ __forceinline__ void prefetch(int m, int n, int cols) const {
+    const char *p = reinterpret_cast<const char *>(h + (size_t)m * ld + n);
+    for (int b = 0; b < cols * 4; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + b));
+  }
+  __device__ __forceinline__ Pre load4(int m, int n, int cnt) const {
+    const float *p = h + (size_t)m * ld + n;
+    if (cnt == 4 && (ld & 3) == 0) return __ldcg(reinterpret_cast<const float4 *>(p));
+    return make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __device__ __forceinline__ void store4(int m, int n, float4 v, int cnt, Pre pre, Row) const {
+    float *p = h + (size_t)m * ld + n;
+    if (cnt == 4 && (ld & 3) == 0) {
+      float4 o = pre;
+      o.x = __fadd_rn(o.x, v.x);
+      o.y = __fadd_rn(o.y, v.y);
+      o.z = __fadd_rn(o.z, v.z);
+      o.w = __fadd_rn(o.w, v.w);
+      *reinterpret_cast<float4 *>(p) = o;
+      return;
+    }
+    const float a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (i < cnt) p[i] = __fadd_rn(p[i], a[i]);
+  }
   __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
     float *p = h + (size_t)m * ld + n;
     if (cnt == 16 && (ld & 3) == 0) {
+      float4 o[4];  // all four loads in flight before any store
 #pragma unroll
-      for (int i = 0; i < 16; i += 4) {
-        float4 o = *reinterpret_cast<float4 *>(p + i);
-        o.x = __fadd_rn(o.x, v[i]);
-        o.y = __fadd_rn(o.y, v[i + 1]);
-        o.z = __fadd_rn(o.z, v[i + 2]);
-        o.w = __fadd_rn(o.w, v[i + 3]);
-        *reinterpret_cast<float4 *>(p + i) = o;
+      for (int i = 0; i < 4; ++i) o[i] = __ldcg(reinterpret_cast<const float4 *>(p + 4 * i));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        o[i].x = __fadd_rn(o[i].x, v[4 * i]);
+        o[i].y = __fadd_rn(o[i].y, v[4 * i + 1]);
+        o[i].z = __fadd_rn(o[i].z, v[4 * i + 2]);
+        o[i].w = __fadd_rn(o[i].w, v[4 * i + 3]);
+        *reinterpret_cast<float4 *>(p + 4 * i) = o[i];
       }
     } else {
 #pragma unroll
@@ -119,6 +190,29 @@ struct EpiSilu {
   int ld;
   __device__ static __forceinline__ float silu(float x) {
     return __fmul_rn(x, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))));
+  }
+  struct Pre {};
+  struct Row {};
+  __device__ __forceinline__ Row row(int) const { return Row{}; }
+  __device__ __forceinline__ void prefetch(int, int, int) const {}
+  __device__ __forceinline__ Pre load4(int, int, int) const { return Pre{}; }
+  __device__ __forceinline__ void store4(int m, int n, float4 v, int cnt, Pre, Row) const {
+    TA *p = u + (size_t)m * ld + n;
+    if (cnt == 4 && (ld & 3) == 0) {
+      if constexpr (sizeof(TA) == 2) {
+        const __nv_bfloat162 h0 = __floats2bfloat162_rn(silu(v.x), silu(v.y));
+        const __nv_bfloat162 h1 = __floats2bfloat162_rn(silu(v.z), silu(v.w));
+        *reinterpret_cast<uint2 *>(p) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
+      } else {
+        *reinterpret_cast<float4 *>(p) = make_float4(silu(v.x), silu(v.y), silu(v.z), silu(v.w));
+      }
+      return;
+    }
+    const float a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (i < cnt) ActIO<TA>::store(p + i, silu(a[i]));
   }
   __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
     TA *p = u + (size_t)m * ld + n;
@@ -150,6 +244,22 @@ struct EpiLogits {
   float *logits;
   const int2 *outrows;  // chunk-local logits row -> (chunk row, slot)
   long long ld;
+  struct Pre {};
+  using Row = int;
+  __device__ __forceinline__ Row row(int m) const { return outrows[m].y; }
+  __device__ __forceinline__ void prefetch(int, int, int) const {}
+  __device__ __forceinline__ Pre load4(int, int, int) const { return Pre{}; }
+  __device__ __forceinline__ void store4(int m, int n, float4 v, int cnt, Pre, int orow) const {
+    float *p = logits + (size_t)orow * ld + n;
+    if (cnt == 4 && (ld & 3) == 0) {
+      *reinterpret_cast<float4 *>(p) = v;
+      return;
+    }
+    const float a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (i < cnt) p[i] = a[i];
+  }
   __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
     float *p = logits + (size_t)outrows[m].y * ld + n;
     if (cnt == 16 && (ld & 3) == 0) {

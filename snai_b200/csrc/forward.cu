@@ -147,14 +147,24 @@ __device__ __forceinline__ void att_softmax(float *s, int n, float *red) {
   __syncthreads();
 }
 
+// RoPE of one 4-channel group (two pairs) with (cos, sin) of both pairs
+// (core/cortex.nim:74-87).
+__device__ __forceinline__ float4 rope4(float4 v, float4 c) {
+  return make_float4(__fsub_rn(__fmul_rn(v.x, c.x), __fmul_rn(v.y, c.y)),
+                     __fadd_rn(__fmul_rn(v.x, c.y), __fmul_rn(v.y, c.x)),
+                     __fsub_rn(__fmul_rn(v.z, c.z), __fmul_rn(v.w, c.w)),
+                     __fadd_rn(__fmul_rn(v.z, c.w), __fmul_rn(v.w, c.z)));
+}
+
 // kvs non-null: K and V of position pos come from the row's staging entry
-// ([M, 2, att_ch]) and are appended to the cache here, where the slot's
-// cache pages are being read anyway (one row per slot in the pass).
+// ([M, 2, att_ch], without RoPE, as q) and are appended to the cache here,
+// where the slot's cache pages are being read anyway (one row per slot in
+// the pass); RoPE of q and k is applied here then.
 template <typename TA>
 __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
     const RowDesc *__restrict__ rows, const float *__restrict__ q, float *__restrict__ kv, TA *__restrict__ out,
     int D, int att_ch, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride, float sqrt_hs,
-    const float *__restrict__ kvs) {
+    const float *__restrict__ kvs, const float2 *__restrict__ rope) {
   constexpr int HS = 64;
   extern __shared__ float smem_att[];
   float *red = smem_att;        // [32]
@@ -168,15 +178,19 @@ __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
 
   float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
   float *vbase = kbase + part_stride;
-  const float4 qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + part * 4);
+  float4 qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + part * 4);
   // cache positions below nc; position pos from the staging entry when deferred
   const int nc = kvs ? n - 1 : n;
   const float *kst = kvs ? kvs + (size_t)m * 2 * att_ch + head * HS : nullptr;
   const float *vst = kvs ? kst + att_ch : nullptr;
-  if (kvs && warp == 0) {
-    // append: lanes 0..15 the K row, lanes 16..31 the V row (16 bytes each)
-    const float4 r = *reinterpret_cast<const float4 *>((half ? vst : kst) + part * 4);
-    *reinterpret_cast<float4 *>((half ? vbase : kbase) + (size_t)rd.pos * HS + part * 4) = r;
+  float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
+  if (kvs) {
+    const float4 cs = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + part * 2);
+    qv = rope4(qv, cs);
+    knew = rope4(*reinterpret_cast<const float4 *>(kst + part * 4), cs);
+    vnew = *reinterpret_cast<const float4 *>(vst + part * 4);
+    if (warp == 0)  // append: lanes 0..15 the K row, lanes 16..31 the V row
+      *reinterpret_cast<float4 *>((half ? vbase : kbase) + (size_t)rd.pos * HS + part * 4) = half ? vnew : knew;
   }
 
   // ---- scores: warp w takes position pairs w, w+4, ...; 8 pairs per sweep ----
@@ -187,7 +201,7 @@ __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
     for (int u = 0; u < U; ++u) {
       const int t = 2 * (p0 + u) + half;
       kr[u] = t < nc   ? __ldcs(reinterpret_cast<const float4 *>(kbase + (size_t)t * HS + part * 4))
-              : t < n ? *reinterpret_cast<const float4 *>(kst + part * 4)
+              : t < n ? knew
                       : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
@@ -212,7 +226,7 @@ __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
     for (int u = 0; u < U; ++u) {
       const int t = 2 * (p0 + u) + half;
       vr[u] = t < nc   ? __ldcs(reinterpret_cast<const float4 *>(vbase + (size_t)t * HS + part * 4))
-              : t < n ? *reinterpret_cast<const float4 *>(vst + part * 4)
+              : t < n ? vnew
                       : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
@@ -245,7 +259,7 @@ template <typename TA>
 __global__ void __launch_bounds__(kAttThreads) attention_generic_kernel(
     const RowDesc *__restrict__ rows, const float *__restrict__ q, float *__restrict__ kv, TA *__restrict__ out,
     int D, int att_ch, int hs, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride,
-    float sqrt_hs, const float *__restrict__ kvs) {
+    float sqrt_hs, const float *__restrict__ kvs, const float2 *__restrict__ rope) {
   extern __shared__ float smem_att[];
   float *red = smem_att;
   float *s = smem_att + 32;
@@ -257,11 +271,25 @@ __global__ void __launch_bounds__(kAttThreads) attention_generic_kernel(
   const float *qr = q + (size_t)m * att_ch + (size_t)head * hs;
   const float *kst = kvs ? kvs + (size_t)m * 2 * att_ch + (size_t)head * hs : nullptr;
   const float *vst = kvs ? kst + att_ch : nullptr;
-  if (kvs)
+  float *qrot = smem_att + 32 + n;  // [hs] q after RoPE (deferred mode)
+  float *krot = qrot + hs;          // [hs] new k after RoPE
+  if (kvs) {
+    // RoPE of q and of the new k (the staging entries hold them unrotated)
+    for (int p = threadIdx.x; p < hs / 2; p += blockDim.x) {
+      const float2 cs = rope[(size_t)rd.pos * (hs / 2) + p];
+      const float a = qr[2 * p], b = qr[2 * p + 1], ka = kst[2 * p], kb = kst[2 * p + 1];
+      qrot[2 * p] = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+      qrot[2 * p + 1] = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+      krot[2 * p] = __fsub_rn(__fmul_rn(ka, cs.x), __fmul_rn(kb, cs.y));
+      krot[2 * p + 1] = __fadd_rn(__fmul_rn(ka, cs.y), __fmul_rn(kb, cs.x));
+    }
+    __syncthreads();
     for (int j = threadIdx.x; j < 2 * hs; j += blockDim.x)
-      (j < hs ? kbase : vbase)[(size_t)rd.pos * hs + (j % hs)] = (j < hs ? kst : vst)[j % hs];
+      (j < hs ? kbase : vbase)[(size_t)rd.pos * hs + (j % hs)] = (j < hs ? krot : vst)[j % hs];
+    qr = qrot;
+  }
   for (int t = threadIdx.x; t < n; t += blockDim.x) {
-    const float *kr = (kvs && t == n - 1) ? kst : kbase + (size_t)t * hs;
+    const float *kr = (kvs && t == n - 1) ? krot : kbase + (size_t)t * hs;
     float d = 0.f;
     for (int j = 0; j < hs; ++j) d = __fadd_rn(d, __fmul_rn(qr[j], kr[j]));
     s[t] = __fdiv_rn(d, sqrt_hs);
@@ -399,13 +427,41 @@ static int launch_tcp(Engine &e, int M, int N, int K, const void *A, const void 
   }
   const int tiles = ((M + kTcBM - 1) / kTcBM) * ((N + BN - 1) / BN);
   const int grid = std::min(tiles, sm_count(e.device));
-  kern<<<grid, 320, Sm::kBytes, e.stream>>>(ta, tb, M, N, K, epi, e.err_d);
+  kern<<<grid, kGemmThreads, Sm::kBytes, e.stream>>>(ta, tb, M, N, K, epi, e.err_d);
+  e.launches++;
+  return 0;
+}
+
+// CTA-pair tcgen05 GEMM (gemm_tc2_kernel): 256 x 256 tiles on SM pairs.
+template <typename TIn, class Epi>
+static int launch_tc2(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
+  constexpr int STAGES = 6;
+  using Sm = Tc2Smem<STAGES>;
+  auto kern = gemm_tc2_kernel<TIn, STAGES, Epi>;
+  static unsigned long long attr_set = 0;  // per instantiation, one bit per device
+  if (!(attr_set & (1ull << e.device))) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Sm::kBytes) != cudaSuccess) {
+      set_error("cudaFuncSetAttribute failed for the CTA-pair GEMM");
+      return -5;
+    }
+    attr_set |= 1ull << e.device;
+  }
+  CUtensorMap ta, tb;
+  const bool bf = sizeof(TIn) == 2;
+  if (!make_tmap(&ta, A, bf, K, M, kTcBM) || !make_tmap(&tb, W, bf, K, N, 128)) {
+    set_error("cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", M, N, K);
+    return -5;
+  }
+  const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  const int pairs = std::max(1, std::min(tiles, sm_count(e.device) / 2));
+  kern<<<2 * pairs, kGemmThreads, Sm::kBytes, e.stream>>>(ta, tb, M, N, K, epi, e.err_d);
   e.launches++;
   return 0;
 }
 
 template <typename TIn, class Epi>
 static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
+  if (M >= 256 && N >= 256) return launch_tc2<TIn>(e, M, N, K, A, W, epi);
   if (N >= 2048) return launch_tcp<TIn, 256>(e, M, N, K, A, W, epi);
   return launch_tcp<TIn, 128>(e, M, N, K, A, W, epi);
 }
@@ -463,13 +519,13 @@ static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_pos
     attention_hs64_kernel<TA><<<grid, kAttThreads, sm, e.stream>>>(e.rows_d, e.q, e.kv, out, d.D, d.att_ch,
                                                                     e.kv_slot_stride, layer_off, e.kv_part_stride,
                                                                     e.kv_head_stride, e.sqrt_hs,
-                                                                    defer ? e.kvs : nullptr);
+                                                                    defer ? e.kvs : nullptr, e.rope);
   } else {
-    const size_t sm = (32 + (size_t)max_n) * sizeof(float);
+    const size_t sm = (32 + (size_t)max_n + 2 * (size_t)d.hs) * sizeof(float);
     attention_generic_kernel<TA><<<grid, kAttThreads, sm, e.stream>>>(e.rows_d, e.q, e.kv, out, d.D, d.att_ch, d.hs,
                                                                        e.kv_slot_stride, layer_off, e.kv_part_stride,
                                                                        e.kv_head_stride, e.sqrt_hs,
-                                                                       defer ? e.kvs : nullptr);
+                                                                       defer ? e.kvs : nullptr, e.rope);
   }
   e.launches++;
   // K and V of positions 0..pos per row, q in, att out

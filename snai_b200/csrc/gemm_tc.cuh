@@ -79,12 +79,93 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Epilogue warps per CTA: four per TMEM lane quarter, each taking a quarter
+// of the tile's columns, so a warp drains its accumulator slice with one
+// round of TMEM loads.
+constexpr int kEpiWarps = 16;
+constexpr int kGemmThreads = (2 + kEpiWarps) * 32;
+
+constexpr int kStageFloats = 32 * 16;  // per-warp transpose buffer: 32 rows x 16 columns
+
+// Drains COLS accumulator columns of one TMEM lane quarter (rows row0 ..
+// row0 + 31), 32 columns per round of TMEM loads and one wait.  Each
+// 16-column run then goes through the warp's shared-memory buffer (16-byte
+// chunks XOR-swizzled by row pair, conflict-free both ways) so that each
+// store instruction covers 8 rows x 64 contiguous bytes instead of 32 rows x
+// 16 bytes; the epilogue functor takes 4-column groups (rows >= M and
+// columns >= N are skipped).
+// A lane's copy of another lane's trivially copyable value (32-bit words).
+template <class T>
+__device__ __forceinline__ T shfl_any(const T &v, int src) {
+  if constexpr (sizeof(T) % 4 != 0 || sizeof(T) == 0) {
+    return v;
+  } else {
+    T out;
+    const uint32_t *pi = reinterpret_cast<const uint32_t *>(&v);
+    uint32_t *po = reinterpret_cast<uint32_t *>(&out);
+#pragma unroll
+    for (int i = 0; i < (int)(sizeof(T) / 4); ++i) po[i] = __shfl_sync(0xffffffffu, pi[i], src);
+    return out;
+  }
+}
+
+template <int COLS, class Epi>
+__device__ __forceinline__ void drain_accumulator(uint32_t tbase, int row0, int M, int n0, int N, const Epi &epi,
+                                                  float *stg) {
+  const int lane = threadIdx.x & 31;
+  using Row = typename Epi::Row;
+  const Row mine = row0 + lane < M ? epi.row(row0 + lane) : Row{};
+  float4 *buf = reinterpret_cast<float4 *>(stg);
+  constexpr int BLK = COLS < 32 ? COLS : 32;  // columns per TMEM load round
+#pragma unroll
+  for (int c0 = 0; c0 < COLS; c0 += BLK) {
+  if (n0 + c0 >= N) break;  // warp-uniform
+  uint32_t rb[BLK];
+#pragma unroll
+  for (int c = 0; c < BLK; c += 16) tmem_ld16_nowait(tbase + (uint32_t)(c0 + c), rb + c);
+  tmem_wait_ld();
+  uint32_t *r = rb - c0;  // r[c0 + j] == rb[j]
+#pragma unroll
+  for (int c = c0; c < c0 + BLK; c += 16) {
+    if (n0 + c >= N) break;  // warp-uniform
+    // this run's reads (residual) go out first and overlap the transpose
+    typename Epi::Pre pre[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int m = row0 + 8 * i + (lane >> 2), n = n0 + c + 4 * (lane & 3);
+      if (m < M && n < N) pre[i] = epi.load4(m, n, min(4, N - n));
+    }
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch)
+      buf[lane * 4 + (ch ^ ((lane >> 1) & 3))] =
+          make_float4(__uint_as_float(r[c + 4 * ch]), __uint_as_float(r[c + 4 * ch + 1]),
+                      __uint_as_float(r[c + 4 * ch + 2]), __uint_as_float(r[c + 4 * ch + 3]));
+    __syncwarp();
+    float4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = 8 * i + (lane >> 2), qq = lane & 3;
+      v[i] = buf[rr * 4 + (qq ^ ((rr >> 1) & 3))];
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = 8 * i + (lane >> 2);
+      const Row ri = shfl_any(mine, rr);
+      const int m = row0 + rr, n = n0 + c + 4 * (lane & 3);
+      if (m < M && n < N) epi.store4(m, n, v[i], min(4, N - n), pre[i], ri);
+    }
+  }
+  }
+}
+
 template <int BN, int STAGES>
 struct TcpSmem {
   static constexpr int kABytes = kTcBM * 128;
   static constexpr int kBBytes = BN * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kStgOffset = STAGES * kStageBytes;  // epilogue transpose buffers
+  static constexpr int kBarOffset = kStgOffset + kEpiWarps * kStageFloats * 4;
   static constexpr int kBytes = kBarOffset + 256 + 1024;
 };
 
@@ -95,14 +176,14 @@ struct TcpSmem {
 //                   running k-block counter);
 //   warp 1          allocates 2*BN TMEM columns (two accumulators); lane 0
 //                   issues the tcgen05.mma of tile i into accumulator i % 2;
-//   warps 2..9      epilogue: two warps per 32-lane TMEM quarter, each taking
-//                   half of the tile's columns; wait for accumulator i % 2,
-//                   tcgen05.ld, hand 16-column runs to Epi, release the
-//                   accumulator; this overlaps the MMAs of tile i + 1.
+//   warps 2..17     epilogue: four warps per 32-lane TMEM quarter, each taking
+//                   a quarter of the tile's columns; wait for accumulator
+//                   i % 2, tcgen05.ld, hand 16-column runs to Epi, release
+//                   the accumulator; this overlaps the MMAs of tile i + 1.
 // All waits are bounded (common.cuh); a failed wait records an error and the
 // CTA winds down.
 template <typename TIn, int BN, int STAGES, class Epi>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcp_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                     int K, Epi epi, int *err) {
   using Sm = TcpSmem<BN, STAGES>;
@@ -132,7 +213,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 8);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     *cta_fail = 0;
     fence_barrier_init();
@@ -206,12 +287,16 @@ __global__ void __launch_bounds__(320, 1)
       }
     }
   } else {
-    // epilogue warps 2..9: TMEM lane quarter = warp % 4, column half by warp
+    // epilogue warps: TMEM lane quarter = warp % 4, column quarter by warp
     const int q = warp & 3;
-    const int c_lo = ((warp - 2) >> 2) * (BN / 2);
+    const int c_lo = ((warp - 2) >> 2) * (BN / 4);
     int tc = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tc) {
       const int acc = tc & 1;
+      {
+        const int pm = (tile % num_m) * kTcBM + q * 32 + lane, pn = (tile / num_m) * BN + c_lo;
+        if (pm < M && pn < N) epi.prefetch(pm, pn, min(BN / 4, N - pn));
+      }
       if (!mbar_wait_bounded(&tfull[acc], (uint32_t)(tc >> 1) & 1u, err, kErrWaitAccum) ||
           *(volatile int *)cta_fail) {
         atomicExch(cta_fail, 1);
@@ -219,15 +304,10 @@ __global__ void __launch_bounds__(320, 1)
       }
       tc_fence_after();
       const int m0 = (tile % num_m) * kTcBM, n0 = (tile / num_m) * BN;
-      const int row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
-#pragma unroll 1
-      for (int c = c_lo; c < c_lo + BN / 2; c += 16) {
-        if (n0 + c >= N) break;  // warp-uniform
-        float v[16];
-        tmem_ld16(tbase + (uint32_t)c, v);
-        if (row < M) epi.store(row, n0 + c, v, min(16, N - (n0 + c)));
-      }
+      if (n0 + c_lo < N)
+        drain_accumulator<BN / 4>(tbase + (uint32_t)c_lo, m0 + q * 32, M, n0 + c_lo, N, epi,
+                                  reinterpret_cast<float *>(smem + Sm::kStgOffset) + (warp - 2) * kStageFloats);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -237,6 +317,279 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, TCOLS);
+}
+
+// ============================================================================
+// CTA-pair GEMM (tcgen05 cta_group::2): a cluster of two CTAs on two SMs
+// computes one 256 x 256 tile.  Each CTA stages its own 128 rows of A and
+// its own 128 rows of W (half of the tile's N) with TMA loads that complete
+// on the leader CTA's barrier; the leader issues M=256, N=256 MMAs that read
+// both CTAs' shared memory and write a 128 x 256 fp32 accumulator into each
+// CTA's TMEM.  Per SM this moves 32 KB per 64-deep k-block for 128x256x64
+// MACs, two thirds of the 128 x 256 single-CTA tile's bytes: the projections
+// are bound by L2 -> SM bandwidth, not by the tensor cores.  No multicast
+// loads are used.
+// ============================================================================
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of `saddr` (a shared::cta address) in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (arrivals come from the peer CTA).
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t parity, int *err, int code) {
+  if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+    if ((it & 63u) == 0 && global_timer_ns() - t0 > kWaitTimeoutNs) {
+      record_error(err, code);
+      return false;
+    }
+  }
+}
+// 2-D tiled load into this CTA's shared memory, completing on a barrier of
+// either CTA of the pair (cluster address); no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *tmap, uint32_t bar_cluster, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Arrives on `bar` in both CTAs of the pair once the pair MMAs issued so far are done.
+__device__ __forceinline__ void tc_commit_pair(uint64_t *bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+template <typename TIn>
+__device__ __forceinline__ void tc_mma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate);
+template <>
+__device__ __forceinline__ void tc_mma_pair<__nv_bfloat16>(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+template <>
+__device__ __forceinline__ void tc_mma_pair<float>(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                   uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// M = 256, N = 256 instruction descriptor
+template <typename TIn>
+__device__ __forceinline__ constexpr uint32_t tc_idesc_pair() {
+  return (1u << 4) | (TcKind<TIn>::kFmt << 7) | (TcKind<TIn>::kFmt << 10) | ((uint32_t)(256 >> 3) << 17) |
+         ((uint32_t)(256 >> 4) << 24);
+}
+
+template <int STAGES>
+struct Tc2Smem {
+  static constexpr int kABytes = kTcBM * 128;  // this CTA's 128 rows of A, one 128-byte K slice each
+  static constexpr int kBBytes = 128 * 128;    // this CTA's 128 rows of W
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStgOffset = STAGES * kStageBytes;  // epilogue transpose buffers
+  static constexpr int kBarOffset = kStgOffset + kEpiWarps * kStageFloats * 4;
+  static constexpr int kBytes = kBarOffset + 256 + 1024;
+};
+
+// Persistent CTA-pair GEMM.  Pair p = blockIdx.x / 2 walks the 256 x 256
+// tiles p, p + pairs, ... (M-fastest).  Roles as in gemm_tcp_kernel; the MMA
+// warp of the leader (cluster rank 0) issues for both CTAs, its commits
+// arrive on both CTAs' barriers, and both CTAs' epilogue warps release an
+// accumulator on the leader's barrier (kEpiWarps per CTA).  Every wait is
+// bounded.
+template <typename TIn, int STAGES, class Epi>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                    int K, Epi epi, int *err) {
+  using Sm = Tc2Smem<STAGES>;
+  constexpr int BK = TcKind<TIn>::kBK;
+  constexpr int KSTEPS = BK / TcKind<TIn>::kUK;
+  constexpr uint32_t IDESC = tc_idesc_pair<TIn>();
+  constexpr uint32_t TCOLS = 512;  // two 256-column accumulators
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + Sm::kBarOffset);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tfull = empty + STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(tempty + 2);
+  int *cta_fail = reinterpret_cast<int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_m = (M + 255) / 256;
+  const int num_tiles = num_m * ((N + 255) / 256);
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpiWarps);
+    }
+    *cta_fail = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, TCOLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < num_tiles; tile += npairs) {
+        const int m0 = (tile % num_m) * 256 + (int)rank * 128;
+        const int n0 = (tile / num_m) * 256 + (int)rank * 128;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, kErrWaitEmpty) || *(volatile int *)cta_fail) {
+            atomicExch(cta_fail, 1);
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * Sm::kStageBytes);
+          const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+          uint8_t *st = smem + s * Sm::kStageBytes;
+          tma_load_2d_pair(st, &tmA, fb, kb * BK, m0);
+          tma_load_2d_pair(st + Sm::kABytes, &tmB, fb, kb * BK, n0);
+        }
+      }
+      // the leader's full barriers also count the peer's copies: do not leave
+      // while one into either CTA is in flight
+      if (leader)
+        for (int j = it - 1; j >= 0 && j >= it - STAGES; --j)
+          if (!mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, err, kErrWaitDrain)) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      int it = 0, tc = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < num_tiles; tile += npairs, ++tc) {
+        const int acc = tc & 1;
+        if (!mbar_wait_cluster_bounded(&tempty[acc], ((uint32_t)(tc >> 1) & 1u) ^ 1u, err, kErrWaitEmpty)) {
+          atomicExch(cta_fail, 1);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * 256);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait_bounded(&full[s], ph, err, kErrWaitFull) || *(volatile int *)cta_fail) {
+            atomicExch(cta_fail, 1);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + s * Sm::kStageBytes);
+          const uint64_t adesc = sw128_desc(a0), bdesc = sw128_desc(a0 + Sm::kABytes);
+#pragma unroll
+          for (int k = 0; k < KSTEPS; ++k)
+            tc_mma_pair<TIn>(d, adesc + 2u * k, bdesc + 2u * k, IDESC, (kb | k) != 0 ? 1u : 0u);
+          tc_commit_pair(&empty[s]);
+        }
+        tc_commit_pair(&tfull[acc]);
+      }
+    }
+  } else {
+    // epilogue warps: TMEM lane quarter = warp % 4, column quarter by warp
+    const int q = warp & 3;
+    const int c_lo = ((warp - 2) >> 2) * 64;
+    const uint32_t te0 = mapa_shared(smem_u32(&tempty[0]), 0), te1 = mapa_shared(smem_u32(&tempty[1]), 0);
+    int tc = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++tc) {
+      const int acc = tc & 1;
+      {
+        const int pm = (tile % num_m) * 256 + (int)rank * 128 + q * 32 + lane, pn = (tile / num_m) * 256 + c_lo;
+        if (pm < M && pn < N) epi.prefetch(pm, pn, min(64, N - pn));
+      }
+      if (!mbar_wait_bounded(&tfull[acc], (uint32_t)(tc >> 1) & 1u, err, kErrWaitAccum) ||
+          *(volatile int *)cta_fail) {
+        atomicExch(cta_fail, 1);
+        break;
+      }
+      tc_fence_after();
+      const int m0 = (tile % num_m) * 256 + (int)rank * 128, n0 = (tile / num_m) * 256;
+      const uint32_t tbase = tmem + (uint32_t)(acc * 256) + ((uint32_t)(q * 32) << 16);
+      if (n0 + c_lo < N)
+        drain_accumulator<64>(tbase + (uint32_t)c_lo, m0 + q * 32, M, n0 + c_lo, N, epi,
+                              reinterpret_cast<float *>(smem + Sm::kStgOffset) + (warp - 2) * kStageFloats);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? te1 : te0);
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer is done with this CTA's TMEM and barriers
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, TCOLS);
 }
 
 }  // namespace snai

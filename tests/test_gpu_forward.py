@@ -142,6 +142,30 @@ def test_batched_teacher_forced(prec, small_model, built):
     e.close()
 
 
+@pytest.mark.parametrize("prec", [PREC_TF32, PREC_BF16])
+def test_pair_tiles_prefill_and_decode(prec, model_dir, built):
+    """Shapes for the CTA-pair tensor-core GEMM: 300 sequences (a partial
+    256-row pair tile), d=256 (N=768/256/1024 projections, K=256/1024) and
+    V=3000 (a partial 256-wide logits tile), prompt rows 2400, then
+    teacher-forced decode steps of 300 rows that also take the logits GEMM."""
+    path = make_model(model_dir, "pair.snai", 3000, 256, 32, 2, seed=21)
+    B, plen, steps = 300, 8, 2
+    rng = np.random.default_rng(11 + prec)
+    prompts = rng.integers(0, 3000, (B, plen)).astype(np.int32)
+    forced = rng.integers(0, 3000, (B, steps)).astype(np.int32)
+    e = Cortex(path, num_heads=4, max_seqs=B, precision=prec)
+    got = [e.forward(prompts)]
+    for s in range(steps):
+        got.append(e.forward(forced[:, s:s + 1]))
+    o = O.Oracle(path, num_heads=4)
+    _, ref, _ = o.generate(prompts, steps, np.zeros((B, steps), np.float32), VARIANT_A, 0.8, 1.15,
+                           forced=forced, want_logits=True)
+    for s in range(steps + 1):
+        err = max(rel_err(got[s][b], ref[b, s]) for b in range(B))
+        assert err < TOL[prec], (s, err)
+    e.close()
+
+
 @pytest.mark.parametrize("prec", [PREC_FP32, PREC_BF16])
 def test_single_sequence_long_prompt(prec, small_model, built):
     """A 90-token prompt of one sequence: 90 rows in one pass (tensor cores in
