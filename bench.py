@@ -291,11 +291,14 @@ def our_arm(args, rank, world, local_rank):
         peak, peak_kind = load_peaks()
         att_n, att_ms, att_bytes, _ = prof["attention"]
         achieved = (att_bytes / att_n) / (att_ms / att_n / 1e3) / 1e9 if att_n else None
+        # DRAM traffic per launch: the ratio of ncu-measured to algorithmic
+        # bytes of a smaller capture (same kernel, traffic proportional to the
+        # KV positions read) times this run's algorithmic bytes per launch
         traffic = None
         tp = os.path.join(ROOT, "profiles", "attention_decode_traffic.json")
-        if os.path.exists(tp):
+        if os.path.exists(tp) and att_n:
             try:
-                traffic = json.load(open(tp)).get("bytes_per_launch")
+                traffic = json.load(open(tp))["traffic_per_algorithmic_byte"] * att_bytes / att_n
             except Exception:
                 traffic = None
         total_prof_ms = sum(v[1] for v in prof.values()) or 1.0
@@ -392,6 +395,55 @@ def sampler_bench(args):
         torch.cuda.empty_cache()
 
 
+def gemm_bench(args):
+    """Projection micro-benchmark: the d=1024 decode step's GEMM shapes (4096
+    rows; qkv N=3072, wo N=1024, up N=4096, down N=1024 with K=4096, logits
+    N=16384) through decode passes of one token per slot, on the benchmark
+    model's weights with a 16-position context (no 68 GB KV cache).  One
+    JSON line per GEMM kind: TFLOP/s from the library's CUDA-event profiler
+    against the measured bf16 peak."""
+    import torch
+    from snai_b200 import PREC_BF16, Cortex, modelgen
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, peak_src = float(json.load(f)["bf16_tflops"]), "measured bf16_tflops"
+    except Exception:
+        peak, peak_src = 1590.0, "fallback"
+    path = os.path.join(tempfile.gettempdir(), f"snai_bench_gemm_d{D}.snai")
+    if not os.path.exists(path) or os.path.getsize(path) != modelgen.expected_size(V, D, 4 * D, L):
+        modelgen.random_model(path, V, D, 16, L, seed=1234, std=0.02)
+    B = args.seqs
+    eng = Cortex(path, num_heads=HEADS, max_seqs=B, precision=PREC_BF16)
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(7)
+
+    def step():
+        if eng.pos(0) >= 15:
+            eng.rewind(0)
+        toks = torch.from_numpy(rng.integers(0, V, B).astype(np.int32)).to(dev)
+        eng.forward_dev(toks, B, 1)
+
+    for _ in range(args.warmup):
+        step()
+    eng.synchronize()
+    eng.profile(True)
+    for _ in range(args.steps):
+        step()
+    eng.synchronize()
+    prof = eng.profile_read()
+    eng.profile(False)
+    for k in ("qkv", "wo", "up", "down", "logits"):
+        n, ms, nbytes, flops = prof[k]
+        if not n:
+            continue
+        tf = flops / (ms / 1e3) / 1e12
+        print(json.dumps({"metric": "projection TFLOP/s", "gemm": k, "value": tf, "unit": "TFLOP/s", "rows": B,
+                          "launches": n, "us_per_launch": 1e3 * ms / n,
+                          "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                                       "frac": tf / peak, "peak_source": peak_src}}), flush=True)
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -400,6 +452,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sampler", action="store_true", help="run the isolated sampling micro-benchmark")
+    ap.add_argument("--gemm", action="store_true", help="run the projection GEMM micro-benchmark")
     ap.add_argument("--seqs", type=int, default=TOTAL_SEQS,
                     help="total sequences (default 4096; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -412,6 +465,10 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return
+    if args.gemm:
+        if rank == 0:
+            gemm_bench(args)
         return
     if args.sampler:
         if rank == 0:
