@@ -327,8 +327,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // both CTAs' shared memory and write a 128 x 256 fp32 accumulator into each
 // CTA's TMEM.  Per SM this moves 32 KB per 64-deep k-block for 128x256x64
 // MACs, two thirds of the 128 x 256 single-CTA tile's bytes: the projections
-// are bound by L2 -> SM bandwidth, not by the tensor cores.  No multicast
-// loads are used.
+// are bound by L2 -> SM bandwidth, not by the tensor cores.  Each CTA loads
+// only its own halves: no load is shared between the two CTAs.
 // ============================================================================
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -372,7 +372,7 @@ __device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_
   }
 }
 // 2-D tiled load into this CTA's shared memory, completing on a barrier of
-// either CTA of the pair (cluster address); no multicast.
+// either CTA of the pair (cluster address); one destination CTA.
 __device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *tmap, uint32_t bar_cluster, int c0,
                                                  int c1) {
   asm volatile(
@@ -391,14 +391,16 @@ __device__ __forceinline__ void tmem_relinquish_pair() {
 __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
-// Arrives on `bar` in both CTAs of the pair once the pair MMAs issued so far are done.
+// Arrives on `bar` in both CTAs of the pair once the pair MMAs issued so far
+// are done: one commit to this CTA's barrier, one to the peer's (by its
+// cluster address).
 __device__ __forceinline__ void tc_commit_pair(uint64_t *bar) {
-  const uint16_t mask = 0x3;
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(mask)
-      : "memory");
+  const uint32_t local = smem_u32(bar);
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(local)
+               : "memory");
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   mapa_shared(local, 1))
+               : "memory");
 }
 
 template <typename TIn>
