@@ -45,6 +45,7 @@ V, D, L, CTX, HEADS = 16384, 1024, 2, 1024, 16
 PROMPT = 512
 TOTAL_SEQS = 4096
 T, TOP_K, TOP_P, REP = 0.7, 40, 0.9, 1.1
+VARIANT = 1  # 0: src/snai_inference.php sampler, 1: src/tensor_ffi_adapter.php sampler
 METRIC = "generated tokens/sec (d=1024 decode)"
 UNIT = "tokens/s"
 CONFIG = {
@@ -61,6 +62,29 @@ CONFIG = {
 }
 
 
+# Smaller configurations of the same metric (--config); the default run is c4.
+CONFIGS = {
+    "c2": dict(D=256, L=4, HEADS=4, PROMPT=256, TOTAL_SEQS=64, VARIANT=0, T=0.8, REP=1.15,
+               workload="d=256 L=4 heads=4 V=16384 ctx=1024, 64 sequences, prompt 256 + decode, "
+                        "variant-A sampling T 0.8 / rep 1.15"),
+    "c3": dict(D=512, L=2, HEADS=8, PROMPT=512, TOTAL_SEQS=512, VARIANT=1, T=0.7, REP=1.1,
+               workload="d=512 L=2 heads=8 V=16384 ctx=1024, 512 sequences, prompt 512 + decode to 1024, "
+                        "top-k 40 / top-p 0.9 / T 0.7 / rep 1.1 sampling"),
+}
+
+
+def apply_config(name):
+    global D, L, HEADS, PROMPT, TOTAL_SEQS, VARIANT, T, REP, METRIC
+    c = CONFIGS[name]
+    D, L, HEADS, PROMPT, TOTAL_SEQS = c["D"], c["L"], c["HEADS"], c["PROMPT"], c["TOTAL_SEQS"]
+    VARIANT, T, REP = c["VARIANT"], c["T"], c["REP"]
+    METRIC = f"generated tokens/sec (d={D} decode)"
+    kv = TOTAL_SEQS * L * 2 * CTX * D * 4 / 1e9
+    CONFIG.update(workload=c["workload"], model=f"seeded SNAI_V4 d{D} L{L} (init_base layout, N(0,0.02))",
+                  global_batch=TOTAL_SEQS, prompt=PROMPT,
+                  l2=f"KV cache {kv:.1f} GB; weights may stay L2-resident (measured as is, no flush)")
+
+
 def load_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -72,7 +96,7 @@ def load_peaks():
 
 def model_path(rank):
     d = os.environ.get("SNAI_BENCH_DIR", tempfile.gettempdir())
-    return os.path.join(d, f"snai_bench_d1024_seed1234_r{rank}.snai")
+    return os.path.join(d, f"snai_bench_d{D}_L{L}_seed1234_r{rank}.snai")
 
 
 def make_model(rank):
@@ -155,10 +179,10 @@ def cpu_sample(steps_timed, nthreads, start_pos=768, nseq=None, warmup=1):
     nseq = nseq or nthreads
     b = o.batch(nseq, start_pos, seed=99)
     for _ in range(warmup):
-        b.step(1, T, REP, TOP_K, TOP_P, nthreads)
+        b.step(VARIANT, T, REP, TOP_K, TOP_P, nthreads)
     secs = 0.0
     for _ in range(steps_timed):
-        secs += b.step(1, T, REP, TOP_K, TOP_P, nthreads)
+        secs += b.step(VARIANT, T, REP, TOP_K, TOP_P, nthreads)
     b.close()
     o.close()
     return nseq * steps_timed / secs, secs, nseq
@@ -187,7 +211,7 @@ def our_arm(args, rank, world, local_rank):
     TOTAL_SEQS = args.seqs
     import torch
     import torch.distributed as dist
-    from snai_b200 import PREC_BF16, Cortex, VARIANT_B, sample_params
+    from snai_b200 import PREC_BF16, Cortex, sample_params
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -224,7 +248,7 @@ def our_arm(args, rank, world, local_rank):
     eng.synchronize()
     prefill_s = max_over_ranks(time.perf_counter() - t0)
 
-    prm = sample_params(VARIANT_B, T, REP, TOP_K, TOP_P)
+    prm = sample_params(VARIANT, T, REP, TOP_K, TOP_P)
     total_steps = args.warmup + args.steps
     U = torch.from_numpy(rng.random((total_steps, B), dtype=np.float32)).to(dev)
     ids = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -234,6 +258,19 @@ def our_arm(args, rank, world, local_rank):
             eng.rewind(PROMPT)
         eng.decode_dev(U[i], prm, ids)
 
+    ids_all = torch.zeros((args.steps, B), dtype=torch.int32, device=dev)
+
+    def steps_dev(i0, n):
+        # n decode steps in one call (cortex_decode_steps: one captured step
+        # replayed as a CUDA graph), rewinding at the context limit
+        while n > 0:
+            if eng.pos(0) >= CTX:
+                eng.rewind(PROMPT)
+            k = min(n, CTX - eng.pos(0))
+            eng.decode_steps_dev(U[i0:i0 + k], prm, ids_all[:k])
+            i0 += k
+            n -= k
+
     # ---- device-resident decode (value) ----
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
@@ -242,24 +279,40 @@ def our_arm(args, rank, world, local_rank):
     barrier()
     torch.cuda.synchronize()
     launches0 = eng.launches
-    eng.profile(True)
+    # The library's CUDA-event profiler brackets every launch with events.  At
+    # d=1024 (8 ms steps, the GPU never waits for the host) it runs inside the
+    # timed region; the small configurations are host-launch-bound, so there
+    # it runs in a separate pass after the timed region.
+    prof_in_timed = args.config == "c4"
+    if prof_in_timed:
+        eng.profile(True)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(visible_gpu_ids(world) if rank == 0 else []) as clk:
         with torch.cuda.stream(stream):
             torch.cuda.nvtx.range_push("timed")
             ev0.record(stream)
-            for i in range(args.steps):
-                step_dev(args.warmup + i)
+            if prof_in_timed:
+                for i in range(args.steps):  # the profiler needs the per-step path
+                    step_dev(args.warmup + i)
+            else:
+                steps_dev(args.warmup, args.steps)
             ev1.record(stream)
             torch.cuda.nvtx.range_pop()
         ev1.synchronize()
         torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
-    prof = eng.profile_read()
-    eng.profile(False)
     launches = eng.launches - launches0
     barrier()
     ms_max = max_over_ranks(ms)
+
+    if not prof_in_timed:
+        eng.profile(True)
+        with torch.cuda.stream(stream):
+            for i in range(min(args.steps, 64)):
+                step_dev(args.warmup + i)
+        eng.synchronize()
+    prof = eng.profile_read()
+    eng.profile(False)
 
     # ---- end to end through the host-pointer C ABI (e2e) ----
     eng.rewind(PROMPT)
@@ -267,9 +320,11 @@ def our_arm(args, rank, world, local_rank):
     out_ids = np.zeros(B, dtype=np.int32)
 
     def step_host(i):
+        # one call per step from host memory (uniforms in, ids out), through
+        # the graph-replayed decode
         if eng.pos(0) >= CTX:
             eng.rewind(PROMPT)
-        out_ids[:] = eng.decode(Uh[i], prm)
+        out_ids[:] = eng.decode_steps(Uh[i:i + 1], prm)[0]
 
     for i in range(args.warmup):
         step_host(i)
@@ -311,8 +366,8 @@ def our_arm(args, rank, world, local_rank):
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded model, random prompt ids)",
             "config": dict(CONFIG, parallelism=f"sequences sharded over {world} GPU(s)"),
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 24 * B, "d2h_bytes_per_step": 4 * B,
-                    "api": "cortex_decode_batch(SNAI_HOST_PTRS)"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B,
+                    "api": "cortex_decode_steps(steps=1, SNAI_HOST_PTRS) per step"},
             "gpu_launches": int(launches),
             "roofline": {"kernel": "attention (decode, fp32 KV)", "bound": "hbm",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -447,7 +502,9 @@ def gemm_bench(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=509)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default: ctx - prompt - 3)")
+    ap.add_argument("--config", choices=["c4", "c2", "c3"], default="c4",
+                    help="c4 (default): the headline d=1024 workload; c2 / c3: the smaller configurations")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -456,6 +513,12 @@ def main():
     ap.add_argument("--seqs", type=int, default=TOTAL_SEQS,
                     help="total sequences (default 4096; smaller only for profiling captures)")
     args = ap.parse_args()
+    if args.config != "c4":
+        apply_config(args.config)
+        if args.seqs == 4096:
+            args.seqs = TOTAL_SEQS
+    if args.steps is None:
+        args.steps = CTX - PROMPT - 3
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))

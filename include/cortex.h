@@ -167,6 +167,17 @@ CORTEX_API int cortex_forward_batch(void *state, const int *tokens, int batch, i
 CORTEX_API int cortex_decode_batch(void *state, const int *slots, int batch, const float *uniforms,
                         const snai_sample_params *params, int *out_ids, int flags);
 
+/* `steps` consecutive cortex_decode_batch steps: step k uses uniforms[k][b]
+ * and writes out_ids[k][b] (both [steps][batch]).  One step is captured once
+ * as a CUDA graph whose rows, uniforms and ids live on the device, and
+ * replayed: a launch-bound small batch pays one graph launch per step.  The
+ * result equals `steps` calls of cortex_decode_batch.  Falls back to those
+ * calls while the profiler is on or when a slot would reach the context
+ * limit within the steps.  No reference counterpart (the PHP host samples one
+ * token per FFI call). */
+CORTEX_API int cortex_decode_steps(void *state, const int *slots, int batch, int steps, const float *uniforms,
+                                   const snai_sample_params *params, int *out_ids, int flags);
+
 /* Copies the current device logits of the given slots to host memory
  * out[n][vocab]. */
 CORTEX_API int cortex_get_logits(void *state, const int *slots, int n, float *out);

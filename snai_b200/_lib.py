@@ -61,6 +61,8 @@ SIGNATURES = {
     "cortex_forward_batch": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int]),
     "cortex_decode_batch": (c_int, [c_void_p, c_void_p, c_int, c_void_p, ctypes.POINTER(SampleParams),
                                     c_void_p, c_int]),
+    "cortex_decode_steps": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, ctypes.POINTER(SampleParams),
+                                    c_void_p, c_int]),
     "cortex_get_logits": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     "cortex_sample": (c_int, [c_void_p, c_int, c_int, ctypes.c_longlong, c_void_p, c_int, c_void_p, c_void_p,
                               ctypes.POINTER(SampleParams), c_void_p, c_void_p]),

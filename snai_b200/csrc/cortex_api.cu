@@ -115,6 +115,9 @@ void free_engine(Engine *e) {
   cudaFree(e->hblock);
   cudaFree(e->kv);
   cudaFree(e->ablock);
+  if (e->graph.exec) cudaGraphExecDestroy(e->graph.exec);
+  cudaFree(e->unif_all);
+  cudaFree(e->ids_all);
   if (e->own_stream) cudaStreamDestroy(e->own_stream);
   delete e;
 }
@@ -192,6 +195,7 @@ Engine *create_engine(const Dims &d, int max_seqs, int device, int precision) {
   a.add(&e->slots_d, (size_t)max_seqs);
   a.add(&e->rope, (size_t)d.ctx * (d.hs / 2));
   a.add(&e->err_d, 4);
+  a.add(&e->step_d, 4);
 
   e->kv_head_stride = (size_t)d.ctx * d.hs;
   e->kv_part_stride = e->kv_head_stride * d.heads;
@@ -778,6 +782,157 @@ extern "C" int cortex_decode_batch(void *state, const int *slots, int batch, con
   if (rc) return rc;
   for (const RowDesc &r : rows) e.pos[r.slot] += 1;
   if (cudaMemcpyAsync(out_ids, e.ids_d, sizeof(int) * batch, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                      e.stream) != cudaSuccess) {
+    set_error("id copy failed");
+    return -4;
+  }
+  return finish(e, !dev);
+}
+
+// `steps` decode steps of `batch` slots: step k samples with uniforms[k] and
+// writes out_ids[k] (both [steps, batch]).  One step is captured as a CUDA
+// graph (the rows, uniforms and ids live on the device, indexed by a device
+// step counter) and replayed, so a step costs one graph launch instead of
+// one host launch per kernel.  Falls back to cortex_decode_batch per step
+// when the profiler is on or a slot would reach the context limit.
+extern "C" int cortex_decode_steps(void *state, const int *slots, int batch, int steps, const float *uniforms,
+                                   const snai_sample_params *params, int *out_ids, int flags) {
+  clear_error();
+  if (!state || !params || !out_ids) {
+    set_error("state, params and out_ids must not be NULL");
+    return -1;
+  }
+  Engine &e = *static_cast<Engine *>(state);
+  if (batch < 0 || batch > e.max_seqs || steps < 0) {
+    set_error("batch %d outside [0, %d] or negative steps %d", batch, e.max_seqs, steps);
+    return -2;
+  }
+  if (batch == 0 || steps == 0) return 0;
+  if (!uniforms && params->temperature > 0.01) {
+    set_error("uniforms must not be NULL for a sampling temperature");
+    return -2;
+  }
+  if (!slots_ok(e, slots, batch)) return -2;
+  const bool dev = flags & SNAI_DEVICE_PTRS;
+  std::vector<int> sl(batch);
+  bool graph_ok = !e.prof;
+  for (int b = 0; b < batch; ++b) {
+    sl[b] = slots ? slots[b] : b;
+    if (!e.logits_valid[sl[b]]) {
+      set_error("slot %d has no logits yet (feed its prompt first)", sl[b]);
+      return -2;
+    }
+    if (e.pos[sl[b]] + steps > e.d.ctx) graph_ok = false;
+  }
+  if (!graph_ok) {
+    for (int k = 0; k < steps; ++k) {
+      const int rc = cortex_decode_batch(state, slots, batch, uniforms ? uniforms + (size_t)k * batch : nullptr,
+                                         params, out_ids + (size_t)k * batch, flags);
+      if (rc) return rc;
+    }
+    return 0;
+  }
+  DeviceGuard g(e.device);
+  const size_t need = (size_t)steps * batch;
+  if (need > e.all_cap) {
+    cudaFree(e.unif_all);
+    cudaFree(e.ids_all);
+    e.unif_all = nullptr;
+    e.ids_all = nullptr;
+    e.all_cap = 0;
+    if (cudaMalloc(&e.unif_all, need * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&e.ids_all, need * sizeof(int)) != cudaSuccess) {
+      set_error("out of device memory for %zu staged uniforms", need);
+      return -3;
+    }
+    e.all_cap = need;
+  }
+  const cudaMemcpyKind in = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  if (cudaMemcpyAsync(e.slots_d, sl.data(), sizeof(int) * batch, cudaMemcpyHostToDevice, e.stream) != cudaSuccess ||
+      (uniforms && cudaMemcpyAsync(e.unif_all, uniforms, sizeof(float) * need, in, e.stream) != cudaSuccess) ||
+      (!uniforms && cudaMemsetAsync(e.unif_all, 0, sizeof(float) * need, e.stream) != cudaSuccess) ||
+      cudaMemsetAsync(e.step_d, 0, sizeof(int), e.stream) != cudaSuccess) {
+    set_error("decode-steps upload failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return -4;
+  }
+  SampleLaunch s;
+  s.logits = e.logits;
+  s.ld = e.d.V;
+  s.row_map = e.slots_d;
+  s.rows = batch;
+  s.V = e.d.V;
+  s.hist = e.hist;
+  s.hist_ld = e.d.ctx;
+  s.hist_cols = e.d.ctx;
+  s.hist_len = e.seq_len_d;
+  s.uniforms = e.unif_d;
+  s.variant = params->variant;
+  s.temperature = params->temperature;
+  s.rep = params->rep_penalty;
+  s.top_k = params->top_k;
+  s.top_p = params->top_p;
+  s.nan_guard = params->nan_guard;
+  s.out_ids = e.ids_d;
+  s.err = e.err_d;
+  int rc = check_sample_args(s);
+  if (rc) return rc;
+  Engine::DecodeGraph &gr = e.graph;
+  const bool same = gr.exec && gr.batch == batch && gr.variant == s.variant && gr.temperature == s.temperature &&
+                    gr.rep == s.rep && gr.top_k == s.top_k && gr.top_p == s.top_p &&
+                    gr.nan_guard == s.nan_guard && gr.unif == e.unif_all && gr.ids == e.ids_all;
+  int k0 = 0;
+  if (!same) {
+    // first step eagerly (sets every kernel's attributes outside a capture),
+    // then capture one step for this and later calls
+    if (gr.exec) cudaGraphExecDestroy(gr.exec);
+    gr.exec = nullptr;
+    rc = decode_step_device(e, batch, s);
+    if (rc) return rc;
+    k0 = 1;
+    {
+      const long long l0 = e.launches;
+      if (cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        set_error("stream capture failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return -4;
+      }
+      rc = decode_step_device(e, batch, s);
+      cudaGraph_t graph = nullptr;
+      const cudaError_t ce = cudaStreamEndCapture(e.stream, &graph);
+      gr.kernels = e.launches - l0;
+      e.launches = l0;  // captured, not launched
+      if (rc || ce != cudaSuccess || !graph) {
+        if (graph) cudaGraphDestroy(graph);
+        if (!rc) set_error("stream capture failed: %s", cudaGetErrorString(ce));
+        return rc ? rc : -4;
+      }
+      const cudaError_t ie = cudaGraphInstantiate(&gr.exec, graph, 0);
+      cudaGraphDestroy(graph);
+      if (ie != cudaSuccess) {
+        gr.exec = nullptr;
+        set_error("graph instantiation failed: %s", cudaGetErrorString(ie));
+        return -4;
+      }
+      gr.batch = batch;
+      gr.variant = s.variant;
+      gr.temperature = s.temperature;
+      gr.rep = s.rep;
+      gr.top_k = s.top_k;
+      gr.top_p = s.top_p;
+      gr.nan_guard = s.nan_guard;
+      gr.unif = e.unif_all;
+      gr.ids = e.ids_all;
+    }
+  }
+  const long long per_step = gr.kernels;
+  for (int k = k0; k < steps; ++k) {
+    if (cudaGraphLaunch(gr.exec, e.stream) != cudaSuccess) {
+      set_error("graph launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+      return -4;
+    }
+    e.launches += per_step;
+  }
+  for (int b = 0; b < batch; ++b) e.pos[sl[b]] += steps;
+  if (cudaMemcpyAsync(out_ids, e.ids_all, sizeof(int) * need, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
                       e.stream) != cudaSuccess) {
     set_error("id copy failed");
     return -4;

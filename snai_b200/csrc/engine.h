@@ -83,6 +83,22 @@ struct Engine {
   int *slots_d = nullptr;     // [max_seqs]
   int *err_d = nullptr;       // device error word
 
+  // decode-step graph (cortex_decode_steps): one captured decode step of
+  // `batch` slots, replayed per step; a device step counter indexes the
+  // per-step uniforms and ids
+  struct DecodeGraph {
+    cudaGraphExec_t exec = nullptr;
+    int batch = 0, variant = 0, top_k = 0, nan_guard = 0;
+    long long kernels = 0;        // kernels in one replay
+    double temperature = 0, rep = 0, top_p = 0;
+    const float *unif = nullptr;  // [steps, batch] read through *step_d
+    int *ids = nullptr;           // [steps, batch] written through *step_d
+  } graph;
+  int *step_d = nullptr;          // device step counter of a graph replay
+  float *unif_all = nullptr;      // [cap, ...] per-step uniforms staged for a replay
+  int *ids_all = nullptr;         // [cap, ...] per-step ids of a replay
+  size_t all_cap = 0;             // elements of unif_all / ids_all
+
   // host staging of a chunk's rows.  Pageable on purpose: cudaMemcpyAsync
   // from pageable memory returns once the source has been consumed, so the
   // buffers can be refilled by the next call without waiting for the GPU.
@@ -129,6 +145,7 @@ void clear_error();
 // chunks of at most e.m_max rows.  If tokens_d is not null, row tokens are
 // tokens_d[row.token].  Returns 0 or a negative error.
 int run_rows(Engine &e, const RowDesc *rows, int n, const int *tokens_d);
+
 // fp32 -> bf16 copy of a weight tensor on e.stream.
 int convert_bf16(Engine &e, const float *src, __nv_bfloat16 *dst, size_t n);
 // Fills n floats with a value on e.stream.
@@ -154,6 +171,12 @@ struct SampleLaunch {
 };
 // Checks the arguments; returns 0 or a negative error (with set_error).
 int check_sample_args(const SampleLaunch &a);
+// One decode step of `batch` slots with everything on the device (the body of
+// a graph): per-step uniforms from unif_all[*step_d], the sampler, the rows
+// built from seq_len_d, the forward pass with tokens ids_d, ids copied to
+// ids_all[*step_d] and the counter advanced.  No host synchronization, no
+// host-to-device copies.  Returns 0 or a negative error.
+int decode_step_device(Engine &e, int batch, const SampleLaunch &sampler);
 int launch_sampler(const SampleLaunch &a, cudaStream_t stream);
 
 }  // namespace snai

@@ -585,6 +585,60 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
   return 0;
 }
 
+// ---- decode step on the device (graph body) ----
+
+// Per-step uniforms of the current step into the sampler's buffer.
+__global__ void stage_step_kernel(const float *__restrict__ unif_all, float *__restrict__ unif,
+                                  const int *__restrict__ step, int batch) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < batch) unif[b] = unif_all[(size_t)(*step) * batch + b];
+}
+
+// Row descriptors of a decode step: slot, its current position, token index b
+// (ids_d[b]), logits into the slot; the logits row map (row b, slot).
+__global__ void decode_rows_kernel(const int *__restrict__ slots, const int *__restrict__ seq_len,
+                                   RowDesc *__restrict__ rows, int2 *__restrict__ outrows, int batch) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < batch) {
+    const int s = slots[b];
+    rows[b] = RowDesc{s, seq_len[s], b, s};
+    outrows[b] = make_int2(b, s);
+  }
+}
+
+// The step's ids out, then the counter advances (one thread does the
+// increment after every thread of its block has read the counter).
+__global__ void finish_step_kernel(const int *__restrict__ ids, int *__restrict__ ids_all, int *__restrict__ step,
+                                   int batch) {
+  const int st = *step;
+  for (int b = threadIdx.x; b < batch; b += blockDim.x) ids_all[(size_t)st * batch + b] = ids[b];
+  __syncthreads();
+  if (threadIdx.x == 0) *step = st + 1;
+}
+
+int decode_step_device(Engine &e, int batch, const SampleLaunch &sampler) {
+  const int tpb = 256, nb = (batch + tpb - 1) / tpb;
+  stage_step_kernel<<<nb, tpb, 0, e.stream>>>(e.unif_all, e.unif_d, e.step_d, batch);
+  e.launches++;
+  int rc = launch_sampler(sampler, e.stream);
+  if (rc) return rc;
+  e.launches++;
+  decode_rows_kernel<<<nb, tpb, 0, e.stream>>>(e.slots_d, e.seq_len_d, e.rows_d, e.outrows_d, batch);
+  e.launches++;
+  const bool tc = tc_path(e, batch);
+  rc = (tc && e.precision == kBF16) ? run_chunk_typed<__nv_bfloat16>(e, batch, e.ids_d, batch, tc, 0.0, true)
+                                    : run_chunk_typed<float>(e, batch, e.ids_d, batch, tc, 0.0, true);
+  if (rc) return rc;
+  finish_step_kernel<<<1, 1024, 0, e.stream>>>(e.ids_d, e.ids_all, e.step_d, batch);
+  e.launches++;
+  const cudaError_t le = cudaGetLastError();
+  if (le != cudaSuccess) {
+    set_error("kernel launch failed: %s", cudaGetErrorString(le));
+    return -4;
+  }
+  return 0;
+}
+
 int run_rows(Engine &e, const RowDesc *rows, int n, const int *tokens_d) {
   for (int c0 = 0; c0 < n; c0 += e.m_max) {
     const int M = std::min(e.m_max, n - c0);

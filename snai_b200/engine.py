@@ -97,6 +97,28 @@ class Cortex:
               "cortex_decode_batch")
         return ids
 
+    def decode_steps(self, uniforms, params, slots=None):
+        """len(uniforms) sample+feed steps for each slot through the graph-
+        replayed decode (uniforms [steps, B]); returns the ids [steps, B]."""
+        u = np.ascontiguousarray(uniforms, dtype=np.float32)
+        steps, B = u.shape
+        sl = None if slots is None else np.ascontiguousarray(slots, dtype=np.int32)
+        ids = np.zeros((steps, B), dtype=np.int32)
+        check(self.lib.cortex_decode_steps(self.h, None if sl is None else _ptr(sl), B, steps, _ptr(u),
+                                           ctypes.byref(params), _ptr(ids), _lib.HOST_PTRS),
+              "cortex_decode_steps")
+        return ids
+
+    def decode_steps_dev(self, uniforms_dev, params, ids_dev, slots=None):
+        """Device-pointer decode_steps: uniforms_dev [steps, B] float32,
+        ids_dev [steps, B] int32 (torch tensors)."""
+        steps, B = uniforms_dev.shape
+        sl = None if slots is None else np.ascontiguousarray(slots, dtype=np.int32)
+        check(self.lib.cortex_decode_steps(self.h, None if sl is None else _ptr(sl), B, steps,
+                                           ctypes.c_void_p(uniforms_dev.data_ptr()), ctypes.byref(params),
+                                           ctypes.c_void_p(ids_dev.data_ptr()), _lib.DEVICE_PTRS),
+              "cortex_decode_steps")
+
     def logits(self, slots):
         s = np.ascontiguousarray(slots, dtype=np.int32)
         out = np.zeros((len(s), self.vocab), dtype=np.float32)

@@ -208,6 +208,46 @@ def test_decode_batch_ids_exact(variant, prec, small_model, built):
     e.close()
 
 
+@pytest.mark.parametrize("variant", [VARIANT_A, VARIANT_B])
+@pytest.mark.parametrize("prec", [PREC_FP32, PREC_BF16])
+def test_decode_steps_graph_equals_decode_batch(variant, prec, small_model, built):
+    """cortex_decode_steps (one captured step replayed as a CUDA graph) gives
+    the ids and final logits of the same number of cortex_decode_batch calls,
+    for a slot subset in a permuted order, host and device pointers, a second
+    call that reuses the graph, and the context-limit fallback."""
+    B, plen = 70, 10
+    rng = np.random.default_rng(30 + variant + 2 * prec)
+    prompts = rng.integers(0, 1000, (B, plen)).astype(np.int32)
+    prm = sample_params(VARIANT_A, 0.8, 1.15) if variant == VARIANT_A else sample_params(VARIANT_B, 0.7, 1.1, 40, 0.9)
+    slots = rng.permutation(B)[:67].astype(np.int32)
+    a = Cortex(small_model, num_heads=2, max_seqs=B, precision=prec)
+    g = Cortex(small_model, num_heads=2, max_seqs=B, precision=prec)
+    a.forward(prompts, want_logits=False)
+    g.forward(prompts, want_logits=False)
+    for call, steps in enumerate((9, 6)):
+        U = rng.random((steps, len(slots))).astype(np.float32)
+        want = np.stack([a.decode(U[k], prm, slots=slots) for k in range(steps)])
+        if call == 0:
+            got = g.decode_steps(U, prm, slots=slots)
+        else:
+            ud = torch.from_numpy(U).cuda()
+            idd = torch.zeros((steps, len(slots)), dtype=torch.int32, device="cuda")
+            g.decode_steps_dev(ud, prm, idd, slots=slots)
+            g.synchronize()
+            got = idd.cpu().numpy()
+        assert np.array_equal(got, want), call
+        assert np.array_equal(g.logits(slots), a.logits(slots))
+        assert [g.pos(int(s)) for s in slots] == [a.pos(int(s)) for s in slots]
+    # past the context (96): the per-step fallback, same results
+    steps = 96 - plen - 15 + 4
+    U = rng.random((steps, len(slots))).astype(np.float32)
+    want = np.stack([a.decode(U[k], prm, slots=slots) for k in range(steps)])
+    got = g.decode_steps(U, prm, slots=slots)
+    assert np.array_equal(got, want)
+    a.close()
+    g.close()
+
+
 def test_decode_matches_oracle_trajectory(small_model, built):
     """Full generation (FP32): ids of GPU and oracle agree step by step while
     their logits agree to fp32 tolerance (a flip needs a near-tie)."""
