@@ -921,6 +921,7 @@ __device__ void rank_candidates(SmemB &sm, int nc, int k) {
     const unsigned long long ki = sm.ckey[i];
     const int vi = sm.cidx[i];
     int rank = 0;
+#pragma unroll 8
     for (int j = 0; j < nc; ++j) rank += precedes(sm.ckey[j], sm.cidx[j], ki, vi) ? 1 : 0;
     if (rank < k) {
       sm.order[rank] = vi;
@@ -1389,14 +1390,16 @@ __device__ __forceinline__ void pipe_reset(RowPipe &p, int par) {
   p.s2[par] = 0.f;
 }
 
-// Marks the history ids in h (each thread's share, -1 for none) in a
-// cleared bitmap; with a list, the thread whose atomicOr set a bit also
-// appends the id to plist (warp-aggregated slots, count in *npen).
-__device__ __forceinline__ void mark_ids(int V, const int (&h)[kHistRegs], uint32_t *bits, int *plist, int *npen) {
+// Marks the history ids in h (each thread's share, -1 for none) that fall in
+// [lo, lo + V) in a cleared bitmap of that range; with a list, the thread
+// whose atomicOr set a bit also appends the (range-local) id to plist
+// (warp-aggregated slots, count in *npen).
+__device__ __forceinline__ void mark_ids(int V, const int (&h)[kHistRegs], uint32_t *bits, int *plist, int *npen,
+                                         int lo = 0) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int r = 0; r < kHistRegs; ++r) {
-    const int t = h[r];
+    const int t = h[r] - lo;
     bool first = false;
     if (t >= 0 && t < V) {
       const uint32_t bit = 1u << (t & 31);
@@ -1415,8 +1418,15 @@ __device__ __forceinline__ void mark_ids(int V, const int (&h)[kHistRegs], uint3
 
 // Kernel start: clears the three bitmaps and both counter sets, builds the
 // bitmap of the CTA's first row and starts its staging.
+// (rows b0, b0 + stride, ...: one CTA per row by default; a CTA of a
+// cluster handles the ids [lo, lo + a.V) of its cluster's rows)
 __device__ __forceinline__ void pipe_start(const SampArgs &a, RowPipe &p, uint32_t *bm, int words, RowFeeder &feed,
-                                           int (&hreg)[kHistRegs], int *plist0) {
+                                           int (&hreg)[kHistRegs], int *plist0, int lo = 0, int b0 = -1,
+                                           int stride = 0) {
+  if (b0 < 0) {
+    b0 = blockIdx.x;
+    stride = gridDim.x;
+  }
   if (threadIdx.x == 0) {
     mbar_init(&p.bar, 1);
     fence_barrier_init();
@@ -1425,13 +1435,12 @@ __device__ __forceinline__ void pipe_start(const SampArgs &a, RowPipe &p, uint32
   }
   for (int i = threadIdx.x; i < 3 * words; i += kSampThreads) bm[i] = 0u;
   __syncthreads();
-  const int b0 = blockIdx.x;
   if (b0 < a.rows) {
     const int r0 = row_of(a, b0);
     if (threadIdx.x == 0) feed.issue(a, r0);
     load_hist_regs(a, r0, hreg);
-    mark_ids(a.V, hreg, bm, plist0, &p.npen[0]);
-    const int b1 = b0 + (int)gridDim.x;
+    mark_ids(a.V, hreg, bm, plist0, &p.npen[0], lo);
+    const int b1 = b0 + stride;
     if (b1 < a.rows) load_hist_regs(a, row_of(a, b1), hreg);
   }
   __syncthreads();
@@ -1443,8 +1452,10 @@ __device__ __forceinline__ void pipe_start(const SampArgs &a, RowPipe &p, uint32
 // list count were reset at the start of row it: pipe_reset) and load row
 // it + 2's.
 __device__ __forceinline__ void pipe_advance(const SampArgs &a, RowPipe &p, uint32_t *bm, int words, int it, int b,
-                                             RowFeeder &feed, int (&hreg)[kHistRegs], int *plist_next) {
-  const int nb = b + (int)gridDim.x;
+                                             RowFeeder &feed, int (&hreg)[kHistRegs], int *plist_next, int lo = 0,
+                                             int stride = 0) {
+  if (stride == 0) stride = gridDim.x;
+  const int nb = b + stride;
   if (nb < a.rows && threadIdx.x == 0) {
     // the stage was written through the generic proxy (settled entries)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1453,8 +1464,8 @@ __device__ __forceinline__ void pipe_advance(const SampArgs &a, RowPipe &p, uint
   uint32_t *clr = bm + ((it + 2) % 3) * words;
   for (int i = threadIdx.x; i < words; i += kSampThreads) clr[i] = 0u;
   if (nb < a.rows) {
-    mark_ids(a.V, hreg, bm + ((it + 1) % 3) * words, plist_next, &p.npen[(it + 1) & 1]);
-    const int nnb = nb + (int)gridDim.x;
+    mark_ids(a.V, hreg, bm + ((it + 1) % 3) * words, plist_next, &p.npen[(it + 1) & 1], lo);
+    const int nnb = nb + stride;
     if (nnb < a.rows) load_hist_regs(a, row_of(a, nnb), hreg);
   }
 }
@@ -2012,6 +2023,693 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
 }
 
 // ---------------------------------------------------------------------------
+// Cluster kernels: rows longer than one CTA's register row.  A cluster of C
+// CTAs (C = ceil(V / 32768), at most 8) takes a row; CTA r holds the ids
+// [32768 r, 32768 (r + 1)) in registers through the same staged-row
+// pipeline, and the row's decisions combine the CTAs' partial results
+// through distributed shared memory (each CTA publishes into its own
+// exchange area, a cluster barrier, then every CTA reads all C entries in
+// rank order, so every CTA derives the same values).
+// ---------------------------------------------------------------------------
+
+constexpr int kSliceLen = kSegLen * kRegLayers;  // ids per CTA of a cluster row
+constexpr int kMaxCluster = 8;
+
+struct XchgA {
+  unsigned int xkey;         // maximum of the slice's unpenalised raw logits (okey32)
+  float l0;                  // raw logit 0 (rank 0)
+  unsigned long long pkey;   // argmax key of the slice's penalised values (global ids)
+  unsigned long long ekey;   // exact-maximum key (rare path)
+  int cand;                  // first global id attaining M in the slice
+  int verdict;               // rank 0: the draw's id or -1
+  double seg[kRegLayers];    // the slice's layer totals of the current draw
+};
+
+__device__ __forceinline__ uint32_t xc_addr(const void *field, uint32_t rank) { return mapa_shared(smem_u32(field), rank); }
+
+// The sequential algorithm of src/snai_inference.php:178-194 over a cluster
+// row, by warp 0 of one CTA; the penalty set is read from the owning CTA's
+// bitmap (bits_u32: this CTA's shared address of the row's bitmap, the same
+// offset in every CTA).
+__device__ __noinline__ int sequential_a_cluster(const SampArgs &a, uint32_t bits_u32, const float *L, double maxv,
+                                                 double u) {
+  const int lane = threadIdx.x & 31;
+  auto pvalue = [&](int v, uint32_t w) -> double {
+    const float t = div_to_f32(L[v], a.T, a.Tinv);
+    const float tt = ((w >> (v & 31)) & 1u) ? penalise_a(t, a.rep, a.repinv) : t;
+    return snai_exp(__dsub_rn((double)tt, maxv));
+  };
+  double sum = 0.0;
+  for (int b = 0; b < a.V; b += 32) {
+    const int v = b + lane;
+    const uint32_t w = ld_cluster_u32(mapa_shared(bits_u32 + (uint32_t)((b % kSliceLen) >> 5) * 4u, b / kSliceLen));
+    const double p = v < a.V ? pvalue(v, w) : 0.0;
+    const int cnt = min(32, a.V - b);
+    for (int j = 0; j < cnt; ++j) sum = __dadd_rn(sum, __shfl_sync(0xffffffffu, p, j));
+  }
+  const double r = __dmul_rn(u, sum);
+  double cum = 0.0;
+  for (int b = 0; b < a.V; b += 32) {
+    const int v = b + lane;
+    const uint32_t w = ld_cluster_u32(mapa_shared(bits_u32 + (uint32_t)((b % kSliceLen) >> 5) * 4u, b / kSliceLen));
+    const double p = v < a.V ? pvalue(v, w) : 0.0;
+    const int cnt = min(32, a.V - b);
+    for (int j = 0; j < cnt; ++j) {
+      cum = __dadd_rn(cum, __shfl_sync(0xffffffffu, p, j));
+      if (cum >= r) return b + j;
+    }
+  }
+  return 0;
+}
+
+// Certified draw over a cluster row (tiers 1 and 2 of variant A): the
+// per-CTA part of draw_reg, the layer totals of all CTAs scanned in id order
+// by every CTA, the crossing layer scanned and certified by its CTA, whose
+// verdict reaches every CTA through rank 0's exchange area.
+template <class ACC, class PE, class PP>
+__device__ __forceinline__ int draw_cluster(SmemRA &sm, XchgA *xc, uint32_t rank, uint32_t C, int lo, int Vtot,
+                                            const uint32_t *bits, const int *plist, const ACC &acc, int Vl, int np,
+                                            double u, double eps, double eabs, const PE &pe, const PP &pp) {
+  constexpr int NV4 = kRegLayers;
+  using PT = decltype(pe(0.f));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int SH = 5 - Log2<NV4>::v;
+  PT part[NV4];
+#pragma unroll
+  for (int i = 0; i < NV4; ++i) {
+    const float4 x = acc(i);
+    part[i] = (pe(x.x) + pe(x.y)) + (pe(x.z) + pe(x.w));
+  }
+  PT pq[kPenCap / kSampThreads];
+#pragma unroll
+  for (int q = 0; q < kPenCap / kSampThreads; ++q) {
+    const int s = threadIdx.x + q * kSampThreads;
+    pq[q] = PT(0);
+    if (s < np) {
+      pq[q] = pp(s);
+      const int sg = plist[s] / kSegLen;
+#pragma unroll
+      for (int i = 0; i < NV4; ++i) part[i] = part[i] + (i == sg ? pq[q] : PT(0));
+    }
+  }
+  const PT lt = warp_reduce_layers<NV4>(part);
+  if ((lane & ((1 << SH) - 1)) == 0) sm.wp[lane >> SH][warp] = (double)lt;
+  __syncthreads();
+  if (warp == 0 && lane < NV4) {
+    double seg = 0.0;
+    for (int w = 0; w < kSampWarps; ++w) seg = __dadd_rn(seg, sm.wp[lane][w]);
+    xc->seg[lane] = seg;
+  }
+  cluster_sync_all();
+  if (warp == 0) {
+    // lane l: global layers 4l .. 4l+3 (layer g = 16 rank + local layer)
+    const int nl = (int)C * NV4;
+    double t[4], run = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int g = 4 * lane + j;
+      t[j] = g < nl ? ld_cluster_f64(xc_addr(&xc->seg[g % NV4], (uint32_t)(g / NV4))) : 0.0;
+      run = __dadd_rn(run, t[j]);
+    }
+    double incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl = __dadd_rn(incl, n);
+    }
+    double excl = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (lane == 0) excl = 0.0;
+    const double S = __shfl_sync(0xffffffffu, incl, 31);
+    const double rr = __dmul_rn(u, S);
+    int first = -1;
+    double base = 0.0, p = excl;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const double nx = __dadd_rn(p, t[j]);
+      if (first < 0 && 4 * lane + j < nl && nx >= rr) {
+        first = 4 * lane + j;
+        base = p;
+      }
+      p = nx;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, first >= 0);
+    const int src = hit ? __ffs(hit) - 1 : 0;
+    const int g = __shfl_sync(0xffffffffu, first, src);
+    base = __shfl_sync(0xffffffffu, base, src);
+    if (lane == 0) {
+      sm.S = S;
+      sm.r = rr;
+      sm.base = base;
+      sm.ss = (isfinite(S) && isfinite(rr) && hit && u >= 0.0 && u <= 1.0) ? g : -1;
+      sm.dcand = INT_MAX;
+    }
+  }
+  __syncthreads();
+  const int gs = sm.ss;
+  if (gs < 0) return -1;  // the same on every CTA: all read the same totals in the same order
+  const int sc = gs / NV4, ss = gs % NV4;
+  if ((int)rank == sc) {
+#pragma unroll
+    for (int q = 0; q < kPenCap / kSampThreads; ++q) {
+      const int s = threadIdx.x + q * kSampThreads;
+      if (s < np) {
+        const int h = plist[s];
+        if (h / kSegLen == ss) sm.segpen[h % kSegLen] = (double)pq[q];
+      }
+    }
+    __syncthreads();
+    const double S = sm.S, rr = sm.r;
+    const int v0 = (threadIdx.x + kSampThreads * ss) * 4;
+    const float4 x = acc(ss);
+    const uint32_t pw = v0 < Vl ? (bits[v0 >> 5] >> (v0 & 31)) & 0xFu : 0u;
+    double pr[4];
+    double c = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float f = f4_at(x, j);
+      pr[j] = v0 + j >= Vl ? 0.0 : ((pw >> j) & 1u) ? sm.segpen[(v0 + j) % kSegLen] : (double)pe(f);
+      c = __dadd_rn(c, pr[j]);
+    }
+    double incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl = __dadd_rn(incl, n);
+    }
+    if (lane == 31) sm.wsum[warp] = incl;
+    __syncthreads();
+    double wt = lane < kSampWarps ? sm.wsum[lane] : 0.0;
+#pragma unroll
+    for (int o = 1; o < kSampWarps; o <<= 1) {
+      const double n = __shfl_up_sync(0xffffffffu, wt, o);
+      if (lane >= o) wt = __dadd_rn(wt, n);
+    }
+    double wbase = __shfl_sync(0xffffffffu, wt, (warp + 31) & 31);
+    if (warp == 0) wbase = 0.0;
+    double ex = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (lane == 0) ex = 0.0;
+    ex = __dadd_rn(wbase, ex);
+    double prev = __dadd_rn(sm.base, ex);
+    int mine = -1;
+    double lo_s = prev, hi_s = prev;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const double cur = __dadd_rn(prev, pr[j]);
+      if (mine < 0 && v0 + j < Vl && cur >= rr) {
+        mine = j;
+        lo_s = prev;
+        hi_s = cur;
+      }
+      prev = cur;
+    }
+    if (mine >= 0) {
+      // the error model of draw_reg, with every CTA's layers in the depth
+      const int cand = lo + v0 + mine;
+      const double slack = (double)((int)C * NV4 + 64);
+      const double er = eps * (1.0 + 2.0 * eps) + 1e-12 * (eps > 0.0);
+      const double Er = u * (er * S + (double)Vtot * eabs + ((double)Vtot + slack) * 0x1p-52 * S) + 0x1p-52 * rr;
+      const double Ehi = er * hi_s + ((double)cand + 1.0) * eabs + ((double)cand + slack) * 0x1p-52 * hi_s;
+      const double Elo = er * lo_s + (double)cand * eabs + ((double)cand + slack) * 0x1p-52 * lo_s;
+      const bool up = hi_s - Ehi >= rr + Er;
+      const bool dn = cand == 0 || lo_s + Elo < rr - Er;
+      atomicMin(&sm.dcand, 2 * cand + ((up && dn) ? 0 : 1));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int key = sm.dcand;
+      const int v = (key != INT_MAX && !(key & 1)) ? key >> 1 : -1;
+      st_cluster_u32(xc_addr(&xc->verdict, 0), (uint32_t)v);
+    }
+  }
+  cluster_sync_all();
+  return (int)ld_cluster_u32(xc_addr(&xc->verdict, 0));
+}
+
+template <int NV4>
+__global__ void __launch_bounds__(kSampThreads, 1) sample_a_cluster(const __grid_constant__ SampArgs a) {
+  static_assert(NV4 == kRegLayers, "one slice per CTA");
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  SmemRA &sm = *reinterpret_cast<SmemRA *>(smem_dyn);
+  RowPipe &pp = sm.pipe;
+  XchgA *xcs = reinterpret_cast<XchgA *>(smem_dyn + sizeof(SmemRA));  // [2], row parity
+  const uint32_t rank = cluster_ctarank(), C = cluster_nctarank();
+  const int lo = (int)rank * kSliceLen;
+  const int Vl = min(a.V - lo, kSliceLen);
+  SampArgs va = a;  // this CTA's slice of every row
+  va.logits = a.logits + lo;
+  va.V = Vl;
+  const int words = kSliceLen / 32;  // bitmap copies at the same offsets in every CTA
+  uint32_t *bm = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemRA) + 2 * sizeof(XchgA));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool greedy = a.T <= 0.01;
+  RowFeeder feed;
+  feed.stage = stage_ptr(smem_dyn, sizeof(SmemRA) + 2 * sizeof(XchgA) + (size_t)8 * words, kSliceLen);
+  feed.bar = &pp.bar;
+  int hreg[kHistRegs];
+  const int cid = (int)(blockIdx.x / C), ncl = (int)(gridDim.x / C);
+  pipe_start(va, pp, bm, words, feed, hreg, sm.plist[0], lo, cid, ncl);
+  cluster_sync_all();  // every CTA's exchange area exists before the first remote access
+
+  int it = 0;
+  for (int b = cid; b < a.rows; b += ncl, ++it) {
+    const int par = it & 1;
+    XchgA *xc = &xcs[par];
+    const uint32_t *bits = bm + (it % 3) * words;
+    int *plist = sm.plist[par];
+    float *pval = sm.pval[par];
+    if (threadIdx.x == 0) pipe_reset(pp, par ^ 1);
+    const bool ok = feed.wait(a.err);  // a timeout is recorded; the cluster keeps its barrier sequence
+    const int np = min(pp.npen[par], kPenCap);
+    unsigned long long pk = 0ull;
+    if (warp * 32 < np) {
+#pragma unroll
+      for (int q = 0; q < kPenCap / kSampThreads; ++q) {
+        const int s = threadIdx.x + q * kSampThreads;
+        if (s < np) {
+          const int h = plist[s];
+          const float raw = feed.stage[h];
+          if (h == 0) pp.l0[par] = raw;
+          const float t = penalise_a(div_to_f32(raw, a.T, a.Tinv), a.rep, a.repinv);
+          pval[s] = t;
+          feed.stage[h] = -INFINITY;
+          const unsigned long long key = argmax_key(t, lo + h);
+          pk = key > pk ? key : pk;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long o2 = __shfl_xor_sync(0xffffffffu, pk, o);
+        pk = o2 > pk ? o2 : pk;
+      }
+    }
+    if (lane == 0) pp.pkey[par][warp] = pk;
+    __syncthreads();
+    float4 r[NV4];
+    float xmax = -INFINITY;
+    const uint32_t st_u32 = smem_u32(feed.stage);
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) {
+      const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+      r[i] = v0 < Vl ? lds4(st_u32 + 4u * v0) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      xmax = fmaxf(xmax, fmax4(r[i]));
+    }
+    if (threadIdx.x == 0 && !(bits[0] & 1u)) pp.l0[par] = r[0].x;
+    const float my_xmax = xmax;
+    xmax = warp_max(xmax);
+    if (lane == 0) atomicMax(&pp.xkey[par], okey32(xmax));
+    __syncthreads();
+    (void)ok;
+    pipe_advance(va, pp, bm, words, it, b, feed, hreg, sm.plist[par ^ 1], lo, ncl);
+
+    // ---- publish the slice's maxima, then combine over the cluster ----
+    pk = pp.pkey[par][lane & (kSampWarps - 1)];
+#pragma unroll
+    for (int o = kSampWarps / 2; o > 0; o >>= 1) {
+      const unsigned long long o2 = __shfl_xor_sync(0xffffffffu, pk, o);
+      pk = o2 > pk ? o2 : pk;
+    }
+    if (threadIdx.x == 0) {
+      xc->xkey = pp.xkey[par];
+      xc->pkey = pk;
+      xc->l0 = pp.l0[par];
+      xc->cand = INT_MAX;
+    }
+    cluster_sync_all();
+    unsigned int xk = 0u;
+    unsigned long long gpk = 0ull;
+    for (uint32_t c = 0; c < C; ++c) {
+      xk = max(xk, ld_cluster_u32(xc_addr(&xc->xkey, c)));
+      const unsigned long long o2 = ld_cluster_u64(xc_addr(&xc->pkey, c));
+      gpk = o2 > gpk ? o2 : gpk;
+    }
+    const float l0 = __uint_as_float(ld_cluster_u32(xc_addr(&xc->l0, 0)));
+    if (a.nan_guard && l0 != l0) {  // src/snai_inference.php:146
+      if (rank == 0 && threadIdx.x == 0) a.out[b] = -1;
+      continue;
+    }
+    xmax = key_to_float(xk);
+    const float pmax = key_to_float((unsigned int)(gpk >> 32));
+    const int pidx = gpk ? (int)(0xffffffffu - (unsigned int)gpk) : INT_MAX;
+    const float tmax = (xmax > -INFINITY) ? div_to_f32(xmax, a.T, a.Tinv) : -INFINITY;
+    const float M = fmaxf(tmax, pmax);
+    const bool simple = a.T > 0.0 && isfinite(M) && isfinite(xmax);
+    const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
+
+    if (greedy && simple) {
+      const double lowt = (double)M - fabs((double)M) * 0x1p-22 - 1e-44;
+      const float xthr = __double2float_rd(lowt * a.T);
+      int mc = INT_MAX;
+      if (my_xmax >= xthr) {
+#pragma unroll
+        for (int i = 0; i < NV4; ++i) {
+          if (fmax4(r[i]) >= xthr) {
+            const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float f = f4_at(r[i], j);
+              if (f >= xthr && div_to_f32(f, a.T, a.Tinv) == M) mc = min(mc, lo + v0 + j);
+            }
+          }
+        }
+      }
+      if (rank == 0 && threadIdx.x == 0 && pmax == M) mc = min(mc, pidx);
+      if (mc != INT_MAX) atomicMin(&xc->cand, mc);
+      cluster_sync_all();
+      if (rank == 0 && threadIdx.x == 0) {
+        int best = INT_MAX;
+        for (uint32_t c = 0; c < C; ++c) best = min(best, (int)ld_cluster_u32(xc_addr(&xc->cand, c)));
+        a.out[b] = best;
+      }
+      continue;
+    }
+
+    float best = M;
+    int bi = INT_MAX;
+    if (!simple) {
+      // exact maximum of the slice's stored values (from global memory), combined over the cluster
+      float lb;
+      int li;
+      exact_max_a(va, bits, L + lo, reinterpret_cast<float *>(sm.wsum), reinterpret_cast<int *>(sm.wsum) + 16, lb,
+                  li);
+      if (threadIdx.x == 0) xc->ekey = li == INT_MAX ? 0ull : argmax_key(lb, lo + li);
+      cluster_sync_all();
+      unsigned long long ek = 0ull;
+      for (uint32_t c = 0; c < C; ++c) {
+        const unsigned long long o2 = ld_cluster_u64(xc_addr(&xc->ekey, c));
+        ek = o2 > ek ? o2 : ek;
+      }
+      best = key_to_float((unsigned int)(ek >> 32));
+      bi = ek ? (int)(0xffffffffu - (unsigned int)ek) : INT_MAX;
+    }
+    const bool any = best > -INFINITY;
+    if (greedy) {
+      if (rank == 0 && threadIdx.x == 0) a.out[b] = any ? bi : 0;
+      continue;
+    }
+    const double maxv = any ? (double)best : -INFINITY;
+    const double u = (double)a.uniforms[b];
+    int id = -1;
+    if (any && simple) {
+      const float c = (float)(1.4426950408889634 * a.Tinv);
+      const float l2e = 1.44269504f;
+      const float m2 = M * l2e;
+      const double tabs = fabs((double)M) + 91.0;
+      const double eps = (tabs + fabs((double)M) + 1.0) * 0x1p-21 + 0x1p-19 + 0x1p-20;
+      id = draw_cluster(
+          sm, xc, rank, C, lo, a.V, bits, plist, [&](int i) { return pick_layer(r, i); }, Vl, np, u, eps, 0x1p-125,
+          [&](float x) { return ex2_approx(fmaf(x, c, -m2)); },
+          [&](int s) { return ex2_approx(fmaf(pval[s], l2e, -m2)); });
+      if (id < 0) {
+        // tier 2: the contract exponential, the slice read from global memory
+        const float *Ls = L + lo;
+        auto acc = [&](int i) {
+          const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+          float4 x = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+          if (v0 < Vl) {
+            x = __ldg(reinterpret_cast<const float4 *>(Ls + v0));
+            const uint32_t w = (bits[v0 >> 5] >> (v0 & 31)) & 0xFu;
+            if (w & 1u) x.x = -INFINITY;
+            if (w & 2u) x.y = -INFINITY;
+            if (w & 4u) x.z = -INFINITY;
+            if (w & 8u) x.w = -INFINITY;
+          }
+          return x;
+        };
+        id = draw_cluster(
+            sm, xc, rank, C, lo, a.V, bits, plist, acc, Vl, np, u, 0.0, 0.0,
+            [&](float x) { return snai_exp(__dsub_rn((double)div_to_f32(x, a.T, a.Tinv), maxv)); },
+            [&](int s) { return snai_exp(__dsub_rn((double)pval[s], maxv)); });
+      }
+    }
+    if (id < 0) {
+      // tier 3 on rank 0, reading every CTA's bitmap: the cluster waits
+      if (rank == 0 && warp == 0) {
+        const int s = sequential_a_cluster(a, smem_u32(bits), L, maxv, u);
+        if (lane == 0) a.out[b] = s;
+      }
+      cluster_sync_all();
+    } else if (rank == 0 && threadIdx.x == 0) {
+      a.out[b] = id;
+    }
+    __syncthreads();
+  }
+  cluster_sync_all();  // no CTA leaves while another may still read its shared memory
+}
+
+struct XchgB {
+  unsigned int xkey;  // maximum of the slice's lower bounds (okey32)
+  float s1, s2;       // spread statistics of rank 0's chunk layer 0
+  int bstar;          // rank 0 -> every CTA: the histogram's threshold bin
+};
+
+// Variant B over a cluster row: the fast selection of sample_b_reg with the
+// maximum and the histogram combined over the cluster (rank 0 sums the
+// CTAs' histograms), every CTA gathering its candidates into rank 0's
+// candidate table, and rank 0 ranking them and running the top-p tail.  Rows
+// the fast path cannot settle take general_select_b on rank 0 over the whole
+// row, with a whole-row history bitmap built for them.
+__global__ void __launch_bounds__(kSampThreads, 1) sample_b_cluster(const __grid_constant__ SampArgs a) {
+  constexpr int NV4 = kRegLayers;
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  SmemB &sm = *reinterpret_cast<SmemB *>(smem_dyn);
+  RowPipe &pp = *reinterpret_cast<RowPipe *>(smem_dyn + sizeof(SmemB));
+  XchgB *xcs = reinterpret_cast<XchgB *>(smem_dyn + sizeof(SmemB) + sizeof(RowPipe));  // [2]
+  const uint32_t rank = cluster_ctarank(), C = cluster_nctarank();
+  const int lo = (int)rank * kSliceLen;
+  const int Vl = min(a.V - lo, kSliceLen);
+  SampArgs va = a;
+  va.logits = a.logits + lo;
+  va.V = Vl;
+  const int words = kSliceLen / 32;
+  uint32_t *bm = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemB) + sizeof(RowPipe) + 2 * sizeof(XchgB));
+  uint32_t *fullbits = bm + 3 * (kSliceLen / 32);  // rank 0: whole-row bitmap for the general path
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int k = min(a.top_k, a.V);
+  const double rep = a.rep;
+  RowFeeder feed;
+  // stage_ptr adds one bitmap of `words` words: the core, three slice
+  // bitmaps and the whole-row bitmap come before the stage
+  feed.stage = stage_ptr(smem_dyn,
+                         sizeof(SmemB) + sizeof(RowPipe) + 2 * sizeof(XchgB) + (size_t)8 * words +
+                             (size_t)((a.V + 31) / 32) * 4,
+                         kSliceLen);
+  feed.bar = &pp.bar;
+  int hreg[kHistRegs];
+  const int cid = (int)(blockIdx.x / C), ncl = (int)(gridDim.x / C);
+  pipe_start(va, pp, bm, words, feed, hreg, sm.plist, lo, cid, ncl);
+  cluster_sync_all();
+  const uint32_t ncand0 = xc_addr(&sm.ncand, 0);
+
+  int it = 0;
+  for (int b = cid; b < a.rows; b += ncl, ++it) {
+    const int par = it & 1;
+    XchgB *xc = &xcs[par];
+    const uint32_t *bits = bm + (it % 3) * words;
+    if (threadIdx.x == 0) pipe_reset(pp, par ^ 1);
+    const bool ok = feed.wait(a.err);
+    (void)ok;
+    const int np = min(pp.npen[par], kPenCap);
+    for (int s = threadIdx.x; s < np; s += kSampThreads) {
+      const int h = sm.plist[s];
+      feed.stage[h] = __double2float_rd(__dsub_rn((double)feed.stage[h], rep));
+    }
+    __syncthreads();
+    float4 r[NV4];
+    float mx = -INFINITY, s1 = 0.f, s2 = 0.f;
+    const uint32_t st_u32 = smem_u32(feed.stage);
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) {
+      const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+      r[i] = v0 < Vl ? lds4(st_u32 + 4u * v0) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      if (i == 0 && v0 < Vl && rank == 0) {
+        const float4 x = r[0];
+        s1 = (x.x + x.y) + (x.z + x.w);
+        s2 = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, x.w * x.w)));
+      }
+      mx = fmaxf(mx, fmax4(r[i]));
+    }
+    const float my_mx = mx;
+    mx = warp_max(mx);
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if (lane == 0) {
+      atomicMax(&pp.xkey[par], okey32(mx));
+      atomicAdd(&pp.s1[par], s1);
+      atomicAdd(&pp.s2[par], s2);
+    }
+    for (int i = threadIdx.x; i < 256; i += kSampThreads) sm.hist[i] = 0u;
+    if (threadIdx.x == 0) sm.ncand = 0;
+    __syncthreads();
+    pipe_advance(va, pp, bm, words, it, b, feed, hreg, sm.plist, lo, ncl);
+    if (threadIdx.x == 0) {
+      xc->xkey = pp.xkey[par];
+      xc->s1 = pp.s1[par];
+      xc->s2 = pp.s2[par];
+    }
+    cluster_sync_all();
+    unsigned int xk = 0u;
+    for (uint32_t c = 0; c < C; ++c) xk = max(xk, ld_cluster_u32(xc_addr(&xc->xkey, c)));
+    mx = key_to_float(xk);
+    s1 = __uint_as_float(ld_cluster_u32(xc_addr(&xc->s1, 0)));
+    s2 = __uint_as_float(ld_cluster_u32(xc_addr(&xc->s2, 0)));
+    const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
+    const int n0 = min(a.V, kSegLen);
+    bool fast = isfinite(mx) && isfinite(s1) && isfinite(s2) && a.V >= k;
+    float R = 0.f;
+    if (fast) {
+      const float mean = s1 / n0;
+      const float sd = sqrtf(fmaxf(s2 / n0 - mean * mean, 0.f));
+      R = 2.5f * sd;
+      fast = R > 0.f && isfinite(R);
+    }
+    int bstar = 255;
+    for (int attempt = 0; fast && attempt < 3 && bstar >= 255; ++attempt) {
+      if (attempt > 0) {
+        for (int i = threadIdx.x; i < 256; i += kSampThreads) sm.hist[i] = 0u;
+        __syncthreads();
+      }
+      const float inv_w = 255.f / R;
+#pragma unroll
+      for (int i = 0; i < NV4; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float d = mx - f4_at(r[i], j);
+          if (d < R) atomicAdd(&sm.hist[min((int)(d * inv_w), 254)], 1u);
+        }
+      }
+      cluster_sync_all();
+      if (rank == 0 && warp == 0) {
+        unsigned int c8[8], run = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          unsigned int h = 0;
+          for (uint32_t c = 0; c < C; ++c) h += ld_cluster_u32(xc_addr(&sm.hist[lane * 8 + q], c));
+          run += h;
+          c8[q] = run;
+        }
+        unsigned int incl = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const unsigned int n = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += n;
+        }
+        const unsigned int before = incl - run;
+        int bs = 255;
+#pragma unroll
+        for (int q = 7; q >= 0; --q)
+          if (before + c8[q] >= (unsigned)k) bs = lane * 8 + q;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) bs = min(bs, __shfl_xor_sync(0xffffffffu, bs, o));
+        if (lane < (int)C) st_cluster_u32(xc_addr(&xc->bstar, (uint32_t)lane), (uint32_t)bs);
+      }
+      cluster_sync_all();
+      bstar = xc->bstar;
+      if (bstar >= 255) R *= 8.f;
+    }
+    fast = fast && bstar < 255;
+    if (fast) {
+      // gather (the superset threshold of sample_b_reg) into rank 0's table
+      const double gd = (double)mx - (double)(bstar + 1) * ((double)R / 255.0) * (1.0 + 0x1p-20);
+      float g = __double2float_rd(gd);
+      g = (g == -INFINITY) ? g : __uint_as_float(g > 0.f ? __float_as_uint(g) - 1u
+                                                          : (g == 0.f ? 0x80000001u : __float_as_uint(g) + 1u));
+      if (my_mx >= g) {
+#pragma unroll
+        for (int i = 0; i < NV4; ++i) {
+          if (fmax4(r[i]) >= g) {
+            const int v0 = (threadIdx.x + kSampThreads * i) * 4;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float f = f4_at(r[i], j);
+              if (f >= g) {
+                const int v = v0 + j;
+                const double val = in_set(bits, v) ? __dsub_rn((double)L[lo + v], rep) : (double)f;
+                const uint32_t slot = atom_cluster_add_u32(ncand0, 1u);
+                if (slot < (uint32_t)kFastCand) {
+                  st_cluster_u64(xc_addr(&sm.ckey[slot], 0), okey64(val));
+                  st_cluster_u32(xc_addr(&sm.cidx[slot], 0), (uint32_t)(lo + v));
+                }
+              }
+            }
+          }
+        }
+      }
+    }
+    cluster_sync_all();
+    if (rank != 0) continue;
+    // ---- rank 0: selection and the top-p tail (the other CTAs go on) ----
+    if (fast) {
+      const int nc = sm.ncand;
+      fast = nc <= kFastCand && nc >= k;
+      if (fast) rank_candidates(sm, nc, k);
+    }
+    if (!fast) {
+      // whole-row history bitmap for the general path
+      const int fw = (a.V + 31) >> 5;
+      for (int i = threadIdx.x; i < fw; i += kSampThreads) fullbits[i] = 0u;
+      __syncthreads();
+      {
+        const int mrow = row_of(a, b);
+        int n = a.hist_len ? a.hist_len[mrow] : a.hist_cols;
+        n = min(max(n, 0), a.hist_cols);
+        const int *hr = a.hist + (size_t)mrow * a.hist_ld;
+        for (int i = threadIdx.x; i < n; i += kSampThreads) {
+          const int t = hr[i];
+          if (t >= 0 && t < a.V) atomicOr(&fullbits[t >> 5], 1u << (t & 31));
+        }
+      }
+      __syncthreads();
+      if (!general_select_b(a, fullbits, L, sm, k)) {
+        if (threadIdx.x == 0) {
+          a.out[b] = -2;
+          record_error(a.err, kErrSamplerArgs);
+        }
+        __syncthreads();
+        continue;
+      }
+    }
+    if (a.T < 0.01) {
+      if (threadIdx.x == 0) a.out[b] = sm.order[0];
+      __syncthreads();
+      continue;
+    }
+    double *P = reinterpret_cast<double *>(sm.ckey);
+    double *Cs = P + kMaxTopK;
+    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = snai_exp(__ddiv_rn(sm.val[i], a.T));
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double s = 0.0;
+      for (int i = 0; i < k; ++i) s = __dadd_rn(s, P[i]);
+      Cs[0] = s;
+    }
+    __syncthreads();
+    const double sum = Cs[0];
+    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = __ddiv_rn(P[i], sum);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double cum = 0.0;
+      int nf = 0;
+      for (int i = 0; i < k; ++i) {
+        cum = __dadd_rn(cum, P[i]);
+        Cs[i] = cum;
+        nf = i + 1;
+        if (cum >= a.top_p) break;
+      }
+      const double rr = __dmul_rn((double)a.uniforms[b], cum);
+      int id = sm.order[0];
+      for (int i = 0; i < nf; ++i)
+        if (rr <= Cs[i]) {
+          id = sm.order[i];
+          break;
+        }
+      a.out[b] = id;
+    }
+    __syncthreads();
+  }
+  cluster_sync_all();
+}
+
+// ---------------------------------------------------------------------------
 // host
 // ---------------------------------------------------------------------------
 
@@ -2081,6 +2779,39 @@ static void launch_persistent(K kern, const SampArgs &a, size_t sm, int per_sm, 
   kern<<<grid, kSampThreads, sm, st>>>(a);
 }
 
+// One cluster of C CTAs per row, clusters walking the rows; returns false if
+// the cluster shape cannot be scheduled (the caller falls back).
+template <class K>
+static bool launch_cluster(K kern, const SampArgs &a, size_t sm, int C, cudaStream_t st, unsigned long long &done) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(done & (1ull << dev))) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    done |= 1ull << dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)C;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kSampThreads);
+  cfg.dynamicSmemBytes = sm;
+  cfg.stream = st;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3((unsigned)C);
+  int fit = 0;
+  if (cudaOccupancyMaxActiveClusters(&fit, kern, &cfg) != cudaSuccess || fit < 1) {
+    cudaGetLastError();
+    return false;
+  }
+  const int clusters = std::max(1, std::min(a.rows, fit));
+  cfg.gridDim = dim3((unsigned)(clusters * C));
+  return cudaLaunchKernelEx(&cfg, kern, a) == cudaSuccess;
+}
+
 template <int NV4>
 static void launch_a(const SampArgs &a, size_t sm, cudaStream_t st) {
   static unsigned long long done = 0;  // attributes set, one bit per device
@@ -2130,6 +2861,33 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   const bool reg = layers <= kRegLayers && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
                    (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 && s.hist_cols <= kPenCap;
   const int nv4 = !reg ? 0 : layers <= 4 ? 4 : layers <= 8 ? 8 : 16;
+  // rows of up to 8 slices: a cluster of CTAs per row
+  const int C = (s.V + kSliceLen - 1) / kSliceLen;
+  const bool clus = !reg && C >= 2 && C <= kMaxCluster && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
+                    (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 && s.hist_cols <= kPenCap;
+  if (clus) {
+    const size_t maps = 3 * (size_t)(kSliceLen / 32) * 4 + (size_t)kSliceLen * 4 + kStageAlign;
+    bool launched;
+    if (s.variant == 0) {
+      static unsigned long long done = 0;
+      launched = launch_cluster(sample_a_cluster<kRegLayers>, a, sizeof(SmemRA) + 2 * sizeof(XchgA) + maps, C,
+                                stream, done);
+    } else {
+      static unsigned long long done = 0;
+      launched = launch_cluster(sample_b_cluster, a,
+                                sizeof(SmemB) + sizeof(RowPipe) + 2 * sizeof(XchgB) + maps +
+                                    (size_t)((s.V + 31) / 32) * 4,
+                                C, stream, done);
+    }
+    if (launched) {
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) {
+        set_error("sampler launch failed: %s", cudaGetErrorString(e));
+        return -4;
+      }
+      return 0;
+    }
+  }
   // register rows: three bitmaps, then the staging buffer (+ alignment slack)
   const size_t rsm = reg ? 3 * (size_t)((s.V + 31) / 32) * 4 + (size_t)s.V * 4 + kStageAlign : 0;
   if (s.variant == 0) {

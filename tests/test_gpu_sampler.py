@@ -94,9 +94,12 @@ def test_variant_b_matches_oracle(V, cfg, built):
     assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_B, T, 1.1, k, p, exp_mode=0))
 
 
-def test_large_vocab_both_variants(built):
-    rng = np.random.default_rng(5)
-    L, hist, U = synth(rng, 16, 131072)
+@pytest.mark.parametrize("V", [50000, 131072, 229380])
+def test_large_vocab_both_variants(V, built):
+    """Rows longer than one CTA's register row: a cluster of CTAs per row
+    (2, 4 and 7 slices; the first and last with a partial final slice)."""
+    rng = np.random.default_rng(5 + V)
+    L, hist, U = synth(rng, 16, V)
     for prm, args in [(sample_params(VARIANT_A, 0.7, 1.15, nan_guard=0), (VARIANT_A, 0.7, 1.15)),
                       (sample_params(VARIANT_A, 0.01, 1.15, nan_guard=0), (VARIANT_A, 0.01, 1.15)),
                       (sample_params(VARIANT_B, 0.7, 1.1, 50, 0.95), (VARIANT_B, 0.7, 1.1, 50, 0.95))]:
