@@ -14,6 +14,8 @@
 // differences from the reference are the dot products' summation order.
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 #include "engine.h"
 
@@ -63,6 +65,7 @@ struct EpiQKV {
     }
   }
 
+  static constexpr bool kTmaReduce = false;
   struct Pre {};
   using Row = RowDesc;
   __device__ __forceinline__ Row row(int m) const { return rows[m]; }
@@ -133,6 +136,11 @@ struct EpiQKV {
 struct EpiResidual {
   float *h;
   int ld;
+  // h as a [M][ld] fp32 tensor, 16 x 32 boxes, 64-byte swizzle: the
+  // tensor-core drains add their staged 32-row x 16-column runs into h with
+  // TMA reduce-adds (the add happens at L2, the SM does not wait for h)
+  CUtensorMap tmap;
+  static constexpr bool kTmaReduce = true;
   using Pre = float4;
   struct Row {};
   __device__ __forceinline__ Row row(int) const { return Row{}; }
@@ -191,6 +199,7 @@ struct EpiSilu {
   __device__ static __forceinline__ float silu(float x) {
     return __fmul_rn(x, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))));
   }
+  static constexpr bool kTmaReduce = false;
   struct Pre {};
   struct Row {};
   __device__ __forceinline__ Row row(int) const { return Row{}; }
@@ -244,6 +253,7 @@ struct EpiLogits {
   float *logits;
   const int2 *outrows;  // chunk-local logits row -> (chunk row, slot)
   long long ld;
+  static constexpr bool kTmaReduce = false;
   struct Pre {};
   using Row = int;
   __device__ __forceinline__ Row row(int m) const { return outrows[m].y; }

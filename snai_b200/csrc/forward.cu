@@ -390,6 +390,28 @@ static bool make_tmap(CUtensorMap *map, const void *base, bool bf16, int K, int 
   return r == CUDA_SUCCESS;
 }
 
+// The residual epilogue of M rows: h and its tensor map for the drains'
+// reduce-adds (16 x 32 fp32 boxes, 64-byte swizzle; valid for every engine
+// shape: d is a multiple of 4 and h is 256-byte aligned).  Returns false
+// (with the error set) if the map cannot be made.
+static bool residual_epi(Engine &e, int M, EpiResidual *r) {
+  *r = EpiResidual{};
+  r->h = e.h;
+  r->ld = e.d.D;
+  auto enc = get_encode_fn();
+  cuuint64_t dims[2] = {(cuuint64_t)e.d.D, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)e.d.D * 4};
+  cuuint32_t box[2] = {16, 32};
+  cuuint32_t estr[2] = {1, 1};
+  if (!enc || enc(&r->tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, e.h, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed for the residual (M=%d D=%d)", M, e.d.D);
+    return false;
+  }
+  return true;
+}
+
 static bool tc_path(const Engine &e, int M) {
   return e.precision != kFP32 && M >= 64 && e.d.D % 16 == 0 && e.d.D >= 64;
 }
@@ -561,12 +583,14 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
     int rc = project(e, kProfQKV, M, 3 * d.D, d.D, x, w.wqkv, w.wqkv_h, eq, 3.0 * M * d.att_ch * 4);
     if (rc) return rc;
     launch_attention<TA>(e, M, l, att, kv_positions, defer);
-    rc = project(e, kProfWo, M, d.D, d.D, att, w.wo, w.wo_h, EpiResidual{e.h, d.D}, 8.0 * M * d.D);
+    EpiResidual res;
+    if (!residual_epi(e, M, &res)) return -5;
+    rc = project(e, kProfWo, M, d.D, d.D, att, w.wo, w.wo_h, res, 8.0 * M * d.D);
     if (rc) return rc;
     launch_norm<TA>(e, M, nullptr, w.rms_ffn, x);
     rc = project(e, kProfUp, M, d.F, d.D, x, w.wup, w.wup_h, EpiSilu<TA>{u, d.F}, ea * M * d.F);
     if (rc) return rc;
-    rc = project(e, kProfDown, M, d.D, d.F, u, w.wdown, w.wdown_h, EpiResidual{e.h, d.D}, 8.0 * M * d.D);
+    rc = project(e, kProfDown, M, d.D, d.F, u, w.wdown, w.wdown_h, res, 8.0 * M * d.D);
     if (rc) return rc;
     if (l + 1 < d.L) launch_norm<TA>(e, M, nullptr, e.layers[l + 1].rms_att, x);
   }

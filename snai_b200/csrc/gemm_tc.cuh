@@ -109,6 +109,18 @@ __device__ __forceinline__ T shfl_any(const T &v, int src) {
   }
 }
 
+// TMA reduce-add of a staged 32-row x 16-column fp32 run into the tensor at
+// (column x, row y); the staging buffer is in the map's 64-byte swizzle.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *tmap, const float *stg, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(smem_u32(stg)), "r"(x), "r"(y)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 template <int COLS, class Epi>
 __device__ __forceinline__ void drain_accumulator(uint32_t tbase, int row0, int M, int n0, int N, const Epi &epi,
                                                   float *stg) {
@@ -128,6 +140,21 @@ __device__ __forceinline__ void drain_accumulator(uint32_t tbase, int row0, int 
 #pragma unroll
   for (int c = c0; c < c0 + BLK; c += 16) {
     if (n0 + c >= N) break;  // warp-uniform
+    if constexpr (Epi::kTmaReduce) {
+      // stage the run (the 64-byte swizzle: chunk ch of row l at ch ^ ((l >> 1) & 3)),
+      // then one lane adds it into the tensor; rows >= M and columns >= N
+      // fall outside the map and are dropped by the copy
+      if (lane == 0) bulk_wait_read_all();  // the previous run has been read out of the buffer
+      __syncwarp();
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch)
+        buf[lane * 4 + (ch ^ ((lane >> 1) & 3))] =
+            make_float4(__uint_as_float(r[c + 4 * ch]), __uint_as_float(r[c + 4 * ch + 1]),
+                        __uint_as_float(r[c + 4 * ch + 2]), __uint_as_float(r[c + 4 * ch + 3]));
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0 && row0 < M) tma_reduce_add_2d(&epi.tmap, stg, n0 + c, row0);
+    } else {
     // this run's reads (residual) go out first and overlap the transpose
     typename Epi::Pre pre[4];
 #pragma unroll
@@ -155,7 +182,12 @@ __device__ __forceinline__ void drain_accumulator(uint32_t tbase, int row0, int 
       const int m = row0 + rr, n = n0 + c + 4 * (lane & 3);
       if (m < M && n < N) epi.store4(m, n, v[i], min(4, N - n), pre[i], ri);
     }
+    }
   }
+  }
+  if constexpr (Epi::kTmaReduce) {
+    if (lane == 0) bulk_wait_all();  // the adds are done before the accumulator is released
+    __syncwarp();
   }
 }
 
@@ -185,7 +217,7 @@ struct TcpSmem {
 template <typename TIn, int BN, int STAGES, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcp_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                    int K, Epi epi, int *err) {
+                    int K, const __grid_constant__ Epi epi, int *err) {
   using Sm = TcpSmem<BN, STAGES>;
   constexpr int BK = TcKind<TIn>::kBK;
   constexpr int KSTEPS = BK / TcKind<TIn>::kUK;
@@ -435,7 +467,7 @@ struct Tc2Smem {
 template <typename TIn, int STAGES, class Epi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                    int K, Epi epi, int *err) {
+                    int K, const __grid_constant__ Epi epi, int *err) {
   using Sm = Tc2Smem<STAGES>;
   constexpr int BK = TcKind<TIn>::kBK;
   constexpr int KSTEPS = BK / TcKind<TIn>::kUK;
