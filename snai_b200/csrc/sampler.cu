@@ -844,7 +844,7 @@ struct SmemB {
   float R;
   int npen;
   uint64_t bar;  // staging barrier
-  unsigned int hist[256];
+  __align__(16) unsigned int hist[256];
   unsigned long long ckey[kCandCap];  // exact order key of a candidate; p[] and cum[] after ranking
   int cidx[kCandCap];
   int order[kMaxTopK];
@@ -915,20 +915,146 @@ __device__ __forceinline__ bool precedes(unsigned long long ki, int vi, unsigned
   return ki > kj || (ki == kj && vi < vj);
 }
 
-// Sorts the nc gathered candidates and keeps the first k in sm.order / sm.val.
-__device__ void rank_candidates(SmemB &sm, int nc, int k) {
-  for (int i = threadIdx.x; i < nc; i += kSampThreads) {
-    const unsigned long long ki = sm.ckey[i];
-    const int vi = sm.cidx[i];
+// Ranks the nc gathered candidates (PHP's arsort order: value descending,
+// then id ascending) and keeps the first k: sm.order[rank] = id and
+// sm.val[rank] = exp(val / T) (src/tensor_ffi_adapter.php:183-184), or the
+// value itself when T < 0.01 (greedy).  G = 2^lg threads share a candidate,
+// each counting the candidates that precede it among every G-th one, and add
+// their counts by shuffles.
+__device__ void rank_candidates(SmemB &sm, int nc, int k, double T) {
+  int lg = 0;
+  while (lg < 5 && (nc << (lg + 1)) <= kSampThreads) ++lg;
+  const int G = 1 << lg, per = kSampThreads >> lg;
+  const int sub = threadIdx.x & (G - 1);
+  const bool want_p = !(T < 0.01);
+  for (int c0 = 0; c0 < nc; c0 += per) {
+    const int i = c0 + (threadIdx.x >> lg);
     int rank = 0;
-#pragma unroll 8
-    for (int j = 0; j < nc; ++j) rank += precedes(sm.ckey[j], sm.cidx[j], ki, vi) ? 1 : 0;
-    if (rank < k) {
+    unsigned long long ki = 0ull;
+    int vi = 0;
+    if (i < nc) {
+      ki = sm.ckey[i];
+      vi = sm.cidx[i];
+#pragma unroll 4
+      for (int j = sub; j < nc; j += G) {
+        const unsigned long long kj = sm.ckey[j];
+        const int vj = sm.cidx[j];
+        rank += (int)((kj > ki) | ((kj == ki) & (vj < vi)));
+      }
+    }
+    for (int o = 1; o < G; o <<= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+    if (i < nc && sub == 0 && rank < k) {
       sm.order[rank] = vi;
-      sm.val[rank] = key_to_double(ki);
+      const double val = key_to_double(ki);
+      sm.val[rank] = want_p ? snai_exp(__ddiv_rn(val, T)) : val;
     }
   }
   __syncthreads();
+}
+
+// Absolute margin of the certified top-p tail.  Against PHP's sequential
+// sums, the warp's tree sum, reciprocal and scanned running sums of k <= 512
+// terms (each running sum at most 1 + 2^-40) differ by at most
+// (2k + 44) 2^-53 <= 1.2e-13; 2^-40 is 7.7 times that.
+constexpr double kTailEps = 0x1p-40;
+
+// First index i in [0, k) with C[i] >= x, INT_MAX if none: lane l scans its
+// own survivors [i0, i1), the warp takes the minimum.
+__device__ __forceinline__ int warp_first_ge(const double *C, int i0, int i1, double x) {
+  int f = INT_MAX;
+  for (int i = i0; i < i1; ++i)
+    if (C[i] >= x) {
+      f = i;
+      break;
+    }
+  return __reduce_min_sync(0xffffffffu, f);
+}
+
+// src/tensor_ffi_adapter.php:180-204 over the k ranked survivors of row b
+// (sm.order, p in sm.val), by warp 0 alone (the other warps return at once).
+// PHP sums p in order, divides each p by the sum, accumulates the quotients
+// in order until the running sum reaches top_p (crossing term included),
+// takes r = u * cum and returns the first survivor whose running sum reaches
+// r.  The warp computes the same running sums by a tree sum, one reciprocal
+// and a lane-then-warp scan, each within kTailEps of PHP's, and accepts the
+// result when every decision clears the margin: the first running sum at or
+// above top_p - eps is also at or above top_p + eps (or both are the last),
+// and for r anywhere in the interval this leaves, the first running sum at
+// or above r - eps is also at or above r + eps and lies in the kept prefix.
+// Otherwise (a decision within 1e-12, or p infinite, NaN or all zero) lane 0
+// redoes PHP's sequential arithmetic exactly.  Greedy (T < 0.01) takes
+// order[0].
+__device__ __forceinline__ void topp_tail(const SampArgs &a, SmemB &sm, int k, int b) {
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  if (a.T < 0.01) {
+    if (lane == 0) a.out[b] = sm.order[0];
+    return;
+  }
+  const double u = (double)a.uniforms[b];
+  const double *P = sm.val;
+  double *C = reinterpret_cast<double *>(sm.ckey);  // the candidate keys are dead after ranking
+  const int m = (k + 31) >> 5;
+  const int i0 = min(k, lane * m), i1 = min(k, i0 + m);
+  double part = 0.0;
+  for (int i = i0; i < i1; ++i) part = __dadd_rn(part, P[i]);
+  double S = part;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) S = __dadd_rn(S, __shfl_xor_sync(0xffffffffu, S, o));
+  int id = -1;
+  if (S > 0.0 && S <= DBL_MAX) {
+    const double inv = __drcp_rn(S);
+    double run = 0.0;
+    for (int i = i0; i < i1; ++i) run = __fma_rn(P[i], inv, run);
+    double incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl = __dadd_rn(incl, n);
+    }
+    double c = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (lane == 0) c = 0.0;
+    for (int i = i0; i < i1; ++i) {
+      c = __fma_rn(P[i], inv, c);
+      C[i] = c;
+    }
+    __syncwarp();
+    const double tp = a.top_p;
+    const int jl = min(warp_first_ge(C, i0, i1, tp - kTailEps), k - 1);
+    const int jh = min(warp_first_ge(C, i0, i1, tp + kTailEps), k - 1);
+    const double rl = __dmul_rn(u, C[jl]) - kTailEps, rh = __dmul_rn(u, C[jh]) + kTailEps;
+    const int sa = warp_first_ge(C, i0, i1, rl - kTailEps);
+    const int sb = warp_first_ge(C, i0, i1, rh + kTailEps);
+    if (sa == sb && sa <= jl) id = sm.order[sa];
+    __syncwarp();
+  }
+  if (id < 0) {
+    double s = 0.0;
+    if (lane == 0)
+      for (int i = 0; i < k; ++i) s = __dadd_rn(s, P[i]);
+    s = __shfl_sync(0xffffffffu, s, 0);
+    for (int i = lane; i < k; i += 32) C[i] = __ddiv_rn(P[i], s);
+    __syncwarp();
+    if (lane == 0) {
+      // $cum_check after i+1 terms is this same running sum
+      double cum = 0.0;
+      int nf = 0;
+      for (int i = 0; i < k; ++i) {
+        cum = __dadd_rn(cum, C[i]);
+        C[i] = cum;
+        nf = i + 1;
+        if (cum >= a.top_p) break;
+      }
+      const double rr = __dmul_rn(u, cum);
+      id = sm.order[0];
+      for (int i = 0; i < nf; ++i)
+        if (rr <= C[i]) {
+          id = sm.order[i];
+          break;
+        }
+    }
+  }
+  if (lane == 0) a.out[b] = id;
 }
 
 // Fast selection (see the file comment).  The row holds lower bounds (the
@@ -1081,7 +1207,7 @@ __device__ __forceinline__ bool fast_select_b(const SampArgs &a, const uint32_t 
   const int nc = sm.ncand;
   __syncthreads();
   if (nc > kFastCand || nc < k) return false;
-  rank_candidates(sm, nc, k);
+  rank_candidates(sm, nc, k, a.T);
   return true;
 }
 // General selection: radix select on the 32-bit keys of the lower bounds
@@ -1205,7 +1331,7 @@ __device__ __noinline__ bool general_select_b(const SampArgs &a, const uint32_t 
   }
   __syncthreads();
   if (sm.overflow) return false;
-  rank_candidates(sm, sm.ncand, k);
+  rank_candidates(sm, sm.ncand, k, a.T);
   return true;
 }
 
@@ -1257,39 +1383,8 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
       if (threadIdx.x == 0) a.out[b] = sm.order[0];
       continue;
     }
-    // the candidate keys are dead after ranking: p and the running sums reuse them
-    double *P = reinterpret_cast<double *>(sm.ckey);
-    double *C = P + kMaxTopK;
-    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = snai_exp(__ddiv_rn(sm.val[i], a.T));
+    topp_tail(a, sm, k, b);
     __syncthreads();
-    if (threadIdx.x == 0) {
-      double s = 0.0;
-      for (int i = 0; i < k; ++i) s = __dadd_rn(s, P[i]);
-      C[0] = s;  // the sum, handed to all threads
-    }
-    __syncthreads();
-    const double sum = C[0];
-    __syncthreads();
-    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = __ddiv_rn(P[i], sum);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double cum = 0.0;
-      int nf = 0;
-      for (int i = 0; i < k; ++i) {
-        cum = __dadd_rn(cum, P[i]);
-        C[i] = cum;  // $cum_check after i+1 terms is this same sum
-        nf = i + 1;
-        if (cum >= a.top_p) break;
-      }
-      const double r = __dmul_rn((double)a.uniforms[b], cum);
-      int id = sm.order[0];
-      for (int i = 0; i < nf; ++i)
-        if (r <= C[i]) {
-          id = sm.order[i];
-          break;
-        }
-      a.out[b] = id;
-    }
   }
 }
 
@@ -1393,9 +1488,11 @@ __device__ __forceinline__ void pipe_reset(RowPipe &p, int par) {
 // Marks the history ids in h (each thread's share, -1 for none) that fall in
 // [lo, lo + V) in a cleared bitmap of that range; with a list, the thread
 // whose atomicOr set a bit also appends the (range-local) id to plist
-// (warp-aggregated slots, count in *npen).
+// (warp-aggregated slots, count in *npen); with `own`, that thread keeps the
+// id in own[r] instead (-1 where it set no bit), so every distinct id has
+// exactly one owner.
 __device__ __forceinline__ void mark_ids(int V, const int (&h)[kHistRegs], uint32_t *bits, int *plist, int *npen,
-                                         int lo = 0) {
+                                         int lo = 0, int *own = nullptr) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int r = 0; r < kHistRegs; ++r) {
@@ -1406,6 +1503,7 @@ __device__ __forceinline__ void mark_ids(int V, const int (&h)[kHistRegs], uint3
       const uint32_t old = atomicOr(&bits[t >> 5], bit);
       first = !(old & bit);
     }
+    if (own) own[r] = first ? t : -1;
     if (plist) {
       const unsigned m = __ballot_sync(0xffffffffu, first);
       int base = 0;
@@ -1422,7 +1520,7 @@ __device__ __forceinline__ void mark_ids(int V, const int (&h)[kHistRegs], uint3
 // cluster handles the ids [lo, lo + a.V) of its cluster's rows)
 __device__ __forceinline__ void pipe_start(const SampArgs &a, RowPipe &p, uint32_t *bm, int words, RowFeeder &feed,
                                            int (&hreg)[kHistRegs], int *plist0, int lo = 0, int b0 = -1,
-                                           int stride = 0) {
+                                           int stride = 0, int *own = nullptr) {
   if (b0 < 0) {
     b0 = blockIdx.x;
     stride = gridDim.x;
@@ -1439,7 +1537,7 @@ __device__ __forceinline__ void pipe_start(const SampArgs &a, RowPipe &p, uint32
     const int r0 = row_of(a, b0);
     if (threadIdx.x == 0) feed.issue(a, r0);
     load_hist_regs(a, r0, hreg);
-    mark_ids(a.V, hreg, bm, plist0, &p.npen[0], lo);
+    mark_ids(a.V, hreg, bm, plist0, &p.npen[0], lo, own);
     const int b1 = b0 + stride;
     if (b1 < a.rows) load_hist_regs(a, row_of(a, b1), hreg);
   }
@@ -1453,7 +1551,7 @@ __device__ __forceinline__ void pipe_start(const SampArgs &a, RowPipe &p, uint32
 // it + 2's.
 __device__ __forceinline__ void pipe_advance(const SampArgs &a, RowPipe &p, uint32_t *bm, int words, int it, int b,
                                              RowFeeder &feed, int (&hreg)[kHistRegs], int *plist_next, int lo = 0,
-                                             int stride = 0) {
+                                             int stride = 0, int *own = nullptr) {
   if (stride == 0) stride = gridDim.x;
   const int nb = b + stride;
   if (nb < a.rows && threadIdx.x == 0) {
@@ -1464,7 +1562,7 @@ __device__ __forceinline__ void pipe_advance(const SampArgs &a, RowPipe &p, uint
   uint32_t *clr = bm + ((it + 2) % 3) * words;
   for (int i = threadIdx.x; i < words; i += kSampThreads) clr[i] = 0u;
   if (nb < a.rows) {
-    mark_ids(a.V, hreg, bm + ((it + 1) % 3) * words, plist_next, &p.npen[(it + 1) & 1], lo);
+    mark_ids(a.V, hreg, bm + ((it + 1) % 3) * words, plist_next, &p.npen[(it + 1) & 1], lo, own);
     const int nnb = nb + stride;
     if (nnb < a.rows) load_hist_regs(a, row_of(a, nnb), hreg);
   }
@@ -1824,26 +1922,38 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
   const int V = a.V;
   const int words = (V + 31) >> 5;
   uint32_t *bm = reinterpret_cast<uint32_t *>(smem_dyn + sizeof(SmemB) + sizeof(RowPipe));
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
   const int k = min(a.top_k, V);
   const double rep = a.rep;
   RowFeeder feed;
   feed.stage = stage_ptr(smem_dyn, sizeof(SmemB) + sizeof(RowPipe) + (size_t)8 * words, V);
   feed.bar = &pp.bar;
   int hreg[kHistRegs];
-  pipe_start(a, pp, bm, words, feed, hreg, sm.plist);
+  // distinct history ids this thread owns in the next row, 16 bits each
+  // (0xFFFF: none; register rows hold at most 32768 ids)
+  static_assert(kHistRegs == 2, "two owned ids per thread");
+  int own_tmp[kHistRegs];
+  pipe_start(a, pp, bm, words, feed, hreg, nullptr, 0, -1, 0, own_tmp);
+  unsigned own_next = (own_tmp[0] & 0xFFFFu) | ((unsigned)own_tmp[1] << 16);
+  float *po = reinterpret_cast<float *>(sm.plist);  // stored logit of an owned id, [q][thread]
 
   int it = 0;
   for (int b = blockIdx.x; b < a.rows; b += gridDim.x, ++it) {
     const int par = it & 1;
     const uint32_t *bits = bm + (it % 3) * words;
+    const unsigned own = own_next;
     if (threadIdx.x == 0) pipe_reset(pp, par ^ 1);
     const bool ok = feed.wait(a.err);
-    // penalised entries -> fp32 lower bound of L - rep, in the stage
-    const int np = min(pp.npen[par], kPenCap);
-    for (int s = threadIdx.x; s < np; s += kSampThreads) {
-      const int h = sm.plist[s];
-      feed.stage[h] = __double2float_rd(__dsub_rn((double)feed.stage[h], rep));
+    // penalised entries -> fp32 lower bound of L - rep, in the stage (each
+    // by its owner, which keeps the stored value)
+#pragma unroll
+    for (int q = 0; q < kHistRegs; ++q) {
+      const unsigned v = (own >> (16 * q)) & 0xFFFFu;
+      if (v != 0xFFFFu) {
+        const float x = feed.stage[v];
+        po[q * kSampThreads + threadIdx.x] = x;
+        feed.stage[v] = __double2float_rd(__dsub_rn((double)x, rep));
+      }
     }
     __syncthreads();
 
@@ -1874,7 +1984,8 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
     for (int i = threadIdx.x; i < 256; i += kSampThreads) sm.hist[i] = 0u;
     if (threadIdx.x == 0) sm.ncand = 0;
     if (!__syncthreads_and(ok)) break;
-    pipe_advance(a, pp, bm, words, it, b, feed, hreg, sm.plist);
+    pipe_advance(a, pp, bm, words, it, b, feed, hreg, nullptr, 0, 0, own_tmp);
+    if (b + (int)gridDim.x < a.rows) own_next = (own_tmp[0] & 0xFFFFu) | ((unsigned)own_tmp[1] << 16);
 
     const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
     mx = key_to_float(pp.xkey[par]);
@@ -1890,9 +2001,11 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
       fast = R > 0.f && isfinite(R);
     }
     int bstar = 255;
-    // ---- histogram of the distance below the maximum, 255 bins over [0, R)
+    // ---- histogram of the distance below the maximum, 255 bins over [0, R);
+    // every warp finds the first bin whose running count reaches k
     for (int attempt = 0; fast && attempt < 3 && bstar >= 255; ++attempt) {
       if (attempt > 0) {
+        __syncthreads();
         for (int i = threadIdx.x; i < 256; i += kSampThreads) sm.hist[i] = 0u;
         __syncthreads();
       }
@@ -1906,30 +2019,31 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
         }
       }
       __syncthreads();
-      if (warp == 0) {
-        unsigned int c[8], run = 0;
+      const uint4 h0 = *reinterpret_cast<const uint4 *>(&sm.hist[lane * 8]);
+      const uint4 h1 = *reinterpret_cast<const uint4 *>(&sm.hist[lane * 8 + 4]);
+      const unsigned int run = (h0.x + h0.y) + (h0.z + h0.w) + ((h1.x + h1.y) + (h1.z + h1.w));
+      unsigned int incl = run;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          run += sm.hist[lane * 8 + q];
-          c[q] = run;
-        }
-        unsigned int incl = run;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const unsigned int n = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += n;
-        }
-        const unsigned int before = incl - run;
-        int bs = 255;
-#pragma unroll
-        for (int q = 7; q >= 0; --q)
-          if (before + c[q] >= (unsigned)k) bs = lane * 8 + q;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) bs = min(bs, __shfl_xor_sync(0xffffffffu, bs, o));
-        if (lane == 0) sm.bstar = bs;
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
       }
-      __syncthreads();
-      bstar = sm.bstar;
+      // the first of this lane's bins whose running count reaches k
+      int bs = 255;
+      if (incl >= (unsigned)k) {
+        unsigned int acc = incl - run;
+        const unsigned int hb[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        bs = lane * 8 + 7;
+#pragma unroll
+        for (int q = 0; q < 7; ++q) {
+          acc += hb[q];
+          if (acc >= (unsigned)k) {
+            bs = lane * 8 + q;
+            break;
+          }
+        }
+      }
+      bstar = __reduce_min_sync(0xffffffffu, bs);
       if (bstar >= 255) R *= 8.f;
     }
     fast = fast && bstar < 255;
@@ -1938,11 +2052,27 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
       // bound exceeds mx - (bstar+1) (R/255) (1 + 2^-21), so at least k
       // lower bounds reach g; every entry whose exact value reaches the
       // least of them has a lower bound (its value rounded down) at least
-      // that large, so `g` admits a superset of the top k.
+      // that large, so `g` admits a superset of the top k.  Unpenalised
+      // entries come from the registers, penalised ones (exact value
+      // L - rep) from their owners.
       const double gd = (double)mx - (double)(bstar + 1) * ((double)R / 255.0) * (1.0 + 0x1p-20);
       float g = __double2float_rd(gd);
       g = (g == -INFINITY) ? g : __uint_as_float(g > 0.f ? __float_as_uint(g) - 1u
                                                           : (g == 0.f ? 0x80000001u : __float_as_uint(g) + 1u));
+#pragma unroll
+      for (int q = 0; q < kHistRegs; ++q) {
+        const unsigned v = (own >> (16 * q)) & 0xFFFFu;
+        if (v != 0xFFFFu) {
+          const double val = __dsub_rn((double)po[q * kSampThreads + threadIdx.x], rep);
+          if (__double2float_rd(val) >= g) {
+            const int slot = atomicAdd(&sm.ncand, 1);
+            if (slot < kFastCand) {
+              sm.ckey[slot] = okey64(val);
+              sm.cidx[slot] = (int)v;
+            }
+          }
+        }
+      }
       if (my_mx >= g) {
 #pragma unroll
         for (int i = 0; i < NV4; ++i) {
@@ -1951,13 +2081,11 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const float f = f4_at(r[i], j);
-              if (f >= g) {
-                const int v = v0 + j;
-                const double val = in_set(bits, v) ? __dsub_rn((double)L[v], rep) : (double)f;
+              if (f >= g && !in_set(bits, v0 + j)) {
                 const int slot = atomicAdd(&sm.ncand, 1);
                 if (slot < kFastCand) {
-                  sm.ckey[slot] = okey64(val);
-                  sm.cidx[slot] = v;
+                  sm.ckey[slot] = okey64((double)f);
+                  sm.cidx[slot] = v0 + j;
                 }
               }
             }
@@ -1967,7 +2095,7 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
       __syncthreads();
       const int nc = sm.ncand;
       fast = nc <= kFastCand && nc >= k;
-      if (fast) rank_candidates(sm, nc, k);
+      if (fast) rank_candidates(sm, nc, k, a.T);
     }
     if (!fast) {
       __syncthreads();
@@ -1980,44 +2108,10 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
         continue;
       }
     }
-
-    // ---- src/tensor_ffi_adapter.php:180-204 over the k survivors ----
-    if (a.T < 0.01) {
-      if (threadIdx.x == 0) a.out[b] = sm.order[0];
-      __syncthreads();
-      continue;
-    }
-    double *P = reinterpret_cast<double *>(sm.ckey);
-    double *C = P + kMaxTopK;
-    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = snai_exp(__ddiv_rn(sm.val[i], a.T));
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double s = 0.0;
-      for (int i = 0; i < k; ++i) s = __dadd_rn(s, P[i]);
-      C[0] = s;
-    }
-    __syncthreads();
-    const double sum = C[0];
-    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = __ddiv_rn(P[i], sum);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double cum = 0.0;
-      int nf = 0;
-      for (int i = 0; i < k; ++i) {
-        cum = __dadd_rn(cum, P[i]);
-        C[i] = cum;  // $cum_check after i+1 terms is this same sum
-        nf = i + 1;
-        if (cum >= a.top_p) break;
-      }
-      const double rr = __dmul_rn((double)a.uniforms[b], cum);
-      int id = sm.order[0];
-      for (int i = 0; i < nf; ++i)
-        if (rr <= C[i]) {
-          id = sm.order[i];
-          break;
-        }
-      a.out[b] = id;
-    }
+    // ---- src/tensor_ffi_adapter.php:180-204 over the k survivors, by warp
+    // 0 (the other warps wait at the barrier: letting them run ahead into
+    // the next row measured slower)
+    topp_tail(a, sm, k, b);
     __syncthreads();
   }
 }
@@ -2641,7 +2735,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_b_cluster(const __grid
     if (fast) {
       const int nc = sm.ncand;
       fast = nc <= kFastCand && nc >= k;
-      if (fast) rank_candidates(sm, nc, k);
+      if (fast) rank_candidates(sm, nc, k, a.T);
     }
     if (!fast) {
       // whole-row history bitmap for the general path
@@ -2673,37 +2767,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_b_cluster(const __grid
       __syncthreads();
       continue;
     }
-    double *P = reinterpret_cast<double *>(sm.ckey);
-    double *Cs = P + kMaxTopK;
-    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = snai_exp(__ddiv_rn(sm.val[i], a.T));
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double s = 0.0;
-      for (int i = 0; i < k; ++i) s = __dadd_rn(s, P[i]);
-      Cs[0] = s;
-    }
-    __syncthreads();
-    const double sum = Cs[0];
-    for (int i = threadIdx.x; i < k; i += kSampThreads) P[i] = __ddiv_rn(P[i], sum);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double cum = 0.0;
-      int nf = 0;
-      for (int i = 0; i < k; ++i) {
-        cum = __dadd_rn(cum, P[i]);
-        Cs[i] = cum;
-        nf = i + 1;
-        if (cum >= a.top_p) break;
-      }
-      const double rr = __dmul_rn((double)a.uniforms[b], cum);
-      int id = sm.order[0];
-      for (int i = 0; i < nf; ++i)
-        if (rr <= Cs[i]) {
-          id = sm.order[i];
-          break;
-        }
-      a.out[b] = id;
-    }
+    topp_tail(a, sm, k, b);
     __syncthreads();
   }
   cluster_sync_all();

@@ -129,6 +129,29 @@ def test_ties_and_edge_uniforms(built):
         assert np.array_equal(got, oracle_ids(L, hist, U, *args, hist_len=hist_len))
 
 
+def test_variant_b_tail_edges(built):
+    """Variant B's top-p tail where the warp's certified sums cannot decide
+    and the exact sequential arithmetic takes over: running sums that land
+    on top_p exactly (k equal logits: 1/2, 1/4 steps), exponentials that
+    overflow to inf (PHP then keeps order[0]), u = 1 (r equal to the last
+    running sum), and T exactly at the greedy threshold."""
+    rng = np.random.default_rng(21)
+    R, V = 32, 4096
+    L = rng.normal(0, 1, (R, V)).astype(np.float32)
+    top = rng.choice(V, (R, 4), replace=True)
+    for r in range(R):
+        L[r, top[r]] = 30.0
+    L[8:12, :4] = 800.0  # exp(800 / T) overflows
+    U = rng.random(R).astype(np.float32)
+    U[0::4] = 1.0
+    U[1::4] = 0.5
+    hist = rng.integers(0, V, (R, 64)).astype(np.int32)
+    for T, rep, k, p in [(0.7, 0.0, 2, 0.5), (0.7, 0.0, 4, 0.5), (1.0, 0.0, 4, 1.0), (0.7, 0.0, 4, 0.75),
+                         (0.01, 0.0, 4, 0.9), (0.7, 1.5, 40, 0.9)]:
+        got = gpu_sample(L, hist, U, sample_params(VARIANT_B, T, rep, k, p))
+        assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_B, T, rep, k, p)), (T, rep, k, p)
+
+
 def test_nan_guard_and_argument_errors(built):
     from snai_b200 import CortexError
     rng = np.random.default_rng(1)
