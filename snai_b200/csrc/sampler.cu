@@ -970,30 +970,22 @@ __device__ __forceinline__ int warp_first_ge(const double *C, int i0, int i1, do
   return __reduce_min_sync(0xffffffffu, f);
 }
 
-// src/tensor_ffi_adapter.php:180-204 over the k ranked survivors of row b
-// (sm.order, p in sm.val), by warp 0 alone (the other warps return at once).
-// PHP sums p in order, divides each p by the sum, accumulates the quotients
-// in order until the running sum reaches top_p (crossing term included),
-// takes r = u * cum and returns the first survivor whose running sum reaches
-// r.  The warp computes the same running sums by a tree sum, one reciprocal
-// and a lane-then-warp scan, each within kTailEps of PHP's, and accepts the
+// src/tensor_ffi_adapter.php:180-204 over k ranked survivors (order[0..k),
+// their p in P[0..k)), by one warp; C is scratch for k doubles.  PHP sums p
+// in order, divides each p by the sum, accumulates the quotients in order
+// until the running sum reaches top_p (crossing term included), takes
+// r = u * cum and returns the first survivor whose running sum reaches r.
+// The warp computes the same running sums by a tree sum, one reciprocal and
+// a lane-then-warp scan, each within kTailEps of PHP's, and accepts the
 // result when every decision clears the margin: the first running sum at or
 // above top_p - eps is also at or above top_p + eps (or both are the last),
 // and for r anywhere in the interval this leaves, the first running sum at
 // or above r - eps is also at or above r + eps and lies in the kept prefix.
 // Otherwise (a decision within 1e-12, or p infinite, NaN or all zero) lane 0
-// redoes PHP's sequential arithmetic exactly.  Greedy (T < 0.01) takes
-// order[0].
-__device__ __forceinline__ void topp_tail(const SampArgs &a, SmemB &sm, int k, int b) {
-  if (threadIdx.x >= 32) return;
-  const int lane = threadIdx.x;
-  if (a.T < 0.01) {
-    if (lane == 0) a.out[b] = sm.order[0];
-    return;
-  }
-  const double u = (double)a.uniforms[b];
-  const double *P = sm.val;
-  double *C = reinterpret_cast<double *>(sm.ckey);  // the candidate keys are dead after ranking
+// redoes PHP's sequential arithmetic exactly.  Returns the id on every lane.
+__device__ __forceinline__ int warp_topp(const int *order, const double *P, double *C, int k, double u,
+                                         double top_p) {
+  const int lane = threadIdx.x & 31;
   const int m = (k + 31) >> 5;
   const int i0 = min(k, lane * m), i1 = min(k, i0 + m);
   double part = 0.0;
@@ -1019,13 +1011,12 @@ __device__ __forceinline__ void topp_tail(const SampArgs &a, SmemB &sm, int k, i
       C[i] = c;
     }
     __syncwarp();
-    const double tp = a.top_p;
-    const int jl = min(warp_first_ge(C, i0, i1, tp - kTailEps), k - 1);
-    const int jh = min(warp_first_ge(C, i0, i1, tp + kTailEps), k - 1);
+    const int jl = min(warp_first_ge(C, i0, i1, top_p - kTailEps), k - 1);
+    const int jh = min(warp_first_ge(C, i0, i1, top_p + kTailEps), k - 1);
     const double rl = __dmul_rn(u, C[jl]) - kTailEps, rh = __dmul_rn(u, C[jh]) + kTailEps;
     const int sa = warp_first_ge(C, i0, i1, rl - kTailEps);
     const int sb = warp_first_ge(C, i0, i1, rh + kTailEps);
-    if (sa == sb && sa <= jl) id = sm.order[sa];
+    if (sa == sb && sa <= jl) id = order[sa];
     __syncwarp();
   }
   if (id < 0) {
@@ -1043,18 +1034,34 @@ __device__ __forceinline__ void topp_tail(const SampArgs &a, SmemB &sm, int k, i
         cum = __dadd_rn(cum, C[i]);
         C[i] = cum;
         nf = i + 1;
-        if (cum >= a.top_p) break;
+        if (cum >= top_p) break;
       }
       const double rr = __dmul_rn(u, cum);
-      id = sm.order[0];
+      id = order[0];
       for (int i = 0; i < nf; ++i)
         if (rr <= C[i]) {
-          id = sm.order[i];
+          id = order[i];
           break;
         }
     }
+    id = __shfl_sync(0xffffffffu, id, 0);
+    __syncwarp();
   }
-  if (lane == 0) a.out[b] = id;
+  return id;
+}
+
+// The tail of row b over the CTA's ranked survivors (sm.order, p in sm.val),
+// by warp 0 alone (the other warps return at once).  Greedy (T < 0.01)
+// takes order[0].
+__device__ __forceinline__ void topp_tail(const SampArgs &a, SmemB &sm, int k, int b) {
+  if (threadIdx.x >= 32) return;
+  if (a.T < 0.01) {
+    if (threadIdx.x == 0) a.out[b] = sm.order[0];
+    return;
+  }
+  const double u = (double)a.uniforms[b];
+  const int id = warp_topp(sm.order, sm.val, reinterpret_cast<double *>(sm.ckey), k, u, a.top_p);
+  if (threadIdx.x == 0) a.out[b] = id;
 }
 
 // Fast selection (see the file comment).  The row holds lower bounds (the
@@ -2117,6 +2124,619 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
 }
 
 // ---------------------------------------------------------------------------
+// Streaming variant B: one warp per row, no block barriers.
+//
+// A warp streams its rows' logits through a ring of shared-memory chunks
+// filled by cp.async (kStreamSlots in flight, running on into the warp's
+// next row) and keeps
+// a buffer of candidates whose lower bound lb (the logit, or fp32 round-down
+// of L - rep for a penalised id) reaches a threshold t.  t starts at -inf;
+// when the buffer fills, a radix select over the buffer's lb keys finds its
+// k-th largest lb, which becomes t, and the buffer keeps the entries at or
+// above it.  t never exceeds the row's k-th largest lb, and every entry of
+// the top k by exact value (L or L - rep, in double) has lb >= t, so the
+// buffer always holds the top k.  At the row's end a last select cuts the
+// buffer to the entries at or above the k-th largest lb, those are ranked
+// by (exact value descending, id ascending) and the warp runs the top-p tail.
+// Rows whose candidates cannot be cut (more ties than the buffer holds, or
+// fewer than k comparable entries, e.g. NaN) take an exact warp-level radix
+// select over 64-bit keys of the exact values, streaming the row again.
+//
+// History ids reach a per-warp stage by 4-byte cp.async copies issued one
+// row ahead; at a row's start they are marked in the warp's bitmap.
+// ---------------------------------------------------------------------------
+
+constexpr int kStreamCap = 512;       // candidate buffer entries per warp
+constexpr int kStreamSlots = 2;       // staged chunks in flight per warp
+constexpr int kStreamPer = 8;         // 16-byte words per lane per chunk
+constexpr int kStreamChunk = 32 * kStreamPer;  // 16-byte words per chunk
+static_assert(kStreamPer * 4 <= 64, "one mask bit per staged entry of a lane");
+constexpr int kStreamHistMax = 1024;  // history ids staged per warp
+constexpr int kStreamMaxK = 256;      // top-k the buffer supports
+constexpr int kStreamWarps = 20;      // warps per CTA at most
+
+// Per-warp shared-memory carve (the same on host and device); every region
+// starts on a 16-byte boundary (cp.async destinations, uint4 reads).
+struct StreamLayout {
+  int words, hist_cap;
+  unsigned off_val, off_bm, off_id, off_rh, off_hs, off_p, off_ord, bytes;  // ring at 0
+};
+__host__ __device__ inline StreamLayout stream_layout(int V, int hist_cols, int k) {
+  auto up16 = [](unsigned x) { return (x + 15u) & ~15u; };
+  StreamLayout L;
+  L.words = (V + 31) / 32;
+  L.hist_cap = (hist_cols + 31) & ~31;
+  unsigned o = up16(kStreamSlots * kStreamChunk * 16);  // staged chunks
+  L.off_val = o;
+  o = up16(o + kStreamCap * 8);  // double values (then 64-bit keys, then running sums)
+  L.off_bm = o;
+  o = up16(o + (unsigned)L.words * 4u);
+  L.off_id = o;
+  o = up16(o + kStreamCap * 4);
+  L.off_rh = o;
+  o = up16(o + 256 * 4);
+  L.off_hs = o;
+  o = up16(o + (unsigned)L.hist_cap * 4u);
+  L.off_p = o;
+  o = up16(o + (unsigned)k * 8u);
+  L.off_ord = o;
+  o = up16(o + (unsigned)k * 4u);
+  L.bytes = o;
+  return L;
+}
+
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Largest digit d with (count of keys whose digit is >= d) >= need, from a
+// 256-bin histogram; `above` = count of digits > d.  -1 if all bins hold
+// fewer than `need`.  Every lane returns the same values.
+__device__ __forceinline__ int warp_top_digit(const unsigned *rh, unsigned need, unsigned &above) {
+  const int lane = threadIdx.x & 31;
+  const uint4 h0 = reinterpret_cast<const uint4 *>(rh)[lane * 2];
+  const uint4 h1 = reinterpret_cast<const uint4 *>(rh)[lane * 2 + 1];
+  const unsigned b[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  const unsigned sum = ((b[0] + b[1]) + (b[2] + b[3])) + ((b[4] + b[5]) + (b[6] + b[7]));
+  unsigned incl = sum;  // this lane's bins and every higher lane's
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned n = __shfl_down_sync(0xffffffffu, incl, o);
+    if (lane + o < 32) incl += n;
+  }
+  int d = -1;
+  unsigned ab = 0u;
+  if (incl >= need && incl - sum < need) {
+    unsigned acc = incl - sum;
+#pragma unroll
+    for (int q = 7; q >= 0; --q) {
+      if (d < 0 && acc + b[q] >= need) {
+        d = lane * 8 + q;
+        ab = acc;
+      }
+      acc += b[q];
+    }
+  }
+  d = __reduce_max_sync(0xffffffffu, d);
+  above = d >= 0 ? __shfl_sync(0xffffffffu, ab, d >> 3) : 0u;
+  return d;
+}
+
+__device__ __forceinline__ unsigned lb_key(double val) { return okey32(__double2float_rd(val)); }
+
+// Cuts the buffer to the entries whose lb key has the top 16 bits of the
+// k-th largest or more (two 8-bit radix rounds); returns the new count
+// (>= k) and sets t to the lowest float of that 16-bit bucket.  Needs
+// cnt >= k.
+__device__ __noinline__ int stream_compact(double *bval, int *bid, unsigned *rh, int cnt, int k, float &t) {
+  const int lane = threadIdx.x & 31;
+  unsigned prefix = 0u, need = (unsigned)k;
+  for (int shift = 24; shift >= 16; shift -= 8) {
+    for (int i = lane; i < 256; i += 32) rh[i] = 0u;
+    __syncwarp();
+    const unsigned hm = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+    for (int i = lane; i < cnt; i += 32) {
+      const unsigned key = lb_key(bval[i]);
+      if ((key & hm) == (prefix & hm)) atomicAdd(&rh[(key >> shift) & 255u], 1u);
+    }
+    __syncwarp();
+    unsigned above;
+    const int d = warp_top_digit(rh, need, above);
+    __syncwarp();
+    need -= above;
+    prefix |= (unsigned)d << shift;
+  }
+  int w = 0;
+  for (int i0 = 0; i0 < cnt; i0 += 32) {
+    const int i = i0 + lane;
+    double v = 0.0;
+    int id = 0;
+    bool keep = false;
+    if (i < cnt) {
+      v = bval[i];
+      id = bid[i];
+      keep = lb_key(v) >= prefix;
+    }
+    __syncwarp();
+    const unsigned m = __ballot_sync(0xffffffffu, keep);
+    if (keep) {
+      const int slot = w + __popc(m & ((1u << lane) - 1u));
+      bval[slot] = v;
+      bid[slot] = id;
+    }
+    w += __popc(m);
+    __syncwarp();
+  }
+  t = key_to_float(prefix);
+  if (t != t) t = -INFINITY;  // the bucket of -inf starts at NaN patterns
+  return w;
+}
+
+// Raw-logit threshold admitting every entry with lb >= t.
+__device__ __forceinline__ float stream_traw(float t, double rep) {
+  if (rep >= 0.0 || t == -INFINITY) return t;
+  const double x = (double)t + rep - 0x1p-50 * (fabs((double)t) + fabs(rep));
+  const float f = __double2float_rd(x);
+  return f == -INFINITY ? f : __uint_as_float(f > 0.f ? __float_as_uint(f) - 1u
+                                                      : (f == 0.f ? 0x80000001u : __float_as_uint(f) + 1u));
+}
+
+struct StreamState {
+  int cnt;
+  int ovf;
+  float t, traw;
+};
+
+// Entries of this lane's chunk words marked in `bits` (bit 4r + j: word r,
+// element j; a superset of those with raw logit >= traw) whose lb reaches t
+// join the buffer.  Slots come from one warp scan; a batch that does not fit
+// is taken word by word, the buffer cut whenever the next word could
+// overflow it.  rf: the staged chunk, c0: its first word.
+__device__ __forceinline__ unsigned long long stream_filter(const float *rf, unsigned long long bits, int c0,
+                                                            const uint32_t *bm, double rep, float t) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long keep = 0ull;
+  while (bits) {
+    const int b = __ffsll((long long)bits) - 1;
+    bits &= bits - 1ull;
+    const int r = b >> 2, j = b & 3;
+    const float f = rf[(32 * r + lane) * 4 + j];
+    const int v = (c0 + 32 * r + lane) * 4 + j;
+    const double val = in_set(bm, v) ? __dsub_rn((double)f, rep) : (double)f;
+    if (__double2float_rd(val) >= t) keep |= 1ull << b;
+  }
+  return keep;
+}
+__device__ __forceinline__ void stream_write(const float *rf, unsigned long long keep, int c0, int slot,
+                                             const uint32_t *bm, double rep, double *bval, int *bid) {
+  const int lane = threadIdx.x & 31;
+  while (keep) {
+    const int b = __ffsll((long long)keep) - 1;
+    keep &= keep - 1ull;
+    const int r = b >> 2, j = b & 3;
+    const float f = rf[(32 * r + lane) * 4 + j];
+    const int v = (c0 + 32 * r + lane) * 4 + j;
+    bval[slot] = in_set(bm, v) ? __dsub_rn((double)f, rep) : (double)f;
+    bid[slot] = v;
+    ++slot;
+  }
+}
+__device__ __forceinline__ int warp_excl_scan(int c, int &tot) {
+  const int lane = threadIdx.x & 31;
+  int incl = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  tot = __shfl_sync(0xffffffffu, incl, 31);
+  return incl - c;
+}
+__device__ __forceinline__ void stream_take(const float *rf, unsigned long long bits, int c0, StreamState &st,
+                                            double *bval, int *bid, const uint32_t *bm, unsigned *rh, int k,
+                                            double rep, int cut_at) {
+  if (st.ovf) return;
+  unsigned long long keep = stream_filter(rf, bits, c0, bm, rep, st.t);
+  int tot;
+  int ex = warp_excl_scan(__popcll(keep), tot);
+  if (st.cnt + tot <= kStreamCap) {
+    stream_write(rf, keep, c0, st.cnt + ex, bm, rep, bval, bid);
+    st.cnt += tot;
+  } else {
+#pragma unroll 1
+    for (int r = 0; r < kStreamPer; ++r) {
+      unsigned long long kr = keep & (0xFull << (4 * r));
+      if (st.cnt > kStreamCap - 128) {
+        st.cnt = stream_compact(bval, bid, rh, st.cnt, k, st.t);
+        st.traw = stream_traw(st.t, rep);
+        if (st.cnt > kStreamCap - 128) {
+          st.ovf = 1;
+          return;
+        }
+        kr = stream_filter(rf, kr, c0, bm, rep, st.t);
+      }
+      ex = warp_excl_scan(__popcll(kr), tot);
+      stream_write(rf, kr, c0, st.cnt + ex, bm, rep, bval, bid);
+      st.cnt += tot;
+    }
+  }
+  if (st.cnt > cut_at) {
+    st.cnt = stream_compact(bval, bid, rh, st.cnt, k, st.t);
+    st.traw = stream_traw(st.t, rep);
+    if (st.cnt > kStreamCap - 128) st.ovf = 1;
+  }
+}
+
+// A row whose buffer came up short: two radix rounds over the row's lb keys
+// find the 16-bit bucket of the k-th largest, and the entries at or above
+// it are gathered (exact values) into the buffer.  Returns their count, or
+// 0 if they do not fit (or the row has fewer than k comparable entries).
+__device__ __noinline__ int stream_regather(const float *Lrow, int V, const uint32_t *bm, double *bval, int *bid,
+                                            unsigned *rh, int k, double rep) {
+  const int lane = threadIdx.x & 31;
+  const int n4 = V >> 2;
+  const float4 *L4 = reinterpret_cast<const float4 *>(Lrow);
+  auto val_of = [&](float f, int v) { return in_set(bm, v) ? __dsub_rn((double)f, rep) : (double)f; };
+  unsigned prefix = 0u, need = (unsigned)k;
+  for (int shift = 24; shift >= 16; shift -= 8) {
+    for (int i = lane; i < 256; i += 32) rh[i] = 0u;
+    __syncwarp();
+    const unsigned hm = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+    for (int idx = lane; idx < n4; idx += 32) {
+      const float4 x = __ldg(L4 + idx);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float f = f4_at(x, j);
+        if (f == f) {
+          const unsigned key = lb_key(val_of(f, idx * 4 + j));
+          if ((key & hm) == (prefix & hm)) atomicAdd(&rh[(key >> shift) & 255u], 1u);
+        }
+      }
+    }
+    __syncwarp();
+    unsigned above;
+    const int d = warp_top_digit(rh, need, above);
+    __syncwarp();
+    if (d < 0) return 0;
+    need -= above;
+    prefix |= (unsigned)d << shift;
+  }
+  int cnt = 0;
+  for (int idx0 = 0; idx0 < n4; idx0 += 32) {
+    const int idx = idx0 + lane;
+    float4 x = make_float4(NAN, NAN, NAN, NAN);
+    if (idx < n4) x = __ldg(L4 + idx);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float f = f4_at(x, j);
+      const double val = val_of(f, idx * 4 + j);
+      const bool take = f == f && lb_key(val) >= prefix;
+      const unsigned m = __ballot_sync(0xffffffffu, take);
+      const int slot = cnt + __popc(m & ((1u << lane) - 1u));
+      if (take && slot < kStreamCap) {
+        bval[slot] = val;
+        bid[slot] = idx * 4 + j;
+      }
+      cnt += __popc(m);
+    }
+  }
+  __syncwarp();
+  return cnt <= kStreamCap ? cnt : 0;
+}
+
+// Exact top-k of a row by a radix select over 64-bit keys of the exact
+// values (the row streamed once per digit), then the entries above the k-th
+// key and, of those equal to it, the first in id order, gathered in id
+// order: exactly k entries.  Returns k, or 0 if the row has fewer entries.
+__device__ __noinline__ int stream_exact(const float *Lrow, int V, const uint32_t *bm, double *bval, int *bid,
+                                         unsigned *rh, int k, double rep) {
+  const int lane = threadIdx.x & 31;
+  const int n4 = V >> 2;
+  const float4 *L4 = reinterpret_cast<const float4 *>(Lrow);
+  auto key_of = [&](float f, int v) { return okey64(in_set(bm, v) ? __dsub_rn((double)f, rep) : (double)f); };
+  unsigned long long prefix = 0ull;
+  unsigned need = (unsigned)k;
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int i = lane; i < 256; i += 32) rh[i] = 0u;
+    __syncwarp();
+    const unsigned long long hm = shift == 56 ? 0ull : (~0ull << (shift + 8));
+    for (int idx = lane; idx < n4; idx += 32) {
+      const float4 x = __ldg(L4 + idx);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const unsigned long long key = key_of(f4_at(x, j), idx * 4 + j);
+        if ((key & hm) == (prefix & hm)) atomicAdd(&rh[(unsigned)(key >> shift) & 255u], 1u);
+      }
+    }
+    __syncwarp();
+    unsigned above;
+    const int d = warp_top_digit(rh, need, above);
+    __syncwarp();
+    if (d < 0) return 0;
+    need -= above;
+    prefix |= (unsigned long long)d << shift;
+  }
+  // `need` entries equal to the k-th key are taken, in id order
+  int cnt = 0;
+  unsigned eq_left = need;
+  for (int idx0 = 0; idx0 < n4; idx0 += 32) {
+    const int idx = idx0 + lane;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (idx < n4) x = __ldg(L4 + idx);
+    unsigned long long key[4];
+    int gt = 0, eq = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      key[j] = idx < n4 ? key_of(f4_at(x, j), idx * 4 + j) : 0ull;
+      const bool valid = idx < n4;
+      gt += valid && key[j] > prefix;
+      eq += valid && key[j] == prefix;
+    }
+    int eq_ex = eq, take_ex;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, eq_ex, o);
+      if (lane >= o) eq_ex += n;
+    }
+    const int eq_tot = __shfl_sync(0xffffffffu, eq_ex, 31);
+    eq_ex -= eq;  // equal entries before this lane's
+    int take = gt;
+    {
+      int e = eq_ex;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (idx < n4 && key[j] == prefix) {
+          take += (unsigned)e < eq_left;
+          ++e;
+        }
+    }
+    take_ex = take;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, take_ex, o);
+      if (lane >= o) take_ex += n;
+    }
+    const int take_tot = __shfl_sync(0xffffffffu, take_ex, 31);
+    int slot = cnt + take_ex - take;
+    int e = eq_ex;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (idx < n4) {
+        const int v = idx * 4 + j;
+        bool t = key[j] > prefix;
+        if (key[j] == prefix) {
+          t = (unsigned)e < eq_left;
+          ++e;
+        }
+        if (t) {
+          bval[slot] = key_to_double(key[j]);
+          bid[slot] = v;
+          ++slot;
+        }
+      }
+    }
+    cnt += take_tot;
+    eq_left -= (unsigned)min(eq_tot, (int)eq_left);
+    __syncwarp();
+  }
+  return cnt;
+}
+
+// Row end: cut, rank, top-p tail; writes out[b].
+__device__ __noinline__ void stream_finish(const SampArgs &a, int b, StreamState st, double *bval, int *bid,
+                                           const uint32_t *bm, unsigned *rh, double *P, int *ord, int k) {
+  const int lane = threadIdx.x & 31;
+  int M = 0;
+  if (!st.ovf && st.cnt >= k) {
+    float t = st.t;
+    M = stream_compact(bval, bid, rh, st.cnt, k, t);
+  } else {
+    const float *Lrow = a.logits + (size_t)row_of(a, b) * a.ld;
+    M = st.ovf ? 0 : stream_regather(Lrow, a.V, bm, bval, bid, rh, k, a.rep);
+    if (M < k) M = stream_exact(Lrow, a.V, bm, bval, bid, rh, k, a.rep);
+    if (M < k) {
+      if (lane == 0) {
+        a.out[b] = -2;
+        record_error(a.err, kErrSamplerArgs);
+      }
+      return;
+    }
+  }
+  // exact order keys in place, then ranks (value descending, id ascending)
+  unsigned long long *bkey = reinterpret_cast<unsigned long long *>(bval);
+  for (int i = lane; i < M; i += 32) bkey[i] = okey64(bval[i]);
+  __syncwarp();
+  const bool want_p = !(a.T < 0.01);
+  for (int i = lane; i < M; i += 32) {
+    const unsigned long long ki = bkey[i];
+    const int vi = bid[i];
+    int rank = 0;
+#pragma unroll 4
+    for (int j = 0; j < M; ++j) {
+      const unsigned long long kj = bkey[j];
+      const int vj = bid[j];
+      rank += (int)((kj > ki) | ((kj == ki) & (vj < vi)));
+    }
+    if (rank < k) {
+      ord[rank] = vi;
+      const double val = key_to_double(ki);
+      P[rank] = want_p ? snai_exp(__ddiv_rn(val, a.T)) : val;
+    }
+  }
+  __syncwarp();
+  int id;
+  if (!want_p) {
+    id = ord[0];
+  } else {
+    const double u = (double)a.uniforms[b];
+    id = warp_topp(ord, P, bval, k, u, a.top_p);
+  }
+  if (lane == 0) a.out[b] = id;
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __grid_constant__ SampArgs a, int W) {
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int V = a.V, n4 = V >> 2, S = (n4 + kStreamChunk - 1) / kStreamChunk;
+  const int k = a.T < 0.01 ? 1 : min(a.top_k, V);
+  const StreamLayout Ly = stream_layout(V, a.hist_cols, k);
+  uint8_t *base = smem_dyn + (size_t)warp * Ly.bytes;
+  float4 *ring = reinterpret_cast<float4 *>(base);
+  double *bval = reinterpret_cast<double *>(base + Ly.off_val);
+  uint32_t *bm = reinterpret_cast<uint32_t *>(base + Ly.off_bm);
+  int *bid = reinterpret_cast<int *>(base + Ly.off_id);
+  unsigned *rh = reinterpret_cast<unsigned *>(base + Ly.off_rh);
+  int *hs = reinterpret_cast<int *>(base + Ly.off_hs);
+  double *P = reinterpret_cast<double *>(base + Ly.off_p);
+  int *ord = reinterpret_cast<int *>(base + Ly.off_ord);
+  const int NW = gridDim.x * W, gw = blockIdx.x * W + warp;
+  if (warp >= W || gw >= a.rows) return;
+  const int nrows = (a.rows - 1 - gw) / NW + 1;
+  const bool has_hist = a.hist != nullptr && a.hist_cols > 0;
+  // logits / history row of the warp's i-th row (-1 past the last)
+  auto mrow_of = [&](int i) -> int { return i < nrows ? row_of(a, gw + i * NW) : -1; };
+  // history of a row -> stage (its count returned)
+  auto stage = [&](int mrow) -> int {
+    if (!has_hist || mrow < 0) return 0;
+    const int *hr = a.hist + (size_t)mrow * a.hist_ld;
+    for (int c = lane; c < a.hist_cols; c += 32) cp_async4(hs + c, hr + c);
+    cp_async_commit();
+    const int n = a.hist_len ? a.hist_len[mrow] : a.hist_cols;
+    return min(max(n, 0), a.hist_cols);
+  };
+  for (int w = lane; w < Ly.words; w += 32) bm[w] = 0u;
+  __syncwarp();
+  int mp = mrow_of(0), mq = mrow_of(1);
+  // the first row's history is marked before any chunk is staged
+  int hn = stage(mp);
+  auto mark = [&]() {
+    for (int c = lane; c < hn; c += 32) {
+      const int t = hs[c];
+      if (t >= 0 && t < V) atomicOr(&bm[t >> 5], 1u << (t & 31));
+    }
+    __syncwarp();
+  };
+  if (has_hist) {
+    cp_async_wait<0>();
+    __syncwarp();
+    mark();
+    hn = stage(mq);
+  }
+
+  // Chunk q of the warp's stream (row q / S, chunk q % S of it) is staged
+  // in slot q % kStreamSlots, each lane copying (cp.async, one group per
+  // chunk) and later reading the same two 16-byte words; the copy position
+  // (pi, ps) runs kStreamSlots chunks ahead of the consumed one, and mq,
+  // the row after pi, is loaded a whole row before it is needed.
+  int pi = 0, ps = 0;
+  const float4 *Lp = mp >= 0 ? reinterpret_cast<const float4 *>(a.logits + (size_t)mp * a.ld) : nullptr;
+  auto issue = [&](int slot) {
+    if (Lp != nullptr) {
+      const int c0 = ps * kStreamChunk + lane;
+#pragma unroll
+      for (int r = 0; r < kStreamPer; ++r)
+        if (c0 + 32 * r < n4) cp_async16(ring + slot * kStreamChunk + 32 * r + lane, Lp + c0 + 32 * r);
+    }
+    cp_async_commit();
+    if (++ps == S) {
+      ps = 0;
+      ++pi;
+      Lp = mq >= 0 ? reinterpret_cast<const float4 *>(a.logits + (size_t)mq * a.ld) : nullptr;
+      mq = mrow_of(pi + 1);
+    }
+  };
+  for (int q = 0; q < kStreamSlots; ++q) issue(q);
+
+  StreamState st{0, 0, -INFINITY, -INFINITY};
+  // the buffer is cut once it holds more than cut_at entries (at most
+  // kStreamCap - 128, so one more chunk word per lane always fits)
+  const int cut_at = kStreamCap - 128;
+  // G groups of gl lanes for the opening threshold: one group (the chunk's
+  // maximum, a true bound) for k = 1; else G >= 8 groups and G >= 2.5 x
+  // (x = top-k entries expected in one chunk), so that for a row in random
+  // order a group maximum exceeds the k-th largest with probability
+  // 1 - exp(-x/G) <= 1/3 and all G of them do so in ~1e-4 of the rows (those
+  // take the three-pass path).  G >= k makes it a true bound.
+  int gl = 32;
+  if (k > 1) {
+    const float x = (float)k * (float)(kStreamChunk * 4) / (float)V;
+    int G = 8;
+    while (G < 32 && G < k && (float)G < 2.5f * x) G <<= 1;
+    gl = 32 / G;
+  }
+  const long long total = (long long)nrows * S;
+  int ci = 0, cs = 0;
+  for (long long q = 0; q < total; ++q) {
+    const int slot = (int)(q % kStreamSlots);
+    cp_async_wait<kStreamSlots - 1>();  // this chunk (and row ci's history, staged a row ago)
+    if (cs == 0 && ci > 0 && has_hist) {
+      // mark row ci's history, then stage row ci + 1's
+      if (S < kStreamSlots) cp_async_wait<0>();
+      __syncwarp();
+      mark();
+      hn = stage(pi == ci ? mq : mrow_of(ci + 1));
+    }
+    const int c0 = cs * kStreamChunk;
+    const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    float4 x[kStreamPer];
+    float m = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kStreamPer; ++r) {
+      x[r] = c0 + 32 * r + lane < n4 ? ring[slot * kStreamChunk + 32 * r + lane] : ninf;
+      m = fmaxf(m, fmax4(x[r]));
+    }
+    if (cs == 0) {
+      // Opening threshold: the least of G group maxima of the row's first
+      // chunk.  At least G entries reach it; when fewer than k entries end
+      // up at or above it, the row is redone exactly (rows where it lands
+      // above the k-th largest: ~1e-4 for the group count chosen).
+      float g = m;
+      for (int o = 1; o < gl; o <<= 1) g = fmaxf(g, __shfl_xor_sync(0xffffffffu, g, o));
+      for (int o = gl; o < 32; o <<= 1) g = fminf(g, __shfl_xor_sync(0xffffffffu, g, o));
+      if (!(g == g)) g = -INFINITY;
+      // a penalised group maximum has lb >= raw - rep
+      if (a.rep > 0.0 && g != -INFINITY) {
+        const float f = __double2float_rd((double)g - a.rep);
+        g = f == -INFINITY ? f : __uint_as_float(f > 0.f ? __float_as_uint(f) - 1u
+                                                         : (f == 0.f ? 0x80000001u : __float_as_uint(f) + 1u));
+      }
+      st.t = g;
+      st.traw = stream_traw(g, a.rep);
+    }
+    if (__any_sync(0xffffffffu, m >= st.traw)) {
+      unsigned long long bits = 0ull;
+#pragma unroll
+      for (int r = 0; r < kStreamPer; ++r) {
+        const bool valid = c0 + 32 * r + lane < n4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (valid && f4_at(x[r], j) >= st.traw) bits |= 1ull << (4 * r + j);
+      }
+      stream_take(reinterpret_cast<const float *>(ring + slot * kStreamChunk), bits, c0, st, bval, bid, bm, rh, k,
+                  a.rep, cut_at);
+    }
+    issue(slot);  // the slot's next chunk (this lane's words were read above)
+    if (++cs == S) {
+      stream_finish(a, gw + ci * NW, st, bval, bid, bm, rh, P, ord, k);
+      for (int w = lane; w < Ly.words; w += 32) bm[w] = 0u;
+      __syncwarp();
+      st = StreamState{0, 0, -INFINITY, -INFINITY};
+      cs = 0;
+      ++ci;
+    }
+  }
+  cp_async_wait<0>();
+}
+
+// ---------------------------------------------------------------------------
 // Cluster kernels: rows longer than one CTA's register row.  A cluster of C
 // CTAs (C = ceil(V / 32768), at most 8) takes a row; CTA r holds the ids
 // [32768 r, 32768 (r + 1)) in registers through the same staged-row
@@ -2918,6 +3538,30 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   a.nan_guard = s.nan_guard;
   a.out = s.out_ids;
   a.err = s.err;
+  // variant B over 16-byte aligned rows: the streaming kernel, one warp per row
+  if (s.variant != 0 && (s.V & 3) == 0 && (s.ld & 3) == 0 && (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 &&
+      s.hist_cols <= kStreamHistMax) {
+    const int kk = s.temperature < 0.01 ? 1 : std::min(s.top_k, s.V);
+    const StreamLayout Ly = stream_layout(s.V, s.hist_cols, kk);
+    const int W = std::min<int>(kStreamWarps, (int)((227u * 1024u) / Ly.bytes));
+    if (kk <= kStreamMaxK && W >= 2) {
+      static unsigned long long done = 0;
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (!(done & (1ull << dev))) {
+        cudaFuncSetAttribute(sample_b_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        done |= 1ull << dev;
+      }
+      const int grid = std::min(sm_count(), (s.rows + W - 1) / W);
+      sample_b_stream<<<grid, W * 32, (size_t)W * Ly.bytes, stream>>>(a, W);
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) {
+        set_error("sampler launch failed: %s", cudaGetErrorString(e));
+        return -4;
+      }
+      return 0;
+    }
+  }
   const size_t bitmap = ((size_t)((s.V + 31) / 32) * 4 + 15) & ~(size_t)15;
   const int layers = (s.V + kSegLen - 1) / kSegLen;
   // register rows: whole 16-byte chunks from 16-byte aligned row starts, and

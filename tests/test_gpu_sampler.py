@@ -152,6 +152,28 @@ def test_variant_b_tail_edges(built):
         assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_B, T, rep, k, p)), (T, rep, k, p)
 
 
+def test_variant_b_ordered_and_clustered_rows(built):
+    """Rows whose largest logits all sit at the start (descending order) or
+    the end (ascending), rows where a few hundred entries share the top
+    values, and rows with NaN and -inf entries: the opening threshold of
+    the one-warp-per-row kernel is then far off, and the row is regathered
+    or selected exactly."""
+    rng = np.random.default_rng(31)
+    R, V = 16, 16384
+    L = rng.normal(0, 2, (R, V)).astype(np.float32)
+    L[0:4] = -np.sort(-L[0:4], axis=1)
+    L[4:8] = np.sort(L[4:8], axis=1)
+    L[8:10, rng.choice(V, 300, replace=False)] = 9.5
+    L[10, ::7] = np.nan
+    L[11, ::3] = -np.inf
+    L[12, :V - 20] = np.nan
+    U = rng.random(R).astype(np.float32)
+    hist = rng.integers(0, V, (R, 128)).astype(np.int32)
+    for T, rep, k, p in [(0.7, 1.1, 50, 0.95), (0.0, 1.1, 40, 0.9), (1.3, 0.0, 128, 0.99), (0.7, -0.5, 40, 0.9)]:
+        got = gpu_sample(L, hist, U, sample_params(VARIANT_B, T, rep, k, p))
+        assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_B, T, rep, k, p)), (T, rep, k, p)
+
+
 def test_nan_guard_and_argument_errors(built):
     from snai_b200 import CortexError
     rng = np.random.default_rng(1)
