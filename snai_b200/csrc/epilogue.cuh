@@ -38,6 +38,18 @@ struct EpiQKV {
   // decode step's rows, all at one position, would otherwise hammer one
   // table row from every SM at once)
   float *kvs;
+  // tma != 0 (staging mode with att_ch == D): q [M][att_ch] and the staging
+  // buffer [M][2 att_ch] as fp32 tensors (16 x 32 boxes, 64-byte swizzle);
+  // the drains store their runs by TMA
+  int tma;
+  CUtensorMap tq, tkv;
+
+  static constexpr bool kTmaStore = true;
+  __device__ __forceinline__ const CUtensorMap *tma_out(int n, int &x) const {
+    if (!tma) return nullptr;
+    x = n < D ? n : n - D;
+    return n < D ? &tq : &tkv;
+  }
 
   __device__ __forceinline__ float *kv_dst(const RowDesc &rd, int m, int part, int head, int j) const {
     if (kvs) return kvs + ((size_t)m * 2 + (part - 1)) * att_ch + (size_t)head * hs + j;
@@ -141,6 +153,7 @@ struct EpiResidual {
   // TMA reduce-adds (the add happens at L2, the SM does not wait for h)
   CUtensorMap tmap;
   static constexpr bool kTmaReduce = true;
+  static constexpr bool kTmaStore = false;
   using Pre = float4;
   struct Row {};
   __device__ __forceinline__ Row row(int) const { return Row{}; }
@@ -191,15 +204,20 @@ struct EpiResidual {
   }
 };
 
-// u = SiLU(C) = C * (1 / (1 + exp(-C)))  (core/cortex.nim:545-548)
+// u = SiLU(C) = C * (1 / (1 + exp(-C)))  (core/cortex.nim:545-548).  A bf16
+// u (the BF16 tensor-core mode) is rounded to 8 bits of mantissa, so there
+// the exponential and the quotient are the hardware approximations (a few
+// fp32 ulps, far below the bf16 rounding); an fp32 u keeps the IEEE steps.
 template <typename TA>
 struct EpiSilu {
   TA *u;
   int ld;
   __device__ static __forceinline__ float silu(float x) {
+    if constexpr (sizeof(TA) == 2) return __fdividef(x, __fadd_rn(1.0f, __expf(-x)));
     return __fmul_rn(x, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))));
   }
   static constexpr bool kTmaReduce = false;
+  static constexpr bool kTmaStore = false;
   struct Pre {};
   struct Row {};
   __device__ __forceinline__ Row row(int) const { return Row{}; }
@@ -254,6 +272,7 @@ struct EpiLogits {
   const int2 *outrows;  // chunk-local logits row -> (chunk row, slot)
   long long ld;
   static constexpr bool kTmaReduce = false;
+  static constexpr bool kTmaStore = false;
   struct Pre {};
   using Row = int;
   __device__ __forceinline__ Row row(int m) const { return outrows[m].y; }

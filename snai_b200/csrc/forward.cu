@@ -412,6 +412,34 @@ static bool residual_epi(Engine &e, int M, EpiResidual *r) {
   return true;
 }
 
+// TMA stores for the QKV drains when K and V go to the staging buffer and
+// every channel is an attention channel: q as [M][att_ch], the staging
+// buffer as [M][2 att_ch], fp32, 16 x 32 boxes, 64-byte swizzle.  Leaves the
+// plain stores on any failure.
+static void qkv_tma_maps(Engine &e, int M, EpiQKV *q) {
+  q->tma = 0;
+  if (q->kvs == nullptr || e.d.att_ch != e.d.D || (e.d.att_ch & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(e.q) & 15) != 0 || (reinterpret_cast<uintptr_t>(e.kvs) & 15) != 0)
+    return;
+  auto enc = get_encode_fn();
+  if (!enc) return;
+  cuuint32_t box[2] = {16, 32};
+  cuuint32_t estr[2] = {1, 1};
+  cuuint64_t dq[2] = {(cuuint64_t)e.d.att_ch, (cuuint64_t)M};
+  cuuint64_t sq[1] = {(cuuint64_t)e.d.att_ch * 4};
+  cuuint64_t dk[2] = {(cuuint64_t)e.d.att_ch * 2, (cuuint64_t)M};
+  cuuint64_t sk[1] = {(cuuint64_t)e.d.att_ch * 8};
+  if (enc(&q->tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, e.q, dq, sq, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return;
+  if (enc(&q->tkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, e.kvs, dk, sk, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return;
+  q->tma = 1;
+}
+
 static bool tc_path(const Engine &e, int M) {
   return e.precision != kFP32 && M >= 64 && e.d.D % 16 == 0 && e.d.D >= 64;
 }
@@ -580,6 +608,7 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
     const LayerWeights &w = e.layers[l];
     EpiQKV eq{e.rows_d, e.q, e.kv, e.rope, d.D, d.att_ch, d.hs, e.kv_slot_stride, (size_t)l * e.kv_layer_stride,
               e.kv_part_stride, e.kv_head_stride, defer ? e.kvs : nullptr};
+    if (tc_path(e, M)) qkv_tma_maps(e, M, &eq);
     int rc = project(e, kProfQKV, M, 3 * d.D, d.D, x, w.wqkv, w.wqkv_h, eq, 3.0 * M * d.att_ch * 4);
     if (rc) return rc;
     launch_attention<TA>(e, M, l, att, kv_positions, defer);

@@ -118,6 +118,14 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *tmap, const
                : "memory");
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
+// TMA store of a staged 32-row x 16-column fp32 run to the tensor at (x, y).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *tmap, const float *stg, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(smem_u32(stg)), "r"(x), "r"(y)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
@@ -155,6 +163,23 @@ __device__ __forceinline__ void drain_accumulator(uint32_t tbase, int row0, int 
       __syncwarp();
       if (lane == 0 && row0 < M) tma_reduce_add_2d(&epi.tmap, stg, n0 + c, row0);
     } else {
+    // runs the epilogue stores by TMA (same staging; the run's tensor and
+    // column come from the epilogue)
+    int tx = 0;
+    const CUtensorMap *tm = nullptr;
+    if constexpr (Epi::kTmaStore) tm = epi.tma_out(n0 + c, tx);
+    if (tm != nullptr) {
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch)
+        buf[lane * 4 + (ch ^ ((lane >> 1) & 3))] =
+            make_float4(__uint_as_float(r[c + 4 * ch]), __uint_as_float(r[c + 4 * ch + 1]),
+                        __uint_as_float(r[c + 4 * ch + 2]), __uint_as_float(r[c + 4 * ch + 3]));
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0 && row0 < M) tma_store_2d(tm, stg, tx, row0);
+    } else {
     // this run's reads (residual) go out first and overlap the transpose
     typename Epi::Pre pre[4];
 #pragma unroll
@@ -183,10 +208,11 @@ __device__ __forceinline__ void drain_accumulator(uint32_t tbase, int row0, int 
       if (m < M && n < N) epi.store4(m, n, v[i], min(4, N - n), pre[i], ri);
     }
     }
+    }
   }
   }
-  if constexpr (Epi::kTmaReduce) {
-    if (lane == 0) bulk_wait_all();  // the adds are done before the accumulator is released
+  if constexpr (Epi::kTmaReduce || Epi::kTmaStore) {
+    if (lane == 0) bulk_wait_all();  // the adds / stores are done before the accumulator is released
     __syncwarp();
   }
 }
