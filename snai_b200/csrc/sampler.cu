@@ -74,7 +74,12 @@ struct SampArgs {
   int nan_guard;
   int *out;
   int *err;
+  int redo;  // only the rows whose out[] holds kRedoMark (variant A's CTA-per-row kernel)
 };
+
+// out[] of a row the one-warp-per-row variant-A kernel could not certify
+// (the CTA-per-row kernel's launch that follows redoes exactly these).
+constexpr int kRedoMark = -3;
 
 // ---------------------------------------------------------------------------
 // shared helpers
@@ -640,10 +645,11 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
   RowFeeder feed;
   feed.stage = stage_ptr(smem_dyn, sizeof(SmemA), V);
   feed.bar = &sm.bar;
-  const bool staged = NV4 > 0 && (V & 3) == 0 && ((a.ld & 3) == 0) &&
+  // a redo pass takes rows out of order: no row staging or history run ahead
+  const bool staged = NV4 > 0 && !a.redo && (V & 3) == 0 && ((a.ld & 3) == 0) &&
                       ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0) &&
                       ((reinterpret_cast<uintptr_t>(feed.stage) & 15) == 0);
-  const bool hist_in_regs = a.hist_cols <= 512 * kHistRegs;
+  const bool hist_in_regs = !a.redo && a.hist_cols <= 512 * kHistRegs;
   int hreg[kHistRegs];
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar, 1);
@@ -657,6 +663,7 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
   }
 
   for (int b = blockIdx.x; b < a.rows; b += gridDim.x) {
+    if (a.redo && a.out[b] != kRedoMark) continue;  // the same value on every thread
     const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
     Row<NV4> row;
     const float l0 = row_prologue(a, b, row, bits, sm.plist, &sm.npen, feed, staged, hreg, hist_in_regs, pen_fn);
@@ -787,7 +794,7 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
     }
     const double u = (double)a.uniforms[b];
     int id = -1;
-    if (any && simple) {
+    if (any && simple && !a.redo) {  // a redo row has failed a tier-1 bound already
       // tier 1: p~ = 2^(x c - M log2e), c = fp32(log2e / T); penalised entries
       // use their exact value t: 2^(t log2e - M log2e).
       const float c = (float)(1.4426950408889634 * a.Tinv);
@@ -2737,6 +2744,379 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
 }
 
 // ---------------------------------------------------------------------------
+// Streaming variant A (T > 0.01): one warp per row, no block barriers.
+//
+// The warp streams the row through the same cp.async ring as the variant-B
+// kernel.  Lane l reads the chunk's 16-byte words 8l .. 8l + 7 (in a rotated
+// order, so the shared-memory reads do not conflict): its 32 entries are
+// contiguous ids, covered by one 32-bit word of the history bitmap.  Per
+// 1024-entry chunk the warp takes the maximum mu of y = x c (x the raw
+// logit, c = fp32(log2e / T); penalised ids excluded) and the fp32 sum s of
+// 2^(y - mu), the penalised ids contributing 2^(t log2e - mu) with their
+// exact stored value t; (mu, s) go to a per-warp table.  At the row's end
+// the exact maximum M (the tempered maximum raw logit, or a penalised t)
+// fixes m2 = fp32(M log2e); the chunk totals s 2^(mu - m2) give S and the
+// chunk where u S is crossed; that chunk is read again, each lane sums the
+// p~ = 2^(x c - m2) (penalised: 2^(t log2e - m2)) of its 32 ids, a warp
+// scan finds the lane where the running sum crosses u S and that lane walks
+// its ids.  The draw is accepted when r is farther from the running sums at
+// the chosen id and its predecessor than the error bound of the register-row
+// kernel's tier 1 (widened for the two-step exponent and the fp32 chunk
+// sums); otherwise the contract exponential redoes the same search exactly
+// (tier 2), and rows it cannot settle (or NaN rows) run PHP's sequential
+// loop (tier 3).
+// ---------------------------------------------------------------------------
+
+constexpr int kStreamAWarps = 16;  // warps per CTA at most (128 registers a thread)
+
+struct StreamALayout {
+  int words, hist_cap, nch;
+  unsigned off_bm, off_hs, off_ch, off_pv, bytes;  // ring at 0
+};
+__host__ __device__ inline StreamALayout stream_a_layout(int V, int hist_cols) {
+  auto up16 = [](unsigned x) { return (x + 15u) & ~15u; };
+  StreamALayout L;
+  L.words = (V + 31) / 32;
+  L.hist_cap = (hist_cols + 31) & ~31;
+  L.nch = ((V >> 2) + kStreamChunk - 1) / kStreamChunk;
+  unsigned o = up16(kStreamSlots * kStreamChunk * 16);
+  L.off_bm = o;
+  o = up16(o + (unsigned)L.words * 4u);
+  L.off_hs = o;
+  o = up16(o + (unsigned)L.hist_cap * 4u);
+  L.off_ch = o;  // per chunk: (mu, s, s of the penalised ids, -) floats
+  o = up16(o + (unsigned)L.nch * 16u);
+  L.off_pv = o;  // the crossing chunk: 32 values of each lane, [e][lane]
+  o = up16(o + 32u * 32u * 4u);
+  L.bytes = o;
+  return L;
+}
+
+// Prefix of the chunk totals tot(c) in chunk order: S, and the first chunk
+// whose inclusive prefix reaches rr = u S with the prefix before it.
+template <class TOT>
+__device__ __forceinline__ int chunk_prefix(int nch, double u, const TOT &tot, double &S, double &rr, double &before) {
+  const int lane = threadIdx.x & 31;
+  S = 0.0;
+  for (int c0 = 0; c0 < nch; c0 += 32) {
+    const double t = c0 + lane < nch ? tot(c0 + lane) : 0.0;
+    S = __dadd_rn(S, warp_sum_d(t));
+  }
+  rr = __dmul_rn(u, S);
+  double carry = 0.0;
+  for (int c0 = 0; c0 < nch; c0 += 32) {
+    const double t = c0 + lane < nch ? tot(c0 + lane) : 0.0;
+    double incl = t;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl = __dadd_rn(incl, n);
+    }
+    double ex = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (lane == 0) ex = 0.0;
+    const unsigned m = __ballot_sync(0xffffffffu, c0 + lane < nch && __dadd_rn(carry, incl) >= rr);
+    if (m) {
+      const int src = __ffs(m) - 1;
+      before = __dadd_rn(carry, __shfl_sync(0xffffffffu, ex, src));
+      return c0 + src;
+    }
+    carry = __dadd_rn(carry, __shfl_sync(0xffffffffu, incl, 31));
+  }
+  before = carry;
+  return nch - 1;
+}
+
+// Running sums over chunk cs in id order, from `base`: lane l owns ids
+// 32l .. 32l + 31 of the chunk, pf(e) gives p of its e-th one.  Returns the
+// first id whose running sum reaches rr (INT_MAX if none) with the running
+// sums before (lo) and after (hi) it.
+template <class PF>
+__device__ __forceinline__ int chunk_crossing(const PF &pf, int cs, int V, double base, double rr, double &lo,
+                                              double &hi) {
+  const int lane = threadIdx.x & 31;
+  double w = 0.0;
+#pragma unroll 4
+  for (int e = 0; e < 32; ++e) w = __dadd_rn(w, pf(e));
+  double incl = w;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl = __dadd_rn(incl, n);
+  }
+  double ex = __shfl_up_sync(0xffffffffu, incl, 1);
+  if (lane == 0) ex = 0.0;
+  const unsigned m = __ballot_sync(0xffffffffu, __dadd_rn(base, incl) >= rr);
+  if (!m) return INT_MAX;
+  const int src = __ffs(m) - 1;
+  int cand = INT_MAX;
+  double mlo = 0.0, mhi = 0.0;
+  if (lane == src) {
+    double run = __dadd_rn(base, ex);
+    const int v0 = cs * kStreamChunk * 4 + 32 * lane;
+    for (int e = 0; e < 32 && v0 + e < V; ++e) {
+      const double cur = __dadd_rn(run, pf(e));
+      if (cur >= rr) {
+        cand = v0 + e;
+        mlo = run;
+        mhi = cur;
+        break;
+      }
+      run = cur;
+    }
+  }
+  cand = __shfl_sync(0xffffffffu, cand, src);
+  lo = __shfl_sync(0xffffffffu, mlo, src);
+  hi = __shfl_sync(0xffffffffu, mhi, src);
+  return cand;
+}
+
+// Certificate of the crossing id `cand` (running sums lo, hi around it)
+// against r, for sums whose entries are within er*p + eabs of the contract
+// values, plus at most `eadd` over all entries together, and whose depth is
+// at most `slack` beyond PHP's sequential one.
+__device__ __forceinline__ bool certify_cross(int cand, double lo, double hi, double S, double rr, double u, int V,
+                                              double er, double eabs, double eadd, double slack) {
+  const double Er = u * (er * S + eadd + (double)V * eabs + ((double)V + slack) * 0x1p-52 * S) + 0x1p-52 * rr;
+  const double Ehi = er * hi + eadd + ((double)cand + 1.0) * eabs + ((double)cand + slack) * 0x1p-52 * hi;
+  const double Elo = er * lo + eadd + (double)cand * eabs + ((double)cand + slack) * 0x1p-52 * lo;
+  return hi - Ehi >= rr + Er && (cand == 0 || lo + Elo < rr - Er);
+}
+
+// This lane's 32 raw logits of chunk cs (-inf past the row), loaded at once.
+__device__ __forceinline__ void lane_block(const float *Lrow, int cs, int V, float4 (&xw)[8]) {
+  const int lane = threadIdx.x & 31;
+  const int n4 = V >> 2;
+  const float4 *L4 = reinterpret_cast<const float4 *>(Lrow);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int wd = cs * kStreamChunk + 8 * lane + k;
+    xw[k] = wd < n4 ? __ldg(L4 + wd) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+  }
+}
+
+// Row end of the variant-A stream: M, tier 1 (then 2, then 3); writes out[b].
+__device__ __noinline__ void stream_a_finish(const SampArgs &a, int b, float xmax, float pmax, float l0, int ovf,
+                                             float4 *tab, const uint32_t *bm, float *pv, int nch, float cexp) {
+  const int lane = threadIdx.x & 31;
+  const int V = a.V;
+  xmax = warp_max(xmax);
+  pmax = warp_max(pmax);
+  l0 = __shfl_sync(0xffffffffu, l0, 0);
+  ovf = __any_sync(0xffffffffu, ovf);
+  if (a.nan_guard && l0 != l0) {  // src/snai_inference.php:146
+    if (lane == 0) a.out[b] = -1;
+    return;
+  }
+  const float tmax = xmax > -INFINITY ? div_to_f32(xmax, a.T, a.Tinv) : -INFINITY;
+  const float M = fmaxf(tmax, pmax);
+  // PHP: max starts at -INF and only a strictly larger value moves it
+  const bool any = M > -INFINITY;
+  const double u = (double)a.uniforms[b];
+  const float *Lrow = a.logits + (size_t)row_of(a, b) * a.ld;
+  int id = -1;
+  if (any && isfinite(M) && !ovf) {
+    const float l2e = 1.44269504f;
+    const float m2 = M * l2e;
+    double S, rr, before;
+    const int cs = chunk_prefix(
+        nch, u, [&](int c) { const float4 e = tab[c]; return (double)e.y * (double)ex2_approx(e.x - m2); }, S, rr,
+        before);
+    // the penalised ids' share Sp and its distance-weighted sum Wp
+    double Sp = 0.0, Wp = 0.0;
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+      double sp = 0.0, wp = 0.0;
+      if (c0 + lane < nch) {
+        const float4 e = tab[c0 + lane];
+        sp = (double)e.z * (double)ex2_approx(e.x - m2);
+        wp = fabs((double)m2 - (double)e.x) * sp;
+      }
+      Sp = __dadd_rn(Sp, warp_sum_d(sp));
+      Wp = __dadd_rn(Wp, warp_sum_d(wp));
+    }
+    if (isfinite(S) && isfinite(rr) && S > 0.0 && u >= 0.0 && u <= 1.0) {
+      const int v0 = cs * kStreamChunk * 4 + 32 * lane;
+      const int bw = cs * kStreamPer * 4 + lane;  // the bitmap word of this lane's 32 ids
+      const unsigned pm = bw < (V + 31) / 32 ? bm[bw] : 0u;
+      {
+        // p~ of this lane's 32 ids to the scratch: unpenalised ones from the
+        // loaded words, then the penalised ones over them
+        float4 xw[8];
+        lane_block(Lrow, cs, V, xw);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float f = f4_at(xw[k], j);
+            pv[(4 * k + j) * 32 + lane] = v0 + 4 * k + j < V ? ex2_approx(fmaf(f, cexp, -m2)) : 0.f;
+          }
+        for (unsigned bits = pm; bits; bits &= bits - 1u) {
+          const int e = __ffs(bits) - 1;
+          const float f = Lrow[v0 + e];
+          pv[e * 32 + lane] = ex2_approx(fmaf(penalise_a(div_to_f32(f, a.T, a.Tinv), a.rep, a.repinv), l2e, -m2));
+        }
+      }
+      __syncwarp();
+      double lo = 0.0, hi = 0.0;
+      const int cand = chunk_crossing([&](int e) { return (double)pv[e * 32 + lane]; }, cs, V, before, rr, lo, hi);
+      __syncwarp();
+      // p~ against the contract value p = 2^-dist, dist = (M - t) log2e >= 0:
+      // x c against t log2e (the roundings of c and of t) and m2 against
+      // M log2e move the exponent by at most 2^-23 (2.886 |M| + dist), the
+      // fma and mu - m2 (mu between an unpenalised entry's x c and m2) by
+      // 2^-24 dist each: a relative 2^-24 (4 |M| + 2.77 dist) in all, with
+      // 2^-22 per ex2.approx (two per chunk-total entry).  Summed over the
+      // entries, 2.77 dist p adds up to at most 2.77 S log2 V (the entropy
+      // of p / S is at most log2 V, and S >= 1).  A penalised id's fma works
+      // against its chunk's unpenalised mu: 2^-24 |m2 - mu| more on its p
+      // (Wp).  fp32 sums: 16 levels for an unpenalised chunk total, 38 for
+      // the penalised part (Sp).  Entries that underflow count as an
+      // absolute 2^-125.
+      const double er = (5.0 * fabs((double)M) + 16.0) * 0x1p-24 + 0x1p-21 + 1e-12;  // 4 |M|, rounded up
+      const double eadd =
+          0x1p-24 * (2.78 * log2((double)V) * S * (1.0 + 1e-3) + 0.7 * Wp + 38.0 * Sp) * (1.0 + 2.0 * er);
+      if (cand != INT_MAX && certify_cross(cand, lo, hi, S, rr, u, V, er, 0x1p-125, eadd, 80.0 + nch)) id = cand;
+    }
+  }
+  // not certified (or not finite, or a NaN logit): the CTA-per-row kernel's
+  // exact tiers take the row in the launch that follows
+  if (lane == 0) a.out[b] = id >= 0 ? id : kRedoMark;
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kStreamAWarps * 32, 1) sample_a_stream(const __grid_constant__ SampArgs a, int W) {
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int V = a.V, n4 = V >> 2, S = (n4 + kStreamChunk - 1) / kStreamChunk;
+  const StreamALayout Ly = stream_a_layout(V, a.hist_cols);
+  uint8_t *base = smem_dyn + (size_t)warp * Ly.bytes;
+  float4 *ring = reinterpret_cast<float4 *>(base);
+  uint32_t *bm = reinterpret_cast<uint32_t *>(base + Ly.off_bm);
+  int *hs = reinterpret_cast<int *>(base + Ly.off_hs);
+  float4 *tab = reinterpret_cast<float4 *>(base + Ly.off_ch);
+  float *pv = reinterpret_cast<float *>(base + Ly.off_pv);
+  const int NW = gridDim.x * W, gw = blockIdx.x * W + warp;
+  if (warp >= W || gw >= a.rows) return;
+  const int nrows = (a.rows - 1 - gw) / NW + 1;
+  const bool has_hist = a.hist != nullptr && a.hist_cols > 0;
+  const float cexp = (float)(1.4426950408889634 * a.Tinv);
+  const float l2e = 1.44269504f;
+  auto mrow_of = [&](int i) -> int { return i < nrows ? row_of(a, gw + i * NW) : -1; };
+  auto stage = [&](int mrow) -> int {
+    if (!has_hist || mrow < 0) return 0;
+    const int *hr = a.hist + (size_t)mrow * a.hist_ld;
+    for (int c = lane; c < a.hist_cols; c += 32) cp_async4(hs + c, hr + c);
+    cp_async_commit();
+    const int n = a.hist_len ? a.hist_len[mrow] : a.hist_cols;
+    return min(max(n, 0), a.hist_cols);
+  };
+  for (int w = lane; w < Ly.words; w += 32) bm[w] = 0u;
+  __syncwarp();
+  int mp = mrow_of(0), mq = mrow_of(1);
+  int hn = stage(mp);
+  auto mark = [&]() {
+    for (int c = lane; c < hn; c += 32) {
+      const int t = hs[c];
+      if (t >= 0 && t < V) atomicOr(&bm[t >> 5], 1u << (t & 31));
+    }
+    __syncwarp();
+  };
+  if (has_hist) {
+    cp_async_wait<0>();
+    __syncwarp();
+    mark();
+    hn = stage(mq);
+  }
+  int pi = 0, ps = 0;
+  const float4 *Lp = mp >= 0 ? reinterpret_cast<const float4 *>(a.logits + (size_t)mp * a.ld) : nullptr;
+  auto issue = [&](int slot) {
+    if (Lp != nullptr) {
+      const int c0 = ps * kStreamChunk + lane;
+#pragma unroll
+      for (int r = 0; r < kStreamPer; ++r)
+        if (c0 + 32 * r < n4) cp_async16(ring + slot * kStreamChunk + 32 * r + lane, Lp + c0 + 32 * r);
+    }
+    cp_async_commit();
+    if (++ps == S) {
+      ps = 0;
+      ++pi;
+      Lp = mq >= 0 ? reinterpret_cast<const float4 *>(a.logits + (size_t)mq * a.ld) : nullptr;
+      mq = mrow_of(pi + 1);
+    }
+  };
+  for (int q = 0; q < kStreamSlots; ++q) issue(q);
+
+  float xmax = -INFINITY, pmax = -INFINITY, l0 = 0.f;
+  int ovf = 0;
+  const long long total = (long long)nrows * S;
+  int ci = 0, cs = 0;
+  for (long long q = 0; q < total; ++q) {
+    const int slot = (int)(q % kStreamSlots);
+    cp_async_wait<kStreamSlots - 1>();
+    if (cs == 0 && ci > 0 && has_hist) {
+      if (S < kStreamSlots) cp_async_wait<0>();
+      __syncwarp();
+      mark();
+      hn = stage(pi == ci ? mq : mrow_of(ci + 1));
+    }
+    // every lane's copies of this chunk are complete: the lanes read across
+    __syncwarp();
+    const float4 *rs = ring + slot * kStreamChunk + 8 * lane;  // this lane's eight words
+    const int wd0 = cs * kStreamChunk + 8 * lane;
+    const int bw = cs * kStreamPer * 4 + lane;
+    const unsigned pm = bw < Ly.words ? bm[bw] : 0u;
+    float4 x[8];
+    float m = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int k = (r + lane) & 7;  // rotated: the eight lanes of a phase hit distinct banks
+      x[r] = wd0 + k < n4 ? rs[k] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      const unsigned nib = (pm >> (4 * k)) & 0xFu;
+      if (nib & 1u) x[r].x = -INFINITY;
+      if (nib & 2u) x[r].y = -INFINITY;
+      if (nib & 4u) x[r].z = -INFINITY;
+      if (nib & 8u) x[r].w = -INFINITY;
+      m = fmaxf(m, fmax4(x[r]));
+    }
+    if (cs == 0 && lane == 0) l0 = reinterpret_cast<const float *>(rs)[0];  // the raw logit 0
+    xmax = fmaxf(xmax, m);
+    const float wm = warp_max(m);
+    const float mu = wm > -INFINITY ? wm * cexp : 0.f;
+    float sum = 0.f, sump = 0.f;
+    // penalised ids of this lane, their stored values from the staged words
+    for (unsigned bits = pm; bits; bits &= bits - 1u) {
+      const int e = __ffs(bits) - 1;
+      const float t =
+          penalise_a(div_to_f32(reinterpret_cast<const float *>(rs)[e], a.T, a.Tinv), a.rep, a.repinv);
+      pmax = fmaxf(pmax, t);
+      const float y = fmaf(t, l2e, -mu);
+      ovf |= y > 120.f;
+      sump += ex2_approx(y);
+    }
+    __syncwarp();  // every lane has read the slot
+    issue(slot);
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      sum += (ex2_approx(fmaf(x[r].x, cexp, -mu)) + ex2_approx(fmaf(x[r].y, cexp, -mu))) +
+             (ex2_approx(fmaf(x[r].z, cexp, -mu)) + ex2_approx(fmaf(x[r].w, cexp, -mu)));
+    sum = warp_sum(sum);
+    sump = warp_sum(sump);
+    if (lane == 0) tab[cs] = make_float4(mu, sum + sump, sump, 0.f);
+    if (++cs == S) {
+      __syncwarp();
+      stream_a_finish(a, gw + ci * NW, xmax, pmax, l0, ovf, tab, bm, pv, S, cexp);
+      for (int w = lane; w < Ly.words; w += 32) bm[w] = 0u;
+      __syncwarp();
+      xmax = -INFINITY;
+      pmax = -INFINITY;
+      ovf = 0;
+      cs = 0;
+      ++ci;
+    }
+  }
+  cp_async_wait<0>();
+}
+
+// ---------------------------------------------------------------------------
 // Cluster kernels: rows longer than one CTA's register row.  A cluster of C
 // CTAs (C = ceil(V / 32768), at most 8) takes a row; CTA r holds the ids
 // [32768 r, 32768 (r + 1)) in registers through the same staged-row
@@ -3538,6 +3918,34 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   a.nan_guard = s.nan_guard;
   a.out = s.out_ids;
   a.err = s.err;
+  a.redo = 0;
+  // variant A (T > 0.01) over 16-byte aligned rows: the streaming kernel
+  if (s.variant == 0 && s.temperature > 0.01 && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
+      (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 && s.hist_cols <= kStreamHistMax) {
+    const StreamALayout Ly = stream_a_layout(s.V, s.hist_cols);
+    const int W = std::min<int>(kStreamAWarps, (int)((227u * 1024u) / Ly.bytes));
+    if (W >= 2) {
+      static unsigned long long done = 0;
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (!(done & (1ull << dev))) {
+        cudaFuncSetAttribute(sample_a_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        done |= 1ull << dev;
+      }
+      const int grid = std::min(sm_count(), (s.rows + W - 1) / W);
+      sample_a_stream<<<grid, W * 32, (size_t)W * Ly.bytes, stream>>>(a, W);
+      // the rows it could not certify, exactly, by the CTA-per-row kernel
+      SampArgs r = a;
+      r.redo = 1;
+      launch_a<0>(r, sizeof(SmemA) + (((size_t)((s.V + 31) / 32) * 4 + 15) & ~(size_t)15), stream);
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) {
+        set_error("sampler launch failed: %s", cudaGetErrorString(e));
+        return -4;
+      }
+      return 0;
+    }
+  }
   // variant B over 16-byte aligned rows: the streaming kernel, one warp per row
   if (s.variant != 0 && (s.V & 3) == 0 && (s.ld & 3) == 0 && (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 &&
       s.hist_cols <= kStreamHistMax) {

@@ -152,6 +152,31 @@ def test_variant_b_tail_edges(built):
         assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_B, T, rep, k, p)), (T, rep, k, p)
 
 
+def test_variant_a_stream_edges(built):
+    """Variant A through the one-warp-per-row kernel: logits of magnitude 1e4
+    (wide error bounds: the exact tiers), a history covering a quarter of
+    the vocabulary with penalties above and below 1, rows of -inf but for a
+    few ids, a NaN entry (the sequential tier), u = 0 and 1, a partial last
+    chunk."""
+    rng = np.random.default_rng(41)
+    R, V = 24, 4096 + 1024 + 8
+    L = rng.normal(0, 3, (R, V)).astype(np.float32)
+    L[0:3] *= 3000.0
+    L[3:5] = -np.inf
+    L[3, [7, 900, 5000]] = [1.0, 2.0, 1.5]
+    L[4, V - 1] = 0.0
+    L[5, 1234] = np.nan
+    L[6:8, rng.choice(V, 40, replace=False)] += 15.0
+    U = rng.random(R).astype(np.float32)
+    U[8] = 0.0
+    U[9] = 1.0
+    U[10] = np.float32(np.nextafter(np.float32(1.0), np.float32(0.0)))
+    hist = rng.integers(0, V, (R, 1024)).astype(np.int32)
+    for T, rep in [(0.7, 1.15), (0.25, 0.5), (2.0, 1.0), (0.011, 3.0)]:
+        got = gpu_sample(L, hist, U, sample_params(VARIANT_A, T, rep, nan_guard=0))
+        assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_A, T, rep)), (T, rep)
+
+
 def test_variant_b_ordered_and_clustered_rows(built):
     """Rows whose largest logits all sit at the start (descending order) or
     the end (ascending), rows where a few hundred entries share the top
