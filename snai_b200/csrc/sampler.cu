@@ -2959,21 +2959,25 @@ __device__ __noinline__ void stream_a_finish(const SampArgs &a, int b, float xma
       double lo = 0.0, hi = 0.0;
       const int cand = chunk_crossing([&](int e) { return (double)pv[e * 32 + lane]; }, cs, V, before, rr, lo, hi);
       __syncwarp();
-      // p~ against the contract value p = 2^-dist, dist = (M - t) log2e >= 0:
-      // x c against t log2e (the roundings of c and of t) and m2 against
-      // M log2e move the exponent by at most 2^-23 (2.886 |M| + dist), the
-      // fma and mu - m2 (mu between an unpenalised entry's x c and m2) by
-      // 2^-24 dist each: a relative 2^-24 (4 |M| + 2.77 dist) in all, with
-      // 2^-22 per ex2.approx (two per chunk-total entry).  Summed over the
-      // entries, 2.77 dist p adds up to at most 2.77 S log2 V (the entropy
-      // of p / S is at most log2 V, and S >= 1).  A penalised id's fma works
-      // against its chunk's unpenalised mu: 2^-24 |m2 - mu| more on its p
-      // (Wp).  fp32 sums: 16 levels for an unpenalised chunk total, 38 for
-      // the penalised part (Sp).  Entries that underflow count as an
-      // absolute 2^-125.
-      const double er = (5.0 * fabs((double)M) + 16.0) * 0x1p-24 + 0x1p-21 + 1e-12;  // 4 |M|, rounded up
-      const double eadd =
-          0x1p-24 * (2.78 * log2((double)V) * S * (1.0 + 1e-3) + 0.7 * Wp + 38.0 * Sp) * (1.0 + 2.0 * er);
+      // p~ against the contract value p = 2^-dist, dist = (M - t) log2e >= 0.
+      // The draw only compares running sums with u S, so a factor common to
+      // every p~ cancels: the roundings of c and of m2 shift every
+      // unpenalised exponent by the same M log2e (dc - dm) plus at most
+      // 2^-24 dist each (penalised exponents: the same with log2e's rounding;
+      // the two groups differ by at most 2.9 |M| 2^-24, charged on Sp).
+      // Per entry there remain t's rounding (2^-24 (1.443 |M| + dist)), the
+      // fma and mu - m2 (mu between an unpenalised entry's x c and m2: 2^-24
+      // dist each): a relative 2^-24 (|M| + 2.77 dist), with 2^-22 per
+      // ex2.approx (two per chunk-total entry).  Summed over the entries,
+      // 2.77 dist p adds up to at most 2.77 S log2 V (the entropy of p / S
+      // is at most log2 V, and S >= 1).  A penalised id's fma works against
+      // its chunk's unpenalised mu: 2^-24 |m2 - mu| more on its p (Wp).
+      // fp32 sums: 16 levels for an unpenalised chunk total, 38 for the
+      // penalised part.  Entries that underflow count as an absolute 2^-125.
+      const double er = (1.5 * fabs((double)M) + 16.0) * 0x1p-24 + 0x1p-21 + 1e-12;
+      const double eadd = 0x1p-24 *
+                          (2.78 * log2((double)V) * S * (1.0 + 1e-3) + 0.7 * Wp + (38.0 + 3.0 * fabs((double)M)) * Sp) *
+                          (1.0 + 2.0 * er);
       if (cand != INT_MAX && certify_cross(cand, lo, hi, S, rr, u, V, er, 0x1p-125, eadd, 80.0 + nch)) id = cand;
     }
   }
