@@ -3923,11 +3923,16 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   a.out = s.out_ids;
   a.err = s.err;
   a.redo = 0;
+  // The one-warp-per-row kernels pay off from a few rows per SM on; a
+  // smaller batch is quicker with a whole CTA per row.  Warps per CTA: at
+  // most what the rows fill across all SMs.
+  const bool many = s.rows >= 4 * sm_count();
+  const int wrows = (s.rows + sm_count() - 1) / sm_count();
   // variant A (T > 0.01) over 16-byte aligned rows: the streaming kernel
-  if (s.variant == 0 && s.temperature > 0.01 && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
+  if (many && s.variant == 0 && s.temperature > 0.01 && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
       (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 && s.hist_cols <= kStreamHistMax) {
     const StreamALayout Ly = stream_a_layout(s.V, s.hist_cols);
-    const int W = std::min<int>(kStreamAWarps, (int)((227u * 1024u) / Ly.bytes));
+    const int W = std::min<int>({kStreamAWarps, (int)((227u * 1024u) / Ly.bytes), wrows});
     if (W >= 2) {
       static unsigned long long done = 0;
       int dev = 0;
@@ -3951,11 +3956,11 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
     }
   }
   // variant B over 16-byte aligned rows: the streaming kernel, one warp per row
-  if (s.variant != 0 && (s.V & 3) == 0 && (s.ld & 3) == 0 && (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 &&
-      s.hist_cols <= kStreamHistMax) {
+  if (many && s.variant != 0 && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
+      (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 && s.hist_cols <= kStreamHistMax) {
     const int kk = s.temperature < 0.01 ? 1 : std::min(s.top_k, s.V);
     const StreamLayout Ly = stream_layout(s.V, s.hist_cols, kk);
-    const int W = std::min<int>(kStreamWarps, (int)((227u * 1024u) / Ly.bytes));
+    const int W = std::min<int>({kStreamWarps, (int)((227u * 1024u) / Ly.bytes), wrows});
     if (kk <= kStreamMaxK && W >= 2) {
       static unsigned long long done = 0;
       int dev = 0;

@@ -38,6 +38,17 @@ def gpu_sample(L, hist, U, params, hist_len=None, ld=None):
     return out.cpu().numpy()
 
 
+def stream_batch(L, hist, U):
+    """The rows tiled (uniforms varied) to a batch large enough (4 rows per
+    SM) for the one-warp-per-row kernels; smaller batches take the
+    CTA-per-row kernels."""
+    need = 4 * torch.cuda.get_device_properties(0).multi_processor_count
+    reps = -(-need // L.shape[0])
+    rng = np.random.default_rng(L.shape[0] * 7 + L.shape[1])
+    U2 = np.concatenate([U] + [rng.random(len(U)).astype(np.float32) for _ in range(reps - 1)])
+    return np.tile(L, (reps, 1)), np.tile(hist, (reps, 1)), U2
+
+
 def oracle_ids(L, hist, U, variant, T, rep, k=40, p=0.9, exp_mode=1, hist_len=None):
     ids = []
     for r in range(L.shape[0]):
@@ -146,10 +157,12 @@ def test_variant_b_tail_edges(built):
     U[0::4] = 1.0
     U[1::4] = 0.5
     hist = rng.integers(0, V, (R, 64)).astype(np.int32)
+    Lb, Hb, Ub = stream_batch(L, hist, U)
     for T, rep, k, p in [(0.7, 0.0, 2, 0.5), (0.7, 0.0, 4, 0.5), (1.0, 0.0, 4, 1.0), (0.7, 0.0, 4, 0.75),
                          (0.01, 0.0, 4, 0.9), (0.7, 1.5, 40, 0.9)]:
-        got = gpu_sample(L, hist, U, sample_params(VARIANT_B, T, rep, k, p))
-        assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_B, T, rep, k, p)), (T, rep, k, p)
+        for LL, HH, UU in ((L, hist, U), (Lb, Hb, Ub)):
+            got = gpu_sample(LL, HH, UU, sample_params(VARIANT_B, T, rep, k, p))
+            assert np.array_equal(got, oracle_ids(LL, HH, UU, VARIANT_B, T, rep, k, p)), (len(LL), T, rep, k, p)
 
 
 def test_variant_a_stream_edges(built):
@@ -172,9 +185,11 @@ def test_variant_a_stream_edges(built):
     U[9] = 1.0
     U[10] = np.float32(np.nextafter(np.float32(1.0), np.float32(0.0)))
     hist = rng.integers(0, V, (R, 1024)).astype(np.int32)
+    Lb, Hb, Ub = stream_batch(L, hist, U)
     for T, rep in [(0.7, 1.15), (0.25, 0.5), (2.0, 1.0), (0.011, 3.0)]:
-        got = gpu_sample(L, hist, U, sample_params(VARIANT_A, T, rep, nan_guard=0))
-        assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_A, T, rep)), (T, rep)
+        for LL, HH, UU in ((L, hist, U), (Lb, Hb, Ub)):
+            got = gpu_sample(LL, HH, UU, sample_params(VARIANT_A, T, rep, nan_guard=0))
+            assert np.array_equal(got, oracle_ids(LL, HH, UU, VARIANT_A, T, rep)), (len(LL), T, rep)
 
 
 def test_variant_b_ordered_and_clustered_rows(built):
@@ -194,9 +209,28 @@ def test_variant_b_ordered_and_clustered_rows(built):
     L[12, :V - 20] = np.nan
     U = rng.random(R).astype(np.float32)
     hist = rng.integers(0, V, (R, 128)).astype(np.int32)
+    Lb, Hb, Ub = stream_batch(L, hist, U)
     for T, rep, k, p in [(0.7, 1.1, 50, 0.95), (0.0, 1.1, 40, 0.9), (1.3, 0.0, 128, 0.99), (0.7, -0.5, 40, 0.9)]:
-        got = gpu_sample(L, hist, U, sample_params(VARIANT_B, T, rep, k, p))
-        assert np.array_equal(got, oracle_ids(L, hist, U, VARIANT_B, T, rep, k, p)), (T, rep, k, p)
+        for LL, HH, UU in ((L, hist, U), (Lb, Hb, Ub)):
+            got = gpu_sample(LL, HH, UU, sample_params(VARIANT_B, T, rep, k, p))
+            assert np.array_equal(got, oracle_ids(LL, HH, UU, VARIANT_B, T, rep, k, p)), (len(LL), T, rep, k, p)
+
+
+@pytest.mark.parametrize("V", [16384, 32000, 131072])
+def test_streaming_kernels_large_batch(V, built):
+    """A batch of 4 rows per SM (the one-warp-per-row kernels) of the sampler
+    benchmark's kind of rows, both variants, with a ragged history."""
+    rng = np.random.default_rng(3 * V)
+    need = 4 * torch.cuda.get_device_properties(0).multi_processor_count
+    L, hist, U = synth(rng, need, V)
+    hist_len = rng.integers(0, hist.shape[1] + 1, need).astype(np.int32)
+    for variant, T, rep, k, p in [(VARIANT_A, 0.7, 1.15, 40, 0.9), (VARIANT_B, 0.7, 1.15, 50, 0.95),
+                                  (VARIANT_B, 0.0, 1.1, 40, 0.9)]:
+        prm = (sample_params(VARIANT_A, T, rep, nan_guard=0) if variant == VARIANT_A
+               else sample_params(VARIANT_B, T, rep, k, p))
+        got = gpu_sample(L, hist, U, prm, hist_len=hist_len)
+        want = oracle_ids(L, hist, U, variant, T, rep, k, p, hist_len=hist_len)
+        assert np.array_equal(got, want), (variant, T)
 
 
 def test_nan_guard_and_argument_errors(built):
