@@ -2744,7 +2744,9 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
 }
 
 // ---------------------------------------------------------------------------
-// Streaming variant A (T > 0.01): one warp per row, no block barriers.
+// Streaming variant A: one warp per row, no block barriers.  (Greedy, T <=
+// 0.01: the chunks keep their maximum only, and the row's end looks for the
+// first id attaining M in the chunks that can hold one.)
 //
 // The warp streams the row through the same cp.async ring as the variant-B
 // kernel.  Lane l reads the chunk's 16-byte words 8l .. 8l + 7 (in a rotated
@@ -2895,16 +2897,65 @@ __device__ __forceinline__ void lane_block(const float *Lrow, int cs, int V, flo
 }
 
 // Row end of the variant-A stream: M, tier 1 (then 2, then 3); writes out[b].
-__device__ __noinline__ void stream_a_finish(const SampArgs &a, int b, float xmax, float pmax, float l0, int ovf,
-                                             float4 *tab, const uint32_t *bm, float *pv, int nch, float cexp) {
+__device__ __noinline__ void stream_a_finish(const SampArgs &a, int b, float xmax, float pmax, int pidx, float l0,
+                                             int ovf, float4 *tab, const uint32_t *bm, float *pv, int nch, float cexp) {
   const int lane = threadIdx.x & 31;
   const int V = a.V;
   xmax = warp_max(xmax);
-  pmax = warp_max(pmax);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {  // the largest penalised value, its first id
+    const float ob = __shfl_xor_sync(0xffffffffu, pmax, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, pidx, o);
+    if (ob > pmax || (ob == pmax && oi < pidx)) {
+      pmax = ob;
+      pidx = oi;
+    }
+  }
   l0 = __shfl_sync(0xffffffffu, l0, 0);
   ovf = __any_sync(0xffffffffu, ovf);
   if (a.nan_guard && l0 != l0) {  // src/snai_inference.php:146
     if (lane == 0) a.out[b] = -1;
+    return;
+  }
+  if (a.T <= 0.01) {
+    // greedy: the first id attaining M.  An unpenalised entry with
+    // fp32(x/T) == M has x >= (M - |M| 2^-22) T; only the chunks whose
+    // maximum reaches that bound are read again, in id order.
+    const float tmax = xmax > -INFINITY ? div_to_f32(xmax, a.T, a.Tinv) : -INFINITY;
+    const float M = fmaxf(tmax, pmax);
+    int best = 0;  // PHP: max starts at -INF and only a strictly larger value moves it
+    if (M > -INFINITY && !(isfinite(M) && isfinite(xmax))) {
+      best = kRedoMark;  // the CTA-per-row kernel's exact maximum
+    } else if (M > -INFINITY) {
+      best = pmax == M ? pidx : INT_MAX;
+      const double lowt = (double)M - fabs((double)M) * 0x1p-22 - 1e-44;
+      const float xthr = __double2float_rd(lowt * a.T);
+      const float *Lrow = a.logits + (size_t)row_of(a, b) * a.ld;
+      const int words = (V + 31) / 32;
+      for (int c = 0; c < nch; ++c) {
+        if (!(tab[c].x >= xthr)) continue;  // the same value on every lane
+        float4 xw[8];
+        lane_block(Lrow, c, V, xw);
+        const int bw = c * kStreamPer * 4 + lane;
+        const unsigned pm = bw < words ? bm[bw] : 0u;
+        const int v0 = c * kStreamChunk * 4 + 32 * lane;
+        int f = INT_MAX;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int e = 4 * k + j;
+            const float x = f4_at(xw[k], j);
+            if (v0 + e < V && !((pm >> e) & 1u) && x >= xthr && f == INT_MAX && div_to_f32(x, a.T, a.Tinv) == M)
+              f = v0 + e;
+          }
+        f = __reduce_min_sync(0xffffffffu, f);
+        best = min(best, f);
+        if (f != INT_MAX) break;
+      }
+    }
+    if (lane == 0) a.out[b] = best;
+    __syncwarp();
     return;
   }
   const float tmax = xmax > -INFINITY ? div_to_f32(xmax, a.T, a.Tinv) : -INFINITY;
@@ -2987,6 +3038,7 @@ __device__ __noinline__ void stream_a_finish(const SampArgs &a, int b, float xma
   __syncwarp();
 }
 
+template <bool GREEDY>
 __global__ void __launch_bounds__(kStreamAWarps * 32, 1) sample_a_stream(const __grid_constant__ SampArgs a, int W) {
   extern __shared__ __align__(16) uint8_t smem_dyn[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -3050,7 +3102,8 @@ __global__ void __launch_bounds__(kStreamAWarps * 32, 1) sample_a_stream(const _
   for (int q = 0; q < kStreamSlots; ++q) issue(q);
 
   float xmax = -INFINITY, pmax = -INFINITY, l0 = 0.f;
-  int ovf = 0;
+  int pidx = INT_MAX, ovf = 0;
+  constexpr bool greedy = GREEDY;
   const long long total = (long long)nrows * S;
   int ci = 0, cs = 0;
   for (long long q = 0; q < total; ++q) {
@@ -3091,27 +3144,33 @@ __global__ void __launch_bounds__(kStreamAWarps * 32, 1) sample_a_stream(const _
       const int e = __ffs(bits) - 1;
       const float t =
           penalise_a(div_to_f32(reinterpret_cast<const float *>(rs)[e], a.T, a.Tinv), a.rep, a.repinv);
-      pmax = fmaxf(pmax, t);
+      if (t > pmax) {  // this lane's ids ascend: ties keep the first
+        pmax = t;
+        pidx = cs * kStreamChunk * 4 + 32 * lane + e;
+      }
       const float y = fmaf(t, l2e, -mu);
       ovf |= y > 120.f;
-      sump += ex2_approx(y);
+      sump += greedy ? 0.f : ex2_approx(y);
     }
     __syncwarp();  // every lane has read the slot
     issue(slot);
+    if (!greedy) {
 #pragma unroll
-    for (int r = 0; r < 8; ++r)
-      sum += (ex2_approx(fmaf(x[r].x, cexp, -mu)) + ex2_approx(fmaf(x[r].y, cexp, -mu))) +
-             (ex2_approx(fmaf(x[r].z, cexp, -mu)) + ex2_approx(fmaf(x[r].w, cexp, -mu)));
-    sum = warp_sum(sum);
-    sump = warp_sum(sump);
-    if (lane == 0) tab[cs] = make_float4(mu, sum + sump, sump, 0.f);
+      for (int r = 0; r < 8; ++r)
+        sum += (ex2_approx(fmaf(x[r].x, cexp, -mu)) + ex2_approx(fmaf(x[r].y, cexp, -mu))) +
+               (ex2_approx(fmaf(x[r].z, cexp, -mu)) + ex2_approx(fmaf(x[r].w, cexp, -mu)));
+      sum = warp_sum(sum);
+      sump = warp_sum(sump);
+    }
+    if (lane == 0) tab[cs] = greedy ? make_float4(wm, 0.f, 0.f, 0.f) : make_float4(mu, sum + sump, sump, 0.f);
     if (++cs == S) {
       __syncwarp();
-      stream_a_finish(a, gw + ci * NW, xmax, pmax, l0, ovf, tab, bm, pv, S, cexp);
+      stream_a_finish(a, gw + ci * NW, xmax, pmax, pidx, l0, ovf, tab, bm, pv, S, cexp);
       for (int w = lane; w < Ly.words; w += 32) bm[w] = 0u;
       __syncwarp();
       xmax = -INFINITY;
       pmax = -INFINITY;
+      pidx = INT_MAX;
       ovf = 0;
       cs = 0;
       ++ci;
@@ -3928,8 +3987,9 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   // most what the rows fill across all SMs.
   const bool many = s.rows >= 4 * sm_count();
   const int wrows = (s.rows + sm_count() - 1) / sm_count();
-  // variant A (T > 0.01) over 16-byte aligned rows: the streaming kernel
-  if (many && s.variant == 0 && s.temperature > 0.01 && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
+  // variant A over 16-byte aligned rows: the streaming kernel (greedy only for
+  // rows longer than a register row, where it beats the CTA clusters)
+  if (many && s.variant == 0 && (s.temperature > 0.01 || s.V > kSliceLen) && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
       (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 && s.hist_cols <= kStreamHistMax) {
     const StreamALayout Ly = stream_a_layout(s.V, s.hist_cols);
     const int W = std::min<int>({kStreamAWarps, (int)((227u * 1024u) / Ly.bytes), wrows});
@@ -3938,11 +3998,15 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
       int dev = 0;
       cudaGetDevice(&dev);
       if (!(done & (1ull << dev))) {
-        cudaFuncSetAttribute(sample_a_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(sample_a_stream<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(sample_a_stream<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         done |= 1ull << dev;
       }
       const int grid = std::min(sm_count(), (s.rows + W - 1) / W);
-      sample_a_stream<<<grid, W * 32, (size_t)W * Ly.bytes, stream>>>(a, W);
+      if (s.temperature <= 0.01)
+        sample_a_stream<true><<<grid, W * 32, (size_t)W * Ly.bytes, stream>>>(a, W);
+      else
+        sample_a_stream<false><<<grid, W * 32, (size_t)W * Ly.bytes, stream>>>(a, W);
       // the rows it could not certify, exactly, by the CTA-per-row kernel
       SampArgs r = a;
       r.redo = 1;

@@ -186,7 +186,7 @@ def test_variant_a_stream_edges(built):
     U[10] = np.float32(np.nextafter(np.float32(1.0), np.float32(0.0)))
     hist = rng.integers(0, V, (R, 1024)).astype(np.int32)
     Lb, Hb, Ub = stream_batch(L, hist, U)
-    for T, rep in [(0.7, 1.15), (0.25, 0.5), (2.0, 1.0), (0.011, 3.0)]:
+    for T, rep in [(0.7, 1.15), (0.25, 0.5), (2.0, 1.0), (0.011, 3.0), (0.01, 1.15), (0.004, 0.5)]:
         for LL, HH, UU in ((L, hist, U), (Lb, Hb, Ub)):
             got = gpu_sample(LL, HH, UU, sample_params(VARIANT_A, T, rep, nan_guard=0))
             assert np.array_equal(got, oracle_ids(LL, HH, UU, VARIANT_A, T, rep)), (len(LL), T, rep)
@@ -224,8 +224,8 @@ def test_streaming_kernels_large_batch(V, built):
     need = 4 * torch.cuda.get_device_properties(0).multi_processor_count
     L, hist, U = synth(rng, need, V)
     hist_len = rng.integers(0, hist.shape[1] + 1, need).astype(np.int32)
-    for variant, T, rep, k, p in [(VARIANT_A, 0.7, 1.15, 40, 0.9), (VARIANT_B, 0.7, 1.15, 50, 0.95),
-                                  (VARIANT_B, 0.0, 1.1, 40, 0.9)]:
+    for variant, T, rep, k, p in [(VARIANT_A, 0.7, 1.15, 40, 0.9), (VARIANT_A, 0.01, 1.15, 40, 0.9),
+                                  (VARIANT_B, 0.7, 1.15, 50, 0.95), (VARIANT_B, 0.0, 1.1, 40, 0.9)]:
         prm = (sample_params(VARIANT_A, T, rep, nan_guard=0) if variant == VARIANT_A
                else sample_params(VARIANT_B, T, rep, k, p))
         got = gpu_sample(L, hist, U, prm, hist_len=hist_len)
