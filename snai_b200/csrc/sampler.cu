@@ -78,8 +78,12 @@ struct SampArgs {
 };
 
 // out[] of a row the one-warp-per-row variant-A kernel could not certify
-// (the CTA-per-row kernel's launch that follows redoes exactly these).
+// (the CTA-per-row kernel's launch that follows redoes exactly these).  The
+// redo launch writes its results as -(v + 10) (<= kRedoDone) so that every
+// CTA still recognises the marked rows while others finish theirs; a last
+// small launch decodes them.
 constexpr int kRedoMark = -3;
+constexpr int kRedoDone = -8;
 
 // ---------------------------------------------------------------------------
 // shared helpers
@@ -662,14 +666,15 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
     if (hist_in_regs) load_hist_regs(a, r0, hreg);
   }
 
-  for (int b = blockIdx.x; b < a.rows; b += gridDim.x) {
-    if (a.redo && a.out[b] != kRedoMark) continue;  // the same value on every thread
+  // a redo launch writes -(v + 10)
+  auto put = [&](int b, int v) { a.out[b] = a.redo ? -(v + 10) : v; };
+  auto row_body = [&](int b) {
     const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
     Row<NV4> row;
     const float l0 = row_prologue(a, b, row, bits, sm.plist, &sm.npen, feed, staged, hreg, hist_in_regs, pen_fn);
     if (a.nan_guard && l0 != l0) {  // src/snai_inference.php:146
-      if (threadIdx.x == 0) a.out[b] = -1;
-      continue;
+      if (threadIdx.x == 0) put(b, -1);
+      return;
     }
     const int nl = row.layers();
 
@@ -789,8 +794,8 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
     const bool any = best > -INFINITY;
     const double maxv = any ? (double)best : -INFINITY;
     if (a.T <= 0.01) {
-      if (threadIdx.x == 0) a.out[b] = any ? bi : 0;
-      continue;
+      if (threadIdx.x == 0) put(b, any ? bi : 0);
+      return;
     }
     const double u = (double)a.uniforms[b];
     int id = -1;
@@ -826,12 +831,55 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
       // tier 3
       if (warp == 0) {
         const int s = sequential_a(a, bits, L, maxv, u);
-        if (lane == 0) a.out[b] = s;
+        if (lane == 0) put(b, s);
       }
     } else if (threadIdx.x == 0) {
-      a.out[b] = id;
+      put(b, id);
+    }
+    };
+  if (!a.redo) {
+    for (int b = blockIdx.x; b < a.rows; b += gridDim.x) row_body(b);
+  } else {
+    // the marked rows (kRedoMark, or already redone: <= kRedoDone) in id
+    // order; this CTA takes those of rank = blockIdx.x (mod gridDim.x)
+    __shared__ int redo_cnt[kSampWarps];
+    __shared__ int redo_list[kSampThreads];
+    int seen = 0;
+    for (int b0 = 0; b0 < a.rows; b0 += kSampThreads) {
+      const int bb = b0 + (int)threadIdx.x;
+      const int ov = bb < a.rows ? a.out[bb] : 0;
+      const bool mk = ov == kRedoMark || ov <= kRedoDone;
+      const unsigned bal = __ballot_sync(0xffffffffu, mk);
+      if (lane == 0) redo_cnt[warp] = __popc(bal);
+      __syncthreads();
+      int before = 0, tot = 0;
+      for (int w = 0; w < kSampWarps; ++w) {
+        const int c = redo_cnt[w];
+        before += w < warp ? c : 0;
+        tot += c;
+      }
+      const int rank = seen + before + __popc(bal & ((1u << lane) - 1u));
+      const bool mine = mk && ov == kRedoMark && rank % (int)gridDim.x == (int)blockIdx.x;
+      const unsigned bm2 = __ballot_sync(0xffffffffu, mine);
+      __syncthreads();
+      if (lane == 0) redo_cnt[warp] = __popc(bm2);
+      __syncthreads();
+      int b2 = 0, t2 = 0;
+      for (int w = 0; w < kSampWarps; ++w) {
+        const int c = redo_cnt[w];
+        b2 += w < warp ? c : 0;
+        t2 += c;
+      }
+      if (mine) redo_list[b2 + __popc(bm2 & ((1u << lane) - 1u))] = bb;
+      __syncthreads();
+      for (int q = 0; q < t2; ++q) {
+        row_body(redo_list[q]);
+        __syncthreads();
+      }
+      seen += tot;
     }
   }
+
 }
 
 // ---------------------------------------------------------------------------
@@ -3948,6 +3996,12 @@ static void launch_a(const SampArgs &a, size_t sm, cudaStream_t st) {
     launch_persistent(sample_a_reg<NV4>, a, sm, NV4 <= 8 ? 2 : 1, st, done);
 }
 
+// Last step of a variant-A redo: the redone rows' -(v + 10) back to v.
+__global__ void redo_decode_kernel(int *out, int rows) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < rows && out[b] <= kRedoDone) out[b] = -out[b] - 10;
+}
+
 template <int NV4>
 static void launch_b(const SampArgs &a, size_t sm, cudaStream_t st) {
   static unsigned long long done = 0;
@@ -4011,6 +4065,7 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
       SampArgs r = a;
       r.redo = 1;
       launch_a<0>(r, sizeof(SmemA) + (((size_t)((s.V + 31) / 32) * 4 + 15) & ~(size_t)15), stream);
+      redo_decode_kernel<<<(s.rows + 255) / 256, 256, 0, stream>>>(a.out, s.rows);
       const cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) {
         set_error("sampler launch failed: %s", cudaGetErrorString(e));
