@@ -2712,8 +2712,9 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
 
   StreamState st{0, 0, -INFINITY, -INFINITY};
   // the buffer is cut once it holds more than cut_at entries (at most
-  // kStreamCap - 128, so one more chunk word per lane always fits)
-  const int cut_at = kStreamCap - 128;
+  // kStreamCap - 128, so one more chunk word per lane always fits); cutting
+  // early in the row raises t sooner and spares later chunks their pushes
+  const int cut_at = min(kStreamCap - 128, max(2 * k, 128));
   // G groups of gl lanes for the opening threshold: one group (the chunk's
   // maximum, a true bound) for k = 1; else G >= 8 groups and G >= 2.5 x
   // (x = top-k entries expected in one chunk), so that for a row in random
