@@ -192,6 +192,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 
 // ---- small math ---------------------------------------------------------------
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream serialization attribute may start while the previous kernel of its
+// stream is still running: grid_dep_wait() returns once that kernel has
+// completed and its writes are visible (at once for a kernel launched
+// without the attribute), and grid_dep_launch() lets the next kernel launched
+// with the attribute start once every CTA of this one has called it.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

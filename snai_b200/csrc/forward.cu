@@ -70,6 +70,8 @@ __global__ void __launch_bounds__(kNormThreads) embed_norm_kernel(const RowDesc 
                                                                   TA *__restrict__ x, int *__restrict__ hist,
                                                                   int *__restrict__ seq_len, int V, int D, int ctx) {
   __shared__ float red[kNormThreads / 32];
+  grid_dep_wait();
+  grid_dep_launch();
   const int m = blockIdx.x;
   const RowDesc rd = rows[m];
   const int raw = tokens_d ? tokens_d[rd.token] : rd.token;
@@ -92,6 +94,8 @@ template <typename TA>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *__restrict__ h, const int2 *__restrict__ gather,
                                                                const float *__restrict__ w, TA *__restrict__ x, int D) {
   __shared__ float red[kNormThreads / 32];
+  grid_dep_wait();
+  grid_dep_launch();
   const int m = blockIdx.x;
   const int src = gather ? gather[m].x : m;
   const float *hr = h + (size_t)src * D;
@@ -170,6 +174,8 @@ __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
   float *red = smem_att;        // [32]
   float *acc = smem_att + 32;   // [4 warps][64]
   float *s = smem_att + 32 + 4 * HS;
+  grid_dep_wait();
+  grid_dep_launch();
   const int m = blockIdx.y, head = blockIdx.x;
   const RowDesc rd = rows[m];
   const int n = rd.pos + 1;
@@ -263,6 +269,8 @@ __global__ void __launch_bounds__(kAttThreads) attention_generic_kernel(
   extern __shared__ float smem_att[];
   float *red = smem_att;
   float *s = smem_att + 32;
+  grid_dep_wait();
+  grid_dep_launch();
   const int m = blockIdx.y, head = blockIdx.x;
   const RowDesc rd = rows[m];
   const int n = rd.pos + 1;
@@ -310,48 +318,122 @@ __global__ void __launch_bounds__(kAttThreads) attention_generic_kernel(
 // fp32 GEMV for small row counts: C[M,N] = X[M,K] * W[N,K]^T
 // ============================================================================
 //
-// Each warp owns two adjacent weight rows (a RoPE pair), streams them once
-// with 16-byte loads (lane k-slices of 4), and multiplies them with up to MB
-// activation rows per sweep; activation rows are re-read through L1/L2.
+// A warp owns four consecutive weight rows (two RoPE pairs) over one slice of
+// K; the S warps of a row quad split K between them and P quads share a CTA
+// (S * P <= 8 warps).  A pass covers up to 512 columns of the slice: each
+// lane loads its 4 x 16 weights of the pass into registers at once (8 KB of
+// loads in flight per warp), so with one pass per slice (K <= 4096) a quad is
+// read from HBM once whatever M is.  Activation rows come through L1 in
+// groups of MB; the 4 * MB partial dot products of a group are summed over
+// the warp by a transposing butterfly (a stage halves the values each lane
+// keeps, so a group costs about 4 * MB shuffles instead of 20 * MB), the S
+// slice sums are added in slice order through shared memory, and the lanes
+// owning an even row emit (row, row + 1) pairs to the epilogue.
 
-constexpr int kGemvWarps = 8;
+constexpr int kGemvMaxWarps = 8;
+constexpr int kGemvPass = 512;  // K columns per warp pass: 4 float4 per lane per row
+
+// Butterfly reduce-scatter over the warp: stage O (16, 8, ...) pairs lane
+// with lane ^ O; while a lane holds C > 1 values it keeps the lower or upper
+// half (by lane & O) and adds the partner's copy of that half.  Afterwards
+// the lane holds in v[0] the warp sum of value lane / (32 / NV).
+template <int C, int O, int NV>
+__device__ __forceinline__ void gemv_reduce(float (&v)[NV], int lane) {
+  if constexpr (O > 0) {
+    if constexpr (C > 1) {
+      constexpr int H = C / 2;
+      const bool up = (lane & O) != 0;
+#pragma unroll
+      for (int j = 0; j < H; ++j) {
+        const float send = up ? v[j] : v[j + H];
+        const float keep = up ? v[j + H] : v[j];
+        v[j] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, O));
+      }
+      gemv_reduce<H, O / 2, NV>(v, lane);
+    } else {
+      v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], O));
+      gemv_reduce<1, O / 2, NV>(v, lane);
+    }
+  }
+}
 
 template <int MB, class Epi>
-__global__ void __launch_bounds__(kGemvWarps * 32) gemv_f32_kernel(const float *__restrict__ W, int N, int K,
-                                                                   const float *__restrict__ X, int M, Epi epi) {
+__global__ void __launch_bounds__(kGemvMaxWarps * 32, 2)
+    gemv_f32_kernel(const float *__restrict__ W, int N, int K, const float *__restrict__ X, int M, int S, int slice,
+                    Epi epi) {
+  constexpr int NV = 4 * MB;   // values a lane reduces per group: [m][row]
+  constexpr int G = 32 / NV;   // lanes holding each reduced value
+  __shared__ float part[kGemvMaxWarps][NV];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = (blockIdx.x * kGemvWarps + warp) * 2;
-  if (n0 >= N) return;
-  const bool two = n0 + 1 < N;
-  const float *w0 = W + (size_t)n0 * K;
-  const float *w1 = two ? w0 + K : w0;
-  for (int m0 = 0; m0 < M; m0 += MB) {
-    float a0[MB], a1[MB];
+  const int s = warp % S;
+  const int n0 = (blockIdx.x * (blockDim.x >> 5) / S + warp / S) * 4;
+  const bool live = n0 < N;
+  const int ks = s * slice, ke = min(K, ks + slice);
+  const int passes = ke > ks ? (ke - ks + kGemvPass - 1) / kGemvPass : 0;
+  float4 w[4][4];
+  auto load_w = [&](int kb) {
 #pragma unroll
-    for (int j = 0; j < MB; ++j) a0[j] = a1[j] = 0.f;
-#pragma unroll 2
-    for (int k = lane * 4; k < K; k += 128) {
-      const float4 wa = __ldcs(reinterpret_cast<const float4 *>(w0 + k));
-      const float4 wb = __ldcs(reinterpret_cast<const float4 *>(w1 + k));
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
-      for (int j = 0; j < MB; ++j) {
-        if (m0 + j < M) {
-          const float4 xv = __ldg(reinterpret_cast<const float4 *>(X + (size_t)(m0 + j) * K + k));
-          a0[j] = fmaf(wa.x, xv.x, fmaf(wa.y, xv.y, fmaf(wa.z, xv.z, fmaf(wa.w, xv.w, a0[j]))));
-          a1[j] = fmaf(wb.x, xv.x, fmaf(wb.y, xv.y, fmaf(wb.z, xv.z, fmaf(wb.w, xv.w, a1[j]))));
+      for (int i = 0; i < 4; ++i) {
+        const int k = kb + lane * 4 + 128 * i;
+        w[r][i] = (live && n0 + r < N && k < ke)
+                      ? __ldcg(reinterpret_cast<const float4 *>(W + (size_t)(n0 + r) * K + k))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+  };
+  auto dot_group = [&](int kb, int m0, float (&acc)[NV]) {
+#pragma unroll
+    for (int j = 0; j < MB; ++j) {
+      if (m0 + j >= M) break;
+      const float *xr = X + (size_t)(m0 + j) * K;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = kb + lane * 4 + 128 * i;
+        if (k < ke) {
+          const float4 xv = __ldg(reinterpret_cast<const float4 *>(xr + k));
+#pragma unroll
+          for (int r = 0; r < 4; ++r)
+            acc[4 * j + r] = fmaf(w[r][i].x, xv.x, fmaf(w[r][i].y, xv.y, fmaf(w[r][i].z, xv.z,
+                                                                               fmaf(w[r][i].w, xv.w, acc[4 * j + r]))));
         }
       }
     }
+  };
+  // the weights do not depend on the previous kernel: with one pass they are
+  // in flight before the wait for its results
+  if (passes == 1) load_w(ks);
+  grid_dep_wait();
+  grid_dep_launch();
+  for (int m0 = 0; m0 < M; m0 += MB) {
+    float acc[NV];
 #pragma unroll
-    for (int j = 0; j < MB; ++j) {
-      a0[j] = warp_sum(a0[j]);
-      a1[j] = warp_sum(a1[j]);
+    for (int j = 0; j < NV; ++j) acc[j] = 0.f;
+    if (passes == 1) {
+      dot_group(ks, m0, acc);
+    } else {
+      for (int p = 0; p < passes; ++p) {
+        load_w(ks + p * kGemvPass);
+        dot_group(ks + p * kGemvPass, m0, acc);
+      }
     }
-#pragma unroll
-    for (int j = 0; j < MB; ++j) {
-      if (lane == j && m0 + j < M) {
-        float v[16] = {a0[j], a1[j]};
-        epi.store(m0 + j, n0, v, two ? 2 : 1);
+    gemv_reduce<NV, 16, NV>(acc, lane);
+    float tot = acc[0];
+    if (S > 1) {
+      if (lane % G == 0) part[warp][lane / G] = tot;
+      __syncthreads();
+      if (s == 0) {
+        tot = part[warp][lane / G];
+        for (int t = 1; t < S; ++t) tot = __fadd_rn(tot, part[warp + t][lane / G]);
+      }
+      __syncthreads();
+    }
+    if (s == 0) {
+      const float t1 = __shfl_down_sync(0xffffffffu, tot, G);
+      const int idx = lane / G, m = m0 + idx / 4, r = idx % 4;
+      if (live && lane % G == 0 && (r & 1) == 0 && m < M && n0 + r < N) {
+        float v[16] = {tot, t1};
+        epi.store(m, n0 + r, v, n0 + r + 1 < N ? 2 : 1);
       }
     }
   }
@@ -516,19 +598,42 @@ static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *
   return launch_tcp<TIn, 128>(e, M, N, K, A, W, epi);
 }
 
+// Launches kern on the engine's stream; with pdl as a programmatic dependent
+// launch (the kernel begins with grid_dep_wait before it reads anything the
+// previous kernel writes).
+template <typename... KArgs, typename... Args>
+static void launch_k(Engine &e, bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = e.stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  e.launches++;
+}
+
 template <class Epi>
 static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const float *W, const Epi &epi) {
-  const int warps = (N + 1) / 2;
-  dim3 grid((warps + kGemvWarps - 1) / kGemvWarps);
-  if (M <= 1)
-    gemv_f32_kernel<1, Epi><<<grid, kGemvWarps * 32, 0, e.stream>>>(W, N, K, X, M, epi);
-  else if (M <= 2)
-    gemv_f32_kernel<2, Epi><<<grid, kGemvWarps * 32, 0, e.stream>>>(W, N, K, X, M, epi);
-  else if (M <= 4)
-    gemv_f32_kernel<4, Epi><<<grid, kGemvWarps * 32, 0, e.stream>>>(W, N, K, X, M, epi);
-  else
-    gemv_f32_kernel<8, Epi><<<grid, kGemvWarps * 32, 0, e.stream>>>(W, N, K, X, M, epi);
-  e.launches++;
+  // S warps split K into slices of whole 128-column steps (one 512-column
+  // pass each up to K = 4096); P row quads per CTA while that still leaves
+  // two CTAs per SM
+  const int S = std::max(1, std::min(kGemvMaxWarps, (K + kGemvPass - 1) / kGemvPass));
+  const int slice = ((K + S - 1) / S + 127) / 128 * 128;
+  const int quads = (N + 3) / 4, target = 2 * sm_count(e.device);
+  int P = 1;
+  while (2 * P * S <= kGemvMaxWarps && quads / (2 * P) >= target) P *= 2;
+  const dim3 grid((quads + P - 1) / P), block(32 * S * P);
+  auto kern = M <= 1 ? gemv_f32_kernel<1, Epi>
+              : M <= 2 ? gemv_f32_kernel<2, Epi>
+              : M <= 4 ? gemv_f32_kernel<4, Epi>
+                       : gemv_f32_kernel<8, Epi>;
+  launch_k(e, true, kern, grid, block, 0, W, N, K, X, M, S, slice, epi);
 }
 
 // C[M,N] = A[M,K] * W[N,K]^T with the epilogue `epi`.  `a_bytes` / `out_bytes`:
@@ -566,18 +671,15 @@ static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_pos
   }
   if (d.hs == 64) {
     const size_t sm = (32 + 4 * 64 + (size_t)max_n) * sizeof(float);
-    attention_hs64_kernel<TA><<<grid, kAttThreads, sm, e.stream>>>(e.rows_d, e.q, e.kv, out, d.D, d.att_ch,
-                                                                    e.kv_slot_stride, layer_off, e.kv_part_stride,
-                                                                    e.kv_head_stride, e.sqrt_hs,
-                                                                    defer ? e.kvs : nullptr, e.rope);
+    launch_k(e, !tc_path(e, M), attention_hs64_kernel<TA>, grid, dim3(kAttThreads), sm, e.rows_d, e.q, e.kv, out,
+             d.D, d.att_ch, e.kv_slot_stride, layer_off, e.kv_part_stride, e.kv_head_stride, e.sqrt_hs,
+             defer ? e.kvs : nullptr, e.rope);
   } else {
     const size_t sm = (32 + (size_t)max_n + 2 * (size_t)d.hs) * sizeof(float);
-    attention_generic_kernel<TA><<<grid, kAttThreads, sm, e.stream>>>(e.rows_d, e.q, e.kv, out, d.D, d.att_ch, d.hs,
-                                                                       e.kv_slot_stride, layer_off, e.kv_part_stride,
-                                                                       e.kv_head_stride, e.sqrt_hs,
-                                                                       defer ? e.kvs : nullptr, e.rope);
+    launch_k(e, !tc_path(e, M), attention_generic_kernel<TA>, grid, dim3(kAttThreads), sm, e.rows_d, e.q, e.kv,
+             out, d.D, d.att_ch, d.hs, e.kv_slot_stride, layer_off, e.kv_part_stride, e.kv_head_stride, e.sqrt_hs,
+             defer ? e.kvs : nullptr, e.rope);
   }
-  e.launches++;
   // K and V of positions 0..pos per row, q in, att out
   prof_end(e, tok, kProfAttention, kv_positions * 2.0 * d.att_ch * 4 + (double)M * d.att_ch * 4 + (double)M * d.D * sizeof(TA),
            kv_positions * 4.0 * d.att_ch);
@@ -586,8 +688,7 @@ static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_pos
 template <typename TA>
 static void launch_norm(Engine &e, int M, const int2 *gather, const float *w, TA *x) {
   const int tok = prof_begin(e);
-  rmsnorm_kernel<TA><<<M, kNormThreads, 0, e.stream>>>(e.h, gather, w, x, e.d.D);
-  e.launches++;
+  launch_k(e, !tc_path(e, M), rmsnorm_kernel<TA>, dim3(M), dim3(kNormThreads), 0, e.h, gather, w, x, e.d.D);
   prof_end(e, tok, kProfNorm, (double)M * e.d.D * (4 + sizeof(TA)), 0.0);
 }
 
@@ -600,9 +701,8 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
   TA *att = static_cast<TA *>(e.att);
   TA *u = static_cast<TA *>(e.u);
   int tok = prof_begin(e);
-  embed_norm_kernel<TA><<<M, kNormThreads, 0, e.stream>>>(e.rows_d, tokens_d, e.emb, e.layers[0].rms_att, e.h, x,
-                                                          e.hist, e.seq_len_d, d.V, d.D, d.ctx);
-  e.launches++;
+  launch_k(e, !tc_path(e, M), embed_norm_kernel<TA>, dim3(M), dim3(kNormThreads), 0, e.rows_d, tokens_d, e.emb,
+           e.layers[0].rms_att, e.h, x, e.hist, e.seq_len_d, d.V, d.D, d.ctx);
   prof_end(e, tok, kProfEmbed, (double)M * d.D * (8 + ea), 0.0);
   for (int l = 0; l < d.L; ++l) {
     const LayerWeights &w = e.layers[l];

@@ -166,6 +166,31 @@ def test_pair_tiles_prefill_and_decode(prec, model_dir, built):
     e.close()
 
 
+@pytest.mark.parametrize("B", [1, 2, 3, 5, 9])
+def test_gemv_shapes(B, model_dir, built):
+    """fp32 GEMV edges: d=1040 (K=1040 in three 384-column slices; W_down's
+    K=4160 in eight 640-column slices of two passes, the last slice empty),
+    V=1001 (a last row quad of one row), 16 heads of 64 channels (16 unused
+    channels), and row counts that fill activation groups of 1, 2, 4 and 8
+    partly (prompt rows 3B, decode rows B)."""
+    path = make_model(model_dir, "gemv.snai", 1001, 1040, 16, 1, seed=33)
+    plen, steps = 3, 2
+    rng = np.random.default_rng(40 + B)
+    prompts = rng.integers(0, 1001, (B, plen)).astype(np.int32)
+    forced = rng.integers(0, 1001, (B, steps)).astype(np.int32)
+    e = Cortex(path, num_heads=16, max_seqs=B, precision=PREC_FP32)
+    got = [e.forward(prompts)]
+    for s in range(steps):
+        got.append(e.forward(forced[:, s:s + 1]))
+    o = O.Oracle(path, num_heads=16)
+    _, ref, _ = o.generate(prompts, steps, np.zeros((B, steps), np.float32), VARIANT_A, 0.8, 1.15,
+                           forced=forced, want_logits=True)
+    for s in range(steps + 1):
+        err = max(rel_err(got[s][b], ref[b, s]) for b in range(B))
+        assert err < TOL[PREC_FP32], (s, err)
+    e.close()
+
+
 @pytest.mark.parametrize("prec", [PREC_FP32, PREC_BF16])
 def test_single_sequence_long_prompt(prec, small_model, built):
     """A 90-token prompt of one sequence: 90 rows in one pass (tensor cores in
