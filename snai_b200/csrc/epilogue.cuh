@@ -197,9 +197,13 @@ struct EpiResidual {
         *reinterpret_cast<float4 *>(p + 4 * i) = o[i];
       }
     } else {
+      // partial runs (the GEMV's row pairs): a reduction at L2 instead of a
+      // load the thread would wait for; each element has this one addend, so
+      // h + v is rounded once, as in the loaded form (the atomic flushes
+      // subnormal sums to zero)
 #pragma unroll
       for (int i = 0; i < 16; ++i)
-        if (i < cnt) p[i] = __fadd_rn(p[i], v[i]);
+        if (i < cnt) atomicAdd(p + i, v[i]);
     }
   }
 };

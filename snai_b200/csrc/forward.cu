@@ -62,6 +62,37 @@ __device__ __forceinline__ float rms_inv(float ss, int D) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
 }
 
+// rms_inv of a D-row computed by one warp in exactly the operations and order
+// of block_sumsq in a kNormThreads CTA (virtual warp w = threads 32w..32w+31),
+// so a GEMV that normalises its own input rows reads the values the norm
+// kernel would have written.
+__device__ __forceinline__ float warp_row_rms_inv(const float *__restrict__ hr, int D, int lane) {
+  constexpr int NW = kNormThreads / 32;
+  float p[NW];
+#pragma unroll
+  for (int w = 0; w < NW; ++w) p[w] = 0.f;
+  // 4 * kNormThreads elements per round, all loads in flight before the
+  // sums; a missing element adds 0 * 0, which leaves the sum as it is
+  for (int base = 0; base < D; base += 4 * kNormThreads) {
+    float v[NW][4];
+#pragma unroll
+    for (int w = 0; w < NW; ++w)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = base + 32 * w + lane + kNormThreads * j;
+        v[w][j] = i < D ? __ldg(hr + i) : 0.f;
+      }
+#pragma unroll
+    for (int w = 0; w < NW; ++w)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[w] = __fmaf_rn(v[w][j], v[w][j], p[w]);
+  }
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) t += warp_sum(p[w]);
+  return rms_inv(t, D);
+}
+
 template <typename TA>
 __global__ void __launch_bounds__(kNormThreads) embed_norm_kernel(const RowDesc *__restrict__ rows,
                                                                   const int *__restrict__ tokens_d,
@@ -329,6 +360,10 @@ __global__ void __launch_bounds__(kAttThreads) attention_generic_kernel(
 // keeps, so a group costs about 4 * MB shuffles instead of 20 * MB), the S
 // slice sums are added in slice order through shared memory, and the lanes
 // owning an even row emit (row, row + 1) pairs to the epilogue.
+//
+// With NORM the input rows are RMSNorm(X[src(m)], nw) (src(m) = m, or
+// gather[m].x): each warp computes the rows' rms_inv itself, so a pass of at
+// most a few rows needs no separate norm launch.
 
 constexpr int kGemvMaxWarps = 8;
 constexpr int kGemvPass = 512;  // K columns per warp pass: 4 float4 per lane per row
@@ -357,10 +392,15 @@ __device__ __forceinline__ void gemv_reduce(float (&v)[NV], int lane) {
   }
 }
 
-template <int MB, class Epi>
+struct GemvNorm {
+  const float *w;       // RMSNorm weights [K]; nullptr: X is the input as is
+  const int2 *gather;   // input row m = X[gather[m].x], or X[m] when nullptr
+};
+
+template <int MB, bool NORM, class Epi>
 __global__ void __launch_bounds__(kGemvMaxWarps * 32, 2)
     gemv_f32_kernel(const float *__restrict__ W, int N, int K, const float *__restrict__ X, int M, int S, int slice,
-                    Epi epi) {
+                    Epi epi, GemvNorm nrm) {
   constexpr int NV = 4 * MB;   // values a lane reduces per group: [m][row]
   constexpr int G = 32 / NV;   // lanes holding each reduced value
   __shared__ float part[kGemvMaxWarps][NV];
@@ -386,12 +426,26 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 2)
 #pragma unroll
     for (int j = 0; j < MB; ++j) {
       if (m0 + j >= M) break;
-      const float *xr = X + (size_t)(m0 + j) * K;
+      const float *xr;
+      float inv = 1.f;
+      if constexpr (NORM) {
+        xr = X + (size_t)(nrm.gather ? nrm.gather[m0 + j].x : m0 + j) * K;
+        inv = warp_row_rms_inv(xr, K, lane);
+      } else {
+        xr = X + (size_t)(m0 + j) * K;
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int k = kb + lane * 4 + 128 * i;
         if (k < ke) {
-          const float4 xv = __ldg(reinterpret_cast<const float4 *>(xr + k));
+          float4 xv = __ldg(reinterpret_cast<const float4 *>(xr + k));
+          if constexpr (NORM) {
+            const float4 nw = __ldg(reinterpret_cast<const float4 *>(nrm.w + k));
+            xv.x = __fmul_rn(__fmul_rn(xv.x, inv), nw.x);
+            xv.y = __fmul_rn(__fmul_rn(xv.y, inv), nw.y);
+            xv.z = __fmul_rn(__fmul_rn(xv.z, inv), nw.z);
+            xv.w = __fmul_rn(__fmul_rn(xv.w, inv), nw.w);
+          }
 #pragma unroll
           for (int r = 0; r < 4; ++r)
             acc[4 * j + r] = fmaf(w[r][i].x, xv.x, fmaf(w[r][i].y, xv.y, fmaf(w[r][i].z, xv.z,
@@ -619,7 +673,8 @@ static void launch_k(Engine &e, bool pdl, void (*kern)(KArgs...), dim3 grid, dim
 }
 
 template <class Epi>
-static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const float *W, const Epi &epi) {
+static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const float *W, const Epi &epi,
+                        GemvNorm nrm) {
   // S warps split K into slices of whole 128-column steps (one 512-column
   // pass each up to K = 4096); P row quads per CTA while that still leaves
   // two CTAs per SM
@@ -629,18 +684,24 @@ static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const fl
   int P = 1;
   while (2 * P * S <= kGemvMaxWarps && quads / (2 * P) >= target) P *= 2;
   const dim3 grid((quads + P - 1) / P), block(32 * S * P);
-  auto kern = M <= 1 ? gemv_f32_kernel<1, Epi>
-              : M <= 2 ? gemv_f32_kernel<2, Epi>
-              : M <= 4 ? gemv_f32_kernel<4, Epi>
-                       : gemv_f32_kernel<8, Epi>;
-  launch_k(e, true, kern, grid, block, 0, W, N, K, X, M, S, slice, epi);
+  void (*kern)(const float *, int, int, const float *, int, int, int, Epi, GemvNorm);
+  if (nrm.w)  // one row (kGemvNormRows)
+    kern = gemv_f32_kernel<1, true, Epi>;
+  else
+    kern = M <= 1   ? gemv_f32_kernel<1, false, Epi>
+           : M <= 2 ? gemv_f32_kernel<2, false, Epi>
+           : M <= 4 ? gemv_f32_kernel<4, false, Epi>
+                    : gemv_f32_kernel<8, false, Epi>;
+  launch_k(e, true, kern, grid, block, 0, W, N, K, X, M, S, slice, epi, nrm);
 }
 
 // C[M,N] = A[M,K] * W[N,K]^T with the epilogue `epi`.  `a_bytes` / `out_bytes`:
 // bytes per element of A and algorithmic output bytes (for the profiler).
+// With nrm.w (GEMV path only) A is the residual stream h and the input rows
+// are RMSNorm(h, nrm.w), normalised inside the GEMV.
 template <class Epi>
 static int project(Engine &e, int kind, int M, int N, int K, const void *A, const float *W32,
-                   const __nv_bfloat16 *W16, const Epi &epi, double out_bytes) {
+                   const __nv_bfloat16 *W16, const Epi &epi, double out_bytes, GemvNorm nrm = GemvNorm{}) {
   if (M <= 0) return 0;
   const bool tc = tc_path(e, M);
   const bool bf = tc && e.precision == kBF16;
@@ -650,7 +711,7 @@ static int project(Engine &e, int kind, int M, int N, int K, const void *A, cons
   if (tc) {
     rc = bf ? launch_tc<__nv_bfloat16>(e, M, N, K, A, W16, epi) : launch_tc<float>(e, M, N, K, A, W32, epi);
   } else {
-    launch_gemv(e, M, N, K, static_cast<const float *>(A), W32, epi);
+    launch_gemv(e, M, N, K, static_cast<const float *>(A), W32, epi, nrm);
   }
   prof_end(e, tok, kind, w_bytes + a_bytes + out_bytes, 2.0 * M * N * K);
   return rc;
@@ -692,6 +753,15 @@ static void launch_norm(Engine &e, int M, const int2 *gather, const float *w, TA
   prof_end(e, tok, kProfNorm, (double)M * e.d.D * (4 + sizeof(TA)), 0.0);
 }
 
+// Passes of at most this many rows on the GEMV path normalise inside the
+// GEMVs that consume the norms.  Each warp recomputes a row's rms_inv (one
+// more L2 round trip per row before its dot products), which pays for the
+// norm launch it saves at one row (80.9 -> 72.2 us per d=1024 decode pass),
+// breaks even at two and loses from three rows on.
+constexpr int kGemvNormRows = 1;
+
+static bool gemv_norm(const Engine &e, int M) { return !tc_path(e, M) && M <= kGemvNormRows; }
+
 template <typename TA>
 static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, bool out_tc, double kv_positions,
                            bool defer) {
@@ -709,19 +779,25 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
     EpiQKV eq{e.rows_d, e.q, e.kv, e.rope, d.D, d.att_ch, d.hs, e.kv_slot_stride, (size_t)l * e.kv_layer_stride,
               e.kv_part_stride, e.kv_head_stride, defer ? e.kvs : nullptr};
     if (tc_path(e, M)) qkv_tma_maps(e, M, &eq);
-    int rc = project(e, kProfQKV, M, 3 * d.D, d.D, x, w.wqkv, w.wqkv_h, eq, 3.0 * M * d.att_ch * 4);
+    // layer 0 reads the embedding kernel's normalised rows; later layers
+    // normalise h inside the QKV GEMV on a small pass
+    const bool fuse = gemv_norm(e, M);
+    const bool fq = fuse && l > 0;
+    int rc = project(e, kProfQKV, M, 3 * d.D, d.D, fq ? static_cast<const void *>(e.h) : x, w.wqkv, w.wqkv_h, eq,
+                     3.0 * M * d.att_ch * 4, fq ? GemvNorm{w.rms_att, nullptr} : GemvNorm{});
     if (rc) return rc;
     launch_attention<TA>(e, M, l, att, kv_positions, defer);
     EpiResidual res;
     if (!residual_epi(e, M, &res)) return -5;
     rc = project(e, kProfWo, M, d.D, d.D, att, w.wo, w.wo_h, res, 8.0 * M * d.D);
     if (rc) return rc;
-    launch_norm<TA>(e, M, nullptr, w.rms_ffn, x);
-    rc = project(e, kProfUp, M, d.F, d.D, x, w.wup, w.wup_h, EpiSilu<TA>{u, d.F}, ea * M * d.F);
+    if (!fuse) launch_norm<TA>(e, M, nullptr, w.rms_ffn, x);
+    rc = project(e, kProfUp, M, d.F, d.D, fuse ? static_cast<const void *>(e.h) : x, w.wup, w.wup_h,
+                 EpiSilu<TA>{u, d.F}, ea * M * d.F, fuse ? GemvNorm{w.rms_ffn, nullptr} : GemvNorm{});
     if (rc) return rc;
     rc = project(e, kProfDown, M, d.D, d.F, u, w.wdown, w.wdown_h, res, 8.0 * M * d.D);
     if (rc) return rc;
-    if (l + 1 < d.L) launch_norm<TA>(e, M, nullptr, e.layers[l + 1].rms_att, x);
+    if (l + 1 < d.L && !fuse) launch_norm<TA>(e, M, nullptr, e.layers[l + 1].rms_att, x);
   }
   if (n_out > 0) {
     EpiLogits el{e.logits, e.outrows_d, (long long)d.V};
@@ -731,6 +807,9 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
       launch_norm<__nv_bfloat16>(e, n_out, e.outrows_d, e.rms_final, xo);
       return project(e, kProfLogits, n_out, d.V, d.D, xo, e.w_out, e.w_out_h, el, ob);
     }
+    if (gemv_norm(e, n_out))
+      return project(e, kProfLogits, n_out, d.V, d.D, e.h, e.w_out, e.w_out_h, el, ob,
+                     GemvNorm{e.rms_final, e.outrows_d});
     float *xo = static_cast<float *>(e.xo);
     launch_norm<float>(e, n_out, e.outrows_d, e.rms_final, xo);
     return project(e, kProfLogits, n_out, d.V, d.D, xo, e.w_out, e.w_out_h, el, ob);
