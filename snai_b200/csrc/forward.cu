@@ -454,11 +454,12 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 2)
       }
     }
   };
-  // the weights do not depend on the previous kernel: with one pass they are
-  // in flight before the wait for its results
+  // nothing before the wait reads what an earlier kernel writes: the next
+  // kernel may start at once (it waits for this one in turn), and with one
+  // pass the weights are in flight before the wait for the previous results
+  grid_dep_launch();
   if (passes == 1) load_w(ks);
   grid_dep_wait();
-  grid_dep_launch();
   for (int m0 = 0; m0 < M; m0 += MB) {
     float acc[NV];
 #pragma unroll
