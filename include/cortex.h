@@ -219,14 +219,29 @@ CORTEX_API int cortex_profile_read(void *state, int kind, long long *launches, d
  * effects as cortex_forward_batch; the pass's activation scratch lives in
  * one 8 MiB array in the library's device image instead of the state's
  * buffers, and the call makes no cudaMalloc/cudaFree or other allocating
- * GPU call.  Rows are processed in chunks that fit the array; a model whose
- * single row needs more than 8 MiB of scratch is rejected with an error.
- * The first call on a device looks the array's address up (make that first
- * call before any stream capture).  All calls on a device share the array:
- * calls that overlap on the GPU (two streams, two threads) race.  Nothing in
- * the array has to start at zero: every byte a call reads it wrote first. */
+ * GPU call.  Rows are processed in chunks that fit the array (whole 128-row
+ * tiles when more than 128 rows fit); a model whose single row needs more
+ * than 8 MiB of scratch is rejected with an error.  Every call looks the
+ * array's device address up with the state's device current (the first
+ * call on a device may load the library's device code, so make it before
+ * any stream capture).  While the kernel profiler (cortex_profile_enable)
+ * is on, its first calls create the CUDA events it brackets launches with;
+ * with the profiler off nothing is created.  All calls on a device share
+ * the array: calls that overlap on the GPU (two streams, two threads) race.
+ * Nothing in the array has to start at zero: every byte a call reads it
+ * wrote first. */
 CORTEX_API int cortex_forward_batch_noalloc(void *state, const int *tokens, int batch, int n_tok, const int *slots,
                                             float *logits, int flags);
+
+/* Self-test of the failure path every kernel wait takes.  No counterpart in
+ * the reference (whose engine has no device waits).  Queues one kernel on
+ * the state's stream that waits on an mbarrier nothing completes; the wait
+ * gives up after limit_ns (1 us .. 2 s) of GPU time, records its error code
+ * in the state's device error word and returns, so the GPU context stays
+ * usable.  The next cortex_synchronize then returns -6 and
+ * cortex_last_error() names the expired wait; the error word is cleared by
+ * that report.  Returns 0 once queued. */
+CORTEX_API int cortex_selftest_wait_timeout(void *state, long long limit_ns);
 
 /* Number of kernels the state has launched since it was created. */
 CORTEX_API long long cortex_kernel_launches(void *state);

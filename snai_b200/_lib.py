@@ -73,6 +73,7 @@ SIGNATURES = {
     "cortex_profile_read": (c_int, [c_void_p, c_int, ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(c_double),
                                     ctypes.POINTER(c_double), ctypes.POINTER(c_double)]),
     "cortex_forward_batch_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int]),
+    "cortex_selftest_wait_timeout": (c_int, [c_void_p, ctypes.c_longlong]),
     "cortex_kernel_launches": (ctypes.c_longlong, [c_void_p]),
 }
 

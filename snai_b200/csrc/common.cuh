@@ -19,6 +19,7 @@ enum DevError : int {
   kErrWaitAccum = 3,    // epilogue timed out waiting for the accumulator
   kErrWaitDrain = 4,    // exit path timed out draining in-flight copies
   kErrSamplerArgs = 5,  // sampler saw an impossible row (checked on host too)
+  kErrWaitSelfTest = 6, // the bounded-wait self-test's wait expired (its expected outcome)
 };
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
@@ -65,17 +66,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Returns false (and
-// records `code`) if it has not completed within kWaitTimeoutNs.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code) {
+// records `code`) if it has not completed within `limit_ns` of global-timer
+// time.
+__device__ __forceinline__ bool mbar_wait_bounded_ns(uint64_t* bar, uint32_t parity, int* err, int code,
+                                                     unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0 && global_timer_ns() - t0 > kWaitTimeoutNs) {
+    if ((it & 63u) == 0 && global_timer_ns() - t0 > limit_ns) {
       record_error(err, code);
       return false;
     }
   }
+}
+
+// The same with the kernels' limit, kWaitTimeoutNs.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_bounded_ns(bar, parity, err, code, kWaitTimeoutNs);
 }
 
 // ---- clusters and distributed shared memory ----------------------------------

@@ -317,7 +317,10 @@ int check_device_error(Engine &e) {
   }
   if (code) {
     cudaMemset(e.err_d, 0, sizeof(int));
-    set_error("device-side error %d (a bounded wait expired or the sampler overflowed)", code);
+    set_error("device-side error %d (%s)", code,
+              code == 6   ? "the bounded-wait self-test's wait expired"
+              : code == 5 ? "the sampler saw an impossible row"
+                          : "a bounded wait in a kernel expired");
     return -6;
   }
   return 0;
@@ -835,17 +838,20 @@ extern "C" int cortex_decode_steps(void *state, const int *slots, int batch, int
   DeviceGuard g(e.device);
   const size_t need = (size_t)steps * batch;
   if (need > e.all_cap) {
+    // room for a whole context of steps of every slot (at most 8 M entries),
+    // so that later calls with more steps keep the captured graph
+    const size_t want = std::max(need, std::min<size_t>((size_t)e.d.ctx * e.max_seqs, 8u << 20));
     cudaFree(e.unif_all);
     cudaFree(e.ids_all);
     e.unif_all = nullptr;
     e.ids_all = nullptr;
     e.all_cap = 0;
-    if (cudaMalloc(&e.unif_all, need * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&e.ids_all, need * sizeof(int)) != cudaSuccess) {
-      set_error("out of device memory for %zu staged uniforms", need);
+    if (cudaMalloc(&e.unif_all, want * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&e.ids_all, want * sizeof(int)) != cudaSuccess) {
+      set_error("out of device memory for %zu staged uniforms", want);
       return -3;
     }
-    e.all_cap = need;
+    e.all_cap = want;
   }
   const cudaMemcpyKind in = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
   if (cudaMemcpyAsync(e.slots_d, sl.data(), sizeof(int) * batch, cudaMemcpyHostToDevice, e.stream) != cudaSuccess ||
@@ -1059,6 +1065,21 @@ extern "C" int cortex_profile_read(void *state, int kind, long long *launches, d
   return 0;
 }
 
+extern "C" int cortex_selftest_wait_timeout(void *state, long long limit_ns) {
+  clear_error();
+  if (!state) {
+    set_error("state is NULL");
+    return -1;
+  }
+  if (limit_ns < 1000 || limit_ns > 2000000000ll) {
+    set_error("limit_ns %lld outside [1 us, 2 s]", limit_ns);
+    return -2;
+  }
+  Engine &e = *static_cast<Engine *>(state);
+  DeviceGuard g(e.device);
+  return wait_selftest(e, limit_ns);
+}
+
 extern "C" long long cortex_kernel_launches(void *state) {
   return state ? static_cast<Engine *>(state)->launches : 0;
 }
@@ -1082,27 +1103,20 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-void *g_noalloc_ptr[kMaxDevices] = {};
-
 // Device address of g_noalloc_scratch on the current device.  The host-side
-// name is only a stand-in for the symbol, so the address is looked up once
-// per device (with that device current) and cached.
+// name is only a stand-in for the symbol, so the address is looked up with
+// the state's device current.  It is looked up on every call (cheap once
+// the module is loaded, and no allocation), so a context that was reset and
+// made again never sees a stale address.
 int noalloc_scratch(int dev, void **out) {
-  if (dev < 0 || dev >= kMaxDevices) {
-    set_error("device %d outside the no-alloc table", dev);
-    return -2;
+  void *p = nullptr;
+  const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (err != cudaSuccess || !p) {
+    set_error("cudaGetSymbolAddress(no-alloc scratch) failed on device %d: %s", dev, cudaGetErrorString(err));
+    cudaGetLastError();
+    return -4;
   }
-  if (!g_noalloc_ptr[dev]) {
-    void *p = nullptr;
-    const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (err != cudaSuccess || !p) {
-      set_error("cudaGetSymbolAddress(no-alloc scratch) failed on device %d: %s", dev, cudaGetErrorString(err));
-      return -4;
-    }
-    g_noalloc_ptr[dev] = p;
-  }
-  *out = g_noalloc_ptr[dev];
+  *out = p;
   return 0;
 }
 
@@ -1145,6 +1159,9 @@ extern "C" int cortex_forward_batch_noalloc(void *state, const int *tokens, int 
   const size_t one = carve_rows(probe, 1, nullptr);
   int rows = (int)std::min<size_t>((size_t)e.m_max, kNoAllocScratchBytes / std::max<size_t>(one, 1));
   while (rows > 0 && carve_rows(probe, rows, nullptr) > kNoAllocScratchBytes) --rows;
+  // whole 128-row tensor-core tiles per chunk when the array holds them (the
+  // state's own chunks are multiples of 128 rows too)
+  if (rows > 128) rows = rows / 128 * 128;
   if (rows < 1) {
     set_error("no-alloc forward: one row of this model needs %zu bytes of scratch, more than the %zu-byte array",
               one, kNoAllocScratchBytes);

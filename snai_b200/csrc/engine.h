@@ -4,7 +4,10 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
+#include <atomic>
 #include <map>
+#include <mutex>
+#include <set>
 #include <string>
 #include <tuple>
 #include <vector>
@@ -12,6 +15,31 @@
 namespace snai {
 
 enum Precision { kFP32 = 0, kTF32 = 1, kBF16 = 2 };
+
+// One-time set-up per device (kernel attributes), safe when several host
+// threads drive engines at once (one thread per GPU, or several on one GPU)
+// and for any device number: the set-up runs under the lock, so no thread
+// launches before the attribute it needs is in place.
+class DeviceOnce {
+ public:
+  // Runs f() (returning true on success) the first time `dev` asks; later
+  // calls return true at once.  A failed f() is retried by the next call.
+  template <class F>
+  bool run(int dev, F &&f) {
+    std::lock_guard<std::mutex> g(mu_);
+    if (done_.count(dev)) return true;
+    if (!f()) return false;
+    done_.insert(dev);
+    return true;
+  }
+
+ private:
+  std::mutex mu_;
+  std::set<int> done_;
+};
+
+// Multiprocessor count of a device (queried once per device, thread-safe).
+int device_sm_count(int dev);
 
 // Shape of a model.  Rules of core/cortex.nim:261-271: ffn = 4*dim whatever
 // the file header says; head size hs = dim/heads forced even and >= 2; RoPE
@@ -178,5 +206,10 @@ int check_sample_args(const SampleLaunch &a);
 // host-to-device copies.  Returns 0 or a negative error.
 int decode_step_device(Engine &e, int batch, const SampleLaunch &sampler);
 int launch_sampler(const SampleLaunch &a, cudaStream_t stream);
+
+// Bounded-wait self-test (forward.cu): a kernel whose mbarrier wait never
+// completes gives up after limit_ns and records an error in e.err_d; the id
+// buffer's first entry becomes 1.  Returns 0 once queued.
+int wait_selftest(Engine &e, long long limit_ns);
 
 }  // namespace snai

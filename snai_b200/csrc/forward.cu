@@ -18,6 +18,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 
@@ -399,7 +400,7 @@ struct GemvNorm {
 
 template <int MB, bool NORM, class Epi>
 __global__ void __launch_bounds__(kGemvMaxWarps * 32, 2)
-    gemv_f32_kernel(const float *__restrict__ W, int N, int K, const float *__restrict__ X, int M, int S, int slice,
+    snai_rowproj_f32_kernel(const float *__restrict__ W, int N, int K, const float *__restrict__ X, int M, int S, int slice,
                     Epi epi, GemvNorm nrm) {
   constexpr int NV = 4 * MB;   // values a lane reduces per group: [m][row]
   constexpr int G = 32 / NV;   // lanes holding each reduced value
@@ -499,16 +500,15 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 2)
 // ============================================================================
 
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
+  // a function-local static: initialised once, thread-safe
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
     cudaDriverEntryPointQueryResult q;
     void *p = nullptr;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+  }();
   return fn;
 }
 
@@ -581,30 +581,36 @@ static bool tc_path(const Engine &e, int M) {
   return e.precision != kFP32 && M >= 64 && e.d.D % 16 == 0 && e.d.D >= 64;
 }
 
-static int sm_count(int dev) {
-  static int cached[64] = {};
-  if (dev < 0 || dev >= 64) return 148;
-  if (!cached[dev]) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
+static int sm_count(int dev) { return device_sm_count(dev); }
+
+int device_sm_count(int dev) {
+  static std::atomic<int> cached[64];
+  const bool slot = dev >= 0 && dev < 64;
+  if (slot) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c) return c;
   }
-  return cached[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = 148;
+  }
+  if (slot) cached[dev].store(n, std::memory_order_relaxed);
+  return n;
 }
 
-// Persistent tcgen05 GEMM (gemm_tcp_kernel): 128 x BN tiles, one CTA per SM.
+// Persistent tcgen05 GEMM (snai_tileproj_tc_kernel): 128 x BN tiles, one CTA per SM.
 template <typename TIn, int BN, class Epi>
 static int launch_tcp(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
   constexpr int STAGES = BN == 256 ? 4 : 6;
   using Sm = TcpSmem<BN, STAGES>;
-  auto kern = gemm_tcp_kernel<TIn, BN, STAGES, Epi>;
-  static unsigned long long attr_set = 0;  // per instantiation, one bit per device
-  if (!(attr_set & (1ull << e.device))) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Sm::kBytes) != cudaSuccess) {
-      set_error("cudaFuncSetAttribute failed for the tensor-core GEMM");
-      return -5;
-    }
-    attr_set |= 1ull << e.device;
+  auto kern = snai_tileproj_tc_kernel<TIn, BN, STAGES, Epi>;
+  static DeviceOnce attr;  // per instantiation
+  if (!attr.run(e.device, [&] {
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Sm::kBytes) == cudaSuccess;
+      })) {
+    set_error("cudaFuncSetAttribute failed for the tensor-core projection");
+    return -5;
   }
   CUtensorMap ta, tb;
   const bool bf = sizeof(TIn) == 2;
@@ -619,19 +625,18 @@ static int launch_tcp(Engine &e, int M, int N, int K, const void *A, const void 
   return 0;
 }
 
-// CTA-pair tcgen05 GEMM (gemm_tc2_kernel): 256 x 256 tiles on SM pairs.
+// CTA-pair tcgen05 GEMM (snai_pairproj_tc_kernel): 256 x 256 tiles on SM pairs.
 template <typename TIn, class Epi>
 static int launch_tc2(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
   constexpr int STAGES = 6;
   using Sm = Tc2Smem<STAGES>;
-  auto kern = gemm_tc2_kernel<TIn, STAGES, Epi>;
-  static unsigned long long attr_set = 0;  // per instantiation, one bit per device
-  if (!(attr_set & (1ull << e.device))) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Sm::kBytes) != cudaSuccess) {
-      set_error("cudaFuncSetAttribute failed for the CTA-pair GEMM");
-      return -5;
-    }
-    attr_set |= 1ull << e.device;
+  auto kern = snai_pairproj_tc_kernel<TIn, STAGES, Epi>;
+  static DeviceOnce attr;  // per instantiation
+  if (!attr.run(e.device, [&] {
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Sm::kBytes) == cudaSuccess;
+      })) {
+    set_error("cudaFuncSetAttribute failed for the CTA-pair projection");
+    return -5;
   }
   CUtensorMap ta, tb;
   const bool bf = sizeof(TIn) == 2;
@@ -687,12 +692,12 @@ static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const fl
   const dim3 grid((quads + P - 1) / P), block(32 * S * P);
   void (*kern)(const float *, int, int, const float *, int, int, int, Epi, GemvNorm);
   if (nrm.w)  // one row (kGemvNormRows)
-    kern = gemv_f32_kernel<1, true, Epi>;
+    kern = snai_rowproj_f32_kernel<1, true, Epi>;
   else
-    kern = M <= 1   ? gemv_f32_kernel<1, false, Epi>
-           : M <= 2 ? gemv_f32_kernel<2, false, Epi>
-           : M <= 4 ? gemv_f32_kernel<4, false, Epi>
-                    : gemv_f32_kernel<8, false, Epi>;
+    kern = M <= 1   ? snai_rowproj_f32_kernel<1, false, Epi>
+           : M <= 2 ? snai_rowproj_f32_kernel<2, false, Epi>
+           : M <= 4 ? snai_rowproj_f32_kernel<4, false, Epi>
+                    : snai_rowproj_f32_kernel<8, false, Epi>;
   launch_k(e, true, kern, grid, block, 0, W, N, K, X, M, S, slice, epi, nrm);
 }
 
@@ -725,12 +730,13 @@ static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_pos
   const size_t layer_off = (size_t)layer * e.kv_layer_stride;
   dim3 grid(d.heads, M);
   const int max_n = d.ctx;
-  static unsigned long long attr_set = 0;  // one bit per device
-  if (!(attr_set & (1ull << e.device))) {
-    cudaFuncSetAttribute(attention_hs64_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    cudaFuncSetAttribute(attention_generic_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr_set |= 1ull << e.device;
-  }
+  static DeviceOnce attr;  // per instantiation
+  attr.run(e.device, [] {
+    return cudaFuncSetAttribute(attention_hs64_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                200 * 1024) == cudaSuccess &&
+           cudaFuncSetAttribute(attention_generic_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                200 * 1024) == cudaSuccess;
+  });
   if (d.hs == 64) {
     const size_t sm = (32 + 4 * 64 + (size_t)max_n) * sizeof(float);
     launch_k(e, !tc_path(e, M), attention_hs64_kernel<TA>, grid, dim3(kAttThreads), sm, e.rows_d, e.q, e.kv, out,
@@ -814,6 +820,36 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
     float *xo = static_cast<float *>(e.xo);
     launch_norm<float>(e, n_out, e.outrows_d, e.rms_final, xo);
     return project(e, kProfLogits, n_out, d.V, d.D, xo, e.w_out, e.w_out_h, el, ob);
+  }
+  return 0;
+}
+
+// ---- bounded-wait self-test ----
+//
+// One warp initialises an mbarrier that expects one arrival and waits on its
+// first phase, which nothing completes.  The wait gives up after limit_ns,
+// records kErrWaitSelfTest in the engine's error word (the same path every
+// kernel's expired wait takes) and the kernel returns normally, so the
+// context stays usable.  `out` receives 1 if the wait gave up, 0 if it
+// (impossibly) completed.
+__global__ void wait_selftest_kernel(int *__restrict__ err, int *__restrict__ out, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  const bool done = mbar_wait_bounded_ns(&bar, 0, err, kErrWaitSelfTest, limit_ns);
+  if (threadIdx.x == 0) *out = done ? 0 : 1;
+}
+
+int wait_selftest(Engine &e, long long limit_ns) {
+  wait_selftest_kernel<<<1, 32, 0, e.stream>>>(e.err_d, e.ids_d, (unsigned long long)limit_ns);
+  e.launches++;
+  const cudaError_t le = cudaGetLastError();
+  if (le != cudaSuccess) {
+    set_error("kernel launch failed: %s", cudaGetErrorString(le));
+    return -4;
   }
   return 0;
 }

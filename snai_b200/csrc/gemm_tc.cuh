@@ -242,7 +242,7 @@ struct TcpSmem {
 // CTA winds down.
 template <typename TIn, int BN, int STAGES, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tcp_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+    snai_tileproj_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                     int K, const __grid_constant__ Epi epi, int *err) {
   using Sm = TcpSmem<BN, STAGES>;
   constexpr int BK = TcKind<TIn>::kBK;
@@ -485,14 +485,14 @@ struct Tc2Smem {
 };
 
 // Persistent CTA-pair GEMM.  Pair p = blockIdx.x / 2 walks the 256 x 256
-// tiles p, p + pairs, ... (M-fastest).  Roles as in gemm_tcp_kernel; the MMA
+// tiles p, p + pairs, ... (M-fastest).  Roles as in snai_tileproj_tc_kernel; the MMA
 // warp of the leader (cluster rank 0) issues for both CTAs, its commits
 // arrive on both CTAs' barriers, and both CTAs' epilogue warps release an
 // accumulator on the leader's barrier (kEpiWarps per CTA).  Every wait is
 // bounded.
 template <typename TIn, int STAGES, class Epi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
-    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+    snai_pairproj_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                     int K, const __grid_constant__ Epi epi, int *err) {
   using Sm = Tc2Smem<STAGES>;
   constexpr int BK = TcKind<TIn>::kBK;

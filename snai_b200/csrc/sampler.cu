@@ -3929,28 +3929,24 @@ int check_sample_args(const SampleLaunch &s) {
 }
 
 static int sm_count() {
-  static int cached[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
-  if (!cached[dev]) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
+  return device_sm_count(dev);
+}
+
+// The full 227 KB of dynamic shared memory and the largest carve-out.
+template <class K>
+static bool set_smem_attrs(K kern) {
+  return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) == cudaSuccess &&
+         cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) == cudaSuccess;
 }
 
 template <class K>
 static void launch_persistent(K kern, const SampArgs &a, size_t sm, int per_sm, cudaStream_t st,
-                              unsigned long long &done) {
+                              DeviceOnce &done) {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(done & (1ull << dev))) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    done |= 1ull << dev;
-  }
+  done.run(dev, [&] { return set_smem_attrs(kern); });
   const int grid = std::min(a.rows, sm_count() * per_sm);
   kern<<<grid, kSampThreads, sm, st>>>(a);
 }
@@ -3958,14 +3954,10 @@ static void launch_persistent(K kern, const SampArgs &a, size_t sm, int per_sm, 
 // One cluster of C CTAs per row, clusters walking the rows; returns false if
 // the cluster shape cannot be scheduled (the caller falls back).
 template <class K>
-static bool launch_cluster(K kern, const SampArgs &a, size_t sm, int C, cudaStream_t st, unsigned long long &done) {
+static bool launch_cluster(K kern, const SampArgs &a, size_t sm, int C, cudaStream_t st, DeviceOnce &done) {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(done & (1ull << dev))) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    done |= 1ull << dev;
-  }
+  done.run(dev, [&] { return set_smem_attrs(kern); });
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -3990,7 +3982,7 @@ static bool launch_cluster(K kern, const SampArgs &a, size_t sm, int C, cudaStre
 
 template <int NV4>
 static void launch_a(const SampArgs &a, size_t sm, cudaStream_t st) {
-  static unsigned long long done = 0;  // attributes set, one bit per device
+  static DeviceOnce done;  // attributes set, per device
   if constexpr (NV4 == 0)
     launch_persistent(sample_a_kernel<0>, a, sm, 1, st, done);
   else
@@ -4005,7 +3997,7 @@ __global__ void redo_decode_kernel(int *out, int rows) {
 
 template <int NV4>
 static void launch_b(const SampArgs &a, size_t sm, cudaStream_t st) {
-  static unsigned long long done = 0;
+  static DeviceOnce done;
   if constexpr (NV4 == 0)
     launch_persistent(sample_b_kernel<0>, a, sm, 1, st, done);
   else
@@ -4049,14 +4041,15 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
     const StreamALayout Ly = stream_a_layout(s.V, s.hist_cols);
     const int W = std::min<int>({kStreamAWarps, (int)((227u * 1024u) / Ly.bytes), wrows});
     if (W >= 2) {
-      static unsigned long long done = 0;
+      static DeviceOnce done;
       int dev = 0;
       cudaGetDevice(&dev);
-      if (!(done & (1ull << dev))) {
-        cudaFuncSetAttribute(sample_a_stream<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        cudaFuncSetAttribute(sample_a_stream<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        done |= 1ull << dev;
-      }
+      done.run(dev, [] {
+        return cudaFuncSetAttribute(sample_a_stream<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    227 * 1024) == cudaSuccess &&
+               cudaFuncSetAttribute(sample_a_stream<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    227 * 1024) == cudaSuccess;
+      });
       const int grid = std::min(sm_count(), (s.rows + W - 1) / W);
       if (s.temperature <= 0.01)
         sample_a_stream<true><<<grid, W * 32, (size_t)W * Ly.bytes, stream>>>(a, W);
@@ -4082,13 +4075,13 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
     const StreamLayout Ly = stream_layout(s.V, s.hist_cols, kk);
     const int W = std::min<int>({kStreamWarps, (int)((227u * 1024u) / Ly.bytes), wrows});
     if (kk <= kStreamMaxK && W >= 2) {
-      static unsigned long long done = 0;
+      static DeviceOnce done;
       int dev = 0;
       cudaGetDevice(&dev);
-      if (!(done & (1ull << dev))) {
-        cudaFuncSetAttribute(sample_b_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        done |= 1ull << dev;
-      }
+      done.run(dev, [] {
+        return cudaFuncSetAttribute(sample_b_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) ==
+               cudaSuccess;
+      });
       const int grid = std::min(sm_count(), (s.rows + W - 1) / W);
       sample_b_stream<<<grid, W * 32, (size_t)W * Ly.bytes, stream>>>(a, W);
       const cudaError_t e = cudaGetLastError();
@@ -4114,11 +4107,11 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
     const size_t maps = 3 * (size_t)(kSliceLen / 32) * 4 + (size_t)kSliceLen * 4 + kStageAlign;
     bool launched;
     if (s.variant == 0) {
-      static unsigned long long done = 0;
+      static DeviceOnce done;
       launched = launch_cluster(sample_a_cluster<kRegLayers>, a, sizeof(SmemRA) + 2 * sizeof(XchgA) + maps, C,
                                 stream, done);
     } else {
-      static unsigned long long done = 0;
+      static DeviceOnce done;
       launched = launch_cluster(sample_b_cluster, a,
                                 sizeof(SmemB) + sizeof(RowPipe) + 2 * sizeof(XchgB) + maps +
                                     (size_t)((s.V + 31) / 32) * 4,
