@@ -557,36 +557,48 @@ def sampling_lines(peaks, steps=10, warmup=3, check_rows=64, cpu_rows=256):
     return out_lines
 
 
-def gemv_pass_line(peaks, passes=50, rows=1):
+def gemv_pass_line(peaks, passes=50, rows=1, pos=16, split=True):
     """The small-batch path the PHP host drives: one decode pass of `rows`
     rows (embedding, 2 layers of fp32 GEMV projections and attention, final
-    norm, logits) on the d=1024 benchmark model in FP32 mode, at positions
-    16..16+passes.  L2 is flushed (256 MB written) before each pass, so the
-    fp32 weights (168 MB) stream from HBM; each pass is timed with its own
-    CUDA events.  Bytes per pass are the library's algorithmic sums (weights
-    once, KV read, activations)."""
+    norm, logits) on the d=1024 benchmark model in FP32 mode, at position
+    `pos` (each pass rewinds to it).  L2 is flushed (256 MB written) before
+    each pass, so the fp32 weights (168 MB) stream from HBM; each pass is
+    timed with its own CUDA events.  Bytes per pass are the library's
+    algorithmic sums (weights once, KV read, activations).  split=False
+    turns the split-position attention off (SNAI_ATTENTION_SPLIT=0) to
+    compare."""
     import torch
     from snai_b200 import PREC_FP32, Cortex
     dev = torch.device("cuda")
-    eng = Cortex(make_model("c4"), num_heads=16, max_seqs=rows, precision=PREC_FP32)
+    old = os.environ.get("SNAI_ATTENTION_SPLIT")
+    os.environ["SNAI_ATTENTION_SPLIT"] = "1" if split else "0"
+    try:
+        eng = Cortex(make_model("c4"), num_heads=16, max_seqs=rows, precision=PREC_FP32)
+    finally:
+        if old is None:
+            del os.environ["SNAI_ATTENTION_SPLIT"]
+        else:
+            os.environ["SNAI_ATTENTION_SPLIT"] = old
     stream = torch.cuda.Stream(device=dev)
     eng.set_stream(stream.cuda_stream)
     rng = np.random.default_rng(7)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     with torch.cuda.stream(stream):
-        eng.forward_dev(torch.from_numpy(rng.integers(0, V, 16 * rows).astype(np.int32)).to(dev), rows, 16)
-        # algorithmic bytes of one pass from the profiler
+        eng.forward_dev(torch.from_numpy(rng.integers(0, V, pos * rows).astype(np.int32)).to(dev), rows, pos)
+        # algorithmic bytes and the attention time of one pass from the profiler
         eng.profile(True)
         for _ in range(3):
+            eng.rewind(pos)
+            flush.zero_()
             eng.forward_dev(torch.from_numpy(rng.integers(0, V, rows).astype(np.int32)).to(dev), rows, 1)
         eng.synchronize()
         prof = eng.profile_read()
         eng.profile(False)
         pass_bytes = sum(v[2] for v in prof.values()) / 3
-        eng.rewind(16)
         toks = [torch.from_numpy(rng.integers(0, V, rows).astype(np.int32)).to(dev) for _ in range(passes)]
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(passes)]
         for i, (a, b) in enumerate(ev):
+            eng.rewind(pos)
             flush.zero_()
             # hold the stream so the pass is queued whole and its kernels run back to back
             torch.cuda._sleep(400000)
@@ -599,9 +611,12 @@ def gemv_pass_line(peaks, passes=50, rows=1):
     del flush
     torch.cuda.empty_cache()
     gbs = pass_bytes / (us / 1e6) / 1e9
+    att_n, att_ms, att_bytes, _ = prof["attention"]
     return {"metric": "one-row decode pass GB/s (fp32 GEMV path, d=1024)", "value": gbs, "unit": "GB/s",
-            "rows": rows, "us_per_pass": us, "bytes_per_pass": pass_bytes, "passes": passes,
-            "timing": "median of per-pass CUDA events", "l2": "flushed (256 MB written) before each pass",
+            "rows": rows, "position": pos, "us_per_pass": us, "bytes_per_pass": pass_bytes, "passes": passes,
+            "attention_us_per_launch": 1e3 * att_ms / max(1, att_n),
+            "attention_split": split, "timing": "median of per-pass CUDA events",
+            "l2": "flushed (256 MB written) before each pass",
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s",
                          "frac": gbs / peaks["hbm"], "peak_source": f"{peaks['kind']} hbm_gbs"}}
 
@@ -688,18 +703,27 @@ def our_arm(args, rank, world, local_rank):
                                     "sample": f"{nseq} sequences x {n_cpu} decode steps from position {p0}, one "
                                               f"thread per sequence ({secs:.1f} s)"}
     if world == 1 and args.config == "c4" and not args.no_extras:
-        # the other workloads of the metric, one GPU
+        # the other workloads of the metric, one GPU; a failure is recorded
+        # in its key and does not lose the headline line
         for name in ("c3", "c2"):
-            r = decode_run(name, args, 0, 1, local_rank, dist_, peaks, extra=True)
-            line[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "e2e", "roofline", "positions",
-                                            "ids_sha256", "prefill", "clocks")}
-            line[name]["config"] = config_dict(CONFIGS[name])
-            line[name]["kernels"] = {k: {kk: vv for kk, vv in v.items() if kk in ("share", "GB/s", "TFLOP/s",
-                                                                                  "frac_hbm",
-                                                                                  "frac_bf16_sustained")}
-                                     for k, v in r["kernels"].items()}
-        line["gemv_pass"] = gemv_pass_line(peaks)
-        line["sampling"] = sampling_lines(peaks)
+            try:
+                r = decode_run(name, args, 0, 1, local_rank, dist_, peaks, extra=True)
+                line[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "e2e", "roofline",
+                                                "positions", "ids_sha256", "prefill", "clocks")}
+                line[name]["config"] = config_dict(CONFIGS[name])
+                line[name]["kernels"] = {k: {kk: vv for kk, vv in v.items()
+                                             if kk in ("share", "GB/s", "TFLOP/s", "frac_hbm", "frac_bf16_sustained")}
+                                         for k, v in r["kernels"].items()}
+            except Exception as ex:  # noqa: BLE001
+                line[name] = {"error": f"{type(ex).__name__}: {ex}"}
+        for key, fn in (("gemv_pass", gemv_pass_line),
+                        ("gemv_pass_pos1000", lambda p: gemv_pass_line(p, pos=1000)),
+                        ("gemv_pass_pos1000_unsplit", lambda p: gemv_pass_line(p, pos=1000, split=False)),
+                        ("sampling", sampling_lines)):
+            try:
+                line[key] = fn(peaks)
+            except Exception as ex:  # noqa: BLE001
+                line[key] = {"error": f"{type(ex).__name__}: {ex}"}
     if rank == 0:
         print(json.dumps(line), flush=True)
 

@@ -149,6 +149,7 @@ Engine *create_engine(const Dims &d, int max_seqs, int device, int precision) {
   int chunk = env_int("SNAI_CHUNK_ROWS", 0);
   if (chunk <= 0) chunk = std::max(max_seqs, std::min(8192, std::max(d.ctx, 256)));
   e->m_max = (int)align_up((size_t)std::max(chunk, max_seqs), 128);
+  e->att_split = env_int("SNAI_ATTENTION_SPLIT", 1) != 0;
 
   const size_t D = d.D, F = d.F, V = d.V;
   // ---- weights ----
@@ -187,6 +188,8 @@ Engine *create_engine(const Dims &d, int max_seqs, int device, int precision) {
   a.add(&e->att, M * D * sizeof(float));
   a.add(&e->u, M * F * sizeof(float));
   a.add(&e->xo, M * D * sizeof(float));
+  a.add(&e->att_part, (size_t)640 * (d.hs + 2));
+  a.add(&e->att_cnt, 256);
   a.add(&e->logits, (size_t)max_seqs * V);
   a.add(&e->hist, (size_t)max_seqs * d.ctx);
   a.add(&e->seq_len_d, (size_t)max_seqs);

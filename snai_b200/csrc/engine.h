@@ -22,15 +22,14 @@ enum Precision { kFP32 = 0, kTF32 = 1, kBF16 = 2 };
 // launches before the attribute it needs is in place.
 class DeviceOnce {
  public:
-  // Runs f() (returning true on success) the first time `dev` asks; later
-  // calls return true at once.  A failed f() is retried by the next call.
+  // Runs f() (returning true on success) the first time `dev` asks and
+  // returns its result; later calls return true at once.
   template <class F>
   bool run(int dev, F &&f) {
     std::lock_guard<std::mutex> g(mu_);
     if (done_.count(dev)) return true;
-    if (!f()) return false;
     done_.insert(dev);
-    return true;
+    return f();
   }
 
  private:
@@ -40,6 +39,27 @@ class DeviceOnce {
 
 // Multiprocessor count of a device (queried once per device, thread-safe).
 int device_sm_count(int dev);
+
+// Raises a kernel's dynamic shared-memory limit to `bytes`, less the
+// kernel's static shared memory (a CTA may use 227 KB in all).  A failure is
+// cleared from the runtime's error state, so that it cannot surface as the
+// error of a later launch, and returned as false.
+template <class K>
+bool set_dyn_smem(K kern, int bytes) {
+  const void *fn = reinterpret_cast<const void *>(kern);
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  const int limit = 227 * 1024 - (int)fa.sharedSizeBytes;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes < limit ? bytes : limit) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return true;
+}
 
 // Shape of a model.  Rules of core/cortex.nim:261-271: ffn = 4*dim whatever
 // the file header says; head size hs = dim/heads forced even and >= 2; RoPE
@@ -73,6 +93,7 @@ struct Engine {
   int precision = kFP32;
   int max_seqs = 1;
   int m_max = 0;  // rows per forward chunk
+  bool att_split = true;  // split-position attention for passes of few rows (SNAI_ATTENTION_SPLIT=0: off)
   cudaStream_t own_stream = nullptr;
   cudaStream_t stream = nullptr;
 
@@ -103,6 +124,8 @@ struct Engine {
   void *att = nullptr;        // [m_max, D]
   void *u = nullptr;          // [m_max, F]
   void *xo = nullptr;         // [m_max, D] normed rows that need logits
+  float *att_part = nullptr;  // split-position attention: partial results [640][hs + 2]
+  int *att_cnt = nullptr;     // split-position attention: arrival counters [256], zero between launches
   float *logits = nullptr;    // [max_seqs, V], per slot
   int *hist = nullptr;        // [max_seqs, ctx] every token fed to the slot
   int *seq_len_d = nullptr;   // [max_seqs] tokens fed (device copy of pos)

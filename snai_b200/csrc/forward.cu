@@ -291,6 +291,156 @@ __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
   if (head == gridDim.x - 1) att_zero_tail(orow, att_ch, D);
 }
 
+// Split-position decode attention for passes of few rows (rows x heads below
+// the SM count, e.g. the one-row decode pass of the PHP host).  CTA
+// (head, row, c) of S covers positions [c*chunk, min(n, (c+1)*chunk)), chunk =
+// ceil(n / S) rounded up to even (S is fixed per launch, the positions come
+// from the row descriptors, so a captured launch serves every later step).
+// It writes its local max m_c (starting at -9999, the reference's
+// initialisation, core/cortex.nim:517), l_c = sum exp(s_t - m_c) and
+// o_c = sum exp(s_t - m_c) v_t to part[row][head][c].  The last CTA of a
+// (row, head) to finish (an arrival counter, reset by it for the next launch)
+// merges the S results in split order: M = max m_c, w_c = exp(m_c - M),
+// att = sum w_c o_c / sum w_c l_c.  In decode passes (kvs non-null) every
+// CTA rotates q and the CTA holding position pos appends the new K/V row.
+constexpr int kSplitPartEntries = 640;  // (row, head, split) partial results
+constexpr int kSplitCounters = 256;     // (row, head) arrival counters
+
+template <typename TA>
+__global__ void __launch_bounds__(kAttThreads) attention_split_hs64_kernel(
+    const RowDesc *__restrict__ rows, const float *__restrict__ q, float *__restrict__ kv, TA *__restrict__ out,
+    int D, int att_ch, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride, float sqrt_hs,
+    const float *__restrict__ kvs, const float2 *__restrict__ rope, float *__restrict__ part, int *__restrict__ cnt) {
+  constexpr int HS = 64, PW = HS + 2, U = 8;
+  extern __shared__ float smem_att[];
+  float *red = smem_att;              // [32]
+  float *acc = smem_att + 32;         // [4 warps][64]
+  float *s = smem_att + 32 + 4 * HS;  // [chunk]
+  __shared__ int is_last;
+  grid_dep_wait();
+  grid_dep_launch();
+  const int head = blockIdx.x, m = blockIdx.y, c = blockIdx.z, S = gridDim.z, H = gridDim.x;
+  const RowDesc rd = rows[m];
+  const int n = rd.pos + 1;
+  const int chunk = ((n + S - 1) / S + 1) & ~1;
+  const int t0 = min(n, c * chunk), t1 = min(n, t0 + chunk), cn = t1 - t0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int half = lane >> 4, part_i = lane & 15;
+
+  float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
+  float *vbase = kbase + part_stride;
+  float4 qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + part_i * 4);
+  const int nc = kvs ? n - 1 : n;  // cache positions below nc; position pos from the staging entry
+  float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
+  if (kvs) {
+    const float *kst = kvs + (size_t)m * 2 * att_ch + head * HS;
+    const float4 cs = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + part_i * 2);
+    qv = rope4(qv, cs);
+    knew = rope4(*reinterpret_cast<const float4 *>(kst + part_i * 4), cs);
+    vnew = *reinterpret_cast<const float4 *>(kst + att_ch + part_i * 4);
+    if (warp == 0 && t0 <= n - 1 && n - 1 < t1)  // append: lanes 0..15 the K row, 16..31 the V row
+      *reinterpret_cast<float4 *>((half ? vbase : kbase) + (size_t)rd.pos * HS + part_i * 4) = half ? vnew : knew;
+  }
+
+  // ---- scores of positions t0..t1-1 ----
+  for (int p0 = warp * U; 2 * p0 < cn; p0 += 4 * U) {
+    float4 kr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = t0 + 2 * (p0 + u) + half;
+      kr[u] = t < min(nc, t1) ? __ldcs(reinterpret_cast<const float4 *>(kbase + (size_t)t * HS + part_i * 4))
+              : t < t1       ? knew
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float d = qv.x * kr[u].x + qv.y * kr[u].y + qv.z * kr[u].z + qv.w * kr[u].w;
+      d += __shfl_xor_sync(0xffffffffu, d, 8);
+      d += __shfl_xor_sync(0xffffffffu, d, 4);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      const int t = t0 + 2 * (p0 + u) + half;
+      if (part_i == 0 && t < t1) s[t - t0] = __fdiv_rn(d, sqrt_hs);
+    }
+  }
+  __syncthreads();
+  // ---- local max from -9999, exponentials, their sum ----
+  float mx = -9999.0f;
+  for (int i = threadIdx.x; i < cn; i += blockDim.x) mx = fmaxf(mx, s[i]);
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  float sum = 0.f;
+  for (int i = threadIdx.x; i < cn; i += blockDim.x) {
+    const float ev = expf(__fsub_rn(s[i], mx));
+    s[i] = ev;
+    sum += ev;
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) red[warp] = sum;
+  __syncthreads();
+  sum = red[0] + red[1] + red[2] + red[3];
+
+  // ---- sum of exp-weighted values ----
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int p0 = warp * U; 2 * p0 < cn; p0 += 4 * U) {
+    float4 vr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = t0 + 2 * (p0 + u) + half;
+      vr[u] = t < min(nc, t1) ? __ldcs(reinterpret_cast<const float4 *>(vbase + (size_t)t * HS + part_i * 4))
+              : t < t1       ? vnew
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = t0 + 2 * (p0 + u) + half;
+      const float wt = t < t1 ? s[t - t0] : 0.f;
+      a.x = __fadd_rn(a.x, __fmul_rn(vr[u].x, wt));
+      a.y = __fadd_rn(a.y, __fmul_rn(vr[u].y, wt));
+      a.z = __fadd_rn(a.z, __fmul_rn(vr[u].z, wt));
+      a.w = __fadd_rn(a.w, __fmul_rn(vr[u].w, wt));
+    }
+  }
+  a.x += __shfl_xor_sync(0xffffffffu, a.x, 16);
+  a.y += __shfl_xor_sync(0xffffffffu, a.y, 16);
+  a.z += __shfl_xor_sync(0xffffffffu, a.z, 16);
+  a.w += __shfl_xor_sync(0xffffffffu, a.w, 16);
+  if (half == 0) *reinterpret_cast<float4 *>(acc + warp * HS + part_i * 4) = a;
+  __syncthreads();
+  float *pp = part + (size_t)(m * H + head) * S * PW;
+  if (threadIdx.x < HS)
+    pp[c * PW + 2 + threadIdx.x] =
+        acc[threadIdx.x] + acc[HS + threadIdx.x] + acc[2 * HS + threadIdx.x] + acc[3 * HS + threadIdx.x];
+  if (threadIdx.x == 0) {
+    pp[c * PW] = mx;
+    pp[c * PW + 1] = sum;
+  }
+  // ---- the last CTA of (row, head) merges the S partial results ----
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(&cnt[m * H + head], 1) == S - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  TA *orow = out + (size_t)m * D;
+  if (threadIdx.x < HS) {
+    float M = -9999.0f;
+    for (int cc = 0; cc < S; ++cc) M = fmaxf(M, __ldcg(pp + cc * PW));
+    float L = 0.f, o = 0.f;
+    for (int cc = 0; cc < S; ++cc) {
+      const float w = expf(__fsub_rn(__ldcg(pp + cc * PW), M));
+      L = __fadd_rn(L, __fmul_rn(w, __ldcg(pp + cc * PW + 1)));
+      o = __fadd_rn(o, __fmul_rn(w, __ldcg(pp + cc * PW + 2 + threadIdx.x)));
+    }
+    ActIO<TA>::store(orow + head * HS + threadIdx.x, __fdiv_rn(o, L));
+  }
+  if (threadIdx.x == 0) cnt[m * H + head] = 0;
+  if (head == H - 1) att_zero_tail(orow, att_ch, D);
+}
+
 // Any even head size: threads take positions for the scores and channels for
 // the weighted sum.
 template <typename TA>
@@ -606,9 +756,7 @@ static int launch_tcp(Engine &e, int M, int N, int K, const void *A, const void 
   using Sm = TcpSmem<BN, STAGES>;
   auto kern = snai_tileproj_tc_kernel<TIn, BN, STAGES, Epi>;
   static DeviceOnce attr;  // per instantiation
-  if (!attr.run(e.device, [&] {
-        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Sm::kBytes) == cudaSuccess;
-      })) {
+  if (!attr.run(e.device, [&] { return set_dyn_smem(kern, (int)Sm::kBytes); })) {
     set_error("cudaFuncSetAttribute failed for the tensor-core projection");
     return -5;
   }
@@ -632,9 +780,7 @@ static int launch_tc2(Engine &e, int M, int N, int K, const void *A, const void 
   using Sm = Tc2Smem<STAGES>;
   auto kern = snai_pairproj_tc_kernel<TIn, STAGES, Epi>;
   static DeviceOnce attr;  // per instantiation
-  if (!attr.run(e.device, [&] {
-        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Sm::kBytes) == cudaSuccess;
-      })) {
+  if (!attr.run(e.device, [&] { return set_dyn_smem(kern, (int)Sm::kBytes); })) {
     set_error("cudaFuncSetAttribute failed for the CTA-pair projection");
     return -5;
   }
@@ -732,12 +878,24 @@ static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_pos
   const int max_n = d.ctx;
   static DeviceOnce attr;  // per instantiation
   attr.run(e.device, [] {
-    return cudaFuncSetAttribute(attention_hs64_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                200 * 1024) == cudaSuccess &&
-           cudaFuncSetAttribute(attention_generic_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                200 * 1024) == cudaSuccess;
+    const bool a = set_dyn_smem(attention_hs64_kernel<TA>, 200 * 1024);
+    const bool b = set_dyn_smem(attention_split_hs64_kernel<TA>, 200 * 1024);
+    return set_dyn_smem(attention_generic_kernel<TA>, 200 * 1024) && a && b;
   });
-  if (d.hs == 64) {
+  // few rows: split the positions of each (row, head) over S CTAs so that
+  // about two CTAs run per SM
+  const int rh = M * d.heads, nsm = sm_count(e.device);
+  int S = 1;
+  if (d.hs == 64 && e.att_split && e.att_part && rh < nsm && rh <= kSplitCounters) {
+    S = std::min((2 * nsm + rh - 1) / rh, (d.ctx + 63) / 64);
+    S = std::min(S, kSplitPartEntries / rh);
+  }
+  if (S >= 2) {
+    const size_t sm = (32 + 4 * 64 + (size_t)((d.ctx + S - 1) / S + 2)) * sizeof(float);
+    launch_k(e, !tc_path(e, M), attention_split_hs64_kernel<TA>, dim3(d.heads, M, S), dim3(kAttThreads), sm,
+             e.rows_d, e.q, e.kv, out, d.D, d.att_ch, e.kv_slot_stride, layer_off, e.kv_part_stride,
+             e.kv_head_stride, e.sqrt_hs, defer ? e.kvs : nullptr, e.rope, e.att_part, e.att_cnt);
+  } else if (d.hs == 64) {
     const size_t sm = (32 + 4 * 64 + (size_t)max_n) * sizeof(float);
     launch_k(e, !tc_path(e, M), attention_hs64_kernel<TA>, grid, dim3(kAttThreads), sm, e.rows_d, e.q, e.kv, out,
              d.D, d.att_ch, e.kv_slot_stride, layer_off, e.kv_part_stride, e.kv_head_stride, e.sqrt_hs,

@@ -3937,8 +3937,12 @@ static int sm_count() {
 // The full 227 KB of dynamic shared memory and the largest carve-out.
 template <class K>
 static bool set_smem_attrs(K kern) {
-  return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) == cudaSuccess &&
-         cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) == cudaSuccess;
+  const bool ok = set_dyn_smem(kern, 227 * 1024);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return ok;
 }
 
 template <class K>
@@ -4045,10 +4049,8 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
       int dev = 0;
       cudaGetDevice(&dev);
       done.run(dev, [] {
-        return cudaFuncSetAttribute(sample_a_stream<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    227 * 1024) == cudaSuccess &&
-               cudaFuncSetAttribute(sample_a_stream<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    227 * 1024) == cudaSuccess;
+        const bool a = set_dyn_smem(sample_a_stream<false>, 227 * 1024);
+        return set_dyn_smem(sample_a_stream<true>, 227 * 1024) && a;
       });
       const int grid = std::min(sm_count(), (s.rows + W - 1) / W);
       if (s.temperature <= 0.01)
@@ -4078,10 +4080,7 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
       static DeviceOnce done;
       int dev = 0;
       cudaGetDevice(&dev);
-      done.run(dev, [] {
-        return cudaFuncSetAttribute(sample_b_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) ==
-               cudaSuccess;
-      });
+      done.run(dev, [] { return set_dyn_smem(sample_b_stream, 227 * 1024); });
       const int grid = std::min(sm_count(), (s.rows + W - 1) / W);
       sample_b_stream<<<grid, W * 32, (size_t)W * Ly.bytes, stream>>>(a, W);
       const cudaError_t e = cudaGetLastError();

@@ -333,3 +333,36 @@ def test_device_pointer_path(small_model, built):
     assert np.array_equal(ids.cpu().numpy(), ids_host)
     e1.close()
     e2.close()
+
+
+@pytest.mark.parametrize("prec", [PREC_FP32, PREC_BF16])
+def test_split_attention_ragged_positions(prec, model_dir, built):
+    """Passes of few rows split each (row, head)'s positions over several
+    CTAs and merge their partial softmax terms.  Three slots at very
+    different positions (899, 499, 36: some splits of the short rows are
+    empty) and one slot at position 0, then one more token each, against
+    the oracle at every step (a one-row pass, a two-row and a four-row
+    pass)."""
+    path = make_model(model_dir, "split.snai", 2000, 128, 1024, 2, seed=51)
+    lens = [899, 499, 36, 0]
+    rng = np.random.default_rng(60 + prec)
+    toks = [rng.integers(0, 2000, n + 3).astype(np.int32) for n in lens]
+    e = Cortex(path, num_heads=2, max_seqs=4, precision=prec)
+    refs = []
+    for s, n in enumerate(lens):
+        o = O.Oracle(path, num_heads=2)
+        r = [o.forward(toks[s][:n]) if n else None]
+        for i in range(3):
+            r.append(o.forward(toks[s][n + i:n + i + 1]))
+        refs.append(r)
+        o.close()
+        if n:
+            e.forward([toks[s][:n]], slots=[s], want_logits=False)
+    tol = TOL[prec]  # the prompts ran through the tensor cores in BF16 mode
+    for group in ([0], [1, 2], [0, 1, 2, 3]):
+        t = np.asarray([[toks[s][e.pos(s)]] for s in group], dtype=np.int32)
+        got = e.forward(t, slots=np.asarray(group, dtype=np.int32))
+        for j, s in enumerate(group):
+            k = e.pos(s) - lens[s]  # tokens fed after the prompt
+            assert rel_err(got[j], refs[s][k]) < tol, (group, s, k)
+    e.close()
