@@ -89,7 +89,7 @@ def metric_name(c):
 
 def config_dict(c):
     return {"workload": c["workload"], "model": c["model"], "global_batch": c["SEQS"], "seq_len": CTX,
-            "prompt": c["PROMPT"], "gemm": "tcgen05 bf16 x bf16 -> fp32 (fp32 GEMV below 64 rows)",
+            "prompt": c["PROMPT"], "gemm": "tcgen05 bf16 x bf16 -> fp32",
             "kv_cache": "fp32",
             "l2": "inputs larger than L2 (KV cache %.1f GB in all)" % (c["SEQS"] * c["L"] * 2 * CTX * c["D"] * 4 / 1e9),
             "parallelism": PARALLELISM}
@@ -627,13 +627,14 @@ def gemm_bench(args):
     K=4096, logits N=16384) through decode passes of one token per slot, on
     the benchmark model's weights at positions 16..  One JSON line per GEMM
     kind: TFLOP/s from the library's CUDA-event profiler against the measured
-    bf16 peak; below 64 rows the projections run as fp32 GEMVs and the line
-    gives GB/s against the measured copy peak."""
+    bf16 peak (BF16 mode); below 64 rows the engine runs in FP32 mode, whose
+    projections are fp32 GEMVs, and the line gives GB/s against the measured
+    copy peak."""
     import torch
-    from snai_b200 import PREC_BF16, Cortex
+    from snai_b200 import PREC_BF16, PREC_FP32, Cortex
     peaks = load_peaks()
     B = args.seqs
-    eng = Cortex(make_model("c4"), num_heads=16, max_seqs=B, precision=PREC_BF16)
+    eng = Cortex(make_model("c4"), num_heads=16, max_seqs=B, precision=PREC_FP32 if B < 64 else PREC_BF16)
     dev = torch.device("cuda")
     rng = np.random.default_rng(7)
     stream = torch.cuda.Stream(device=dev)

@@ -98,8 +98,9 @@ CORTEX_API float cortex_train_step(void *state, int *raw_inputs, int *raw_target
 /* ======================================================================== */
 
 /* GEMM operand precision.  FP32 runs every projection as fp32 FFMA GEMV
- * (closest to the reference).  TF32 / BF16 run projections with at least 64
- * rows on tcgen05 tensor cores (fp32 accumulate); fewer rows use fp32 GEMV. */
+ * (closest to the reference).  TF32 / BF16 run every projection on tcgen05
+ * tensor cores (fp32 accumulate), whatever the number of rows in a pass, so
+ * a sequence's results do not depend on the other sequences of its pass. */
 #define SNAI_PREC_FP32 0
 #define SNAI_PREC_TF32 1
 #define SNAI_PREC_BF16 2

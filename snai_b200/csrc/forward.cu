@@ -12,8 +12,8 @@
 //                  W_down proj.   -> h += .
 //                  rmsnorm        -> x = RMSNorm(h, rms_att[l+1])
 //   rows that need logits: x = RMSNorm(h, rms_final) -> W_out projection.
-// Projections with fewer than 64 rows (or in FP32 mode) run as fp32 GEMV;
-// larger ones as tcgen05 GEMMs (gemm_tc.cuh) in TF32 or BF16.
+// Projections run as fp32 GEMV in FP32 mode and as tcgen05 GEMMs
+// (gemm_tc.cuh) in TF32 or BF16 mode, for any number of rows.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -727,8 +727,13 @@ static void qkv_tma_maps(Engine &e, int M, EpiQKV *q) {
   q->tma = 1;
 }
 
+// TF32 / BF16 modes run every projection on the tensor cores, whatever the
+// row count: a row's result must not depend on how many rows share its pass
+// (a decode pass of 3 rows, the logits rows of a prompt chunk, a shard of
+// the sequences), and the tensor-core kernels give a row the same bits for
+// any M (same K order, one accumulator per output).
 static bool tc_path(const Engine &e, int M) {
-  return e.precision != kFP32 && M >= 64 && e.d.D % 16 == 0 && e.d.D >= 64;
+  return e.precision != kFP32 && M >= 1 && e.d.D % 16 == 0 && e.d.D >= 64;
 }
 
 static int sm_count(int dev) { return device_sm_count(dev); }

@@ -8,10 +8,9 @@ same model, two calls in a row (a prompt, then one more token), and
 compares the logits (np.array_equal) and the per-slot positions.
 
 The d=1024 case needs several chunks of the 8 MiB array (128 rows each):
-4 sequences x 100 prompt tokens are chunks of 128, 128, 128 and 16 rows, so
-in BF16 mode the last chunk falls below the 64-row tensor-core threshold
-onto the fp32 projection path.  The reference state is made with the same
-chunk size (SNAI_CHUNK_ROWS) so both entry points split the rows alike.
+4 sequences x 100 prompt tokens are chunks of 128, 128, 128 and 16 rows
+(a partial last chunk).  The reference state is made with the same chunk
+size (SNAI_CHUNK_ROWS) so both entry points split the rows alike.
 
 The file is named to run last, so a failure here cannot hide other tests."""
 import ctypes
