@@ -621,6 +621,32 @@ def gemv_pass_line(peaks, passes=50, rows=1, pos=16, split=True):
                          "frac": gbs / peaks["hbm"], "peak_source": f"{peaks['kind']} hbm_gbs"}}
 
 
+def group_load_line(name, n, single_s):
+    """Loads the configuration's model onto devices 0..n-1 from one process
+    (cortex_group_load, one sequence slot per GPU) and reports the wall time
+    beside a single-GPU load (cortex_load_stream_ex) of the same file."""
+    import torch
+    from snai_b200 import PREC_BF16, Cortex, CortexGroup
+    c = CONFIGS[name]
+    if torch.cuda.device_count() < n:
+        return {"error": f"rank 0 sees {torch.cuda.device_count()} GPUs, fewer than {n}"}
+    path = make_model(name)
+    try:
+        t0 = time.perf_counter()
+        e = Cortex(path, num_heads=c["HEADS"], max_seqs=1, device=0, precision=PREC_BF16)
+        one_s = time.perf_counter() - t0
+        e.close()
+        g = CortexGroup(path, c["HEADS"], n, list(range(n)), precision=PREC_BF16)
+        out = {"devices": n, "seconds": g.load_seconds, "single_gpu_seconds": one_s,
+               "rank_single_gpu_seconds": single_s, "model_bytes": os.path.getsize(path),
+               "how": "one file read into GPU 0 (pinned double-buffered), peer copies to the others, bf16 packing "
+                      "on every GPU"}
+        g.close()
+        return out
+    except Exception as ex:  # noqa: BLE001
+        return {"error": f"{type(ex).__name__}: {ex}"}
+
+
 def gemm_bench(args):
     """Projection micro-benchmark: the d=1024 decode step's GEMM shapes
     (`--seqs` rows; qkv N=3072, wo N=1024, up N=4096, down N=1024 with
@@ -703,6 +729,14 @@ def our_arm(args, rank, world, local_rank):
             line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": nthreads, "kind": "port",
                                     "sample": f"{nseq} sequences x {n_cpu} decode steps from position {p0}, one "
                                               f"thread per sequence ({secs:.1f} s)"}
+    if world > 1 and not args.no_extras:
+        # one process loading the model onto every GPU of the run: one file
+        # read, fp32 weights fanned out from the first GPU by peer copies
+        # (cortex_group_load), beside this rank's own single-GPU load
+        dist_.barrier()
+        if rank == 0:
+            line["group_load"] = group_load_line(args.config, world, res["load_s"])
+        dist_.barrier()
     if world == 1 and args.config == "c4" and not args.no_extras:
         # the other workloads of the metric, one GPU; a failure is recorded
         # in its key and does not lose the headline line
@@ -741,7 +775,9 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the c3/c2/sampling/GEMV extra keys")
     ap.add_argument("--sampler", action="store_true", help="only the isolated sampling workload, one line each")
     ap.add_argument("--gemm", action="store_true", help="only the projection micro-benchmark")
-    ap.add_argument("--seqs", type=int, default=4096, help="rows of the projection micro-benchmark")
+    ap.add_argument("--seqs", type=int, default=None,
+                    help="total sequences of the decode configuration (default: the configuration's), or rows of "
+                         "the projection micro-benchmark (default 4096)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -754,9 +790,13 @@ def main():
         reference_arm(args, rank, world)
         return
     if args.gemm:
+        if args.seqs is None:
+            args.seqs = 4096
         if rank == 0:
             gemm_bench(args)
         return
+    if args.seqs is not None:
+        CONFIGS[args.config] = dict(CONFIGS[args.config], SEQS=args.seqs)
     if args.sampler:
         if rank == 0:
             for ln in sampling_lines(load_peaks(), steps=args.steps, warmup=args.warmup):

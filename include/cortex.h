@@ -234,6 +234,40 @@ CORTEX_API int cortex_profile_read(void *state, int kind, long long *launches, d
 CORTEX_API int cortex_forward_batch_noalloc(void *state, const int *tokens, int batch, int n_tok, const int *slots,
                                             float *logits, int flags);
 
+/* ------------------------------------------------------------------------ */
+/* Engine groups: one process, several GPUs.  No counterpart in the          */
+/* reference (one sequence per CortexState, core/cortex.nim:24-59); this is  */
+/* how a single host process (the PHP host has no launcher) uses several     */
+/* GPUs.  Sequences are independent, so a group splits total_seqs into      */
+/* contiguous shards, shard i = [total*i/n, total*(i+1)/n) on devices[i]     */
+/* (a device may be listed more than once), with no tensor exchanged         */
+/* between the engines.                                                      */
+/* ------------------------------------------------------------------------ */
+
+/* Reads the SNAI_V4 file once (pinned double-buffered reads into the first
+ * engine), copies the fp32 weights from the first GPU to the others by peer
+ * copies, and packs the bf16 copies on every GPU.  NULL on failure (the
+ * reasons of cortex_load_stream, or a device that cannot be used). */
+CORTEX_API void *cortex_group_load(const char *filepath, int num_heads, int total_seqs, const int *devices,
+                                   int n_devices, int precision);
+CORTEX_API void cortex_group_free(void *group);
+/* Number of engines; the i-th engine's state (usable with every cortex_*
+ * call of part 2, e.g. cortex_seq_rewind); its shard. */
+CORTEX_API int cortex_group_size(void *group);
+CORTEX_API void *cortex_group_engine(void *group, int i);
+CORTEX_API int cortex_group_shard(void *group, int i, int *first, int *count);
+/* Wall seconds cortex_group_load took (file read, copies, packing). */
+CORTEX_API double cortex_group_load_seconds(void *group);
+/* cortex_forward_batch for every sequence of the group at once (host
+ * memory): tokens [total][n_tok], logits [total][vocab] or NULL.  One host
+ * thread per engine; returns when every engine is done. */
+CORTEX_API int cortex_group_forward(void *group, const int *tokens, int n_tok, float *logits);
+/* cortex_decode_steps for every sequence of the group (host memory):
+ * uniforms [steps][total], out_ids [steps][total], gathered from the
+ * engines by their threads. */
+CORTEX_API int cortex_group_decode_steps(void *group, int steps, const float *uniforms,
+                                         const snai_sample_params *params, int *out_ids);
+
 /* Self-test of the failure path every kernel wait takes.  No counterpart in
  * the reference (whose engine has no device waits).  Queues one kernel on
  * the state's stream that waits on an mbarrier nothing completes; the wait

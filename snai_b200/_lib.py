@@ -73,6 +73,14 @@ SIGNATURES = {
     "cortex_profile_read": (c_int, [c_void_p, c_int, ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(c_double),
                                     ctypes.POINTER(c_double), ctypes.POINTER(c_double)]),
     "cortex_forward_batch_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int]),
+    "cortex_group_load": (c_void_p, [c_char_p, c_int, c_int, c_void_p, c_int, c_int]),
+    "cortex_group_free": (None, [c_void_p]),
+    "cortex_group_size": (c_int, [c_void_p]),
+    "cortex_group_engine": (c_void_p, [c_void_p, c_int]),
+    "cortex_group_shard": (c_int, [c_void_p, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "cortex_group_load_seconds": (c_double, [c_void_p]),
+    "cortex_group_forward": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+    "cortex_group_decode_steps": (c_int, [c_void_p, c_int, c_void_p, ctypes.POINTER(SampleParams), c_void_p]),
     "cortex_selftest_wait_timeout": (c_int, [c_void_p, ctypes.c_longlong]),
     "cortex_kernel_launches": (ctypes.c_longlong, [c_void_p]),
 }

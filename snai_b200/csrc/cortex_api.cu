@@ -11,8 +11,13 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <chrono>
+#include <condition_variable>
+#include <functional>
 #include <limits>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/cortex.h"
@@ -218,6 +223,7 @@ Engine *create_engine(const Dims &d, int max_seqs, int device, int precision) {
     return nullptr;
   }
   w.place(e->wblock);
+  e->wblock_bytes = w.off;
   if (hw.off) hw.place(e->hblock);
   a.place(e->ablock);
   if (cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
@@ -257,17 +263,27 @@ Engine *create_engine(const Dims &d, int max_seqs, int device, int precision) {
 }
 
 // fp32 -> bf16 copies of every projection weight (BF16 mode).
+// Every projection weight in one launch per 64 tensors.
 int refresh_bf16(Engine &e) {
   if (e.precision != kBF16) return 0;
   const size_t D = e.d.D, F = e.d.F, V = e.d.V;
-  int rc = convert_bf16(e, e.w_out, e.w_out_h, V * D);
+  Bf16Segments segs;
+  int rc = 0;
+  auto add = [&](const float *s, __nv_bfloat16 *d, size_t n) {
+    if (segs.count == 64) {
+      rc |= convert_bf16_segments(e, segs);
+      segs.count = 0;
+    }
+    segs.seg[segs.count++] = Bf16Segments::Seg{s, d, n};
+  };
+  add(e.w_out, e.w_out_h, V * D);
   for (auto &l : e.layers) {
-    rc |= convert_bf16(e, l.wqkv, l.wqkv_h, 3 * D * D);
-    rc |= convert_bf16(e, l.wo, l.wo_h, D * D);
-    rc |= convert_bf16(e, l.wup, l.wup_h, F * D);
-    rc |= convert_bf16(e, l.wdown, l.wdown_h, D * F);
+    add(l.wqkv, l.wqkv_h, 3 * D * D);
+    add(l.wo, l.wo_h, D * D);
+    add(l.wup, l.wup_h, F * D);
+    add(l.wdown, l.wdown_h, D * F);
   }
-  return rc;
+  return rc | convert_bf16_segments(e, segs);
 }
 
 // Device pointer and element count of a tensor (core/cortex.nim:439-462).
@@ -417,8 +433,10 @@ int forward_batch(Engine &e, const int *tokens, int batch, int n_tok, const int 
   return finish(e, !dev);
 }
 
-Engine *load_stream(const char *path, int num_heads, int max_seqs, int device, int precision) {
-  clear_error();
+// SNAI_V4 header (src/tensor_io.php:22-59, core/cortex.nim:969-996) and the
+// engine shape it gives; the file is left at the first tensor.  NULL (with
+// the error set) on a bad open, magic or header.
+FILE *open_snai(const char *path, int num_heads, Dims *d, uint32_t *ffn_out) {
   if (!path) {
     set_error("filepath is NULL");
     return nullptr;
@@ -459,41 +477,58 @@ Engine *load_stream(const char *path, int num_heads, int max_seqs, int device, i
     set_error("%s: ffn_dim %u > 4 * hidden_dim %u", path, ffn, dim);
     return nullptr;
   }
-  Dims d;
-  if (!make_dims((int)vocab, (int)dim, (int)ctx, (int)layers, num_heads, &d)) {
+  if (!make_dims((int)vocab, (int)dim, (int)ctx, (int)layers, num_heads, d)) {
     fclose(f);
     return nullptr;
   }
-  Engine *e = create_engine(d, max_seqs, device, precision);
-  if (!e) {
-    fclose(f);
-    return nullptr;
-  }
-  DeviceGuard g(e->device);
-  const size_t kChunk = 16u << 20;  // floats per staging round
-  std::vector<float> stage;
-  stage.resize(std::min<size_t>(kChunk, (size_t)vocab * dim + 16));
-  bool ok = true;
+  *ffn_out = ffn;
+  return f;
+}
+
+// Reads every tensor of an open SNAI_V4 file straight into the engine's
+// fp32 weights, in file order (core/cortex.nim:998-1041: read n floats or
+// fail).  Two pinned staging buffers alternate: the file is read into one
+// while the other's host-to-device copy runs on the engine's stream.
+bool read_weights(Engine *e, FILE *f, uint32_t ffn) {
+  constexpr size_t kStage = 8u << 20;  // floats per staging buffer (32 MB)
+  float *stage[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  bool ok = cudaHostAlloc(reinterpret_cast<void **>(&stage[0]), kStage * 4, cudaHostAllocDefault) == cudaSuccess &&
+            cudaHostAlloc(reinterpret_cast<void **>(&stage[1]), kStage * 4, cudaHostAllocDefault) == cudaSuccess &&
+            cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming) == cudaSuccess &&
+            cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) set_error("pinned staging buffers for the loader: %s", cudaGetErrorString(cudaGetLastError()));
+  int b = 0;
+  bool used[2] = {false, false};
   auto blast = [&](float *dst, size_t n) {
-    // core/cortex.nim:998-1000: read n floats or fail
-    for (size_t done = 0; ok && done < n;) {
-      const size_t c = std::min(stage.size(), n - done);
-      if (fread(stage.data(), sizeof(float), c, f) != c) {
+    for (size_t at = 0; ok && at < n;) {
+      const size_t c = std::min(kStage, n - at);
+      if (used[b] && cudaEventSynchronize(done[b]) != cudaSuccess) {  // its last copy has left the buffer
         ok = false;
+        set_error("loader copy failed: %s", cudaGetErrorString(cudaGetLastError()));
         break;
       }
-      if (cudaMemcpy(dst + done, stage.data(), c * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+      if (fread(stage[b], sizeof(float), c, f) != c) {
         ok = false;
+        set_error("file ends before all tensors were read");
         break;
       }
-      done += c;
+      if (cudaMemcpyAsync(dst + at, stage[b], c * sizeof(float), cudaMemcpyHostToDevice, e->stream) != cudaSuccess ||
+          cudaEventRecord(done[b], e->stream) != cudaSuccess) {
+        ok = false;
+        set_error("loader copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+        break;
+      }
+      used[b] = true;
+      b ^= 1;
+      at += c;
     }
   };
-  const size_t D = dim, FF = (size_t)ffn * dim;
-  blast(e->emb, (size_t)vocab * D);
-  blast(e->w_out, (size_t)vocab * D);
+  const size_t D = e->d.D, V = e->d.V, FF = (size_t)ffn * D;
+  blast(e->emb, V * D);
+  blast(e->w_out, V * D);
   blast(e->rms_final, D);
-  for (uint32_t l = 0; ok && l < layers; ++l) {
+  for (int l = 0; ok && l < e->d.L; ++l) {
     LayerWeights &w = e->layers[l];
     blast(w.rms_att, D);
     blast(w.rms_ffn, D);
@@ -504,9 +539,33 @@ Engine *load_stream(const char *path, int num_heads, int max_seqs, int device, i
     blast(w.wup, FF);
     blast(w.wdown, FF);
   }
+  if (cudaStreamSynchronize(e->stream) != cudaSuccess && ok) {
+    ok = false;
+    set_error("loader copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+  }
+  for (int i = 0; i < 2; ++i) {
+    if (stage[i]) cudaFreeHost(stage[i]);
+    if (done[i]) cudaEventDestroy(done[i]);
+  }
+  return ok;
+}
+
+Engine *load_stream(const char *path, int num_heads, int max_seqs, int device, int precision) {
+  clear_error();
+  Dims d;
+  uint32_t ffn = 0;
+  FILE *f = open_snai(path, num_heads, &d, &ffn);
+  if (!f) return nullptr;
+  Engine *e = create_engine(d, max_seqs, device, precision);
+  if (!e) {
+    fclose(f);
+    return nullptr;
+  }
+  DeviceGuard g(e->device);
+  const bool ok = read_weights(e, f, ffn);
   fclose(f);
   if (!ok) {
-    set_error("%s: file ends before all tensors were read", path);
+    set_error("%s: %s", path, g_err.c_str());
     free_engine(e);
     return nullptr;
   }
@@ -1085,6 +1144,232 @@ extern "C" int cortex_selftest_wait_timeout(void *state, long long limit_ns) {
 
 extern "C" long long cortex_kernel_launches(void *state) {
   return state ? static_cast<Engine *>(state)->launches : 0;
+}
+
+// ============================================================================
+// Engine groups: one process driving several GPUs
+// ============================================================================
+//
+// Sequences are independent (core/cortex.nim:487-563 shares nothing between
+// them), so a group splits `total` sequences into contiguous shards, one
+// engine per listed device, and never exchanges tensors between them.  The
+// model file is read once: into the first engine, then its fp32 weight
+// block is copied to every other engine by peer copies over NVLink (the
+// engines' weight layouts are identical), and each GPU packs its own bf16
+// copies.  Calls run one worker thread per engine; ids and logits are
+// gathered into the caller's host arrays.
+namespace snai {
+namespace {
+
+struct Group {
+  std::vector<Engine *> engines;
+  std::vector<int> first, count;  // shard of each engine
+  int total = 0;
+  double load_s = 0.0;
+  // worker pool: one thread per engine
+  std::vector<std::thread> workers;
+  std::mutex mu;
+  std::condition_variable cv_go, cv_done;
+  std::function<int(int)> task;
+  long long generation = 0;
+  int pending = 0;
+  bool quit = false;
+  std::vector<int> rc;
+  std::vector<std::string> err;
+
+  void start() {
+    rc.assign(engines.size(), 0);
+    err.assign(engines.size(), std::string());
+    for (size_t i = 0; i < engines.size(); ++i)
+      workers.emplace_back([this, i] {
+        long long seen = 0;
+        for (;;) {
+          std::function<int(int)> t;
+          {
+            std::unique_lock<std::mutex> lk(mu);
+            cv_go.wait(lk, [&] { return quit || generation != seen; });
+            if (quit) return;
+            seen = generation;
+            t = task;
+          }
+          clear_error();
+          const int r = t((int)i);
+          std::string msg = r ? g_err : std::string();
+          std::lock_guard<std::mutex> lk(mu);
+          rc[i] = r;
+          err[i] = msg;
+          if (--pending == 0) cv_done.notify_all();
+        }
+      });
+  }
+  // Runs f(i) for every engine on its worker; returns the first failure.
+  int run(std::function<int(int)> f) {
+    std::unique_lock<std::mutex> lk(mu);
+    task = std::move(f);
+    pending = (int)engines.size();
+    ++generation;
+    cv_go.notify_all();
+    cv_done.wait(lk, [&] { return pending == 0; });
+    for (size_t i = 0; i < engines.size(); ++i)
+      if (rc[i]) {
+        set_error("engine %zu (device %d): %s", i, engines[i]->device, err[i].c_str());
+        return rc[i];
+      }
+    return 0;
+  }
+  ~Group() {
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      quit = true;
+    }
+    cv_go.notify_all();
+    for (auto &t : workers) t.join();
+    for (Engine *e : engines) free_engine(e);
+  }
+};
+
+Group *load_group(const char *path, int num_heads, int total, const int *devices, int n, int precision) {
+  clear_error();
+  if (!devices || n < 1 || total < n) {
+    set_error("a group needs at least one device and one sequence per device (devices=%d, sequences=%d)", n, total);
+    return nullptr;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  Dims d;
+  uint32_t ffn = 0;
+  FILE *f = open_snai(path, num_heads, &d, &ffn);
+  if (!f) return nullptr;
+  Group *g = new Group();
+  g->total = total;
+  for (int i = 0; i < n; ++i) {
+    const int a = (int)((long long)total * i / n), b = (int)((long long)total * (i + 1) / n);
+    Engine *e = create_engine(d, b - a, devices[i], precision);
+    if (!e) {
+      fclose(f);
+      delete g;
+      return nullptr;
+    }
+    g->engines.push_back(e);
+    g->first.push_back(a);
+    g->count.push_back(b - a);
+  }
+  Engine *e0 = g->engines[0];
+  bool ok;
+  {
+    DeviceGuard dg(e0->device);
+    ok = read_weights(e0, f, ffn);
+  }
+  fclose(f);
+  if (!ok) {
+    set_error("%s: %s", path, g_err.c_str());
+    delete g;
+    return nullptr;
+  }
+  // fan the fp32 weights out from the first engine by peer copies
+  for (int i = 1; ok && i < n; ++i) {
+    Engine *e = g->engines[i];
+    DeviceGuard dg(e->device);
+    if (e->device != e0->device) {
+      int can = 0;
+      if (cudaDeviceCanAccessPeer(&can, e->device, e0->device) == cudaSuccess && can) {
+        const cudaError_t pe = cudaDeviceEnablePeerAccess(e0->device, 0);
+        if (pe != cudaSuccess && pe != cudaErrorPeerAccessAlreadyEnabled) ok = false;
+        cudaGetLastError();
+      }
+    }
+    if (ok && cudaMemcpyPeerAsync(e->wblock, e->device, e0->wblock, e0->device, e0->wblock_bytes, e->stream) !=
+                  cudaSuccess)
+      ok = false;
+    if (!ok) set_error("weight copy to device %d failed: %s", e->device, cudaGetErrorString(cudaGetLastError()));
+  }
+  for (int i = 0; ok && i < n; ++i) {
+    Engine *e = g->engines[i];
+    DeviceGuard dg(e->device);
+    if (refresh_bf16(*e) || cudaStreamSynchronize(e->stream) != cudaSuccess) {
+      ok = false;
+      set_error("weight conversion on device %d failed: %s", e->device, cudaGetErrorString(cudaGetLastError()));
+    }
+  }
+  if (!ok) {
+    delete g;
+    return nullptr;
+  }
+  g->start();
+  g->load_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  return g;
+}
+
+}  // namespace
+}  // namespace snai
+
+extern "C" void *cortex_group_load(const char *filepath, int num_heads, int total_seqs, const int *devices,
+                                   int n_devices, int precision) {
+  return load_group(filepath, num_heads, total_seqs, devices, n_devices, precision);
+}
+
+extern "C" void cortex_group_free(void *group) { delete static_cast<Group *>(group); }
+
+extern "C" int cortex_group_size(void *group) {
+  return group ? (int)static_cast<Group *>(group)->engines.size() : 0;
+}
+
+extern "C" void *cortex_group_engine(void *group, int i) {
+  Group *g = static_cast<Group *>(group);
+  if (!g || i < 0 || i >= (int)g->engines.size()) return nullptr;
+  return g->engines[i];
+}
+
+extern "C" int cortex_group_shard(void *group, int i, int *first, int *count) {
+  Group *g = static_cast<Group *>(group);
+  if (!g || i < 0 || i >= (int)g->engines.size()) return -1;
+  if (first) *first = g->first[i];
+  if (count) *count = g->count[i];
+  return 0;
+}
+
+extern "C" double cortex_group_load_seconds(void *group) {
+  return group ? static_cast<Group *>(group)->load_s : 0.0;
+}
+
+extern "C" int cortex_group_forward(void *group, const int *tokens, int n_tok, float *logits) {
+  clear_error();
+  Group *g = static_cast<Group *>(group);
+  if (!g || !tokens) {
+    set_error("group and tokens must not be NULL");
+    return -1;
+  }
+  const long long V = g->engines[0]->d.V;
+  return g->run([&](int i) {
+    Engine &e = *g->engines[i];
+    return forward_batch(e, tokens + (size_t)g->first[i] * n_tok, g->count[i], n_tok, nullptr,
+                         logits ? logits + (size_t)g->first[i] * V : nullptr, SNAI_HOST_PTRS);
+  });
+}
+
+extern "C" int cortex_group_decode_steps(void *group, int steps, const float *uniforms,
+                                         const snai_sample_params *params, int *out_ids) {
+  clear_error();
+  Group *g = static_cast<Group *>(group);
+  if (!g || !params || !out_ids || steps < 0) {
+    set_error("group, params and out_ids must not be NULL, steps >= 0");
+    return -1;
+  }
+  if (steps == 0) return 0;
+  const size_t T = (size_t)g->total;
+  return g->run([&](int i) {
+    const int a = g->first[i], B = g->count[i];
+    // this shard's columns of [steps][total], contiguous
+    std::vector<float> u(uniforms ? (size_t)steps * B : 0);
+    for (int k = 0; uniforms && k < steps; ++k)
+      std::copy(uniforms + k * T + a, uniforms + k * T + a + B, u.begin() + (size_t)k * B);
+    std::vector<int> ids((size_t)steps * B);
+    const int r = cortex_decode_steps(g->engines[i], nullptr, B, steps, uniforms ? u.data() : nullptr, params,
+                                      ids.data(), SNAI_HOST_PTRS);
+    if (r) return r;
+    for (int k = 0; k < steps; ++k) std::copy(ids.begin() + (size_t)k * B, ids.begin() + (size_t)(k + 1) * B,
+                                              out_ids + k * T + a);
+    return 0;
+  });
 }
 
 // ============================================================================

@@ -99,6 +99,7 @@ struct Engine {
 
   // weights (fp32 masters; bf16 copies in BF16 mode)
   void *wblock = nullptr;
+  size_t wblock_bytes = 0;
   void *hblock = nullptr;
   float *emb = nullptr, *w_out = nullptr, *rms_final = nullptr;
   __nv_bfloat16 *w_out_h = nullptr;
@@ -199,6 +200,17 @@ int run_rows(Engine &e, const RowDesc *rows, int n, const int *tokens_d);
 
 // fp32 -> bf16 copy of a weight tensor on e.stream.
 int convert_bf16(Engine &e, const float *src, __nv_bfloat16 *dst, size_t n);
+// fp32 -> bf16 copies of up to 64 tensors (each a multiple of 4 elements,
+// 16-byte aligned) in one launch on e.stream.
+struct Bf16Segments {
+  struct Seg {
+    const float *src;
+    __nv_bfloat16 *dst;
+    size_t n;
+  } seg[64];
+  int count = 0;
+};
+int convert_bf16_segments(Engine &e, const Bf16Segments &segs);
 // Fills n floats with a value on e.stream.
 int fill_f32(Engine &e, float *dst, size_t n, float v);
 

@@ -42,6 +42,22 @@ __global__ void to_bf16_kernel(const float *__restrict__ src, __nv_bfloat16 *__r
     dst[i] = __float2bfloat16_rn(src[i]);
 }
 
+// Every tensor of a segment table in one launch: blockIdx.y picks the
+// segment, the grid's x dimension strides over it with 4-element steps
+// (every segment's length is a multiple of 4: d is).
+__global__ void to_bf16_segments_kernel(const Bf16Segments segs) {
+  const Bf16Segments::Seg s = segs.seg[blockIdx.y];
+  const size_t n4 = s.n / 4;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 v = __ldcs(reinterpret_cast<const float4 *>(s.src) + i);
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t *>(&lo);
+    pk.y = *reinterpret_cast<uint32_t *>(&hi);
+    *reinterpret_cast<uint2 *>(s.dst + 4 * i) = pk;
+  }
+}
+
 constexpr int kNormThreads = 256;
 
 // Block sum of squares of a D-vector (parallel tree; the reference sums
@@ -296,26 +312,29 @@ __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
 // (head, row, c) of S covers positions [c*chunk, min(n, (c+1)*chunk)), chunk =
 // ceil(n / S) rounded up to even (S is fixed per launch, the positions come
 // from the row descriptors, so a captured launch serves every later step).
-// It writes its local max m_c (starting at -9999, the reference's
-// initialisation, core/cortex.nim:517), l_c = sum exp(s_t - m_c) and
-// o_c = sum exp(s_t - m_c) v_t to part[row][head][c].  The last CTA of a
-// (row, head) to finish (an arrival counter, reset by it for the next launch)
-// merges the S results in split order: M = max m_c, w_c = exp(m_c - M),
-// att = sum w_c o_c / sum w_c l_c.  In decode passes (kvs non-null) every
-// CTA rotates q and the CTA holding position pos appends the new K/V row.
+// Each warp takes position pairs in sweeps of U pairs: it loads the K and V
+// rows of a sweep together (all loads in flight at once), keeps a running
+// max starting at -9999 (the reference's initialisation,
+// core/cortex.nim:517), the sum of exp(s_t - max) and the exp-weighted
+// value sum, rescaling both when the max rises.  The four warps' results are
+// merged into the CTA's (m_c, l_c, o_c), written to part[row][head][c]; the
+// last CTA of a (row, head) to finish (an arrival counter, reset by it for
+// the next launch) merges the S results in split order: M = max m_c,
+// w_c = exp(m_c - M), att = sum w_c o_c / sum w_c l_c.  In decode passes (kvs
+// non-null) every CTA rotates q and the CTA holding position pos appends the
+// new K/V row.
 constexpr int kSplitPartEntries = 640;  // (row, head, split) partial results
 constexpr int kSplitCounters = 256;     // (row, head) arrival counters
+constexpr int kSplitMax = 128;          // splits per (row, head)
 
 template <typename TA>
 __global__ void __launch_bounds__(kAttThreads) attention_split_hs64_kernel(
     const RowDesc *__restrict__ rows, const float *__restrict__ q, float *__restrict__ kv, TA *__restrict__ out,
     int D, int att_ch, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride, float sqrt_hs,
     const float *__restrict__ kvs, const float2 *__restrict__ rope, float *__restrict__ part, int *__restrict__ cnt) {
-  constexpr int HS = 64, PW = HS + 2, U = 8;
-  extern __shared__ float smem_att[];
-  float *red = smem_att;              // [32]
-  float *acc = smem_att + 32;         // [4 warps][64]
-  float *s = smem_att + 32 + 4 * HS;  // [chunk]
+  constexpr int HS = 64, PW = HS + 2, U = 8, NW = kAttThreads / 32;
+  __shared__ __align__(16) float wpart[NW][HS + 8];  // per warp: max, sum, (pad), 64 weighted value sums from [4]
+  __shared__ float wsplit[kSplitMax], lsplit[kSplitMax], ohalf[HS];
   __shared__ int is_last;
   grid_dep_wait();
   grid_dep_launch();
@@ -325,33 +344,41 @@ __global__ void __launch_bounds__(kAttThreads) attention_split_hs64_kernel(
   const int chunk = ((n + S - 1) / S + 1) & ~1;
   const int t0 = min(n, c * chunk), t1 = min(n, t0 + chunk), cn = t1 - t0;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int half = lane >> 4, part_i = lane & 15;
+  const int half = lane >> 4, pi = lane & 15;
 
   float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
   float *vbase = kbase + part_stride;
-  float4 qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + part_i * 4);
-  const int nc = kvs ? n - 1 : n;  // cache positions below nc; position pos from the staging entry
+  float4 qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + pi * 4);
+  const int nc = min(kvs ? n - 1 : n, t1);  // cache positions below nc; position pos from the staging entry
   float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
   if (kvs) {
     const float *kst = kvs + (size_t)m * 2 * att_ch + head * HS;
-    const float4 cs = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + part_i * 2);
+    const float4 cs = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + pi * 2);
     qv = rope4(qv, cs);
-    knew = rope4(*reinterpret_cast<const float4 *>(kst + part_i * 4), cs);
-    vnew = *reinterpret_cast<const float4 *>(kst + att_ch + part_i * 4);
+    knew = rope4(*reinterpret_cast<const float4 *>(kst + pi * 4), cs);
+    vnew = *reinterpret_cast<const float4 *>(kst + att_ch + pi * 4);
     if (warp == 0 && t0 <= n - 1 && n - 1 < t1)  // append: lanes 0..15 the K row, 16..31 the V row
-      *reinterpret_cast<float4 *>((half ? vbase : kbase) + (size_t)rd.pos * HS + part_i * 4) = half ? vnew : knew;
+      *reinterpret_cast<float4 *>((half ? vbase : kbase) + (size_t)rd.pos * HS + pi * 4) = half ? vnew : knew;
   }
 
-  // ---- scores of positions t0..t1-1 ----
-  for (int p0 = warp * U; 2 * p0 < cn; p0 += 4 * U) {
-    float4 kr[U];
+  // ---- per warp: running max, exp sum and weighted values over its pairs ----
+  float wm = -9999.0f, wl = 0.f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int p0 = warp * U; 2 * p0 < cn; p0 += NW * U) {
+    float4 kr[U], vr[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int t = t0 + 2 * (p0 + u) + half;
-      kr[u] = t < min(nc, t1) ? __ldcs(reinterpret_cast<const float4 *>(kbase + (size_t)t * HS + part_i * 4))
-              : t < t1       ? knew
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      const bool cached = t < nc;
+      kr[u] = cached ? __ldcs(reinterpret_cast<const float4 *>(kbase + (size_t)t * HS + pi * 4))
+              : t < t1 ? knew
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      vr[u] = cached ? __ldcs(reinterpret_cast<const float4 *>(vbase + (size_t)t * HS + pi * 4))
+              : t < t1 ? vnew
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    float sc[U];
+    float mx = wm;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       float d = qv.x * kr[u].x + qv.y * kr[u].y + qv.z * kr[u].z + qv.w * kr[u].w;
@@ -359,83 +386,90 @@ __global__ void __launch_bounds__(kAttThreads) attention_split_hs64_kernel(
       d += __shfl_xor_sync(0xffffffffu, d, 4);
       d += __shfl_xor_sync(0xffffffffu, d, 2);
       d += __shfl_xor_sync(0xffffffffu, d, 1);
-      const int t = t0 + 2 * (p0 + u) + half;
-      if (part_i == 0 && t < t1) s[t - t0] = __fdiv_rn(d, sqrt_hs);
+      sc[u] = __fdiv_rn(d, sqrt_hs);
+      if (t0 + 2 * (p0 + u) + half < t1) mx = fmaxf(mx, sc[u]);
     }
-  }
-  __syncthreads();
-  // ---- local max from -9999, exponentials, their sum ----
-  float mx = -9999.0f;
-  for (int i = threadIdx.x; i < cn; i += blockDim.x) mx = fmaxf(mx, s[i]);
-  mx = warp_max(mx);
-  if (lane == 0) red[warp] = mx;
-  __syncthreads();
-  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  __syncthreads();
-  float sum = 0.f;
-  for (int i = threadIdx.x; i < cn; i += blockDim.x) {
-    const float ev = expf(__fsub_rn(s[i], mx));
-    s[i] = ev;
-    sum += ev;
-  }
-  sum = warp_sum(sum);
-  if (lane == 0) red[warp] = sum;
-  __syncthreads();
-  sum = red[0] + red[1] + red[2] + red[3];
-
-  // ---- sum of exp-weighted values ----
-  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int p0 = warp * U; 2 * p0 < cn; p0 += 4 * U) {
-    float4 vr[U];
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float scale = expf(__fsub_rn(wm, mx));
+    wl = __fmul_rn(wl, scale);
+    o.x = __fmul_rn(o.x, scale);
+    o.y = __fmul_rn(o.y, scale);
+    o.z = __fmul_rn(o.z, scale);
+    o.w = __fmul_rn(o.w, scale);
+    float ls = 0.f;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int t = t0 + 2 * (p0 + u) + half;
-      vr[u] = t < min(nc, t1) ? __ldcs(reinterpret_cast<const float4 *>(vbase + (size_t)t * HS + part_i * 4))
-              : t < t1       ? vnew
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (t0 + 2 * (p0 + u) + half < t1) {
+        const float e = expf(__fsub_rn(sc[u], mx));
+        ls = __fadd_rn(ls, e);
+        o.x = __fadd_rn(o.x, __fmul_rn(vr[u].x, e));
+        o.y = __fadd_rn(o.y, __fmul_rn(vr[u].y, e));
+        o.z = __fadd_rn(o.z, __fmul_rn(vr[u].z, e));
+        o.w = __fadd_rn(o.w, __fmul_rn(vr[u].w, e));
+      }
     }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int t = t0 + 2 * (p0 + u) + half;
-      const float wt = t < t1 ? s[t - t0] : 0.f;
-      a.x = __fadd_rn(a.x, __fmul_rn(vr[u].x, wt));
-      a.y = __fadd_rn(a.y, __fmul_rn(vr[u].y, wt));
-      a.z = __fadd_rn(a.z, __fmul_rn(vr[u].z, wt));
-      a.w = __fadd_rn(a.w, __fmul_rn(vr[u].w, wt));
-    }
+    wl = __fadd_rn(wl, __fadd_rn(ls, __shfl_xor_sync(0xffffffffu, ls, 16)));
+    wm = mx;
   }
-  a.x += __shfl_xor_sync(0xffffffffu, a.x, 16);
-  a.y += __shfl_xor_sync(0xffffffffu, a.y, 16);
-  a.z += __shfl_xor_sync(0xffffffffu, a.z, 16);
-  a.w += __shfl_xor_sync(0xffffffffu, a.w, 16);
-  if (half == 0) *reinterpret_cast<float4 *>(acc + warp * HS + part_i * 4) = a;
+  o.x += __shfl_xor_sync(0xffffffffu, o.x, 16);
+  o.y += __shfl_xor_sync(0xffffffffu, o.y, 16);
+  o.z += __shfl_xor_sync(0xffffffffu, o.z, 16);
+  o.w += __shfl_xor_sync(0xffffffffu, o.w, 16);
+  if (lane < 16) *reinterpret_cast<float4 *>(&wpart[warp][4 + 4 * pi]) = o;
+  if (lane == 0) {
+    wpart[warp][0] = wm;
+    wpart[warp][1] = wl;
+  }
   __syncthreads();
+  // ---- this CTA's (m_c, l_c, o_c) from its warps ----
   float *pp = part + (size_t)(m * H + head) * S * PW;
-  if (threadIdx.x < HS)
-    pp[c * PW + 2 + threadIdx.x] =
-        acc[threadIdx.x] + acc[HS + threadIdx.x] + acc[2 * HS + threadIdx.x] + acc[3 * HS + threadIdx.x];
-  if (threadIdx.x == 0) {
-    pp[c * PW] = mx;
-    pp[c * PW + 1] = sum;
+  if (threadIdx.x < HS) {
+    float M = wpart[0][0];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) M = fmaxf(M, wpart[w][0]);
+    float L = 0.f, ov = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float sw = expf(__fsub_rn(wpart[w][0], M));
+      L = __fadd_rn(L, __fmul_rn(sw, wpart[w][1]));
+      ov = __fadd_rn(ov, __fmul_rn(sw, wpart[w][4 + threadIdx.x]));
+    }
+    pp[c * PW + 2 + threadIdx.x] = ov;
+    if (threadIdx.x == 0) {
+      pp[c * PW] = M;
+      pp[c * PW + 1] = L;
+    }
   }
-  // ---- the last CTA of (row, head) merges the S partial results ----
+  // ---- the last CTA of (row, head) merges the S results ----
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) is_last = atomicAdd(&cnt[m * H + head], 1) == S - 1;
   __syncthreads();
   if (!is_last) return;
   __threadfence();
+  if (threadIdx.x < S) wsplit[threadIdx.x] = __ldcg(pp + threadIdx.x * PW);
+  __syncthreads();
+  float M = -9999.0f;
+  for (int cc = 0; cc < S; ++cc) M = fmaxf(M, wsplit[cc]);
+  __syncthreads();
+  if (threadIdx.x < S) {
+    const float w = expf(__fsub_rn(wsplit[threadIdx.x], M));
+    wsplit[threadIdx.x] = w;
+    lsplit[threadIdx.x] = __fmul_rn(w, __ldcg(pp + threadIdx.x * PW + 1));
+  }
+  __syncthreads();
+  // channel ch, splits of parity h (two threads per channel), in split order
+  const int ch = threadIdx.x & (HS - 1), h = threadIdx.x >> 6;
+  float ov = 0.f;
+#pragma unroll 8
+  for (int cc = h; cc < S; cc += 2) ov = __fadd_rn(ov, __fmul_rn(wsplit[cc], __ldcg(pp + cc * PW + 2 + ch)));
+  if (h == 1) ohalf[ch] = ov;
+  __syncthreads();
   TA *orow = out + (size_t)m * D;
-  if (threadIdx.x < HS) {
-    float M = -9999.0f;
-    for (int cc = 0; cc < S; ++cc) M = fmaxf(M, __ldcg(pp + cc * PW));
-    float L = 0.f, o = 0.f;
-    for (int cc = 0; cc < S; ++cc) {
-      const float w = expf(__fsub_rn(__ldcg(pp + cc * PW), M));
-      L = __fadd_rn(L, __fmul_rn(w, __ldcg(pp + cc * PW + 1)));
-      o = __fadd_rn(o, __fmul_rn(w, __ldcg(pp + cc * PW + 2 + threadIdx.x)));
-    }
-    ActIO<TA>::store(orow + head * HS + threadIdx.x, __fdiv_rn(o, L));
+  if (h == 0) {
+    float L = 0.f;
+    for (int cc = 0; cc < S; ++cc) L = __fadd_rn(L, lsplit[cc]);
+    ActIO<TA>::store(orow + head * HS + ch, __fdiv_rn(__fadd_rn(ov, ohalf[ch]), L));
   }
   if (threadIdx.x == 0) cnt[m * H + head] = 0;
   if (head == H - 1) att_zero_tail(orow, att_ch, D);
@@ -893,11 +927,10 @@ static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_pos
   int S = 1;
   if (d.hs == 64 && e.att_split && e.att_part && rh < nsm && rh <= kSplitCounters) {
     S = std::min((2 * nsm + rh - 1) / rh, (d.ctx + 63) / 64);
-    S = std::min(S, kSplitPartEntries / rh);
+    S = std::min({S, kSplitPartEntries / rh, kSplitMax});
   }
   if (S >= 2) {
-    const size_t sm = (32 + 4 * 64 + (size_t)((d.ctx + S - 1) / S + 2)) * sizeof(float);
-    launch_k(e, !tc_path(e, M), attention_split_hs64_kernel<TA>, dim3(d.heads, M, S), dim3(kAttThreads), sm,
+    launch_k(e, !tc_path(e, M), attention_split_hs64_kernel<TA>, dim3(d.heads, M, S), dim3(kAttThreads), 0,
              e.rows_d, e.q, e.kv, out, d.D, d.att_ch, e.kv_slot_stride, layer_off, e.kv_part_stride,
              e.kv_head_stride, e.sqrt_hs, defer ? e.kvs : nullptr, e.rope, e.att_part, e.att_cnt);
   } else if (d.hs == 64) {
@@ -1162,6 +1195,13 @@ void prof_collect(Engine &e) {
     e.prof_free.push_back(p.a);
   }
   e.prof_pending.clear();
+}
+
+int convert_bf16_segments(Engine &e, const Bf16Segments &segs) {
+  if (segs.count <= 0) return 0;
+  to_bf16_segments_kernel<<<dim3(2 * device_sm_count(e.device), segs.count), 256, 0, e.stream>>>(segs);
+  e.launches++;
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
 int convert_bf16(Engine &e, const float *src, __nv_bfloat16 *dst, size_t n) {

@@ -170,6 +170,58 @@ class Cortex:
         return out
 
 
+class CortexGroup:
+    """Engines on several GPUs in one process (cortex_group_*): `total`
+    sequences split into contiguous shards, one per listed device; one file
+    read, weights fanned out by peer copies; calls gathered on the host."""
+
+    def __init__(self, path, num_heads, total, devices, precision=_lib.PREC_FP32):
+        self.lib = load()
+        d = np.ascontiguousarray(devices, dtype=np.int32)
+        h = self.lib.cortex_group_load(str(path).encode(), int(num_heads), int(total), _ptr(d), len(d),
+                                       int(precision))
+        if not h:
+            raise CortexError(f"could not create the group: {_lib.last_error()}")
+        self.h = h
+        self.total = total
+        self.size = self.lib.cortex_group_size(h)
+        self.vocab = self.lib.get_vocab_size(self.lib.cortex_group_engine(h, 0))
+        self.load_seconds = self.lib.cortex_group_load_seconds(h)
+
+    def shard(self, i):
+        a, n = ctypes.c_int(), ctypes.c_int()
+        check(self.lib.cortex_group_shard(self.h, i, ctypes.byref(a), ctypes.byref(n)), "cortex_group_shard")
+        return a.value, a.value + n.value
+
+    def engine_state(self, i):
+        return self.lib.cortex_group_engine(self.h, i)
+
+    def forward(self, tokens, want_logits=True):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros((self.total, self.vocab), dtype=np.float32) if want_logits else None
+        check(self.lib.cortex_group_forward(self.h, _ptr(t), t.shape[1], None if out is None else _ptr(out)),
+              "cortex_group_forward")
+        return out
+
+    def decode_steps(self, uniforms, params):
+        u = np.ascontiguousarray(uniforms, dtype=np.float32)
+        ids = np.zeros(u.shape, dtype=np.int32)
+        check(self.lib.cortex_group_decode_steps(self.h, u.shape[0], _ptr(u), ctypes.byref(params), _ptr(ids)),
+              "cortex_group_decode_steps")
+        return ids
+
+    def close(self):
+        if self.h:
+            self.lib.cortex_group_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def sample_device(logits_dev, uniforms_dev, params, hist_dev=None, hist_len_dev=None, out_dev=None, stream=0):
     """Stateless GPU sampler over device tensors (cortex_sample)."""
     lib = load()
