@@ -632,6 +632,9 @@ def group_load_line(name, n, single_s):
         return {"error": f"rank 0 sees {torch.cuda.device_count()} GPUs, fewer than {n}"}
     path = make_model(name)
     try:
+        for i in range(n):  # every GPU's context exists before the timed loads
+            torch.zeros(1, device=f"cuda:{i}")
+            torch.cuda.synchronize(i)
         t0 = time.perf_counter()
         e = Cortex(path, num_heads=c["HEADS"], max_seqs=1, device=0, precision=PREC_BF16)
         one_s = time.perf_counter() - t0
