@@ -120,7 +120,8 @@ def make_model(name, rank=0):
             modelgen.random_model(drone, V, 128, 512, 2, seed=1234, std=0.02)
         p = os.path.join(bench_dir(), f"snai_bench_c2_up256_r{rank}.snai")
         if not os.path.exists(p) or os.path.getsize(p) != modelgen.expected_size(V, D, 4 * D, L):
-            modelgen.upscale_model(drone, p, D, seed=4321)
+            from snai_b200 import upscale_file
+            upscale_file(drone, p, D, seed=4321)  # Net2Net upscale on the GPU
         return p
     p = os.path.join(bench_dir(), f"snai_bench_d{D}_L{L}_seed1234_r{rank}.snai")
     if not os.path.exists(p) or os.path.getsize(p) != modelgen.expected_size(V, D, 4 * D, L):
@@ -644,6 +645,20 @@ def group_load_line(name, n, single_s):
                "rank_single_gpu_seconds": single_s, "model_bytes": os.path.getsize(path),
                "how": "one file read into GPU 0 (pinned double-buffered), peer copies to the others, bf16 packing "
                       "on every GPU"}
+        # the federated average of the n engines' weights (cortex_group_average):
+        # each GPU reads its shard from every GPU (peer loads), then copies the
+        # other shards in (peer copies); NVLink bytes per GPU, each way
+        g.average()
+        t0 = time.perf_counter()
+        reps = 5
+        for _ in range(reps):
+            g.average()
+        avg_s = (time.perf_counter() - t0) / reps
+        wbytes = (os.path.getsize(path) - 28)
+        link = 2.0 * wbytes * (n - 1) / n
+        out["average"] = {"seconds": avg_s, "weight_bytes": wbytes, "nvlink_bytes_per_gpu": link,
+                          "GB/s_per_gpu": link / avg_s / 1e9, "peer_copy_reference_GB/s": 770.0,
+                          "timing": f"wall clock over {reps} calls, each waiting for every GPU"}
         g.close()
         return out
     except Exception as ex:  # noqa: BLE001

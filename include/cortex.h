@@ -268,6 +268,41 @@ CORTEX_API int cortex_group_forward(void *group, const int *tokens, int n_tok, f
 CORTEX_API int cortex_group_decode_steps(void *group, int steps, const float *uniforms,
                                          const snai_sample_params *params, int *out_ids);
 
+/* ------------------------------------------------------------------------ */
+/* Merging, federated averaging and Net2Net upscaling on the GPU.  The      */
+/* reference does these in PHP outside the engine; here they are library    */
+/* calls.  Return 0, or a negative code with cortex_last_error().           */
+/* ------------------------------------------------------------------------ */
+
+/* src/net2net_forge.php:29-102 merge_models / src/train_cluster.php:144-224
+ * average_models_stream: writes out_path = the first file's 28-byte header
+ * (every header must equal it, else -2) followed by, for every float j of
+ * the first file, fp32((sum_i double(x_i[j])) / n) summed in file order (a
+ * shorter file contributes 0.0 past its end).  1 <= n <= 64; the sums run
+ * on `device`. */
+CORTEX_API int cortex_merge_files(const char *const *paths, int n, const char *out_path, int device);
+
+/* src/net2net_forge.php:149-214 upscale_model on `device`: hidden_dim ->
+ * target_dim (> hidden_dim, else -2), ffn -> 4 * target_dim, ctx x 2,
+ * layers x 2 (new layer l repeats l % old_layers, its Wo and W_down scaled
+ * by 0.01); old entries fp32(double(x) * scale), new entries
+ * fp32(((u * 2) - 1) * 0.005).  The reference draws u from mt_rand(); here
+ * u comes from SplitMix64 keyed by (seed, output tensor, element), so the
+ * same seed gives the same file. */
+CORTEX_API int cortex_upscale_file(const char *in_path, const char *out_path, int target_dim, unsigned long long seed,
+                                   int device);
+
+/* The federated average (the arithmetic of src/train_cluster.php:144-224)
+ * of n engine states' weights in GPU memory, typically one engine per GPU:
+ * afterwards every state holds fp32((sum_i double(w_i)) / n), summed in
+ * state order.  Each GPU computes its shard of the weights reading the
+ * other GPUs' copies with peer loads over NVLink, then every GPU copies the
+ * shards in (peer copies) and repacks its bf16 copies.  Same model shape
+ * everywhere; 1 <= n <= 64.  KV caches and positions are untouched. */
+CORTEX_API int cortex_average_states(void *const *states, int n);
+/* cortex_average_states over a group's engines. */
+CORTEX_API int cortex_group_average(void *group);
+
 /* Self-test of the failure path every kernel wait takes.  No counterpart in
  * the reference (whose engine has no device waits).  Queues one kernel on
  * the state's stream that waits on an mbarrier nothing completes; the wait

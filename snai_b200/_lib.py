@@ -81,6 +81,10 @@ SIGNATURES = {
     "cortex_group_load_seconds": (c_double, [c_void_p]),
     "cortex_group_forward": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     "cortex_group_decode_steps": (c_int, [c_void_p, c_int, c_void_p, ctypes.POINTER(SampleParams), c_void_p]),
+    "cortex_merge_files": (c_int, [ctypes.POINTER(c_char_p), c_int, c_char_p, c_int]),
+    "cortex_upscale_file": (c_int, [c_char_p, c_char_p, c_int, ctypes.c_ulonglong, c_int]),
+    "cortex_average_states": (c_int, [ctypes.POINTER(c_void_p), c_int]),
+    "cortex_group_average": (c_int, [c_void_p]),
     "cortex_selftest_wait_timeout": (c_int, [c_void_p, ctypes.c_longlong]),
     "cortex_kernel_launches": (ctypes.c_longlong, [c_void_p]),
 }

@@ -1373,6 +1373,368 @@ extern "C" int cortex_group_decode_steps(void *group, int steps, const float *un
 }
 
 // ============================================================================
+// Merging, federated averaging and Net2Net upscaling (net2net.cu kernels)
+// ============================================================================
+namespace snai {
+namespace {
+
+// Reads up to n bytes; returns the count (short only at the end of the file).
+size_t read_full(FILE *f, void *dst, size_t n) {
+  size_t got = 0;
+  while (got < n) {
+    const size_t r = fread(static_cast<char *>(dst) + got, 1, n - got, f);
+    if (r == 0) break;
+    got += r;
+  }
+  return got;
+}
+
+struct Files {
+  std::vector<FILE *> f;
+  ~Files() {
+    for (FILE *x : f)
+      if (x) fclose(x);
+  }
+};
+
+struct DevBuf {
+  void *p = nullptr;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+};
+struct HostBuf {
+  void *p = nullptr;
+  ~HostBuf() {
+    if (p) cudaFreeHost(p);
+  }
+};
+
+// src/net2net_forge.php:29-102 (merge_models) and src/train_cluster.php:144-224
+// (average_models_stream): the first file's header (every header must equal
+// it), then float j = fp32((sum_i double(x_i[j])) / n) for every float of
+// the first file; a shorter file contributes 0.0 past its end.
+int merge_files(const char *const *paths, int n, const char *out_path, int device) {
+  clear_error();
+  if (!paths || n < 1 || n > kMergeMaxSources || !out_path) {
+    set_error("merge needs 1..%d input files and an output path", kMergeMaxSources);
+    return -2;
+  }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    set_error("device %d not available", device);
+    return -2;
+  }
+  DeviceGuard g(device);
+  Files in;
+  unsigned char hdr0[28];
+  for (int i = 0; i < n; ++i) {
+    FILE *f = paths[i] ? fopen(paths[i], "rb") : nullptr;
+    if (!f) {
+      set_error("cannot read %s", paths[i] ? paths[i] : "(null)");
+      return -2;
+    }
+    in.f.push_back(f);
+    unsigned char h[28];
+    const size_t got = read_full(f, h, 28);
+    if (i == 0) {
+      memcpy(hdr0, h, 28);
+      if (got != 28) {
+        set_error("%s: short header", paths[0]);
+        return -2;
+      }
+    } else if (got != 28 || memcmp(h, hdr0, 28) != 0) {
+      set_error("%s: header differs from %s (model shapes do not match)", paths[i], paths[0]);
+      return -2;
+    }
+  }
+  FILE *out = fopen(out_path, "wb");
+  if (!out) {
+    set_error("cannot write %s", out_path);
+    return -2;
+  }
+  Files outf;
+  outf.f.push_back(out);
+  if (fwrite(hdr0, 1, 28, out) != 28) {
+    set_error("write to %s failed", out_path);
+    return -2;
+  }
+  constexpr size_t kChunk = 4u << 20;  // floats per file per round
+  HostBuf hin, hout;
+  DevBuf din, dout;
+  cudaStream_t st = nullptr;
+  if (cudaHostAlloc(&hin.p, kChunk * 4 * n, cudaHostAllocDefault) != cudaSuccess ||
+      cudaHostAlloc(&hout.p, kChunk * 4, cudaHostAllocDefault) != cudaSuccess ||
+      cudaMalloc(&din.p, kChunk * 4 * n) != cudaSuccess || cudaMalloc(&dout.p, kChunk * 4) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
+    set_error("merge buffers: %s", cudaGetErrorString(cudaGetLastError()));
+    if (st) cudaStreamDestroy(st);
+    return -3;
+  }
+  float *hi = static_cast<float *>(hin.p), *ho = static_cast<float *>(hout.p);
+  float *di = static_cast<float *>(din.p), *dd = static_cast<float *>(dout.p);
+  int rc = 0;
+  for (;;) {
+    const size_t got0 = read_full(in.f[0], hi, kChunk * 4);
+    const size_t nf = got0 / 4;  // whole floats of the first file (intval(strlen / 4))
+    if (got0 == 0) break;
+    for (int i = 1; i < n; ++i) {
+      const size_t gi = read_full(in.f[i], hi + (size_t)i * kChunk, nf * 4) / 4;
+      std::fill(hi + (size_t)i * kChunk + gi, hi + (size_t)i * kChunk + nf, 0.0f);  // past the end: 0.0
+    }
+    MergeSources srcs;
+    srcs.n = n;
+    for (int i = 0; i < n; ++i) srcs.src[i] = di + (size_t)i * kChunk;
+    bool ok = true;
+    for (int i = 0; ok && i < n; ++i)
+      ok = cudaMemcpyAsync(di + (size_t)i * kChunk, hi + (size_t)i * kChunk, nf * 4, cudaMemcpyHostToDevice, st) ==
+           cudaSuccess;
+    ok = ok && launch_merge_mean(srcs, dd, nf, device, st) == 0 &&
+         cudaMemcpyAsync(ho, dd, nf * 4, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+         cudaStreamSynchronize(st) == cudaSuccess;
+    if (!ok) {
+      set_error("merge on device %d failed: %s", device, cudaGetErrorString(cudaGetLastError()));
+      rc = -4;
+      break;
+    }
+    if (fwrite(ho, 4, nf, out) != nf) {
+      set_error("write to %s failed", out_path);
+      rc = -2;
+      break;
+    }
+    if (got0 < kChunk * 4) break;
+  }
+  cudaStreamDestroy(st);
+  return rc;
+}
+
+// src/net2net_forge.php:149-214 upscale_model on the GPU.
+int upscale_file(const char *in_path, const char *out_path, int target_dim, uint64_t seed, int device) {
+  clear_error();
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    set_error("device %d not available", device);
+    return -2;
+  }
+  FILE *f = in_path ? fopen(in_path, "rb") : nullptr;
+  if (!f) {
+    set_error("input file not found: %s", in_path ? in_path : "(null)");
+    return -2;
+  }
+  Files in;
+  in.f.push_back(f);
+  unsigned char hdr[28];
+  if (read_full(f, hdr, 28) != 28) {
+    set_error("%s: short header", in_path);
+    return -2;
+  }
+  uint32_t p[5];
+  for (int i = 0; i < 5; ++i)
+    p[i] = (uint32_t)hdr[8 + 4 * i] | ((uint32_t)hdr[9 + 4 * i] << 8) | ((uint32_t)hdr[10 + 4 * i] << 16) |
+           ((uint32_t)hdr[11 + 4 * i] << 24);
+  const int64_t vocab = p[0], old_dim = p[1], old_ffn = p[2], old_ctx = p[3], old_layers = p[4];
+  if (target_dim <= old_dim) {
+    set_error("target dimension %d must be larger than the current %lld", target_dim, (long long)old_dim);
+    return -2;
+  }
+  if (vocab < 1 || old_dim < 1 || old_layers < 1 || target_dim > 65536 || vocab * (int64_t)target_dim > (1ll << 33)) {
+    set_error("%s: unsupported shape", in_path);
+    return -2;
+  }
+  const int64_t new_dim = target_dim, new_ffn = 4 * new_dim, new_ctx = old_ctx * 2, new_layers = old_layers * 2;
+  // the whole input (missing floats of a short file read as 0.0, like the reference's unpack of a short row)
+  const int64_t layer_floats = 2 * old_dim + 4 * old_dim * old_dim + 2 * old_dim * old_ffn;
+  const int64_t in_floats = 2 * vocab * old_dim + old_dim + old_layers * layer_floats;
+  std::vector<float> src((size_t)in_floats, 0.0f);
+  read_full(f, src.data(), (size_t)in_floats * 4);
+  FILE *out = out_path ? fopen(out_path, "wb") : nullptr;
+  if (!out) {
+    set_error("cannot write %s", out_path ? out_path : "(null)");
+    return -2;
+  }
+  Files outf;
+  outf.f.push_back(out);
+  unsigned char oh[28];
+  memcpy(oh, hdr, 8);  // the input's magic
+  const uint32_t np[5] = {(uint32_t)vocab, (uint32_t)new_dim, (uint32_t)new_ffn, (uint32_t)new_ctx,
+                          (uint32_t)new_layers};
+  for (int i = 0; i < 5; ++i)
+    for (int b = 0; b < 4; ++b) oh[8 + 4 * i + b] = (unsigned char)(np[i] >> (8 * b));
+  if (fwrite(oh, 1, 28, out) != 28) {
+    set_error("write to %s failed", out_path);
+    return -2;
+  }
+  DeviceGuard g(device);
+  const size_t max_new = (size_t)std::max<int64_t>({vocab * new_dim, new_ffn * new_dim});
+  const size_t max_old = (size_t)std::max<int64_t>({vocab * old_dim, old_ffn * old_dim, old_dim * old_dim});
+  DevBuf dold, dnew;
+  std::vector<float> host(max_new);
+  if (cudaMalloc(&dold.p, max_old * 4) != cudaSuccess || cudaMalloc(&dnew.p, max_new * 4) != cudaSuccess) {
+    set_error("upscale buffers: %s", cudaGetErrorString(cudaGetLastError()));
+    return -3;
+  }
+  uint64_t stream = 0;  // output tensor index: keys the noise
+  auto grow = [&](const float *old, int64_t orr, int64_t oc, int64_t nr, int64_t nc, double scale) -> int {
+    if (cudaMemcpy(dold.p, old, (size_t)(orr * oc) * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        launch_upscale_tensor(static_cast<float *>(dold.p), (int)orr, (int)oc, static_cast<float *>(dnew.p), (int)nr,
+                              (int)nc, scale, seed, stream++, device, nullptr) != 0 ||
+        cudaMemcpy(host.data(), dnew.p, (size_t)(nr * nc) * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+      set_error("upscale on device %d failed: %s", device, cudaGetErrorString(cudaGetLastError()));
+      return -4;
+    }
+    if (fwrite(host.data(), 4, (size_t)(nr * nc), out) != (size_t)(nr * nc)) {
+      set_error("write to %s failed", out_path);
+      return -2;
+    }
+    return 0;
+  };
+  const float *at = src.data();
+  int rc = grow(at, vocab, old_dim, vocab, new_dim, 1.0);  // embeddings
+  at += vocab * old_dim;
+  if (!rc) rc = grow(at, vocab, old_dim, vocab, new_dim, 1.0);  // w_out
+  at += vocab * old_dim;
+  if (!rc) rc = grow(at, 1, old_dim, 1, new_dim, 1.0);  // rms_final
+  at += old_dim;
+  const float *layer0 = at;
+  for (int64_t l = 0; !rc && l < new_layers; ++l) {
+    const float *q = layer0 + (l % old_layers) * layer_floats;  // new layers repeat l % old_layers
+    const double os = l >= old_layers ? 0.01 : 1.0;              // Wo and W_down of a new layer
+    const int64_t dd = old_dim * old_dim;
+    if (!rc) rc = grow(q, 1, old_dim, 1, new_dim, 1.0);
+    if (!rc) rc = grow(q + old_dim, 1, old_dim, 1, new_dim, 1.0);
+    if (!rc) rc = grow(q + 2 * old_dim, old_dim, old_dim, new_dim, new_dim, 1.0);
+    if (!rc) rc = grow(q + 2 * old_dim + dd, old_dim, old_dim, new_dim, new_dim, 1.0);
+    if (!rc) rc = grow(q + 2 * old_dim + 2 * dd, old_dim, old_dim, new_dim, new_dim, 1.0);
+    if (!rc) rc = grow(q + 2 * old_dim + 3 * dd, old_dim, old_dim, new_dim, new_dim, os);
+    if (!rc) rc = grow(q + 2 * old_dim + 4 * dd, old_ffn, old_dim, new_ffn, new_dim, 1.0);
+    if (!rc) rc = grow(q + 2 * old_dim + 4 * dd + old_ffn * old_dim, old_dim, old_ffn, new_dim, new_ffn, os);
+  }
+  return rc;
+}
+
+// The federated average of engines' weights in GPU memory: every engine ends
+// with fp32((sum_i double(w_i)) / n), summed in engine order.  Device g
+// computes shard g of the weight block from every engine's copy (peer loads
+// over NVLink where the copies are on other GPUs) into a buffer of its own;
+// once all shards exist, every engine copies them into its weights (peer
+// copies) and packs its bf16 copies.
+int average_engines(Engine *const *es, int n) {
+  if (n < 1 || n > kMergeMaxSources) {
+    set_error("averaging needs 1..%d engines", kMergeMaxSources);
+    return -2;
+  }
+  for (int i = 0; i < n; ++i) {
+    if (!es[i]) {
+      set_error("engine %d is NULL", i);
+      return -1;
+    }
+    const Dims &a = es[0]->d, &b = es[i]->d;
+    if (a.V != b.V || a.D != b.D || a.L != b.L || es[i]->wblock_bytes != es[0]->wblock_bytes) {
+      set_error("engine %d has another model shape than engine 0", i);
+      return -2;
+    }
+  }
+  const size_t E = es[0]->wblock_bytes / 4;
+  for (int i = 0; i < n; ++i) {
+    DeviceGuard g(es[i]->device);
+    cudaStreamSynchronize(es[i]->stream);
+    for (int j = 0; j < n; ++j) {
+      if (es[j]->device == es[i]->device) continue;
+      int can = 0;
+      if (cudaDeviceCanAccessPeer(&can, es[i]->device, es[j]->device) != cudaSuccess || !can) {
+        set_error("device %d cannot read device %d's memory", es[i]->device, es[j]->device);
+        return -5;
+      }
+      const cudaError_t pe = cudaDeviceEnablePeerAccess(es[j]->device, 0);
+      if (pe != cudaSuccess && pe != cudaErrorPeerAccessAlreadyEnabled) {
+        set_error("peer access %d -> %d: %s", es[i]->device, es[j]->device, cudaGetErrorString(pe));
+        return -5;
+      }
+      cudaGetLastError();
+    }
+  }
+  std::vector<DevBuf> part(n);
+  std::vector<size_t> a0(n), cnt(n);
+  for (int i = 0; i < n; ++i) {
+    a0[i] = E * i / n;
+    cnt[i] = E * (i + 1) / n - a0[i];
+  }
+  MergeSources srcs;
+  srcs.n = n;
+  for (int i = 0; i < n; ++i) {
+    DeviceGuard g(es[i]->device);
+    for (int j = 0; j < n; ++j) srcs.src[j] = static_cast<const float *>(es[j]->wblock) + a0[i];
+    if (cudaMalloc(&part[i].p, std::max<size_t>(cnt[i], 1) * 4) != cudaSuccess ||
+        launch_merge_mean(srcs, static_cast<float *>(part[i].p), cnt[i], es[i]->device, es[i]->stream) != 0) {
+      set_error("average on device %d failed: %s", es[i]->device, cudaGetErrorString(cudaGetLastError()));
+      return -4;
+    }
+  }
+  for (int i = 0; i < n; ++i) {  // every shard is done before any engine's weights change
+    DeviceGuard g(es[i]->device);
+    if (cudaStreamSynchronize(es[i]->stream) != cudaSuccess) {
+      set_error("average on device %d failed: %s", es[i]->device, cudaGetErrorString(cudaGetLastError()));
+      return -4;
+    }
+  }
+  for (int i = 0; i < n; ++i) {
+    DeviceGuard g(es[i]->device);
+    for (int j = 0; j < n; ++j)
+      if (cudaMemcpyPeerAsync(static_cast<float *>(es[i]->wblock) + a0[j], es[i]->device, part[j].p, es[j]->device,
+                              cnt[j] * 4, es[i]->stream) != cudaSuccess) {
+        set_error("shard copy %d -> %d failed: %s", es[j]->device, es[i]->device,
+                  cudaGetErrorString(cudaGetLastError()));
+        return -4;
+      }
+    if (refresh_bf16(*es[i])) {
+      set_error("bf16 packing on device %d failed", es[i]->device);
+      return -4;
+    }
+  }
+  for (int i = 0; i < n; ++i) {
+    DeviceGuard g(es[i]->device);
+    if (cudaStreamSynchronize(es[i]->stream) != cudaSuccess) {
+      set_error("average on device %d failed: %s", es[i]->device, cudaGetErrorString(cudaGetLastError()));
+      return -4;
+    }
+  }
+  return 0;
+}
+
+}  // namespace
+}  // namespace snai
+
+extern "C" int cortex_merge_files(const char *const *paths, int n, const char *out_path, int device) {
+  return merge_files(paths, n, out_path, device);
+}
+
+extern "C" int cortex_upscale_file(const char *in_path, const char *out_path, int target_dim,
+                                   unsigned long long seed, int device) {
+  return upscale_file(in_path, out_path, target_dim, seed, device);
+}
+
+extern "C" int cortex_average_states(void *const *states, int n) {
+  clear_error();
+  if (!states) {
+    set_error("states is NULL");
+    return -1;
+  }
+  std::vector<Engine *> es(n > 0 ? n : 0);
+  for (int i = 0; i < n; ++i) es[i] = static_cast<Engine *>(states[i]);
+  return average_engines(es.data(), n);
+}
+
+extern "C" int cortex_group_average(void *group) {
+  clear_error();
+  Group *g = static_cast<Group *>(group);
+  if (!g) {
+    set_error("group is NULL");
+    return -1;
+  }
+  return average_engines(g->engines.data(), (int)g->engines.size());
+}
+
+// ============================================================================
 // Forward pass without allocation
 // ============================================================================
 //

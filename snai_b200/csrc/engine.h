@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
+#include <cstdint>
+
 #include <atomic>
 #include <map>
 #include <mutex>
@@ -241,6 +243,20 @@ int check_sample_args(const SampleLaunch &a);
 // host-to-device copies.  Returns 0 or a negative error.
 int decode_step_device(Engine &e, int batch, const SampleLaunch &sampler);
 int launch_sampler(const SampleLaunch &a, cudaStream_t stream);
+
+// ---- merging and Net2Net (net2net.cu) ----
+constexpr int kMergeMaxSources = 64;
+struct MergeSources {
+  const float *src[kMergeMaxSources];
+  int n = 0;
+};
+// out[j] = fp32((sum_i double(src_i[j])) / n), sources summed in order (any
+// GPU's memory the device can read).
+int launch_merge_mean(const MergeSources &srcs, float *out, size_t count, int device, cudaStream_t stream);
+// One Net2Net-upscaled tensor: old values (x scale) inside [old_r, old_c),
+// seeded noise in [-0.005, 0.005] elsewhere.
+int launch_upscale_tensor(const float *old, int old_r, int old_c, float *out, int new_r, int new_c, double scale,
+                          uint64_t seed, uint64_t stream, int device, cudaStream_t st);
 
 // Bounded-wait self-test (forward.cu): a kernel whose mbarrier wait never
 // completes gives up after limit_ns and records an error in e.err_d; the id

@@ -210,6 +210,10 @@ class CortexGroup:
               "cortex_group_decode_steps")
         return ids
 
+    def average(self):
+        """Federated average of the engines' weights (cortex_group_average)."""
+        check(self.lib.cortex_group_average(self.h), "cortex_group_average")
+
     def close(self):
         if self.h:
             self.lib.cortex_group_free(self.h)
@@ -357,3 +361,29 @@ def run_inference(path, prompt_ids, uniforms, temperature=0.25, rep_penalty=1.15
         return out, "max"
     finally:
         eng.close()
+
+
+def merge_files(paths, out_path, device=0):
+    """src/net2net_forge.php merge_models / src/train_cluster.php
+    average_models_stream on the GPU (cortex_merge_files)."""
+    lib = load()
+    arr = (ctypes.c_char_p * len(paths))(*[str(p).encode() for p in paths])
+    check(lib.cortex_merge_files(arr, len(paths), str(out_path).encode(), int(device)), "cortex_merge_files")
+    return out_path
+
+
+def upscale_file(in_path, out_path, target_dim, seed=4321, device=0):
+    """src/net2net_forge.php upscale_model on the GPU (cortex_upscale_file)."""
+    lib = load()
+    check(lib.cortex_upscale_file(str(in_path).encode(), str(out_path).encode(), int(target_dim), int(seed),
+                                  int(device)), "cortex_upscale_file")
+    return out_path
+
+
+def average_states(engines):
+    """Federated average of the engines' weights in GPU memory
+    (cortex_average_states): Cortex objects or raw state pointers."""
+    lib = load()
+    hs = [e.h if hasattr(e, "h") else e for e in engines]
+    arr = (ctypes.c_void_p * len(hs))(*hs)
+    check(lib.cortex_average_states(arr, len(hs)), "cortex_average_states")

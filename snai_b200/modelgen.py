@@ -7,9 +7,9 @@ rms_final [d], and per layer rms_att [d], rms_ffn [d], Wq, Wk, Wv, Wo [d,d],
 W_up [ffn,d], W_down [d,ffn].
 
 `random_model` restates src/init_base.php:77-100 (layout, unit RMSNorm
-weights) with seeded N(0, std) weights instead of the unseeded uniform ones;
-`upscale_model` restates the upscale of src/net2net_forge.php:108-214 with a
-seeded noise generator.
+weights) with seeded N(0, std) weights instead of the unseeded uniform ones.
+Net2Net upscaling and merging are library calls (cortex_upscale_file,
+cortex_merge_files).
 """
 import os
 import struct
@@ -87,44 +87,3 @@ def read_model(path):
             n = int(np.prod(shape))
             out[name] = np.frombuffer(f.read(4 * n), dtype="<f4").reshape(shape).copy()
     return h, out
-
-
-NOISE_FACTOR = 0.005  # src/net2net_forge.php: NOISE_FACTOR
-
-
-def upscale_model(in_path, out_path, target_dim, seed=4321):
-    """src/net2net_forge.php:149-214.  dim -> target_dim, ffn -> 4*target_dim,
-    ctx x2, layers x2.  Old entries are copied (times 0.01 for Wo and W_down of
-    the new layers, which repeat layer l % old_layers); every new entry is
-    uniform noise in [-0.005, 0.005] (seeded here, mt_rand there)."""
-    h, t = read_model(in_path)
-    vocab, old_dim, old_ffn, old_ctx, old_layers = (h["vocab_size"], h["hidden_dim"], h["ffn_dim"], h["ctx_size"],
-                                                    h["num_layers"])
-    if target_dim <= old_dim:
-        raise ValueError("target_dim must be larger than the current dim")
-    new_dim, new_ffn, new_ctx, new_layers = target_dim, 4 * target_dim, old_ctx * 2, old_layers * 2
-    rng = np.random.default_rng(seed)
-
-    def grow(old, new_shape, scale=1.0):
-        # src/net2net_forge.php:108-147: row by row; old values * scale, noise elsewhere
-        out = ((rng.random(new_shape) * 2.0 - 1.0) * NOISE_FACTOR).astype(np.float32)
-        old2 = old.reshape(old.shape[0] if old.ndim == 2 else 1, -1)
-        r, c = old2.shape
-        dst = out.reshape(new_shape[0] if len(new_shape) == 2 else 1, -1)
-        dst[:r, :c] = (old2.astype(np.float64) * scale).astype(np.float32)
-        return out
-
-    with open(out_path, "wb") as f:
-        _write_header(f, vocab, new_dim, new_ffn, new_ctx, new_layers)
-        f.write(grow(t["embeddings"], (vocab, new_dim)).astype("<f4").tobytes())
-        f.write(grow(t["w_out"], (vocab, new_dim)).astype("<f4").tobytes())
-        f.write(grow(t["rms_final"], (new_dim,)).astype("<f4").tobytes())
-        for l in range(new_layers):
-            src = l % old_layers
-            out_scale = 0.01 if l >= old_layers else 1.0
-            for key, shape, scale in [("rms_att", (new_dim,), 1.0), ("rms_ffn", (new_dim,), 1.0),
-                                      ("w_q", (new_dim, new_dim), 1.0), ("w_k", (new_dim, new_dim), 1.0),
-                                      ("w_v", (new_dim, new_dim), 1.0), ("w_o", (new_dim, new_dim), out_scale),
-                                      ("w_up", (new_ffn, new_dim), 1.0), ("w_down", (new_dim, new_ffn), out_scale)]:
-                f.write(grow(t[f"{src}.{key}"], shape, scale).astype("<f4").tobytes())
-    return out_path

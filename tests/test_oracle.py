@@ -271,18 +271,3 @@ def test_file_format(model_dir, built, tmp_path):
     short = tmp_path / "short.snai"
     short.write_bytes(open(p, "rb").read()[:-4])
     assert not O.lib().oracle_load_stream(str(short).encode(), 1)
-
-
-def test_upscale_layout(model_dir, built, tmp_path):
-    src = make_model(model_dir, "up_src.snai", 50, 16, 8, 2, seed=9)
-    dst = str(tmp_path / "up.snai")
-    modelgen.upscale_model(src, dst, 32, seed=1)
-    h, t = modelgen.read_model(dst)
-    assert (h["hidden_dim"], h["ffn_dim"], h["ctx_size"], h["num_layers"]) == (32, 128, 16, 4)
-    assert os.path.getsize(dst) == modelgen.expected_size(50, 32, 128, 4)
-    _, s = modelgen.read_model(src)
-    assert np.array_equal(t["embeddings"][:, :16], s["embeddings"])
-    assert np.all(np.abs(t["embeddings"][:, 16:]) <= 0.005)
-    assert np.array_equal(t["2.w_q"][:16, :16], s["0.w_q"])  # new layer repeats layer 0
-    assert np.allclose(t["3.w_o"][:16, :16], (s["1.w_o"].astype(np.float64) * 0.01).astype(np.float32))
-    assert np.array_equal(t["1.w_down"][:16, :64], s["1.w_down"])
