@@ -665,6 +665,45 @@ def group_load_line(name, n, single_s):
         return {"error": f"{type(ex).__name__}: {ex}"}
 
 
+def tokenizer_bench(vocab_path, n_words=200000):
+    """Encode/decode throughput of the library's C++ tokenizer
+    (cortex_tokenizer_*) on seeded text (words of the vocabulary joined by
+    spaces and newlines), beside the oracle's Python restatement of
+    src/snai_tokenizer.php on a tenth of it.  Host code: no GPU involved."""
+    import ctypes
+
+    import oracle.tokenizer as OT
+    from snai_b200 import load
+    lib = load()
+    ot = OT.Tokenizer(vocab_path)
+    rng = np.random.default_rng(5)
+    words = [w.replace(OT.META, "") for w in ot.vocab if w.startswith(OT.META) and len(w) > 1][:4000] or ["abc"]
+    pick = rng.integers(0, len(words), n_words)
+    text = "".join(words[i] + ("\n" if k % 17 == 16 else " ") for k, i in enumerate(pick)).encode("utf-8")
+    h = lib.cortex_tokenizer_load(vocab_path.encode())
+    n = lib.cortex_tokenizer_encode(h, text, len(text), None, 0)  # warms the merge cache
+    ids = np.zeros(n, dtype=np.int32)
+    t0 = time.perf_counter()
+    lib.cortex_tokenizer_encode(h, text, len(text), ids.ctypes.data_as(ctypes.c_void_p), n)
+    enc_s = time.perf_counter() - t0
+    buf = ctypes.create_string_buffer(len(text) * 2 + 16)
+    t0 = time.perf_counter()
+    lib.cortex_tokenizer_decode(h, ids.ctypes.data_as(ctypes.c_void_p), n, 0, buf, len(buf))
+    dec_s = time.perf_counter() - t0
+    lib.cortex_tokenizer_free(h)
+    sub_text = text[:len(text) // 10].decode("utf-8", errors="ignore")
+    ot.encode(sub_text)
+    t0 = time.perf_counter()
+    py_ids = ot.encode(sub_text)
+    py_s = time.perf_counter() - t0
+    return {"metric": "tokenizer encode MB/s (host)", "value": len(text) / enc_s / 1e6, "unit": "MB/s",
+            "tokens_per_s": n / enc_s, "decode_tokens_per_s": n / dec_s, "bytes": len(text), "tokens": n,
+            "cpu_baseline": {"value": len(sub_text.encode()) / py_s / 1e6, "unit": "MB/s", "cores": 1, "kind": "port",
+                             "sample": f"oracle/tokenizer.py (Python restatement of the PHP encode) on "
+                                       f"{len(py_ids)} tokens"},
+            "vocab": os.path.basename(vocab_path)}
+
+
 def gemm_bench(args):
     """Projection micro-benchmark: the d=1024 decode step's GEMM shapes
     (`--seqs` rows; qkv N=3072, wo N=1024, up N=4096, down N=1024 with
@@ -793,6 +832,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the c3/c2/sampling/GEMV extra keys")
     ap.add_argument("--sampler", action="store_true", help="only the isolated sampling workload, one line each")
     ap.add_argument("--gemm", action="store_true", help="only the projection micro-benchmark")
+    ap.add_argument("--tokenizer", metavar="VOCAB_JSON", help="only the tokenizer throughput (host code)")
     ap.add_argument("--seqs", type=int, default=None,
                     help="total sequences of the decode configuration (default: the configuration's), or rows of "
                          "the projection micro-benchmark (default 4096)")
@@ -806,6 +846,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return
+    if args.tokenizer:
+        print(json.dumps(tokenizer_bench(args.tokenizer)), flush=True)
         return
     if args.gemm:
         if args.seqs is None:

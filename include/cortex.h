@@ -303,6 +303,29 @@ CORTEX_API int cortex_average_states(void *const *states, int n);
 /* cortex_average_states over a group's engines. */
 CORTEX_API int cortex_group_average(void *group);
 
+/* ------------------------------------------------------------------------ */
+/* The reference's BPE tokenizer (src/snai_tokenizer.php) as library calls. */
+/* ------------------------------------------------------------------------ */
+
+/* src/snai_tokenizer.php:23-38: loads the HF-style vocabulary JSON
+ * (model.vocab, model.merges; e.g. lib/symbio_vocab.json).  NULL on failure.
+ * A tokenizer may be shared by threads (its merge cache is locked). */
+CORTEX_API void *cortex_tokenizer_load(const char *vocab_json);
+CORTEX_API void cortex_tokenizer_free(void *tok);
+/* src/snai_tokenizer.php:41-43 getVocabSize. */
+CORTEX_API int cortex_tokenizer_vocab_size(void *tok);
+/* src/snai_tokenizer.php:118-185 encode of text_len bytes (strlen when
+ * text_len < 0): invalid UTF-8 -> '?', a leading ' ' unless the text starts
+ * with ' ', '[' or '<', the special tokens split out, BPE per U+2581 chunk,
+ * unknown pieces -> <unk>.  No NFKC (the PHP code applies it only when its
+ * intl extension is loaded).  Writes up to max_ids ids and returns how many
+ * the text has (negative on error). */
+CORTEX_API int cortex_tokenizer_encode(void *tok, const char *text, int text_len, int *ids, int max_ids);
+/* src/snai_tokenizer.php:187-199 decode: the ids' strings (unknown ids
+ * skipped), U+2581 -> ' ', trimmed when trim != 0.  Writes at most
+ * max_bytes - 1 bytes and a NUL; returns the full length in bytes. */
+CORTEX_API int cortex_tokenizer_decode(void *tok, const int *ids, int n, int trim, char *out, int max_bytes);
+
 /* Self-test of the failure path every kernel wait takes.  No counterpart in
  * the reference (whose engine has no device waits).  Queues one kernel on
  * the state's stream that waits on an mbarrier nothing completes; the wait

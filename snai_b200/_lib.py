@@ -85,6 +85,11 @@ SIGNATURES = {
     "cortex_upscale_file": (c_int, [c_char_p, c_char_p, c_int, ctypes.c_ulonglong, c_int]),
     "cortex_average_states": (c_int, [ctypes.POINTER(c_void_p), c_int]),
     "cortex_group_average": (c_int, [c_void_p]),
+    "cortex_tokenizer_load": (c_void_p, [c_char_p]),
+    "cortex_tokenizer_free": (None, [c_void_p]),
+    "cortex_tokenizer_vocab_size": (c_int, [c_void_p]),
+    "cortex_tokenizer_encode": (c_int, [c_void_p, c_char_p, c_int, c_void_p, c_int]),
+    "cortex_tokenizer_decode": (c_int, [c_void_p, c_void_p, c_int, c_int, c_char_p, c_int]),
     "cortex_selftest_wait_timeout": (c_int, [c_void_p, ctypes.c_longlong]),
     "cortex_kernel_launches": (ctypes.c_longlong, [c_void_p]),
 }

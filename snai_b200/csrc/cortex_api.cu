@@ -123,6 +123,7 @@ void free_engine(Engine *e) {
   if (e->graph.exec) cudaGraphExecDestroy(e->graph.exec);
   cudaFree(e->unif_all);
   cudaFree(e->ids_all);
+  cudaFree(e->avg_tmp);
   if (e->own_stream) cudaStreamDestroy(e->own_stream);
   delete e;
 }
@@ -1653,19 +1654,32 @@ int average_engines(Engine *const *es, int n) {
       cudaGetLastError();
     }
   }
-  std::vector<DevBuf> part(n);
+  std::vector<float *> part(n);
   std::vector<size_t> a0(n), cnt(n);
-  for (int i = 0; i < n; ++i) {
-    a0[i] = E * i / n;
-    cnt[i] = E * (i + 1) / n - a0[i];
+  for (int i = 0; i <= n; ++i) {  // shard boundaries on 64-float (256-byte) multiples
+    const size_t b = i == n ? E : E * i / n / 64 * 64;
+    if (i < n) a0[i] = b;
+    if (i > 0) cnt[i - 1] = b - a0[i - 1];
   }
   MergeSources srcs;
   srcs.n = n;
   for (int i = 0; i < n; ++i) {
     DeviceGuard g(es[i]->device);
     for (int j = 0; j < n; ++j) srcs.src[j] = static_cast<const float *>(es[j]->wblock) + a0[i];
-    if (cudaMalloc(&part[i].p, std::max<size_t>(cnt[i], 1) * 4) != cudaSuccess ||
-        launch_merge_mean(srcs, static_cast<float *>(part[i].p), cnt[i], es[i]->device, es[i]->stream) != 0) {
+    Engine &e = *es[i];
+    const size_t need = std::max<size_t>(cnt[i], 1) * 4;
+    if (e.avg_tmp_bytes < need) {  // a shard buffer per engine, kept for later averages
+      cudaFree(e.avg_tmp);
+      e.avg_tmp = nullptr;
+      e.avg_tmp_bytes = 0;
+      if (cudaMalloc(&e.avg_tmp, need) != cudaSuccess) {
+        set_error("average buffer on device %d: %s", e.device, cudaGetErrorString(cudaGetLastError()));
+        return -3;
+      }
+      e.avg_tmp_bytes = need;
+    }
+    part[i] = static_cast<float *>(e.avg_tmp);
+    if (launch_merge_mean(srcs, part[i], cnt[i], es[i]->device, es[i]->stream) != 0) {
       set_error("average on device %d failed: %s", es[i]->device, cudaGetErrorString(cudaGetLastError()));
       return -4;
     }
@@ -1680,7 +1694,7 @@ int average_engines(Engine *const *es, int n) {
   for (int i = 0; i < n; ++i) {
     DeviceGuard g(es[i]->device);
     for (int j = 0; j < n; ++j)
-      if (cudaMemcpyPeerAsync(static_cast<float *>(es[i]->wblock) + a0[j], es[i]->device, part[j].p, es[j]->device,
+      if (cudaMemcpyPeerAsync(static_cast<float *>(es[i]->wblock) + a0[j], es[i]->device, part[j], es[j]->device,
                               cnt[j] * 4, es[i]->stream) != cudaSuccess) {
         set_error("shard copy %d -> %d failed: %s", es[j]->device, es[i]->device,
                   cudaGetErrorString(cudaGetLastError()));

@@ -102,6 +102,8 @@ struct Engine {
   // weights (fp32 masters; bf16 copies in BF16 mode)
   void *wblock = nullptr;
   size_t wblock_bytes = 0;
+  void *avg_tmp = nullptr;  // this engine's shard of a cross-engine average (kept for the next one)
+  size_t avg_tmp_bytes = 0;
   void *hblock = nullptr;
   float *emb = nullptr, *w_out = nullptr, *rms_final = nullptr;
   __nv_bfloat16 *w_out_h = nullptr;

@@ -26,9 +26,27 @@ namespace snai {
 // Element-wise mean of n arrays (n <= kMergeMaxSources): out[j] =
 // fp32((sum_i double(src_i[j])) / n), summed in source order.  Sources may be
 // another GPU's memory (peer loads over NVLink).
-__global__ void merge_mean_kernel(const MergeSources srcs, float *__restrict__ out, size_t count) {
+__global__ void merge_mean_kernel(const MergeSources srcs, float *__restrict__ out, size_t count, bool vec) {
   const double n = (double)srcs.n;
-  for (size_t j = blockIdx.x * (size_t)blockDim.x + threadIdx.x; j < count; j += (size_t)gridDim.x * blockDim.x) {
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
+  size_t done = 0;
+  if (vec) {  // 16-byte aligned sources and output: four floats per load
+    const size_t n4 = count / 4;
+    for (size_t j = tid; j < n4; j += stride) {
+      double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+      for (int i = 0; i < srcs.n; ++i) {
+        const float4 v = __ldcs(reinterpret_cast<const float4 *>(srcs.src[i]) + j);
+        s0 += (double)v.x;
+        s1 += (double)v.y;
+        s2 += (double)v.z;
+        s3 += (double)v.w;
+      }
+      reinterpret_cast<float4 *>(out)[j] = make_float4((float)(s0 / n), (float)(s1 / n), (float)(s2 / n),
+                                                       (float)(s3 / n));
+    }
+    done = n4 * 4;
+  }
+  for (size_t j = done + tid; j < count; j += stride) {
     double s = 0.0;
     for (int i = 0; i < srcs.n; ++i) s += (double)__ldcs(srcs.src[i] + j);
     out[j] = (float)(s / n);
@@ -37,7 +55,9 @@ __global__ void merge_mean_kernel(const MergeSources srcs, float *__restrict__ o
 
 int launch_merge_mean(const MergeSources &srcs, float *out, size_t count, int device, cudaStream_t stream) {
   if (count == 0) return 0;
-  merge_mean_kernel<<<4 * device_sm_count(device), 256, 0, stream>>>(srcs, out, count);
+  bool vec = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  for (int i = 0; i < srcs.n; ++i) vec = vec && (reinterpret_cast<uintptr_t>(srcs.src[i]) & 15) == 0;
+  merge_mean_kernel<<<4 * device_sm_count(device), 256, 0, stream>>>(srcs, out, count, vec);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
