@@ -28,7 +28,7 @@ def _worker(rank, world, port, path, prompts, U, out_dir):
     import torch.distributed as dist
 
     import oracle as O
-    from snai_b200.shard import gather_ids, max_over_ranks, shard_range
+    from snai_b200.shard import gather_ids, gather_ids_host, max_over_ranks, shard_range
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -38,8 +38,11 @@ def _worker(rank, world, port, path, prompts, U, out_dir):
     ids, _, secs = o.generate(prompts[a:b], U.shape[1], U[a:b], 1, 0.7, 1.1, 40, 0.9, nthreads=2)
     # rows of ids in sequence order: shard (a, b) of sequences = elements (a*steps, b*steps)
     flat = gather_ids(ids.ravel(), len(prompts) * U.shape[1])
+    at0 = gather_ids_host(ids.ravel(), len(prompts) * U.shape[1])
+    assert (at0 is None) == (rank != 0)
     m = max_over_ranks(secs if rank == 0 else secs + 1000.0)
     if rank == 0:
+        assert np.array_equal(at0.numpy(), flat.numpy())
         np.save(os.path.join(out_dir, "ids.npy"), flat.numpy())
         np.save(os.path.join(out_dir, "max.npy"), np.array([m]))
     dist.barrier()
