@@ -18,6 +18,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <climits>
 #include <atomic>
 #include <cstdio>
 #include <cstring>
@@ -838,9 +839,29 @@ static int launch_tc2(Engine &e, int M, int N, int K, const void *A, const void 
 
 template <typename TIn, class Epi>
 static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
-  if (M >= 256 && N >= 256) return launch_tc2<TIn>(e, M, N, K, A, W, epi);
-  if (N >= 2048) return launch_tcp<TIn, 256>(e, M, N, K, A, W, epi);
-  return launch_tcp<TIn, 128>(e, M, N, K, A, W, epi);
+  // Tile shape by a per-CTA cost model: a CTA streams (rows of A + rows of W)
+  // per k-block for every tile it owns, so the cost is (tiles per CTA) x
+  // (128 + BN), with the CTA pair's 256 x 256 tile at 128 + 128 per CTA.
+  // Large M keeps the pair tiles; few rows (one GPU's share of the
+  // sequences, small batches) take narrower single-CTA tiles on more SMs.
+  // Every shape gives a row the same bits (same K order, one accumulator).
+  const int sms = sm_count(e.device);
+  auto waves = [](long long tiles, long long slots) { return (tiles + slots - 1) / slots; };
+  const long long mt = (M + kTcBM - 1) / kTcBM;
+  long long best = (M >= 256 && N >= 256) ? waves((long long)((M + 255) / 256) * ((N + 255) / 256), sms / 2) * 256
+                                          : LLONG_MAX;
+  int pick = 0;  // 0 pair, else BN
+  for (int bn : {256, 128, 64}) {
+    const long long c = waves(mt * ((N + bn - 1) / bn), sms) * (128 + bn);
+    if (c < best) {
+      best = c;
+      pick = bn;
+    }
+  }
+  if (pick == 0) return launch_tc2<TIn>(e, M, N, K, A, W, epi);
+  if (pick == 256) return launch_tcp<TIn, 256>(e, M, N, K, A, W, epi);
+  if (pick == 128) return launch_tcp<TIn, 128>(e, M, N, K, A, W, epi);
+  return launch_tcp<TIn, 64>(e, M, N, K, A, W, epi);
 }
 
 // Launches kern on the engine's stream; with pdl as a programmatic dependent

@@ -4,17 +4,19 @@ The decode benchmark's two models (seeded SNAI_V4, V=16384, ctx 1024,
 L=2): d=1024 with 16 heads and d=512 with 8 heads.  Four distinct
 sequences get a 960-token prompt, so attention reads up to 964 cached
 positions, then three teacher-forced decode steps; each sequence is
-replicated over 256 slots, so every projection of a decode step runs as a
-256-row CTA-pair tensor-core GEMM: QKV (N=3D), Wo (N=D), W_up (N=4D),
-W_down (N=D, K=4D) and the logits GEMM (N=16384).  The prompt runs as
-1024-row chunks through the same GEMMs.  Checked against the oracle
-(the CPU restatement of core/cortex.nim:487-563, teacher-forced on the
-same tokens):
+replicated over 2048 slots, so a decode step's projections run at 2048 rows
+(one GPU's share of the benchmark at N=2: the CTA-pair tensor-core GEMM for
+QKV (N=3D), W_up (N=4D), W_down (N=D, K=4D) and the logits (N=16384), the
+128 x 64 single-CTA tiles for Wo), and the prompts as 1024-row chunks.
+Checked against the oracle (the CPU restatement of core/cortex.nim:487-563,
+teacher-forced on the same tokens):
 
 * logits after the prompt and after every forced token, per precision,
   max |gpu - oracle| / max |oracle| within the stated tolerance;
-* the replicas of a sequence get bit-identical logits (a row's result does
-  not depend on the other rows of the pass);
+* the replicas of a sequence get bit-identical logits, and a second engine
+  with one slot per sequence (passes of 4 rows: single-CTA tiles
+  throughout) gets the same bits (a row's result does not depend on the
+  other rows of the pass or on the tile shape);
 * one more step through the fused decode (cortex_decode_batch: sample, then
   feed) gives, row by row, exactly the id the oracle's sampler picks from
   the GPU's logits with the same history and uniform
@@ -48,7 +50,7 @@ CASES = {
     "d1024": dict(V=16384, D=1024, L=2, heads=16, ctx=1024),
     "d512": dict(V=16384, D=512, L=2, heads=8, ctx=1024),
 }
-S, P, T, R = 4, 960, 3, 256  # sequences, prompt length, forced steps, slots
+S, P, T, R = 4, 960, 3, 2048  # sequences, prompt length, forced steps, slots
 
 
 @functools.lru_cache(maxsize=None)
@@ -86,15 +88,21 @@ def test_bench_shapes_logits_and_ids(case, prec, model_dir, built):
         assert err < TOL[prec], (s, err)
     print(f"{case} prec {prec}: max rel err per step {errs}")
     assert e.pos(0) == P + T
+    small = Cortex(path, num_heads=c["heads"], max_seqs=S, precision=prec)
+    mine = [small.forward(prompts)] + [small.forward(forced[:, s:s + 1]) for s in range(T)]
+    for s in range(T + 1):
+        assert np.array_equal(mine[s], got[s][:S]), s
+    small.close()
     # one decode step through the fused path: ids vs the oracle sampler on the GPU logits
     lg = e.logits(np.arange(R))
     rng = np.random.default_rng(5 + prec)
     U = rng.random(S).astype(np.float32)[seq]
     ids = e.decode(U, sample_params(VARIANT_B, 0.7, 1.1, 40, 0.9))
-    for r in range(R):
-        hist = list(prompts[seq[r]]) + list(forced[seq[r]])
+    for r in range(S):  # the replicas share logits, history and uniform, so their ids too
+        hist = list(prompts[r]) + list(forced[r])
         want = O.sample_b(lg[r], hist, 0.7, 40, 0.9, 1.1, U[r])
         assert ids[r] == want, (r, ids[r], want)
+        assert (ids[seq == r] == want).all(), r
     e.close()
 
 
