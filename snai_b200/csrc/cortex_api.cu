@@ -103,10 +103,13 @@ bool make_dims(int vocab, int dim, int ctx, int layers, int heads, Dims *d) {
     set_error("num_heads %d gives head size %d: %d heads x %d > hidden_dim %d", heads, hs, d->heads, hs, dim);
     return false;
   }
-  // attention keeps a score per position and two rotated head vectors in shared memory
-  if (((size_t)ctx + 2 * (size_t)hs) * sizeof(float) + 2048 > 200 * 1024) {
+  // attention keeps, in shared memory, a 68-float partial per 64 positions
+  // (head size 64) or a score per position and two head vectors (others)
+  const size_t att_smem = hs == 64 ? ((size_t)(ctx + 63) / 64 + 8) * 68 * sizeof(float)
+                                   : ((size_t)ctx + 2 * (size_t)hs) * sizeof(float) + 2048;
+  if (att_smem > 200 * 1024) {
     set_error("ctx_size %d with head size %d exceeds this engine's attention limit (%d positions)", ctx, hs,
-              (200 * 1024 - 2048) / 4 - 2 * hs);
+              hs == 64 ? (200 * 1024 / (68 * 4) - 8) * 64 : (200 * 1024 - 2048) / 4 - 2 * hs);
     return false;
   }
   return true;
@@ -194,7 +197,8 @@ Engine *create_engine(const Dims &d, int max_seqs, int device, int precision) {
   a.add(&e->att, M * D * sizeof(float));
   a.add(&e->u, M * F * sizeof(float));
   a.add(&e->xo, M * D * sizeof(float));
-  a.add(&e->att_part, (size_t)640 * (d.hs + 2));
+  e->att_part_entries = (size_t)device_sm_count(device) * std::min((d.ctx + 63) / 64, 128);
+  a.add(&e->att_part, e->att_part_entries * 68);
   a.add(&e->att_cnt, 256);
   a.add(&e->logits, (size_t)max_seqs * V);
   a.add(&e->hist, (size_t)max_seqs * d.ctx);

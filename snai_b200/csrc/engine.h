@@ -129,8 +129,9 @@ struct Engine {
   void *att = nullptr;        // [m_max, D]
   void *u = nullptr;          // [m_max, F]
   void *xo = nullptr;         // [m_max, D] normed rows that need logits
-  float *att_part = nullptr;  // split-position attention: partial results [640][hs + 2]
-  int *att_cnt = nullptr;     // split-position attention: arrival counters [256], zero between launches
+  float *att_part = nullptr;    // split attention: chunk partials [att_part_entries][68]
+  size_t att_part_entries = 0;  // SMs x min(ceil(ctx / 64), 128)
+  int *att_cnt = nullptr;       // split attention: arrival counters [256], zero between launches
   float *logits = nullptr;    // [max_seqs, V], per slot
   int *hist = nullptr;        // [max_seqs, ctx] every token fed to the slot
   int *seq_len_d = nullptr;   // [max_seqs] tokens fed (device copy of pos)

@@ -209,269 +209,226 @@ __device__ __forceinline__ float4 rope4(float4 v, float4 c) {
                      __fadd_rn(__fmul_rn(v.z, c.w), __fmul_rn(v.w, c.z)));
 }
 
-// kvs non-null: K and V of position pos come from the row's staging entry
-// ([M, 2, att_ch], without RoPE, as q) and are appended to the cache here,
-// where the slot's cache pages are being read anyway (one row per slot in
-// the pass); RoPE of q and k is applied here then.
+// ---- attention, head size 64: one canonical formula for every kernel ----
+//
+// The positions 0..n-1 of a (row, head) are cut into chunks of 64 (4 warps x
+// 8 position pairs).  Warp w of a chunk loads the K and V rows of its 8 pairs
+// at once (a warp reads two 256-byte rows per instruction, so every load is a
+// contiguous 512-byte span of the head-major cache) and computes
+//   m_w = max(-9999, s_t) (the reference's initialisation, core/cortex.nim:517),
+//   l_w = sum exp(s_t - m_w),  o_w = sum exp(s_t - m_w) v_t   (t in pair order),
+// s_t = (q . k_t) / sqrtf(hs).  A chunk's four warps combine in warp order:
+//   M_c = max_w m_w,  L_c = sum_w exp(m_w - M_c) l_w,  O_c = sum_w exp(m_w - M_c) o_w,
+// and the chunks in chunk order:
+//   M = max(-9999, M_c),  att = (sum_c exp(M_c - M) O_c) / (sum_c exp(M_c - M) L_c).
+// The whole-row kernel (a CTA per (row, head), chunks in a loop) and the
+// split kernel (a CTA per chunk, for passes of few rows) run exactly these
+// operations, so a row's attention has the same bits whichever kernel runs
+// it, whatever else is in its pass.  Channels >= heads*hs of att are zero
+// (:512-513).
+//
+// kvs non-null (a decode pass, one row per slot): K and V of position pos
+// come from the row's staging entry ([M, 2, att_ch], without RoPE, as q) and
+// are appended to the cache here, where the slot's cache pages are read
+// anyway; RoPE of q and k is applied here then.
+constexpr int kAttChunk = 64;  // positions per chunk
+constexpr int kAttPW = 68;     // floats per partial: max, sum, (pad), 64 weighted value sums from [4]
+constexpr int kSplitCounters = 256;  // (row, head) arrival counters of the split kernel
+constexpr int kSplitMax = 128;       // chunks (= CTAs) per (row, head) in the split kernel: ctx <= 8192
+
+struct AttRow {
+  float *kbase, *vbase;
+  float4 qv, knew, vnew;
+  int n, nc;  // positions, and positions below nc read from the cache
+};
+
+// The row's q (rotated in a decode pass), its cache pointers and the staged
+// K/V of position pos.  `append` writes the staged row to the cache (one
+// warp of one CTA per (row, head)).
+__device__ __forceinline__ AttRow att_row(const RowDesc &rd, const float *__restrict__ q, float *__restrict__ kv,
+                                          int m, int head, int att_ch, size_t slot_stride, size_t layer_off,
+                                          size_t part_stride, size_t head_stride, const float *__restrict__ kvs,
+                                          const float2 *__restrict__ rope, bool append) {
+  constexpr int HS = 64;
+  const int lane = threadIdx.x & 31, half = lane >> 4, pi = lane & 15;
+  AttRow r;
+  r.n = rd.pos + 1;
+  r.nc = kvs ? r.n - 1 : r.n;
+  r.kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
+  r.vbase = r.kbase + part_stride;
+  r.qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + pi * 4);
+  r.knew = make_float4(0.f, 0.f, 0.f, 0.f);
+  r.vnew = r.knew;
+  if (kvs) {
+    const float *kst = kvs + (size_t)m * 2 * att_ch + head * HS;
+    const float4 cs = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + pi * 2);
+    r.qv = rope4(r.qv, cs);
+    r.knew = rope4(*reinterpret_cast<const float4 *>(kst + pi * 4), cs);
+    r.vnew = *reinterpret_cast<const float4 *>(kst + att_ch + pi * 4);
+    if (append)  // lanes 0..15 the K row, lanes 16..31 the V row
+      *reinterpret_cast<float4 *>((half ? r.vbase : r.kbase) + (size_t)rd.pos * HS + pi * 4) = half ? r.vnew : r.knew;
+  }
+  return r;
+}
+
+// This warp's (m_w, l_w, o_w) of the chunk starting at t0 into wp (kAttPW floats).
+__device__ __forceinline__ void att_warp_chunk(const AttRow &r, int t0, float sqrt_hs, float *wp) {
+  constexpr int HS = 64, U = 8;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane >> 4, pi = lane & 15;
+  const int t1 = min(r.n, t0 + kAttChunk);
+  float4 kr[U], vr[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int t = t0 + 2 * (warp * U + u) + half;
+    const bool cached = t < min(r.nc, t1);
+    kr[u] = cached ? __ldcs(reinterpret_cast<const float4 *>(r.kbase + (size_t)t * HS + pi * 4))
+            : t < t1 ? r.knew
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    vr[u] = cached ? __ldcs(reinterpret_cast<const float4 *>(r.vbase + (size_t)t * HS + pi * 4))
+            : t < t1 ? r.vnew
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float sc[U];
+  float mx = -9999.0f;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    float d = r.qv.x * kr[u].x + r.qv.y * kr[u].y + r.qv.z * kr[u].z + r.qv.w * kr[u].w;
+    d += __shfl_xor_sync(0xffffffffu, d, 8);
+    d += __shfl_xor_sync(0xffffffffu, d, 4);
+    d += __shfl_xor_sync(0xffffffffu, d, 2);
+    d += __shfl_xor_sync(0xffffffffu, d, 1);
+    sc[u] = __fdiv_rn(d, sqrt_hs);
+    if (t0 + 2 * (warp * U + u) + half < t1) mx = fmaxf(mx, sc[u]);
+  }
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+  float ls = 0.f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if (t0 + 2 * (warp * U + u) + half < t1) {
+      const float e = expf(__fsub_rn(sc[u], mx));
+      ls = __fadd_rn(ls, e);
+      o.x = __fadd_rn(o.x, __fmul_rn(vr[u].x, e));
+      o.y = __fadd_rn(o.y, __fmul_rn(vr[u].y, e));
+      o.z = __fadd_rn(o.z, __fmul_rn(vr[u].z, e));
+      o.w = __fadd_rn(o.w, __fmul_rn(vr[u].w, e));
+    }
+  }
+  ls = __fadd_rn(ls, __shfl_xor_sync(0xffffffffu, ls, 16));
+  o.x = __fadd_rn(o.x, __shfl_xor_sync(0xffffffffu, o.x, 16));
+  o.y = __fadd_rn(o.y, __shfl_xor_sync(0xffffffffu, o.y, 16));
+  o.z = __fadd_rn(o.z, __shfl_xor_sync(0xffffffffu, o.z, 16));
+  o.w = __fadd_rn(o.w, __shfl_xor_sync(0xffffffffu, o.w, 16));
+  if (lane < 16) *reinterpret_cast<float4 *>(wp + 4 + 4 * pi) = o;
+  if (lane == 0) {
+    wp[0] = mx;
+    wp[1] = ls;
+  }
+}
+
+// Channel ch (< 64) of a chunk's partial from its four warps' (warp order).
+__device__ __forceinline__ void att_chunk_combine(const float *wp4, int ch, float *dst) {
+  float M = wp4[0];
+#pragma unroll
+  for (int w = 1; w < 4; ++w) M = fmaxf(M, wp4[w * kAttPW]);
+  float L = 0.f, O = 0.f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float s = expf(__fsub_rn(wp4[w * kAttPW], M));
+    L = __fadd_rn(L, __fmul_rn(s, wp4[w * kAttPW + 1]));
+    O = __fadd_rn(O, __fmul_rn(s, wp4[w * kAttPW + 4 + ch]));
+  }
+  dst[4 + ch] = O;
+  if (ch == 0) {
+    dst[0] = M;
+    dst[1] = L;
+  }
+}
+
+// Channel ch of att from C chunk partials (chunk order); LD reads a float.
+template <class LD>
+__device__ __forceinline__ float att_merge(const float *cp, int C, int ch, LD ld) {
+  float M = -9999.0f;
+  for (int c = 0; c < C; ++c) M = fmaxf(M, ld(cp + c * kAttPW));
+  float L = 0.f, O = 0.f;
+  for (int c = 0; c < C; ++c) {
+    const float s = expf(__fsub_rn(ld(cp + c * kAttPW), M));
+    L = __fadd_rn(L, __fmul_rn(s, ld(cp + c * kAttPW + 1)));
+    O = __fadd_rn(O, __fmul_rn(s, ld(cp + c * kAttPW + 4 + ch)));
+  }
+  return __fdiv_rn(O, L);
+}
+
+// Whole-row kernel: a CTA per (row, head), its chunks in a loop (warp
+// partials double-buffered, one barrier per chunk), chunk partials in shared
+// memory, then the merge.
 template <typename TA>
 __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
     const RowDesc *__restrict__ rows, const float *__restrict__ q, float *__restrict__ kv, TA *__restrict__ out,
     int D, int att_ch, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride, float sqrt_hs,
     const float *__restrict__ kvs, const float2 *__restrict__ rope) {
   constexpr int HS = 64;
-  extern __shared__ float smem_att[];
-  float *red = smem_att;        // [32]
-  float *acc = smem_att + 32;   // [4 warps][64]
-  float *s = smem_att + 32 + 4 * HS;
+  extern __shared__ __align__(16) float smem_att[];
+  float *wpart = smem_att;                  // [2][4 warps][kAttPW]
+  float *cpart = smem_att + 2 * 4 * kAttPW;  // [chunks][kAttPW]
   grid_dep_wait();
   grid_dep_launch();
-  const int m = blockIdx.y, head = blockIdx.x;
+  const int m = blockIdx.y, head = blockIdx.x, warp = threadIdx.x >> 5;
   const RowDesc rd = rows[m];
-  const int n = rd.pos + 1;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int half = lane >> 4, part = lane & 15;
-
-  float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
-  float *vbase = kbase + part_stride;
-  float4 qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + part * 4);
-  // cache positions below nc; position pos from the staging entry when deferred
-  const int nc = kvs ? n - 1 : n;
-  const float *kst = kvs ? kvs + (size_t)m * 2 * att_ch + head * HS : nullptr;
-  const float *vst = kvs ? kst + att_ch : nullptr;
-  float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
-  if (kvs) {
-    const float4 cs = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + part * 2);
-    qv = rope4(qv, cs);
-    knew = rope4(*reinterpret_cast<const float4 *>(kst + part * 4), cs);
-    vnew = *reinterpret_cast<const float4 *>(vst + part * 4);
-    if (warp == 0)  // append: lanes 0..15 the K row, lanes 16..31 the V row
-      *reinterpret_cast<float4 *>((half ? vbase : kbase) + (size_t)rd.pos * HS + part * 4) = half ? vnew : knew;
+  const AttRow r = att_row(rd, q, kv, m, head, att_ch, slot_stride, layer_off, part_stride, head_stride, kvs, rope,
+                           warp == 0);
+  const int C = (r.n + kAttChunk - 1) / kAttChunk;
+  for (int c = 0; c < C; ++c) {
+    float *wp4 = wpart + (c & 1) * 4 * kAttPW;
+    att_warp_chunk(r, c * kAttChunk, sqrt_hs, wp4 + warp * kAttPW);
+    __syncthreads();
+    if (threadIdx.x < HS) att_chunk_combine(wp4, threadIdx.x, cpart + c * kAttPW);
   }
-
-  // ---- scores: warp w takes position pairs w, w+4, ...; 8 pairs per sweep ----
-  constexpr int U = 8;
-  for (int p0 = warp * U; 2 * p0 < n; p0 += 4 * U) {
-    float4 kr[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int t = 2 * (p0 + u) + half;
-      kr[u] = t < nc   ? __ldcs(reinterpret_cast<const float4 *>(kbase + (size_t)t * HS + part * 4))
-              : t < n ? knew
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      float d = qv.x * kr[u].x + qv.y * kr[u].y + qv.z * kr[u].z + qv.w * kr[u].w;
-      d += __shfl_xor_sync(0xffffffffu, d, 8);
-      d += __shfl_xor_sync(0xffffffffu, d, 4);
-      d += __shfl_xor_sync(0xffffffffu, d, 2);
-      d += __shfl_xor_sync(0xffffffffu, d, 1);
-      const int t = 2 * (p0 + u) + half;
-      if (part == 0 && t < n) s[t] = __fdiv_rn(d, sqrt_hs);
-    }
-  }
-  __syncthreads();
-  att_softmax(s, n, red);
-
-  // ---- weighted sum of values ----
-  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int p0 = warp * U; 2 * p0 < n; p0 += 4 * U) {
-    float4 vr[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int t = 2 * (p0 + u) + half;
-      vr[u] = t < nc   ? __ldcs(reinterpret_cast<const float4 *>(vbase + (size_t)t * HS + part * 4))
-              : t < n ? vnew
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int t = 2 * (p0 + u) + half;
-      const float wt = t < n ? s[t] : 0.f;
-      a.x = __fadd_rn(a.x, __fmul_rn(vr[u].x, wt));
-      a.y = __fadd_rn(a.y, __fmul_rn(vr[u].y, wt));
-      a.z = __fadd_rn(a.z, __fmul_rn(vr[u].z, wt));
-      a.w = __fadd_rn(a.w, __fmul_rn(vr[u].w, wt));
-    }
-  }
-  a.x += __shfl_xor_sync(0xffffffffu, a.x, 16);
-  a.y += __shfl_xor_sync(0xffffffffu, a.y, 16);
-  a.z += __shfl_xor_sync(0xffffffffu, a.z, 16);
-  a.w += __shfl_xor_sync(0xffffffffu, a.w, 16);
-  if (half == 0) *reinterpret_cast<float4 *>(acc + warp * HS + part * 4) = a;
   __syncthreads();
   TA *orow = out + (size_t)m * D;
-  if (threadIdx.x < HS) {
-    const float r = acc[threadIdx.x] + acc[HS + threadIdx.x] + acc[2 * HS + threadIdx.x] + acc[3 * HS + threadIdx.x];
-    ActIO<TA>::store(orow + head * HS + threadIdx.x, r);
-  }
+  if (threadIdx.x < HS)
+    ActIO<TA>::store(orow + head * HS + threadIdx.x, att_merge(cpart, C, threadIdx.x, [](const float *p) { return *p; }));
   if (head == gridDim.x - 1) att_zero_tail(orow, att_ch, D);
 }
 
-// Split-position decode attention for passes of few rows (rows x heads below
-// the SM count, e.g. the one-row decode pass of the PHP host).  CTA
-// (head, row, c) of S covers positions [c*chunk, min(n, (c+1)*chunk)), chunk =
-// ceil(n / S) rounded up to even (S is fixed per launch, the positions come
-// from the row descriptors, so a captured launch serves every later step).
-// Each warp takes position pairs in sweeps of U pairs: it loads the K and V
-// rows of a sweep together (all loads in flight at once), keeps a running
-// max starting at -9999 (the reference's initialisation,
-// core/cortex.nim:517), the sum of exp(s_t - max) and the exp-weighted
-// value sum, rescaling both when the max rises.  The four warps' results are
-// merged into the CTA's (m_c, l_c, o_c), written to part[row][head][c]; the
-// last CTA of a (row, head) to finish (an arrival counter, reset by it for
-// the next launch) merges the S results in split order: M = max m_c,
-// w_c = exp(m_c - M), att = sum w_c o_c / sum w_c l_c.  In decode passes (kvs
-// non-null) every CTA rotates q and the CTA holding position pos appends the
-// new K/V row.
-constexpr int kSplitPartEntries = 640;  // (row, head, split) partial results
-constexpr int kSplitCounters = 256;     // (row, head) arrival counters
-constexpr int kSplitMax = 128;          // splits per (row, head)
-
+// Split kernel for passes of few rows (rows x heads below the SM count, e.g.
+// the one-row decode pass of the PHP host): CTA (head, row, c) computes chunk
+// c (when the row has it) into part[row][head][c]; the last CTA of the
+// (row, head) to arrive (an arrival counter, reset by it for the next launch;
+// nobody waits on it) merges the chunks.  gridDim.z = ceil(ctx / 64), so a
+// captured launch serves every later step.
 template <typename TA>
 __global__ void __launch_bounds__(kAttThreads) attention_split_hs64_kernel(
     const RowDesc *__restrict__ rows, const float *__restrict__ q, float *__restrict__ kv, TA *__restrict__ out,
     int D, int att_ch, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride, float sqrt_hs,
     const float *__restrict__ kvs, const float2 *__restrict__ rope, float *__restrict__ part, int *__restrict__ cnt) {
-  constexpr int HS = 64, PW = HS + 2, U = 8, NW = kAttThreads / 32;
-  __shared__ __align__(16) float wpart[NW][HS + 8];  // per warp: max, sum, (pad), 64 weighted value sums from [4]
-  __shared__ float wsplit[kSplitMax], lsplit[kSplitMax], ohalf[HS];
+  constexpr int HS = 64;
+  __shared__ __align__(16) float wp4[4 * kAttPW];
   __shared__ int is_last;
   grid_dep_wait();
   grid_dep_launch();
   const int head = blockIdx.x, m = blockIdx.y, c = blockIdx.z, S = gridDim.z, H = gridDim.x;
+  const int warp = threadIdx.x >> 5;
   const RowDesc rd = rows[m];
-  const int n = rd.pos + 1;
-  const int chunk = ((n + S - 1) / S + 1) & ~1;
-  const int t0 = min(n, c * chunk), t1 = min(n, t0 + chunk), cn = t1 - t0;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int half = lane >> 4, pi = lane & 15;
-
-  float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
-  float *vbase = kbase + part_stride;
-  float4 qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + pi * 4);
-  const int nc = min(kvs ? n - 1 : n, t1);  // cache positions below nc; position pos from the staging entry
-  float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
-  if (kvs) {
-    const float *kst = kvs + (size_t)m * 2 * att_ch + head * HS;
-    const float4 cs = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + pi * 2);
-    qv = rope4(qv, cs);
-    knew = rope4(*reinterpret_cast<const float4 *>(kst + pi * 4), cs);
-    vnew = *reinterpret_cast<const float4 *>(kst + att_ch + pi * 4);
-    if (warp == 0 && t0 <= n - 1 && n - 1 < t1)  // append: lanes 0..15 the K row, 16..31 the V row
-      *reinterpret_cast<float4 *>((half ? vbase : kbase) + (size_t)rd.pos * HS + pi * 4) = half ? vnew : knew;
+  const int n = rd.pos + 1, C = (n + kAttChunk - 1) / kAttChunk;
+  float *pp = part + (size_t)(m * H + head) * S * kAttPW;
+  if (c < C) {
+    const AttRow r = att_row(rd, q, kv, m, head, att_ch, slot_stride, layer_off, part_stride, head_stride, kvs,
+                             rope, warp == 0 && c == (n - 1) / kAttChunk);
+    att_warp_chunk(r, c * kAttChunk, sqrt_hs, wp4 + warp * kAttPW);
+    __syncthreads();
+    if (threadIdx.x < HS) att_chunk_combine(wp4, threadIdx.x, pp + c * kAttPW);
   }
-
-  // ---- per warp: running max, exp sum and weighted values over its pairs ----
-  float wm = -9999.0f, wl = 0.f;
-  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int p0 = warp * U; 2 * p0 < cn; p0 += NW * U) {
-    float4 kr[U], vr[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int t = t0 + 2 * (p0 + u) + half;
-      const bool cached = t < nc;
-      kr[u] = cached ? __ldcs(reinterpret_cast<const float4 *>(kbase + (size_t)t * HS + pi * 4))
-              : t < t1 ? knew
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-      vr[u] = cached ? __ldcs(reinterpret_cast<const float4 *>(vbase + (size_t)t * HS + pi * 4))
-              : t < t1 ? vnew
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    float sc[U];
-    float mx = wm;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      float d = qv.x * kr[u].x + qv.y * kr[u].y + qv.z * kr[u].z + qv.w * kr[u].w;
-      d += __shfl_xor_sync(0xffffffffu, d, 8);
-      d += __shfl_xor_sync(0xffffffffu, d, 4);
-      d += __shfl_xor_sync(0xffffffffu, d, 2);
-      d += __shfl_xor_sync(0xffffffffu, d, 1);
-      sc[u] = __fdiv_rn(d, sqrt_hs);
-      if (t0 + 2 * (p0 + u) + half < t1) mx = fmaxf(mx, sc[u]);
-    }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-    const float scale = expf(__fsub_rn(wm, mx));
-    wl = __fmul_rn(wl, scale);
-    o.x = __fmul_rn(o.x, scale);
-    o.y = __fmul_rn(o.y, scale);
-    o.z = __fmul_rn(o.z, scale);
-    o.w = __fmul_rn(o.w, scale);
-    float ls = 0.f;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (t0 + 2 * (p0 + u) + half < t1) {
-        const float e = expf(__fsub_rn(sc[u], mx));
-        ls = __fadd_rn(ls, e);
-        o.x = __fadd_rn(o.x, __fmul_rn(vr[u].x, e));
-        o.y = __fadd_rn(o.y, __fmul_rn(vr[u].y, e));
-        o.z = __fadd_rn(o.z, __fmul_rn(vr[u].z, e));
-        o.w = __fadd_rn(o.w, __fmul_rn(vr[u].w, e));
-      }
-    }
-    wl = __fadd_rn(wl, __fadd_rn(ls, __shfl_xor_sync(0xffffffffu, ls, 16)));
-    wm = mx;
-  }
-  o.x += __shfl_xor_sync(0xffffffffu, o.x, 16);
-  o.y += __shfl_xor_sync(0xffffffffu, o.y, 16);
-  o.z += __shfl_xor_sync(0xffffffffu, o.z, 16);
-  o.w += __shfl_xor_sync(0xffffffffu, o.w, 16);
-  if (lane < 16) *reinterpret_cast<float4 *>(&wpart[warp][4 + 4 * pi]) = o;
-  if (lane == 0) {
-    wpart[warp][0] = wm;
-    wpart[warp][1] = wl;
-  }
-  __syncthreads();
-  // ---- this CTA's (m_c, l_c, o_c) from its warps ----
-  float *pp = part + (size_t)(m * H + head) * S * PW;
-  if (threadIdx.x < HS) {
-    float M = wpart[0][0];
-#pragma unroll
-    for (int w = 1; w < NW; ++w) M = fmaxf(M, wpart[w][0]);
-    float L = 0.f, ov = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const float sw = expf(__fsub_rn(wpart[w][0], M));
-      L = __fadd_rn(L, __fmul_rn(sw, wpart[w][1]));
-      ov = __fadd_rn(ov, __fmul_rn(sw, wpart[w][4 + threadIdx.x]));
-    }
-    pp[c * PW + 2 + threadIdx.x] = ov;
-    if (threadIdx.x == 0) {
-      pp[c * PW] = M;
-      pp[c * PW + 1] = L;
-    }
-  }
-  // ---- the last CTA of (row, head) merges the S results ----
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) is_last = atomicAdd(&cnt[m * H + head], 1) == S - 1;
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  if (threadIdx.x < S) wsplit[threadIdx.x] = __ldcg(pp + threadIdx.x * PW);
-  __syncthreads();
-  float M = -9999.0f;
-  for (int cc = 0; cc < S; ++cc) M = fmaxf(M, wsplit[cc]);
-  __syncthreads();
-  if (threadIdx.x < S) {
-    const float w = expf(__fsub_rn(wsplit[threadIdx.x], M));
-    wsplit[threadIdx.x] = w;
-    lsplit[threadIdx.x] = __fmul_rn(w, __ldcg(pp + threadIdx.x * PW + 1));
-  }
-  __syncthreads();
-  // channel ch, splits of parity h (two threads per channel), in split order
-  const int ch = threadIdx.x & (HS - 1), h = threadIdx.x >> 6;
-  float ov = 0.f;
-#pragma unroll 8
-  for (int cc = h; cc < S; cc += 2) ov = __fadd_rn(ov, __fmul_rn(wsplit[cc], __ldcg(pp + cc * PW + 2 + ch)));
-  if (h == 1) ohalf[ch] = ov;
-  __syncthreads();
   TA *orow = out + (size_t)m * D;
-  if (h == 0) {
-    float L = 0.f;
-    for (int cc = 0; cc < S; ++cc) L = __fadd_rn(L, lsplit[cc]);
-    ActIO<TA>::store(orow + head * HS + ch, __fdiv_rn(__fadd_rn(ov, ohalf[ch]), L));
-  }
+  if (threadIdx.x < HS)
+    ActIO<TA>::store(orow + head * HS + threadIdx.x,
+                     att_merge(pp, C, threadIdx.x, [](const float *p) { return __ldcg(p); }));
   if (threadIdx.x == 0) cnt[m * H + head] = 0;
   if (head == H - 1) att_zero_tail(orow, att_ch, D);
 }
@@ -942,20 +899,18 @@ static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_pos
     const bool b = set_dyn_smem(attention_split_hs64_kernel<TA>, 200 * 1024);
     return set_dyn_smem(attention_generic_kernel<TA>, 200 * 1024) && a && b;
   });
-  // few rows: split the positions of each (row, head) over S CTAs so that
-  // about two CTAs run per SM
-  const int rh = M * d.heads, nsm = sm_count(e.device);
-  int S = 1;
-  if (d.hs == 64 && e.att_split && e.att_part && rh < nsm && rh <= kSplitCounters) {
-    S = std::min((2 * nsm + rh - 1) / rh, (d.ctx + 63) / 64);
-    S = std::min({S, kSplitPartEntries / rh, kSplitMax});
-  }
-  if (S >= 2) {
-    launch_k(e, !tc_path(e, M), attention_split_hs64_kernel<TA>, dim3(d.heads, M, S), dim3(kAttThreads), 0,
+  // few rows: a CTA per 64-position chunk of every (row, head), whatever the
+  // row's position (the chunk count follows ctx, so a captured launch fits
+  // every later step); same bits as the whole-row kernel
+  const int rh = M * d.heads, nsm = sm_count(e.device), chunks = (d.ctx + kAttChunk - 1) / kAttChunk;
+  const bool split = d.hs == 64 && e.att_split && e.att_part && rh < nsm && rh <= kSplitCounters &&
+                     chunks <= kSplitMax && (size_t)rh * chunks <= e.att_part_entries;
+  if (split) {
+    launch_k(e, !tc_path(e, M), attention_split_hs64_kernel<TA>, dim3(d.heads, M, chunks), dim3(kAttThreads), 0,
              e.rows_d, e.q, e.kv, out, d.D, d.att_ch, e.kv_slot_stride, layer_off, e.kv_part_stride,
              e.kv_head_stride, e.sqrt_hs, defer ? e.kvs : nullptr, e.rope, e.att_part, e.att_cnt);
   } else if (d.hs == 64) {
-    const size_t sm = (32 + 4 * 64 + (size_t)max_n) * sizeof(float);
+    const size_t sm = (size_t)(2 * 4 + chunks) * kAttPW * sizeof(float);
     launch_k(e, !tc_path(e, M), attention_hs64_kernel<TA>, grid, dim3(kAttThreads), sm, e.rows_d, e.q, e.kv, out,
              d.D, d.att_ch, e.kv_slot_stride, layer_off, e.kv_part_stride, e.kv_head_stride, e.sqrt_hs,
              defer ? e.kvs : nullptr, e.rope);
