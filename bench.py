@@ -558,7 +558,7 @@ def sampling_lines(peaks, steps=10, warmup=3, check_rows=64, cpu_rows=256):
     return out_lines
 
 
-def gemv_pass_line(peaks, passes=50, rows=1, pos=16, split=True):
+def gemv_pass_line(peaks, passes=50, rows=1, pos=16, split=True, fused=False):
     """The small-batch path the PHP host drives: one decode pass of `rows`
     rows (embedding, 2 layers of fp32 GEMV projections and attention, final
     norm, logits) on the d=1024 benchmark model in FP32 mode, at position
@@ -567,19 +567,23 @@ def gemv_pass_line(peaks, passes=50, rows=1, pos=16, split=True):
     timed with its own CUDA events.  Bytes per pass are the library's
     algorithmic sums (weights once, KV read, activations).  split=False
     turns the split-position attention off (SNAI_ATTENTION_SPLIT=0) to
-    compare."""
+    compare; fused=True runs the pass as the persistent pass kernel
+    (SNAI_PASS_KERNEL=1) instead of one kernel per stage."""
     import torch
     from snai_b200 import PREC_FP32, Cortex
     dev = torch.device("cuda")
-    old = os.environ.get("SNAI_ATTENTION_SPLIT")
+    saved = {k: os.environ.get(k) for k in ("SNAI_ATTENTION_SPLIT", "SNAI_PASS_KERNEL")}
+    # fused: the persistent pass kernel (opt-in in the library)
     os.environ["SNAI_ATTENTION_SPLIT"] = "1" if split else "0"
+    os.environ["SNAI_PASS_KERNEL"] = "1" if fused else "0"
     try:
         eng = Cortex(make_model("c4"), num_heads=16, max_seqs=rows, precision=PREC_FP32)
     finally:
-        if old is None:
-            del os.environ["SNAI_ATTENTION_SPLIT"]
-        else:
-            os.environ["SNAI_ATTENTION_SPLIT"] = old
+        for k, v in saved.items():
+            if v is None:
+                del os.environ[k]
+            else:
+                os.environ[k] = v
     stream = torch.cuda.Stream(device=dev)
     eng.set_stream(stream.cuda_stream)
     rng = np.random.default_rng(7)
@@ -615,8 +619,10 @@ def gemv_pass_line(peaks, passes=50, rows=1, pos=16, split=True):
     att_n, att_ms, att_bytes, _ = prof["attention"]
     return {"metric": "one-row decode pass GB/s (fp32 GEMV path, d=1024)", "value": gbs, "unit": "GB/s",
             "rows": rows, "position": pos, "us_per_pass": us, "bytes_per_pass": pass_bytes, "passes": passes,
-            "attention_us_per_launch": 1e3 * att_ms / max(1, att_n),
-            "attention_split": split, "timing": "median of per-pass CUDA events",
+            "attention_us_per_launch": 1e3 * att_ms / att_n if att_n else None,
+            "attention_split": split, "persistent_pass_kernel": bool(fused and prof["pass"][0]),
+            "launches_per_pass": sum(v[0] for v in prof.values()) / 3,
+            "timing": "median of per-pass CUDA events",
             "l2": "flushed (256 MB written) before each pass",
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s",
                          "frac": gbs / peaks["hbm"], "peak_source": f"{peaks['kind']} hbm_gbs"}}
@@ -809,6 +815,7 @@ def our_arm(args, rank, world, local_rank):
             except Exception as ex:  # noqa: BLE001
                 line[name] = {"error": f"{type(ex).__name__}: {ex}"}
         for key, fn in (("gemv_pass", gemv_pass_line),
+                        ("gemv_pass_persistent", lambda p: gemv_pass_line(p, fused=True)),
                         ("gemv_pass_pos1000", lambda p: gemv_pass_line(p, pos=1000)),
                         ("gemv_pass_pos1000_unsplit", lambda p: gemv_pass_line(p, pos=1000, split=False)),
                         ("sampling", sampling_lines)):

@@ -206,7 +206,8 @@ CORTEX_API int cortex_seq_rewind(void *state, const int *slots, int n, int pos);
 /* Kernel-class profiler.  When on, every launch is bracketed by CUDA events
  * on the state's stream and its algorithmic bytes and FLOPs are counted.
  * kind: 0 embedding+norm, 1 rmsnorm, 2 QKV projection, 3 attention,
- * 4 Wo projection, 5 W_up, 6 W_down, 7 logits projection, 8 sampler.
+ * 4 Wo projection, 5 W_up, 6 W_down, 7 logits projection, 8 sampler,
+ * 9 the persistent kernel of a whole one- or two-row fp32 decode pass.
  * Enabling (or disabling) clears the counters; reading waits for the
  * stream. */
 CORTEX_API int cortex_profile_enable(void *state, int on);

@@ -103,13 +103,10 @@ bool make_dims(int vocab, int dim, int ctx, int layers, int heads, Dims *d) {
     set_error("num_heads %d gives head size %d: %d heads x %d > hidden_dim %d", heads, hs, d->heads, hs, dim);
     return false;
   }
-  // attention keeps, in shared memory, a 68-float partial per 64 positions
-  // (head size 64) or a score per position and two head vectors (others)
-  const size_t att_smem = hs == 64 ? ((size_t)(ctx + 63) / 64 + 8) * 68 * sizeof(float)
-                                   : ((size_t)ctx + 2 * (size_t)hs) * sizeof(float) + 2048;
-  if (att_smem > 200 * 1024) {
+  // attention keeps a score per position and two head vectors in shared memory
+  if (((size_t)ctx + 2 * (size_t)hs) * sizeof(float) + 2048 > 200 * 1024) {
     set_error("ctx_size %d with head size %d exceeds this engine's attention limit (%d positions)", ctx, hs,
-              hs == 64 ? (200 * 1024 / (68 * 4) - 8) * 64 : (200 * 1024 - 2048) / 4 - 2 * hs);
+              (200 * 1024 - 2048) / 4 - 2 * hs);
     return false;
   }
   return true;
@@ -159,6 +156,7 @@ Engine *create_engine(const Dims &d, int max_seqs, int device, int precision) {
   if (chunk <= 0) chunk = std::max(max_seqs, std::min(8192, std::max(d.ctx, 256)));
   e->m_max = (int)align_up((size_t)std::max(chunk, max_seqs), 128);
   e->att_split = env_int("SNAI_ATTENTION_SPLIT", 1) != 0;
+  e->pass_kernel = env_int("SNAI_PASS_KERNEL", 0) != 0;
 
   const size_t D = d.D, F = d.F, V = d.V;
   // ---- weights ----
@@ -209,6 +207,8 @@ Engine *create_engine(const Dims &d, int max_seqs, int device, int precision) {
   a.add(&e->rope, (size_t)d.ctx * (d.hs / 2));
   a.add(&e->err_d, 4);
   a.add(&e->step_d, 4);
+  a.add(&e->pass_layers, (size_t)d.L);
+  a.add(&e->pass_bar, 2);
 
   e->kv_head_stride = (size_t)d.ctx * d.hs;
   e->kv_part_stride = e->kv_head_stride * d.heads;
@@ -256,6 +256,12 @@ Engine *create_engine(const Dims &d, int max_seqs, int device, int precision) {
       rope[(size_t)p * (d.hs / 2) + i / 2] = make_float2(::cosf(theta), 1.0f * ::sinf(theta));
     }
   cudaMemcpyAsync(e->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice, e->stream);
+  std::vector<PassLayer> pl(d.L);
+  for (int l = 0; l < d.L; ++l) {
+    const LayerWeights &w = e->layers[l];
+    pl[l] = PassLayer{w.rms_att, w.rms_ffn, w.wqkv, w.wo, w.wup, w.wdown};
+  }
+  cudaMemcpyAsync(e->pass_layers, pl.data(), pl.size() * sizeof(PassLayer), cudaMemcpyHostToDevice, e->stream);
   e->sqrt_hs = ::sqrtf((float)d.hs);
   e->pos.assign(max_seqs, 0);
   e->logits_valid.assign(max_seqs, 0);
@@ -341,6 +347,9 @@ int check_device_error(Engine &e) {
   }
   if (code) {
     cudaMemset(e.err_d, 0, sizeof(int));
+    // a kernel that gave up may have left its arrival counters mid-way
+    cudaMemset(e.pass_bar, 0, 2 * sizeof(unsigned));
+    cudaMemset(e.att_cnt, 0, 256 * sizeof(int));
     set_error("device-side error %d (%s)", code,
               code == 6   ? "the bounded-wait self-test's wait expired"
               : code == 5 ? "the sampler saw an impossible row"

@@ -89,6 +89,12 @@ struct LayerWeights {
   __nv_bfloat16 *wqkv_h = nullptr, *wo_h = nullptr, *wup_h = nullptr, *wdown_h = nullptr;
 };
 
+// One layer's fp32 weights for the persistent one-row pass kernel (a device
+// table of these is made with the engine).
+struct PassLayer {
+  const float *rms_att, *rms_ffn, *wqkv, *wo, *wup, *wdown;
+};
+
 struct Engine {
   Dims d;
   int device = 0;
@@ -96,6 +102,9 @@ struct Engine {
   int max_seqs = 1;
   int m_max = 0;  // rows per forward chunk
   bool att_split = true;  // split-position attention for passes of few rows (SNAI_ATTENTION_SPLIT=0: off)
+  bool pass_kernel = false;  // one persistent kernel for FP32 passes of 1-2 rows (SNAI_PASS_KERNEL=1: on)
+  PassLayer *pass_layers = nullptr;  // [L] on the device
+  unsigned *pass_bar = nullptr;      // [2] grid-barrier counters of the pass kernel, zero between launches
   cudaStream_t own_stream = nullptr;
   cudaStream_t stream = nullptr;
 
@@ -185,7 +194,7 @@ struct Engine {
 // Kernel classes of the profiler (cortex_profile_read `kind`).
 enum ProfKind : int {
   kProfEmbed = 0, kProfNorm = 1, kProfQKV = 2, kProfAttention = 3, kProfWo = 4, kProfUp = 5, kProfDown = 6,
-  kProfLogits = 7, kProfSampler = 8, kProfKinds = 9
+  kProfLogits = 7, kProfSampler = 8, kProfPass = 9, kProfKinds = 10
 };
 // Brackets one launch: returns a token for prof_end (or -1 when off).
 int prof_begin(Engine &e);

@@ -18,6 +18,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <climits>
 #include <atomic>
 #include <cstdio>
@@ -84,6 +85,7 @@ __device__ __forceinline__ float rms_inv(float ss, int D) {
 // of block_sumsq in a kNormThreads CTA (virtual warp w = threads 32w..32w+31),
 // so a GEMV that normalises its own input rows reads the values the norm
 // kernel would have written.
+template <bool COHERENT = false>
 __device__ __forceinline__ float warp_row_rms_inv(const float *__restrict__ hr, int D, int lane) {
   constexpr int NW = kNormThreads / 32;
   float p[NW];
@@ -98,7 +100,7 @@ __device__ __forceinline__ float warp_row_rms_inv(const float *__restrict__ hr, 
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int i = base + 32 * w + lane + kNormThreads * j;
-        v[w][j] = i < D ? __ldg(hr + i) : 0.f;
+        v[w][j] = i < D ? (COHERENT ? __ldcg(hr + i) : __ldg(hr + i)) : 0.f;
       }
 #pragma unroll
     for (int w = 0; w < NW; ++w)
@@ -209,9 +211,14 @@ __device__ __forceinline__ float4 rope4(float4 v, float4 c) {
                      __fadd_rn(__fmul_rn(v.z, c.w), __fmul_rn(v.w, c.z)));
 }
 
-// ---- attention, head size 64: one canonical formula for every kernel ----
+// ---- attention of passes with few rows, head size 64: a chunked formula ----
 //
-// The positions 0..n-1 of a (row, head) are cut into chunks of 64 (4 warps x
+// The whole-row kernel below (a CTA per (row, head), the passes of many
+// rows) computes the reference's order: all scores, max, exponentials, sum,
+// weights, weighted values.  Passes with few rows (rows x heads below the SM
+// count) need more CTAs per (row, head), so the split kernel, and the
+// persistent one-row pass kernel, compute a chunked formula instead:
+// the positions 0..n-1 of a (row, head) are cut into chunks of 64 (4 warps x
 // 8 position pairs).  Warp w of a chunk loads the K and V rows of its 8 pairs
 // at once (a warp reads two 256-byte rows per instruction, so every load is a
 // contiguous 512-byte span of the head-major cache) and computes
@@ -221,11 +228,13 @@ __device__ __forceinline__ float4 rope4(float4 v, float4 c) {
 //   M_c = max_w m_w,  L_c = sum_w exp(m_w - M_c) l_w,  O_c = sum_w exp(m_w - M_c) o_w,
 // and the chunks in chunk order:
 //   M = max(-9999, M_c),  att = (sum_c exp(M_c - M) O_c) / (sum_c exp(M_c - M) L_c).
-// The whole-row kernel (a CTA per (row, head), chunks in a loop) and the
-// split kernel (a CTA per chunk, for passes of few rows) run exactly these
-// operations, so a row's attention has the same bits whichever kernel runs
-// it, whatever else is in its pass.  Channels >= heads*hs of att are zero
-// (:512-513).
+// The split kernel and the pass kernel run exactly these operations, so a
+// row's attention has the same bits in either; against the whole-row kernel
+// they differ by rounding (a few fp32 ulps), so a row's bits depend on
+// whether its pass has few rows.  (A chunked whole-row kernel was measured
+// 8-10 % slower than the one below at the d=1024 benchmark's HBM roofline,
+// so passes of many rows keep the reference's order.)  Channels >=
+// heads*hs of att are zero (:512-513).
 //
 // kvs non-null (a decode pass, one row per slot): K and V of position pos
 // come from the row's staging entry ([M, 2, att_ch], without RoPE, as q) and
@@ -245,6 +254,9 @@ struct AttRow {
 // The row's q (rotated in a decode pass), its cache pointers and the staged
 // K/V of position pos.  `append` writes the staged row to the cache (one
 // warp of one CTA per (row, head)).
+// COHERENT: q and the staged K/V were written earlier in the same kernel by
+// other CTAs (the persistent pass kernel): read them from L2.
+template <bool COHERENT = false>
 __device__ __forceinline__ AttRow att_row(const RowDesc &rd, const float *__restrict__ q, float *__restrict__ kv,
                                           int m, int head, int att_ch, size_t slot_stride, size_t layer_off,
                                           size_t part_stride, size_t head_stride, const float *__restrict__ kvs,
@@ -256,25 +268,28 @@ __device__ __forceinline__ AttRow att_row(const RowDesc &rd, const float *__rest
   r.nc = kvs ? r.n - 1 : r.n;
   r.kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
   r.vbase = r.kbase + part_stride;
-  r.qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + pi * 4);
+  auto ld4 = [](const float *p) {
+    return COHERENT ? __ldcg(reinterpret_cast<const float4 *>(p)) : *reinterpret_cast<const float4 *>(p);
+  };
+  r.qv = ld4(q + (size_t)m * att_ch + head * HS + pi * 4);
   r.knew = make_float4(0.f, 0.f, 0.f, 0.f);
   r.vnew = r.knew;
   if (kvs) {
     const float *kst = kvs + (size_t)m * 2 * att_ch + head * HS;
     const float4 cs = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + pi * 2);
     r.qv = rope4(r.qv, cs);
-    r.knew = rope4(*reinterpret_cast<const float4 *>(kst + pi * 4), cs);
-    r.vnew = *reinterpret_cast<const float4 *>(kst + att_ch + pi * 4);
+    r.knew = rope4(ld4(kst + pi * 4), cs);
+    r.vnew = ld4(kst + att_ch + pi * 4);
     if (append)  // lanes 0..15 the K row, lanes 16..31 the V row
       *reinterpret_cast<float4 *>((half ? r.vbase : r.kbase) + (size_t)rd.pos * HS + pi * 4) = half ? r.vnew : r.knew;
   }
   return r;
 }
 
-// This warp's (m_w, l_w, o_w) of the chunk starting at t0 into wp (kAttPW floats).
-__device__ __forceinline__ void att_warp_chunk(const AttRow &r, int t0, float sqrt_hs, float *wp) {
+// Warp `warp` (0..3)'s (m_w, l_w, o_w) of the chunk starting at t0 into wp (kAttPW floats).
+__device__ __forceinline__ void att_warp_chunk(const AttRow &r, int t0, float sqrt_hs, float *wp, int warp) {
   constexpr int HS = 64, U = 8;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane >> 4, pi = lane & 15;
+  const int lane = threadIdx.x & 31, half = lane >> 4, pi = lane & 15;
   const int t1 = min(r.n, t0 + kAttChunk);
   float4 kr[U], vr[U];
 #pragma unroll
@@ -301,12 +316,18 @@ __device__ __forceinline__ void att_warp_chunk(const AttRow &r, int t0, float sq
     if (t0 + 2 * (warp * U + u) + half < t1) mx = fmaxf(mx, sc[u]);
   }
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+  // each position's exponential once: lane u of a half computes it for its
+  // half's position u, the half's lanes read it by shuffle
+  float own = 0.f;
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+    if (pi == u) own = expf(__fsub_rn(sc[u], mx));
   float ls = 0.f;
   float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int u = 0; u < U; ++u) {
+    const float e = __shfl_sync(0xffffffffu, own, (lane & 16) | u);
     if (t0 + 2 * (warp * U + u) + half < t1) {
-      const float e = expf(__fsub_rn(sc[u], mx));
       ls = __fadd_rn(ls, e);
       o.x = __fadd_rn(o.x, __fmul_rn(vr[u].x, e));
       o.y = __fadd_rn(o.y, __fmul_rn(vr[u].y, e));
@@ -359,35 +380,108 @@ __device__ __forceinline__ float att_merge(const float *cp, int C, int ch, LD ld
   return __fdiv_rn(O, L);
 }
 
-// Whole-row kernel: a CTA per (row, head), its chunks in a loop (warp
-// partials double-buffered, one barrier per chunk), chunk partials in shared
-// memory, then the merge.
+// Whole-row kernel: one CTA per (row, head).  Scores s_t = (q . k_t) /
+// sqrtf(hs) for t <= pos go to shared memory; max starts at -9999 as in the
+// reference (:517); then e_t = exp(s_t - max), the sum, w_t = e_t / sum, and
+// att = sum_t w_t v_t.  A warp reads two positions per load instruction (16
+// lanes x 16 bytes per 256-byte key row), so every load is a contiguous
+// 512-byte span of the head-major cache.
+// kvs non-null: K and V of position pos come from the row's staging entry
+// ([M, 2, att_ch], without RoPE, as q) and are appended to the cache here,
+// where the slot's cache pages are being read anyway (one row per slot in
+// the pass); RoPE of q and k is applied here then.
 template <typename TA>
 __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
     const RowDesc *__restrict__ rows, const float *__restrict__ q, float *__restrict__ kv, TA *__restrict__ out,
     int D, int att_ch, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride, float sqrt_hs,
     const float *__restrict__ kvs, const float2 *__restrict__ rope) {
   constexpr int HS = 64;
-  extern __shared__ __align__(16) float smem_att[];
-  float *wpart = smem_att;                  // [2][4 warps][kAttPW]
-  float *cpart = smem_att + 2 * 4 * kAttPW;  // [chunks][kAttPW]
+  extern __shared__ float smem_att[];
+  float *red = smem_att;        // [32]
+  float *acc = smem_att + 32;   // [4 warps][64]
+  float *s = smem_att + 32 + 4 * HS;
   grid_dep_wait();
   grid_dep_launch();
-  const int m = blockIdx.y, head = blockIdx.x, warp = threadIdx.x >> 5;
+  const int m = blockIdx.y, head = blockIdx.x;
   const RowDesc rd = rows[m];
-  const AttRow r = att_row(rd, q, kv, m, head, att_ch, slot_stride, layer_off, part_stride, head_stride, kvs, rope,
-                           warp == 0);
-  const int C = (r.n + kAttChunk - 1) / kAttChunk;
-  for (int c = 0; c < C; ++c) {
-    float *wp4 = wpart + (c & 1) * 4 * kAttPW;
-    att_warp_chunk(r, c * kAttChunk, sqrt_hs, wp4 + warp * kAttPW);
-    __syncthreads();
-    if (threadIdx.x < HS) att_chunk_combine(wp4, threadIdx.x, cpart + c * kAttPW);
+  const int n = rd.pos + 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int half = lane >> 4, part = lane & 15;
+
+  float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
+  float *vbase = kbase + part_stride;
+  float4 qv = *reinterpret_cast<const float4 *>(q + (size_t)m * att_ch + head * HS + part * 4);
+  // cache positions below nc; position pos from the staging entry when deferred
+  const int nc = kvs ? n - 1 : n;
+  const float *kst = kvs ? kvs + (size_t)m * 2 * att_ch + head * HS : nullptr;
+  const float *vst = kvs ? kst + att_ch : nullptr;
+  float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
+  if (kvs) {
+    const float4 cs = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + part * 2);
+    qv = rope4(qv, cs);
+    knew = rope4(*reinterpret_cast<const float4 *>(kst + part * 4), cs);
+    vnew = *reinterpret_cast<const float4 *>(vst + part * 4);
+    if (warp == 0)  // append: lanes 0..15 the K row, lanes 16..31 the V row
+      *reinterpret_cast<float4 *>((half ? vbase : kbase) + (size_t)rd.pos * HS + part * 4) = half ? vnew : knew;
+  }
+
+  // ---- scores: warp w takes position pairs w, w+4, ...; 8 pairs per sweep ----
+  constexpr int U = 8;
+  for (int p0 = warp * U; 2 * p0 < n; p0 += 4 * U) {
+    float4 kr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = 2 * (p0 + u) + half;
+      kr[u] = t < nc   ? __ldcs(reinterpret_cast<const float4 *>(kbase + (size_t)t * HS + part * 4))
+              : t < n ? knew
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float d = qv.x * kr[u].x + qv.y * kr[u].y + qv.z * kr[u].z + qv.w * kr[u].w;
+      d += __shfl_xor_sync(0xffffffffu, d, 8);
+      d += __shfl_xor_sync(0xffffffffu, d, 4);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      const int t = 2 * (p0 + u) + half;
+      if (part == 0 && t < n) s[t] = __fdiv_rn(d, sqrt_hs);
+    }
   }
   __syncthreads();
+  att_softmax(s, n, red);
+
+  // ---- weighted sum of values ----
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int p0 = warp * U; 2 * p0 < n; p0 += 4 * U) {
+    float4 vr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = 2 * (p0 + u) + half;
+      vr[u] = t < nc   ? __ldcs(reinterpret_cast<const float4 *>(vbase + (size_t)t * HS + part * 4))
+              : t < n ? vnew
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = 2 * (p0 + u) + half;
+      const float wt = t < n ? s[t] : 0.f;
+      a.x = __fadd_rn(a.x, __fmul_rn(vr[u].x, wt));
+      a.y = __fadd_rn(a.y, __fmul_rn(vr[u].y, wt));
+      a.z = __fadd_rn(a.z, __fmul_rn(vr[u].z, wt));
+      a.w = __fadd_rn(a.w, __fmul_rn(vr[u].w, wt));
+    }
+  }
+  a.x += __shfl_xor_sync(0xffffffffu, a.x, 16);
+  a.y += __shfl_xor_sync(0xffffffffu, a.y, 16);
+  a.z += __shfl_xor_sync(0xffffffffu, a.z, 16);
+  a.w += __shfl_xor_sync(0xffffffffu, a.w, 16);
+  if (half == 0) *reinterpret_cast<float4 *>(acc + warp * HS + part * 4) = a;
+  __syncthreads();
   TA *orow = out + (size_t)m * D;
-  if (threadIdx.x < HS)
-    ActIO<TA>::store(orow + head * HS + threadIdx.x, att_merge(cpart, C, threadIdx.x, [](const float *p) { return *p; }));
+  if (threadIdx.x < HS) {
+    const float r = acc[threadIdx.x] + acc[HS + threadIdx.x] + acc[2 * HS + threadIdx.x] + acc[3 * HS + threadIdx.x];
+    ActIO<TA>::store(orow + head * HS + threadIdx.x, r);
+  }
   if (head == gridDim.x - 1) att_zero_tail(orow, att_ch, D);
 }
 
@@ -415,7 +509,7 @@ __global__ void __launch_bounds__(kAttThreads) attention_split_hs64_kernel(
   if (c < C) {
     const AttRow r = att_row(rd, q, kv, m, head, att_ch, slot_stride, layer_off, part_stride, head_stride, kvs,
                              rope, warp == 0 && c == (n - 1) / kAttChunk);
-    att_warp_chunk(r, c * kAttChunk, sqrt_hs, wp4 + warp * kAttPW);
+    att_warp_chunk(r, c * kAttChunk, sqrt_hs, wp4 + warp * kAttPW, warp);
     __syncthreads();
     if (threadIdx.x < HS) att_chunk_combine(wp4, threadIdx.x, pp + c * kAttPW);
   }
@@ -632,6 +726,416 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 2)
       if (live && lane % G == 0 && (r & 1) == 0 && m < M && n0 + r < N) {
         float v[16] = {tot, t1};
         epi.store(m, n0 + r, v, n0 + r + 1 < N ? 2 : 1);
+      }
+    }
+  }
+}
+
+// ============================================================================
+// the small-batch decode pass in one persistent kernel
+// ============================================================================
+//
+// A decode pass of one or two rows (the PHP host's cortex_forward step) reads
+// every weight once: 168 MB at d=1024, as fp32 matrices whose dot products
+// are tiny.  As separate launches (embedding, per layer QKV / attention / Wo
+// / W_up / W_down, logits) every kernel pays its own DRAM ramp and tail.
+// Here one CTA per SM runs the whole pass:
+//   * warp 0 streams this CTA's share of every weight matrix of the pass, in
+//     pass order, into a shared-memory ring with bulk copies (slots of 16*d
+//     bytes: a quad of rows of a d-wide matrix, or one row of W_down), never
+//     waiting for activations, so the weight stream keeps running through
+//     the stage boundaries;
+//   * warps 1..8 compute each stage from the ring and the stage's input
+//     vector in shared memory, then meet the other CTAs at a grid barrier
+//     (a monotonic counter, bounded spin) before the next stage reads what
+//     this one wrote.
+// Stages per layer: QKV (input RMSNorm(h), or of the embedding row in layer
+// 0), attention (64-position chunks of every (row, head) over the CTAs, the
+// last chunk of a (row, head) merging), Wo (+h), W_up (input RMSNorm(h),
+// SiLU), W_down (+h); then the logits (input RMSNorm(h)).  The arithmetic is
+// the fp32 GEMV's and the attention kernels' operation for operation (a
+// row's K in 512-column slices, lanes' FMA chains over four float4 per
+// slice, the warp butterfly, the slice sums in slice order; norms by the
+// GEMV's rms_inv; the canonical chunked attention), so the pass gives the
+// bits of the kernel-per-stage path.  Cross-CTA data written inside the
+// kernel (h, q, staged K/V, attention partials, att, u) is read from L2.
+// Used for FP32 passes of 1 or 2 rows of distinct slots that all want
+// logits, d = 512 or 1024, head size 64, vocab a multiple of 4, ctx <= 8192.
+constexpr int kPassThreads = 9 * 32;
+constexpr int kPassMaxRows = 2;
+constexpr int kPassMaxSlots = 32;
+constexpr size_t kPassRingBytes = 176 * 1024;
+
+struct PassArgs {
+  int M, D, F, V, L, H, S, ctx;
+  const RowDesc *rows;
+  const int *tokens_d;
+  const float *emb, *w_out, *rms_final;
+  const PassLayer *layers;
+  float *kv;
+  size_t slot_stride, layer_stride, part_stride, head_stride;
+  const float2 *rope;
+  float sqrt_hs;
+  float *h, *q, *kvs, *att, *u, *logits;
+  int *hist, *seq_len;
+  float *part;
+  int *cnt;
+  unsigned *bar;  // [0] arrivals, [1] finished CTAs; zero between launches
+  int *err;
+};
+
+struct PassSmem {
+  uint64_t full[kPassMaxSlots], empty[kPassMaxSlots];
+  float xs[kPassMaxRows * 4096];       // the stage's input rows
+  __align__(16) float wp4[2][4 * kAttPW];  // attention: two 4-warp groups
+  float inv[kPassMaxRows];
+  int flag[2];
+  int abort;
+};
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Every consumer thread of every CTA: returns once all CTAs have arrived at
+// barrier number `no` (their writes before it visible), or false (error
+// recorded) if that takes longer than kWaitTimeoutNs.
+__device__ bool pass_grid_sync(const PassArgs &a, PassSmem &sm, unsigned no) {
+  named_sync(1, 256);
+  if (threadIdx.x == 32) {
+    __threadfence();
+    atomicAdd(&a.bar[0], 1u);
+    const unsigned target = (no + 1) * gridDim.x;
+    bool ok = true;
+    if (ld_acquire_u32(&a.bar[0]) < target) {
+      const unsigned long long t0 = global_timer_ns();
+      for (uint32_t it = 1;; ++it) {
+        if (ld_acquire_u32(&a.bar[0]) >= target) break;
+        if ((it & 63u) == 0 && global_timer_ns() - t0 > kWaitTimeoutNs) {
+          record_error(a.err, kErrWaitAccum);
+          ok = false;
+          break;
+        }
+      }
+    }
+    sm.flag[0] = ok;
+    if (!ok) sm.abort = 1;
+  }
+  named_sync(1, 256);
+  return sm.flag[0] != 0;
+}
+
+// xs[m][k] = RMSNorm(src row m, w)[k] for the pass's rows; src row m is the
+// embedding row of the row's token (layer 0) or h.
+template <bool EMB>
+__device__ void pass_norm(const PassArgs &a, PassSmem &sm, const float *w) {
+  const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31, ct = threadIdx.x - 32;
+  auto src = [&](int m) -> const float * {
+    if constexpr (EMB) {
+      const RowDesc rd = a.rows[m];
+      const int raw = a.tokens_d ? a.tokens_d[rd.token] : rd.token;
+      const int tid = (raw < 0 || raw >= a.V) ? 0 : raw;
+      return a.emb + (size_t)tid * a.D;
+    } else {
+      return a.h + (size_t)m * a.D;
+    }
+  };
+  if (cw < a.M) {
+    const float inv = EMB ? warp_row_rms_inv<false>(src(cw), a.D, lane) : warp_row_rms_inv<true>(src(cw), a.D, lane);
+    if (lane == 0) sm.inv[cw] = inv;
+  }
+  named_sync(1, 256);
+  for (int m = 0; m < a.M; ++m) {
+    const float *s = src(m);
+    for (int k = 4 * ct; k < a.D; k += 4 * 256) {
+      const float4 hv = EMB ? __ldg(reinterpret_cast<const float4 *>(s + k)) : __ldcg(reinterpret_cast<const float4 *>(s + k));
+      const float4 wv = __ldg(reinterpret_cast<const float4 *>(w + k));
+      const float inv = sm.inv[m];
+      *reinterpret_cast<float4 *>(sm.xs + m * a.D + k) =
+          make_float4(__fmul_rn(__fmul_rn(hv.x, inv), wv.x), __fmul_rn(__fmul_rn(hv.y, inv), wv.y),
+                      __fmul_rn(__fmul_rn(hv.z, inv), wv.z), __fmul_rn(__fmul_rn(hv.w, inv), wv.w));
+    }
+  }
+  named_sync(1, 256);
+}
+
+// xs[m][0..K) = src[m * K ..] (a vector written earlier in this kernel).
+__device__ void pass_load(const PassArgs &a, PassSmem &sm, const float *src, int K) {
+  const int ct = threadIdx.x - 32;
+  for (int m = 0; m < a.M; ++m)
+    for (int k = 4 * ct; k < K; k += 4 * 256)
+      *reinterpret_cast<float4 *>(sm.xs + m * K + k) = __ldcg(reinterpret_cast<const float4 *>(src + (size_t)m * K + k));
+  named_sync(1, 256);
+}
+
+// This CTA's quads of an R-row matrix: [q0, q1) of R / 4.
+__device__ __forceinline__ void pass_quads(int R, int &q0, int &q1) {
+  const long long Q = R / 4;
+  q0 = (int)(Q * blockIdx.x / gridDim.x);
+  q1 = (int)(Q * (blockIdx.x + 1) / gridDim.x);
+}
+
+// One weight stage of the consumers: the CTA's rows of W (R x K, K = D or
+// F = 4D) from the ring, dot products with xs, Epi(m, n, v, cnt) on the
+// results.  Consumer warp w takes the stage's slots w, w + 8, ...: it waits
+// for its slot, computes every row of it (K in 512-column slices, each
+// slice's lanes FMA-chained over four float4 and butterfly-summed, the
+// slices added in order), releases the slot and stores the rows itself, so
+// the warps never wait for each other inside a stage.  `it` counts ring
+// slots in step with the producer.
+template <class Epi>
+__device__ bool pass_stage(const PassArgs &a, PassSmem &sm, const uint8_t *ring, int ns, int R, int K, int &it,
+                           const Epi &epi) {
+  const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
+  const int slot_bytes = 16 * a.D;
+  const int rows_per_slot = K == a.D ? 4 : 1;
+  const int T = K / 512;  // 512-column slices of a row
+  int q0, q1;
+  pass_quads(R, q0, q1);
+  const int nslots = (q1 - q0) * (4 / rows_per_slot);
+  bool ok = true;
+  for (int j = cw; ok && j < nslots; j += 8) {
+    const int sl = (it + j) % ns;
+    if (!mbar_wait_bounded(&sm.full[sl], (uint32_t)((it + j) / ns) & 1u, a.err, kErrWaitFull) || sm.abort) {
+      ok = false;
+      sm.abort = 1;
+      break;
+    }
+    const float *wsl = reinterpret_cast<const float *>(ring + (size_t)sl * slot_bytes);
+    float tot[4][kPassMaxRows];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      if (r >= rows_per_slot) break;
+      for (int t = 0; t < T; ++t) {
+        float acc[kPassMaxRows];
+#pragma unroll
+        for (int m = 0; m < kPassMaxRows; ++m) acc[m] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = t * 512 + lane * 4 + 128 * i;
+          const float4 w = *reinterpret_cast<const float4 *>(wsl + r * K + k);
+#pragma unroll
+          for (int m = 0; m < kPassMaxRows; ++m) {
+            const float4 xv = m < a.M ? *reinterpret_cast<const float4 *>(sm.xs + m * K + k)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            acc[m] = fmaf(w.x, xv.x, fmaf(w.y, xv.y, fmaf(w.z, xv.z, fmaf(w.w, xv.w, acc[m]))));
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < kPassMaxRows; ++m) {
+          const float s = warp_sum(acc[m]);
+          tot[r][m] = t == 0 ? s : __fadd_rn(tot[r][m], s);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[sl]);  // every lane has read the slot
+    if (rows_per_slot == 4) {
+      if (lane < 2 * a.M) {  // row pairs of a d-wide matrix
+        const int pr = lane / a.M, m = lane % a.M;
+        float v[16] = {};
+#pragma unroll
+        for (int r = 0; r < 4; r += 2)
+          if (pr == r / 2) {
+#pragma unroll
+            for (int mm = 0; mm < kPassMaxRows; ++mm)
+              if (mm == m) {
+                v[0] = tot[r][mm];
+                v[1] = tot[r + 1][mm];
+              }
+          }
+        epi.store(m, (q0 + j) * 4 + 2 * pr, v, 2);
+      }
+    } else if (lane < a.M) {  // one row of W_down
+      float v[16] = {};
+#pragma unroll
+      for (int mm = 0; mm < kPassMaxRows; ++mm)
+        if (mm == lane) v[0] = tot[0][mm];
+      epi.store(lane, q0 * 4 + j, v, 1);
+    }
+  }
+  it += nslots;
+  named_sync(1, 256);
+  return ok && !sm.abort;
+}
+
+// logits[rows[m].out][n] = C (core/cortex.nim:555-561)
+struct PassLogits {
+  float *logits;
+  const RowDesc *rows;
+  int V;
+  __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
+    float *p = logits + (size_t)rows[m].out * V + n;
+    for (int i = 0; i < cnt; ++i) p[i] = v[i];
+  }
+};
+
+// The attention stage: work items (row, head, chunk) over the CTAs, two at a
+// time (warps 1-4 and 5-8); the last chunk of a (row, head) to finish merges
+// into att.
+__device__ bool pass_attention(const PassArgs &a, PassSmem &sm, int l) {
+  const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
+  const int grp = cw >> 2, wq = cw & 3, gt = wq * 32 + lane;  // group, warp and thread in group
+  const size_t layer_off = (size_t)l * a.layer_stride;
+  int C[kPassMaxRows] = {0, 0};
+  int total = 0;
+  for (int m = 0; m < a.M; ++m) {
+    C[m] = (a.rows[m].pos + 1 + kAttChunk - 1) / kAttChunk;
+    total += a.H * C[m];
+  }
+  const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
+  const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+  for (int base = i0; base < i1; base += 2) {
+    const int item = base + grp;
+    if (item < i1) {
+      int m = 0, rem = item;
+      while (m + 1 < a.M && rem >= a.H * C[m]) rem -= a.H * C[m++];
+      const int head = rem / C[m], c = rem % C[m];
+      const RowDesc rd = a.rows[m];
+      const int n = rd.pos + 1;
+      const AttRow r = att_row<true>(rd, a.q, a.kv, m, head, a.D, a.slot_stride, layer_off, a.part_stride,
+                                     a.head_stride, a.kvs, a.rope, wq == 0 && c == (n - 1) / kAttChunk);
+      att_warp_chunk(r, c * kAttChunk, a.sqrt_hs, sm.wp4[grp] + wq * kAttPW, wq);
+      named_sync(2 + grp, 128);
+      float *pp = a.part + (size_t)(m * a.H + head) * a.S * kAttPW;
+      if (gt < 64) att_chunk_combine(sm.wp4[grp], gt, pp + c * kAttPW);
+      __threadfence();
+      named_sync(2 + grp, 128);
+      if (gt == 0) sm.flag[grp] = atomicAdd(&a.cnt[m * a.H + head], 1) == C[m] - 1;
+      named_sync(2 + grp, 128);
+      if (sm.flag[grp]) {
+        __threadfence();
+        if (gt < 64)
+          a.att[(size_t)m * a.D + head * 64 + gt] = att_merge(pp, C[m], gt, [](const float *p) { return __ldcg(p); });
+        if (gt == 0) a.cnt[m * a.H + head] = 0;
+      }
+      named_sync(2 + grp, 128);
+    }
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(kPassThreads, 1) snai_pass_kernel(const __grid_constant__ PassArgs a) {
+  extern __shared__ __align__(1024) uint8_t pass_smem[];
+  PassSmem &sm = *reinterpret_cast<PassSmem *>(pass_smem);
+  uint8_t *ring = pass_smem + ((sizeof(PassSmem) + 1023) & ~size_t(1023));
+  const int slot_bytes = 16 * a.D;
+  const int ns = min(kPassMaxSlots, (int)(kPassRingBytes / slot_bytes));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    sm.abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // ---- producer: every weight slot of this CTA, in pass order ----
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      auto stream = [&](const float *W, int R, int K) {
+        int q0, q1;
+        pass_quads(R, q0, q1);
+        const int nslots = (q1 - q0) * (K == a.D ? 1 : 4);
+        const char *base = reinterpret_cast<const char *>(W + (size_t)q0 * 4 * K);
+        for (int j = 0; ok && j < nslots; ++j, ++it) {
+          const int sl = it % ns;
+          if (!mbar_wait_bounded(&sm.empty[sl], ((uint32_t)(it / ns) & 1u) ^ 1u, a.err, kErrWaitEmpty) ||
+              *(volatile int *)&sm.abort) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sm.full[sl], (uint32_t)slot_bytes);
+          asm volatile(
+              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                  smem_u32(ring + (size_t)sl * slot_bytes)),
+              "l"(base + (size_t)j * slot_bytes), "r"(slot_bytes), "r"(smem_u32(&sm.full[sl]))
+              : "memory");
+        }
+      };
+      for (int l = 0; ok && l < a.L; ++l) {
+        const PassLayer &ly = a.layers[l];
+        stream(ly.wqkv, 3 * a.D, a.D);
+        stream(ly.wo, a.D, a.D);
+        stream(ly.wup, a.F, a.D);
+        stream(ly.wdown, a.D, a.F);
+      }
+      if (ok) stream(a.w_out, a.V, a.D);
+      // do not leave while a copy into this CTA's shared memory is in flight
+      for (int j = it - 1; j >= 0 && j >= it - ns; --j)
+        if (!mbar_wait_bounded(&sm.full[j % ns], (uint32_t)(j / ns) & 1u, a.err, kErrWaitDrain)) break;
+    }
+  } else {
+    // ---- consumers ----
+    const int ct = threadIdx.x - 32;
+    int it = 0;
+    unsigned bar = 0;
+    bool ok = true;
+    // the embedding row into h (a share per CTA), the token into the history
+    if (blockIdx.x == 0 && ct < a.M) {
+      const RowDesc rd = a.rows[ct];
+      const int raw = a.tokens_d ? a.tokens_d[rd.token] : rd.token;
+      a.hist[(size_t)rd.slot * a.ctx + rd.pos] = raw;
+      atomicMax(&a.seq_len[rd.slot], rd.pos + 1);
+    }
+    {
+      const int tot = a.M * a.D;
+      const int e0 = (int)((long long)tot * blockIdx.x / gridDim.x), e1 = (int)((long long)tot * (blockIdx.x + 1) / gridDim.x);
+      for (int e = e0 + ct; e < e1; e += 256) {
+        const int m = e / a.D, k = e - m * a.D;
+        const RowDesc rd = a.rows[m];
+        const int raw = a.tokens_d ? a.tokens_d[rd.token] : rd.token;
+        const int tid = (raw < 0 || raw >= a.V) ? 0 : raw;
+        a.h[(size_t)m * a.D + k] = a.emb[(size_t)tid * a.D + k];
+      }
+    }
+    for (int l = 0; ok && l < a.L; ++l) {
+      const PassLayer &ly = a.layers[l];
+      EpiQKV eq{a.rows, a.q, a.kv, a.rope, a.D, a.D, 64, a.slot_stride, (size_t)l * a.layer_stride,
+                a.part_stride, a.head_stride, a.kvs};
+      eq.tma = 0;
+      if (l == 0)
+        pass_norm<true>(a, sm, ly.rms_att);
+      else
+        pass_norm<false>(a, sm, ly.rms_att);
+      ok = pass_stage(a, sm, ring, ns, 3 * a.D, a.D, it, eq) && pass_grid_sync(a, sm, bar++);
+      if (!ok) break;
+      pass_attention(a, sm, l);
+      ok = pass_grid_sync(a, sm, bar++);
+      if (!ok) break;
+      pass_load(a, sm, a.att, a.D);
+      EpiResidual er{};
+      er.h = a.h;
+      er.ld = a.D;
+      ok = pass_stage(a, sm, ring, ns, a.D, a.D, it, er) && pass_grid_sync(a, sm, bar++);
+      if (!ok) break;
+      pass_norm<false>(a, sm, ly.rms_ffn);
+      ok = pass_stage(a, sm, ring, ns, a.F, a.D, it, EpiSilu<float>{a.u, a.F}) && pass_grid_sync(a, sm, bar++);
+      if (!ok) break;
+      pass_load(a, sm, a.u, a.F);
+      ok = pass_stage(a, sm, ring, ns, a.D, a.F, it, er) && pass_grid_sync(a, sm, bar++);
+    }
+    if (ok) {
+      pass_norm<false>(a, sm, a.rms_final);
+      ok = pass_stage(a, sm, ring, ns, a.V, a.D, it, PassLogits{a.logits, a.rows, a.V});
+    }
+    if (!ok) sm.abort = 1;
+    // the last CTA to finish resets the counters for the next launch (every
+    // CTA has passed every barrier by then)
+    named_sync(1, 256);
+    if (ct == 0 && ok) {
+      __threadfence();
+      if (atomicAdd(&a.bar[1], 1u) == gridDim.x - 1) {
+        a.bar[0] = 0;
+        a.bar[1] = 0;
       }
     }
   }
@@ -910,7 +1414,7 @@ static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_pos
              e.rows_d, e.q, e.kv, out, d.D, d.att_ch, e.kv_slot_stride, layer_off, e.kv_part_stride,
              e.kv_head_stride, e.sqrt_hs, defer ? e.kvs : nullptr, e.rope, e.att_part, e.att_cnt);
   } else if (d.hs == 64) {
-    const size_t sm = (size_t)(2 * 4 + chunks) * kAttPW * sizeof(float);
+    const size_t sm = (32 + 4 * 64 + (size_t)max_n) * sizeof(float);
     launch_k(e, !tc_path(e, M), attention_hs64_kernel<TA>, grid, dim3(kAttThreads), sm, e.rows_d, e.q, e.kv, out,
              d.D, d.att_ch, e.kv_slot_stride, layer_off, e.kv_part_stride, e.kv_head_stride, e.sqrt_hs,
              defer ? e.kvs : nullptr, e.rope);
@@ -941,10 +1445,100 @@ constexpr int kGemvNormRows = 1;
 
 static bool gemv_norm(const Engine &e, int M) { return !tc_path(e, M) && M <= kGemvNormRows; }
 
+// The persistent pass kernel serves FP32 decode passes of 1-2 rows of
+// distinct slots that all want logits (the shapes it is written for), when
+// the stream is not being captured into a graph.
+static bool pass_kernel_ok(Engine &e, int M, int n_out, bool defer) {
+  const Dims &d = e.d;
+  if (!(e.pass_kernel && e.precision == kFP32 && e.pass_layers && M >= 1 && M <= kPassMaxRows && n_out == M && defer &&
+        d.hs == 64 && d.att_ch == d.D && (d.D == 512 || d.D == 1024) && d.V % 4 == 0 && d.ctx <= 8192 &&
+        (size_t)M * d.heads * ((d.ctx + kAttChunk - 1) / kAttChunk) <= e.att_part_entries && M * d.heads <= kSplitCounters))
+    return false;
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(e.stream, &st) != cudaSuccess || st != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return false;
+  }
+  static DeviceOnce attr;
+  static std::atomic<int> fits[64];
+  const size_t smem = ((sizeof(PassSmem) + 1023) & ~size_t(1023)) + kPassRingBytes + 1024;
+  attr.run(e.device, [&] { return set_dyn_smem(snai_pass_kernel, (int)smem); });
+  if (e.device < 0 || e.device >= 64) return false;
+  int f = fits[e.device].load();
+  if (f == 0) {  // one CTA per SM must fit, or the cooperative launch is refused
+    int nb = 0;
+    f = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, snai_pass_kernel, kPassThreads, smem) == cudaSuccess &&
+                nb >= 1
+            ? 1
+            : -1;
+    cudaGetLastError();
+    fits[e.device].store(f);
+  }
+  return f == 1;
+}
+
+static int launch_pass(Engine &e, int M, const int *tokens_d, double kv_positions) {
+  const Dims &d = e.d;
+  PassArgs a{};
+  a.M = M;
+  a.D = d.D;
+  a.F = d.F;
+  a.V = d.V;
+  a.L = d.L;
+  a.H = d.heads;
+  a.S = (d.ctx + kAttChunk - 1) / kAttChunk;
+  a.ctx = d.ctx;
+  a.rows = e.rows_d;
+  a.tokens_d = tokens_d;
+  a.emb = e.emb;
+  a.w_out = e.w_out;
+  a.rms_final = e.rms_final;
+  a.layers = e.pass_layers;
+  a.kv = e.kv;
+  a.slot_stride = e.kv_slot_stride;
+  a.layer_stride = e.kv_layer_stride;
+  a.part_stride = e.kv_part_stride;
+  a.head_stride = e.kv_head_stride;
+  a.rope = e.rope;
+  a.sqrt_hs = e.sqrt_hs;
+  a.h = e.h;
+  a.q = e.q;
+  a.kvs = e.kvs;
+  a.att = static_cast<float *>(e.att);
+  a.u = static_cast<float *>(e.u);
+  a.logits = e.logits;
+  a.hist = e.hist;
+  a.seq_len = e.seq_len_d;
+  a.part = e.att_part;
+  a.cnt = e.att_cnt;
+  a.bar = e.pass_bar;
+  a.err = e.err_d;
+  const size_t smem = ((sizeof(PassSmem) + 1023) & ~size_t(1023)) + kPassRingBytes + 1024;
+  void *args[] = {&a};
+  const int tok = prof_begin(e);
+  const cudaError_t r = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(snai_pass_kernel),
+                                                    dim3(sm_count(e.device)), dim3(kPassThreads), args, smem,
+                                                    e.stream);
+  e.launches++;
+  const double wbytes = 4.0 * ((double)d.L * (4.0 * d.D * d.D + 2.0 * d.F * d.D) + (double)d.V * d.D);
+  prof_end(e, tok, kProfPass,
+           wbytes + kv_positions * 2.0 * d.att_ch * 4 * d.L + 4.0 * M * (d.V + d.D * (6.0 * d.L + 2)),
+           2.0 * M * (d.L * (4.0 * d.D * d.D + 2.0 * d.F * d.D) + (double)d.V * d.D) + kv_positions * 4.0 * d.att_ch * d.L);
+  if (r != cudaSuccess) {
+    cudaGetLastError();
+    set_error("pass kernel launch failed: %s", cudaGetErrorString(r));
+    return -4;
+  }
+  return 0;
+}
+
 template <typename TA>
 static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, bool out_tc, double kv_positions,
                            bool defer) {
   const Dims &d = e.d;
+  if constexpr (sizeof(TA) == 4) {
+    if (pass_kernel_ok(e, M, n_out, defer)) return launch_pass(e, M, tokens_d, kv_positions);
+  }
   const double ea = sizeof(TA);
   TA *x = static_cast<TA *>(e.x);
   TA *att = static_cast<TA *>(e.att);

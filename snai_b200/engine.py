@@ -154,7 +154,7 @@ class Cortex:
         n = self.slots if s is None else len(s)
         check(self.lib.cortex_seq_rewind(self.h, None if s is None else _ptr(s), n, int(pos)), "cortex_seq_rewind")
 
-    PROFILE_KINDS = ("embed", "rmsnorm", "qkv", "attention", "wo", "up", "down", "logits", "sampler")
+    PROFILE_KINDS = ("embed", "rmsnorm", "qkv", "attention", "wo", "up", "down", "logits", "sampler", "pass")
 
     def profile(self, on=True):
         check(self.lib.cortex_profile_enable(self.h, 1 if on else 0), "cortex_profile_enable")

@@ -366,3 +366,50 @@ def test_split_attention_ragged_positions(prec, model_dir, built):
             k = e.pos(s) - lens[s]  # tokens fed after the prompt
             assert rel_err(got[j], refs[s][k]) < tol, (group, s, k)
     e.close()
+
+
+@pytest.mark.parametrize("dim", [512, 1024])
+def test_pass_kernel_bits_equal_kernel_per_stage(dim, model_dir, built):
+    """FP32 decode passes of one and two rows run as one persistent kernel
+    (weights streamed through a shared-memory ring, grid barriers between
+    the stages).  Its arithmetic is the per-stage kernels' operation for
+    operation, so its logits equal those of an engine with the persistent
+    kernel off (SNAI_PASS_KERNEL=0) bit for bit, and the oracle's within the
+    fp32 tolerance, over a few steps at positions up to ~700.  (The
+    persistent kernel is opt-in, SNAI_PASS_KERNEL=1.)"""
+    import os
+    path = make_model(model_dir, f"pass{dim}.snai", 2000, dim, 1024, 2, seed=61)
+    heads = dim // 64
+    rng = np.random.default_rng(dim)
+    prompts = rng.integers(0, 2000, (2, 700)).astype(np.int32)
+    steps = rng.integers(0, 2000, (2, 4)).astype(np.int32)
+    engines = []
+    for flag in ("1", "0"):
+        os.environ["SNAI_PASS_KERNEL"] = flag
+        try:
+            engines.append(Cortex(path, num_heads=heads, max_seqs=2, precision=PREC_FP32))
+        finally:
+            del os.environ["SNAI_PASS_KERNEL"]
+    fused, staged = engines
+    oracles = [O.Oracle(path, num_heads=heads) for _ in range(2)]
+    for e in engines:
+        e.forward(prompts, want_logits=False)
+    for s in range(2):
+        oracles[s].forward(prompts[s])
+    for k in range(4):
+        group = [0] if k % 2 == 0 else [0, 1]
+        t = steps[group, k:k + 1]
+        a = fused.forward(t, slots=np.asarray(group, np.int32))
+        b = staged.forward(t, slots=np.asarray(group, np.int32))
+        assert np.array_equal(a, b), (k, float(np.abs(a - b).max()))
+        for j, s in enumerate(group):
+            assert rel_err(a[j], oracles[s].forward(t[j])) < TOL[PREC_FP32]
+    # a decode step (sampler, then the one-row pass) through both engines
+    prm = sample_params(VARIANT_A, 0.8, 1.15)
+    u = np.asarray([0.3], np.float32)
+    assert np.array_equal(fused.decode(u, prm, slots=[1]), staged.decode(u, prm, slots=[1]))
+    assert np.array_equal(fused.logits([1]), staged.logits([1]))
+    for e in engines:
+        e.close()
+    for o in oracles:
+        o.close()

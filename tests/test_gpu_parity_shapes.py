@@ -15,8 +15,10 @@ teacher-forced on the same tokens):
   max |gpu - oracle| / max |oracle| within the stated tolerance;
 * the replicas of a sequence get bit-identical logits, and a second engine
   with one slot per sequence (passes of 4 rows: single-CTA tiles
-  throughout) gets the same bits (a row's result does not depend on the
-  other rows of the pass or on the tile shape);
+  throughout; its attention held to the whole-row kernel with
+  SNAI_ATTENTION_SPLIT=0, as passes of many rows use) gets the same bits (a
+  row's result does not depend on the other rows of the pass or on the
+  projection tile shape);
 * one more step through the fused decode (cortex_decode_batch: sample, then
   feed) gives, row by row, exactly the id the oracle's sampler picks from
   the GPU's logits with the same history and uniform
@@ -88,7 +90,12 @@ def test_bench_shapes_logits_and_ids(case, prec, model_dir, built):
         assert err < TOL[prec], (s, err)
     print(f"{case} prec {prec}: max rel err per step {errs}")
     assert e.pos(0) == P + T
-    small = Cortex(path, num_heads=c["heads"], max_seqs=S, precision=prec)
+    import os
+    os.environ["SNAI_ATTENTION_SPLIT"] = "0"
+    try:
+        small = Cortex(path, num_heads=c["heads"], max_seqs=S, precision=prec)
+    finally:
+        del os.environ["SNAI_ATTENTION_SPLIT"]
     mine = [small.forward(prompts)] + [small.forward(forced[:, s:s + 1]) for s in range(T)]
     for s in range(T + 1):
         assert np.array_equal(mine[s], got[s][:S]), s
