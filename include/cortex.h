@@ -83,14 +83,24 @@ CORTEX_API void cortex_load_layer(void *state, int layer_idx, int tensor_type, f
 CORTEX_API void cortex_extract_layer(void *state, int layer_idx, int tensor_type, float *raw_weights, int num_weights);
 
 /* core/cortex.nim:474 / :479.  Adam moment storage per tensor (m when
- * is_variance is false, v otherwise); zero until loaded.  Kept in host
- * memory: this library runs no optimizer. */
+ * is_variance is false, v otherwise), in device memory beside the weights;
+ * zero until loaded or trained (allocShared0). */
 CORTEX_API void cortex_load_adam_layer(void *state, int layer_idx, int tensor_type, bool is_variance, float *raw, int size);
 CORTEX_API void cortex_extract_adam_layer(void *state, int layer_idx, int tensor_type, bool is_variance, float *raw, int size);
 
-/* core/cortex.nim:565 cortex_train_step.  Training is not part of this
- * library: returns NaN (the PHP worker aborts on a NaN loss,
- * src/train_worker.php:152-155) and sets cortex_last_error(). */
+/* core/cortex.nim:565 cortex_train_step.  One sequence of act =
+ * min(num_tokens, ctx) input ids and their targets (ids outside [0, V) read
+ * as 0): forward over every position with the activations kept, softmax
+ * cross-entropy, backpropagation through every position, the global
+ * gradient-norm clip at 1.0 (:230-258) and one Adam step (b1 0.9, b2 0.999,
+ * eps 1e-8, gradients divided by act; the embedding skips rows whose
+ * gradient is 0, :145-207).  Returns the mean loss (0 when act <= 0, with
+ * nothing changed).  Like the reference it leaves the K/V rows of positions
+ * 0..act-1 in the sequence's (slot 0's) cache and its position unchanged.
+ * fp32 arithmetic throughout (the GEMMs sum in another order than the
+ * reference's sequential loops).  On failure returns NaN (the PHP worker
+ * stops on a NaN loss, src/train_worker.php:152-155) and sets
+ * cortex_last_error(). */
 CORTEX_API float cortex_train_step(void *state, int *raw_inputs, int *raw_targets, int num_tokens, float lr);
 
 /* ======================================================================== */
@@ -336,6 +346,30 @@ CORTEX_API int cortex_tokenizer_decode(void *tok, const int *ids, int n, int tri
  * cortex_last_error() names the expired wait; the error word is cleared by
  * that report.  Returns 0 once queued. */
 CORTEX_API int cortex_selftest_wait_timeout(void *state, long long limit_ns);
+
+/* ------------------------------------------------------------------------ */
+/* The two halves of cortex_train_step, and its gradients.  No counterpart   */
+/* in the reference (whose step is one call); for inspecting and testing a   */
+/* step, and for callers that combine gradients before the update.           */
+/* ------------------------------------------------------------------------ */
+
+/* Forward, loss and backward of cortex_train_step (gradients of the summed
+ * loss left in the state's gradient block, the weights unchanged).  Writes
+ * the mean loss to *loss (0 when act <= 0).  Returns 0 or a negative code. */
+CORTEX_API int cortex_train_grads(void *state, const int *raw_inputs, const int *raw_targets, int num_tokens,
+                                  float *loss);
+/* The clip and the Adam step of cortex_train_step on the current gradients,
+ * with Adam's gradient divisor `scale` (cortex_train_step passes act).
+ * Counts one Adam step.  Queued on the state's stream (no host wait). */
+CORTEX_API int cortex_train_apply(void *state, float lr, float scale);
+/* Gradient tensor by (layer, type) as cortex_load_layer / extract_layer;
+ * a size mismatch is a silent no-op. */
+CORTEX_API void cortex_load_grad_layer(void *state, int layer_idx, int tensor_type, const float *raw, int size);
+CORTEX_API void cortex_extract_grad_layer(void *state, int layer_idx, int tensor_type, float *raw, int size);
+/* Adam steps taken (the reference's adam_t), and the clip of the last
+ * cortex_train_apply: its factor, the gradient norm and whether it applied.
+ * Returns 0, or -1 before the first update. */
+CORTEX_API int cortex_train_info(void *state, int *adam_steps, float *clip_factor, float *grad_norm, int *clipped);
 
 /* Number of kernels the state has launched since it was created. */
 CORTEX_API long long cortex_kernel_launches(void *state);

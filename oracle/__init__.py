@@ -26,6 +26,8 @@ _SIGS = {
     "oracle_get_head_size": (_c.c_int, [_vp]),
     "oracle_get_vocab": (_c.c_int, [_vp]),
     "oracle_get_ctx": (_c.c_int, [_vp]),
+    "oracle_get_dim": (_c.c_int, [_vp]),
+    "oracle_get_layers": (_c.c_int, [_vp]),
     "oracle_free": (None, [_vp]),
     "oracle_load_layer": (None, [_vp, _c.c_int, _c.c_int, _vp, _c.c_int]),
     "oracle_extract_layer": (None, [_vp, _c.c_int, _c.c_int, _vp, _c.c_int]),
@@ -42,6 +44,12 @@ _SIGS = {
     "oracle_batch_free": (None, [_vp]),
     "oracle_batch_step": (_c.c_double, [_vp, _c.c_int, _c.c_double, _c.c_double, _c.c_int, _c.c_double,
                                         _c.c_int]),
+    "oracle_train_step": (_c.c_float, [_vp, _vp, _vp, _c.c_int, _c.c_float]),
+    "oracle_train_grads": (_c.c_float, [_vp, _vp, _vp, _c.c_int]),
+    "oracle_train_apply": (None, [_vp, _c.c_float, _c.c_float]),
+    "oracle_train_tensor_get": (None, [_vp, _c.c_int, _c.c_int, _c.c_int, _vp, _c.c_int]),
+    "oracle_train_tensor_set": (None, [_vp, _c.c_int, _c.c_int, _c.c_int, _vp, _c.c_int]),
+    "oracle_adam_t": (_c.c_int, [_vp]),
     "oracle_sample_rows": (_c.c_double, [_vp, _c.c_int, _c.c_int, _vp, _c.c_int, _vp, _c.c_int, _c.c_double,
                                          _c.c_double, _c.c_int, _c.c_double, _c.c_int, _vp, _c.c_int]),
 }
@@ -85,6 +93,8 @@ class Oracle:
             raise RuntimeError("oracle could not load the model")
         self.vocab = L.oracle_get_vocab(self.h)
         self.ctx = L.oracle_get_ctx(self.h)
+        self.dim = L.oracle_get_dim(self.h)
+        self.layers = L.oracle_get_layers(self.h)
 
     def close(self):
         if self.h:
@@ -127,6 +137,48 @@ class Oracle:
                                      exp_mode, None if F is None else _p(F), _p(ids), None if lg is None else _p(lg),
                                      nthreads)
         return ids, lg, secs
+
+    # -- training (core/cortex.nim:565-822) ----------------------------------
+    _WHICH = {"grad": 0, "m": 1, "v": 2}
+
+    def tensor_size(self, layer, ttype):
+        v, dim = self.vocab, self.dim
+        f = 4 * dim
+        return {0: v * dim, 1: v * dim, 2: dim, 10: dim, 11: dim, 12: dim * dim, 13: dim * dim, 14: dim * dim,
+                15: dim * dim, 16: f * dim, 17: f * dim}[ttype]
+
+    def train_step(self, inputs, targets, lr):
+        a = np.ascontiguousarray(inputs, dtype=np.int32)
+        b = np.ascontiguousarray(targets, dtype=np.int32)
+        return float(lib().oracle_train_step(self.h, _p(a), _p(b), len(a), float(lr)))
+
+    def train_grads(self, inputs, targets):
+        a = np.ascontiguousarray(inputs, dtype=np.int32)
+        b = np.ascontiguousarray(targets, dtype=np.int32)
+        return float(lib().oracle_train_grads(self.h, _p(a), _p(b), len(a)))
+
+    def train_apply(self, lr, scale):
+        lib().oracle_train_apply(self.h, float(lr), float(scale))
+
+    @property
+    def adam_steps(self):
+        return lib().oracle_adam_t(self.h)
+
+    def tensor(self, layer, ttype, which="weight"):
+        n = self.tensor_size(layer, ttype)
+        out = np.zeros(n, dtype=np.float32)
+        if which == "weight":
+            lib().oracle_extract_layer(self.h, layer, ttype, _p(out), n)
+        else:
+            lib().oracle_train_tensor_get(self.h, self._WHICH[which], layer, ttype, _p(out), n)
+        return out
+
+    def set_tensor(self, layer, ttype, values, which="weight"):
+        a = np.ascontiguousarray(values, dtype=np.float32)
+        if which == "weight":
+            lib().oracle_load_layer(self.h, layer, ttype, _p(a), a.size)
+        else:
+            lib().oracle_train_tensor_set(self.h, self._WHICH[which], layer, ttype, _p(a), a.size)
 
     def batch(self, nseq, start_pos, seed=1):
         """A persistent batch of sequences for step-by-step CPU timing."""

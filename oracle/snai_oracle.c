@@ -23,6 +23,11 @@
  *                             logits for the last token only)
  *   core/cortex.nim:439-482   tensor type codes of load/extract layer
  *   core/cortex.nim:969-1044  cortex_load_stream (SNAI_V4 header + tensor order)
+ *   core/cortex.nim:565-822   cortex_train_step (forward with saved activations,
+ *                             softmax cross-entropy, BPTT in reverse position
+ *                             order, global gradient-norm clip :230-258, Adam
+ *                             :145-207 with the sparse embedding rule)
+ *   core/cortex.nim:474-482   load/extract of the Adam moments
  *   src/snai_inference.php:151-195     sampler "variant A"
  *   src/tensor_ffi_adapter.php:168-204 sampler "variant B"
  *
@@ -61,11 +66,17 @@ typedef struct {
   float *h, *norm, *att, *ffn, *q, *scores, *tmp;
 } OSeq;
 
-/* The legacy-shaped handle: one model and one sequence. */
+struct OTrain;
+
+/* The legacy-shaped handle: one model and one sequence (and, once a training
+ * call has been made, the gradients, Adam moments and activations). */
 typedef struct {
   OModel *m;
   OSeq *s;
+  struct OTrain *tr;
 } OState;
+
+static void train_free(struct OTrain *t);
 
 static float *zalloc(size_t n) { return (float *)calloc(n ? n : 1, sizeof(float)); }
 
@@ -310,10 +321,13 @@ EXPORT int oracle_get_heads(void *h) { return ((OState *)h)->m->heads; }
 EXPORT int oracle_get_head_size(void *h) { return ((OState *)h)->m->hs; }
 EXPORT int oracle_get_vocab(void *h) { return h ? ((OState *)h)->m->vocab : 0; }
 EXPORT int oracle_get_ctx(void *h) { return h ? ((OState *)h)->m->ctx : 0; }
+EXPORT int oracle_get_dim(void *h) { return h ? ((OState *)h)->m->dim : 0; }
+EXPORT int oracle_get_layers(void *h) { return h ? ((OState *)h)->m->layers : 0; }
 
 EXPORT void oracle_free(void *h) {
   OState *s = (OState *)h;
   if (!s) return;
+  train_free(s->tr);
   seq_free(s->s);
   model_free(s->m);
   free(s);
@@ -889,4 +903,439 @@ EXPORT double oracle_batch_step(void *p, int variant, double temperature, double
   free(th);
   free(jobs);
   return (t1.tv_sec - t0.tv_sec) + 1e-9 * (t1.tv_nsec - t0.tv_nsec);
+}
+
+/* ------------------------------------------------------------------------- */
+/* Training step, core/cortex.nim:565-822 (+ Adam :145-207, clip :230-258)   */
+/* ------------------------------------------------------------------------- */
+
+/* Gradients and Adam moments have the weights' shapes; activations are kept
+ * per layer for ctx positions, as the reference's act_* buffers. */
+typedef struct OTrain {
+  OModel *g, *mm, *vv;
+  int adam_t;
+  int ctx, L, D, F, V;
+  float **a_hidden, **a_norm_att, **a_q, **a_att, **a_hidden_ffn, **a_norm_ffn, **a_ffn_in, **a_ffn_out;
+  float *a_hidden_final, *probs;
+  float **dk, **dv; /* d_k_cache, d_v_cache [L][ctx * D] */
+  float *d_logits, *d_hidden, *d_norm, *d_att, *d_q, *d_ffn, *scores, *d_w, *norm;
+} OTrain;
+
+static void model_zero(OModel *m) {
+  size_t vd = (size_t)m->vocab * m->dim, dd = (size_t)m->dim * m->dim, fd = (size_t)m->ffn * m->dim;
+  memset(m->emb, 0, vd * 4);
+  memset(m->w_out, 0, vd * 4);
+  memset(m->rms_final, 0, (size_t)m->dim * 4);
+  for (int l = 0; l < m->layers; l++) {
+    memset(m->rms_att[l], 0, (size_t)m->dim * 4);
+    memset(m->rms_ffn[l], 0, (size_t)m->dim * 4);
+    memset(m->wq[l], 0, dd * 4); memset(m->wk[l], 0, dd * 4); memset(m->wv[l], 0, dd * 4);
+    memset(m->wo[l], 0, dd * 4); memset(m->wup[l], 0, fd * 4); memset(m->wdown[l], 0, fd * 4);
+  }
+}
+
+static float **alloc_rows(int L, size_t n) {
+  float **p = (float **)calloc(L ? L : 1, sizeof(float *));
+  for (int l = 0; l < L; l++) p[l] = zalloc(n);
+  return p;
+}
+
+static void free_rows(float **p, int L) {
+  if (!p) return;
+  for (int l = 0; l < L; l++) free(p[l]);
+  free(p);
+}
+
+static OTrain *train_get(OState *s) {
+  if (s->tr) return s->tr;
+  const OModel *m = s->m;
+  OTrain *t = (OTrain *)calloc(1, sizeof(OTrain));
+  t->ctx = m->ctx; t->L = m->layers; t->D = m->dim; t->F = m->ffn; t->V = m->vocab;
+  t->g = model_new(m->vocab, m->dim, m->ctx, m->layers, m->heads);
+  t->mm = model_new(m->vocab, m->dim, m->ctx, m->layers, m->heads);
+  t->vv = model_new(m->vocab, m->dim, m->ctx, m->layers, m->heads);
+  model_zero(t->g); model_zero(t->mm); model_zero(t->vv);
+  size_t cd = (size_t)m->ctx * m->dim, cf = (size_t)m->ctx * m->ffn;
+  t->a_hidden = alloc_rows(t->L, cd); t->a_norm_att = alloc_rows(t->L, cd); t->a_q = alloc_rows(t->L, cd);
+  t->a_att = alloc_rows(t->L, cd); t->a_hidden_ffn = alloc_rows(t->L, cd); t->a_norm_ffn = alloc_rows(t->L, cd);
+  t->a_ffn_in = alloc_rows(t->L, cf); t->a_ffn_out = alloc_rows(t->L, cf);
+  t->dk = alloc_rows(t->L, cd); t->dv = alloc_rows(t->L, cd);
+  t->a_hidden_final = zalloc(cd);
+  t->probs = zalloc((size_t)m->ctx * m->vocab);
+  t->d_logits = zalloc(m->vocab); t->d_hidden = zalloc(m->dim); t->d_norm = zalloc(m->dim);
+  t->d_att = zalloc(m->dim); t->d_q = zalloc(m->dim); t->d_ffn = zalloc(m->ffn);
+  t->scores = zalloc(m->ctx); t->d_w = zalloc(m->ctx); t->norm = zalloc(m->dim);
+  s->tr = t;
+  return t;
+}
+
+static void train_free(OTrain *t) {
+  if (!t) return;
+  model_free(t->g); model_free(t->mm); model_free(t->vv);
+  free_rows(t->a_hidden, t->L); free_rows(t->a_norm_att, t->L); free_rows(t->a_q, t->L);
+  free_rows(t->a_att, t->L); free_rows(t->a_hidden_ffn, t->L); free_rows(t->a_norm_ffn, t->L);
+  free_rows(t->a_ffn_in, t->L); free_rows(t->a_ffn_out, t->L); free_rows(t->dk, t->L); free_rows(t->dv, t->L);
+  free(t->a_hidden_final); free(t->probs); free(t->d_logits); free(t->d_hidden); free(t->d_norm);
+  free(t->d_att); free(t->d_q); free(t->d_ffn); free(t->scores); free(t->d_w); free(t->norm);
+  free(t);
+}
+
+/* applyRoPE with backward = true: the rotation by -theta (:74-87). */
+static void apply_rope_back(float *vec, int dim, int hs, int pos) {
+  int nh = dim / hs;
+  for (int h = 0; h < nh; h++) {
+    int off = h * hs;
+    for (int i = 0; i + 1 <= hs - 1; i += 2) {
+      float freq = 1.0f / powf(10000.0f, (float)i / (float)hs);
+      float theta = (float)pos * freq;
+      float c = cosf(theta);
+      float s = -1.0f * sinf(theta);
+      float v0 = vec[off + i], v1 = vec[off + i + 1];
+      vec[off + i] = v0 * c - v1 * s;
+      vec[off + i + 1] = v0 * s + v1 * c;
+    }
+  }
+}
+
+/* matVecMulBackwardAcc (:100-115): d_in (= or +=) M^T d_out, gm += d_out x^T. */
+static void matvec_back(const float *w, float *gw, int rows, int cols, const float *x, const float *d_out,
+                        float *d_in, int accumulate) {
+  if (d_in) {
+    if (!accumulate)
+      for (int c = 0; c < cols; c++) d_in[c] = 0.0f;
+    for (int r = 0; r < rows; r++) {
+      float dov = d_out[r];
+      const float *row = w + (size_t)r * cols;
+      for (int c = 0; c < cols; c++) d_in[c] += row[c] * dov;
+    }
+  }
+  for (int r = 0; r < rows; r++) {
+    float dov = d_out[r];
+    float *grow = gw + (size_t)r * cols;
+    for (int c = 0; c < cols; c++) grow[c] += dov * x[c];
+  }
+}
+
+/* applyRMSNormBackwardAcc (:125-143): d_out becomes the input gradient. */
+static void rmsnorm_back(float *d_out, const float *a, int dim, const float *w, float *gw) {
+  float ss = 0.0f;
+  for (int d = 0; d < dim; d++) ss += a[d] * a[d];
+  float inv = 1.0f / sqrtf((ss / (float)dim) + 1e-5f);
+  float sum_dy_nx = 0.0f;
+  for (int d = 0; d < dim; d++) sum_dy_nx += d_out[d] * w[d] * (a[d] * inv);
+  float mean = sum_dy_nx / (float)dim;
+  for (int d = 0; d < dim; d++) {
+    float nx = a[d] * inv;
+    gw[d] += d_out[d] * nx;
+    d_out[d] = (d_out[d] * w[d] - nx * mean) * inv;
+  }
+}
+
+/* Forward with saved activations, loss and BPTT (:565-818).  Gradients are
+ * zeroed first and left in t->g.  The sequence's KV cache rows 0..act-1 are
+ * overwritten as the reference does; its token count is not touched.
+ * Returns total_loss / act, or 0 when act <= 0. */
+static float train_grads(OState *st, const int *t_in, const int *t_tg, int num_tok) {
+  OModel *m = st->m;
+  OSeq *sq = st->s;
+  OTrain *t = train_get(st);
+  OModel *g = t->g;
+  const int D = m->dim, F = m->ffn, V = m->vocab, L = m->layers, hs = m->hs;
+  int act = num_tok < m->ctx ? num_tok : m->ctx;
+  if (act <= 0) return 0.0f;
+  model_zero(g);
+  for (int l = 0; l < L; l++) {
+    memset(t->dk[l], 0, (size_t)act * D * 4);
+    memset(t->dv[l], 0, (size_t)act * D * 4);
+  }
+  float total_loss = 0.0f;
+  float *h = sq->h, *norm = sq->norm, *att = sq->att;
+  for (int pos = 0; pos < act; pos++) {
+    int tid = t_in[pos], tg = t_tg[pos];
+    if (tid < 0 || tid >= V) tid = 0;
+    if (tg < 0 || tg >= V) tg = 0;
+    const size_t od = (size_t)pos * D, of = (size_t)pos * F;
+    memcpy(h, m->emb + (size_t)tid * D, sizeof(float) * D);
+    for (int l = 0; l < L; l++) {
+      memcpy(t->a_hidden[l] + od, h, sizeof(float) * D);
+      rmsnorm(h, norm, D, m->rms_att[l]);
+      memcpy(t->a_norm_att[l] + od, norm, sizeof(float) * D);
+      float *q = t->a_q[l] + od;
+      matvec(m->wq[l], D, D, norm, q);
+      apply_rope(q, D, hs, pos);
+      float *kp = sq->kc[l] + od, *vp = sq->vc[l] + od;
+      matvec(m->wk[l], D, D, norm, kp);
+      apply_rope(kp, D, hs, pos);
+      matvec(m->wv[l], D, D, norm, vp);
+      for (int d = 0; d < D; d++) att[d] = 0.0f;
+      for (int hh = 0; hh < m->heads; hh++) {
+        int off = hh * hs;
+        float max_s = -9999.0f;
+        for (int tt = 0; tt <= pos; tt++) {
+          const float *tk = sq->kc[l] + (size_t)tt * D;
+          float sc = 0.0f;
+          for (int d = 0; d < hs; d++) sc += q[off + d] * tk[off + d];
+          sc /= sqrtf((float)hs);
+          t->scores[tt] = sc;
+          if (sc > max_s) max_s = sc;
+        }
+        float sum_e = 0.0f;
+        for (int tt = 0; tt <= pos; tt++) {
+          t->scores[tt] = expf(t->scores[tt] - max_s);
+          sum_e += t->scores[tt];
+        }
+        for (int tt = 0; tt <= pos; tt++) {
+          float w = t->scores[tt] / sum_e;
+          const float *tv = sq->vc[l] + (size_t)tt * D;
+          for (int d = 0; d < hs; d++) att[off + d] += tv[off + d] * w;
+        }
+      }
+      memcpy(t->a_att[l] + od, att, sizeof(float) * D);
+      matvec(m->wo[l], D, D, att, t->d_norm);
+      for (int d = 0; d < D; d++) h[d] += t->d_norm[d];
+      memcpy(t->a_hidden_ffn[l] + od, h, sizeof(float) * D);
+      rmsnorm(h, norm, D, m->rms_ffn[l]);
+      memcpy(t->a_norm_ffn[l] + od, norm, sizeof(float) * D);
+      float *fin = t->a_ffn_in[l] + of, *fout = t->a_ffn_out[l] + of;
+      matvec(m->wup[l], F, D, norm, fin);
+      for (int d = 0; d < F; d++) {
+        float v = fin[d];
+        fout[d] = v * (1.0f / (1.0f + expf(-v)));
+      }
+      matvec(m->wdown[l], D, F, fout, att);
+      for (int d = 0; d < D; d++) h[d] += att[d];
+    }
+    memcpy(t->a_hidden_final + od, h, sizeof(float) * D);
+    rmsnorm(h, norm, D, m->rms_final);
+    float max_l = -9999.0f;
+    float *lg = t->probs + (size_t)pos * V;
+    for (int v = 0; v < V; v++) {
+      float s = 0.0f;
+      const float *row = m->w_out + (size_t)v * D;
+      for (int d = 0; d < D; d++) s += norm[d] * row[d];
+      lg[v] = s;
+      if (s > max_l) max_l = s;
+    }
+    float sum_p = 0.0f;
+    for (int v = 0; v < V; v++) {
+      lg[v] = expf(lg[v] - max_l);
+      sum_p += lg[v];
+    }
+    for (int v = 0; v < V; v++) lg[v] /= sum_p;
+    total_loss += -logf(lg[tg] + 1e-7f);
+  }
+
+  for (int pos = act - 1; pos >= 0; pos--) {
+    int tid = t_in[pos], tg = t_tg[pos];
+    if (tid < 0 || tid >= V) tid = 0;
+    if (tg < 0 || tg >= V) tg = 0;
+    const size_t od = (size_t)pos * D, of = (size_t)pos * F;
+    const float *lg = t->probs + (size_t)pos * V;
+    for (int v = 0; v < V; v++) t->d_logits[v] = lg[v] - (v == tg ? 1.0f : 0.0f);
+    for (int d = 0; d < D; d++) t->d_hidden[d] = 0.0f;
+    const float *fh = t->a_hidden_final + od;
+    rmsnorm(fh, t->norm, D, m->rms_final);
+    matvec_back(m->w_out, g->w_out, V, D, t->norm, t->d_logits, t->d_norm, 0);
+    rmsnorm_back(t->d_norm, fh, D, m->rms_final, g->rms_final);
+    for (int d = 0; d < D; d++) t->d_hidden[d] += t->d_norm[d];
+    for (int l = L - 1; l >= 0; l--) {
+      for (int d = 0; d < D; d++) t->d_norm[d] = t->d_hidden[d];
+      matvec_back(m->wdown[l], g->wdown[l], D, F, t->a_ffn_out[l] + of, t->d_norm, t->d_ffn, 0);
+      const float *fin = t->a_ffn_in[l] + of;
+      for (int d = 0; d < F; d++) {
+        float x = fin[d];
+        float sig = 1.0f / (1.0f + expf(-x));
+        t->d_ffn[d] *= sig * (1.0f + x * (1.0f - sig));
+      }
+      matvec_back(m->wup[l], g->wup[l], F, D, t->a_norm_ffn[l] + od, t->d_ffn, t->d_norm, 0);
+      rmsnorm_back(t->d_norm, t->a_hidden_ffn[l] + od, D, m->rms_ffn[l], g->rms_ffn[l]);
+      for (int d = 0; d < D; d++) t->d_hidden[d] += t->d_norm[d];
+      for (int d = 0; d < D; d++) t->d_norm[d] = t->d_hidden[d];
+      matvec_back(m->wo[l], g->wo[l], D, D, t->a_att[l] + od, t->d_norm, t->d_att, 0);
+      const float *q = t->a_q[l] + od;
+      for (int d = 0; d < D; d++) t->d_q[d] = 0.0f;
+      for (int hh = 0; hh < m->heads; hh++) {
+        int off = hh * hs;
+        float scale = 1.0f / sqrtf((float)hs);
+        float max_s = -9999.0f;
+        for (int tt = 0; tt <= pos; tt++) {
+          const float *kt = sq->kc[l] + (size_t)tt * D;
+          float sc = 0.0f;
+          for (int d = 0; d < hs; d++) sc += q[off + d] * kt[off + d];
+          sc *= scale;
+          t->scores[tt] = sc;
+          if (sc > max_s) max_s = sc;
+        }
+        float sum_e = 0.0f;
+        for (int tt = 0; tt <= pos; tt++) {
+          t->scores[tt] = expf(t->scores[tt] - max_s);
+          sum_e += t->scores[tt];
+        }
+        float sum_w_dw = 0.0f;
+        for (int tt = 0; tt <= pos; tt++) {
+          float w = t->scores[tt] / sum_e;
+          t->scores[tt] = w;
+          const float *vt = sq->vc[l] + (size_t)tt * D;
+          float dw = 0.0f;
+          for (int d = 0; d < hs; d++) dw += t->d_att[off + d] * vt[off + d];
+          float *dvt = t->dv[l] + (size_t)tt * D;
+          for (int d = 0; d < hs; d++) dvt[off + d] += t->d_att[off + d] * w;
+          t->d_w[tt] = dw;
+          sum_w_dw += w * dw;
+        }
+        for (int tt = 0; tt <= pos; tt++) {
+          float w = t->scores[tt];
+          float ds = w * (t->d_w[tt] - sum_w_dw) * scale;
+          const float *kt = sq->kc[l] + (size_t)tt * D;
+          float *dkt = t->dk[l] + (size_t)tt * D;
+          for (int d = 0; d < hs; d++) {
+            t->d_q[off + d] += ds * kt[off + d];
+            dkt[off + d] += ds * q[off + d];
+          }
+        }
+      }
+      float *cdk = t->dk[l] + od, *cdv = t->dv[l] + od;
+      apply_rope_back(t->d_q, D, hs, pos);
+      apply_rope_back(cdk, D, hs, pos);
+      const float *na = t->a_norm_att[l] + od;
+      matvec_back(m->wq[l], g->wq[l], D, D, na, t->d_q, t->d_norm, 0);
+      matvec_back(m->wk[l], g->wk[l], D, D, na, cdk, t->d_norm, 1);
+      matvec_back(m->wv[l], g->wv[l], D, D, na, cdv, t->d_norm, 1);
+      rmsnorm_back(t->d_norm, t->a_hidden[l] + od, D, m->rms_att[l], g->rms_att[l]);
+      for (int d = 0; d < D; d++) t->d_hidden[d] += t->d_norm[d];
+    }
+    float *ge = g->emb + (size_t)tid * D;
+    for (int d = 0; d < D; d++) ge[d] += t->d_hidden[d];
+  }
+  return total_loss / (float)act;
+}
+
+static float l2sq(const float *a, size_t n) {
+  float s = 0.0f;
+  for (size_t i = 0; i < n; i++) s += a[i] * a[i];
+  return s;
+}
+
+static void scale_arr(float *a, size_t n, float sc) {
+  for (size_t i = 0; i < n; i++) a[i] *= sc;
+}
+
+/* adamStep (:145-160). */
+static void adam_step(float *w, float *m, float *v, float *g, float lr, float b1, float b2, float b1t, float b2t,
+                      float scale, int sparse) {
+  if (scale == 0.0f) return;
+  float grad = *g / scale;
+  if (sparse && grad == 0.0f) return;
+  if (grad != grad || grad > 9999.0f || grad < -9999.0f) {
+    *g = 0.0f;
+    return;
+  }
+  *m = b1 * *m + (1.0f - b1) * grad;
+  *v = b2 * *v + (1.0f - b2) * grad * grad;
+  float m_hat = *m / b1t;
+  float v_hat = *v / b2t;
+  *w -= lr * m_hat / (sqrtf(v_hat) + 1e-8f);
+  *g = 0.0f;
+}
+
+/* clipGlobalGradientNorm(s, 1.0) (:230-258), then applyGlobalAdamUpdate(lr,
+ * scale) (:162-207, CPU branch). */
+static void train_apply(OState *st, float lr, float scale) {
+  OModel *m = st->m;
+  OTrain *t = train_get(st);
+  OModel *g = t->g;
+  const int L = m->layers;
+  const size_t vd = (size_t)m->vocab * m->dim, dd = (size_t)m->dim * m->dim, fd = (size_t)m->ffn * m->dim;
+  const size_t D = (size_t)m->dim;
+  float total_sq = 0.0f;
+  total_sq += l2sq(g->emb, vd);
+  total_sq += l2sq(g->w_out, vd);
+  total_sq += l2sq(g->rms_final, D);
+  for (int l = 0; l < L; l++) {
+    total_sq += l2sq(g->wq[l], dd);
+    total_sq += l2sq(g->wk[l], dd);
+    total_sq += l2sq(g->wv[l], dd);
+    total_sq += l2sq(g->wo[l], dd);
+    total_sq += l2sq(g->wup[l], fd);
+    total_sq += l2sq(g->wdown[l], fd);
+    total_sq += l2sq(g->rms_att[l], D);
+    total_sq += l2sq(g->rms_ffn[l], D);
+  }
+  const float max_norm = 1.0f;
+  float gn = sqrtf(total_sq);
+  if (gn != gn || gn > max_norm) {
+    float sc = (gn != gn || gn == 0.0f) ? 0.0f : max_norm / gn;
+    scale_arr(g->emb, vd, sc);
+    scale_arr(g->w_out, vd, sc);
+    scale_arr(g->rms_final, D, sc);
+    for (int l = 0; l < L; l++) {
+      scale_arr(g->wq[l], dd, sc); scale_arr(g->wk[l], dd, sc); scale_arr(g->wv[l], dd, sc);
+      scale_arr(g->wo[l], dd, sc); scale_arr(g->wup[l], fd, sc); scale_arr(g->wdown[l], fd, sc);
+      scale_arr(g->rms_att[l], D, sc); scale_arr(g->rms_ffn[l], D, sc);
+    }
+  }
+  t->adam_t += 1;
+  const float b1 = 0.9f, b2 = 0.999f;
+  const float b1t = 1.0f - powf(b1, (float)t->adam_t);
+  const float b2t = 1.0f - powf(b2, (float)t->adam_t);
+  OModel *M = t->mm, *Vv = t->vv;
+#define UPD(W, MM, VV, G, N, SP) \
+  for (size_t i_ = 0; i_ < (N); i_++) adam_step(&(W)[i_], &(MM)[i_], &(VV)[i_], &(G)[i_], lr, b1, b2, b1t, b2t, scale, SP)
+  UPD(m->emb, M->emb, Vv->emb, g->emb, vd, 1);
+  UPD(m->w_out, M->w_out, Vv->w_out, g->w_out, vd, 0);
+  UPD(m->rms_final, M->rms_final, Vv->rms_final, g->rms_final, D, 0);
+  for (int l = 0; l < L; l++) {
+    UPD(m->rms_att[l], M->rms_att[l], Vv->rms_att[l], g->rms_att[l], D, 0);
+    UPD(m->rms_ffn[l], M->rms_ffn[l], Vv->rms_ffn[l], g->rms_ffn[l], D, 0);
+    UPD(m->wq[l], M->wq[l], Vv->wq[l], g->wq[l], dd, 0);
+    UPD(m->wk[l], M->wk[l], Vv->wk[l], g->wk[l], dd, 0);
+    UPD(m->wv[l], M->wv[l], Vv->wv[l], g->wv[l], dd, 0);
+    UPD(m->wo[l], M->wo[l], Vv->wo[l], g->wo[l], dd, 0);
+    UPD(m->wup[l], M->wup[l], Vv->wup[l], g->wup[l], fd, 0);
+    UPD(m->wdown[l], M->wdown[l], Vv->wdown[l], g->wdown[l], fd, 0);
+  }
+#undef UPD
+}
+
+/* cortex_train_step: gradients, clip, Adam; returns the mean loss. */
+EXPORT float oracle_train_step(void *h, const int *t_in, const int *t_tg, int num_tok, float lr) {
+  OState *st = (OState *)h;
+  int act = num_tok < st->m->ctx ? num_tok : st->m->ctx;
+  if (act <= 0) return 0.0f;
+  float loss = train_grads(st, t_in, t_tg, num_tok);
+  train_apply(st, lr, (float)act);
+  return loss;
+}
+
+/* The two halves of a step, for tests: gradients only (left in place)... */
+EXPORT float oracle_train_grads(void *h, const int *t_in, const int *t_tg, int num_tok) {
+  return train_grads((OState *)h, t_in, t_tg, num_tok);
+}
+
+/* ...and clip + Adam on the gradients in place, with Adam's divisor `scale`
+ * (the step's token count). */
+EXPORT void oracle_train_apply(void *h, float lr, float scale) { train_apply((OState *)h, lr, scale); }
+
+/* Gradient (which 0) or Adam first / second moment (1 / 2) tensor by type code. */
+static float *train_tensor(OState *st, int which, int layer, int type, size_t *n) {
+  OTrain *t = train_get(st);
+  OModel *src = which == 0 ? t->g : which == 1 ? t->mm : t->vv;
+  return tensor_ptr(src, layer, type, n);
+}
+
+EXPORT void oracle_train_tensor_get(void *h, int which, int layer, int type, float *out, int n) {
+  size_t want = 0;
+  float *p = train_tensor((OState *)h, which, layer, type, &want);
+  if (p && (size_t)n == want) memcpy(out, p, want * sizeof(float));
+}
+
+EXPORT void oracle_train_tensor_set(void *h, int which, int layer, int type, const float *in, int n) {
+  size_t want = 0;
+  float *p = train_tensor((OState *)h, which, layer, type, &want);
+  if (p && (size_t)n == want) memcpy(p, in, want * sizeof(float));
+}
+
+EXPORT int oracle_adam_t(void *h) {
+  OState *st = (OState *)h;
+  return st->tr ? st->tr->adam_t : 0;
 }

@@ -92,6 +92,12 @@ SIGNATURES = {
     "cortex_tokenizer_decode": (c_int, [c_void_p, c_void_p, c_int, c_int, c_char_p, c_int]),
     "cortex_selftest_wait_timeout": (c_int, [c_void_p, ctypes.c_longlong]),
     "cortex_kernel_launches": (ctypes.c_longlong, [c_void_p]),
+    "cortex_train_grads": (c_int, [c_void_p, c_void_p, c_void_p, c_int, ctypes.POINTER(c_float)]),
+    "cortex_train_apply": (c_int, [c_void_p, c_float, c_float]),
+    "cortex_load_grad_layer": (None, [c_void_p, c_int, c_int, c_void_p, c_int]),
+    "cortex_extract_grad_layer": (None, [c_void_p, c_int, c_int, c_void_p, c_int]),
+    "cortex_train_info": (c_int, [c_void_p, ctypes.POINTER(c_int), ctypes.POINTER(c_float), ctypes.POINTER(c_float),
+                                  ctypes.POINTER(c_int)]),
 }
 
 _lib = None

@@ -124,6 +124,7 @@ void free_engine(Engine *e) {
   cudaFree(e->unif_all);
   cudaFree(e->ids_all);
   cudaFree(e->avg_tmp);
+  train_free(*e);
   if (e->own_stream) cudaStreamDestroy(e->own_stream);
   delete e;
 }
@@ -687,32 +688,118 @@ extern "C" void cortex_extract_layer(void *state, int layer_idx, int tensor_type
   cudaMemcpy(raw_weights, p, n * sizeof(float), cudaMemcpyDeviceToHost);
 }
 
-extern "C" void cortex_load_adam_layer(void *state, int layer_idx, int tensor_type, bool is_variance, float *raw,
-                                       int size) {
+// Copies one gradient / moment tensor in or out (which: 0 gradient, 1 m, 2 v).
+static void train_tensor_copy(void *state, int which, int layer_idx, int tensor_type, float *raw, int size, bool in) {
   if (!state || !raw) return;
   Engine &e = *static_cast<Engine *>(state);
   size_t n = 0;
-  if (!tensor_ptr(e, layer_idx, tensor_type, &n) || (size_t)size != n) return;
-  auto &buf = e.adam[std::make_tuple(layer_idx, tensor_type, is_variance ? 1 : 0)];
-  buf.assign(raw, raw + n);
+  float *w = tensor_ptr(e, layer_idx, tensor_type, &n);
+  if (!w || (size_t)size != n) return;  // silent on mismatch, as :465
+  DeviceGuard g(e.device);
+  float *p = train_tensor(e, which, w);
+  if (!p) {
+    fprintf(stderr, "libcortex: %s\n", g_err.c_str());
+    if (!in) std::fill(raw, raw + n, std::numeric_limits<float>::quiet_NaN());
+    return;
+  }
+  cudaStreamSynchronize(e.stream);
+  if (in)
+    cudaMemcpy(p, raw, n * sizeof(float), cudaMemcpyHostToDevice);
+  else
+    cudaMemcpy(raw, p, n * sizeof(float), cudaMemcpyDeviceToHost);
+}
+
+extern "C" void cortex_load_adam_layer(void *state, int layer_idx, int tensor_type, bool is_variance, float *raw,
+                                       int size) {
+  train_tensor_copy(state, is_variance ? 2 : 1, layer_idx, tensor_type, raw, size, true);
 }
 
 extern "C" void cortex_extract_adam_layer(void *state, int layer_idx, int tensor_type, bool is_variance, float *raw,
                                           int size) {
-  if (!state || !raw) return;
-  Engine &e = *static_cast<Engine *>(state);
-  size_t n = 0;
-  if (!tensor_ptr(e, layer_idx, tensor_type, &n) || (size_t)size != n) return;
-  auto it = e.adam.find(std::make_tuple(layer_idx, tensor_type, is_variance ? 1 : 0));
-  if (it == e.adam.end())
-    std::fill(raw, raw + n, 0.0f);  // fresh moments are zero (allocShared0)
-  else
-    std::copy(it->second.begin(), it->second.end(), raw);
+  train_tensor_copy(state, is_variance ? 2 : 1, layer_idx, tensor_type, raw, size, false);
 }
 
-extern "C" float cortex_train_step(void *, int *, int *, int, float) {
-  set_error("cortex_train_step: training is not part of this library (decode engine only)");
-  return std::numeric_limits<float>::quiet_NaN();
+extern "C" void cortex_load_grad_layer(void *state, int layer_idx, int tensor_type, const float *raw, int size) {
+  train_tensor_copy(state, 0, layer_idx, tensor_type, const_cast<float *>(raw), size, true);
+}
+
+extern "C" void cortex_extract_grad_layer(void *state, int layer_idx, int tensor_type, float *raw, int size) {
+  train_tensor_copy(state, 0, layer_idx, tensor_type, raw, size, false);
+}
+
+extern "C" int cortex_train_grads(void *state, const int *raw_inputs, const int *raw_targets, int num_tokens,
+                                  float *loss) {
+  clear_error();
+  if (!state || !loss) {
+    set_error("cortex_train_grads: NULL state or loss");
+    return -1;
+  }
+  Engine &e = *static_cast<Engine *>(state);
+  const int act = std::min(num_tokens, e.d.ctx);  // core/cortex.nim:566-567
+  *loss = 0.0f;
+  if (act <= 0) return 0;
+  if (!raw_inputs || !raw_targets) {
+    set_error("cortex_train_grads: NULL token arrays");
+    return -1;
+  }
+  DeviceGuard g(e.device);
+  const int rc = train_grads(e, raw_inputs, raw_targets, act, loss);
+  return rc ? rc : check_device_error(e);
+}
+
+extern "C" int cortex_train_apply(void *state, float lr, float scale) {
+  clear_error();
+  if (!state) {
+    set_error("cortex_train_apply: NULL state");
+    return -1;
+  }
+  Engine &e = *static_cast<Engine *>(state);
+  DeviceGuard g(e.device);
+  if (train_apply(e, lr, scale)) return -1;
+  return refresh_bf16(e);  // the tensor-core copies follow the updated weights
+}
+
+extern "C" int cortex_train_info(void *state, int *adam_steps, float *clip_factor, float *grad_norm, int *clipped) {
+  if (!state) return -1;
+  Engine &e = *static_cast<Engine *>(state);
+  DeviceGuard g(e.device);
+  float f = 0.f, n = 0.f;
+  int a = 0;
+  const int rc = train_clip_info(e, &f, &n, &a);
+  if (adam_steps) *adam_steps = train_adam_steps(e);
+  if (rc) return -1;
+  if (clip_factor) *clip_factor = f;
+  if (grad_norm) *grad_norm = n;
+  if (clipped) *clipped = a;
+  return 0;
+}
+
+// core/cortex.nim:565-822: gradients, clip, Adam; the mean loss.
+extern "C" float cortex_train_step(void *state, int *raw_inputs, int *raw_targets, int num_tokens, float lr) {
+  if (!state) {
+    set_error("cortex_train_step: NULL state");
+    return std::numeric_limits<float>::quiet_NaN();
+  }
+  Engine &e = *static_cast<Engine *>(state);
+  const int act = std::min(num_tokens, e.d.ctx);
+  if (act <= 0) return 0.0f;  // :567
+  float loss = 0.0f;
+  int rc = cortex_train_grads(state, raw_inputs, raw_targets, num_tokens, &loss);
+  if (rc == 0) rc = cortex_train_apply(state, lr, (float)act);
+  if (rc == 0) {
+    DeviceGuard g(e.device);
+    if (cudaStreamSynchronize(e.stream) != cudaSuccess) {
+      set_error("cortex_train_step: %s", cudaGetErrorString(cudaGetLastError()));
+      rc = -1;
+    } else {
+      rc = check_device_error(e);
+    }
+  }
+  if (rc != 0) {
+    fprintf(stderr, "libcortex: cortex_train_step failed: %s\n", g_err.c_str());
+    return std::numeric_limits<float>::quiet_NaN();
+  }
+  return loss;
 }
 
 // ============================================================================

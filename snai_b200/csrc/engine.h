@@ -95,6 +95,8 @@ struct PassLayer {
   const float *rms_att, *rms_ffn, *wqkv, *wo, *wup, *wdown;
 };
 
+struct TrainState;  // train.cu
+
 struct Engine {
   Dims d;
   int device = 0;
@@ -175,7 +177,7 @@ struct Engine {
   // host mirrors
   std::vector<int> pos;            // per slot
   std::vector<char> logits_valid;  // per slot
-  std::map<std::tuple<int, int, int>, std::vector<float>> adam;  // (layer, type, is_v)
+  TrainState *train = nullptr;     // gradients, Adam moments, training activations (made on first use)
   long long launches = 0;
 
   // optional per-kernel-class timing (CUDA events on the engine stream)
@@ -269,6 +271,24 @@ int launch_merge_mean(const MergeSources &srcs, float *out, size_t count, int de
 // seeded noise in [-0.005, 0.005] elsewhere.
 int launch_upscale_tensor(const float *old, int old_r, int old_c, float *out, int new_r, int new_c, double scale,
                           uint64_t seed, uint64_t stream, int device, cudaStream_t st);
+
+// ---- training step (train.cu) ----
+// Allocates the Adam moments (zero) if they do not exist yet.
+int train_moments(Engine &e);
+// Device address of the gradient (which 0), first (1) or second (2) Adam
+// moment of the weight at w (a pointer into the weight block); allocates the
+// buffers on first use (nullptr on failure).
+float *train_tensor(Engine &e, int which, const float *w);
+// Forward, loss and backward of core/cortex.nim:565-818 for act >= 1 tokens
+// (host arrays); gradients left in the gradient block, the mean loss in
+// *loss_out (synchronises).  Returns 0 or a negative error.
+int train_grads(Engine &e, const int *tin, const int *ttg, int act, float *loss_out);
+// Global-norm clip (1.0) and one Adam step with gradient divisor `scale`,
+// queued on e.stream.  Returns 0 or a negative error.
+int train_apply(Engine &e, float lr, float scale);
+int train_clip_info(Engine &e, float *factor, float *norm, int *applied);
+int train_adam_steps(const Engine &e);
+void train_free(Engine &e);
 
 // Bounded-wait self-test (forward.cu): a kernel whose mbarrier wait never
 // completes gives up after limit_ns and records an error in e.err_d; the id

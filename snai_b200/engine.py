@@ -50,6 +50,7 @@ class Cortex:
         self.head_size = self.lib.cortex_head_size(h)
         self.heads = self.lib.cortex_num_heads(h)
         self.device = device
+        self.dim = read_header(path)["hidden_dim"] if path is not None else shape[1]
 
     def close(self):
         if self.h:
@@ -168,6 +169,60 @@ class Cortex:
                                                ctypes.byref(fl)), "cortex_profile_read")
             out[name] = (n.value, ms.value, by.value, fl.value)
         return out
+
+
+    # -- training (core/cortex.nim:565-822) ------------------------------------
+    def _tensor_size(self, layer, ttype):
+        d, v, f = self.dim, self.vocab, 4 * self.dim
+        sizes = {0: v * d, 1: v * d, 2: d, 10: d, 11: d, 12: d * d, 13: d * d, 14: d * d, 15: d * d, 16: f * d,
+                 17: f * d}
+        return sizes[ttype]
+
+    def train_step(self, inputs, targets, lr):
+        """cortex_train_step: one step on the sequence (slot 0); the mean loss."""
+        a = np.ascontiguousarray(inputs, dtype=np.int32)
+        b = np.ascontiguousarray(targets, dtype=np.int32)
+        return float(self.lib.cortex_train_step(self.h, _ptr(a), _ptr(b), len(a), float(lr)))
+
+    def train_grads(self, inputs, targets):
+        """Forward + backward only; gradients stay on the device; the mean loss."""
+        a = np.ascontiguousarray(inputs, dtype=np.int32)
+        b = np.ascontiguousarray(targets, dtype=np.int32)
+        loss = ctypes.c_float(0.0)
+        check(self.lib.cortex_train_grads(self.h, _ptr(a), _ptr(b), len(a), ctypes.byref(loss)), "cortex_train_grads")
+        return float(loss.value)
+
+    def train_apply(self, lr, scale):
+        check(self.lib.cortex_train_apply(self.h, float(lr), float(scale)), "cortex_train_apply")
+        self.synchronize()
+
+    def train_info(self):
+        steps, cf, gn, cl = ctypes.c_int(0), ctypes.c_float(0), ctypes.c_float(0), ctypes.c_int(0)
+        rc = self.lib.cortex_train_info(self.h, ctypes.byref(steps), ctypes.byref(cf), ctypes.byref(gn),
+                                        ctypes.byref(cl))
+        return {"adam_steps": steps.value, "clip_factor": cf.value, "grad_norm": gn.value, "clipped": bool(cl.value),
+                "ok": rc == 0}
+
+    def tensor(self, layer, ttype, which="weight"):
+        """A tensor by (layer, type code): which = weight, grad, m or v."""
+        n = self._tensor_size(layer, ttype)
+        out = np.zeros(n, dtype=np.float32)
+        if which == "weight":
+            self.lib.cortex_extract_layer(self.h, layer, ttype, _ptr(out), n)
+        elif which == "grad":
+            self.lib.cortex_extract_grad_layer(self.h, layer, ttype, _ptr(out), n)
+        else:
+            self.lib.cortex_extract_adam_layer(self.h, layer, ttype, which == "v", _ptr(out), n)
+        return out
+
+    def set_tensor(self, layer, ttype, values, which="weight"):
+        a = np.ascontiguousarray(values, dtype=np.float32)
+        if which == "weight":
+            self.lib.cortex_load_layer(self.h, layer, ttype, _ptr(a), a.size)
+        elif which == "grad":
+            self.lib.cortex_load_grad_layer(self.h, layer, ttype, _ptr(a), a.size)
+        else:
+            self.lib.cortex_load_adam_layer(self.h, layer, ttype, which == "v", _ptr(a), a.size)
 
 
 class CortexGroup:
@@ -302,7 +357,7 @@ class SnaiCortexBridge:
         return state
 
     def train_step(self, inputs, targets, lr):
-        """:135-151 (training is outside this library: returns NaN)."""
+        """:135-151: the last ctx tokens of the batch, one training step on the GPU."""
         n = min(len(inputs), self.ctx_size)
         if n == 0:
             return 0.0

@@ -43,7 +43,8 @@ def test_null_state_is_safe(built):
     lib.cortex_free(None)
     lib.cortex_reset_cache(None)
     assert math.isnan(lib.cortex_train_step(None, None, None, 0, 0.1))
-    assert "training" in lib.cortex_last_error().decode()
+    assert "NULL state" in lib.cortex_last_error().decode()
+    assert lib.cortex_train_apply(None, 0.1, 1.0) != 0
 
 
 @pytest.mark.skipif(gpu_available(), reason="checks the no-GPU failure path")
