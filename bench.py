@@ -628,6 +628,77 @@ def gemv_pass_line(peaks, passes=50, rows=1, pos=16, split=True, fused=False):
                          "frac": gbs / peaks["hbm"], "peak_source": f"{peaks['kind']} hbm_gbs"}}
 
 
+def train_flops(D, L, V, att_ch, M):
+    """Algorithmic FLOPs of one training step over M positions: the
+    projections forward (2 M (12 D^2 L + V D)) and twice that backward (the
+    input and the weight gradient), causal attention 2 M^2 att_ch per layer
+    forward (scores, weighted values) and 5 M^2 att_ch backward (scores
+    again, dP, dQ, dK, dV)."""
+    proj = 2.0 * M * (12.0 * D * D * L + V * D)
+    return 3.0 * proj + 7.0 * M * M * att_ch * L
+
+
+def train_line(peaks, name, steps=5, warmup=2, cpu_tokens=16):
+    """cortex_train_step on the configuration's model: one sequence of ctx
+    (1024) tokens per step, as the PHP training worker feeds it
+    (src/train_worker.php:113-145), fp32.  `value` is tokens/s by CUDA events
+    on the engine's stream around each call (host token arrays in, the loss
+    out: the call's own copies are inside); `e2e` is the same by the host
+    clock.  The CPU baseline is the oracle's step (one thread, like the
+    reference) on the first cpu_tokens tokens."""
+    import torch
+    import oracle as O
+    from snai_b200 import PREC_FP32, Cortex
+    c = CONFIGS[name]
+    D, L, H = c["D"], c["L"], c["HEADS"]
+    path = make_model(name)
+    dev = torch.device("cuda")
+    eng = Cortex(path, num_heads=H, max_seqs=1, precision=PREC_FP32)
+    stream = torch.cuda.Stream(device=dev)
+    eng.set_stream(stream.cuda_stream)
+    rng = np.random.default_rng(11)
+    M = CTX
+    seqs = [rng.integers(0, V, M + 1).astype(np.int32) for _ in range(steps + warmup)]
+    lr = 1e-4
+    losses = []
+    for i in range(warmup):
+        eng.train_step(seqs[i][:-1], seqs[i][1:], lr)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t0 = time.perf_counter()
+    for i, (a, b) in enumerate(ev):
+        x = seqs[warmup + i]
+        a.record(stream)
+        losses.append(eng.train_step(x[:-1], x[1:], lr))
+        b.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    launches = eng.launches
+    eng.close()
+    flops = train_flops(D, L, V, H * (D // H), M)
+    tflops = flops / (ms / 1e3) / 1e12
+    fp32_nominal = 148 * 128 * 2 * 1965e6 / 1e12
+    o = O.Oracle(path, num_heads=H)
+    x = seqs[0]
+    tc = time.perf_counter()
+    o.train_step(x[:cpu_tokens], x[1:cpu_tokens + 1], lr)
+    cpu_s = time.perf_counter() - tc
+    o.close()
+    return {"metric": f"training tokens/sec (d={D}, one {M}-token sequence per step)", "value": M / (ms / 1e3),
+            "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "warmup": warmup,
+            "e2e": {"value": M * steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": 2 * 4 * M,
+                    "d2h_bytes_per_step": 4, "api": "cortex_train_step (host token arrays, loss returned)"},
+            "losses": losses, "dtype": "fp32", "gpu_launches_total": launches,
+            "flops_per_step": flops, "TFLOP/s": tflops,
+            "roofline": {"bound": "fp32 FFMA (SIMT GEMMs)", "achieved": tflops, "peak": fp32_nominal,
+                         "unit": "TFLOP/s", "frac": tflops / fp32_nominal,
+                         "peak_source": "nominal: 148 SMs x 128 FFMA lanes x 2 x 1965 MHz"},
+            "config": {"workload": f"{c['model']}, V={V}, ctx {CTX}: cortex_train_step on {M} random ids per step",
+                       "lr": lr},
+            "cpu_baseline": {"value": cpu_tokens / cpu_s, "unit": "tokens/s", "cores": 1, "kind": "port",
+                             "sample": f"the oracle's training step on the first {cpu_tokens} tokens ({cpu_s:.1f} s)"}}
+
+
 def group_load_line(name, n, single_s):
     """Loads the configuration's model onto devices 0..n-1 from one process
     (cortex_group_load, one sequence slot per GPU) and reports the wall time
@@ -818,7 +889,9 @@ def our_arm(args, rank, world, local_rank):
                         ("gemv_pass_persistent", lambda p: gemv_pass_line(p, fused=True)),
                         ("gemv_pass_pos1000", lambda p: gemv_pass_line(p, pos=1000)),
                         ("gemv_pass_pos1000_unsplit", lambda p: gemv_pass_line(p, pos=1000, split=False)),
-                        ("sampling", sampling_lines)):
+                        ("sampling", sampling_lines),
+                        ("train_c2", lambda p: train_line(p, "c2")),
+                        ("train_c4", lambda p: train_line(p, "c4"))):
             try:
                 line[key] = fn(peaks)
             except Exception as ex:  # noqa: BLE001
@@ -840,6 +913,7 @@ def main():
     ap.add_argument("--sampler", action="store_true", help="only the isolated sampling workload, one line each")
     ap.add_argument("--gemm", action="store_true", help="only the projection micro-benchmark")
     ap.add_argument("--tokenizer", metavar="VOCAB_JSON", help="only the tokenizer throughput (host code)")
+    ap.add_argument("--train", action="store_true", help="only the training-step lines (c2 and c4 models)")
     ap.add_argument("--seqs", type=int, default=None,
                     help="total sequences of the decode configuration (default: the configuration's), or rows of "
                          "the projection micro-benchmark (default 4096)")
@@ -856,6 +930,11 @@ def main():
         return
     if args.tokenizer:
         print(json.dumps(tokenizer_bench(args.tokenizer)), flush=True)
+        return
+    if args.train:
+        if rank == 0:
+            for name in ("c2", "c4"):
+                print(json.dumps(train_line(load_peaks(), name, steps=args.steps, warmup=args.warmup)), flush=True)
         return
     if args.gemm:
         if args.seqs is None:

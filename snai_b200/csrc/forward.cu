@@ -1651,6 +1651,13 @@ __global__ void finish_step_kernel(const int *__restrict__ ids, int *__restrict_
   if (threadIdx.x == 0) *step = st + 1;
 }
 
+// One chunk of rows in the operand type of its path.
+static int run_chunk(Engine &e, int M, const int *tokens_d, int n_out, bool out_tc, double kv_positions, bool defer) {
+  return (tc_path(e, M) && e.precision == kBF16)
+             ? run_chunk_typed<__nv_bfloat16>(e, M, tokens_d, n_out, out_tc, kv_positions, defer)
+             : run_chunk_typed<float>(e, M, tokens_d, n_out, out_tc, kv_positions, defer);
+}
+
 int decode_step_device(Engine &e, int batch, const SampleLaunch &sampler) {
   const int tpb = 256, nb = (batch + tpb - 1) / tpb;
   stage_step_kernel<<<nb, tpb, 0, e.stream>>>(e.unif_all, e.unif_d, e.step_d, batch);
@@ -1661,8 +1668,7 @@ int decode_step_device(Engine &e, int batch, const SampleLaunch &sampler) {
   decode_rows_kernel<<<nb, tpb, 0, e.stream>>>(e.slots_d, e.seq_len_d, e.rows_d, e.outrows_d, batch);
   e.launches++;
   const bool tc = tc_path(e, batch);
-  rc = (tc && e.precision == kBF16) ? run_chunk_typed<__nv_bfloat16>(e, batch, e.ids_d, batch, tc, 0.0, true)
-                                    : run_chunk_typed<float>(e, batch, e.ids_d, batch, tc, 0.0, true);
+  rc = run_chunk(e, batch, e.ids_d, batch, tc, 0.0, true);
   if (rc) return rc;
   finish_step_kernel<<<1, 1024, 0, e.stream>>>(e.ids_d, e.ids_all, e.step_d, batch);
   e.launches++;
@@ -1702,11 +1708,8 @@ int run_rows(Engine &e, const RowDesc *rows, int n, const int *tokens_d) {
       set_error("row upload failed: %s", cudaGetErrorString(cudaGetLastError()));
       return -4;
     }
-    const bool tc = tc_path(e, M);
     const bool out_tc = tc_path(e, n_out);
-    const int rc = (tc && e.precision == kBF16)
-                       ? run_chunk_typed<__nv_bfloat16>(e, M, tokens_d, n_out, out_tc, kv_positions, defer)
-                       : run_chunk_typed<float>(e, M, tokens_d, n_out, out_tc, kv_positions, defer);
+    const int rc = run_chunk(e, M, tokens_d, n_out, out_tc, kv_positions, defer);
     if (rc) return rc;
     const cudaError_t le = cudaGetLastError();
     if (le != cudaSuccess) {

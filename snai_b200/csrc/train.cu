@@ -472,36 +472,77 @@ __global__ void __launch_bounds__(kRowThreads) snai_train_rmsnorm_bwd(const floa
   }
 }
 
-// g[d] = sum over rows i = M-1 .. 0 of gprod[i][d], in that order (the
-// reference accumulates while walking the positions backwards, :650).
-__global__ void snai_train_colsum(const float *__restrict__ gprod, int M, int D, float *__restrict__ g) {
+// g[d] = sum over rows i of gprod[i][d] (the RMSNorm weight gradient summed
+// over positions), deterministic in two launches: CTA (c, r) sums the rows of
+// chunk r for 32 columns (8 row slices combined in slice order) into
+// part[r][d]; then the chunks are added in chunk order.
+constexpr int kColChunks = 32;
+
+__global__ void __launch_bounds__(256) snai_train_colsum_part(const float *__restrict__ gprod, int M, int D,
+                                                             float *__restrict__ part) {
+  __shared__ float red[8][33];
+  const int d = blockIdx.x * 32 + threadIdx.x, r = blockIdx.y;
+  const int rows = (M + kColChunks - 1) / kColChunks, i0 = r * rows, i1 = min(M, i0 + rows);
+  float s = 0.f;
+  if (d < D)
+    for (int i = i0 + threadIdx.y; i < i1; i += 8) s = __fadd_rn(s, gprod[(size_t)i * D + d]);
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && d < D) {
+    float t = 0.f;
+    for (int y = 0; y < 8; ++y) t = __fadd_rn(t, red[y][threadIdx.x]);
+    part[(size_t)r * D + d] = t;
+  }
+}
+
+__global__ void snai_train_colsum_fin(const float *__restrict__ part, int D, float *__restrict__ g) {
   const int d = blockIdx.x * blockDim.x + threadIdx.x;
   if (d >= D) return;
   float s = 0.f;
-  for (int i = M - 1; i >= 0; --i) s = __fadd_rn(s, gprod[(size_t)i * D + d]);
+#pragma unroll 8
+  for (int r = 0; r < kColChunks; ++r) s = __fadd_rn(s, part[(size_t)r * D + d]);
   g[d] = s;
 }
 
-// g_emb[tok] += dh[i] over positions i in descending order (:817-818).  The
-// CTA of position i works only if i is the last position holding its token;
-// it then sums that token's rows from i down to 0 in order.
-__global__ void __launch_bounds__(kRowThreads) snai_train_emb_grad(const float *__restrict__ dh, const int *__restrict__ tok,
-                                                                  int act, int V, int D, float *__restrict__ gemb) {
-  __shared__ int later;
-  const int i = blockIdx.x;
+// Token links of the sequence: prev[i] = the last position j < i holding the
+// same (clamped) token, or -1; last[i] = 1 when no later position holds it.
+__global__ void snai_train_tok_links(const int *__restrict__ tok, int act, int V, int *__restrict__ prev,
+                                     int *__restrict__ last) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= act) return;
   auto clamp = [&](int t) { return (t < 0 || t >= V) ? 0 : t; };
   const int t = clamp(tok[i]);
-  if (threadIdx.x == 0) later = 0;
-  __syncthreads();
-  for (int j = i + 1 + threadIdx.x; j < act; j += kRowThreads)
-    if (clamp(tok[j]) == t) later = 1;
-  __syncthreads();
-  if (later) return;
+  int p = -1;
+  for (int j = i - 1; j >= 0; --j)
+    if (clamp(tok[j]) == t) {
+      p = j;
+      break;
+    }
+  prev[i] = p;
+  int l = 1;
+  for (int j = i + 1; j < act; ++j)
+    if (clamp(tok[j]) == t) {
+      l = 0;
+      break;
+    }
+  last[i] = l;
+}
+
+// g_emb[tok] += dh[i] over positions i in descending order (:817-818): the
+// CTA of the last position holding a token walks that token's positions
+// backwards through prev and sums their rows in that order.
+__global__ void __launch_bounds__(kRowThreads) snai_train_emb_grad(const float *__restrict__ dh, const int *__restrict__ tok,
+                                                                  const int *__restrict__ prev,
+                                                                  const int *__restrict__ last, int V, int D,
+                                                                  float *__restrict__ gemb) {
+  const int i = blockIdx.x;
+  if (!last[i]) return;
+  int t = tok[i];
+  if (t < 0 || t >= V) t = 0;
   float *g = gemb + (size_t)t * D;
   for (int k = threadIdx.x; k < D; k += kRowThreads) {
     float s = g[k];
-    for (int j = i; j >= 0; --j)
-      if (clamp(tok[j]) == t) s = __fadd_rn(s, dh[(size_t)j * D + k]);
+    for (int j = i; j >= 0; j = prev[j]) s = __fadd_rn(s, dh[(size_t)j * D + k]);
     g[k] = s;
   }
 }
@@ -608,7 +649,8 @@ struct TrainState {
   std::vector<float *> hid, na, qkv, att, hf, nf, fin, fout;
   float *nfinal = nullptr, *probs = nullptr, *S = nullptr, *dP = nullptr;
   float *dh = nullptr, *dn = nullptr, *dffn = nullptr, *datt = nullptr, *dqkv = nullptr, *gprod = nullptr;
-  float *loss_rows = nullptr, *loss = nullptr, *clip = nullptr;
+  float *loss_rows = nullptr, *loss = nullptr, *clip = nullptr, *colpart = nullptr;
+  int *prev = nullptr, *last = nullptr;
   double *clip_part = nullptr;
 };
 
@@ -715,6 +757,7 @@ static int train_alloc(Engine &e) {
   items.push_back({&t.loss_rows, C});
   items.push_back({&t.loss, 4});
   items.push_back({&t.clip, 4});
+  items.push_back({&t.colpart, (size_t)kColChunks * D});
   size_t off = 0;
   std::vector<size_t> offs;
   for (auto &it : items) {
@@ -722,7 +765,7 @@ static int train_alloc(Engine &e) {
     off = align256(off + it.second * sizeof(float));
   }
   const size_t tok_off = off;
-  off = align256(off + 2 * C * sizeof(int));
+  off = align256(off + 4 * C * sizeof(int));
   const size_t part_off = off;
   off = align256(off + kClipBlocks * sizeof(double));
   if (cudaMalloc(&t.act, off) != cudaSuccess || cudaMalloc(&t.grad, e.wblock_bytes) != cudaSuccess) {
@@ -736,6 +779,8 @@ static int train_alloc(Engine &e) {
   for (size_t i = 0; i < items.size(); ++i) *items[i].first = reinterpret_cast<float *>(base + offs[i]);
   t.tin = reinterpret_cast<int *>(base + tok_off);
   t.ttg = t.tin + C;
+  t.prev = t.ttg + C;
+  t.last = t.prev + C;
   t.clip_part = reinterpret_cast<double *>(base + part_off);
   t.g = static_cast<float *>(t.grad);
   // zero everything once: columns never written (q/k/v/att channels past
@@ -829,12 +874,16 @@ int train_grads(Engine &e, const int *tin, const int *ttg, int act, float *loss_
 
   // ---------------- backward ----------------
   auto G = [&](const float *w) { return mirror(e, t.grad, w); };
-  const int cs_blocks = (D + 255) / 256;
+  auto colsum = [&](float *g) {
+    snai_train_colsum_part<<<dim3((D + 31) / 32, kColChunks), dim3(32, 8), 0, st>>>(t.gprod, M, D, t.colpart);
+    snai_train_colsum_fin<<<(D + 255) / 256, 256, 0, st>>>(t.colpart, D, g);
+    e.launches += 2;
+  };
   rc |= gemm<true, false>(e, args(M, D, V, t.probs, t.Vp, e.w_out, D), 1, EpiStore{t.dn, D, 0}, true);
   rc |= gemm<false, false>(e, args(V, D, M, t.probs, t.Vp, t.nfinal, D), 1, EpiStore{G(e.w_out), D, 0}, true);
   snai_train_rmsnorm_bwd<<<M, kRowThreads, 0, st>>>(t.dn, t.hid[L], e.rms_final, D, t.dh, 1, t.gprod);
-  snai_train_colsum<<<cs_blocks, 256, 0, st>>>(t.gprod, M, D, G(e.rms_final));
-  e.launches += 2;
+  e.launches++;
+  colsum(G(e.rms_final));
   for (int l = L - 1; l >= 0; --l) {
     const LayerWeights &w = e.layers[l];
     // MLP
@@ -843,8 +892,8 @@ int train_grads(Engine &e, const int *tin, const int *ttg, int act, float *loss_
     rc |= gemm<true, false>(e, args(M, D, F, t.dffn, F, w.wup, D), 1, EpiStore{t.dn, D, 0}, true);
     rc |= gemm<false, false>(e, args(F, D, M, t.dffn, F, t.nf[l], D), 1, EpiStore{G(w.wup), D, 0}, true);
     snai_train_rmsnorm_bwd<<<M, kRowThreads, 0, st>>>(t.dn, t.hf[l], w.rms_ffn, D, t.dh, 0, t.gprod);
-    snai_train_colsum<<<cs_blocks, 256, 0, st>>>(t.gprod, M, D, G(w.rms_ffn));
-    e.launches += 2;
+    e.launches++;
+    colsum(G(w.rms_ffn));
     // Wo
     rc |= gemm<true, false>(e, args(M, D, D, t.dh, D, w.wo, D), 1, EpiStore{t.datt, D, 0}, true);
     rc |= gemm<false, false>(e, args(D, D, M, t.dh, D, t.att[l], D), 1, EpiStore{G(w.wo), D, 0}, true);
@@ -869,11 +918,12 @@ int train_grads(Engine &e, const int *tin, const int *ttg, int act, float *loss_
     rc |= gemm<true, false>(e, args(M, D, 3 * D, t.dqkv, D3, w.wqkv, D), 1, EpiStore{t.dn, D, 0}, true);
     rc |= gemm<false, false>(e, args(3 * D, D, M, t.dqkv, D3, t.na[l], D), 1, EpiStore{G(w.wqkv), D, 0}, true);
     snai_train_rmsnorm_bwd<<<M, kRowThreads, 0, st>>>(t.dn, t.hid[l], w.rms_att, D, t.dh, 0, t.gprod);
-    snai_train_colsum<<<cs_blocks, 256, 0, st>>>(t.gprod, M, D, G(w.rms_att));
-    e.launches += 2;
+    e.launches++;
+    colsum(G(w.rms_att));
   }
-  snai_train_emb_grad<<<M, kRowThreads, 0, st>>>(t.dh, t.tin, M, V, D, G(e.emb));
-  e.launches++;
+  snai_train_tok_links<<<(M + 127) / 128, 128, 0, st>>>(t.tin, M, V, t.prev, t.last);
+  snai_train_emb_grad<<<M, kRowThreads, 0, st>>>(t.dh, t.tin, t.prev, t.last, V, D, G(e.emb));
+  e.launches += 2;
   if (rc || launch_rc("training backward")) return -1;
   if (cudaMemcpyAsync(loss_out, t.loss, sizeof(float), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
       cudaStreamSynchronize(st) != cudaSuccess) {

@@ -27,7 +27,7 @@ from snai_b200 import PREC_BF16, PREC_FP32, Cortex, SnaiCortexBridge, load  # no
 from conftest import make_model, rel_err  # noqa: E402
 
 TYPES = (10, 11, 12, 13, 14, 15, 16, 17)
-GRAD_TOL = 1e-4   # max |gpu - oracle| / max |oracle| per gradient tensor (fp32, different summation order)
+GRAD_TOL = 2e-5   # max |gpu - oracle| / max |oracle| per gradient tensor (fp32, different summation order; 2.5e-6 measured)
 LOSS_TOL = 2e-5   # relative, mean loss
 
 
@@ -120,12 +120,17 @@ def test_adam_with_clip(model_dir, built):
     o.train_apply(0.01, 5.0)
     info = e.train_info()
     assert info["clipped"] and info["grad_norm"] > 1
+    # the reference sums the 3.7 M squares sequentially in fp32, the GPU in
+    # double: the clip factors differ by about 1e-5 relative, m follows it
+    # and v its square; a weight moves by lr * x / (x + 1e-8), x = |clipped
+    # gradient| / scale, so only gradients near 1e-8 feel the factor: at most
+    # about lr * 1e-5 (the weights' atol below is lr * 2e-4)
     for k in keys(2):
         for which in ("m", "v"):
             a, b = e.tensor(k[0], k[1], which), o.tensor(k[0], k[1], which)
-            assert np.allclose(a, b, rtol=1e-5, atol=0), (k, which)
+            assert np.allclose(a, b, rtol=1e-4, atol=0), (k, which)
         a, b = e.tensor(k[0], k[1]), o.tensor(k[0], k[1])
-        assert np.allclose(a, b, rtol=1e-6, atol=1e-9), k
+        assert np.allclose(a, b, rtol=1e-6, atol=0.01 * 2e-4), (k, float(np.abs(a - b).max()))
     e.close()
     o.close()
 
