@@ -638,22 +638,24 @@ def train_flops(D, L, V, att_ch, M):
     return 3.0 * proj + 7.0 * M * M * att_ch * L
 
 
-def train_line(peaks, name, steps=5, warmup=2, cpu_tokens=16):
+def train_line(peaks, name, steps=5, warmup=2, cpu_tokens=16, tf32=False):
     """cortex_train_step on the configuration's model: one sequence of ctx
     (1024) tokens per step, as the PHP training worker feeds it
     (src/train_worker.php:113-145), fp32.  `value` is tokens/s by CUDA events
     on the engine's stream around each call (host token arrays in, the loss
     out: the call's own copies are inside); `e2e` is the same by the host
     clock.  The CPU baseline is the oracle's step (one thread, like the
-    reference) on the first cpu_tokens tokens."""
+    reference) on the first cpu_tokens tokens.  tf32: a TF32 engine, whose
+    projection GEMMs run on the tensor cores (the attention products stay
+    fp32 SIMT)."""
     import torch
     import oracle as O
-    from snai_b200 import PREC_FP32, Cortex
+    from snai_b200 import PREC_FP32, PREC_TF32, Cortex
     c = CONFIGS[name]
     D, L, H = c["D"], c["L"], c["HEADS"]
     path = make_model(name)
     dev = torch.device("cuda")
-    eng = Cortex(path, num_heads=H, max_seqs=1, precision=PREC_FP32)
+    eng = Cortex(path, num_heads=H, max_seqs=1, precision=PREC_TF32 if tf32 else PREC_FP32)
     stream = torch.cuda.Stream(device=dev)
     eng.set_stream(stream.cuda_stream)
     rng = np.random.default_rng(11)
@@ -678,6 +680,14 @@ def train_line(peaks, name, steps=5, warmup=2, cpu_tokens=16):
     flops = train_flops(D, L, V, H * (D // H), M)
     tflops = flops / (ms / 1e3) / 1e12
     fp32_nominal = 148 * 128 * 2 * 1965e6 / 1e12
+    if tf32:
+        # dense TF32 tensor peak: half the measured bf16 GEMM peak (no TF32 figure is measured here)
+        roof = {"bound": "tensor (TF32 projections) + fp32 SIMT attention", "achieved": tflops,
+                "peak": peaks["bf16"] / 2, "unit": "TFLOP/s", "frac": tflops / (peaks["bf16"] / 2),
+                "peak_source": f"half the {peaks['kind']} bf16 GEMM peak"}
+    else:
+        roof = {"bound": "fp32 FFMA (SIMT GEMMs)", "achieved": tflops, "peak": fp32_nominal, "unit": "TFLOP/s",
+                "frac": tflops / fp32_nominal, "peak_source": "nominal: 148 SMs x 128 FFMA lanes x 2 x 1965 MHz"}
     o = O.Oracle(path, num_heads=H)
     x = seqs[0]
     tc = time.perf_counter()
@@ -688,11 +698,8 @@ def train_line(peaks, name, steps=5, warmup=2, cpu_tokens=16):
             "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "warmup": warmup,
             "e2e": {"value": M * steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": 2 * 4 * M,
                     "d2h_bytes_per_step": 4, "api": "cortex_train_step (host token arrays, loss returned)"},
-            "losses": losses, "dtype": "fp32", "gpu_launches_total": launches,
-            "flops_per_step": flops, "TFLOP/s": tflops,
-            "roofline": {"bound": "fp32 FFMA (SIMT GEMMs)", "achieved": tflops, "peak": fp32_nominal,
-                         "unit": "TFLOP/s", "frac": tflops / fp32_nominal,
-                         "peak_source": "nominal: 148 SMs x 128 FFMA lanes x 2 x 1965 MHz"},
+            "losses": losses, "dtype": "tf32 projections, fp32 otherwise" if tf32 else "fp32",
+            "gpu_launches_total": launches, "flops_per_step": flops, "TFLOP/s": tflops, "roofline": roof,
             "config": {"workload": f"{c['model']}, V={V}, ctx {CTX}: cortex_train_step on {M} random ids per step",
                        "lr": lr},
             "cpu_baseline": {"value": cpu_tokens / cpu_s, "unit": "tokens/s", "cores": 1, "kind": "port",
@@ -891,7 +898,8 @@ def our_arm(args, rank, world, local_rank):
                         ("gemv_pass_pos1000_unsplit", lambda p: gemv_pass_line(p, pos=1000, split=False)),
                         ("sampling", sampling_lines),
                         ("train_c2", lambda p: train_line(p, "c2")),
-                        ("train_c4", lambda p: train_line(p, "c4"))):
+                        ("train_c4", lambda p: train_line(p, "c4")),
+                        ("train_c4_tf32", lambda p: train_line(p, "c4", tf32=True))):
             try:
                 line[key] = fn(peaks)
             except Exception as ex:  # noqa: BLE001
@@ -933,8 +941,9 @@ def main():
         return
     if args.train:
         if rank == 0:
-            for name in ("c2", "c4"):
-                print(json.dumps(train_line(load_peaks(), name, steps=args.steps, warmup=args.warmup)), flush=True)
+            for name, tf32 in (("c2", False), ("c4", False), ("c2", True), ("c4", True)):
+                print(json.dumps(train_line(load_peaks(), name, steps=args.steps, warmup=args.warmup, tf32=tf32)),
+                      flush=True)
         return
     if args.gemm:
         if args.seqs is None:

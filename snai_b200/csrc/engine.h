@@ -289,6 +289,10 @@ int train_apply(Engine &e, float lr, float scale);
 int train_clip_info(Engine &e, float *factor, float *norm, int *applied);
 int train_adam_steps(const Engine &e);
 void train_free(Engine &e);
+struct EpiTrain;  // epilogue.cuh
+// C[M, N] = A[M, K] W[N, K]^T on the TF32 tensor cores with a training
+// epilogue (forward.cu).  Returns 0 or a negative error.
+int train_gemm_tc(Engine &e, int M, int N, int K, const float *A, const float *W, const EpiTrain &epi);
 
 // Bounded-wait self-test (forward.cu): a kernel whose mbarrier wait never
 // completes gives up after limit_ns and records an error in e.err_d; the id

@@ -306,4 +306,69 @@ struct EpiLogits {
   }
 };
 
+// ---- the training step's products on the tensor cores (train.cu) ----
+//
+// C = acc, C = R + acc (a residual into a new buffer), the MLP's SiLU (fin =
+// acc and fout = SiLU(acc)) and its derivative (C = acc * s (1 + x (1 - s)),
+// s = 1 / (1 + exp(-x)), x = fin; core/cortex.nim:678-681), row-major with
+// leading dimension ld, in the reference's float operations.
+struct EpiTrain {
+  enum Kind { kStore = 0, kAdd = 1, kSilu = 2, kSiluBack = 3 };
+  int kind;
+  float *C;         // output (fin for kSilu)
+  float *C2;        // fout (kSilu)
+  const float *R;   // residual (kAdd) or fin (kSiluBack)
+  long long ld;
+  static constexpr bool kTmaReduce = false;
+  static constexpr bool kTmaStore = false;
+  using Pre = float4;
+  struct Row {};
+  __device__ __forceinline__ Row row(int) const { return Row{}; }
+  __device__ __forceinline__ void prefetch(int, int, int) const {}
+  __device__ __forceinline__ Pre load4(int m, int n, int cnt) const {
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (kind == kAdd || kind == kSiluBack) {
+      const float *p = R + (size_t)m * ld + n;
+      if (cnt == 4 && (ld & 3) == 0) return __ldg(reinterpret_cast<const float4 *>(p));
+      r.x = p[0];
+      if (cnt > 1) r.y = p[1];
+      if (cnt > 2) r.z = p[2];
+      if (cnt > 3) r.w = p[3];
+    }
+    return r;
+  }
+  __device__ static __forceinline__ float silu(float x) {
+    return __fmul_rn(x, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))));
+  }
+  __device__ static __forceinline__ float silu_back(float d, float x) {
+    const float s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+    return __fmul_rn(d, __fmul_rn(s, __fadd_rn(1.0f, __fmul_rn(x, __fsub_rn(1.0f, s)))));
+  }
+  __device__ __forceinline__ void store4(int m, int n, float4 v, int cnt, Pre pre, Row) const {
+    float a[4] = {v.x, v.y, v.z, v.w};
+    const float r[4] = {pre.x, pre.y, pre.z, pre.w};
+    float b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (kind == kAdd) a[i] = __fadd_rn(r[i], a[i]);
+      if (kind == kSiluBack) a[i] = silu_back(a[i], r[i]);
+      b[i] = kind == kSilu ? silu(a[i]) : 0.f;
+    }
+    float *p = C + (size_t)m * ld + n;
+    float *q = C2 + (size_t)m * ld + n;
+    if (cnt == 4 && (ld & 3) == 0) {
+      *reinterpret_cast<float4 *>(p) = make_float4(a[0], a[1], a[2], a[3]);
+      if (kind == kSilu) *reinterpret_cast<float4 *>(q) = make_float4(b[0], b[1], b[2], b[3]);
+      return;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (i < cnt) {
+        p[i] = a[i];
+        if (kind == kSilu) q[i] = b[i];
+      }
+  }
+  __device__ __forceinline__ void store(int, int, const float *, int) const {}
+};
+
 }  // namespace snai

@@ -1325,6 +1325,14 @@ static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *
   return launch_tcp<TIn, 64>(e, M, N, K, A, W, epi);
 }
 
+// A product of the training step on the TF32 tensor cores: C[M, N] =
+// A[M, K] * W[N, K]^T, both fp32 and K-major (rows 16-byte aligned), with the
+// training epilogue.
+int train_gemm_tc(Engine &e, int M, int N, int K, const float *A, const float *W, const EpiTrain &epi) {
+  if (M <= 0 || N <= 0) return 0;
+  return launch_tc<float>(e, M, N, K, A, W, epi);
+}
+
 // Launches kern on the engine's stream; with pdl as a programmatic dependent
 // launch (the kernel begins with grid_dep_wait before it reads anything the
 // previous kernel writes).

@@ -46,6 +46,7 @@
 
 #include "common.cuh"
 #include "engine.h"
+#include "epilogue.cuh"
 
 namespace snai {
 
@@ -78,6 +79,7 @@ struct GemmArgs {
   const float *B;
   long long ldb, sB;
   int causal;
+  int splits = 1, kchunk = 0;  // split-K: blockIdx.z = batch * splits + split; split s takes k in [s kchunk, (s+1) kchunk)
 };
 
 // Stores v[0..cnt) at p (a float4 store when it can).
@@ -89,7 +91,7 @@ __device__ __forceinline__ void store_run(float *p, const float *v, int cnt) {
   }
 }
 
-struct EpiStore {  // C = acc
+struct SimtStore {  // C = acc
   float *C;
   long long ldc, sC;
   __device__ __forceinline__ void operator()(int z, int m, int n, const float *v, int cnt) const {
@@ -97,7 +99,7 @@ struct EpiStore {  // C = acc
   }
 };
 
-struct EpiAdd {  // C = R + acc (a residual into a new buffer)
+struct SimtAdd {  // C = R + acc (a residual into a new buffer)
   float *C;
   const float *R;
   long long ld;
@@ -110,7 +112,7 @@ struct EpiAdd {  // C = R + acc (a residual into a new buffer)
 };
 
 // fin = acc, fout = fin * (1 / (1 + exp(-fin)))  (core/cortex.nim:624-627)
-struct EpiSilu {
+struct SimtSilu {
   float *fin, *fout;
   long long ld;
   __device__ __forceinline__ void operator()(int, int m, int n, const float *v, int cnt) const {
@@ -122,7 +124,7 @@ struct EpiSilu {
 };
 
 // dffn = acc * (sig * (1 + x * (1 - sig))), sig = 1 / (1 + exp(-x)), x = fin  (:678-681)
-struct EpiSiluBack {
+struct SimtSiluBack {
   float *C;
   const float *X;
   long long ld;
@@ -143,14 +145,19 @@ template <bool A_KC, bool B_KC, bool VEC, class Epi>
 __global__ void __launch_bounds__(kGThreads, 2) snai_train_sgemm(const GemmArgs g, const Epi epi) {
   __shared__ __align__(16) float As[2][kGBK][kGLd];
   __shared__ __align__(16) float Bs[2][kGBK][kGLd];
-  const int z = blockIdx.z;
+  const int z = blockIdx.z;  // the epilogue's batch index (batch * splits + split when split)
+  const int zb = z / g.splits, sp = z % g.splits;
   const int m0 = blockIdx.y * kGBM, n0 = blockIdx.x * kGBN;
   if (g.causal == 1 && n0 > m0 + kGBM - 1) return;
-  const float *__restrict__ A = g.A + z * g.sA;
-  const float *__restrict__ B = g.B + z * g.sB;
+  const float *__restrict__ A = g.A + zb * g.sA;
+  const float *__restrict__ B = g.B + zb * g.sB;
   int kb = 0, ke = g.K;
   if (g.causal == 2) ke = min(g.K, m0 + kGBM);
   if (g.causal == 3) kb = min(m0, g.K);
+  if (g.splits > 1) {  // kchunk is a multiple of kGBK, so every split starts on a tile
+    kb = max(kb, sp * g.kchunk);
+    ke = min(ke, (sp + 1) * g.kchunk);
+  }
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
 
   // one float4 (or four scalars) per operand per k step
@@ -248,6 +255,29 @@ __global__ void __launch_bounds__(kGThreads, 2) snai_train_sgemm(const GemmArgs 
       const int cnt = min(4, g.N - n);
       epi(z, m, n, &acc[i][h * 4], cnt);
     }
+  }
+}
+
+// Split-K: C = sum over splits s of P[z][s] (in split order), then the
+// GEMM's epilogue; P is [batch][splits][M][N].
+template <class Epi>
+__global__ void __launch_bounds__(256) snai_train_splitk_reduce(const float *__restrict__ P, int splits, int M, int N,
+                                                               int batch, const Epi epi) {
+  const int N4 = (N + 3) / 4;
+  const long long total = (long long)batch * M * N4;
+  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
+    const int z = (int)(i / ((long long)M * N4));
+    const long long r = i % ((long long)M * N4);
+    const int m = (int)(r / N4), n = (int)(r % N4) * 4;
+    const int cnt = min(4, N - n);
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < splits; ++s) {
+      const float *p = P + (((size_t)z * splits + s) * M + m) * (size_t)N + n;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j < cnt) v[j] = __fadd_rn(v[j], p[j]);
+    }
+    epi(z, m, n, v, cnt);
   }
 }
 
@@ -558,6 +588,24 @@ __global__ void snai_train_kv_publish(const float *__restrict__ qkv, long long l
   }
 }
 
+// out[c][r] = in[r][c] for r < R, c < C, and out[c][r] = 0 for R <= r < Rp:
+// the K-major operands of the tensor-core form of the NN and TN products
+// (32 x 32 tiles through shared memory, both sides coalesced).
+__global__ void __launch_bounds__(256) snai_train_transpose(const float *__restrict__ in, long long ldi, int R, int C,
+                                                           float *__restrict__ out, int Rp) {
+  __shared__ float t[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int y = threadIdx.y; y < 32; y += 8) {
+    const int r = r0 + y, c = c0 + threadIdx.x;
+    t[y][threadIdx.x] = (r < R && c < C) ? in[(long long)r * ldi + c] : 0.f;
+  }
+  __syncthreads();
+  for (int y = threadIdx.y; y < 32; y += 8) {
+    const int c = c0 + y, r = r0 + threadIdx.x;
+    if (c < C && r < Rp) out[(long long)c * Rp + r] = t[threadIdx.x][y];
+  }
+}
+
 // ============================================================================
 // global-norm clip and Adam over the whole gradient block
 // ============================================================================
@@ -652,7 +700,12 @@ struct TrainState {
   float *loss_rows = nullptr, *loss = nullptr, *clip = nullptr, *colpart = nullptr;
   int *prev = nullptr, *last = nullptr;
   double *clip_part = nullptr;
+  // tensor-core engines (TF32 / BF16): transposed operands of the NN and TN
+  // products -- a weight W^T, dY^T and X^T with the positions padded to Mp
+  float *wt = nullptr, *yt = nullptr, *xt = nullptr;
+  float *split = nullptr;  // split-K partials
 };
+constexpr size_t kSplitFloats = size_t(16) << 20;  // 64 MB of split-K partials
 
 namespace {
 
@@ -675,12 +728,40 @@ int launch_rc(const char *what) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// One GEMM launch; VEC when every operand row start is 16-byte aligned.
+// One GEMM launch; VEC when every operand row start is 16-byte aligned.  A
+// grid of fewer tiles than twice the SMs with a long k range is split over k
+// (partials in `split`, summed in split order by a second launch that runs
+// the epilogue), so that every SM gets work.
 template <bool A_KC, bool B_KC, class Epi>
-int gemm(Engine &e, const GemmArgs &g, int batch, const Epi &epi, bool vec) {
+int gemm(Engine &e, const GemmArgs &g0, int batch, const Epi &epi, bool vec) {
+  GemmArgs g = g0;
   if (g.M <= 0 || g.N <= 0) return 0;
-  const dim3 grid((g.N + kGBN - 1) / kGBN, (g.M + kGBM - 1) / kGBM, batch);
+  const int gx = (g.N + kGBN - 1) / kGBN, gy = (g.M + kGBM - 1) / kGBM;
   vec = vec && aligned16(g.A) && aligned16(g.B) && g.lda % 4 == 0 && g.ldb % 4 == 0 && g.sA % 4 == 0 && g.sB % 4 == 0;
+  const long long tiles = (long long)gx * gy * batch;
+  const int sms = device_sm_count(e.device);
+  int splits = 1;
+  if (e.train && e.train->split && g.causal != 1 && tiles < 2 * sms && g.K >= 1024) {
+    splits = (int)std::min<long long>({(2 * sms + tiles - 1) / tiles, (long long)g.K / 512,
+                                       (long long)(kSplitFloats / ((size_t)batch * g.M * g.N))});
+    if (splits < 2) splits = 1;
+  }
+  if (splits > 1) {
+    g.splits = splits;
+    g.kchunk = ((g.K + splits - 1) / splits + kGBK - 1) / kGBK * kGBK;
+    const SimtStore part{e.train->split, (long long)g.N, (long long)g.M * g.N};
+    const dim3 grid(gx, gy, batch * splits);
+    if (vec)
+      snai_train_sgemm<A_KC, B_KC, true, SimtStore><<<grid, kGThreads, 0, e.stream>>>(g, part);
+    else
+      snai_train_sgemm<A_KC, B_KC, false, SimtStore><<<grid, kGThreads, 0, e.stream>>>(g, part);
+    const long long n4 = (long long)batch * g.M * ((g.N + 3) / 4);
+    const int rb = (int)std::min<long long>((n4 + 255) / 256, (long long)sms * 8);
+    snai_train_splitk_reduce<Epi><<<rb, 256, 0, e.stream>>>(e.train->split, splits, g.M, g.N, batch, epi);
+    e.launches += 2;
+    return launch_rc("training GEMM");
+  }
+  const dim3 grid(gx, gy, batch);
   if (vec)
     snai_train_sgemm<A_KC, B_KC, true, Epi><<<grid, kGThreads, 0, e.stream>>>(g, epi);
   else
@@ -758,6 +839,13 @@ static int train_alloc(Engine &e) {
   items.push_back({&t.loss, 4});
   items.push_back({&t.clip, 4});
   items.push_back({&t.colpart, (size_t)kColChunks * D});
+  items.push_back({&t.split, kSplitFloats});
+  if (e.precision != kFP32) {
+    const size_t Cp = (C + 3) / 4 * 4, Nmax = (std::max({(size_t)d.V, 3 * D, F}) + 3) / 4 * 4;
+    items.push_back({&t.wt, Nmax * std::max(D, F)});
+    items.push_back({&t.yt, Nmax * Cp});
+    items.push_back({&t.xt, std::max(D, F) * Cp});
+  }
   size_t off = 0;
   std::vector<size_t> offs;
   for (auto &it : items) {
@@ -833,6 +921,37 @@ int train_grads(Engine &e, const int *tin, const int *ttg, int act, float *loss_
   const float inv_sqrt = 1.0f / std::sqrt((float)hs);  // the backward's scale (:706), host float as the reference
   const int rw_blocks = (M * 32 + 255) / 256;          // warp-per-row kernels: 8 rows per CTA
 
+  // The projections' three products.  FP32 engines run them as fp32 SIMT
+  // GEMMs; TF32 / BF16 engines on the TF32 tensor cores (fp32 operands),
+  // whose tiles take K-major operands only, so the NN product uses W^T and
+  // the TN product dY^T and X^T (positions padded to Mp with zeros).
+  const bool tc = e.precision != kFP32;
+  const int Mp = (M + 3) / 4 * 4;
+  using ET = EpiTrain;
+  auto transpose = [&](const float *in, long long ldi, int R, int Cc, float *out, int Rp) {
+    snai_train_transpose<<<dim3((Cc + 31) / 32, (Rp + 31) / 32), dim3(32, 8), 0, st>>>(in, ldi, R, Cc, out, Rp);
+    e.launches++;
+  };
+  // C[M, N] = A[M, K] W[N, K]^T (A rows dense)
+  auto nt = [&](int N, int K, const float *A, const float *W, const ET &te, auto simt) -> int {
+    if (tc) return train_gemm_tc(e, M, N, K, A, W, te);
+    return gemm<true, true>(e, args(M, N, K, A, K, W, K), 1, simt, true);
+  };
+  // C[M, N] = A[M, K] W[K, N] (W a weight [K, N]; A's rows are K rounded up to 4)
+  auto nn = [&](int N, int K, const float *A, long long lda, const float *W, const ET &te, auto simt) -> int {
+    if (!tc) return gemm<true, false>(e, args(M, N, K, A, lda, W, N), 1, simt, true);
+    const int Kp = (K + 3) / 4 * 4;
+    transpose(W, N, K, N, t.wt, Kp);
+    return train_gemm_tc(e, M, N, Kp, A, t.wt, te);
+  };
+  // C[R, Cc] = sum over positions i of Y[i][r] X[i][c] (a weight gradient)
+  auto tn = [&](int R, int Cc, const float *Y, long long ldy, const float *X, long long ldx, float *C) -> int {
+    if (!tc) return gemm<false, false>(e, args(R, Cc, M, Y, ldy, X, ldx), 1, SimtStore{C, Cc, 0}, true);
+    transpose(Y, ldy, M, R, t.yt, Mp);
+    transpose(X, ldx, M, Cc, t.xt, Mp);
+    return train_gemm_tc(e, R, Cc, Mp, t.yt, t.xt, ET{ET::kStore, C, nullptr, nullptr, Cc});
+  };
+
   // ---------------- forward ----------------
   snai_train_embed<<<M, kRowThreads, 0, st>>>(t.tin, e.emb, t.hid[0], V, D);
   e.launches++;
@@ -840,27 +959,28 @@ int train_grads(Engine &e, const int *tin, const int *ttg, int act, float *loss_
     const LayerWeights &w = e.layers[l];
     snai_train_rmsnorm<<<M, kRowThreads, 0, st>>>(t.hid[l], w.rms_att, t.na[l], D);
     e.launches++;
-    rc |= gemm<true, true>(e, args(M, 3 * D, D, t.na[l], D, w.wqkv, D), 1, EpiStore{t.qkv[l], D3, 0}, true);
+    rc |= nt(3 * D, D, t.na[l], w.wqkv, ET{ET::kStore, t.qkv[l], nullptr, nullptr, D3}, SimtStore{t.qkv[l], D3, 0});
     snai_train_rope<<<dim3((D + 255) / 256, M), 256, 0, st>>>(t.qkv[l], D3, M, D, hs,
                                                                                                    e.rope, 1.0f);
     e.launches++;
     // S_h = Q_h K_h^T, then P = softmax
     rc |= gemm<true, true>(e, args(M, M, hs, t.qkv[l], D3, t.qkv[l] + D, D3, 1, hs, hs), H,
-                           EpiStore{t.S, t.ldS, (long long)M * t.ldS}, hvec);
+                           SimtStore{t.S, t.ldS, (long long)M * t.ldS}, hvec);
     snai_train_softmax_fwd<<<dim3(rw_blocks, H), 256, 0, st>>>(t.S, M, t.ldS, e.sqrt_hs);
     e.launches++;
     // att_h = P_h V_h
     rc |= gemm<true, false>(e, args(M, hs, M, t.S, t.ldS, t.qkv[l] + 2 * D, D3, 2, (long long)M * t.ldS, hs), H,
-                            EpiStore{t.att[l], D, hs}, hvec);
-    rc |= gemm<true, true>(e, args(M, D, D, t.att[l], D, w.wo, D), 1, EpiAdd{t.hf[l], t.hid[l], D}, true);
+                            SimtStore{t.att[l], D, hs}, hvec);
+    rc |= nt(D, D, t.att[l], w.wo, ET{ET::kAdd, t.hf[l], nullptr, t.hid[l], D}, SimtAdd{t.hf[l], t.hid[l], D});
     snai_train_rmsnorm<<<M, kRowThreads, 0, st>>>(t.hf[l], w.rms_ffn, t.nf[l], D);
     e.launches++;
-    rc |= gemm<true, true>(e, args(M, F, D, t.nf[l], D, w.wup, D), 1, EpiSilu{t.fin[l], t.fout[l], F}, true);
-    rc |= gemm<true, true>(e, args(M, D, F, t.fout[l], F, w.wdown, F), 1, EpiAdd{t.hid[l + 1], t.hf[l], D}, true);
+    rc |= nt(F, D, t.nf[l], w.wup, ET{ET::kSilu, t.fin[l], t.fout[l], nullptr, F}, SimtSilu{t.fin[l], t.fout[l], F});
+    rc |= nt(D, F, t.fout[l], w.wdown, ET{ET::kAdd, t.hid[l + 1], nullptr, t.hf[l], D},
+             SimtAdd{t.hid[l + 1], t.hf[l], D});
   }
   snai_train_rmsnorm<<<M, kRowThreads, 0, st>>>(t.hid[L], e.rms_final, t.nfinal, D);
   e.launches++;
-  rc |= gemm<true, true>(e, args(M, V, D, t.nfinal, D, e.w_out, D), 1, EpiStore{t.probs, t.Vp, 0}, true);
+  rc |= nt(V, D, t.nfinal, e.w_out, ET{ET::kStore, t.probs, nullptr, nullptr, t.Vp}, SimtStore{t.probs, t.Vp, 0});
   snai_train_xent<<<M, kRowThreads, 0, st>>>(t.probs, V, t.Vp, t.ttg, t.loss_rows);
   snai_train_loss_sum<<<1, 32, 0, st>>>(t.loss_rows, M, t.loss);
   e.launches += 2;
@@ -879,44 +999,45 @@ int train_grads(Engine &e, const int *tin, const int *ttg, int act, float *loss_
     snai_train_colsum_fin<<<(D + 255) / 256, 256, 0, st>>>(t.colpart, D, g);
     e.launches += 2;
   };
-  rc |= gemm<true, false>(e, args(M, D, V, t.probs, t.Vp, e.w_out, D), 1, EpiStore{t.dn, D, 0}, true);
-  rc |= gemm<false, false>(e, args(V, D, M, t.probs, t.Vp, t.nfinal, D), 1, EpiStore{G(e.w_out), D, 0}, true);
+  rc |= nn(D, V, t.probs, t.Vp, e.w_out, ET{ET::kStore, t.dn, nullptr, nullptr, D}, SimtStore{t.dn, D, 0});
+  rc |= tn(V, D, t.probs, t.Vp, t.nfinal, D, G(e.w_out));
   snai_train_rmsnorm_bwd<<<M, kRowThreads, 0, st>>>(t.dn, t.hid[L], e.rms_final, D, t.dh, 1, t.gprod);
   e.launches++;
   colsum(G(e.rms_final));
   for (int l = L - 1; l >= 0; --l) {
     const LayerWeights &w = e.layers[l];
     // MLP
-    rc |= gemm<true, false>(e, args(M, F, D, t.dh, D, w.wdown, F), 1, EpiSiluBack{t.dffn, t.fin[l], F}, true);
-    rc |= gemm<false, false>(e, args(D, F, M, t.dh, D, t.fout[l], F), 1, EpiStore{G(w.wdown), F, 0}, true);
-    rc |= gemm<true, false>(e, args(M, D, F, t.dffn, F, w.wup, D), 1, EpiStore{t.dn, D, 0}, true);
-    rc |= gemm<false, false>(e, args(F, D, M, t.dffn, F, t.nf[l], D), 1, EpiStore{G(w.wup), D, 0}, true);
+    rc |= nn(F, D, t.dh, D, w.wdown, ET{ET::kSiluBack, t.dffn, nullptr, t.fin[l], F},
+             SimtSiluBack{t.dffn, t.fin[l], F});
+    rc |= tn(D, F, t.dh, D, t.fout[l], F, G(w.wdown));
+    rc |= nn(D, F, t.dffn, F, w.wup, ET{ET::kStore, t.dn, nullptr, nullptr, D}, SimtStore{t.dn, D, 0});
+    rc |= tn(F, D, t.dffn, F, t.nf[l], D, G(w.wup));
     snai_train_rmsnorm_bwd<<<M, kRowThreads, 0, st>>>(t.dn, t.hf[l], w.rms_ffn, D, t.dh, 0, t.gprod);
     e.launches++;
     colsum(G(w.rms_ffn));
     // Wo
-    rc |= gemm<true, false>(e, args(M, D, D, t.dh, D, w.wo, D), 1, EpiStore{t.datt, D, 0}, true);
-    rc |= gemm<false, false>(e, args(D, D, M, t.dh, D, t.att[l], D), 1, EpiStore{G(w.wo), D, 0}, true);
+    rc |= nn(D, D, t.dh, D, w.wo, ET{ET::kStore, t.datt, nullptr, nullptr, D}, SimtStore{t.datt, D, 0});
+    rc |= tn(D, D, t.dh, D, t.att[l], D, G(w.wo));
     // attention: recomputed scores, dP = dO V^T, then dS, dQ, dK, dV
     const long long sS = (long long)M * t.ldS;
-    rc |= gemm<true, true>(e, args(M, M, hs, t.qkv[l], D3, t.qkv[l] + D, D3, 1, hs, hs), H, EpiStore{t.S, t.ldS, sS},
+    rc |= gemm<true, true>(e, args(M, M, hs, t.qkv[l], D3, t.qkv[l] + D, D3, 1, hs, hs), H, SimtStore{t.S, t.ldS, sS},
                            hvec);
     rc |= gemm<true, true>(e, args(M, M, hs, t.datt, D, t.qkv[l] + 2 * D, D3, 1, hs, hs), H,
-                           EpiStore{t.dP, t.ldS, sS}, hvec);
+                           SimtStore{t.dP, t.ldS, sS}, hvec);
     snai_train_softmax_bwd<<<dim3(rw_blocks, H), 256, 0, st>>>(t.S, t.dP, M, t.ldS, inv_sqrt);
     e.launches++;
-    rc |= gemm<true, false>(e, args(M, hs, M, t.dP, t.ldS, t.qkv[l] + D, D3, 2, sS, hs), H, EpiStore{t.dqkv, D3, hs},
+    rc |= gemm<true, false>(e, args(M, hs, M, t.dP, t.ldS, t.qkv[l] + D, D3, 2, sS, hs), H, SimtStore{t.dqkv, D3, hs},
                             hvec);
     rc |= gemm<false, false>(e, args(M, hs, M, t.dP, t.ldS, t.qkv[l], D3, 3, sS, hs), H,
-                             EpiStore{t.dqkv + D, D3, hs}, hvec);
+                             SimtStore{t.dqkv + D, D3, hs}, hvec);
     rc |= gemm<false, false>(e, args(M, hs, M, t.S, t.ldS, t.datt, D, 3, sS, hs), H,
-                             EpiStore{t.dqkv + 2 * D, D3, hs}, hvec);
+                             SimtStore{t.dqkv + 2 * D, D3, hs}, hvec);
     snai_train_rope<<<dim3((D + 255) / 256, M), 256, 0, st>>>(t.dqkv, D3, M, D, hs, e.rope,
                                                                                           -1.0f);
     e.launches++;
     // Wq, Wk, Wv (one stacked [3D, D] matrix)
-    rc |= gemm<true, false>(e, args(M, D, 3 * D, t.dqkv, D3, w.wqkv, D), 1, EpiStore{t.dn, D, 0}, true);
-    rc |= gemm<false, false>(e, args(3 * D, D, M, t.dqkv, D3, t.na[l], D), 1, EpiStore{G(w.wqkv), D, 0}, true);
+    rc |= nn(D, 3 * D, t.dqkv, D3, w.wqkv, ET{ET::kStore, t.dn, nullptr, nullptr, D}, SimtStore{t.dn, D, 0});
+    rc |= tn(3 * D, D, t.dqkv, D3, t.na[l], D, G(w.wqkv));
     snai_train_rmsnorm_bwd<<<M, kRowThreads, 0, st>>>(t.dn, t.hid[l], w.rms_att, D, t.dh, 0, t.gprod);
     e.launches++;
     colsum(G(w.rms_att));
