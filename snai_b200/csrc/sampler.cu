@@ -2197,41 +2197,40 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
 // fewer than k comparable entries, e.g. NaN) take an exact warp-level radix
 // select over 64-bit keys of the exact values, streaming the row again.
 //
-// History ids reach a per-warp stage by 4-byte cp.async copies issued one
-// row ahead; at a row's start they are marked in the warp's bitmap.
+// At a row's start the warp marks the row's history ids in its bitmap,
+// reading them straight from global memory (eight loads in flight per lane).
 // ---------------------------------------------------------------------------
 
-constexpr int kStreamCap = 512;       // candidate buffer entries per warp
+constexpr int kStreamCapMax = 1024;   // candidate buffer entries per warp at most (top-k 256)
 constexpr int kStreamSlots = 2;       // staged chunks in flight per warp
 constexpr int kStreamPer = 8;         // 16-byte words per lane per chunk
 constexpr int kStreamChunk = 32 * kStreamPer;  // 16-byte words per chunk
 static_assert(kStreamPer * 4 <= 64, "one mask bit per staged entry of a lane");
-constexpr int kStreamHistMax = 1024;  // history ids staged per warp
 constexpr int kStreamMaxK = 256;      // top-k the buffer supports
 constexpr int kStreamWarps = 20;      // warps per CTA at most
 
 // Per-warp shared-memory carve (the same on host and device); every region
 // starts on a 16-byte boundary (cp.async destinations, uint4 reads).
 struct StreamLayout {
-  int words, hist_cap;
-  unsigned off_val, off_bm, off_id, off_rh, off_hs, off_p, off_ord, bytes;  // ring at 0
+  int words, cap;  // cap: candidate buffer entries (room for 2k + 128, at least 256)
+  unsigned off_val, off_bm, off_id, off_rh, off_p, off_ord, bytes;  // ring at 0
 };
-__host__ __device__ inline StreamLayout stream_layout(int V, int hist_cols, int k) {
+__host__ __device__ inline StreamLayout stream_layout(int V, int k) {
   auto up16 = [](unsigned x) { return (x + 15u) & ~15u; };
   StreamLayout L;
   L.words = (V + 31) / 32;
-  L.hist_cap = (hist_cols + 31) & ~31;
+  L.cap = (2 * k + 128 + 31) / 32 * 32;
+  if (L.cap < 256) L.cap = 256;
+  if (L.cap > kStreamCapMax) L.cap = kStreamCapMax;
   unsigned o = up16(kStreamSlots * kStreamChunk * 16);  // staged chunks
   L.off_val = o;
-  o = up16(o + kStreamCap * 8);  // double values (then 64-bit keys, then running sums)
+  o = up16(o + (unsigned)L.cap * 8u);  // double values (then 64-bit keys, then running sums)
   L.off_bm = o;
   o = up16(o + (unsigned)L.words * 4u);
   L.off_id = o;
-  o = up16(o + kStreamCap * 4);
+  o = up16(o + (unsigned)L.cap * 4u);
   L.off_rh = o;
   o = up16(o + 256 * 4);
-  L.off_hs = o;
-  o = up16(o + (unsigned)L.hist_cap * 4u);
   L.off_p = o;
   o = up16(o + (unsigned)k * 8u);
   L.off_ord = o;
@@ -2349,6 +2348,27 @@ struct StreamState {
   float t, traw;
 };
 
+// Marks the history ids of logits row `mrow` (the first hist_len[mrow], or
+// all hist_cols) in the warp's bitmap, loading them from global memory.
+__device__ __forceinline__ void mark_history(const SampArgs &a, int mrow, uint32_t *bm) {
+  const int lane = threadIdx.x & 31;
+  if (a.hist == nullptr || a.hist_cols <= 0 || mrow < 0) return;
+  const int *hr = a.hist + (size_t)mrow * a.hist_ld;
+  const int n = min(max(a.hist_len ? a.hist_len[mrow] : a.hist_cols, 0), a.hist_cols);
+  for (int c0 = 0; c0 < n; c0 += 32 * 8) {
+    int t[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = c0 + 32 * j + lane;
+      t[j] = c < n ? __ldg(hr + c) : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (t[j] >= 0 && t[j] < a.V) atomicOr(&bm[t[j] >> 5], 1u << (t[j] & 31));
+  }
+  __syncwarp();
+}
+
 // Entries of this lane's chunk words marked in `bits` (bit 4r + j: word r,
 // element j; a superset of those with raw logit >= traw) whose lb reaches t
 // join the buffer.  Slots come from one warp scan; a batch that does not fit
@@ -2396,22 +2416,22 @@ __device__ __forceinline__ int warp_excl_scan(int c, int &tot) {
 }
 __device__ __forceinline__ void stream_take(const float *rf, unsigned long long bits, int c0, StreamState &st,
                                             double *bval, int *bid, const uint32_t *bm, unsigned *rh, int k,
-                                            double rep, int cut_at) {
+                                            double rep, int cut_at, int cap) {
   if (st.ovf) return;
   unsigned long long keep = stream_filter(rf, bits, c0, bm, rep, st.t);
   int tot;
   int ex = warp_excl_scan(__popcll(keep), tot);
-  if (st.cnt + tot <= kStreamCap) {
+  if (st.cnt + tot <= cap) {
     stream_write(rf, keep, c0, st.cnt + ex, bm, rep, bval, bid);
     st.cnt += tot;
   } else {
 #pragma unroll 1
     for (int r = 0; r < kStreamPer; ++r) {
       unsigned long long kr = keep & (0xFull << (4 * r));
-      if (st.cnt > kStreamCap - 128) {
+      if (st.cnt > cap - 128) {
         st.cnt = stream_compact(bval, bid, rh, st.cnt, k, st.t);
         st.traw = stream_traw(st.t, rep);
-        if (st.cnt > kStreamCap - 128) {
+        if (st.cnt > cap - 128) {
           st.ovf = 1;
           return;
         }
@@ -2425,7 +2445,7 @@ __device__ __forceinline__ void stream_take(const float *rf, unsigned long long 
   if (st.cnt > cut_at) {
     st.cnt = stream_compact(bval, bid, rh, st.cnt, k, st.t);
     st.traw = stream_traw(st.t, rep);
-    if (st.cnt > kStreamCap - 128) st.ovf = 1;
+    if (st.cnt > cap - 128) st.ovf = 1;
   }
 }
 
@@ -2434,7 +2454,7 @@ __device__ __forceinline__ void stream_take(const float *rf, unsigned long long 
 // it are gathered (exact values) into the buffer.  Returns their count, or
 // 0 if they do not fit (or the row has fewer than k comparable entries).
 __device__ __noinline__ int stream_regather(const float *Lrow, int V, const uint32_t *bm, double *bval, int *bid,
-                                            unsigned *rh, int k, double rep) {
+                                            unsigned *rh, int k, double rep, int cap) {
   const int lane = threadIdx.x & 31;
   const int n4 = V >> 2;
   const float4 *L4 = reinterpret_cast<const float4 *>(Lrow);
@@ -2475,7 +2495,7 @@ __device__ __noinline__ int stream_regather(const float *Lrow, int V, const uint
       const bool take = f == f && lb_key(val) >= prefix;
       const unsigned m = __ballot_sync(0xffffffffu, take);
       const int slot = cnt + __popc(m & ((1u << lane) - 1u));
-      if (take && slot < kStreamCap) {
+      if (take && slot < cap) {
         bval[slot] = val;
         bid[slot] = idx * 4 + j;
       }
@@ -2483,7 +2503,7 @@ __device__ __noinline__ int stream_regather(const float *Lrow, int V, const uint
     }
   }
   __syncwarp();
-  return cnt <= kStreamCap ? cnt : 0;
+  return cnt <= cap ? cnt : 0;
 }
 
 // Exact top-k of a row by a radix select over 64-bit keys of the exact
@@ -2586,7 +2606,7 @@ __device__ __noinline__ int stream_exact(const float *Lrow, int V, const uint32_
 
 // Row end: cut, rank, top-p tail; writes out[b].
 __device__ __noinline__ void stream_finish(const SampArgs &a, int b, StreamState st, double *bval, int *bid,
-                                           const uint32_t *bm, unsigned *rh, double *P, int *ord, int k) {
+                                           const uint32_t *bm, unsigned *rh, double *P, int *ord, int k, int cap) {
   const int lane = threadIdx.x & 31;
   int M = 0;
   if (!st.ovf && st.cnt >= k) {
@@ -2594,7 +2614,7 @@ __device__ __noinline__ void stream_finish(const SampArgs &a, int b, StreamState
     M = stream_compact(bval, bid, rh, st.cnt, k, t);
   } else {
     const float *Lrow = a.logits + (size_t)row_of(a, b) * a.ld;
-    M = st.ovf ? 0 : stream_regather(Lrow, a.V, bm, bval, bid, rh, k, a.rep);
+    M = st.ovf ? 0 : stream_regather(Lrow, a.V, bm, bval, bid, rh, k, a.rep, cap);
     if (M < k) M = stream_exact(Lrow, a.V, bm, bval, bid, rh, k, a.rep);
     if (M < k) {
       if (lane == 0) {
@@ -2642,49 +2662,26 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int V = a.V, n4 = V >> 2, S = (n4 + kStreamChunk - 1) / kStreamChunk;
   const int k = a.T < 0.01 ? 1 : min(a.top_k, V);
-  const StreamLayout Ly = stream_layout(V, a.hist_cols, k);
+  const StreamLayout Ly = stream_layout(V, k);
+  const int cap = Ly.cap;
   uint8_t *base = smem_dyn + (size_t)warp * Ly.bytes;
   float4 *ring = reinterpret_cast<float4 *>(base);
   double *bval = reinterpret_cast<double *>(base + Ly.off_val);
   uint32_t *bm = reinterpret_cast<uint32_t *>(base + Ly.off_bm);
   int *bid = reinterpret_cast<int *>(base + Ly.off_id);
   unsigned *rh = reinterpret_cast<unsigned *>(base + Ly.off_rh);
-  int *hs = reinterpret_cast<int *>(base + Ly.off_hs);
   double *P = reinterpret_cast<double *>(base + Ly.off_p);
   int *ord = reinterpret_cast<int *>(base + Ly.off_ord);
   const int NW = gridDim.x * W, gw = blockIdx.x * W + warp;
   if (warp >= W || gw >= a.rows) return;
   const int nrows = (a.rows - 1 - gw) / NW + 1;
-  const bool has_hist = a.hist != nullptr && a.hist_cols > 0;
   // logits / history row of the warp's i-th row (-1 past the last)
   auto mrow_of = [&](int i) -> int { return i < nrows ? row_of(a, gw + i * NW) : -1; };
-  // history of a row -> stage (its count returned)
-  auto stage = [&](int mrow) -> int {
-    if (!has_hist || mrow < 0) return 0;
-    const int *hr = a.hist + (size_t)mrow * a.hist_ld;
-    for (int c = lane; c < a.hist_cols; c += 32) cp_async4(hs + c, hr + c);
-    cp_async_commit();
-    const int n = a.hist_len ? a.hist_len[mrow] : a.hist_cols;
-    return min(max(n, 0), a.hist_cols);
-  };
   for (int w = lane; w < Ly.words; w += 32) bm[w] = 0u;
   __syncwarp();
   int mp = mrow_of(0), mq = mrow_of(1);
   // the first row's history is marked before any chunk is staged
-  int hn = stage(mp);
-  auto mark = [&]() {
-    for (int c = lane; c < hn; c += 32) {
-      const int t = hs[c];
-      if (t >= 0 && t < V) atomicOr(&bm[t >> 5], 1u << (t & 31));
-    }
-    __syncwarp();
-  };
-  if (has_hist) {
-    cp_async_wait<0>();
-    __syncwarp();
-    mark();
-    hn = stage(mq);
-  }
+  mark_history(a, mp, bm);
 
   // Chunk q of the warp's stream (row q / S, chunk q % S of it) is staged
   // in slot q % kStreamSlots, each lane copying (cp.async, one group per
@@ -2712,9 +2709,9 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
 
   StreamState st{0, 0, -INFINITY, -INFINITY};
   // the buffer is cut once it holds more than cut_at entries (at most
-  // kStreamCap - 128, so one more chunk word per lane always fits); cutting
-  // early in the row raises t sooner and spares later chunks their pushes
-  const int cut_at = min(kStreamCap - 128, max(2 * k, 128));
+  // cap - 128, so one more chunk word per lane always fits); cutting early in
+  // the row raises t sooner and spares later chunks their pushes
+  const int cut_at = min(cap - 128, max(2 * k, 128));
   // G groups of gl lanes for the opening threshold: one group (the chunk's
   // maximum, a true bound) for k = 1; else G >= 8 groups and G >= 2.5 x
   // (x = top-k entries expected in one chunk), so that for a row in random
@@ -2732,14 +2729,8 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
   int ci = 0, cs = 0;
   for (long long q = 0; q < total; ++q) {
     const int slot = (int)(q % kStreamSlots);
-    cp_async_wait<kStreamSlots - 1>();  // this chunk (and row ci's history, staged a row ago)
-    if (cs == 0 && ci > 0 && has_hist) {
-      // mark row ci's history, then stage row ci + 1's
-      if (S < kStreamSlots) cp_async_wait<0>();
-      __syncwarp();
-      mark();
-      hn = stage(pi == ci ? mq : mrow_of(ci + 1));
-    }
+    cp_async_wait<kStreamSlots - 1>();  // this chunk
+    if (cs == 0 && ci > 0) mark_history(a, mrow_of(ci), bm);
     const int c0 = cs * kStreamChunk;
     const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
     float4 x[kStreamPer];
@@ -2777,11 +2768,11 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
           if (valid && f4_at(x[r], j) >= st.traw) bits |= 1ull << (4 * r + j);
       }
       stream_take(reinterpret_cast<const float *>(ring + slot * kStreamChunk), bits, c0, st, bval, bid, bm, rh, k,
-                  a.rep, cut_at);
+                  a.rep, cut_at, cap);
     }
     issue(slot);  // the slot's next chunk (this lane's words were read above)
     if (++cs == S) {
-      stream_finish(a, gw + ci * NW, st, bval, bid, bm, rh, P, ord, k);
+      stream_finish(a, gw + ci * NW, st, bval, bid, bm, rh, P, ord, k, cap);
       for (int w = lane; w < Ly.words; w += 32) bm[w] = 0u;
       __syncwarp();
       st = StreamState{0, 0, -INFINITY, -INFINITY};
@@ -2821,20 +2812,17 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
 constexpr int kStreamAWarps = 16;  // warps per CTA at most (128 registers a thread)
 
 struct StreamALayout {
-  int words, hist_cap, nch;
-  unsigned off_bm, off_hs, off_ch, off_pv, bytes;  // ring at 0
+  int words, nch;
+  unsigned off_bm, off_ch, off_pv, bytes;  // ring at 0
 };
-__host__ __device__ inline StreamALayout stream_a_layout(int V, int hist_cols) {
+__host__ __device__ inline StreamALayout stream_a_layout(int V) {
   auto up16 = [](unsigned x) { return (x + 15u) & ~15u; };
   StreamALayout L;
   L.words = (V + 31) / 32;
-  L.hist_cap = (hist_cols + 31) & ~31;
   L.nch = ((V >> 2) + kStreamChunk - 1) / kStreamChunk;
   unsigned o = up16(kStreamSlots * kStreamChunk * 16);
   L.off_bm = o;
   o = up16(o + (unsigned)L.words * 4u);
-  L.off_hs = o;
-  o = up16(o + (unsigned)L.hist_cap * 4u);
   L.off_ch = o;  // per chunk: (mu, s, s of the penalised ids, -) floats
   o = up16(o + (unsigned)L.nch * 16u);
   L.off_pv = o;  // the crossing chunk: 32 values of each lane, [e][lane]
@@ -3092,45 +3080,22 @@ __global__ void __launch_bounds__(kStreamAWarps * 32, 1) sample_a_stream(const _
   extern __shared__ __align__(16) uint8_t smem_dyn[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int V = a.V, n4 = V >> 2, S = (n4 + kStreamChunk - 1) / kStreamChunk;
-  const StreamALayout Ly = stream_a_layout(V, a.hist_cols);
+  const StreamALayout Ly = stream_a_layout(V);
   uint8_t *base = smem_dyn + (size_t)warp * Ly.bytes;
   float4 *ring = reinterpret_cast<float4 *>(base);
   uint32_t *bm = reinterpret_cast<uint32_t *>(base + Ly.off_bm);
-  int *hs = reinterpret_cast<int *>(base + Ly.off_hs);
   float4 *tab = reinterpret_cast<float4 *>(base + Ly.off_ch);
   float *pv = reinterpret_cast<float *>(base + Ly.off_pv);
   const int NW = gridDim.x * W, gw = blockIdx.x * W + warp;
   if (warp >= W || gw >= a.rows) return;
   const int nrows = (a.rows - 1 - gw) / NW + 1;
-  const bool has_hist = a.hist != nullptr && a.hist_cols > 0;
   const float cexp = (float)(1.4426950408889634 * a.Tinv);
   const float l2e = 1.44269504f;
   auto mrow_of = [&](int i) -> int { return i < nrows ? row_of(a, gw + i * NW) : -1; };
-  auto stage = [&](int mrow) -> int {
-    if (!has_hist || mrow < 0) return 0;
-    const int *hr = a.hist + (size_t)mrow * a.hist_ld;
-    for (int c = lane; c < a.hist_cols; c += 32) cp_async4(hs + c, hr + c);
-    cp_async_commit();
-    const int n = a.hist_len ? a.hist_len[mrow] : a.hist_cols;
-    return min(max(n, 0), a.hist_cols);
-  };
   for (int w = lane; w < Ly.words; w += 32) bm[w] = 0u;
   __syncwarp();
   int mp = mrow_of(0), mq = mrow_of(1);
-  int hn = stage(mp);
-  auto mark = [&]() {
-    for (int c = lane; c < hn; c += 32) {
-      const int t = hs[c];
-      if (t >= 0 && t < V) atomicOr(&bm[t >> 5], 1u << (t & 31));
-    }
-    __syncwarp();
-  };
-  if (has_hist) {
-    cp_async_wait<0>();
-    __syncwarp();
-    mark();
-    hn = stage(mq);
-  }
+  mark_history(a, mp, bm);
   int pi = 0, ps = 0;
   const float4 *Lp = mp >= 0 ? reinterpret_cast<const float4 *>(a.logits + (size_t)mp * a.ld) : nullptr;
   auto issue = [&](int slot) {
@@ -3158,12 +3123,7 @@ __global__ void __launch_bounds__(kStreamAWarps * 32, 1) sample_a_stream(const _
   for (long long q = 0; q < total; ++q) {
     const int slot = (int)(q % kStreamSlots);
     cp_async_wait<kStreamSlots - 1>();
-    if (cs == 0 && ci > 0 && has_hist) {
-      if (S < kStreamSlots) cp_async_wait<0>();
-      __syncwarp();
-      mark();
-      hn = stage(pi == ci ? mq : mrow_of(ci + 1));
-    }
+    if (cs == 0 && ci > 0) mark_history(a, mrow_of(ci), bm);
     // every lane's copies of this chunk are complete: the lanes read across
     __syncwarp();
     const float4 *rs = ring + slot * kStreamChunk + 8 * lane;  // this lane's eight words
@@ -4041,8 +4001,8 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   // variant A over 16-byte aligned rows: the streaming kernel (greedy only for
   // rows longer than a register row, where it beats the CTA clusters)
   if (many && s.variant == 0 && (s.temperature > 0.01 || s.V > kSliceLen) && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
-      (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 && s.hist_cols <= kStreamHistMax) {
-    const StreamALayout Ly = stream_a_layout(s.V, s.hist_cols);
+      (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0) {
+    const StreamALayout Ly = stream_a_layout(s.V);
     const int W = std::min<int>({kStreamAWarps, (int)((227u * 1024u) / Ly.bytes), wrows});
     if (W >= 2) {
       static DeviceOnce done;
@@ -4072,9 +4032,9 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
   }
   // variant B over 16-byte aligned rows: the streaming kernel, one warp per row
   if (many && s.variant != 0 && (s.V & 3) == 0 && (s.ld & 3) == 0 &&
-      (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0 && s.hist_cols <= kStreamHistMax) {
+      (reinterpret_cast<uintptr_t>(s.logits) & 15) == 0) {
     const int kk = s.temperature < 0.01 ? 1 : std::min(s.top_k, s.V);
-    const StreamLayout Ly = stream_layout(s.V, s.hist_cols, kk);
+    const StreamLayout Ly = stream_layout(s.V, kk);
     const int W = std::min<int>({kStreamWarps, (int)((227u * 1024u) / Ly.bytes), wrows});
     if (kk <= kStreamMaxK && W >= 2) {
       static DeviceOnce done;

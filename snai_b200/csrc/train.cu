@@ -536,26 +536,33 @@ __global__ void snai_train_colsum_fin(const float *__restrict__ part, int D, flo
 
 // Token links of the sequence: prev[i] = the last position j < i holding the
 // same (clamped) token, or -1; last[i] = 1 when no later position holds it.
-__global__ void snai_train_tok_links(const int *__restrict__ tok, int act, int V, int *__restrict__ prev,
-                                     int *__restrict__ last) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= act) return;
+// One CTA; the first kLinkMax clamped ids are staged in shared memory.
+constexpr int kLinkMax = 8192;
+
+__global__ void __launch_bounds__(1024) snai_train_tok_links(const int *__restrict__ tok, int act, int V,
+                                                            int *__restrict__ prev, int *__restrict__ last) {
+  __shared__ int ids[kLinkMax];
   auto clamp = [&](int t) { return (t < 0 || t >= V) ? 0 : t; };
-  const int t = clamp(tok[i]);
-  int p = -1;
-  for (int j = i - 1; j >= 0; --j)
-    if (clamp(tok[j]) == t) {
-      p = j;
-      break;
-    }
-  prev[i] = p;
-  int l = 1;
-  for (int j = i + 1; j < act; ++j)
-    if (clamp(tok[j]) == t) {
-      l = 0;
-      break;
-    }
-  last[i] = l;
+  for (int i = threadIdx.x; i < act && i < kLinkMax; i += blockDim.x) ids[i] = clamp(tok[i]);
+  __syncthreads();
+  auto id = [&](int j) { return j < kLinkMax ? ids[j] : clamp(tok[j]); };
+  for (int i = threadIdx.x; i < act; i += blockDim.x) {
+    const int t = id(i);
+    int p = -1;
+    for (int j = i - 1; j >= 0; --j)
+      if (id(j) == t) {
+        p = j;
+        break;
+      }
+    prev[i] = p;
+    int l = 1;
+    for (int j = i + 1; j < act; ++j)
+      if (id(j) == t) {
+        l = 0;
+        break;
+      }
+    last[i] = l;
+  }
 }
 
 // g_emb[tok] += dh[i] over positions i in descending order (:817-818): the
@@ -1042,7 +1049,7 @@ int train_grads(Engine &e, const int *tin, const int *ttg, int act, float *loss_
     e.launches++;
     colsum(G(w.rms_att));
   }
-  snai_train_tok_links<<<(M + 127) / 128, 128, 0, st>>>(t.tin, M, V, t.prev, t.last);
+  snai_train_tok_links<<<1, 1024, 0, st>>>(t.tin, M, V, t.prev, t.last);
   snai_train_emb_grad<<<M, kRowThreads, 0, st>>>(t.dh, t.tin, t.prev, t.last, V, D, G(e.emb));
   e.launches += 2;
   if (rc || launch_rc("training backward")) return -1;
