@@ -1301,19 +1301,26 @@ static int launch_tc2(Engine &e, int M, int N, int K, const void *A, const void 
 template <typename TIn, class Epi>
 static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
   // Tile shape by a per-CTA cost model: a CTA streams (rows of A + rows of W)
-  // per k-block for every tile it owns, so the cost is (tiles per CTA) x
-  // (128 + BN), with the CTA pair's 256 x 256 tile at 128 + 128 per CTA.
+  // per k-block for every tile it owns and multiplies them, so the cost is
+  // (tiles per CTA) x max(128 + BN, MMA time), with the CTA pair's 256 x 256
+  // tile at 128 + 128 rows and a 128 x 256 block per CTA.
   // Large M keeps the pair tiles; few rows (one GPU's share of the
   // sequences, small batches) take narrower single-CTA tiles on more SMs.
   // Every shape gives a row the same bits (same K order, one accumulator).
   const int sms = sm_count(e.device);
   auto waves = [](long long tiles, long long slots) { return (tiles + slots - 1) / slots; };
+  // per k-block a CTA loads 128 + BN rows of 128 bytes and multiplies a
+  // 128 x BN block, about 1.14 BN row-loads of time at the SM's L2 and
+  // tensor rates; whichever is longer is the tile's cost (so a 512-row QKV
+  // takes 128 x 128 tiles on 96 SMs rather than 48 CTA pairs)
+  auto cost = [](long long rows, long long bn) { return std::max(rows, bn + bn / 8); };
   const long long mt = (M + kTcBM - 1) / kTcBM;
-  long long best = (M >= 256 && N >= 256) ? waves((long long)((M + 255) / 256) * ((N + 255) / 256), sms / 2) * 256
-                                          : LLONG_MAX;
+  long long best = (M >= 256 && N >= 256)
+                       ? waves((long long)((M + 255) / 256) * ((N + 255) / 256), sms / 2) * cost(256, 256)
+                       : LLONG_MAX;
   int pick = 0;  // 0 pair, else BN
   for (int bn : {256, 128, 64}) {
-    const long long c = waves(mt * ((N + bn - 1) / bn), sms) * (128 + bn);
+    const long long c = waves(mt * ((N + bn - 1) / bn), sms) * cost(128 + bn, bn);
     if (c < best) {
       best = c;
       pick = bn;
