@@ -669,21 +669,41 @@ struct AdamArgs {
 };
 
 // adamStep (:145-160) per element, after the clip factor (:255-258).
+__device__ __forceinline__ void adam_elem(const AdamArgs &a, size_t i, bool apply, float cf, float g, float &w,
+                                          float &m, float &v) {
+  float gg = g;
+  if (apply) gg = __fmul_rn(gg, cf);
+  const float grad = __fdiv_rn(gg, a.scale);
+  if (i < a.sparse_end && grad == 0.0f) return;
+  if (grad != grad || grad > 9999.0f || grad < -9999.0f) return;
+  m = __fadd_rn(__fmul_rn(a.b1, m), __fmul_rn(a.omb1, grad));
+  v = __fadd_rn(__fmul_rn(a.b2, v), __fmul_rn(__fmul_rn(a.omb2, grad), grad));
+  const float mh = __fdiv_rn(m, a.b1t), vh = __fdiv_rn(v, a.b2t);
+  w = __fsub_rn(w, __fdiv_rn(__fmul_rn(a.lr, mh), __fadd_rn(__fsqrt_rn(vh), 1e-8f)));
+}
+
+// Four elements per thread (the weight block is a multiple of 64 floats);
+// w, m, v are read and written only where the gradient is not zero or the
+// element is outside the embedding, as the sparse rule leaves the others.
 __global__ void __launch_bounds__(kRowThreads) snai_train_adam(const AdamArgs a) {
   const bool apply = a.clip[1] != 0.0f;
   const float cf = a.clip[0];
-  for (size_t i = (size_t)blockIdx.x * kRowThreads + threadIdx.x; i < a.n; i += (size_t)gridDim.x * kRowThreads) {
-    float gg = a.g[i];
-    if (apply) gg = __fmul_rn(gg, cf);
-    const float grad = __fdiv_rn(gg, a.scale);
-    if (i < a.sparse_end && grad == 0.0f) continue;
-    if (grad != grad || grad > 9999.0f || grad < -9999.0f) continue;
-    const float m = __fadd_rn(__fmul_rn(a.b1, a.m[i]), __fmul_rn(a.omb1, grad));
-    const float v = __fadd_rn(__fmul_rn(a.b2, a.v[i]), __fmul_rn(__fmul_rn(a.omb2, grad), grad));
-    a.m[i] = m;
-    a.v[i] = v;
-    const float mh = __fdiv_rn(m, a.b1t), vh = __fdiv_rn(v, a.b2t);
-    a.w[i] = __fsub_rn(a.w[i], __fdiv_rn(__fmul_rn(a.lr, mh), __fadd_rn(__fsqrt_rn(vh), 1e-8f)));
+  const size_t n4 = a.n / 4;
+  const float4 *g4 = reinterpret_cast<const float4 *>(a.g);
+  float4 *w4 = reinterpret_cast<float4 *>(a.w), *m4 = reinterpret_cast<float4 *>(a.m),
+         *v4 = reinterpret_cast<float4 *>(a.v);
+  for (size_t j = (size_t)blockIdx.x * kRowThreads + threadIdx.x; j < n4; j += (size_t)gridDim.x * kRowThreads) {
+    const float4 g = __ldcs(g4 + j);
+    const size_t i = 4 * j;
+    if (i + 4 <= a.sparse_end && g.x == 0.f && g.y == 0.f && g.z == 0.f && g.w == 0.f) continue;
+    float4 w = w4[j], m = m4[j], v = v4[j];
+    adam_elem(a, i, apply, cf, g.x, w.x, m.x, v.x);
+    adam_elem(a, i + 1, apply, cf, g.y, w.y, m.y, v.y);
+    adam_elem(a, i + 2, apply, cf, g.z, w.z, m.z, v.z);
+    adam_elem(a, i + 3, apply, cf, g.w, w.w, m.w, v.w);
+    w4[j] = w;
+    m4[j] = m;
+    v4[j] = v;
   }
 }
 
@@ -749,7 +769,7 @@ int gemm(Engine &e, const GemmArgs &g0, int batch, const Epi &epi, bool vec) {
   const int sms = device_sm_count(e.device);
   int splits = 1;
   if (e.train && e.train->split && g.causal != 1 && tiles < 2 * sms && g.K >= 1024) {
-    splits = (int)std::min<long long>({(2 * sms + tiles - 1) / tiles, (long long)g.K / 512,
+    splits = (int)std::min<long long>({(2 * sms + tiles - 1) / tiles, (long long)g.K / 256,
                                        (long long)(kSplitFloats / ((size_t)batch * g.M * g.N))});
     if (splits < 2) splits = 1;
   }
@@ -1089,7 +1109,7 @@ int train_apply(Engine &e, float lr, float scale) {
   a.b2t = 1.0f - ::powf(a.b2, (float)t.adam_t);
   a.scale = scale;
   a.clip = t.clip;
-  const int blocks = (int)std::min<size_t>((n + kRowThreads - 1) / kRowThreads, (size_t)device_sm_count(e.device) * 8);
+  const int blocks = (int)std::min<size_t>((n / 4 + kRowThreads - 1) / kRowThreads, (size_t)device_sm_count(e.device) * 8);
   if (scale != 0.0f) {  // adamStep returns at once when scale == 0 (:147)
     snai_train_adam<<<blocks, kRowThreads, 0, st>>>(a);
     e.launches++;
