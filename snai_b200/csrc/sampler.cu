@@ -74,7 +74,7 @@ struct SampArgs {
   int nan_guard;
   int *out;
   int *err;
-  int redo;  // only the rows whose out[] holds kRedoMark (variant A's CTA-per-row kernel)
+  int redo;  // only the rows whose out[] holds kRedoMark (variant A's CTA-per-row kernel); 2: each staged whole
 };
 
 // out[] of a row the one-warp-per-row variant-A kernel could not certify
@@ -344,9 +344,11 @@ struct Row {
       float4 o = fetch(i);
       const int v0 = (threadIdx.x + kSampThreads * i) * 4;
       pbits = v0 < V ? (bits[v0 >> 5] >> (v0 & 31)) & 0xFu : 0u;
+      if (!S) {  // a staged row holds the penalised values already
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if ((pbits >> j) & 1u) f4_set(o, j, pf(f4_at(o, j)));
+        for (int j = 0; j < 4; ++j)
+          if ((pbits >> j) & 1u) f4_set(o, j, pf(f4_at(o, j)));
+      }
       return o;
     }
   }
@@ -420,7 +422,7 @@ __device__ __forceinline__ float row_prologue(const SampArgs &a, int b, Row<NV4>
   row.load(bits, pf);
   __syncthreads();  // the stage has been consumed
   const int nb = b + (int)gridDim.x;
-  if (nb < a.rows) {
+  if (nb < a.rows && !a.redo) {  // a redo pass stages each of its rows itself
     const int nrow = row_of(a, nb);
     if (staged && threadIdx.x == 0) feed.issue(a, nrow);
     if (hist_in_regs) load_hist_regs(a, nrow, hreg);
@@ -649,8 +651,10 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
   RowFeeder feed;
   feed.stage = stage_ptr(smem_dyn, sizeof(SmemA), V);
   feed.bar = &sm.bar;
-  // a redo pass takes rows out of order: no row staging or history run ahead
-  const bool staged = NV4 > 0 && !a.redo && (V & 3) == 0 && ((a.ld & 3) == 0) &&
+  // a redo pass takes rows out of order: no history run ahead, and its rows
+  // are staged one at a time (redo 2: the launch made room for a row) so that
+  // its passes over the row read shared memory instead of L2
+  const bool staged = (NV4 > 0 || a.redo == 2) && (a.redo != 1) && (V & 3) == 0 && ((a.ld & 3) == 0) &&
                       ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0) &&
                       ((reinterpret_cast<uintptr_t>(feed.stage) & 15) == 0);
   const bool hist_in_regs = !a.redo && a.hist_cols <= 512 * kHistRegs;
@@ -660,7 +664,10 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
     fence_barrier_init();
   }
   __syncthreads();
-  if ((int)blockIdx.x < a.rows) {
+  // the in-order pipeline stages its first row here; a redo pass issues each
+  // of its rows' copies in row_body and waits for it there, so a CTA never
+  // leaves with a copy into its shared memory in flight
+  if ((int)blockIdx.x < a.rows && !a.redo) {
     const int r0 = row_of(a, blockIdx.x);
     if (staged && threadIdx.x == 0) feed.issue(a, r0);
     if (hist_in_regs) load_hist_regs(a, r0, hreg);
@@ -670,6 +677,11 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
   auto put = [&](int b, int v) { a.out[b] = a.redo ? -(v + 10) : v; };
   auto row_body = [&](int b) {
     const float *L = a.logits + (size_t)row_of(a, b) * a.ld;
+    if (a.redo && staged && threadIdx.x == 0) {
+      // the previous row's penalty writes to the stage come before this copy
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      feed.issue(a, row_of(a, b));
+    }
     Row<NV4> row;
     const float l0 = row_prologue(a, b, row, bits, sm.plist, &sm.npen, feed, staged, hreg, hist_in_regs, pen_fn);
     if (a.nan_guard && l0 != l0) {  // src/snai_inference.php:146
@@ -4019,8 +4031,10 @@ int launch_sampler(const SampleLaunch &s, cudaStream_t stream) {
         sample_a_stream<false><<<grid, W * 32, (size_t)W * Ly.bytes, stream>>>(a, W);
       // the rows it could not certify, exactly, by the CTA-per-row kernel
       SampArgs r = a;
-      r.redo = 1;
-      launch_a<0>(r, sizeof(SmemA) + (((size_t)((s.V + 31) / 32) * 4 + 15) & ~(size_t)15), stream);
+      const size_t core = sizeof(SmemA) + (((size_t)((s.V + 31) / 32) * 4 + 15) & ~(size_t)15);
+      const size_t staged = core + (size_t)s.V * 4 + kStageAlign;
+      r.redo = staged <= 227u * 1024u ? 2 : 1;  // room to stage a whole row: its passes read shared memory
+      launch_a<0>(r, r.redo == 2 ? staged : core, stream);
       redo_decode_kernel<<<(s.rows + 255) / 256, 256, 0, stream>>>(a.out, s.rows);
       const cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) {

@@ -54,7 +54,7 @@ namespace snai {
 // fp32 SIMT GEMM, three operand layouts, batched, with causal tile limits
 // ============================================================================
 //
-// C(m, n) = sum_k A(m, k) B(n, k) over a 128 x 128 tile per CTA, 256
+// C(m, n) = sum_k A(m, k) B(n, k) over a 128 x 128 (or 128 x 64) tile per CTA, 256
 // threads, 8 x 8 outputs per thread (rows ty*4..+3 and 64+ty*4..+3, columns
 // tx*4..+3 and 64+tx*4..+3, so every shared-memory read is a broadcast or a
 // conflict-free float4), k in steps of 8 through a two-stage shared-memory
@@ -69,7 +69,7 @@ namespace snai {
 // causal: 1 skips tiles with n0 > m0 + 127 (scores of later positions);
 // 2 ends k at m0 + 128 (A(m, k) = 0 for k > m); 3 starts k at m0 (A(m, k) = 0
 // for k < m).
-constexpr int kGBM = 128, kGBN = 128, kGBK = 8, kGThreads = 256;
+constexpr int kGBM = 128, kGBK = 8, kGThreads = 256;  // tile rows, k step, threads (tile width: 128 or 64)
 constexpr int kGLd = kGBM + 4;  // shared row stride: the transposing stores of the two k halves hit distinct banks
 
 struct GemmArgs {
@@ -141,13 +141,15 @@ struct SimtSiluBack {
   }
 };
 
-template <bool A_KC, bool B_KC, bool VEC, class Epi>
+template <bool A_KC, bool B_KC, bool VEC, int BN, class Epi>
 __global__ void __launch_bounds__(kGThreads, 2) snai_train_sgemm(const GemmArgs g, const Epi epi) {
+  constexpr int NH = BN / 64;       // 64-column halves of the tile
+  constexpr int BLd = BN + 4;       // B's shared row stride
   __shared__ __align__(16) float As[2][kGBK][kGLd];
-  __shared__ __align__(16) float Bs[2][kGBK][kGLd];
+  __shared__ __align__(16) float Bs[2][kGBK][BLd];
   const int z = blockIdx.z;  // the epilogue's batch index (batch * splits + split when split)
   const int zb = z / g.splits, sp = z % g.splits;
-  const int m0 = blockIdx.y * kGBM, n0 = blockIdx.x * kGBN;
+  const int m0 = blockIdx.y * kGBM, n0 = blockIdx.x * BN;
   if (g.causal == 1 && n0 > m0 + kGBM - 1) return;
   const float *__restrict__ A = g.A + zb * g.sA;
   const float *__restrict__ B = g.B + zb * g.sB;
@@ -160,11 +162,13 @@ __global__ void __launch_bounds__(kGThreads, 2) snai_train_sgemm(const GemmArgs 
   }
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
 
-  // one float4 (or four scalars) per operand per k step
-  // [r][k] operand: r = tid >> 1, k = (tid & 1) * 4;  [k][r] operand: k = tid >> 5, r = (tid & 31) * 4
-  auto load = [&](const float *__restrict__ P, long long ld, int r0, int R, bool kc, int k0) -> float4 {
+  // one float4 (or four scalars) per operand of width W per k step
+  // [r][k] operand: r = tid >> 1, k = (tid & 1) * 4 (threads with r < W);
+  // [k][r] operand: k = tid / (W / 4), r = (tid % (W / 4)) * 4 (threads with k < kGBK)
+  auto load = [&](const float *__restrict__ P, long long ld, int r0, int R, bool kc, int k0, int W) -> float4 {
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (kc) {
+      if ((tid >> 1) >= W) return v;
       const int r = r0 + (tid >> 1), k = k0 + (tid & 1) * 4;
       if (r < R) {
         const float *p = P + (long long)r * ld + k;
@@ -178,7 +182,9 @@ __global__ void __launch_bounds__(kGThreads, 2) snai_train_sgemm(const GemmArgs 
         }
       }
     } else {
-      const int k = k0 + (tid >> 5), r = r0 + (tid & 31) * 4;
+      const int q = W / 4;
+      if (tid / q >= kGBK) return v;
+      const int k = k0 + tid / q, r = r0 + (tid % q) * 4;
       if (k < ke && r < R) {
         const float *p = P + (long long)k * ld + r;
         if (VEC) {
@@ -193,53 +199,62 @@ __global__ void __launch_bounds__(kGThreads, 2) snai_train_sgemm(const GemmArgs 
     }
     return v;
   };
-  auto store = [&](float (*S)[kGLd], float4 v, bool kc) {
+  auto store = [&](float *S, int ld, float4 v, bool kc, int W) {
     if (kc) {
+      if ((tid >> 1) >= W) return;
       const int r = tid >> 1, k = (tid & 1) * 4;
-      S[k][r] = v.x;
-      S[k + 1][r] = v.y;
-      S[k + 2][r] = v.z;
-      S[k + 3][r] = v.w;
+      S[k * ld + r] = v.x;
+      S[(k + 1) * ld + r] = v.y;
+      S[(k + 2) * ld + r] = v.z;
+      S[(k + 3) * ld + r] = v.w;
     } else {
-      *reinterpret_cast<float4 *>(&S[tid >> 5][(tid & 31) * 4]) = v;
+      const int q = W / 4;
+      if (tid / q >= kGBK) return;
+      *reinterpret_cast<float4 *>(&S[(tid / q) * ld + (tid % q) * 4]) = v;
     }
   };
 
-  float acc[8][8];
+  float acc[8][4 * NH];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 4 * NH; ++j) acc[i][j] = 0.f;
 
   const int nt = ke > kb ? (ke - kb + kGBK - 1) / kGBK : 0;
   if (nt > 0) {
-    store(As[0], load(A, g.lda, m0, g.M, A_KC, kb), A_KC);
-    store(Bs[0], load(B, g.ldb, n0, g.N, B_KC, kb), B_KC);
+    store(&As[0][0][0], kGLd, load(A, g.lda, m0, g.M, A_KC, kb, kGBM), A_KC, kGBM);
+    store(&Bs[0][0][0], BLd, load(B, g.ldb, n0, g.N, B_KC, kb, BN), B_KC, BN);
   }
   __syncthreads();
   for (int t = 0; t < nt; ++t) {
     const int cur = t & 1;
     float4 na = make_float4(0.f, 0.f, 0.f, 0.f), nb = na;
     if (t + 1 < nt) {
-      na = load(A, g.lda, m0, g.M, A_KC, kb + (t + 1) * kGBK);
-      nb = load(B, g.ldb, n0, g.N, B_KC, kb + (t + 1) * kGBK);
+      na = load(A, g.lda, m0, g.M, A_KC, kb + (t + 1) * kGBK, kGBM);
+      nb = load(B, g.ldb, n0, g.N, B_KC, kb + (t + 1) * kGBK, BN);
     }
 #pragma unroll
     for (int kk = 0; kk < kGBK; ++kk) {
       const float4 a0 = *reinterpret_cast<const float4 *>(&As[cur][kk][ty * 4]);
       const float4 a1 = *reinterpret_cast<const float4 *>(&As[cur][kk][64 + ty * 4]);
-      const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[cur][kk][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[cur][kk][64 + tx * 4]);
       const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      float b[4 * NH];
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        const float4 bh = *reinterpret_cast<const float4 *>(&Bs[cur][kk][h * 64 + tx * 4]);
+        b[4 * h] = bh.x;
+        b[4 * h + 1] = bh.y;
+        b[4 * h + 2] = bh.z;
+        b[4 * h + 3] = bh.w;
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        for (int j = 0; j < 4 * NH; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
     }
     if (t + 1 < nt) {
-      store(As[cur ^ 1], na, A_KC);
-      store(Bs[cur ^ 1], nb, B_KC);
+      store(&As[cur ^ 1][0][0], kGLd, na, A_KC, kGBM);
+      store(&Bs[cur ^ 1][0][0], BLd, nb, B_KC, BN);
     }
     __syncthreads();
   }
@@ -249,7 +264,7 @@ __global__ void __launch_bounds__(kGThreads, 2) snai_train_sgemm(const GemmArgs 
     const int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
     if (m >= g.M) continue;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < NH; ++h) {
       const int n = n0 + h * 64 + tx * 4;
       if (n >= g.N) continue;
       const int cnt = min(4, g.N - n);
@@ -755,15 +770,10 @@ int launch_rc(const char *what) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// One GEMM launch; VEC when every operand row start is 16-byte aligned.  A
-// grid of fewer tiles than twice the SMs with a long k range is split over k
-// (partials in `split`, summed in split order by a second launch that runs
-// the epilogue), so that every SM gets work.
-template <bool A_KC, bool B_KC, class Epi>
-int gemm(Engine &e, const GemmArgs &g0, int batch, const Epi &epi, bool vec) {
+template <bool A_KC, bool B_KC, int BN, class Epi>
+int gemm_bn(Engine &e, const GemmArgs &g0, int batch, const Epi &epi, bool vec) {
   GemmArgs g = g0;
-  if (g.M <= 0 || g.N <= 0) return 0;
-  const int gx = (g.N + kGBN - 1) / kGBN, gy = (g.M + kGBM - 1) / kGBM;
+  const int gx = (g.N + BN - 1) / BN, gy = (g.M + kGBM - 1) / kGBM;
   vec = vec && aligned16(g.A) && aligned16(g.B) && g.lda % 4 == 0 && g.ldb % 4 == 0 && g.sA % 4 == 0 && g.sB % 4 == 0;
   const long long tiles = (long long)gx * gy * batch;
   const int sms = device_sm_count(e.device);
@@ -779,9 +789,9 @@ int gemm(Engine &e, const GemmArgs &g0, int batch, const Epi &epi, bool vec) {
     const SimtStore part{e.train->split, (long long)g.N, (long long)g.M * g.N};
     const dim3 grid(gx, gy, batch * splits);
     if (vec)
-      snai_train_sgemm<A_KC, B_KC, true, SimtStore><<<grid, kGThreads, 0, e.stream>>>(g, part);
+      snai_train_sgemm<A_KC, B_KC, true, BN, SimtStore><<<grid, kGThreads, 0, e.stream>>>(g, part);
     else
-      snai_train_sgemm<A_KC, B_KC, false, SimtStore><<<grid, kGThreads, 0, e.stream>>>(g, part);
+      snai_train_sgemm<A_KC, B_KC, false, BN, SimtStore><<<grid, kGThreads, 0, e.stream>>>(g, part);
     const long long n4 = (long long)batch * g.M * ((g.N + 3) / 4);
     const int rb = (int)std::min<long long>((n4 + 255) / 256, (long long)sms * 8);
     snai_train_splitk_reduce<Epi><<<rb, 256, 0, e.stream>>>(e.train->split, splits, g.M, g.N, batch, epi);
@@ -790,11 +800,23 @@ int gemm(Engine &e, const GemmArgs &g0, int batch, const Epi &epi, bool vec) {
   }
   const dim3 grid(gx, gy, batch);
   if (vec)
-    snai_train_sgemm<A_KC, B_KC, true, Epi><<<grid, kGThreads, 0, e.stream>>>(g, epi);
+    snai_train_sgemm<A_KC, B_KC, true, BN, Epi><<<grid, kGThreads, 0, e.stream>>>(g, epi);
   else
-    snai_train_sgemm<A_KC, B_KC, false, Epi><<<grid, kGThreads, 0, e.stream>>>(g, epi);
+    snai_train_sgemm<A_KC, B_KC, false, BN, Epi><<<grid, kGThreads, 0, e.stream>>>(g, epi);
   e.launches++;
   return launch_rc("training GEMM");
+}
+
+// One GEMM launch; VEC when every operand row start is 16-byte aligned.  A
+// grid of fewer tiles than twice the SMs with a long k range is split over k
+// (partials in `split`, summed in split order by a second launch that runs
+// the epilogue), so that every SM gets work.  Products at most 64 columns
+// wide (the per-head attention products) take 128 x 64 tiles.
+template <bool A_KC, bool B_KC, class Epi>
+int gemm(Engine &e, const GemmArgs &g, int batch, const Epi &epi, bool vec) {
+  if (g.M <= 0 || g.N <= 0) return 0;
+  if (g.N <= 64) return gemm_bn<A_KC, B_KC, 64>(e, g, batch, epi, vec);
+  return gemm_bn<A_KC, B_KC, 128>(e, g, batch, epi, vec);
 }
 
 GemmArgs args(int M, int N, int K, const float *A, long long lda, const float *B, long long ldb, int causal = 0,
