@@ -2215,9 +2215,11 @@ __global__ void __launch_bounds__(kSampThreads, NV4 <= 8 ? 2 : 1) sample_b_reg(c
 
 constexpr int kStreamCapMax = 1024;   // candidate buffer entries per warp at most (top-k 256)
 constexpr int kStreamSlots = 2;       // staged chunks in flight per warp
-constexpr int kStreamPer = 8;         // 16-byte words per lane per chunk
+constexpr int kStreamPer = 8;         // 16-byte words per lane per chunk (variant A: 32 ids, one bitmap word)
 constexpr int kStreamChunk = 32 * kStreamPer;  // 16-byte words per chunk
-static_assert(kStreamPer * 4 <= 64, "one mask bit per staged entry of a lane");
+constexpr int kStreamBPer = 8;        // variant B: 16-byte words per lane per chunk (4 and 6 measured slower at V=16384)
+constexpr int kStreamBChunk = 32 * kStreamBPer;
+static_assert(kStreamBPer * 4 <= 64, "one mask bit per staged entry of a lane");
 constexpr int kStreamMaxK = 256;      // top-k the buffer supports
 constexpr int kStreamWarps = 20;      // warps per CTA at most
 
@@ -2234,7 +2236,7 @@ __host__ __device__ inline StreamLayout stream_layout(int V, int k) {
   L.cap = (2 * k + 128 + 31) / 32 * 32;
   if (L.cap < 256) L.cap = 256;
   if (L.cap > kStreamCapMax) L.cap = kStreamCapMax;
-  unsigned o = up16(kStreamSlots * kStreamChunk * 16);  // staged chunks
+  unsigned o = up16(kStreamSlots * kStreamBChunk * 16);  // staged chunks
   L.off_val = o;
   o = up16(o + (unsigned)L.cap * 8u);  // double values (then 64-bit keys, then running sums)
   L.off_bm = o;
@@ -2438,7 +2440,7 @@ __device__ __forceinline__ void stream_take(const float *rf, unsigned long long 
     st.cnt += tot;
   } else {
 #pragma unroll 1
-    for (int r = 0; r < kStreamPer; ++r) {
+    for (int r = 0; r < kStreamBPer; ++r) {
       unsigned long long kr = keep & (0xFull << (4 * r));
       if (st.cnt > cap - 128) {
         st.cnt = stream_compact(bval, bid, rh, st.cnt, k, st.t);
@@ -2672,7 +2674,7 @@ __device__ __noinline__ void stream_finish(const SampArgs &a, int b, StreamState
 __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __grid_constant__ SampArgs a, int W) {
   extern __shared__ __align__(16) uint8_t smem_dyn[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int V = a.V, n4 = V >> 2, S = (n4 + kStreamChunk - 1) / kStreamChunk;
+  const int V = a.V, n4 = V >> 2, S = (n4 + kStreamBChunk - 1) / kStreamBChunk;
   const int k = a.T < 0.01 ? 1 : min(a.top_k, V);
   const StreamLayout Ly = stream_layout(V, k);
   const int cap = Ly.cap;
@@ -2704,10 +2706,10 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
   const float4 *Lp = mp >= 0 ? reinterpret_cast<const float4 *>(a.logits + (size_t)mp * a.ld) : nullptr;
   auto issue = [&](int slot) {
     if (Lp != nullptr) {
-      const int c0 = ps * kStreamChunk + lane;
+      const int c0 = ps * kStreamBChunk + lane;
 #pragma unroll
-      for (int r = 0; r < kStreamPer; ++r)
-        if (c0 + 32 * r < n4) cp_async16(ring + slot * kStreamChunk + 32 * r + lane, Lp + c0 + 32 * r);
+      for (int r = 0; r < kStreamBPer; ++r)
+        if (c0 + 32 * r < n4) cp_async16(ring + slot * kStreamBChunk + 32 * r + lane, Lp + c0 + 32 * r);
     }
     cp_async_commit();
     if (++ps == S) {
@@ -2732,7 +2734,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
   // take the three-pass path).  G >= k makes it a true bound.
   int gl = 32;
   if (k > 1) {
-    const float x = (float)k * (float)(kStreamChunk * 4) / (float)V;
+    const float x = (float)k * (float)(kStreamBChunk * 4) / (float)V;
     int G = 8;
     while (G < 32 && G < k && (float)G < 2.5f * x) G <<= 1;
     gl = 32 / G;
@@ -2743,13 +2745,13 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
     const int slot = (int)(q % kStreamSlots);
     cp_async_wait<kStreamSlots - 1>();  // this chunk
     if (cs == 0 && ci > 0) mark_history(a, mrow_of(ci), bm);
-    const int c0 = cs * kStreamChunk;
+    const int c0 = cs * kStreamBChunk;
     const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-    float4 x[kStreamPer];
+    float4 x[kStreamBPer];
     float m = -INFINITY;
 #pragma unroll
-    for (int r = 0; r < kStreamPer; ++r) {
-      x[r] = c0 + 32 * r + lane < n4 ? ring[slot * kStreamChunk + 32 * r + lane] : ninf;
+    for (int r = 0; r < kStreamBPer; ++r) {
+      x[r] = c0 + 32 * r + lane < n4 ? ring[slot * kStreamBChunk + 32 * r + lane] : ninf;
       m = fmaxf(m, fmax4(x[r]));
     }
     if (cs == 0) {
@@ -2773,13 +2775,13 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
     if (__any_sync(0xffffffffu, m >= st.traw)) {
       unsigned long long bits = 0ull;
 #pragma unroll
-      for (int r = 0; r < kStreamPer; ++r) {
+      for (int r = 0; r < kStreamBPer; ++r) {
         const bool valid = c0 + 32 * r + lane < n4;
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           if (valid && f4_at(x[r], j) >= st.traw) bits |= 1ull << (4 * r + j);
       }
-      stream_take(reinterpret_cast<const float *>(ring + slot * kStreamChunk), bits, c0, st, bval, bid, bm, rh, k,
+      stream_take(reinterpret_cast<const float *>(ring + slot * kStreamBChunk), bits, c0, st, bval, bid, bm, rh, k,
                   a.rep, cut_at, cap);
     }
     issue(slot);  // the slot's next chunk (this lane's words were read above)
