@@ -233,3 +233,43 @@ def test_train_zero_tokens_and_ctx_cut(model_dir, built):
     e.close()
     o.close()
     o2.close()
+
+
+def test_training_cluster_round(model_dir, built):
+    """The reference's training-cluster round (src/train_cluster.php:144-224
+    with src/train_worker.php:113-145): each worker trains its own copy of
+    the model on its own text, then the workers' weights are averaged.  Here
+    two FP32 engines take two steps each on different sequences, then
+    cortex_average_states averages them on the GPU; the oracle does the same
+    with two oracle states and the merge restatement.  Every averaged weight
+    is within two Adam steps of the oracle's (a gradient below the GEMMs'
+    rounding may step the other way), and the update directions agree."""
+    from snai_b200 import average_states
+    p = make_model(model_dir, "tr_a.snai", 1001, 128, 140, 2, seed=21, std=0.08)
+    rng = np.random.default_rng(12)
+    lr = 0.003
+    data = [[seq(rng, 1001, 120) for _ in range(2)] for _ in range(2)]
+    engines = [Cortex(p, num_heads=2) for _ in range(2)]
+    oracles = [O.Oracle(p, num_heads=2) for _ in range(2)]
+    W0 = {k: oracles[0].tensor(k[0], k[1]).astype(np.float64) for k in keys(2)}
+    for w in range(2):
+        for x, y in data[w]:
+            lg = engines[w].train_step(x, y, lr)
+            lo = oracles[w].train_step(x, y, lr)
+            assert abs(lg - lo) <= 1e-4 * abs(lo), (w, lg, lo)
+    average_states(engines)
+    for k in keys(2):
+        a = engines[0].tensor(k[0], k[1]).astype(np.float64)
+        assert np.array_equal(a, engines[1].tensor(k[0], k[1]))  # every engine holds the average
+        # src/train_cluster.php:188-205: sum in worker order (double), divide, store fp32
+        b = ((oracles[0].tensor(k[0], k[1]).astype(np.float64) + oracles[1].tensor(k[0], k[1])) / 2.0)
+        b = b.astype(np.float32).astype(np.float64)
+        assert np.abs(a - b).max() <= 2 * lr + 1e-6, k
+        da, db = a - W0[k], b - W0[k]
+        if db.any():
+            cos = float(da @ db / (np.linalg.norm(da) * np.linalg.norm(db)))
+            assert cos > 0.999, (k, cos)
+    for e in engines:
+        e.close()
+    for o in oracles:
+        o.close()
