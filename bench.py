@@ -922,6 +922,8 @@ def main():
     ap.add_argument("--gemm", action="store_true", help="only the projection micro-benchmark")
     ap.add_argument("--tokenizer", metavar="VOCAB_JSON", help="only the tokenizer throughput (host code)")
     ap.add_argument("--train", action="store_true", help="only the training-step lines (c2 and c4 models)")
+    ap.add_argument("--pass-lines", action="store_true",
+                    help="only the one-row fp32 pass lines (kernel per stage, persistent kernel, position 1000)")
     ap.add_argument("--seqs", type=int, default=None,
                     help="total sequences of the decode configuration (default: the configuration's), or rows of "
                          "the projection micro-benchmark (default 4096)")
@@ -938,6 +940,13 @@ def main():
         return
     if args.tokenizer:
         print(json.dumps(tokenizer_bench(args.tokenizer)), flush=True)
+        return
+    if args.pass_lines:
+        if rank == 0:
+            p = load_peaks()
+            for key, kw in (("gemv_pass", {}), ("gemv_pass_persistent", {"fused": True}),
+                            ("gemv_pass_pos1000", {"pos": 1000})):
+                print(json.dumps(dict(key=key, **gemv_pass_line(p, **kw))), flush=True)
         return
     if args.train:
         if rank == 0:
