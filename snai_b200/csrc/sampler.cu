@@ -2398,8 +2398,10 @@ __device__ __forceinline__ unsigned long long stream_filter(const float *rf, uns
     const int r = b >> 2, j = b & 3;
     const float f = rf[(32 * r + lane) * 4 + j];
     const int v = (c0 + 32 * r + lane) * 4 + j;
-    const double val = in_set(bm, v) ? __dsub_rn((double)f, rep) : (double)f;
-    if (__double2float_rd(val) >= t) keep |= 1ull << b;
+    // an unpenalised entry's lower bound is its float (fp32 -> double -> fp32
+    // rounds back to it): only penalised ids need the double subtraction
+    const bool ok = in_set(bm, v) ? __double2float_rd(__dsub_rn((double)f, rep)) >= t : f >= t;
+    if (ok) keep |= 1ull << b;
   }
   return keep;
 }

@@ -54,6 +54,7 @@ def seq(rng, V, n):
     ("tr_a", 1001, 128, 140, 2, 2, 131),  # hs 64, two row tiles, V and act not multiples of 4
     ("tr_b", 3001, 256, 300, 1, 4, 290),  # three row tiles, 24 logits column tiles
     ("tr_c", 203, 24, 40, 2, 4, 37),      # head size 6: unaligned head slices (scalar GEMM loads)
+    ("tr_d", 16384, 512, 300, 1, 8, 260), # the benchmark vocabulary and head size: K=16384 split-K products
 ])
 def test_train_gradients_vs_oracle(model_dir, built, shape, precision):
     name, V, D, ctx, L, heads, n = shape
