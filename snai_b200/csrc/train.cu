@@ -21,13 +21,15 @@
 //   weight gradient dY^T X as a TN GEMM), the SiLU derivative in the epilogue
 //   of dffn, attention from the recomputed scores (multiplied by 1/sqrtf(hs),
 //   as the reference's backward does), RMSNorm backward per row with the
-//   weight gradient summed over positions in the reference's (descending)
-//   order, inverse RoPE on dq, dk, and the embedding gradient scattered in
-//   descending position order.
+//   weight gradient summed over positions by a deterministic two-level sum,
+//   inverse RoPE on dq, dk, and the embedding gradient summed per token in
+//   descending position order, as the reference adds it.
 //
-// Precision: fp32 arithmetic throughout, as the reference (every GEMM is an
-// fp32 SIMT GEMM with fp32 accumulation; only the summation order differs
-// from the reference's sequential sums).  Adam itself is element-wise and
+// Precision: FP32 engines compute in fp32 throughout, as the reference (every
+// GEMM an fp32 SIMT GEMM with fp32 accumulation; only the summation order
+// differs from the reference's sequential sums).  TF32 and BF16 engines run
+// the projections' products on the TF32 tensor cores (fp32 operands, fp32
+// accumulation); everything else stays fp32.  Adam is element-wise and
 // rounds exactly as the reference (IEEE division and square root), so given
 // the same gradients and clip factor its result is bit-for-bit the
 // reference's.
@@ -54,11 +56,11 @@ namespace snai {
 // fp32 SIMT GEMM, three operand layouts, batched, with causal tile limits
 // ============================================================================
 //
-// C(m, n) = sum_k A(m, k) B(n, k) over a 128 x 128 (or 128 x 64) tile per CTA, 256
-// threads, 8 x 8 outputs per thread (rows ty*4..+3 and 64+ty*4..+3, columns
-// tx*4..+3 and 64+tx*4..+3, so every shared-memory read is a broadcast or a
-// conflict-free float4), k in steps of 8 through a two-stage shared-memory
-// ring fed from registers.
+// C(m, n) = sum_k A(m, k) B(n, k) over a 128 x 128 (or 128 x 64) tile per
+// CTA, 256 threads, 8 x 8 (8 x 4) outputs per thread (rows ty*4..+3 and
+// 64+ty*4..+3, columns tx*4..+3 and 64+tx*4..+3, so every shared-memory read
+// is a broadcast or a conflict-free float4), k in steps of 8 through a
+// two-stage shared-memory ring fed from registers.
 //   A_KC: A stored [m][k] (k contiguous), else [k][m] (m contiguous)
 //   B_KC: B stored [n][k] (k contiguous), else [k][n] (n contiguous)
 // so NT (X W^T) is <true, true>, NN (dY W) is <true, false> and TN (dY^T X)
@@ -990,6 +992,10 @@ int train_grads(Engine &e, const int *tin, const int *ttg, int act, float *loss_
   auto nn = [&](int N, int K, const float *A, long long lda, const float *W, const ET &te, auto simt) -> int {
     if (!tc) return gemm<true, false>(e, args(M, N, K, A, lda, W, N), 1, simt, true);
     const int Kp = (K + 3) / 4 * 4;
+    if (lda != Kp) {  // the tensor-core tiles read dense rows
+      set_error("training step: NN operand rows of %lld floats, %d expected", lda, Kp);
+      return -1;
+    }
     transpose(W, N, K, N, t.wt, Kp);
     return train_gemm_tc(e, M, N, Kp, A, t.wt, te);
   };
