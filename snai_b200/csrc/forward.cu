@@ -1250,9 +1250,29 @@ int device_sm_count(int dev) {
   return n;
 }
 
+// Launches kern on the engine's stream; with pdl as a programmatic dependent
+// launch (the kernel begins with grid_dep_wait before it reads anything the
+// previous kernel writes).
+template <typename... KArgs, typename... Args>
+static void launch_k(Engine &e, bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = e.stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  e.launches++;
+}
+
 // Persistent tcgen05 GEMM (snai_tileproj_tc_kernel): 128 x BN tiles, one CTA per SM.
 template <typename TIn, int BN, class Epi>
-static int launch_tcp(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
+static int launch_tcp(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi, bool pdl) {
   constexpr int STAGES = BN == 256 ? 4 : 6;
   using Sm = TcpSmem<BN, STAGES>;
   auto kern = snai_tileproj_tc_kernel<TIn, BN, STAGES, Epi>;
@@ -1269,14 +1289,13 @@ static int launch_tcp(Engine &e, int M, int N, int K, const void *A, const void 
   }
   const int tiles = ((M + kTcBM - 1) / kTcBM) * ((N + BN - 1) / BN);
   const int grid = std::min(tiles, sm_count(e.device));
-  kern<<<grid, kGemmThreads, Sm::kBytes, e.stream>>>(ta, tb, M, N, K, epi, e.err_d);
-  e.launches++;
+  launch_k(e, pdl, kern, dim3(grid), dim3(kGemmThreads), Sm::kBytes, ta, tb, M, N, K, epi, e.err_d);
   return 0;
 }
 
 // CTA-pair tcgen05 GEMM (snai_pairproj_tc_kernel): 256 x 256 tiles on SM pairs.
 template <typename TIn, class Epi>
-static int launch_tc2(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
+static int launch_tc2(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi, bool pdl) {
   constexpr int STAGES = 6;
   using Sm = Tc2Smem<STAGES>;
   auto kern = snai_pairproj_tc_kernel<TIn, STAGES, Epi>;
@@ -1293,13 +1312,16 @@ static int launch_tc2(Engine &e, int M, int N, int K, const void *A, const void 
   }
   const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
   const int pairs = std::max(1, std::min(tiles, sm_count(e.device) / 2));
-  kern<<<2 * pairs, kGemmThreads, Sm::kBytes, e.stream>>>(ta, tb, M, N, K, epi, e.err_d);
-  e.launches++;
+  launch_k(e, pdl, kern, dim3(2 * pairs), dim3(kGemmThreads), Sm::kBytes, ta, tb, M, N, K, epi, e.err_d);
   return 0;
 }
 
+// pdl: launch as a programmatic dependent of the previous kernel (its set-up
+// overlaps that kernel's tail).  Not after a long kernel of small CTAs
+// (attention): the GEMM's CTAs, parked on every SM with their shared memory
+// until it ends, would take that kernel's room.
 template <typename TIn, class Epi>
-static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi) {
+static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *W, const Epi &epi, bool pdl = true) {
   // Tile shape by a per-CTA cost model: a CTA streams (rows of A + rows of W)
   // per k-block for every tile it owns and multiplies them, so the cost is
   // (tiles per CTA) x max(128 + BN, MMA time), with the CTA pair's 256 x 256
@@ -1326,10 +1348,10 @@ static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *
       pick = bn;
     }
   }
-  if (pick == 0) return launch_tc2<TIn>(e, M, N, K, A, W, epi);
-  if (pick == 256) return launch_tcp<TIn, 256>(e, M, N, K, A, W, epi);
-  if (pick == 128) return launch_tcp<TIn, 128>(e, M, N, K, A, W, epi);
-  return launch_tcp<TIn, 64>(e, M, N, K, A, W, epi);
+  if (pick == 0) return launch_tc2<TIn>(e, M, N, K, A, W, epi, pdl);
+  if (pick == 256) return launch_tcp<TIn, 256>(e, M, N, K, A, W, epi, pdl);
+  if (pick == 128) return launch_tcp<TIn, 128>(e, M, N, K, A, W, epi, pdl);
+  return launch_tcp<TIn, 64>(e, M, N, K, A, W, epi, pdl);
 }
 
 // A product of the training step on the TF32 tensor cores: C[M, N] =
@@ -1338,26 +1360,6 @@ static int launch_tc(Engine &e, int M, int N, int K, const void *A, const void *
 int train_gemm_tc(Engine &e, int M, int N, int K, const float *A, const float *W, const EpiTrain &epi) {
   if (M <= 0 || N <= 0) return 0;
   return launch_tc<float>(e, M, N, K, A, W, epi);
-}
-
-// Launches kern on the engine's stream; with pdl as a programmatic dependent
-// launch (the kernel begins with grid_dep_wait before it reads anything the
-// previous kernel writes).
-template <typename... KArgs, typename... Args>
-static void launch_k(Engine &e, bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                     Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = e.stream;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = pdl ? 1 : 0;
-  cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
-  e.launches++;
 }
 
 template <class Epi>
@@ -1386,10 +1388,13 @@ static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const fl
 // C[M,N] = A[M,K] * W[N,K]^T with the epilogue `epi`.  `a_bytes` / `out_bytes`:
 // bytes per element of A and algorithmic output bytes (for the profiler).
 // With nrm.w (GEMV path only) A is the residual stream h and the input rows
-// are RMSNorm(h, nrm.w), normalised inside the GEMV.
+// are RMSNorm(h, nrm.w), normalised inside the GEMV.  after_long: the previous
+// kernel is a long one (attention), so a tensor-core launch does not start
+// early as its programmatic dependent.
 template <class Epi>
 static int project(Engine &e, int kind, int M, int N, int K, const void *A, const float *W32,
-                   const __nv_bfloat16 *W16, const Epi &epi, double out_bytes, GemvNorm nrm = GemvNorm{}) {
+                   const __nv_bfloat16 *W16, const Epi &epi, double out_bytes, GemvNorm nrm = GemvNorm{},
+                   bool after_long = false) {
   if (M <= 0) return 0;
   const bool tc = tc_path(e, M);
   const bool bf = tc && e.precision == kBF16;
@@ -1397,7 +1402,8 @@ static int project(Engine &e, int kind, int M, int N, int K, const void *A, cons
   const int tok = prof_begin(e);
   int rc = 0;
   if (tc) {
-    rc = bf ? launch_tc<__nv_bfloat16>(e, M, N, K, A, W16, epi) : launch_tc<float>(e, M, N, K, A, W32, epi);
+    rc = bf ? launch_tc<__nv_bfloat16>(e, M, N, K, A, W16, epi, !after_long)
+            : launch_tc<float>(e, M, N, K, A, W32, epi, !after_long);
   } else {
     launch_gemv(e, M, N, K, static_cast<const float *>(A), W32, epi, nrm);
   }
@@ -1405,6 +1411,9 @@ static int project(Engine &e, int kind, int M, int N, int K, const void *A, cons
   return rc;
 }
 
+// Attention is a programmatic dependent only on the GEMV path: after a
+// tensor-core projection, its grid of many small CTAs launched early measured
+// 15 % slower (9.2 against 8.0 ms per d=1024 decode step of 4096 rows).
 template <typename TA>
 static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_positions, bool defer) {
   const Dims &d = e.d;
@@ -1447,7 +1456,7 @@ static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_pos
 template <typename TA>
 static void launch_norm(Engine &e, int M, const int2 *gather, const float *w, TA *x) {
   const int tok = prof_begin(e);
-  launch_k(e, !tc_path(e, M), rmsnorm_kernel<TA>, dim3(M), dim3(kNormThreads), 0, e.h, gather, w, x, e.d.D);
+  launch_k(e, true, rmsnorm_kernel<TA>, dim3(M), dim3(kNormThreads), 0, e.h, gather, w, x, e.d.D);
   prof_end(e, tok, kProfNorm, (double)M * e.d.D * (4 + sizeof(TA)), 0.0);
 }
 
@@ -1559,7 +1568,7 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
   TA *att = static_cast<TA *>(e.att);
   TA *u = static_cast<TA *>(e.u);
   int tok = prof_begin(e);
-  launch_k(e, !tc_path(e, M), embed_norm_kernel<TA>, dim3(M), dim3(kNormThreads), 0, e.rows_d, tokens_d, e.emb,
+  launch_k(e, true, embed_norm_kernel<TA>, dim3(M), dim3(kNormThreads), 0, e.rows_d, tokens_d, e.emb,
            e.layers[0].rms_att, e.h, x, e.hist, e.seq_len_d, d.V, d.D, d.ctx);
   prof_end(e, tok, kProfEmbed, (double)M * d.D * (8 + ea), 0.0);
   for (int l = 0; l < d.L; ++l) {
@@ -1577,7 +1586,7 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
     launch_attention<TA>(e, M, l, att, kv_positions, defer);
     EpiResidual res;
     if (!residual_epi(e, M, &res)) return -5;
-    rc = project(e, kProfWo, M, d.D, d.D, att, w.wo, w.wo_h, res, 8.0 * M * d.D);
+    rc = project(e, kProfWo, M, d.D, d.D, att, w.wo, w.wo_h, res, 8.0 * M * d.D, GemvNorm{}, true);
     if (rc) return rc;
     if (!fuse) launch_norm<TA>(e, M, nullptr, w.rms_ffn, x);
     rc = project(e, kProfUp, M, d.F, d.D, fuse ? static_cast<const void *>(e.h) : x, w.wup, w.wup_h,

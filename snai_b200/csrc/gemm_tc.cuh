@@ -288,6 +288,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  // launched as a programmatic dependent: the set-up above (barriers, TMEM,
+  // descriptor prefetch) overlapped the previous kernel's tail; nothing it
+  // wrote is read before this wait.  The next kernel may then start its own
+  // set-up (a GEMM's shared memory keeps it off this kernel's SMs).
+  grid_dep_wait();
+  grid_dep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -542,6 +548,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  // programmatic dependent launch, as in the single-CTA kernel
+  grid_dep_wait();
+  grid_dep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
