@@ -62,11 +62,9 @@ __global__ void to_bf16_segments_kernel(const Bf16Segments segs) {
 
 constexpr int kNormThreads = 256;
 
-// Block sum of squares of a D-vector (parallel tree; the reference sums
-// sequentially, core/cortex.nim:119).
-__device__ __forceinline__ float block_sumsq(const float *x, int D, float *red) {
-  float s = 0.f;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) s = __fmaf_rn(x[i], x[i], s);
+// The block's sum of its threads' partial sums: warp sums, then the warps'
+// in warp order (every thread gets it).
+__device__ __forceinline__ float block_reduce_sum(float s, float *red) {
   s = warp_sum(s);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
   __syncthreads();
@@ -74,6 +72,14 @@ __device__ __forceinline__ float block_sumsq(const float *x, int D, float *red) 
   for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
   __syncthreads();
   return t;
+}
+
+// Block sum of squares of a D-vector (parallel tree; the reference sums
+// sequentially, core/cortex.nim:119).
+__device__ __forceinline__ float block_sumsq(const float *x, int D, float *red) {
+  float s = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) s = __fmaf_rn(x[i], x[i], s);
+  return block_reduce_sum(s, red);
 }
 
 // 1 / sqrt(ss/D + 1e-5), in the reference's float operations (:121).
@@ -113,30 +119,75 @@ __device__ __forceinline__ float warp_row_rms_inv(const float *__restrict__ hr, 
   return rms_inv(t, D);
 }
 
+// The rows of a pass of at most kRowPackMax rows, passed by value to the
+// embedding kernel, which writes them to the device row arrays for the later
+// kernels of the pass (so the pass needs no host-to-device copy).  n = 0: the
+// rows are on the device already.
+constexpr int kRowPackMax = 8;
+struct RowPack {
+  RowDesc r[kRowPackMax];
+  int2 out[kRowPackMax];
+  int n, n_out;
+};
+
+// h[m] = emb[token], x[m] = RMSNorm(h[m], w); the token into the history.
+// Rows of D <= 16 * kNormThreads keep their values in registers between the
+// copy and the norm (the same sums as block_sumsq over h).
 template <typename TA>
-__global__ void __launch_bounds__(kNormThreads) embed_norm_kernel(const RowDesc *__restrict__ rows,
+__global__ void __launch_bounds__(kNormThreads) embed_norm_kernel(const RowDesc *rows, const RowPack pk,
+                                                                  RowDesc *rows_w,
+                                                                  int2 *__restrict__ outrows_w,
                                                                   const int *__restrict__ tokens_d,
                                                                   const float *__restrict__ emb,
                                                                   const float *__restrict__ w, float *__restrict__ h,
                                                                   TA *__restrict__ x, int *__restrict__ hist,
                                                                   int *__restrict__ seq_len, int V, int D, int ctx) {
+  constexpr int RV = 16;
   __shared__ float red[kNormThreads / 32];
   grid_dep_wait();
   grid_dep_launch();
   const int m = blockIdx.x;
-  const RowDesc rd = rows[m];
+  const RowDesc rd = pk.n ? pk.r[m] : rows[m];
+  if (pk.n) {
+    if (threadIdx.x == 0) rows_w[m] = rd;
+    if (m == 0 && (int)threadIdx.x < pk.n_out) outrows_w[threadIdx.x] = pk.out[threadIdx.x];
+  }
   const int raw = tokens_d ? tokens_d[rd.token] : rd.token;
   const int tid = (raw < 0 || raw >= V) ? 0 : raw;
   const float *e = emb + (size_t)tid * D;
   float *hr = h + (size_t)m * D;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) hr[i] = e[i];
   if (threadIdx.x == 0) {
     hist[(size_t)rd.slot * ctx + rd.pos] = raw;
     atomicMax(&seq_len[rd.slot], rd.pos + 1);
   }
+  TA *xr = x + (size_t)m * D;
+  if (D <= RV * kNormThreads) {
+    float v[RV];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < RV; ++j) {
+      const int i = threadIdx.x + j * kNormThreads;
+      v[j] = i < D ? e[i] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < RV; ++j) {
+      const int i = threadIdx.x + j * kNormThreads;
+      if (i < D) {
+        hr[i] = v[j];
+        s = __fmaf_rn(v[j], v[j], s);
+      }
+    }
+    const float inv = rms_inv(block_reduce_sum(s, red), D);
+#pragma unroll
+    for (int j = 0; j < RV; ++j) {
+      const int i = threadIdx.x + j * kNormThreads;
+      if (i < D) ActIO<TA>::store(xr + i, __fmul_rn(__fmul_rn(v[j], inv), w[i]));
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < D; i += blockDim.x) hr[i] = e[i];
   __syncthreads();
   const float inv = rms_inv(block_sumsq(hr, D, red), D);
-  TA *xr = x + (size_t)m * D;
   for (int i = threadIdx.x; i < D; i += blockDim.x) ActIO<TA>::store(xr + i, __fmul_rn(__fmul_rn(hr[i], inv), w[i]));
 }
 
@@ -506,20 +557,43 @@ __global__ void __launch_bounds__(kAttThreads) attention_split_hs64_kernel(
   const RowDesc rd = rows[m];
   const int n = rd.pos + 1, C = (n + kAttChunk - 1) / kAttChunk;
   float *pp = part + (size_t)(m * H + head) * S * kAttPW;
-  if (c < C) {
-    const AttRow r = att_row(rd, q, kv, m, head, att_ch, slot_stride, layer_off, part_stride, head_stride, kvs,
-                             rope, warp == 0 && c == (n - 1) / kAttChunk);
-    att_warp_chunk(r, c * kAttChunk, sqrt_hs, wp4 + warp * kAttPW, warp);
-    __syncthreads();
-    if (threadIdx.x < HS) att_chunk_combine(wp4, threadIdx.x, pp + c * kAttPW);
+  // the row's C chunks take part; the other CTAs of the (row, head) leave
+  if (c >= C) return;
+  TA *orow = out + (size_t)m * D;
+  const AttRow r = att_row(rd, q, kv, m, head, att_ch, slot_stride, layer_off, part_stride, head_stride, kvs, rope,
+                           warp == 0 && c == (n - 1) / kAttChunk);
+  att_warp_chunk(r, c * kAttChunk, sqrt_hs, wp4 + warp * kAttPW, warp);
+  __syncthreads();
+  if (C == 1) {
+    // one chunk: its partial (att_chunk_combine's operations) and the merge
+    // of that one partial (att_merge's), in registers, straight to att
+    if (threadIdx.x < HS) {
+      const int ch = threadIdx.x;
+      float Mc = wp4[0];
+#pragma unroll
+      for (int w = 1; w < 4; ++w) Mc = fmaxf(Mc, wp4[w * kAttPW]);
+      float Lc = 0.f, Oc = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float s = expf(__fsub_rn(wp4[w * kAttPW], Mc));
+        Lc = __fadd_rn(Lc, __fmul_rn(s, wp4[w * kAttPW + 1]));
+        Oc = __fadd_rn(Oc, __fmul_rn(s, wp4[w * kAttPW + 4 + ch]));
+      }
+      const float Mm = fmaxf(-9999.0f, Mc);
+      const float s = expf(__fsub_rn(Mc, Mm));
+      const float L = __fadd_rn(0.f, __fmul_rn(s, Lc)), O = __fadd_rn(0.f, __fmul_rn(s, Oc));
+      ActIO<TA>::store(orow + head * HS + ch, __fdiv_rn(O, L));
+    }
+    if (head == H - 1) att_zero_tail(orow, att_ch, D);
+    return;
   }
+  if (threadIdx.x < HS) att_chunk_combine(wp4, threadIdx.x, pp + c * kAttPW);
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(&cnt[m * H + head], 1) == S - 1;
+  if (threadIdx.x == 0) is_last = atomicAdd(&cnt[m * H + head], 1) == C - 1;
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  TA *orow = out + (size_t)m * D;
   if (threadIdx.x < HS)
     ActIO<TA>::store(orow + head * HS + threadIdx.x,
                      att_merge(pp, C, threadIdx.x, [](const float *p) { return __ldcg(p); }));
@@ -727,6 +801,147 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 2)
         float v[16] = {tot, t1};
         epi.store(m, n0 + r, v, n0 + r + 1 < N ? 2 : 1);
       }
+    }
+  }
+}
+
+// ============================================================================
+// fp32 GEMV for one or two rows: the CTA's weight rows staged in shared memory
+// ============================================================================
+//
+// A pass of one or two rows reads every weight once and does little
+// arithmetic with it, so a chain of these GEMVs is bound by how early each
+// one's weights are on their way.  Here a CTA owns R consecutive weight rows
+// over all of K (one contiguous block of R * K * 4 <= 64 KB) and copies them
+// into shared memory with bulk copies issued before it waits for the
+// previous kernel.  The CTA holds few registers, so CTAs of the next GEMV of
+// the chain find room beside it and start their own copies while this one
+// computes.  The arithmetic is the register GEMV's: the same slices of K, the
+// same lane FMA chains over four float4 per slice, the same warp butterfly,
+// and the slice sums added in slice order, so a row gets the same bits from
+// either kernel.
+constexpr int kRowTileBytes = 64 * 1024;
+constexpr int kRowTileThreads = 128;
+constexpr int kRowTileMaxItems = 16;  // (row quad, K slice) pairs of a CTA
+constexpr uint32_t kRowTileCopy = 16 * 1024;
+
+template <int MB, bool NORM, class Epi>
+__global__ void __launch_bounds__(kRowTileThreads)
+    snai_rowtile_f32_kernel(const float *__restrict__ W, int N, int K, const float *__restrict__ X, int M, int S,
+                            int slice, int R, Epi epi, GemvNorm nrm, int *err) {
+  constexpr int NV = 4 * MB;  // values a lane reduces per item: [m][row]
+  constexpr int G = 32 / NV;
+  extern __shared__ __align__(128) uint8_t rowtile_smem[];
+  __shared__ __align__(8) uint64_t full;
+  __shared__ float part[kRowTileMaxItems][NV];
+  const float *tile = reinterpret_cast<const float *>(rowtile_smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * R;
+  const int rows = min(R, N - row0);
+  // the weights never change during a pass: they may be fetched before the
+  // previous kernel has finished
+  if (threadIdx.x == 0) {
+    const uint32_t bytes = (uint32_t)rows * (uint32_t)K * 4u;
+    mbar_init(&full, 1);
+    fence_barrier_init();
+    mbar_arrive_expect_tx(&full, bytes);
+    const char *src = reinterpret_cast<const char *>(W + (size_t)row0 * K);
+    for (uint32_t o = 0; o < bytes; o += kRowTileCopy) {
+      const uint32_t n = min(kRowTileCopy, bytes - o);
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              smem_u32(rowtile_smem + o)),
+          "l"(src + o), "r"(n), "r"(smem_u32(&full))
+          : "memory");
+    }
+  }
+  __syncthreads();
+  grid_dep_launch();
+  grid_dep_wait();
+  const int nq = (rows + 3) / 4, items = nq * S;
+  float inv[MB];
+#pragma unroll
+  for (int j = 0; j < MB; ++j) inv[j] = 1.f;
+  if constexpr (NORM) {
+#pragma unroll
+    for (int j = 0; j < MB; ++j)
+      if (j < M && warp < items) inv[j] = warp_row_rms_inv(X + (size_t)(nrm.gather ? nrm.gather[j].x : j) * K, K, lane);
+  }
+  // this lane's input values of item `it`'s K slice (normalised with NORM)
+  auto load_x = [&](int it, float4(&xv)[MB][4]) {
+    const int qi = it / S, s = it - qi * S;
+    const int ks = s * slice, ke = min(K, ks + slice);
+#pragma unroll
+    for (int j = 0; j < MB; ++j) {
+      const float *xr = X + (size_t)(NORM && nrm.gather ? nrm.gather[j].x : j) * K;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = ks + lane * 4 + 128 * i;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < M && k < ke) {
+          v = __ldg(reinterpret_cast<const float4 *>(xr + k));
+          if constexpr (NORM) {
+            const float4 nw = __ldg(reinterpret_cast<const float4 *>(nrm.w + k));
+            v.x = __fmul_rn(__fmul_rn(v.x, inv[j]), nw.x);
+            v.y = __fmul_rn(__fmul_rn(v.y, inv[j]), nw.y);
+            v.z = __fmul_rn(__fmul_rn(v.z, inv[j]), nw.z);
+            v.w = __fmul_rn(__fmul_rn(v.w, inv[j]), nw.w);
+          }
+        }
+        xv[j][i] = v;
+      }
+    }
+  };
+  float4 xv[MB][4];
+  if (warp < items) load_x(warp, xv);
+  // every thread sees the copies land (or the whole CTA gives up together)
+  const bool late = !mbar_wait_bounded(&full, 0u, err, kErrWaitFull);
+  if (__syncthreads_or(late)) {
+    // do not leave while copies into this CTA's shared memory may be in flight
+    if (threadIdx.x == 0) mbar_wait_bounded(&full, 0u, err, kErrWaitDrain);
+    return;
+  }
+  for (int it = warp; it < items; it += kRowTileThreads / 32) {
+    if (it != warp) load_x(it, xv);
+    const int qi = it / S, s = it - qi * S;
+    const int ks = s * slice, ke = min(K, ks + slice);
+    float acc[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) acc[j] = 0.f;
+#pragma unroll
+    for (int j = 0; j < MB; ++j) {
+      if (j >= M) break;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = ks + lane * 4 + 128 * i;
+        if (k < ke) {
+          const float4 x4 = xv[j][i];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const float4 w = 4 * qi + r < rows ? *reinterpret_cast<const float4 *>(tile + (size_t)(4 * qi + r) * K + k)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            acc[4 * j + r] =
+                fmaf(w.x, x4.x, fmaf(w.y, x4.y, fmaf(w.z, x4.z, fmaf(w.w, x4.w, acc[4 * j + r]))));
+          }
+        }
+      }
+    }
+    gemv_reduce<NV, 16, NV>(acc, lane);
+    if (lane % G == 0) part[it][lane / G] = acc[0];
+  }
+  __syncthreads();
+  // per quad and (row, weight row) pair: the slice sums in slice order
+  for (int t = threadIdx.x; t < nq * NV; t += blockDim.x) {
+    const int qi = t / NV, jv = t - qi * NV, m = jv / 4, r = jv % 4;
+    const int n = row0 + 4 * qi + r;
+    if ((r & 1) == 0 && m < M && n < N) {
+      float v0 = part[qi * S][jv], v1 = part[qi * S][jv + 1];
+      for (int s = 1; s < S; ++s) {
+        v0 = __fadd_rn(v0, part[qi * S + s][jv]);
+        v1 = __fadd_rn(v1, part[qi * S + s][jv + 1]);
+      }
+      float v[16] = {v0, v1};
+      epi.store(m, n, v, n + 1 < N ? 2 : 1);
     }
   }
 }
@@ -1370,6 +1585,29 @@ static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const fl
   // two CTAs per SM
   const int S = std::max(1, std::min(kGemvMaxWarps, (K + kGemvPass - 1) / kGemvPass));
   const int slice = ((K + S - 1) / S + 127) / 128 * 128;
+  // one or two rows: the staged-tile kernel, R rows of W per CTA (the most
+  // that fit its 64 KB, fewer while that leaves under two CTAs per SM)
+  if (M <= 2 && (size_t)K * 16 <= kRowTileBytes && (K & 3) == 0) {
+    int R = 16;
+    while (R > 4 && (size_t)R * K * 4 > kRowTileBytes) R /= 2;
+    while (R > 4 && (N + R - 1) / R < 2 * sm_count(e.device)) R /= 2;
+    if ((R / 4) * S <= kRowTileMaxItems) {
+      void (*kern)(const float *, int, int, const float *, int, int, int, int, Epi, GemvNorm, int *) =
+          nrm.w ? snai_rowtile_f32_kernel<1, true, Epi>
+                : (M <= 1 ? snai_rowtile_f32_kernel<1, false, Epi> : snai_rowtile_f32_kernel<2, false, Epi>);
+      static DeviceOnce attr;  // per Epi: the three instantiations at once
+      const bool ready = attr.run(e.device, [] {
+        const bool a = set_dyn_smem(snai_rowtile_f32_kernel<1, true, Epi>, kRowTileBytes);
+        const bool b = set_dyn_smem(snai_rowtile_f32_kernel<1, false, Epi>, kRowTileBytes);
+        return set_dyn_smem(snai_rowtile_f32_kernel<2, false, Epi>, kRowTileBytes) && a && b;
+      });
+      if (ready) {
+        launch_k(e, true, kern, dim3((N + R - 1) / R), dim3(kRowTileThreads), (size_t)R * K * 4, W, N, K, X, M, S,
+                 slice, R, epi, nrm, e.err_d);
+        return;
+      }
+    }
+  }
   const int quads = (N + 3) / 4, target = 2 * sm_count(e.device);
   int P = 1;
   while (2 * P * S <= kGemvMaxWarps && quads / (2 * P) >= target) P *= 2;
@@ -1556,19 +1794,42 @@ static int launch_pass(Engine &e, int M, const int *tokens_d, double kv_position
   return 0;
 }
 
+// Copies a chunk's rows (e.rows_stage, e.out_stage) to the device.
+static int upload_rows(Engine &e, int M, int n_out) {
+  if (cudaMemcpyAsync(e.rows_d, e.rows_stage.data(), sizeof(RowDesc) * M, cudaMemcpyHostToDevice, e.stream) !=
+          cudaSuccess ||
+      (n_out && cudaMemcpyAsync(e.outrows_d, e.out_stage.data(), sizeof(int2) * n_out, cudaMemcpyHostToDevice,
+                                e.stream) != cudaSuccess)) {
+    set_error("row upload failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return -4;
+  }
+  return 0;
+}
+
+// pack: the chunk's rows by value (the embedding kernel writes them to the
+// device), or nullptr when they are on the device already.
 template <typename TA>
 static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, bool out_tc, double kv_positions,
-                           bool defer) {
+                           bool defer, const RowPack *pack) {
   const Dims &d = e.d;
   if constexpr (sizeof(TA) == 4) {
-    if (pass_kernel_ok(e, M, n_out, defer)) return launch_pass(e, M, tokens_d, kv_positions);
+    if (pass_kernel_ok(e, M, n_out, defer)) {
+      if (pack) {
+        const int rc = upload_rows(e, M, n_out);
+        if (rc) return rc;
+      }
+      return launch_pass(e, M, tokens_d, kv_positions);
+    }
   }
+  RowPack pk{};
+  if (pack) pk = *pack;
   const double ea = sizeof(TA);
   TA *x = static_cast<TA *>(e.x);
   TA *att = static_cast<TA *>(e.att);
   TA *u = static_cast<TA *>(e.u);
   int tok = prof_begin(e);
-  launch_k(e, true, embed_norm_kernel<TA>, dim3(M), dim3(kNormThreads), 0, e.rows_d, tokens_d, e.emb,
+  launch_k(e, true, embed_norm_kernel<TA>, dim3(M), dim3(kNormThreads), 0, e.rows_d, pk, e.rows_d, e.outrows_d,
+           tokens_d, e.emb,
            e.layers[0].rms_att, e.h, x, e.hist, e.seq_len_d, d.V, d.D, d.ctx);
   prof_end(e, tok, kProfEmbed, (double)M * d.D * (8 + ea), 0.0);
   for (int l = 0; l < d.L; ++l) {
@@ -1676,10 +1937,11 @@ __global__ void finish_step_kernel(const int *__restrict__ ids, int *__restrict_
 }
 
 // One chunk of rows in the operand type of its path.
-static int run_chunk(Engine &e, int M, const int *tokens_d, int n_out, bool out_tc, double kv_positions, bool defer) {
+static int run_chunk(Engine &e, int M, const int *tokens_d, int n_out, bool out_tc, double kv_positions, bool defer,
+                     const RowPack *pack = nullptr) {
   return (tc_path(e, M) && e.precision == kBF16)
-             ? run_chunk_typed<__nv_bfloat16>(e, M, tokens_d, n_out, out_tc, kv_positions, defer)
-             : run_chunk_typed<float>(e, M, tokens_d, n_out, out_tc, kv_positions, defer);
+             ? run_chunk_typed<__nv_bfloat16>(e, M, tokens_d, n_out, out_tc, kv_positions, defer, pack)
+             : run_chunk_typed<float>(e, M, tokens_d, n_out, out_tc, kv_positions, defer, pack);
 }
 
 int decode_step_device(Engine &e, int batch, const SampleLaunch &sampler) {
@@ -1725,15 +1987,20 @@ int run_rows(Engine &e, const RowDesc *rows, int n, const int *tokens_d) {
       defer = !e.slot_seen[s];
       e.slot_seen[s] = 1;
     }
-    if (cudaMemcpyAsync(e.rows_d, e.rows_stage.data(), sizeof(RowDesc) * M, cudaMemcpyHostToDevice, e.stream) !=
-            cudaSuccess ||
-        (n_out && cudaMemcpyAsync(e.outrows_d, e.out_stage.data(), sizeof(int2) * n_out, cudaMemcpyHostToDevice,
-                                  e.stream) != cudaSuccess)) {
-      set_error("row upload failed: %s", cudaGetErrorString(cudaGetLastError()));
-      return -4;
+    // a chunk of a few rows goes to the device by value, with the first kernel
+    const bool by_value = M <= kRowPackMax;
+    RowPack pack{};
+    if (by_value) {
+      for (int i = 0; i < M; ++i) pack.r[i] = e.rows_stage[i];
+      for (int i = 0; i < n_out; ++i) pack.out[i] = e.out_stage[i];
+      pack.n = M;
+      pack.n_out = n_out;
+    } else {
+      const int rc = upload_rows(e, M, n_out);
+      if (rc) return rc;
     }
     const bool out_tc = tc_path(e, n_out);
-    const int rc = run_chunk(e, M, tokens_d, n_out, out_tc, kv_positions, defer);
+    const int rc = run_chunk(e, M, tokens_d, n_out, out_tc, kv_positions, defer, by_value ? &pack : nullptr);
     if (rc) return rc;
     const cudaError_t le = cudaGetLastError();
     if (le != cudaSuccess) {

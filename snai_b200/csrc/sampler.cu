@@ -2688,7 +2688,10 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) sample_b_stream(const __
   unsigned *rh = reinterpret_cast<unsigned *>(base + Ly.off_rh);
   double *P = reinterpret_cast<double *>(base + Ly.off_p);
   int *ord = reinterpret_cast<int *>(base + Ly.off_ord);
-  const int NW = gridDim.x * W, gw = blockIdx.x * W + warp;
+  // warp-major numbering: row r goes to CTA r % grid, so every SM gets an
+  // equal share of the rows (to within one); the warps of an SM share its
+  // issue slots, so the SM with the most rows sets the kernel's time
+  const int NW = gridDim.x * W, gw = warp * gridDim.x + blockIdx.x;
   if (warp >= W || gw >= a.rows) return;
   const int nrows = (a.rows - 1 - gw) / NW + 1;
   // logits / history row of the warp's i-th row (-1 past the last)
@@ -3102,7 +3105,10 @@ __global__ void __launch_bounds__(kStreamAWarps * 32, 1) sample_a_stream(const _
   uint32_t *bm = reinterpret_cast<uint32_t *>(base + Ly.off_bm);
   float4 *tab = reinterpret_cast<float4 *>(base + Ly.off_ch);
   float *pv = reinterpret_cast<float *>(base + Ly.off_pv);
-  const int NW = gridDim.x * W, gw = blockIdx.x * W + warp;
+  // warp-major numbering: row r goes to CTA r % grid, so every SM gets an
+  // equal share of the rows (to within one); the warps of an SM share its
+  // issue slots, so the SM with the most rows sets the kernel's time
+  const int NW = gridDim.x * W, gw = warp * gridDim.x + blockIdx.x;
   if (warp >= W || gw >= a.rows) return;
   const int nrows = (a.rows - 1 - gw) / NW + 1;
   const float cexp = (float)(1.4426950408889634 * a.Tinv);
