@@ -311,7 +311,8 @@ template <bool COHERENT = false>
 __device__ __forceinline__ AttRow att_row(const RowDesc &rd, const float *__restrict__ q, float *__restrict__ kv,
                                           int m, int head, int att_ch, size_t slot_stride, size_t layer_off,
                                           size_t part_stride, size_t head_stride, const float *__restrict__ kvs,
-                                          const float2 *__restrict__ rope, bool append) {
+                                          const float2 *__restrict__ rope, bool append,
+                                          const float4 *cs_pre = nullptr) {
   constexpr int HS = 64;
   const int lane = threadIdx.x & 31, half = lane >> 4, pi = lane & 15;
   AttRow r;
@@ -327,7 +328,7 @@ __device__ __forceinline__ AttRow att_row(const RowDesc &rd, const float *__rest
   r.vnew = r.knew;
   if (kvs) {
     const float *kst = kvs + (size_t)m * 2 * att_ch + head * HS;
-    const float4 cs = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + pi * 2);
+    const float4 cs = cs_pre ? *cs_pre : *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + pi * 2);
     r.qv = rope4(r.qv, cs);
     r.knew = rope4(ld4(kst + pi * 4), cs);
     r.vnew = ld4(kst + att_ch + pi * 4);
@@ -337,22 +338,39 @@ __device__ __forceinline__ AttRow att_row(const RowDesc &rd, const float *__rest
   return r;
 }
 
-// Warp `warp` (0..3)'s (m_w, l_w, o_w) of the chunk starting at t0 into wp (kAttPW floats).
-__device__ __forceinline__ void att_warp_chunk(const AttRow &r, int t0, float sqrt_hs, float *wp, int warp) {
-  constexpr int HS = 64, U = 8;
+// Warp `warp` (0..3)'s K and V rows of the chunk starting at t0 that come
+// from the cache (positions below nc; zero elsewhere).
+constexpr int kAttU = 8;  // position pairs per warp of a chunk
+__device__ __forceinline__ void att_chunk_load(const float *kbase, const float *vbase, int nc, int n, int t0, int warp,
+                                               float4 (&kr)[kAttU], float4 (&vr)[kAttU]) {
+  constexpr int HS = 64, U = kAttU;
   const int lane = threadIdx.x & 31, half = lane >> 4, pi = lane & 15;
-  const int t1 = min(r.n, t0 + kAttChunk);
-  float4 kr[U], vr[U];
+  const int t1 = min(n, t0 + kAttChunk);
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const int t = t0 + 2 * (warp * U + u) + half;
-    const bool cached = t < min(r.nc, t1);
-    kr[u] = cached ? __ldcs(reinterpret_cast<const float4 *>(r.kbase + (size_t)t * HS + pi * 4))
-            : t < t1 ? r.knew
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
-    vr[u] = cached ? __ldcs(reinterpret_cast<const float4 *>(r.vbase + (size_t)t * HS + pi * 4))
-            : t < t1 ? r.vnew
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool cached = t < min(nc, t1);
+    kr[u] = cached ? __ldcs(reinterpret_cast<const float4 *>(kbase + (size_t)t * HS + pi * 4))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    vr[u] = cached ? __ldcs(reinterpret_cast<const float4 *>(vbase + (size_t)t * HS + pi * 4))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// Warp `warp` (0..3)'s (m_w, l_w, o_w) of the chunk starting at t0 into wp
+// (kAttPW floats), from its cached rows (att_chunk_load) and the new position's.
+__device__ __forceinline__ void att_chunk_compute(const AttRow &r, int t0, float sqrt_hs, float *wp, int warp,
+                                                  float4 (&kr)[kAttU], float4 (&vr)[kAttU]) {
+  constexpr int U = kAttU;
+  const int lane = threadIdx.x & 31, half = lane >> 4, pi = lane & 15;
+  const int t1 = min(r.n, t0 + kAttChunk);
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int t = t0 + 2 * (warp * U + u) + half;
+    if (!(t < min(r.nc, t1)) && t < t1) {
+      kr[u] = r.knew;
+      vr[u] = r.vnew;
+    }
   }
   float sc[U];
   float mx = -9999.0f;
@@ -396,6 +414,13 @@ __device__ __forceinline__ void att_warp_chunk(const AttRow &r, int t0, float sq
     wp[0] = mx;
     wp[1] = ls;
   }
+}
+
+// Warp `warp` (0..3)'s (m_w, l_w, o_w) of the chunk starting at t0 into wp (kAttPW floats).
+__device__ __forceinline__ void att_warp_chunk(const AttRow &r, int t0, float sqrt_hs, float *wp, int warp) {
+  float4 kr[kAttU], vr[kAttU];
+  att_chunk_load(r.kbase, r.vbase, r.nc, r.n, t0, warp, kr, vr);
+  att_chunk_compute(r, t0, sqrt_hs, wp, warp, kr, vr);
 }
 
 // Channel ch (< 64) of a chunk's partial from its four warps' (warp order).
@@ -544,25 +569,44 @@ __global__ void __launch_bounds__(kAttThreads) attention_hs64_kernel(
 // captured launch serves every later step.
 template <typename TA>
 __global__ void __launch_bounds__(kAttThreads) attention_split_hs64_kernel(
-    const RowDesc *__restrict__ rows, const float *__restrict__ q, float *__restrict__ kv, TA *__restrict__ out,
-    int D, int att_ch, size_t slot_stride, size_t layer_off, size_t part_stride, size_t head_stride, float sqrt_hs,
-    const float *__restrict__ kvs, const float2 *__restrict__ rope, float *__restrict__ part, int *__restrict__ cnt) {
+    const RowDesc *__restrict__ rows, const RowPack pk, const float *__restrict__ q, float *__restrict__ kv,
+    TA *__restrict__ out, int D, int att_ch, size_t slot_stride, size_t layer_off, size_t part_stride,
+    size_t head_stride, float sqrt_hs, const float *__restrict__ kvs, const float2 *__restrict__ rope,
+    float *__restrict__ part, int *__restrict__ cnt) {
   constexpr int HS = 64;
   __shared__ __align__(16) float wp4[4 * kAttPW];
   __shared__ int is_last;
+  const int head = blockIdx.x, m = blockIdx.y, c = blockIdx.z, S = gridDim.z, H = gridDim.x;
+  const int warp = threadIdx.x >> 5, pi = threadIdx.x & 15;
+  // A decode pass whose rows came by value: the row, this chunk's cached K
+  // and V rows and the RoPE factors are read before the wait for the
+  // previous kernel (QKV), which writes none of them: earlier passes wrote
+  // the cache, and no kernel of this pass starts before the previous pass
+  // has finished (the pass's first kernel waits before it lets the next
+  // one start).
+  const bool early = pk.n > 0 && kvs != nullptr;
+  float4 kr[kAttU], vr[kAttU], cs = make_float4(0.f, 0.f, 0.f, 0.f);
+  RowDesc rd = early ? pk.r[m] : RowDesc{};
+  if (early) {
+    const int n = rd.pos + 1;
+    if (c * kAttChunk < n) {
+      const float *kbase = kv + (size_t)rd.slot * slot_stride + layer_off + (size_t)head * head_stride;
+      att_chunk_load(kbase, kbase + part_stride, n - 1, n, c * kAttChunk, warp, kr, vr);
+      cs = *reinterpret_cast<const float4 *>(rope + (size_t)rd.pos * (HS / 2) + pi * 2);
+    }
+  }
   grid_dep_wait();
   grid_dep_launch();
-  const int head = blockIdx.x, m = blockIdx.y, c = blockIdx.z, S = gridDim.z, H = gridDim.x;
-  const int warp = threadIdx.x >> 5;
-  const RowDesc rd = rows[m];
+  if (!early) rd = rows[m];
   const int n = rd.pos + 1, C = (n + kAttChunk - 1) / kAttChunk;
   float *pp = part + (size_t)(m * H + head) * S * kAttPW;
   // the row's C chunks take part; the other CTAs of the (row, head) leave
   if (c >= C) return;
   TA *orow = out + (size_t)m * D;
   const AttRow r = att_row(rd, q, kv, m, head, att_ch, slot_stride, layer_off, part_stride, head_stride, kvs, rope,
-                           warp == 0 && c == (n - 1) / kAttChunk);
-  att_warp_chunk(r, c * kAttChunk, sqrt_hs, wp4 + warp * kAttPW, warp);
+                           warp == 0 && c == (n - 1) / kAttChunk, early ? &cs : nullptr);
+  if (!early) att_chunk_load(r.kbase, r.vbase, r.nc, r.n, c * kAttChunk, warp, kr, vr);
+  att_chunk_compute(r, c * kAttChunk, sqrt_hs, wp4 + warp * kAttPW, warp, kr, vr);
   __syncthreads();
   if (C == 1) {
     // one chunk: its partial (att_chunk_combine's operations) and the merge
@@ -859,41 +903,58 @@ __global__ void __launch_bounds__(kRowTileThreads)
   grid_dep_launch();
   grid_dep_wait();
   const int nq = (rows + 3) / 4, items = nq * S;
-  float inv[MB];
-#pragma unroll
-  for (int j = 0; j < MB; ++j) inv[j] = 1.f;
-  if constexpr (NORM) {
-#pragma unroll
-    for (int j = 0; j < MB; ++j)
-      if (j < M && warp < items) inv[j] = warp_row_rms_inv(X + (size_t)(nrm.gather ? nrm.gather[j].x : j) * K, K, lane);
-  }
-  // this lane's input values of item `it`'s K slice (normalised with NORM)
-  auto load_x = [&](int it, float4(&xv)[MB][4]) {
+  // this lane's input values of item `it`'s K slice, as read (and the norm
+  // weights there with NORM) ...
+  auto load_x = [&](int it, float4(&xv)[MB][4], float4(&nw)[4]) {
     const int qi = it / S, s = it - qi * S;
     const int ks = s * slice, ke = min(K, ks + slice);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = ks + lane * 4 + 128 * i;
+      nw[i] = NORM && k < ke ? __ldg(reinterpret_cast<const float4 *>(nrm.w + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 #pragma unroll
     for (int j = 0; j < MB; ++j) {
       const float *xr = X + (size_t)(NORM && nrm.gather ? nrm.gather[j].x : j) * K;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int k = ks + lane * 4 + 128 * i;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (j < M && k < ke) {
-          v = __ldg(reinterpret_cast<const float4 *>(xr + k));
-          if constexpr (NORM) {
-            const float4 nw = __ldg(reinterpret_cast<const float4 *>(nrm.w + k));
-            v.x = __fmul_rn(__fmul_rn(v.x, inv[j]), nw.x);
-            v.y = __fmul_rn(__fmul_rn(v.y, inv[j]), nw.y);
-            v.z = __fmul_rn(__fmul_rn(v.z, inv[j]), nw.z);
-            v.w = __fmul_rn(__fmul_rn(v.w, inv[j]), nw.w);
-          }
-        }
-        xv[j][i] = v;
+        xv[j][i] = j < M && k < ke ? __ldg(reinterpret_cast<const float4 *>(xr + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
   };
-  float4 xv[MB][4];
-  if (warp < items) load_x(warp, xv);
+  // ... then normalised (NORM): x * inv * w
+  float inv[MB];
+#pragma unroll
+  for (int j = 0; j < MB; ++j) inv[j] = 1.f;
+  auto norm_x = [&](int it, float4(&xv)[MB][4], const float4(&nw)[4]) {
+    if constexpr (NORM) {
+      const int qi = it / S, s = it - qi * S;
+      const int ks = s * slice, ke = min(K, ks + slice);
+#pragma unroll
+      for (int j = 0; j < MB; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = ks + lane * 4 + 128 * i;
+          if (j < M && k < ke) {
+            float4 &v = xv[j][i];
+            v.x = __fmul_rn(__fmul_rn(v.x, inv[j]), nw[i].x);
+            v.y = __fmul_rn(__fmul_rn(v.y, inv[j]), nw[i].y);
+            v.z = __fmul_rn(__fmul_rn(v.z, inv[j]), nw[i].z);
+            v.w = __fmul_rn(__fmul_rn(v.w, inv[j]), nw[i].w);
+          }
+        }
+    }
+  };
+  float4 xv[MB][4], nw[4];
+  // the first item's inputs are on their way while the rows' rms is taken
+  if (warp < items) load_x(warp, xv, nw);
+  if constexpr (NORM) {
+#pragma unroll
+    for (int j = 0; j < MB; ++j)
+      if (j < M && warp < items) inv[j] = warp_row_rms_inv(X + (size_t)(nrm.gather ? nrm.gather[j].x : j) * K, K, lane);
+  }
+  if (warp < items) norm_x(warp, xv, nw);
   // every thread sees the copies land (or the whole CTA gives up together)
   const bool late = !mbar_wait_bounded(&full, 0u, err, kErrWaitFull);
   if (__syncthreads_or(late)) {
@@ -902,7 +963,10 @@ __global__ void __launch_bounds__(kRowTileThreads)
     return;
   }
   for (int it = warp; it < items; it += kRowTileThreads / 32) {
-    if (it != warp) load_x(it, xv);
+    if (it != warp) {
+      load_x(it, xv, nw);
+      norm_x(it, xv, nw);
+    }
     const int qi = it / S, s = it - qi * S;
     const int ks = s * slice, ke = min(K, ks + slice);
     float acc[NV];
@@ -942,6 +1006,173 @@ __global__ void __launch_bounds__(kRowTileThreads)
       }
       float v[16] = {v0, v1};
       epi.store(m, n, v, n + 1 < N ? 2 : 1);
+    }
+  }
+}
+
+// ============================================================================
+// fp32 GEMV for one or two rows over many weight rows: a shared-memory ring
+// ============================================================================
+//
+// For a matrix of many rows (the logits, V x D) the staged-tile kernel runs
+// in waves, and each wave's copies start only when a CTA of the wave before
+// has finished.  Here one CTA per SM streams its contiguous share of row
+// quads through shared memory: consumer warp w takes the CTA's quads w,
+// w + 8, ... through its own D slots (a quad of rows over all of K, K <=
+// 1024, per slot), and one producer thread refills each slot as soon as its
+// warp has read it, issuing the first copies before the dependency wait.  A
+// warp's slots are used strictly in turn, so a wait on a slot's phase never
+// sees an older phase of the same parity.  A consumer warp computes a whole
+// quad, both K slices in slice order, with the register GEMV's lane FMA
+// chains and butterfly, so a row's bits are those of the other GEMVs.
+constexpr int kRingConsumers = 8;
+constexpr int kRingThreads = (kRingConsumers + 1) * 32;
+constexpr int kRingSlotsMax = 16;
+constexpr int kRingBytes = 128 * 1024;
+constexpr int kRingMinQuadsPerSm = 16;  // below this the staged-tile kernel's one wave is as quick
+
+template <int MB, bool NORM, class Epi>
+__global__ void __launch_bounds__(kRingThreads, 1)
+    snai_rowring_f32_kernel(const float *__restrict__ W, int N, int K, const float *__restrict__ X, int M, int S,
+                            int slice, int D, Epi epi, GemvNorm nrm, int *err) {
+  constexpr int NV = 4 * MB;
+  constexpr int G = 32 / NV;
+  constexpr int SMAX = 2;  // K <= 1024: at most two 512-column slices
+  extern __shared__ __align__(128) uint8_t ring_smem[];
+  __shared__ __align__(8) uint64_t full[kRingSlotsMax], empty[kRingSlotsMax];
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quads = (N + 3) / 4;
+  const int q0 = (int)((long long)quads * blockIdx.x / gridDim.x);
+  const int q1 = (int)((long long)quads * (blockIdx.x + 1) / gridDim.x);
+  const uint32_t slot_bytes = 16u * (uint32_t)K;
+  const int NS = kRingConsumers * D;  // slot w * D + d: warp w's d-th
+  // quad j of the CTA: warp j % 8, its (j / 8)-th, slot use (j / 8) / D
+  auto slot_of = [&](int j) { return (j % kRingConsumers) * D + (j / kRingConsumers) % D; };
+  auto use_of = [&](int j) { return (j / kRingConsumers) / D; };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  grid_dep_launch();
+  if (warp == kRingConsumers) {
+    // ---- producer: the CTA's quads in order, each once its slot is free ----
+    // (the weights never change during a pass: the first copies go out before
+    // the wait for the previous kernel)
+    if (lane == 0) {
+      int j = 0;
+      for (int q = q0; q < q1; ++q, ++j) {
+        const int sl = slot_of(j), u = use_of(j);
+        if (u > 0 && (!mbar_wait_bounded(&empty[sl], (uint32_t)(u - 1) & 1u, err, kErrWaitEmpty) ||
+                      *(volatile int *)&abort_flag)) {
+          abort_flag = 1;
+          break;
+        }
+        const uint32_t bytes = (uint32_t)min(4, N - 4 * q) * (uint32_t)K * 4u;
+        mbar_arrive_expect_tx(&full[sl], bytes);
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                smem_u32(ring_smem + (size_t)sl * slot_bytes)),
+            "l"(W + (size_t)q * 4 * K), "r"(bytes), "r"(smem_u32(&full[sl]))
+            : "memory");
+      }
+      // do not leave while a copy into this CTA's shared memory is in flight
+      for (int i = j - 1; i >= 0 && i >= j - NS; --i)
+        if (!mbar_wait_bounded(&full[slot_of(i)], (uint32_t)use_of(i) & 1u, err, kErrWaitDrain)) break;
+    }
+    return;
+  }
+  // ---- consumers ----
+  grid_dep_wait();
+  // the lane's inputs of both slices as read, then (NORM) the rows' rms while
+  // they are on their way, then x * inv * w
+  float4 xv[MB][SMAX][4], nw[SMAX][4];
+#pragma unroll
+  for (int s = 0; s < SMAX; ++s)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int ks = s * slice, ke = min(K, ks + slice);
+      const int k = ks + lane * 4 + 128 * i;
+      const bool in = s < S && k < ke;
+      nw[s][i] = NORM && in ? __ldg(reinterpret_cast<const float4 *>(nrm.w + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < MB; ++j) {
+        const float *xr = X + (size_t)(NORM && nrm.gather ? nrm.gather[j].x : j) * K;
+        xv[j][s][i] = j < M && in ? __ldg(reinterpret_cast<const float4 *>(xr + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  if constexpr (NORM) {
+#pragma unroll
+    for (int j = 0; j < MB; ++j) {
+      if (j >= M) break;
+      const float inv = warp_row_rms_inv(X + (size_t)(nrm.gather ? nrm.gather[j].x : j) * K, K, lane);
+#pragma unroll
+      for (int s = 0; s < SMAX; ++s)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int ks = s * slice, ke = min(K, ks + slice);
+          const int k = ks + lane * 4 + 128 * i;
+          if (s < S && k < ke) {
+            float4 &v = xv[j][s][i];
+            v.x = __fmul_rn(__fmul_rn(v.x, inv), nw[s][i].x);
+            v.y = __fmul_rn(__fmul_rn(v.y, inv), nw[s][i].y);
+            v.z = __fmul_rn(__fmul_rn(v.z, inv), nw[s][i].z);
+            v.w = __fmul_rn(__fmul_rn(v.w, inv), nw[s][i].w);
+          }
+        }
+    }
+  }
+  for (int j = warp; q0 + j < q1; j += kRingConsumers) {
+    const int sl = slot_of(j), n0 = (q0 + j) * 4;
+    if (!mbar_wait_bounded(&full[sl], (uint32_t)use_of(j) & 1u, err, kErrWaitFull) ||
+        *(volatile int *)&abort_flag) {
+      abort_flag = 1;
+      break;
+    }
+    const float *wq = reinterpret_cast<const float *>(ring_smem + (size_t)sl * slot_bytes);
+    float tot = 0.f;
+#pragma unroll
+    for (int s = 0; s < SMAX; ++s) {
+      if (s >= S) break;
+      const int ks = s * slice, ke = min(K, ks + slice);
+      float acc[NV];
+#pragma unroll
+      for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+#pragma unroll
+      for (int jm = 0; jm < MB; ++jm) {
+        if (jm >= M) break;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = ks + lane * 4 + 128 * i;
+          if (k < ke) {
+            const float4 x4 = xv[jm][s][i];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const float4 w = n0 + r < N ? *reinterpret_cast<const float4 *>(wq + (size_t)r * K + k)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+              acc[4 * jm + r] =
+                  fmaf(w.x, x4.x, fmaf(w.y, x4.y, fmaf(w.z, x4.z, fmaf(w.w, x4.w, acc[4 * jm + r]))));
+            }
+          }
+        }
+      }
+      if (s == S - 1) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[sl]);  // every lane has read the slot
+      }
+      gemv_reduce<NV, 16, NV>(acc, lane);
+      tot = s == 0 ? acc[0] : __fadd_rn(tot, acc[0]);
+    }
+    const float t1 = __shfl_down_sync(0xffffffffu, tot, G);
+    const int idx = lane / G, m = idx / 4, r = idx % 4;
+    if (lane % G == 0 && (r & 1) == 0 && m < M && n0 + r < N) {
+      float v[16] = {tot, t1};
+      epi.store(m, n0 + r, v, n0 + r + 1 < N ? 2 : 1);
     }
   }
 }
@@ -1585,6 +1816,26 @@ static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const fl
   // two CTAs per SM
   const int S = std::max(1, std::min(kGemvMaxWarps, (K + kGemvPass - 1) / kGemvPass));
   const int slice = ((K + S - 1) / S + 127) / 128 * 128;
+  // one or two rows over many weight rows (K <= 1024): the ring kernel, one
+  // CTA per SM
+  const int sms = sm_count(e.device);
+  if (M <= 2 && K <= 1024 && (K & 3) == 0 && (N + 3) / 4 >= kRingMinQuadsPerSm * sms) {
+    const int D = std::max(1, std::min(kRingSlotsMax / kRingConsumers, kRingBytes / (kRingConsumers * 16 * K)));
+    void (*kern)(const float *, int, int, const float *, int, int, int, int, Epi, GemvNorm, int *) =
+        nrm.w ? snai_rowring_f32_kernel<1, true, Epi>
+              : (M <= 1 ? snai_rowring_f32_kernel<1, false, Epi> : snai_rowring_f32_kernel<2, false, Epi>);
+    static DeviceOnce attr;  // per Epi: the three instantiations at once
+    const bool ready = attr.run(e.device, [] {
+      const bool a = set_dyn_smem(snai_rowring_f32_kernel<1, true, Epi>, kRingBytes);
+      const bool b = set_dyn_smem(snai_rowring_f32_kernel<1, false, Epi>, kRingBytes);
+      return set_dyn_smem(snai_rowring_f32_kernel<2, false, Epi>, kRingBytes) && a && b;
+    });
+    if (ready) {
+      launch_k(e, true, kern, dim3(sms), dim3(kRingThreads), (size_t)kRingConsumers * D * 16 * K, W, N, K, X, M, S,
+               slice, D, epi, nrm, e.err_d);
+      return;
+    }
+  }
   // one or two rows: the staged-tile kernel, R rows of W per CTA (the most
   // that fit its 64 KB, fewer while that leaves under two CTAs per SM)
   if (M <= 2 && (size_t)K * 16 <= kRowTileBytes && (K & 3) == 0) {
@@ -1653,7 +1904,8 @@ static int project(Engine &e, int kind, int M, int N, int K, const void *A, cons
 // tensor-core projection, its grid of many small CTAs launched early measured
 // 15 % slower (9.2 against 8.0 ms per d=1024 decode step of 4096 rows).
 template <typename TA>
-static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_positions, bool defer) {
+static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_positions, bool defer,
+                             const RowPack &pk) {
   const Dims &d = e.d;
   const int tok = prof_begin(e);
   const size_t layer_off = (size_t)layer * e.kv_layer_stride;
@@ -1673,7 +1925,7 @@ static void launch_attention(Engine &e, int M, int layer, TA *out, double kv_pos
                      chunks <= kSplitMax && (size_t)rh * chunks <= e.att_part_entries;
   if (split) {
     launch_k(e, !tc_path(e, M), attention_split_hs64_kernel<TA>, dim3(d.heads, M, chunks), dim3(kAttThreads), 0,
-             e.rows_d, e.q, e.kv, out, d.D, d.att_ch, e.kv_slot_stride, layer_off, e.kv_part_stride,
+             e.rows_d, pk, e.q, e.kv, out, d.D, d.att_ch, e.kv_slot_stride, layer_off, e.kv_part_stride,
              e.kv_head_stride, e.sqrt_hs, defer ? e.kvs : nullptr, e.rope, e.att_part, e.att_cnt);
   } else if (d.hs == 64) {
     const size_t sm = (32 + 4 * 64 + (size_t)max_n) * sizeof(float);
@@ -1844,7 +2096,7 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
     int rc = project(e, kProfQKV, M, 3 * d.D, d.D, fq ? static_cast<const void *>(e.h) : x, w.wqkv, w.wqkv_h, eq,
                      3.0 * M * d.att_ch * 4, fq ? GemvNorm{w.rms_att, nullptr} : GemvNorm{});
     if (rc) return rc;
-    launch_attention<TA>(e, M, l, att, kv_positions, defer);
+    launch_attention<TA>(e, M, l, att, kv_positions, defer, pk);
     EpiResidual res;
     if (!residual_epi(e, M, &res)) return -5;
     rc = project(e, kProfWo, M, d.D, d.D, att, w.wo, w.wo_h, res, 8.0 * M * d.D, GemvNorm{}, true);
