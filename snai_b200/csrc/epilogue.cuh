@@ -109,7 +109,9 @@ struct EpiQKV {
   }
 
   __device__ __forceinline__ void store(int m, int n, const float *v, int cnt) const {
-    const RowDesc rd = rows[m];
+    // a staged row needs no descriptor here (RoPE and the append happen in
+    // attention)
+    const RowDesc rd = kvs ? RowDesc{} : rows[m];
     if (cnt == 16 && (hs & 15) == 0 && (D & 15) == 0) {
       // 16 channels of one head of one part (n is a multiple of 16)
       const int part = n / D;

@@ -582,8 +582,8 @@ __global__ void __launch_bounds__(kAttThreads) attention_split_hs64_kernel(
   // and V rows and the RoPE factors are read before the wait for the
   // previous kernel (QKV), which writes none of them: earlier passes wrote
   // the cache, and no kernel of this pass starts before the previous pass
-  // has finished (the pass's first kernel waits before it lets the next
-  // one start).
+  // has finished (the pass's first kernel, the embedding kernel or the QKV
+  // GEMV that does its work, waits before it lets the next one start).
   const bool early = pk.n > 0 && kvs != nullptr;
   float4 kr[kAttU], vr[kAttU], cs = make_float4(0.f, 0.f, 0.f, 0.f);
   RowDesc rd = early ? pk.r[m] : RowDesc{};
@@ -747,9 +747,25 @@ __device__ __forceinline__ void gemv_reduce(float (&v)[NV], int lane) {
   }
 }
 
+// The first QKV GEMV of a one-row pass whose row came by value also does the
+// embedding kernel's work: X is the embedding table, the row's token picks
+// the input row, and CTA 0 writes h, the history and the pass's row
+// descriptors (after the wait for the previous kernel, which may read them).
+struct GemvEmbed {
+  const int *tokens_d;  // the row's token: tokens_d[r.token], or r.token when nullptr
+  float *h;
+  int *hist, *seq_len;
+  int V, ctx;
+  RowDesc *rows_w;
+  int2 *outrows_w;
+};
+
 struct GemvNorm {
   const float *w;       // RMSNorm weights [K]; nullptr: X is the input as is
   const int2 *gather;   // input row m = X[gather[m].x], or X[m] when nullptr
+  int emb = 0;          // 1: the embedding fold above (one row, staged-tile kernel)
+  GemvEmbed ef{};
+  RowPack pk{};
 };
 
 template <int MB, bool NORM, class Epi>
@@ -900,9 +916,36 @@ __global__ void __launch_bounds__(kRowTileThreads)
     }
   }
   __syncthreads();
-  grid_dep_launch();
+  // a pass's first kernel (the embedding fold) lets the next one start only
+  // once the previous pass has finished, as the embedding kernel does
+  const bool first = NORM && nrm.emb;
+  if (!first) grid_dep_launch();
   grid_dep_wait();
+  if (first) grid_dep_launch();
   const int nq = (rows + 3) / 4, items = nq * S;
+  // input row of row j: the token's embedding row (embedding fold), or
+  // gather[j].x, or j
+  int src[MB];
+#pragma unroll
+  for (int j = 0; j < MB; ++j) src[j] = NORM && nrm.gather ? nrm.gather[j].x : j;
+  if constexpr (NORM) {
+    if (nrm.emb) {
+      const RowDesc rd = nrm.pk.r[0];
+      const int raw = nrm.ef.tokens_d ? nrm.ef.tokens_d[rd.token] : rd.token;
+      src[0] = (raw < 0 || raw >= nrm.ef.V) ? 0 : raw;
+      if (blockIdx.x == 0) {
+        // the embedding kernel's writes: h, the history, the row descriptors
+        const float *er = X + (size_t)src[0] * K;
+        for (int k = threadIdx.x; k < K; k += blockDim.x) nrm.ef.h[k] = er[k];
+        if (threadIdx.x == 0) {
+          nrm.ef.hist[(size_t)rd.slot * nrm.ef.ctx + rd.pos] = raw;
+          atomicMax(&nrm.ef.seq_len[rd.slot], rd.pos + 1);
+          nrm.ef.rows_w[0] = rd;
+        }
+        if ((int)threadIdx.x < nrm.pk.n_out) nrm.ef.outrows_w[threadIdx.x] = nrm.pk.out[threadIdx.x];
+      }
+    }
+  }
   // this lane's input values of item `it`'s K slice, as read (and the norm
   // weights there with NORM) ...
   auto load_x = [&](int it, float4(&xv)[MB][4], float4(&nw)[4]) {
@@ -915,7 +958,7 @@ __global__ void __launch_bounds__(kRowTileThreads)
     }
 #pragma unroll
     for (int j = 0; j < MB; ++j) {
-      const float *xr = X + (size_t)(NORM && nrm.gather ? nrm.gather[j].x : j) * K;
+      const float *xr = X + (size_t)src[j] * K;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int k = ks + lane * 4 + 128 * i;
@@ -952,7 +995,7 @@ __global__ void __launch_bounds__(kRowTileThreads)
   if constexpr (NORM) {
 #pragma unroll
     for (int j = 0; j < MB; ++j)
-      if (j < M && warp < items) inv[j] = warp_row_rms_inv(X + (size_t)(nrm.gather ? nrm.gather[j].x : j) * K, K, lane);
+      if (j < M && warp < items) inv[j] = warp_row_rms_inv(X + (size_t)src[j] * K, K, lane);
   }
   if (warp < items) norm_x(warp, xv, nw);
   // every thread sees the copies land (or the whole CTA gives up together)
@@ -1809,8 +1852,8 @@ int train_gemm_tc(Engine &e, int M, int N, int K, const float *A, const float *W
 }
 
 template <class Epi>
-static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const float *W, const Epi &epi,
-                        GemvNorm nrm) {
+static int launch_gemv(Engine &e, int M, int N, int K, const float *X, const float *W, const Epi &epi,
+                       GemvNorm nrm) {
   // S warps split K into slices of whole 128-column steps (one 512-column
   // pass each up to K = 4096); P row quads per CTA while that still leaves
   // two CTAs per SM
@@ -1819,7 +1862,7 @@ static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const fl
   // one or two rows over many weight rows (K <= 1024): the ring kernel, one
   // CTA per SM
   const int sms = sm_count(e.device);
-  if (M <= 2 && K <= 1024 && (K & 3) == 0 && (N + 3) / 4 >= kRingMinQuadsPerSm * sms) {
+  if (!nrm.emb && M <= 2 && K <= 1024 && (K & 3) == 0 && (N + 3) / 4 >= kRingMinQuadsPerSm * sms) {
     const int D = std::max(1, std::min(kRingSlotsMax / kRingConsumers, kRingBytes / (kRingConsumers * 16 * K)));
     void (*kern)(const float *, int, int, const float *, int, int, int, int, Epi, GemvNorm, int *) =
         nrm.w ? snai_rowring_f32_kernel<1, true, Epi>
@@ -1833,7 +1876,7 @@ static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const fl
     if (ready) {
       launch_k(e, true, kern, dim3(sms), dim3(kRingThreads), (size_t)kRingConsumers * D * 16 * K, W, N, K, X, M, S,
                slice, D, epi, nrm, e.err_d);
-      return;
+      return 0;
     }
   }
   // one or two rows: the staged-tile kernel, R rows of W per CTA (the most
@@ -1855,9 +1898,13 @@ static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const fl
       if (ready) {
         launch_k(e, true, kern, dim3((N + R - 1) / R), dim3(kRowTileThreads), (size_t)R * K * 4, W, N, K, X, M, S,
                  slice, R, epi, nrm, e.err_d);
-        return;
+        return 0;
       }
     }
+  }
+  if (nrm.emb) {
+    set_error("the embedding fold needs the staged-tile GEMV (M=%d K=%d)", M, K);
+    return -5;
   }
   const int quads = (N + 3) / 4, target = 2 * sm_count(e.device);
   int P = 1;
@@ -1872,6 +1919,7 @@ static void launch_gemv(Engine &e, int M, int N, int K, const float *X, const fl
            : M <= 4 ? snai_rowproj_f32_kernel<4, false, Epi>
                     : snai_rowproj_f32_kernel<8, false, Epi>;
   launch_k(e, true, kern, grid, block, 0, W, N, K, X, M, S, slice, epi, nrm);
+  return 0;
 }
 
 // C[M,N] = A[M,K] * W[N,K]^T with the epilogue `epi`.  `a_bytes` / `out_bytes`:
@@ -1894,7 +1942,7 @@ static int project(Engine &e, int kind, int M, int N, int K, const void *A, cons
     rc = bf ? launch_tc<__nv_bfloat16>(e, M, N, K, A, W16, epi, !after_long)
             : launch_tc<float>(e, M, N, K, A, W32, epi, !after_long);
   } else {
-    launch_gemv(e, M, N, K, static_cast<const float *>(A), W32, epi, nrm);
+    rc = launch_gemv(e, M, N, K, static_cast<const float *>(A), W32, epi, nrm);
   }
   prof_end(e, tok, kind, w_bytes + a_bytes + out_bytes, 2.0 * M * N * K);
   return rc;
@@ -2079,11 +2127,15 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
   TA *x = static_cast<TA *>(e.x);
   TA *att = static_cast<TA *>(e.att);
   TA *u = static_cast<TA *>(e.u);
-  int tok = prof_begin(e);
-  launch_k(e, true, embed_norm_kernel<TA>, dim3(M), dim3(kNormThreads), 0, e.rows_d, pk, e.rows_d, e.outrows_d,
-           tokens_d, e.emb,
-           e.layers[0].rms_att, e.h, x, e.hist, e.seq_len_d, d.V, d.D, d.ctx);
-  prof_end(e, tok, kProfEmbed, (double)M * d.D * (8 + ea), 0.0);
+  // a one-row pass whose row came by value: the first QKV GEMV does the
+  // embedding kernel's work (one launch fewer)
+  const bool fold = gemv_norm(e, M) && pk.n == 1 && d.D % 4 == 0 && (size_t)d.D * 16 <= kRowTileBytes;
+  if (!fold) {
+    const int tok = prof_begin(e);
+    launch_k(e, true, embed_norm_kernel<TA>, dim3(M), dim3(kNormThreads), 0, e.rows_d, pk, e.rows_d, e.outrows_d,
+             tokens_d, e.emb, e.layers[0].rms_att, e.h, x, e.hist, e.seq_len_d, d.V, d.D, d.ctx);
+    prof_end(e, tok, kProfEmbed, (double)M * d.D * (8 + ea), 0.0);
+  }
   for (int l = 0; l < d.L; ++l) {
     const LayerWeights &w = e.layers[l];
     EpiQKV eq{e.rows_d, e.q, e.kv, e.rope, d.D, d.att_ch, d.hs, e.kv_slot_stride, (size_t)l * e.kv_layer_stride,
@@ -2093,8 +2145,16 @@ static int run_chunk_typed(Engine &e, int M, const int *tokens_d, int n_out, boo
     // normalise h inside the QKV GEMV on a small pass
     const bool fuse = gemv_norm(e, M);
     const bool fq = fuse && l > 0;
-    int rc = project(e, kProfQKV, M, 3 * d.D, d.D, fq ? static_cast<const void *>(e.h) : x, w.wqkv, w.wqkv_h, eq,
-                     3.0 * M * d.att_ch * 4, fq ? GemvNorm{w.rms_att, nullptr} : GemvNorm{});
+    GemvNorm nq = fq ? GemvNorm{w.rms_att, nullptr} : GemvNorm{};
+    const void *qa = fq ? static_cast<const void *>(e.h) : x;
+    if (fold && l == 0) {
+      nq = GemvNorm{w.rms_att, nullptr};
+      nq.emb = 1;
+      nq.ef = GemvEmbed{tokens_d, e.h, e.hist, e.seq_len_d, d.V, d.ctx, e.rows_d, e.outrows_d};
+      nq.pk = pk;
+      qa = e.emb;
+    }
+    int rc = project(e, kProfQKV, M, 3 * d.D, d.D, qa, w.wqkv, w.wqkv_h, eq, 3.0 * M * d.att_ch * 4, nq);
     if (rc) return rc;
     launch_attention<TA>(e, M, l, att, kv_positions, defer, pk);
     EpiResidual res;
