@@ -233,6 +233,28 @@ def test_streaming_kernels_large_batch(V, built):
         assert np.array_equal(got, want), (variant, T)
 
 
+@pytest.mark.parametrize("kind", ["spiky", "flat"])
+def test_variant_a_every_row_of_a_large_batch(kind, built):
+    """Variant A over 4096 rows of V=16384 against the oracle, every row: the
+    rows the streaming kernel cannot certify (a few per thousand of the
+    benchmark's spiky rows, many more of near-uniform ones) go through the
+    CTA-per-row kernel's mixed tier (exact exponentials for the entries that
+    carry the row's mass) and, failing that, the exact tiers."""
+    R, V, H = 4096, 16384, 256
+    rng = np.random.default_rng(11 if kind == "spiky" else 12)
+    if kind == "spiky":
+        L = (rng.standard_normal((R, V)) * 2.0).astype(np.float32)
+        L += (rng.random((R, V)) < 0.01).astype(np.float32) * 12.0
+    else:
+        L = (rng.standard_normal((R, V)) * 0.05).astype(np.float32)
+    hist = rng.integers(0, V, (R, H)).astype(np.int32)
+    U = rng.random(R).astype(np.float32)
+    got = gpu_sample(L, hist, U, sample_params(VARIANT_A, 0.7, 1.15, nan_guard=0))
+    want, _ = O.sample_rows(L, hist, U, VARIANT_A, 0.7, 1.15, exp_mode=1, nthreads=os.cpu_count() or 1)
+    bad = np.flatnonzero(got != want)
+    assert bad.size == 0, (kind, bad[:8], got[bad[:8]], want[bad[:8]])
+
+
 def test_nan_guard_and_argument_errors(built):
     from snai_b200 import CortexError
     rng = np.random.default_rng(1)
