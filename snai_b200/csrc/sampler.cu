@@ -456,12 +456,8 @@ struct SmemA {
 // P(i, j) gives p of entry j of this thread's chunk layer i (as a double);
 // `eps` bounds |p~ - p| / p for every entry (0 for the contract exp) and
 // `eabs` the absolute error of an entry whose p~ underflowed.
-// `eadd` bounds the error of all entries together, over and above eps and
-// eabs (the mixed tier: exact values for the entries that carry the row's
-// mass, tier-1 values for the rest).
 template <int NV4, class PF>
-__device__ __forceinline__ int certified_draw(SmemA &sm, int V, int nl, double u, double eps, double eabs, const PF &P,
-                                              double eadd = 0.0) {
+__device__ __forceinline__ int certified_draw(SmemA &sm, int V, int nl, double u, double eps, double eabs, const PF &P) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // ---- segment sums (segment i = chunk layer i = 2048 consecutive ids) ----
   for (int g0 = 0; g0 < nl; g0 += 32) {
@@ -566,10 +562,10 @@ __device__ __forceinline__ int certified_draw(SmemA &sm, int V, int nl, double u
       // sums are within eps*P(1+2eps) + (v+1)*eabs of the contract's.
       const double slack = (double)(nl + 64);
       const double er = eps * (1.0 + 2.0 * eps) + 1e-12 * (eps > 0.0);
-      const double Er = u * (er * S + eadd + (double)V * eabs + ((double)V + slack) * 0x1p-52 * S) + 0x1p-52 * r;
+      const double Er = u * (er * S + (double)V * eabs + ((double)V + slack) * 0x1p-52 * S) + 0x1p-52 * r;
       const double hi = sm.cand_hi, lo = sm.cand_lo;
-      const double Ehi = er * hi + eadd + ((double)cand + 1.0) * eabs + ((double)cand + slack) * 0x1p-52 * hi;
-      const double Elo = er * lo + eadd + (double)cand * eabs + ((double)cand + slack) * 0x1p-52 * lo;
+      const double Ehi = er * hi + ((double)cand + 1.0) * eabs + ((double)cand + slack) * 0x1p-52 * hi;
+      const double Elo = er * lo + (double)cand * eabs + ((double)cand + slack) * 0x1p-52 * lo;
       const bool up = hi - Ehi >= r + Er;
       const bool dn = cand == 0 || lo + Elo < r - Er;
       ok = up && dn;
@@ -815,57 +811,34 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
     }
     const double u = (double)a.uniforms[b];
     int id = -1;
-    // tier 1: p~ = 2^(x c - M log2e), c = fp32(log2e / T); penalised entries
-    // use their exact value t: 2^(t log2e - M log2e).
-    const float c = (float)(1.4426950408889634 * a.Tinv);
-    const float l2e = 1.44269504f;
-    const float m2 = M * l2e;
-    // |t| <= tabs for every entry (|x/T| rounded up a little)
-    const double tabs = (double)tabs_in * fmax(1.0, fabs(a.Tinv)) * (1.0 + 0x1p-20);
-    const double eps = (tabs + fabs((double)M) + 1.0) * 0x1p-21 + 0x1p-19;
-    auto P1 = [&](int i, int j) {
-      uint32_t pb;
-      const float4 x = row.get(i, bits, pen_fn, pb);
-      const float mult = ((pb >> j) & 1u) ? l2e : c;
-      return (double)ex2_approx(fmaf(f4_at(x, j), mult, -m2));
-    };
-    // tier 2: the contract exponential of the exact stored values
-    auto P2 = [&](int i, int j) {
-      uint32_t pb;
-      const float4 x = row.get(i, bits, pen_fn, pb);
-      const float f = f4_at(x, j);
-      const float t = ((pb >> j) & 1u) ? f : div_to_f32(f, a.T, a.Tinv);
-      return snai_exp(__dsub_rn((double)t, maxv));
-    };
-    if (any && simple && !a.redo)  // a redo row has failed a tier-1 bound already
-      id = certified_draw<NV4>(sm, V, nl, u, eps, 0x1p-125, P1);
-    if (id < 0 && any && simple) {
-      // mixed tier: the contract exponential for the entries with p~ >=
-      // 2^-20 (those that carry the row's mass; p <= 1 at the maximum), the
-      // tier-1 value for the rest, whose errors add up to at most eps times
-      // their total A (A measured first, then taken with margin) plus eabs
-      // for every entry.  Exact whenever certified, like the other tiers.
-      constexpr double kMixThr = 0x1p-20;
-      double small = 0.0;
-      for_layers<NV4>(nl, [&](int i) {
-        const int v0 = (threadIdx.x + kSampThreads * i) * 4;
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (v0 + j < V) {
-            const double q = P1(i, j);
-            if (q < kMixThr) small = __dadd_rn(small, q);
-          }
-      });
-      double A = 0.0;
-      block_excl_scan(small, sm.wsum, A);
-      const double eadd = eps * (1.0 + 2.0 * eps) * A * (1.0 + 0x1p-20) + (double)V * 0x1p-125;
-      auto Pm = [&](int i, int j) {
-        const double q = P1(i, j);
-        return q < kMixThr ? q : P2(i, j);
+    if (any && simple && !a.redo) {  // a redo row has failed a tier-1 bound already
+      // tier 1: p~ = 2^(x c - M log2e), c = fp32(log2e / T); penalised entries
+      // use their exact value t: 2^(t log2e - M log2e).
+      const float c = (float)(1.4426950408889634 * a.Tinv);
+      const float l2e = 1.44269504f;
+      const float m2 = M * l2e;
+      // |t| <= tabs for every entry (|x/T| rounded up a little)
+      const double tabs = (double)tabs_in * fmax(1.0, fabs(a.Tinv)) * (1.0 + 0x1p-20);
+      const double eps = (tabs + fabs((double)M) + 1.0) * 0x1p-21 + 0x1p-19;
+      auto P1 = [&](int i, int j) {
+        uint32_t pb;
+        const float4 x = row.get(i, bits, pen_fn, pb);
+        const float mult = ((pb >> j) & 1u) ? l2e : c;
+        return (double)ex2_approx(fmaf(f4_at(x, j), mult, -m2));
       };
-      id = certified_draw<NV4>(sm, V, nl, u, 0.0, 0.0, Pm, eadd);
+      id = certified_draw<NV4>(sm, V, nl, u, eps, 0x1p-125, P1);
     }
-    if (id < 0 && any) id = certified_draw<NV4>(sm, V, nl, u, 0.0, 0.0, P2);
+    if (id < 0 && any) {
+      // tier 2: the contract exponential of the exact stored values
+      auto P2 = [&](int i, int j) {
+        uint32_t pb;
+        const float4 x = row.get(i, bits, pen_fn, pb);
+        const float f = f4_at(x, j);
+        const float t = ((pb >> j) & 1u) ? f : div_to_f32(f, a.T, a.Tinv);
+        return snai_exp(__dsub_rn((double)t, maxv));
+      };
+      id = certified_draw<NV4>(sm, V, nl, u, 0.0, 0.0, P2);
+    }
     if (id < 0) {
       // tier 3
       if (warp == 0) {
@@ -881,27 +854,13 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
   } else {
     // the marked rows (kRedoMark, or already redone: <= kRedoDone) in id
     // order; this CTA takes those of rank = blockIdx.x (mod gridDim.x)
-    // (the out[] words of 16 rounds of 512 rows are read at once: one trip to
-    // L2 for up to 8192 rows instead of one per round)
-    constexpr int kRounds = 16;
     __shared__ int redo_cnt[kSampWarps];
     __shared__ int redo_list[kSampThreads];
     int seen = 0;
-    unsigned mkbits = 0u, newbits = 0u;  // per round of this block: marked, marked and not yet redone
     for (int b0 = 0; b0 < a.rows; b0 += kSampThreads) {
-      const int round = (b0 / kSampThreads) % kRounds;
-      if (round == 0) {
-        mkbits = newbits = 0u;
-#pragma unroll
-        for (int i = 0; i < kRounds; ++i) {
-          const int bi = b0 + i * kSampThreads + (int)threadIdx.x;
-          const int ov = bi < a.rows ? a.out[bi] : 0;
-          mkbits |= (unsigned)(ov == kRedoMark || ov <= kRedoDone) << i;
-          newbits |= (unsigned)(ov == kRedoMark) << i;
-        }
-      }
       const int bb = b0 + (int)threadIdx.x;
-      const bool mk = (mkbits >> round) & 1u;
+      const int ov = bb < a.rows ? a.out[bb] : 0;
+      const bool mk = ov == kRedoMark || ov <= kRedoDone;
       const unsigned bal = __ballot_sync(0xffffffffu, mk);
       if (lane == 0) redo_cnt[warp] = __popc(bal);
       __syncthreads();
@@ -912,7 +871,7 @@ __global__ void __launch_bounds__(kSampThreads, NV4 > 0 && NV4 <= 8 ? 2 : 1) sam
         tot += c;
       }
       const int rank = seen + before + __popc(bal & ((1u << lane) - 1u));
-      const bool mine = mk && ((newbits >> round) & 1u) && rank % (int)gridDim.x == (int)blockIdx.x;
+      const bool mine = mk && ov == kRedoMark && rank % (int)gridDim.x == (int)blockIdx.x;
       const unsigned bm2 = __ballot_sync(0xffffffffu, mine);
       __syncthreads();
       if (lane == 0) redo_cnt[warp] = __popc(bm2);
