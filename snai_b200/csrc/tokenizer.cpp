@@ -384,14 +384,18 @@ void encode(Tokenizer &t, const char *text, size_t n, std::vector<int> *out) {
   if (!s.empty() && s[0] != ' ' && s[0] != '[' && s[0] != '<') s.insert(s.begin(), ' ');
   // split on the special tokens (leftmost match; first in list order there)
   std::vector<std::pair<std::string, int>> parts;  // (text, special id or -1)
+  // only a position holding some special's first byte can start one
+  bool lead[256] = {};
+  for (const std::string &sp : t.specials) lead[(unsigned char)sp[0]] = true;
   size_t start = 0, pos = 0;
   while (pos < s.size()) {
     int hit = -1;
-    for (size_t k = 0; k < t.specials.size(); ++k)
-      if (s.compare(pos, t.specials[k].size(), t.specials[k]) == 0) {
-        hit = (int)k;
-        break;
-      }
+    if (lead[(unsigned char)s[pos]])
+      for (size_t k = 0; k < t.specials.size(); ++k)
+        if (s.compare(pos, t.specials[k].size(), t.specials[k]) == 0) {
+          hit = (int)k;
+          break;
+        }
     if (hit < 0) {
       ++pos;
       continue;
@@ -402,24 +406,31 @@ void encode(Tokenizer &t, const char *text, size_t n, std::vector<int> *out) {
     start = pos;
   }
   if (start < s.size()) parts.push_back({s.substr(start), -1});
+  std::string key;
   for (auto &p : parts) {
     if (p.second >= 0) {
       out->push_back(p.second);
       continue;
     }
-    std::string w;
-    for (char c : p.first) {
-      if (c == ' ') w += kMeta;
-      else w.push_back(c);
-    }
-    // chunks: a U+2581 or \n, then everything up to the next one
+    // chunks: a U+2581 (a space becomes one) or \n, then everything up to
+    // the next one; the key is the chunk with its space written as U+2581
+    const std::string &x = p.first;
+    auto is_start = [&](size_t k) {
+      return x[k] == ' ' || x[k] == '\n' || (x[k] == kMeta[0] && x.compare(k, 3, kMeta) == 0);
+    };
     size_t i = 0;
-    auto is_start = [&](size_t k) { return w[k] == '\n' || w.compare(k, 3, kMeta) == 0; };
-    while (i < w.size() && !is_start(i)) ++i;
-    while (i < w.size()) {
-      size_t j = i + (w[i] == '\n' ? 1 : 3);
-      while (j < w.size() && !is_start(j)) ++j;
-      const std::vector<int> &ids = bpe_ids(t, w.substr(i, j - i));
+    while (i < x.size() && !is_start(i)) ++i;
+    while (i < x.size()) {
+      size_t j = i + (x[i] == kMeta[0] ? 3 : 1);
+      while (j < x.size() && !is_start(j)) ++j;
+      key.clear();
+      if (x[i] == ' ') {
+        key.append(kMeta, 3);
+        key.append(x, i + 1, j - i - 1);
+      } else {
+        key.append(x, i, j - i);
+      }
+      const std::vector<int> &ids = bpe_ids(t, key);
       out->insert(out->end(), ids.begin(), ids.end());
       i = j;
     }

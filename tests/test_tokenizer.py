@@ -82,7 +82,8 @@ def test_known_answers(tiny, built):
 def test_random_texts_match_oracle(built):
     c, o = CTok(FIXTURE), Tokenizer(FIXTURE)
     rng = np.random.default_rng(0)
-    alphabet = list("abcdeinrstäöüß ABC0123.,!?'\n") + ["[USER]", "[SYMBIO]", "</s>", "<s>", "  ", "\t", "€", "漢"]
+    alphabet = list("abcdeinrstäöüß ABC0123.,!?'\n") + ["[USER]", "[SYMBIO]", "</s>", "<s>", "  ", "\t", "€", "漢",
+                                                            META, META + "a", "<", "[", "<s", "[US", "</"]
     for i in range(300):
         text = "".join(rng.choice(alphabet, size=int(rng.integers(0, 60))))
         if i % 7 == 0:
