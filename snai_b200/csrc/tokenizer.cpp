@@ -19,6 +19,7 @@
 //   :187-199  decode(): concatenate, U+2581 -> ' ', optional trim
 // NFKC (:128-130) runs in PHP only when the intl extension is loaded; it is
 // not applied here (the same as a PHP build without intl).
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -214,6 +215,7 @@ struct Tokenizer {
   std::unordered_map<std::string, int> vocab;
   std::vector<std::pair<std::string, int>> vocab_order;  // key order of the file (first occurrence)
   std::unordered_map<int, std::string> inverse;
+  std::vector<const std::string *> inverse_dense;  // inverse[] by id for ids in [0, 2^22), else via the map
   std::unordered_map<std::string, int> ranks;
   std::unordered_map<std::string, std::vector<int>> cache;  // chunk -> ids
   std::vector<std::string> specials;  // the special tokens the vocab has, in list order
@@ -274,6 +276,12 @@ bool load_vocab(Tokenizer *t, const std::string &text, std::string *err) {
     return false;
   }
   for (const auto &kv : t->vocab_order) t->inverse[kv.second] = kv.first;  // array_flip: later keys win
+  int top = -1;
+  for (const auto &kv : t->inverse)
+    if (kv.first >= 0 && kv.first < (1 << 22)) top = std::max(top, kv.first);
+  t->inverse_dense.assign((size_t)(top + 1), nullptr);
+  for (const auto &kv : t->inverse)
+    if (kv.first >= 0 && kv.first < (1 << 22)) t->inverse_dense[kv.first] = &kv.second;
   for (const char *s : kSpecials)
     if (t->vocab.count(s)) t->specials.push_back(s);
   auto u = t->vocab.find("<unk>");
@@ -497,13 +505,18 @@ extern "C" int cortex_tokenizer_decode(void *tok, const int *ids, int n, int tri
   Tokenizer &t = *static_cast<Tokenizer *>(tok);
   std::string s;
   for (int i = 0; i < n; ++i) {
-    auto it = t.inverse.find(ids[i]);
-    if (it != t.inverse.end()) s += it->second;
+    const int id = ids[i];
+    if (id >= 0 && (size_t)id < t.inverse_dense.size()) {
+      if (const std::string *p = t.inverse_dense[id]) s += *p;
+    } else if (id < 0 || id >= (1 << 22)) {
+      auto it = t.inverse.find(id);
+      if (it != t.inverse.end()) s += it->second;
+    }
   }
   std::string o;
   o.reserve(s.size());
   for (size_t i = 0; i < s.size();) {
-    if (s.compare(i, 3, kMeta) == 0) {
+    if (s[i] == kMeta[0] && s.compare(i, 3, kMeta) == 0) {
       o.push_back(' ');
       i += 3;
     } else {
