@@ -120,9 +120,11 @@ __device__ __forceinline__ float warp_row_rms_inv(const float *__restrict__ hr, 
 }
 
 // The rows of a pass of at most kRowPackMax rows, passed by value to the
-// embedding kernel, which writes them to the device row arrays for the later
-// kernels of the pass (so the pass needs no host-to-device copy).  n = 0: the
-// rows are on the device already.
+// pass's first kernel (the embedding kernel, or the QKV GEMV that does its
+// work), which writes them to the device row arrays for the later kernels of
+// the pass (so the pass needs no host-to-device copy), and to the split
+// attention, which reads its row before its dependency wait.  n = 0: the rows
+// are on the device already.
 constexpr int kRowPackMax = 8;
 struct RowPack {
   RowDesc r[kRowPackMax];
