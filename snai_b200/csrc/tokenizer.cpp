@@ -20,6 +20,7 @@
 // NFKC (:128-130) runs in PHP only when the intl extension is loaded; it is
 // not applied here (the same as a PHP build without intl).
 #include <algorithm>
+#include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -211,13 +212,74 @@ struct JsonReader {
   }
 };
 
+// Memo of bpe() per chunk: open addressing over FNV-1a hashes, keys and ids
+// in two arenas (a chunk is a few bytes; a node-based map spends more time
+// chasing its nodes than hashing).
+struct ChunkCache {
+  struct Slot {
+    uint64_t h = 0;
+    uint32_t key = 0, klen = 0, ids = 0, n = 0;
+    bool used = false;
+  };
+  std::vector<Slot> slots = std::vector<Slot>(1024);
+  std::string keys;
+  std::vector<int> ids;
+  size_t count = 0;
+
+  static uint64_t hash(const std::string &k) {
+    uint64_t h = 1469598103934665603ull;
+    for (unsigned char c : k) h = (h ^ c) * 1099511628211ull;
+    return h;
+  }
+  // the ids of `k` (hash h) as (first, count) into `ids`, or false
+  bool find(const std::string &k, uint64_t h, uint32_t *first, uint32_t *n) const {
+    const size_t mask = slots.size() - 1;
+    for (size_t i = h & mask;; i = (i + 1) & mask) {
+      const Slot &s = slots[i];
+      if (!s.used) return false;
+      if (s.h == h && s.klen == k.size() && keys.compare(s.key, s.klen, k) == 0) {
+        *first = s.ids;
+        *n = s.n;
+        return true;
+      }
+    }
+  }
+  void insert(const std::string &k, uint64_t h, const std::vector<int> &v, uint32_t *first) {
+    if (2 * (count + 1) > slots.size()) {
+      std::vector<Slot> old(2 * slots.size());
+      old.swap(slots);
+      const size_t mask = slots.size() - 1;
+      for (const Slot &s : old)
+        if (s.used) {
+          size_t i = s.h & mask;
+          while (slots[i].used) i = (i + 1) & mask;
+          slots[i] = s;
+        }
+    }
+    const size_t mask = slots.size() - 1;
+    size_t i = h & mask;
+    while (slots[i].used) i = (i + 1) & mask;
+    Slot &s = slots[i];
+    s.used = true;
+    s.h = h;
+    s.key = (uint32_t)keys.size();
+    s.klen = (uint32_t)k.size();
+    keys += k;
+    s.ids = (uint32_t)ids.size();
+    s.n = (uint32_t)v.size();
+    ids.insert(ids.end(), v.begin(), v.end());
+    ++count;
+    *first = s.ids;
+  }
+};
+
 struct Tokenizer {
   std::unordered_map<std::string, int> vocab;
   std::vector<std::pair<std::string, int>> vocab_order;  // key order of the file (first occurrence)
   std::unordered_map<int, std::string> inverse;
   std::vector<const std::string *> inverse_dense;  // inverse[] by id for ids in [0, 2^22), else via the map
   std::unordered_map<std::string, int> ranks;
-  std::unordered_map<std::string, std::vector<int>> cache;  // chunk -> ids
+  ChunkCache cache;  // chunk -> ids
   std::vector<std::string> specials;  // the special tokens the vocab has, in list order
   int unk = 0;
   std::mutex mu;
@@ -344,10 +406,14 @@ std::string sanitize_utf8(const char *s, size_t n) {
 
 size_t utf8_len(unsigned char b) { return b < 0x80 ? 1 : b < 0xE0 ? 2 : b < 0xF0 ? 3 : 4; }
 
-// :56-116 bpe() of one chunk, as vocabulary ids (memoised).
-const std::vector<int> &bpe_ids(Tokenizer &t, const std::string &chunk) {
-  auto hit = t.cache.find(chunk);
-  if (hit != t.cache.end()) return hit->second;
+// :56-116 bpe() of one chunk, as vocabulary ids (memoised), appended to out.
+void bpe_ids(Tokenizer &t, const std::string &chunk, std::vector<int> *out) {
+  const uint64_t h = ChunkCache::hash(chunk);
+  uint32_t first = 0, cnt = 0;
+  if (t.cache.find(chunk, h, &first, &cnt)) {
+    out->insert(out->end(), t.cache.ids.begin() + first, t.cache.ids.begin() + first + cnt);
+    return;
+  }
   std::vector<std::string> word;
   for (size_t i = 0; i < chunk.size();) {
     const size_t l = std::min(utf8_len((unsigned char)chunk[i]), chunk.size() - i);
@@ -384,7 +450,8 @@ const std::vector<int> &bpe_ids(Tokenizer &t, const std::string &chunk) {
     auto v = t.vocab.find(piece);
     ids.push_back(v == t.vocab.end() ? t.unk : v->second);
   }
-  return t.cache.emplace(chunk, std::move(ids)).first->second;
+  t.cache.insert(chunk, h, ids, &first);
+  out->insert(out->end(), ids.begin(), ids.end());
 }
 
 void encode(Tokenizer &t, const char *text, size_t n, std::vector<int> *out) {
@@ -438,8 +505,7 @@ void encode(Tokenizer &t, const char *text, size_t n, std::vector<int> *out) {
       } else {
         key.append(x, i, j - i);
       }
-      const std::vector<int> &ids = bpe_ids(t, key);
-      out->insert(out->end(), ids.begin(), ids.end());
+      bpe_ids(t, key, out);
       i = j;
     }
   }
