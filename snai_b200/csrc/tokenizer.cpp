@@ -281,6 +281,7 @@ struct Tokenizer {
   std::unordered_map<std::string, int> ranks;
   ChunkCache cache;  // chunk -> ids
   std::vector<std::string> specials;  // the special tokens the vocab has, in list order
+  std::vector<int> special_ids;       // and their ids
   int unk = 0;
   std::mutex mu;
 };
@@ -344,8 +345,13 @@ bool load_vocab(Tokenizer *t, const std::string &text, std::string *err) {
   t->inverse_dense.assign((size_t)(top + 1), nullptr);
   for (const auto &kv : t->inverse)
     if (kv.first >= 0 && kv.first < (1 << 22)) t->inverse_dense[kv.first] = &kv.second;
-  for (const char *s : kSpecials)
-    if (t->vocab.count(s)) t->specials.push_back(s);
+  for (const char *s : kSpecials) {
+    auto it = t->vocab.find(s);
+    if (it != t->vocab.end()) {
+      t->specials.push_back(s);
+      t->special_ids.push_back(it->second);
+    }
+  }
   auto u = t->vocab.find("<unk>");
   t->unk = u == t->vocab.end() ? 0 : u->second;
   return true;
@@ -360,8 +366,17 @@ std::string sanitize_utf8(const char *s, size_t n) {
   while (i < n) {
     const unsigned char b = (unsigned char)s[i];
     if (b < 0x80) {
-      out.push_back((char)b);
-      ++i;
+      // a run of ASCII bytes, eight at a time, copied at once
+      size_t j = i + 1;
+      while (j + 8 <= n) {
+        uint64_t w;
+        memcpy(&w, s + j, 8);
+        if (w & 0x8080808080808080ull) break;
+        j += 8;
+      }
+      while (j < n && (unsigned char)s[j] < 0x80) ++j;
+      out.append(s + i, j - i);
+      i = j;
       continue;
     }
     int need;
@@ -457,8 +472,32 @@ void bpe_ids(Tokenizer &t, const std::string &chunk, std::vector<int> *out) {
 void encode(Tokenizer &t, const char *text, size_t n, std::vector<int> *out) {
   std::string s = sanitize_utf8(text, n);
   if (!s.empty() && s[0] != ' ' && s[0] != '[' && s[0] != '<') s.insert(s.begin(), ' ');
-  // split on the special tokens (leftmost match; first in list order there)
-  std::vector<std::pair<std::string, int>> parts;  // (text, special id or -1)
+  // the text between special tokens in chunks: a U+2581 (a space becomes
+  // one) or \n, then everything up to the next one; the key is the chunk
+  // with its space written as U+2581 (text before a part's first chunk
+  // start is dropped)
+  std::string key;
+  auto chunks = [&](size_t a, size_t b) {
+    auto is_start = [&](size_t k) {
+      return s[k] == ' ' || s[k] == '\n' || (s[k] == kMeta[0] && k + 3 <= b && s.compare(k, 3, kMeta) == 0);
+    };
+    size_t i = a;
+    while (i < b && !is_start(i)) ++i;
+    while (i < b) {
+      size_t j = i + (s[i] == kMeta[0] ? 3 : 1);
+      while (j < b && !is_start(j)) ++j;
+      key.clear();
+      if (s[i] == ' ') {
+        key.append(kMeta, 3);
+        key.append(s, i + 1, j - i - 1);
+      } else {
+        key.append(s, i, j - i);
+      }
+      bpe_ids(t, key, out);
+      i = j;
+    }
+  };
+  // split on the special tokens (leftmost match; first in list order there);
   // only a position holding some special's first byte can start one
   bool lead[256] = {};
   for (const std::string &sp : t.specials) lead[(unsigned char)sp[0]] = true;
@@ -475,40 +514,12 @@ void encode(Tokenizer &t, const char *text, size_t n, std::vector<int> *out) {
       ++pos;
       continue;
     }
-    if (pos > start) parts.push_back({s.substr(start, pos - start), -1});
-    parts.push_back({t.specials[hit], t.vocab[t.specials[hit]]});
+    if (pos > start) chunks(start, pos);
+    out->push_back(t.special_ids[hit]);
     pos += t.specials[hit].size();
     start = pos;
   }
-  if (start < s.size()) parts.push_back({s.substr(start), -1});
-  std::string key;
-  for (auto &p : parts) {
-    if (p.second >= 0) {
-      out->push_back(p.second);
-      continue;
-    }
-    // chunks: a U+2581 (a space becomes one) or \n, then everything up to
-    // the next one; the key is the chunk with its space written as U+2581
-    const std::string &x = p.first;
-    auto is_start = [&](size_t k) {
-      return x[k] == ' ' || x[k] == '\n' || (x[k] == kMeta[0] && x.compare(k, 3, kMeta) == 0);
-    };
-    size_t i = 0;
-    while (i < x.size() && !is_start(i)) ++i;
-    while (i < x.size()) {
-      size_t j = i + (x[i] == kMeta[0] ? 3 : 1);
-      while (j < x.size() && !is_start(j)) ++j;
-      key.clear();
-      if (x[i] == ' ') {
-        key.append(kMeta, 3);
-        key.append(x, i + 1, j - i - 1);
-      } else {
-        key.append(x, i, j - i);
-      }
-      bpe_ids(t, key, out);
-      i = j;
-    }
-  }
+  if (start < s.size()) chunks(start, s.size());
 }
 
 }  // namespace
