@@ -97,6 +97,20 @@ def test_random_texts_match_oracle(built):
     c.close()
 
 
+def test_long_text_matches_oracle(built):
+    """One long text of many distinct words (the per-chunk memo grows and
+    rehashes several times), encoded twice (the second time from the memo)."""
+    c, o = CTok(FIXTURE), Tokenizer(FIXTURE)
+    rng = np.random.default_rng(2)
+    letters = list("abcdeinrstäöüßABC")
+    words = ["".join(rng.choice(letters, size=int(rng.integers(1, 9)))) for _ in range(6000)]
+    text = " ".join(words[int(i)] + ("\n" if k % 13 == 12 else "") for k, i in enumerate(rng.integers(0, 6000, 20000)))
+    want = o.encode(text)
+    assert c.encode(text) == want
+    assert c.encode(text) == want
+    c.close()
+
+
 @pytest.mark.skipif(not os.path.exists(REF_VOCAB), reason="the reference's vocabulary file is not here")
 def test_reference_vocabulary_round_trip(built):
     """src/snai_tokenizer.php:202-227: its test string survives encode ->
