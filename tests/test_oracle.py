@@ -223,15 +223,17 @@ def test_oracle_forward_matches_numpy(heads, model_dir, built):
     assert rel_err(lg, ref) < 2e-5
 
 
-def test_oracle_forward_matches_numpy_headline_shape(model_dir, built):
-    """The headline model's width and heads (d=1024, 16 heads of 64, two
-    layers, N(0, 0.02) weights; a small vocabulary) over 40 positions."""
-    p = make_model(model_dir, "d1024.snai", 512, 1024, 48, 2, seed=9, std=0.02)
+@pytest.mark.parametrize("dim,heads", [(1024, 16), (512, 8)])
+def test_oracle_forward_matches_numpy_headline_shape(dim, heads, model_dir, built):
+    """The benchmarked models' widths and heads (d=1024 with 16 heads and
+    d=512 with 8, heads of 64, two layers, N(0, 0.02) weights; a small
+    vocabulary) over 40 positions."""
+    p = make_model(model_dir, f"d{dim}.snai", 512, dim, 48, 2, seed=9, std=0.02)
     h, t = modelgen.read_model(p)
     toks = list(np.random.default_rng(9).integers(0, 512, 40))
-    o = O.Oracle(p, num_heads=16)
+    o = O.Oracle(p, num_heads=heads)
     lg = o.forward(toks)
-    assert rel_err(lg, np_forward(h, t, toks, 16)) < 2e-5
+    assert rel_err(lg, np_forward(h, t, toks, heads)) < 2e-5
 
 
 def test_oracle_one_position_attention_returns_v(model_dir, built):
