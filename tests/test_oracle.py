@@ -143,6 +143,20 @@ def test_oracle_samplers_match_transliteration(exp_mode, built):
             assert b == php_variant_b(L, hist, T, k, p, 1.1, u, exp), (i, T, k, p)
 
 
+def test_oracle_samplers_match_transliteration_benchmark_vocab(built):
+    """The same check at the benchmark's vocabulary (V=16384), the sampler
+    benchmark's settings, one row of each kind."""
+    rng = np.random.default_rng(12)
+    V = 16384
+    for i, L in enumerate(random_rows(rng, 4, V)):
+        hist = list(rng.integers(0, V, 256))
+        u = float(np.float32(rng.random()))
+        for exp_mode, exp in ((0, math.exp), (1, contract_exp)):
+            assert O.sample_a(L, hist, 0.7, 1.15, u, exp_mode) == php_variant_a(L, hist, 0.7, 1.15, u, exp), i
+            b = O.sample_b(L, hist, 0.7, 50, 0.95, 1.15, u, exp_mode)
+            assert b == php_variant_b(L, hist, 0.7, 50, 0.95, 1.15, u, exp), i
+
+
 def test_exp_contract_accuracy(built):
     rng = np.random.default_rng(3)
     x = np.concatenate([rng.uniform(-745, 709, 300000), rng.uniform(-60, 0, 300000), rng.uniform(-1, 1, 100000)])
